@@ -1,0 +1,131 @@
+// Fused (optional per-head Q/K RMSNorm) + rotary embedding + paged KV-cache insert.
+//
+// Input is the packed QKV projection output [T, (Hq + 2*Hkv) * D].  Per token:
+//   q heads: [RMSNorm] -> RoPE -> written back in place (attention reads q from the buffer)
+//   k heads: [RMSNorm] -> RoPE -> written to k_cache at slot_mapping[t]
+//   v heads: copied to v_cache at slot_mapping[t]
+// Cache layout is [num_blocks, Hkv, block_size, D] so that one page of one KV head is a
+// contiguous block_size*D run (a single bulk copy for the attention kernels).  RoPE supports
+// NeoX (rotate halves) and GPT-J (rotate pairs) styles and partial rotary (rot_dim < D); the
+// cos/sin cache is [max_pos, rot_dim] fp32 = [cos(rot_dim/2) | sin(rot_dim/2)].
+//
+// Reference counterparts: vllm_musa/jit_kernel/csrc/norm/qk_mrope.mu:168-1311 (Qwen3 fused
+// QK-norm + RoPE + cache), vllm_musa/jit_kernel/csrc/rope/rotary_embedding.mu:124-708 (RoPE),
+// csrc/musa/cache_kernels.mu:16 (reshape_and_cache_flash NHD).  One warp per (token, head);
+// the head vector is staged in shared memory so any rot_dim / style pairs are one load away.
+#include "../b200_kernels.h"
+#include "../common/common.cuh"
+
+namespace b200 {
+namespace rope {
+
+constexpr int kWarps = 4;
+
+template <int D>
+__global__ void __launch_bounds__(kWarps * 32)
+    rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld_qkv,
+                   const int32_t* __restrict__ positions, const float* __restrict__ cos_sin,
+                   const __nv_bfloat16* __restrict__ q_norm_w,
+                   const __nv_bfloat16* __restrict__ k_norm_w, __nv_bfloat16* __restrict__ k_cache,
+                   __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ slot_mapping,
+                   int T, int Hq, int Hkv, int block_size, int rot_dim, int neox, float eps,
+                   int* err) {
+  constexpr int E = D / 32;  // elements per lane
+  __shared__ float stage[kWarps][D];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  const int64_t gid = (int64_t)blockIdx.x * kWarps + warp;
+  if (gid >= (int64_t)T * heads) return;
+  const int t = gid / heads, h = gid % heads;
+  __nv_bfloat16* src = qkv + t * ld_qkv + (int64_t)h * D + lane * E;
+
+  float v[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = bf2f(src[j]);
+
+  const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv, is_v = h >= Hq + Hkv;
+  const int32_t slot = slot_mapping ? slot_mapping[t] : -1;
+
+  if (!is_v) {
+    const __nv_bfloat16* nw = is_q ? q_norm_w : k_norm_w;
+    if (nw) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) ss += v[j] * v[j];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / D + eps);
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = v[j] * inv * bf2f(nw[lane * E + j]);
+    }
+    if (rot_dim > 0) {
+#pragma unroll
+      for (int j = 0; j < E; ++j) stage[warp][lane * E + j] = v[j];
+      __syncwarp();
+      const int64_t pos = positions[t];
+      const float* cs = cos_sin + pos * rot_dim;
+      const int half = rot_dim / 2;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        const int i = lane * E + j;
+        if (i < rot_dim) {
+          if (neox) {
+            const int f = i < half ? i : i - half;
+            const float c = cs[f], s = cs[half + f];
+            const float other = stage[warp][i < half ? i + half : i - half];
+            v[j] = i < half ? v[j] * c - other * s : v[j] * c + other * s;
+          } else {
+            const int f = i / 2;
+            const float c = cs[f], s = cs[half + f];
+            const float other = stage[warp][i ^ 1];
+            v[j] = (i & 1) ? v[j] * c + other * s : v[j] * c - other * s;
+          }
+        }
+      }
+    }
+  }
+
+  if (is_q) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) src[j] = f2bf(v[j]);
+    return;
+  }
+  if (slot < 0) return;  // padding token: nothing to cache
+  const int kvh = is_k ? h - Hq : h - Hq - Hkv;
+  const int64_t blk = slot / block_size, off = slot % block_size;
+  __nv_bfloat16* dst = (is_k ? k_cache : v_cache) + ((blk * Hkv + kvh) * block_size + off) * D +
+                       lane * E;
+#pragma unroll
+  for (int j = 0; j < E; ++j) dst[j] = f2bf(v[j]);
+}
+
+void run_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
+  if (a.T == 0) return;
+  B200_REQUIRE(a.rot_dim % 2 == 0 && a.rot_dim <= a.D, "rope_kv: rot_dim");
+  const int64_t warps = (int64_t)a.T * (a.Hq + 2 * a.Hkv);
+  const int blocks = (int)((warps + kWarps - 1) / kWarps);
+#define B200_ROPE_LAUNCH(DD)                                                                     \
+  rope_kv_kernel<DD><<<blocks, kWarps * 32, 0, s>>>(                                             \
+      reinterpret_cast<__nv_bfloat16*>(a.qkv), a.ld_qkv, a.positions, a.cos_sin,                 \
+      reinterpret_cast<const __nv_bfloat16*>(a.q_norm_w),                                        \
+      reinterpret_cast<const __nv_bfloat16*>(a.k_norm_w),                                        \
+      reinterpret_cast<__nv_bfloat16*>(a.k_cache), reinterpret_cast<__nv_bfloat16*>(a.v_cache), \
+      a.slot_mapping, a.T, a.Hq, a.Hkv, a.block_size, a.rot_dim, a.neox ? 1 : 0, a.eps, a.err)
+  switch (a.D) {
+    case 64:
+      B200_ROPE_LAUNCH(64);
+      break;
+    case 128:
+      B200_ROPE_LAUNCH(128);
+      break;
+    case 256:
+      B200_ROPE_LAUNCH(256);
+      break;
+    default:
+      B200_REQUIRE(false, "rope_kv: head_dim must be 64, 128 or 256");
+  }
+#undef B200_ROPE_LAUNCH
+  B200_CUDA_OK(cudaGetLastError());
+}
+
+}  // namespace rope
+}  // namespace b200

@@ -1,0 +1,159 @@
+// Plain-C++ launcher interface of the vllm_musa_b200 CUDA kernels.
+//
+// Every kernel translation unit (csrc/**/*.cu) implements one group of these functions and
+// includes no torch header; csrc/torch_bindings.cpp validates torch tensors, fills the
+// argument structs and registers the ops as torch.ops.b200.*.  All launchers are
+// asynchronous on the given stream, allocate nothing, and throw std::runtime_error on bad
+// arguments.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+namespace b200 {
+
+// ------------------------------------------------------------------------------- GEMM
+namespace gemm {
+enum Mode : int { kModeStore = 0, kModeSiluMul = 1, kModeF32 = 2 };
+struct GemmArgs {
+  const void* A;  // [M, K] bf16, row stride lda
+  int64_t lda;
+  const void* B;  // [N, K] bf16, row stride ldb
+  int64_t ldb;
+  void* C;        // [M, N] (or [M, N/2] for SiLU-mul), row stride ldc
+  int64_t ldc;
+  int M, N, K;
+  int mode;
+  int bn, splits;  // 0 = automatic
+  float* workspace;
+  int64_t workspace_numel;
+  int* err;
+};
+struct GemmPlan {
+  int bn, splits;
+  int64_t workspace_floats;
+};
+GemmPlan plan_bf16(int M, int N, int K);
+void run_bf16(const GemmArgs& a, cudaStream_t s);
+}  // namespace gemm
+
+// ------------------------------------------------------------------------------- norms
+namespace norm {
+struct RmsNormArgs {
+  void* out;
+  int64_t ld_out;
+  void* x;
+  int64_t ld_x;
+  void* residual;  // nullptr: plain RMSNorm; else residual += x (in place) first
+  int64_t ld_res;
+  const void* weight;
+  int rows, H;
+  float eps;
+  bool gemma;
+};
+void run_rms_norm(const RmsNormArgs& a, cudaStream_t s);
+void run_rms_norm_gated(void* out, const void* x, const void* z, const void* w, int rows, int H,
+                        int group, float eps, cudaStream_t s);
+}  // namespace norm
+
+// ------------------------------------------------------------------------------- activations
+namespace act {
+void run_act_and_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int rows, int I,
+                     int kind, float limit, cudaStream_t s);
+void run_silu_mul_fp8_quant(void* out, float* scales, const void* x, int64_t ld_x, int rows, int I,
+                            cudaStream_t s);
+void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, int rows, int K,
+                         cudaStream_t s);
+}  // namespace act
+
+// ------------------------------------------------------------------------------- rope + kv
+namespace rope {
+struct RopeKvArgs {
+  void* qkv;
+  int64_t ld_qkv;
+  const int32_t* positions;
+  const float* cos_sin;
+  const void* q_norm_w;  // optional
+  const void* k_norm_w;  // optional
+  void* k_cache;
+  void* v_cache;
+  const int32_t* slot_mapping;
+  int T, Hq, Hkv, D, block_size, rot_dim;
+  bool neox;
+  float eps;
+  int* err;
+};
+void run_rope_kv(const RopeKvArgs& a, cudaStream_t s);
+}  // namespace rope
+
+// ------------------------------------------------------------------------------- attention
+namespace attn {
+struct DecodeArgs {
+  const void* q;
+  int64_t ld_q;
+  void* o;
+  int64_t ld_o;
+  void* k_cache;
+  void* v_cache;
+  int num_blocks;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  const int32_t* seq_lens;
+  int B, Hq, Hkv, D, block_size, max_seq_len, num_splits;
+  float scale;
+  float* ws_o;
+  float* ws_lse;
+  int* err;
+};
+struct PrefillArgs {
+  const void* q;
+  int64_t ld_q;
+  void* o;
+  int64_t ld_o;
+  void* k_cache;
+  void* v_cache;
+  int num_blocks;
+  const int32_t* cu_q;
+  const int32_t* seq_lens;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int32_t* tile_offsets;  // scratch [R+1]
+  int T, R, Hq, Hkv, D, block_size, window;
+  float scale;
+  int* err;
+};
+int decode_num_splits(int B, int Hkv, int max_seq_len);
+void run_decode(const DecodeArgs& a, cudaStream_t s);
+void run_prefill(const PrefillArgs& a, cudaStream_t s);
+}  // namespace attn
+
+// ------------------------------------------------------------------------------- sampling
+namespace sampling {
+struct SampleArgs {
+  const float* logits;
+  int64_t ld;
+  int R, V, vocab_offset;
+  const float* temperature;
+  const int32_t* top_k;
+  const float* top_p;
+  const float* min_p;
+  const int64_t* seeds;
+  const int32_t* steps;
+  float* out_val;
+  int64_t* out_idx;
+};
+void run_sample(const SampleArgs& a, cudaStream_t s);
+void run_merge_candidates(const float* vals, const int64_t* idx, int S, int R, int64_t* out,
+                          cudaStream_t s);
+}  // namespace sampling
+
+// ------------------------------------------------------------------------------- misc
+namespace misc {
+void run_embedding(void* out, const void* table, const int32_t* ids, int T, int H, int64_t vocab,
+                   int64_t vocab_start, cudaStream_t s);
+void run_gather_rows(void* out, const void* in, int64_t ld_in, const int32_t* idx, int R, int H,
+                     int elem_bytes, cudaStream_t s);
+}  // namespace misc
+
+}  // namespace b200

@@ -1,0 +1,36 @@
+// Host-side error helpers for the plain-C++ launchers (no torch headers here, so the
+// kernel translation units stay cheap to compile).  Failures throw std::runtime_error,
+// which the torch bindings surface as Python RuntimeError.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+#define B200_REQUIRE(cond, msg)                                                           \
+  do {                                                                                    \
+    if (!(cond))                                                                          \
+      throw std::runtime_error(std::string("b200: ") + (msg) + " [" + __FILE__ + ":" +    \
+                               std::to_string(__LINE__) + "]");                          \
+  } while (0)
+
+#define B200_CUDA_OK(expr)                                                                \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    if (_e != cudaSuccess)                                                                \
+      throw std::runtime_error(std::string("b200: CUDA error: ") + cudaGetErrorString(_e) + \
+                               " [" + __FILE__ + ":" + std::to_string(__LINE__) + "]");  \
+  } while (0)
+
+namespace b200 {
+inline int num_sms() {
+  static int n = -1;
+  if (n < 0) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n = v > 0 ? v : 148;
+  }
+  return n;
+}
+}  // namespace b200

@@ -1,0 +1,38 @@
+// Warp-level tensor-core helpers (mma.sync m16n8k16 bf16, ldmatrix) used by the attention
+// kernels, whose tiles are small and memory-bound (decode) or a small share of the FLOPs
+// (prefill at the served context lengths).  GEMMs use tcgen05 (tcgen05.cuh).
+#pragma once
+#include "common.cuh"
+
+namespace b200 {
+namespace mma {
+
+B200_DEVICE void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+B200_DEVICE void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                           uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D(16x8 f32) += A(16x16 bf16) * B(16x8 bf16)
+B200_DEVICE void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Address of the 16-byte chunk `chunk` (0..7) of row `row` in a tile written by TMA with the
+// 128-byte swizzle (rows of 128 bytes, tile base 1024-byte aligned).
+B200_DEVICE uint32_t sw128(uint32_t base, int row, int chunk) {
+  return base + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
+}  // namespace mma
+}  // namespace b200

@@ -1,0 +1,120 @@
+// tcgen05 (5th-generation tensor core) helpers for sm_100a: TMEM allocation, shared-memory
+// matrix descriptors, instruction descriptors, MMA issue/commit and TMEM->register loads.
+//
+// Bit layouts follow the PTX ISA description of the tcgen05 shared-memory descriptor and
+// instruction descriptor (the same layouts CUTLASS exposes as UMMA::SmemDescriptor /
+// UMMA::InstrDescriptor):
+//   smem desc: [0,14) start addr>>4, [16,30) leading byte offset>>4, [32,46) stride byte
+//              offset>>4, [46,48) version=1, [49,52) base offset, [52] lbo mode,
+//              [61,64) layout (0 none, 2 = 128B swizzle, 4 = 64B, 6 = 32B)
+//   instr desc (kind::f16): [4,6) D fmt (1=f32), [7,10) A fmt (0 f16, 1 bf16), [10,13) B fmt,
+//              [15] A major (0=K), [16] B major, [17,23) N>>3, [24,29) M>>4
+#pragma once
+#include "common.cuh"
+
+namespace b200 {
+namespace tc {
+
+// ---------------------------------------------------------------------------------------------
+// TMEM allocation (one warp executes these, .sync.aligned)
+// ---------------------------------------------------------------------------------------------
+B200_DEVICE void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+B200_DEVICE void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+B200_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+B200_DEVICE void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+B200_DEVICE void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Descriptors
+// ---------------------------------------------------------------------------------------------
+enum Swizzle : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
+
+// K-major operand tile staged by TMA with 128-byte swizzle: rows of 128 bytes, 8-row
+// core-matrix groups 1024 bytes apart (SBO).  LBO is unused for swizzled K-major layouts.
+B200_DEVICE uint64_t smem_desc_kmajor_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(1) << 16;                    // LBO (ignored for SW128 K-major)
+  d |= (uint64_t)((1024 >> 4) & 0x3FFF) << 32;  // SBO = 8 rows * 128 B
+  d |= (uint64_t)1 << 46;                      // descriptor version (sm_100)
+  d |= (uint64_t)kSwizzle128B << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with fp32 accumulation, both operands K-major.
+template <bool kBf16>
+B200_HOST_DEVICE constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4)                                   // D = f32
+         | ((kBf16 ? 1u : 0u) << 7)                  // A format
+         | ((kBf16 ? 1u : 0u) << 10)                 // B format
+         | (0u << 15) | (0u << 16)                   // both K-major
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------------------------
+// MMA issue (single thread) and commit
+// ---------------------------------------------------------------------------------------------
+B200_DEVICE void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once every previously issued MMA of this thread has completed.
+B200_DEVICE void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// TMEM -> registers.  Warp w may only touch lanes [32*(w%4), 32*(w%4)+32).
+// 32x32b.x32: thread t of the warp receives 32 consecutive 32-bit columns of lane (base+t).
+// ---------------------------------------------------------------------------------------------
+B200_DEVICE void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+B200_DEVICE void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+B200_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+}  // namespace tc
+}  // namespace b200

@@ -1,0 +1,357 @@
+// Continuous-batching scheduler and paged-KV block pool (see scheduler.h).
+//
+// Policy (the behaviour vLLM's V1 scheduler gives the reference):
+//  1. Running requests first, in admission order: one token for a decode, the next prompt
+//     chunk for a partial prefill, within the per-step token budget.  When the pool has no
+//     block for a running request, the most recently admitted running request is preempted
+//     (recompute: its blocks are released and it returns to the head of the waiting queue).
+//  2. If nothing was preempted, waiting requests are admitted FCFS while the budget, the
+//     sequence cap and the pool allow; prefix-cache hits skip their cached full blocks.
+// The step's inputs are laid out decodes first (one query token each), then prefills, which
+// is the order the attention kernels consume them in.
+#include "scheduler.h"
+
+#include <algorithm>
+#include <stdexcept>
+
+namespace b200 {
+namespace rt {
+
+// ------------------------------------------------------------------------------ BlockPool
+BlockPool::BlockPool(int num_blocks)
+    : num_blocks_(num_blocks),
+      ref_(num_blocks, 0),
+      hash_(num_blocks, 0),
+      pos_(num_blocks),
+      in_free_(num_blocks, true) {
+  for (int b = 0; b < num_blocks; ++b) pos_[b] = free_.insert(free_.end(), b);
+  free_count_ = num_blocks;
+}
+
+int BlockPool::allocate() {
+  if (free_.empty()) return -1;
+  const int b = free_.front();
+  free_.pop_front();
+  in_free_[b] = false;
+  --free_count_;
+  if (hash_[b] != 0) {
+    auto it = cached_.find(hash_[b]);
+    if (it != cached_.end() && it->second == b) cached_.erase(it);
+    hash_[b] = 0;
+  }
+  ref_[b] = 1;
+  return b;
+}
+
+void BlockPool::release(int b) {
+  if (ref_[b] <= 0) throw std::runtime_error("BlockPool: double free");
+  if (--ref_[b] == 0) {
+    pos_[b] = free_.insert(free_.end(), b);
+    in_free_[b] = true;
+    ++free_count_;
+  }
+}
+
+void BlockPool::touch(int b) {
+  if (ref_[b] == 0 && in_free_[b]) {
+    free_.erase(pos_[b]);
+    in_free_[b] = false;
+    --free_count_;
+  }
+  ++ref_[b];
+}
+
+int BlockPool::lookup(uint64_t h) const {
+  auto it = cached_.find(h);
+  return it == cached_.end() ? -1 : it->second;
+}
+
+void BlockPool::set_hash(int b, uint64_t h) {
+  if (h == 0 || hash_[b] != 0) return;
+  if (cached_.count(h)) return;  // an identical block is already cached
+  hash_[b] = h;
+  cached_[h] = b;
+}
+
+// ------------------------------------------------------------------------------ Scheduler
+static inline uint64_t mix64(uint64_t x) {
+  // splitmix64 finaliser
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+uint64_t Scheduler::block_hash(uint64_t parent, const int32_t* toks, int n) const {
+  uint64_t h = mix64(parent ^ 0x5bd1e9955bd1e995ull);
+  for (int i = 0; i < n; ++i) h = mix64(h ^ (uint64_t)(uint32_t)toks[i]);
+  return h == 0 ? 1 : h;
+}
+
+Scheduler::Scheduler(const SchedulerConfig& cfg, int num_blocks, const StepBuffers& buf)
+    : cfg_(cfg), pool_(num_blocks), buf_(buf) {
+  if (cfg_.block_size <= 0) throw std::runtime_error("scheduler: block_size must be > 0");
+  if ((int64_t)cfg_.max_blocks_per_seq * cfg_.block_size < cfg_.max_model_len)
+    throw std::runtime_error("scheduler: block-table width cannot hold max_model_len");
+  if (buf_.max_tokens < cfg_.max_num_batched_tokens || buf_.max_reqs < cfg_.max_num_seqs)
+    throw std::runtime_error("scheduler: step buffers smaller than the batch limits");
+}
+
+void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt,
+                            const SamplingCfg& sp) {
+  if (reqs_.count(id)) throw std::runtime_error("scheduler: duplicate request id");
+  if (prompt.empty()) throw std::runtime_error("scheduler: empty prompt");
+  if ((int)prompt.size() >= cfg_.max_model_len)
+    throw std::runtime_error("scheduler: prompt length " + std::to_string(prompt.size()) +
+                             " leaves no room below max_model_len " +
+                             std::to_string(cfg_.max_model_len));
+  Request r;
+  r.id = id;
+  r.tokens = prompt;
+  r.num_prompt = (int)prompt.size();
+  r.sp = sp;
+  reqs_.emplace(id, std::move(r));
+  waiting_.push_back(id);
+}
+
+void Scheduler::free_request_blocks(Request& r) {
+  // reverse order: the tail blocks (least likely shared) are handed out first
+  for (auto it = r.blocks.rbegin(); it != r.blocks.rend(); ++it) pool_.release(*it);
+  r.blocks.clear();
+  r.block_hashes.clear();
+}
+
+bool Scheduler::abort_request(int64_t id) {
+  auto it = reqs_.find(id);
+  if (it == reqs_.end() || it->second.status == kFinished) return false;
+  Request& r = it->second;
+  if (r.status == kWaiting) {
+    waiting_.erase(std::remove(waiting_.begin(), waiting_.end(), id), waiting_.end());
+  } else {
+    running_.erase(std::remove(running_.begin(), running_.end(), id), running_.end());
+  }
+  free_request_blocks(r);
+  r.status = kFinished;
+  r.reason = kAbort;
+  r.finish_step = step_;
+  return true;
+}
+
+void Scheduler::preempt(Request& r) {
+  free_request_blocks(r);
+  r.num_computed = 0;
+  r.num_cached_prefix = 0;
+  r.status = kWaiting;
+  r.num_preemptions++;
+  waiting_.push_front(r.id);
+}
+
+bool Scheduler::ensure_blocks(Request& r, int num_tokens) {
+  const int need = (num_tokens + cfg_.block_size - 1) / cfg_.block_size - (int)r.blocks.size();
+  if (need <= 0) return true;
+  if ((int)r.blocks.size() + need > cfg_.max_blocks_per_seq) return false;
+  if (pool_.num_free() < need) return false;
+  for (int i = 0; i < need; ++i) r.blocks.push_back(pool_.allocate());
+  return true;
+}
+
+void Scheduler::admit_prefix(Request& r) {
+  if (!cfg_.prefix_caching) return;
+  const int bs = cfg_.block_size;
+  const int n_full = ((int)r.tokens.size() - 1) / bs;  // keep >= 1 token to compute
+  uint64_t parent = 0;
+  for (int j = 0; j < n_full; ++j) {
+    const uint64_t h = block_hash(parent, r.tokens.data() + j * bs, bs);
+    pool_.cache_queries++;
+    const int b = pool_.lookup(h);
+    if (b < 0) break;
+    pool_.cache_hits++;
+    pool_.touch(b);
+    r.blocks.push_back(b);
+    r.block_hashes.push_back(h);
+    parent = h;
+  }
+  r.num_computed = (int)r.blocks.size() * bs;
+  r.num_cached_prefix = r.num_computed;
+}
+
+void Scheduler::register_full_blocks(Request& r) {
+  if (!cfg_.prefix_caching) return;
+  const int bs = cfg_.block_size;
+  while ((int)r.block_hashes.size() < (int)r.blocks.size() &&
+         ((int)r.block_hashes.size() + 1) * bs <= r.num_computed) {
+    const int j = (int)r.block_hashes.size();
+    const uint64_t parent = j == 0 ? 0 : r.block_hashes[j - 1];
+    const uint64_t h = block_hash(parent, r.tokens.data() + j * bs, bs);
+    pool_.set_hash(r.blocks[j], h);
+    r.block_hashes.push_back(h);
+  }
+}
+
+StepPlan Scheduler::schedule() {
+  StepPlan plan;
+  if (waiting_.empty() && running_.empty()) return plan;
+  ++step_;
+  struct Item {
+    Request* r;
+    int start, q;
+    bool samples;
+  };
+  std::vector<Item> items;
+  items.reserve(running_.size() + 16);
+  int budget = cfg_.max_num_batched_tokens;
+  bool preempted = false;
+
+  for (size_t i = 0; i < running_.size() && budget > 0; ++i) {
+    Request& r = reqs_.at(running_[i]);
+    const int remaining = (int)r.tokens.size() - r.num_computed;
+    if (remaining <= 0) continue;
+    int q = std::min(remaining, budget);
+    if (cfg_.long_prefill_threshold > 0 && q > 1) q = std::min(q, cfg_.long_prefill_threshold);
+    if (!cfg_.chunked_prefill && q < remaining) continue;
+    bool self_preempted = false;
+    while (!ensure_blocks(r, r.num_computed + q)) {
+      const int64_t victim = running_.back();
+      running_.pop_back();
+      preempted = true;
+      plan.num_preempted++;
+      preempt(reqs_.at(victim));
+      if (victim == r.id) {
+        self_preempted = true;
+        break;
+      }
+    }
+    if (self_preempted) break;
+    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size()});
+    budget -= q;
+  }
+
+  while (!preempted && !waiting_.empty() && budget > 0 &&
+         (int)running_.size() < cfg_.max_num_seqs) {
+    Request& r = reqs_.at(waiting_.front());
+    if (r.num_computed == 0 && r.blocks.empty()) admit_prefix(r);
+    const int remaining = (int)r.tokens.size() - r.num_computed;
+    int q = std::min(remaining, budget);
+    if (cfg_.long_prefill_threshold > 0 && q > 1) q = std::min(q, cfg_.long_prefill_threshold);
+    if (!cfg_.chunked_prefill && q < remaining) break;
+    if (!ensure_blocks(r, r.num_computed + q)) break;
+    waiting_.pop_front();
+    r.status = kRunning;
+    running_.push_back(r.id);
+    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size()});
+    budget -= q;
+  }
+
+  // decodes (one query token) first, then prefills; stable within each class
+  std::stable_partition(items.begin(), items.end(), [](const Item& it) { return it.q == 1; });
+
+  const int bs = cfg_.block_size;
+  int t = 0, s = 0;
+  buf_.cu_q[0] = 0;
+  last_sample_ids_.clear();
+  for (size_t i = 0; i < items.size(); ++i) {
+    Item& it = items[i];
+    Request& r = *it.r;
+    for (int j = 0; j < it.q; ++j) {
+      const int pos = it.start + j;
+      buf_.input_ids[t] = r.tokens[pos];
+      buf_.positions[t] = pos;
+      buf_.slot_mapping[t] = r.blocks[pos / bs] * bs + pos % bs;
+      ++t;
+    }
+    buf_.cu_q[i + 1] = t;
+    const int seq_len = it.start + it.q;
+    buf_.seq_lens[i] = seq_len;
+    plan.max_seq_len = std::max(plan.max_seq_len, seq_len);
+    std::copy(r.blocks.begin(), r.blocks.end(),
+              buf_.block_tables + (int64_t)i * cfg_.max_blocks_per_seq);
+    if (it.q == 1)
+      plan.num_decodes++;
+    else {
+      plan.num_prefills++;
+      plan.num_prefill_tokens += it.q;
+    }
+    if (it.samples) {
+      buf_.logits_idx[s] = t - 1;
+      buf_.temperature[s] = r.sp.temperature;
+      buf_.top_k[s] = r.sp.top_k;
+      buf_.top_p[s] = r.sp.top_p;
+      buf_.min_p[s] = r.sp.min_p;
+      buf_.seeds[s] = r.sp.seed;
+      buf_.steps[s] = r.num_output();
+      if (r.sp.temperature > 0.f) plan.all_greedy = false;
+      if (r.sp.temperature > 0.f && (r.sp.top_k > 0 || r.sp.top_p < 1.f || r.sp.min_p > 0.f))
+        plan.any_filter = true;
+      last_sample_ids_.push_back(r.id);
+      ++s;
+    }
+    r.num_computed = seq_len;
+    register_full_blocks(r);
+  }
+  plan.num_tokens = t;
+  plan.num_reqs = (int)items.size();
+  plan.num_samples = s;
+  plan.sample_req_ids = last_sample_ids_;
+  return plan;
+}
+
+std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, int n) {
+  if (n != (int)last_sample_ids_.size())
+    throw std::runtime_error("scheduler.update: expected " +
+                             std::to_string(last_sample_ids_.size()) + " tokens, got " +
+                             std::to_string(n));
+  std::vector<std::pair<int64_t, int>> finished;
+  for (int k = 0; k < n; ++k) {
+    auto itr = reqs_.find(last_sample_ids_[k]);
+    if (itr == reqs_.end()) continue;
+    Request& r = itr->second;
+    if (r.status != kRunning) continue;  // aborted or preempted while in flight
+    const int32_t tok = (int32_t)sampled[k];
+    r.tokens.push_back(tok);
+    if (r.first_token_step < 0) r.first_token_step = step_;
+    const int out = r.num_output();
+    FinishReason why = kNotFinished;
+    const bool may_stop = out >= r.sp.min_tokens;
+    if (may_stop && !r.sp.ignore_eos && tok == r.sp.eos_id) why = kStop;
+    if (may_stop && why == kNotFinished &&
+        std::find(r.sp.stop_ids.begin(), r.sp.stop_ids.end(), tok) != r.sp.stop_ids.end())
+      why = kStop;
+    if (why == kNotFinished &&
+        (out >= r.sp.max_tokens || (int)r.tokens.size() >= cfg_.max_model_len))
+      why = kLength;
+    if (why != kNotFinished) {
+      r.status = kFinished;
+      r.reason = why;
+      r.finish_step = step_;
+      free_request_blocks(r);
+      finished.emplace_back(r.id, (int)why);
+    }
+  }
+  if (!finished.empty()) {
+    running_.erase(std::remove_if(running_.begin(), running_.end(),
+                                  [this](int64_t id) { return reqs_.at(id).status == kFinished; }),
+                   running_.end());
+  }
+  last_sample_ids_.clear();
+  return finished;
+}
+
+std::vector<int32_t> Scheduler::output_tokens(int64_t id) const {
+  auto it = reqs_.find(id);
+  if (it == reqs_.end()) return {};
+  const Request& r = it->second;
+  return std::vector<int32_t>(r.tokens.begin() + r.num_prompt, r.tokens.end());
+}
+
+const Request* Scheduler::get(int64_t id) const {
+  auto it = reqs_.find(id);
+  return it == reqs_.end() ? nullptr : &it->second;
+}
+
+void Scheduler::forget(int64_t id) {
+  auto it = reqs_.find(id);
+  if (it != reqs_.end() && it->second.status == kFinished) reqs_.erase(it);
+}
+
+}  // namespace rt
+}  // namespace b200

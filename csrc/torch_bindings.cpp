@@ -1,0 +1,478 @@
+// torch.ops.b200.* registration for the sm_100a kernels, plus pybind11 helpers.
+//
+// This is the only translation unit that includes torch headers next to the kernel launchers:
+// it checks devices, dtypes, shapes, strides and alignment, then calls the plain-C++ launchers
+// declared in b200_kernels.h on the current CUDA stream.  Mirrors the role of the reference's
+// csrc/musa/torch_bindings.cpp:9-275 (`_C_musa_ops` schemas); the op set is this framework's.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+#include <torch/library.h>
+
+#include <mutex>
+
+#include "b200_kernels.h"
+
+namespace {
+
+using at::Tensor;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+#define CHECK_ROWMAJOR(x) TORCH_CHECK((x).dim() == 2 && (x).stride(1) == 1, #x " must be 2-D, rows contiguous")
+
+cudaStream_t stream_of(const Tensor& t) { return at::cuda::getCurrentCUDAStream(t.device().index()); }
+
+// ---- per-device error word (bounded waits record timeouts here) ----
+std::mutex g_err_mu;
+Tensor g_err[64];
+
+Tensor error_word_for(const at::Device& dev) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  const int i = dev.index();
+  TORCH_CHECK(i >= 0 && i < 64, "device index out of range");
+  if (!g_err[i].defined())
+    g_err[i] = at::zeros({4}, at::TensorOptions().dtype(at::kInt).device(dev));
+  return g_err[i];
+}
+int* err_ptr(const Tensor& t) { return error_word_for(t.device()).data_ptr<int>(); }
+
+template <typename F>
+void guarded(F&& f) {
+  try {
+    f();
+  } catch (const std::runtime_error& e) {
+    TORCH_CHECK(false, e.what());
+  }
+}
+
+// ------------------------------------------------------------------------------------- GEMM
+void gemm_bf16(const Tensor& A, const Tensor& B, Tensor& C, int64_t mode, int64_t bn,
+               int64_t splits, const c10::optional<Tensor>& workspace) {
+  CHECK_CUDA(A);
+  CHECK_CUDA(B);
+  CHECK_CUDA(C);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  CHECK_ROWMAJOR(C);
+  TORCH_CHECK(A.size(1) == B.size(1), "gemm_bf16: K mismatch");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == (mode == 1 ? N / 2 : N), "gemm_bf16: C shape");
+  TORCH_CHECK(C.scalar_type() == (mode == 2 ? at::kFloat : at::kBFloat16), "gemm_bf16: C dtype");
+  const c10::cuda::CUDAGuard g(A.device());
+  b200::gemm::GemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = mode;
+  a.bn = bn;
+  a.splits = splits;
+  if (workspace.has_value()) {
+    TORCH_CHECK(workspace->scalar_type() == at::kFloat && workspace->is_cuda(), "workspace");
+    a.workspace = workspace->data_ptr<float>();
+    a.workspace_numel = workspace->numel();
+  }
+  a.err = err_ptr(A);
+  guarded([&] { b200::gemm::run_bf16(a, stream_of(A)); });
+}
+
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
+  const auto p = b200::gemm::plan_bf16(M, N, K);
+  return {p.bn, p.splits, p.workspace_floats};
+}
+
+// ------------------------------------------------------------------------------------- norms
+void rms_norm(Tensor& out, const Tensor& x, const Tensor& w, double eps, bool gemma) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_ROWMAJOR(x);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(w.is_contiguous() && w.numel() == x.size(1), "rms_norm: weight");
+  const c10::cuda::CUDAGuard g(x.device());
+  b200::norm::RmsNormArgs a{};
+  a.out = out.data_ptr();
+  a.ld_out = out.stride(0);
+  a.x = const_cast<void*>(x.data_ptr());
+  a.ld_x = x.stride(0);
+  a.residual = nullptr;
+  a.weight = w.data_ptr();
+  a.rows = x.size(0);
+  a.H = x.size(1);
+  a.eps = eps;
+  a.gemma = gemma;
+  guarded([&] { b200::norm::run_rms_norm(a, stream_of(x)); });
+}
+
+void fused_add_rms_norm(Tensor& x, Tensor& residual, const Tensor& w, double eps, bool gemma) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(residual);
+  CHECK_BF16(w);
+  CHECK_ROWMAJOR(x);
+  CHECK_ROWMAJOR(residual);
+  TORCH_CHECK(x.sizes() == residual.sizes(), "fused_add_rms_norm: shape mismatch");
+  TORCH_CHECK(w.is_contiguous() && w.numel() == x.size(1), "fused_add_rms_norm: weight");
+  const c10::cuda::CUDAGuard g(x.device());
+  b200::norm::RmsNormArgs a{};
+  a.out = x.data_ptr();
+  a.ld_out = x.stride(0);
+  a.x = x.data_ptr();
+  a.ld_x = x.stride(0);
+  a.residual = residual.data_ptr();
+  a.ld_res = residual.stride(0);
+  a.weight = w.data_ptr();
+  a.rows = x.size(0);
+  a.H = x.size(1);
+  a.eps = eps;
+  a.gemma = gemma;
+  guarded([&] { b200::norm::run_rms_norm(a, stream_of(x)); });
+}
+
+void rms_norm_gated(Tensor& out, const Tensor& x, const Tensor& z, const Tensor& w, int64_t group,
+                    double eps) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(z);
+  CHECK_BF16(w);
+  TORCH_CHECK(x.is_contiguous() && z.is_contiguous() && out.is_contiguous(), "rms_norm_gated");
+  TORCH_CHECK(w.numel() == group, "rms_norm_gated: weight must have `group` elements");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int H = x.size(-1);
+  const int rows = x.numel() / H;
+  guarded([&] {
+    b200::norm::run_rms_norm_gated(out.data_ptr(), x.data_ptr(), z.data_ptr(), w.data_ptr(), rows,
+                                   H, group, eps, stream_of(x));
+  });
+}
+
+// ------------------------------------------------------------------------------------- act
+void act_and_mul(Tensor& out, const Tensor& x, int64_t kind, double limit) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  CHECK_ROWMAJOR(out);
+  const int I = x.size(1) / 2;
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == I, "act_and_mul: out shape");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::act::run_act_and_mul(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), x.size(0),
+                               I, kind, limit, stream_of(x));
+  });
+}
+
+void silu_mul_fp8_quant(Tensor& out, Tensor& scales, const Tensor& x) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  const int I = x.size(1) / 2;
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.is_contiguous() &&
+                  out.size(0) == x.size(0) && out.size(1) == I,
+              "silu_mul_fp8_quant: out");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.is_contiguous() &&
+                  scales.numel() == x.size(0) * (I / 128),
+              "silu_mul_fp8_quant: scales");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::act::run_silu_mul_fp8_quant(out.data_ptr(), scales.data_ptr<float>(), x.data_ptr(),
+                                      x.stride(0), x.size(0), I, stream_of(x));
+  });
+}
+
+void group_quant_fp8(Tensor& out, Tensor& scales, const Tensor& x) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  const int K = x.size(1);
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.is_contiguous() &&
+                  out.sizes() == x.sizes(),
+              "group_quant_fp8: out");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.numel() == x.size(0) * (K / 128),
+              "group_quant_fp8: scales");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::act::run_group_quant_fp8(out.data_ptr(), scales.data_ptr<float>(), x.data_ptr(),
+                                   x.stride(0), x.size(0), K, stream_of(x));
+  });
+}
+
+// ------------------------------------------------------------------------------------- rope+kv
+void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
+             const c10::optional<Tensor>& q_norm_w, const c10::optional<Tensor>& k_norm_w,
+             Tensor& k_cache, Tensor& v_cache, const Tensor& slot_mapping, int64_t Hq, int64_t Hkv,
+             int64_t rot_dim, bool neox, double eps) {
+  CHECK_CUDA(qkv);
+  CHECK_BF16(qkv);
+  CHECK_ROWMAJOR(qkv);
+  CHECK_BF16(k_cache);
+  CHECK_BF16(v_cache);
+  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.is_contiguous(), "positions int32");
+  TORCH_CHECK(slot_mapping.scalar_type() == at::kInt && slot_mapping.is_contiguous(),
+              "slot_mapping int32");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() &&
+                  cos_sin.size(1) == rot_dim,
+              "cos_sin must be fp32 [max_pos, rot_dim]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "kv cache must be contiguous [blocks, Hkv, block_size, D]");
+  const int T = qkv.size(0);
+  const int D = k_cache.size(3);
+  TORCH_CHECK(qkv.size(1) >= (Hq + 2 * Hkv) * D, "rope_kv: qkv width");
+  TORCH_CHECK(k_cache.size(1) == Hkv, "rope_kv: cache heads");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  b200::rope::RopeKvArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.ld_qkv = qkv.stride(0);
+  a.positions = positions.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.q_norm_w = q_norm_w.has_value() ? q_norm_w->data_ptr() : nullptr;
+  a.k_norm_w = k_norm_w.has_value() ? k_norm_w->data_ptr() : nullptr;
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.slot_mapping = slot_mapping.data_ptr<int32_t>();
+  a.T = T;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = D;
+  a.block_size = k_cache.size(2);
+  a.rot_dim = rot_dim;
+  a.neox = neox;
+  a.eps = eps;
+  a.err = err_ptr(qkv);
+  guarded([&] { b200::rope::run_rope_kv(a, stream_of(qkv)); });
+}
+
+// ------------------------------------------------------------------------------------- attention
+void paged_decode(const Tensor& q, Tensor& out, const Tensor& k_cache, const Tensor& v_cache,
+                  const Tensor& block_tables, const Tensor& seq_lens, int64_t Hq, int64_t Hkv,
+                  int64_t max_seq_len, double scale, int64_t num_splits,
+                  const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_ROWMAJOR(q);
+  CHECK_ROWMAJOR(out);
+  CHECK_BF16(k_cache);
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.dim() == 4,
+              "kv cache layout");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.stride(1) == 1, "block_tables");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.is_contiguous(), "seq_lens");
+  const int D = k_cache.size(3);
+  const int B = q.size(0);
+  TORCH_CHECK(seq_lens.numel() >= B && block_tables.size(0) >= B, "decode: batch");
+  TORCH_CHECK(q.size(1) >= Hq * D && out.size(1) >= Hq * D, "decode: widths");
+  const c10::cuda::CUDAGuard g(q.device());
+  b200::attn::DecodeArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = q.stride(0);
+  a.o = out.data_ptr();
+  a.ld_o = out.stride(0);
+  a.k_cache = const_cast<void*>(k_cache.data_ptr());
+  a.v_cache = const_cast<void*>(v_cache.data_ptr());
+  a.num_blocks = k_cache.size(0);
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.bt_stride = block_tables.stride(0);
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = D;
+  a.block_size = k_cache.size(2);
+  a.max_seq_len = max_seq_len;
+  a.num_splits = num_splits;
+  a.scale = scale;
+  if (num_splits > 1) {
+    TORCH_CHECK(ws_o.has_value() && ws_lse.has_value(), "decode: split workspace required");
+    TORCH_CHECK(ws_o->numel() >= (int64_t)B * Hq * num_splits * D &&
+                    ws_lse->numel() >= (int64_t)B * Hq * num_splits,
+                "decode: split workspace too small");
+    a.ws_o = ws_o->data_ptr<float>();
+    a.ws_lse = ws_lse->data_ptr<float>();
+  }
+  a.err = err_ptr(q);
+  guarded([&] { b200::attn::run_decode(a, stream_of(q)); });
+}
+
+void paged_prefill(const Tensor& q, Tensor& out, const Tensor& k_cache, const Tensor& v_cache,
+                   const Tensor& cu_q, const Tensor& seq_lens, const Tensor& block_tables,
+                   Tensor& tile_offsets, int64_t Hq, int64_t Hkv, double scale, int64_t window) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_ROWMAJOR(q);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.dim() == 4,
+              "kv cache layout");
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  block_tables.scalar_type() == at::kInt && tile_offsets.scalar_type() == at::kInt,
+              "prefill: int32 metadata");
+  const int R = seq_lens.numel();
+  TORCH_CHECK(cu_q.numel() >= R + 1 && tile_offsets.numel() >= R + 1, "prefill: metadata sizes");
+  const c10::cuda::CUDAGuard g(q.device());
+  b200::attn::PrefillArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = q.stride(0);
+  a.o = out.data_ptr();
+  a.ld_o = out.stride(0);
+  a.k_cache = const_cast<void*>(k_cache.data_ptr());
+  a.v_cache = const_cast<void*>(v_cache.data_ptr());
+  a.num_blocks = k_cache.size(0);
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.bt_stride = block_tables.stride(0);
+  a.tile_offsets = tile_offsets.data_ptr<int32_t>();
+  a.T = q.size(0);
+  a.R = R;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = k_cache.size(3);
+  a.block_size = k_cache.size(2);
+  a.window = window;
+  a.scale = scale;
+  a.err = err_ptr(q);
+  guarded([&] { b200::attn::run_prefill(a, stream_of(q)); });
+}
+
+int64_t decode_num_splits(int64_t B, int64_t Hkv, int64_t max_seq_len) {
+  return b200::attn::decode_num_splits(B, Hkv, max_seq_len);
+}
+
+// ------------------------------------------------------------------------------------- sampling
+void sample(const Tensor& logits, const c10::optional<Tensor>& temperature,
+            const c10::optional<Tensor>& top_k, const c10::optional<Tensor>& top_p,
+            const c10::optional<Tensor>& min_p, const c10::optional<Tensor>& seeds,
+            const c10::optional<Tensor>& steps, int64_t vocab_offset, Tensor& out_idx,
+            const c10::optional<Tensor>& out_val) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat, "sample: fp32 logits");
+  CHECK_ROWMAJOR(logits);
+  TORCH_CHECK(out_idx.scalar_type() == at::kLong && out_idx.numel() >= logits.size(0), "out_idx");
+  const c10::cuda::CUDAGuard g(logits.device());
+  b200::sampling::SampleArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.R = logits.size(0);
+  a.V = logits.size(1);
+  a.vocab_offset = vocab_offset;
+  a.temperature = temperature.has_value() ? temperature->data_ptr<float>() : nullptr;
+  a.top_k = top_k.has_value() ? top_k->data_ptr<int32_t>() : nullptr;
+  a.top_p = top_p.has_value() ? top_p->data_ptr<float>() : nullptr;
+  a.min_p = min_p.has_value() ? min_p->data_ptr<float>() : nullptr;
+  a.seeds = seeds.has_value() ? seeds->data_ptr<int64_t>() : nullptr;
+  a.steps = steps.has_value() ? steps->data_ptr<int32_t>() : nullptr;
+  a.out_idx = out_idx.data_ptr<int64_t>();
+  a.out_val = out_val.has_value() ? out_val->data_ptr<float>() : nullptr;
+  guarded([&] { b200::sampling::run_sample(a, stream_of(logits)); });
+}
+
+void merge_candidates(const Tensor& vals, const Tensor& idx, Tensor& out) {
+  CHECK_CUDA(vals);
+  TORCH_CHECK(vals.scalar_type() == at::kFloat && idx.scalar_type() == at::kLong &&
+                  vals.is_contiguous() && idx.is_contiguous() && vals.dim() == 2,
+              "merge_candidates: [S, R] fp32 / int64");
+  const c10::cuda::CUDAGuard g(vals.device());
+  guarded([&] {
+    b200::sampling::run_merge_candidates(vals.data_ptr<float>(), idx.data_ptr<int64_t>(),
+                                         vals.size(0), vals.size(1), out.data_ptr<int64_t>(),
+                                         stream_of(vals));
+  });
+}
+
+// ------------------------------------------------------------------------------------- misc
+void embedding(Tensor& out, const Tensor& table, const Tensor& ids, int64_t vocab_start) {
+  CHECK_CUDA(table);
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.scalar_type() == at::kInt &&
+                  ids.is_contiguous(),
+              "embedding: contiguous table/out, int32 ids");
+  TORCH_CHECK(table.element_size() == 2, "embedding: 16-bit table");
+  const c10::cuda::CUDAGuard g(table.device());
+  guarded([&] {
+    b200::misc::run_embedding(out.data_ptr(), table.data_ptr(), ids.data_ptr<int32_t>(),
+                              ids.numel(), table.size(1), table.size(0), vocab_start,
+                              stream_of(table));
+  });
+}
+
+void gather_rows(Tensor& out, const Tensor& x, const Tensor& idx) {
+  CHECK_CUDA(x);
+  CHECK_ROWMAJOR(x);
+  TORCH_CHECK(out.is_contiguous() && idx.scalar_type() == at::kInt && idx.is_contiguous(),
+              "gather_rows: int32 idx");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::misc::run_gather_rows(out.data_ptr(), x.data_ptr(), x.stride(0), idx.data_ptr<int32_t>(),
+                                idx.numel(), x.size(1), x.element_size(), stream_of(x));
+  });
+}
+
+Tensor error_word(const Tensor& like) { return error_word_for(like.device()); }
+
+}  // namespace
+
+TORCH_LIBRARY(b200, m) {
+  m.def(
+      "gemm_bf16(Tensor A, Tensor B, Tensor(a!) C, int mode=0, int bn=0, int splits=0, "
+      "Tensor? workspace=None) -> ()");
+  m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps, bool gemma=False) -> ()");
+  m.def(
+      "fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor weight, float eps, "
+      "bool gemma=False) -> ()");
+  m.def(
+      "rms_norm_gated(Tensor(a!) out, Tensor x, Tensor z, Tensor weight, int group, float eps) -> ()");
+  m.def("act_and_mul(Tensor(a!) out, Tensor x, int kind=0, float limit=0.0) -> ()");
+  m.def("silu_mul_fp8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
+  m.def("group_quant_fp8(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
+  m.def(
+      "rope_kv(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor? q_norm_w, Tensor? "
+      "k_norm_w, Tensor(b!) k_cache, Tensor(c!) v_cache, Tensor slot_mapping, int num_q_heads, "
+      "int num_kv_heads, int rot_dim, bool neox=True, float eps=1e-6) -> ()");
+  m.def(
+      "paged_decode(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor "
+      "block_tables, Tensor seq_lens, int num_q_heads, int num_kv_heads, int max_seq_len, float "
+      "scale, int num_splits=1, Tensor(b!)? ws_o=None, Tensor(c!)? ws_lse=None) -> ()");
+  m.def(
+      "paged_prefill(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor cu_q, "
+      "Tensor seq_lens, Tensor block_tables, Tensor(b!) tile_offsets, int num_q_heads, int "
+      "num_kv_heads, float scale, int window=0) -> ()");
+  m.def(
+      "sample(Tensor logits, Tensor? temperature, Tensor? top_k, Tensor? top_p, Tensor? min_p, "
+      "Tensor? seeds, Tensor? steps, int vocab_offset, Tensor(a!) out_idx, Tensor(b!)? "
+      "out_val=None) -> ()");
+  m.def("merge_candidates(Tensor vals, Tensor idx, Tensor(a!) out) -> ()");
+  m.def("embedding(Tensor(a!) out, Tensor table, Tensor ids, int vocab_start=0) -> ()");
+  m.def("gather_rows(Tensor(a!) out, Tensor x, Tensor idx) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(b200, CUDA, m) {
+  m.impl("gemm_bf16", &gemm_bf16);
+  m.impl("rms_norm", &rms_norm);
+  m.impl("fused_add_rms_norm", &fused_add_rms_norm);
+  m.impl("rms_norm_gated", &rms_norm_gated);
+  m.impl("act_and_mul", &act_and_mul);
+  m.impl("silu_mul_fp8_quant", &silu_mul_fp8_quant);
+  m.impl("group_quant_fp8", &group_quant_fp8);
+  m.impl("rope_kv", &rope_kv);
+  m.impl("paged_decode", &paged_decode);
+  m.impl("paged_prefill", &paged_prefill);
+  m.impl("sample", &sample);
+  m.impl("merge_candidates", &merge_candidates);
+  m.impl("embedding", &embedding);
+  m.impl("gather_rows", &gather_rows);
+}
+
+void register_runtime(pybind11::module_& m);  // csrc/runtime/bindings.cpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "vllm_musa_b200 native extension (sm_100a kernels + host runtime)";
+  m.def("gemm_plan", &gemm_plan, "automatic (bn, splits, workspace_floats) for a bf16 GEMM");
+  m.def("decode_num_splits", &decode_num_splits, "split-KV count for a decode batch");
+  m.def("error_word", &error_word, "per-device error word of the bounded waits");
+  m.attr("BUILT_ARCH") = "sm_100a";
+  register_runtime(m);
+}

@@ -1,0 +1,244 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references of the same op."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from vllm_musa_b200 import ops
+from vllm_musa_b200.ops import _ext
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _check_errors():
+    yield
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        _ext.check_device_errors()
+
+
+def _bf(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).to(DEV)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (7, 4096, 4096), (128, 512, 256), (200, 1000, 4096),
+                                   (256, 6144, 4096), (1024, 2048, 1024), (4096, 4096, 4096),
+                                   (300, 128256 // 8, 4096)])
+def test_gemm_bf16(M, N, K):
+    a, b = _bf(M, K, seed=1), _bf(N, K, seed=2, scale=0.05)
+    ref = a.float() @ b.float().t()
+    out = ops.linear(a, b)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item() / 4 + 1e-2)
+
+
+@pytest.mark.parametrize("bn,splits", [(64, 1), (128, 1), (256, 1), (128, 3), (256, 4), (64, 8)])
+def test_gemm_bf16_forced_plans(bn, splits):
+    M, N, K = 250, 768, 2048
+    a, b = _bf(M, K, seed=3), _bf(N, K, seed=4, scale=0.05)
+    ref = a.float() @ b.float().t()
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm._run(a, b, out, 0, bn, splits)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
+
+
+def test_gemm_fp32_out_and_strided_a():
+    M, N, K = 64, 1000, 512
+    big = _bf(M, K + 64, seed=5)
+    a = big[:, 32:32 + K]
+    b = _bf(N, K, seed=6, scale=0.05)
+    out = ops.linear(a, b, out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    torch.testing.assert_close(out, a.float() @ b.float().t(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("M,I,K", [(5, 688, 256), (256, 1792, 4096), (1000, 512, 1024)])
+def test_gemm_silu_mul_epilogue(M, I, K):
+    x = _bf(M, K, seed=7)
+    g, u = _bf(I, K, seed=8, scale=0.05), _bf(I, K, seed=9, scale=0.05)
+    w = ops.interleave_gate_up(g, u)
+    out = ops.linear_silu_mul(x, w)
+    ref = torch.nn.functional.silu(x.float() @ g.float().t()) * (x.float() @ u.float().t())
+    torch.testing.assert_close(out[:, :I].float(), ref, rtol=2e-2, atol=2e-2)
+    assert out.shape[1] >= I
+
+
+@pytest.mark.parametrize("rows,H", [(1, 256), (33, 4096), (256, 2048), (7, 7168), (4, 5120)])
+def test_rms_norm_and_fused_add(rows, H):
+    x, r, w = _bf(rows, H, seed=1), _bf(rows, H, seed=2), _bf(H, seed=3)
+    y = ops.rms_norm(x, w, 1e-6)
+    ref = ops.norm._rms_ref(x.cpu(), w.cpu(), 1e-6, False)
+    torch.testing.assert_close(y.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+    x2, r2 = x.clone(), r.clone()
+    ops.fused_add_rms_norm(x2, r2, w, 1e-6)
+    xc, rc = x.cpu().clone(), r.cpu().clone()
+    ops.fused_add_rms_norm(xc, rc, w.cpu(), 1e-6)
+    torch.testing.assert_close(r2.cpu(), rc, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(x2.cpu().float(), xc.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_rms_norm_gated():
+    x, z, w = _bf(8, 4096, seed=1), _bf(8, 4096, seed=2), _bf(128, seed=3)
+    y = ops.rms_norm_gated(x, z, w, 128, 1e-6)
+    ref = ops.rms_norm_gated(x.cpu(), z.cpu(), w.cpu(), 128, 1e-6)
+    torch.testing.assert_close(y.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_act_and_mul():
+    x = _bf(17, 2 * 768, seed=4)
+    for kind in (0, 1):
+        y = ops.act_and_mul(x, kind)
+        ref = ops.act_and_mul(x.cpu(), kind)
+        torch.testing.assert_close(y.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def _make_cache(nb, Hkv, bs, D, seed=0):
+    k = _bf(nb, Hkv, bs, D, seed=seed)
+    v = _bf(nb, Hkv, bs, D, seed=seed + 1)
+    return k, v
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,rot,neox,qknorm", [(128, 32, 8, 128, True, False),
+                                                      (128, 32, 4, 128, True, True),
+                                                      (64, 4, 2, 64, True, False),
+                                                      (256, 16, 2, 64, True, True),
+                                                      (128, 8, 8, 64, False, False)])
+def test_rope_kv(D, Hq, Hkv, rot, neox, qknorm):
+    T, bs, nb = 37, 16, 8
+    qkv = _bf(T, (Hq + 2 * Hkv) * D, seed=5)
+    pos = torch.randint(0, 500, (T,), dtype=torch.int32)
+    slots = torch.randperm(nb * bs)[:T].to(torch.int32)
+    slots[3] = -1
+    cs = ops.build_cos_sin_cache(rot, 1024, 10000.0)
+    qn = _bf(D, seed=6) if qknorm else None
+    kn = _bf(D, seed=7) if qknorm else None
+    kc, vc = torch.zeros(nb, Hkv, bs, D, dtype=torch.bfloat16), torch.zeros(nb, Hkv, bs, D, dtype=torch.bfloat16)
+    q_cpu = qkv.cpu().clone()
+    ops.rope_kv(q_cpu, pos, cs, kc, vc, slots, Hq, Hkv, rot, neox,
+                qn.cpu() if qn is not None else None, kn.cpu() if kn is not None else None)
+    kg, vg = kc.zero_().to(DEV), vc.zero_().to(DEV)
+    kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+    ops.rope_kv(q_cpu.clone(), pos, cs, kc2, vc2, slots, Hq, Hkv, rot, neox,
+                qn.cpu() if qn is not None else None, kn.cpu() if kn is not None else None)
+    q_gpu = qkv.clone()
+    ops.rope_kv(q_gpu, pos.to(DEV), cs.to(DEV), kg, vg, slots.to(DEV), Hq, Hkv, rot, neox, qn, kn)
+    torch.testing.assert_close(q_gpu[:, :Hq * D].cpu().float(), q_cpu[:, :Hq * D].float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(kg.cpu().float(), kc2.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(vg.cpu().float(), vc2.float(), rtol=0, atol=0)
+
+
+def _random_tables(B, lens, bs, nb, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    maxb = max((l + bs - 1) // bs for l in lens)
+    perm = torch.randperm(nb, generator=g)
+    bt = torch.zeros(B, maxb + 3, dtype=torch.int32)
+    used = 0
+    for b, l in enumerate(lens):
+        n = (l + bs - 1) // bs
+        bt[b, :n] = perm[used:used + n].to(torch.int32)
+        used += n
+    return bt
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,bs", [(128, 32, 8, 64), (128, 32, 4, 16), (64, 4, 2, 32),
+                                          (256, 16, 2, 64), (128, 64, 8, 128)])
+@pytest.mark.parametrize("splits", [1, 4])
+def test_paged_decode(D, Hq, Hkv, bs, splits):
+    lens = [1, 5, 64, 65, 200, 1000, 129, 3]
+    B = len(lens)
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=11)
+    bt = _random_tables(B, lens, bs, nb)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    q = _bf(B, (Hq + 2 * Hkv) * D, seed=12)
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_decode(q.cpu(), kc.cpu(), vc.cpu(), bt, sl, Hq, Hkv, scale, 1024)
+    out = ops.paged_decode(q, kc, vc, bt.to(DEV), sl.to(DEV), Hq, Hkv, scale, 1024, num_splits=splits)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,bs,window", [(128, 32, 8, 64, 0), (128, 8, 2, 16, 0), (64, 4, 4, 32, 0),
+                                                 (256, 16, 2, 64, 0), (128, 8, 2, 64, 100)])
+def test_paged_prefill_chunked(D, Hq, Hkv, bs, window):
+    # (context already cached, new tokens) per request
+    reqs = [(0, 1), (0, 70), (64, 64), (100, 3), (900, 130), (5, 1)]
+    R = len(reqs)
+    lens = [c + n for c, n in reqs]
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=21)
+    bt = _random_tables(R, lens, bs, nb, seed=3)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([n for _, n in reqs]), 0)), dtype=torch.int32)
+    T = int(cu[-1])
+    q = _bf(T, (Hq + 2 * Hkv) * D, seed=22)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale, window)
+    out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale, window)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_sampling_greedy_and_shards():
+    R, V = 64, 50000
+    logits = torch.randn(R, V, device=DEV) * 3
+    ids = ops.sample_tokens(logits)
+    assert torch.equal(ids.cpu(), logits.argmax(-1).cpu())
+    # vocab-parallel: 4 shards, merged candidates equal the unsharded draw (random and greedy)
+    temp = torch.full((R,), 0.8, device=DEV)
+    temp[::3] = 0
+    seeds = torch.arange(R, dtype=torch.int64, device=DEV) * 7919
+    steps = torch.full((R,), 5, dtype=torch.int32, device=DEV)
+    full = ops.sample_tokens(logits, temp, seeds=seeds, steps=steps)
+    shard = V // 4
+    vals, idxs = [], []
+    for s in range(4):
+        i, v = ops.sample_tokens(logits[:, s * shard:(s + 1) * shard].contiguous(), temp,
+                                 seeds=seeds, steps=steps, vocab_offset=s * shard, return_values=True)
+        vals.append(v)
+        idxs.append(i)
+    merged = torch.empty(R, dtype=torch.int64, device=DEV)
+    torch.ops.b200.merge_candidates(torch.stack(vals), torch.stack(idxs), merged)
+    assert torch.equal(merged, full)
+
+
+def test_sampling_distribution_and_filters():
+    V = 64
+    base = torch.randn(V) * 2
+    R = 4096
+    logits = base.repeat(R, 1).to(DEV)
+    temp = torch.full((R,), 1.0, device=DEV)
+    seeds = torch.arange(R, dtype=torch.int64, device=DEV)
+    steps = torch.zeros(R, dtype=torch.int32, device=DEV)
+    ids = ops.sample_tokens(logits, temp, seeds=seeds, steps=steps).cpu()
+    freq = torch.bincount(ids, minlength=V).float() / R
+    p = torch.softmax(base, -1)
+    assert (freq - p).abs().max() < 0.04
+    # top-k = 5: only the 5 largest appear
+    tk = torch.full((R,), 5, dtype=torch.int32, device=DEV)
+    ids = ops.sample_tokens(logits, temp, top_k=tk, seeds=seeds, steps=steps).cpu()
+    assert set(ids.tolist()) <= set(torch.topk(base, 5).indices.tolist())
+    # top-p = 0.5: support is the smallest prefix reaching 0.5 mass
+    tp = torch.full((R,), 0.5, device=DEV)
+    ids = ops.sample_tokens(logits, temp, top_p=tp, seeds=seeds, steps=steps).cpu()
+    keep = ops.sampling._filter_ref(base, 0, 0.5, 0.0)
+    assert set(ids.tolist()) <= set(torch.nonzero(keep).flatten().tolist())
+    # min-p
+    mp = torch.full((R,), 0.2, device=DEV)
+    ids = ops.sample_tokens(logits, temp, min_p=mp, seeds=seeds, steps=steps).cpu()
+    keep = ops.sampling._filter_ref(base, 0, 1.0, 0.2)
+    assert set(ids.tolist()) <= set(torch.nonzero(keep).flatten().tolist())
+
+
+def test_embedding_and_gather():
+    table = _bf(1000, 256, seed=1)
+    ids = torch.randint(0, 1000, (77,), dtype=torch.int32, device=DEV)
+    out = ops.embedding(ids, table)
+    assert torch.equal(out, table[ids.long()])
+    shard = ops.embedding(ids, table[500:].contiguous(), vocab_start=500)
+    ref = torch.where((ids.long() >= 500)[:, None], table[ids.long()], torch.zeros_like(out))
+    assert torch.equal(shard, ref)
+    x = _bf(50, 4096, seed=2)
+    idx = torch.tensor([0, 49, 3, 3], dtype=torch.int32, device=DEV)
+    assert torch.equal(ops.gather_rows(x, idx), x[idx.long()])

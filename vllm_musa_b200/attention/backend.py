@@ -1,0 +1,47 @@
+"""Paged attention backend: one object per attention layer geometry.
+
+Dispatches the step's decode rows to the split-KV decode kernel and its prefill rows to the
+chunked-prefill kernel (csrc/attention/paged_attention.cu).  Capabilities mirror what the
+reference's MUSA FlashAttention backend advertises (vllm_musa/v1/attention/backends/
+flash_attn.py:238-400): paged KV with 16/32/64/128-token pages, GQA, causal, sliding
+window; head dims 64/128/256.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+from .metadata import AttnMetadata
+
+
+class PagedAttention:
+    SUPPORTED_HEAD_DIMS = (64, 128, 256)
+    SUPPORTED_BLOCK_SIZES = (16, 32, 64, 128, 256)
+
+    def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int,
+                 scale: float | None = None, sliding_window: int = 0):
+        if head_dim not in self.SUPPORTED_HEAD_DIMS:
+            raise ValueError(f"head_dim {head_dim} not supported")
+        self.hq, self.hkv, self.d = num_heads, num_kv_heads, head_dim
+        self.scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+        self.window = sliding_window
+
+    def forward(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                meta: AttnMetadata, out: torch.Tensor | None = None) -> torch.Tensor:
+        """q: [T, >= Hq*D] (rows of the packed qkv buffer); K/V already written to the cache."""
+        T = q.shape[0]
+        if out is None:
+            out = torch.empty(T, self.hq * self.d, dtype=q.dtype, device=q.device)
+        nd, npf = meta.num_decodes, meta.num_prefills
+        if nd:
+            ops.paged_decode(q[:nd], k_cache, v_cache, meta.block_tables[:nd], meta.seq_lens[:nd],
+                             self.hq, self.hkv, self.scale, meta.max_seq_len, out=out[:nd],
+                             num_splits=meta.decode_splits)
+        if npf:
+            ops.paged_prefill(q, k_cache, v_cache, meta.prefill_cu_q, meta.prefill_seq_lens,
+                              meta.prefill_block_tables, self.hq, self.hkv, self.scale,
+                              self.window or meta.sliding_window, out=out,
+                              tile_scratch=meta.tile_scratch)
+        return out

@@ -1,0 +1,217 @@
+"""Engine configuration: model architecture, KV cache, scheduler, parallelism.
+
+The reference takes these from upstream vLLM's ``VllmConfig`` and mutates them in platform
+hooks (vllm_musa/platform.py:442-720: block size 64 pin, custom-op defaults, compile
+ranges).  Here they are plain dataclasses with B200 defaults: 64-token KV pages (one TMA box
+per page and head), chunked prefill with an 8K token budget, CUDA graphs for decode batches.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+from dataclasses import dataclass, field
+from typing import Any, Optional
+
+import torch
+
+
+@dataclass
+class ModelConfig:
+    arch: str = "llama"  # llama | qwen3 | qwen3_moe | deepseek_v3 | qwen3_next
+    vocab_size: int = 32000
+    hidden_size: int = 4096
+    num_layers: int = 32
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 14336
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    rope_scaling: Optional[dict] = None
+    rotary_dim: Optional[int] = None  # default head_dim
+    rope_neox: bool = True
+    max_position: int = 8192
+    tie_word_embeddings: bool = False
+    qk_norm: bool = False
+    attention_bias: bool = False
+    # mixture of experts
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    norm_topk_prob: bool = True
+    shared_expert_intermediate_size: int = 0
+    first_k_dense: int = 0
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+    scoring_func: str = "softmax"
+    # multi-head latent attention (DeepSeek)
+    q_lora_rank: int = 0
+    kv_lora_rank: int = 0
+    qk_nope_head_dim: int = 0
+    qk_rope_head_dim: int = 0
+    v_head_dim: int = 0
+    index_n_heads: int = 0
+    index_head_dim: int = 0
+    index_topk: int = 0
+    num_nextn_predict_layers: int = 0
+    quant: Optional[str] = None  # None | "fp8_block"
+    # hybrid linear attention (Qwen3-Next)
+    full_attention_interval: int = 0
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 0
+    linear_value_head_dim: int = 0
+    linear_conv_kernel_dim: int = 4
+    partial_rotary_factor: float = 1.0
+    attn_output_gate: bool = False
+    eos_token_id: Optional[int] = None
+    dtype: torch.dtype = torch.bfloat16
+    name: str = ""
+
+    @property
+    def rot_dim(self) -> int:
+        if self.rotary_dim:
+            return self.rotary_dim
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def num_params(self) -> int:
+        """Approximate parameter count (dense and MoE decoders)."""
+        H, L, V = self.hidden_size, self.num_layers, self.vocab_size
+        attn = H * (self.num_heads + 2 * self.num_kv_heads) * self.head_dim + \
+            self.num_heads * self.head_dim * H
+        if self.is_moe:
+            mlp = self.num_experts * 3 * H * self.moe_intermediate_size + H * self.num_experts
+            mlp += 3 * H * self.shared_expert_intermediate_size
+        else:
+            mlp = 3 * H * self.intermediate_size
+        emb = V * H * (1 if self.tie_word_embeddings else 2)
+        return L * (attn + mlp) + emb
+
+    @staticmethod
+    def from_hf(config: "str | dict") -> "ModelConfig":
+        """Build from a HuggingFace ``config.json`` (path, directory or dict)."""
+        if isinstance(config, str):
+            path = os.path.join(config, "config.json") if os.path.isdir(config) else config
+            with open(path) as f:
+                hf = json.load(f)
+        else:
+            hf = dict(config)
+        archs = hf.get("architectures") or [""]
+        a = archs[0]
+        mt = hf.get("model_type", "")
+        if "Qwen3Next" in a or mt == "qwen3_next":
+            arch = "qwen3_next"
+        elif "Qwen3Moe" in a or mt == "qwen3_moe":
+            arch = "qwen3_moe"
+        elif "Qwen3" in a or mt == "qwen3":
+            arch = "qwen3"
+        elif "Deepseek" in a or mt.startswith("deepseek"):
+            arch = "deepseek_v3"
+        else:
+            arch = "llama"
+        H = hf["hidden_size"]
+        nh = hf["num_attention_heads"]
+        c = ModelConfig(
+            arch=arch,
+            vocab_size=hf["vocab_size"],
+            hidden_size=H,
+            num_layers=hf["num_hidden_layers"],
+            num_heads=nh,
+            num_kv_heads=hf.get("num_key_value_heads", nh),
+            head_dim=hf.get("head_dim") or H // nh,
+            intermediate_size=hf.get("intermediate_size", 4 * H),
+            rms_norm_eps=hf.get("rms_norm_eps", 1e-6),
+            rope_theta=hf.get("rope_theta", 10000.0),
+            rope_scaling=hf.get("rope_scaling"),
+            max_position=hf.get("max_position_embeddings", 8192),
+            tie_word_embeddings=hf.get("tie_word_embeddings", False),
+            qk_norm=arch in ("qwen3", "qwen3_moe", "qwen3_next"),
+            attention_bias=hf.get("attention_bias", False),
+            num_experts=hf.get("num_experts", hf.get("n_routed_experts", 0)) or 0,
+            num_experts_per_tok=hf.get("num_experts_per_tok", 0) or 0,
+            moe_intermediate_size=hf.get("moe_intermediate_size", 0) or 0,
+            norm_topk_prob=hf.get("norm_topk_prob", True),
+            shared_expert_intermediate_size=hf.get("shared_expert_intermediate_size", 0) or
+            (hf.get("n_shared_experts", 0) or 0) * (hf.get("moe_intermediate_size", 0) or 0),
+            first_k_dense=hf.get("first_k_dense_replace", 0) or 0,
+            n_group=hf.get("n_group", 1) or 1,
+            topk_group=hf.get("topk_group", 1) or 1,
+            routed_scaling_factor=hf.get("routed_scaling_factor", 1.0) or 1.0,
+            scoring_func=hf.get("scoring_func", "softmax"),
+            q_lora_rank=hf.get("q_lora_rank", 0) or 0,
+            kv_lora_rank=hf.get("kv_lora_rank", 0) or 0,
+            qk_nope_head_dim=hf.get("qk_nope_head_dim", 0) or 0,
+            qk_rope_head_dim=hf.get("qk_rope_head_dim", 0) or 0,
+            v_head_dim=hf.get("v_head_dim", 0) or 0,
+            index_n_heads=hf.get("index_n_heads", 0) or 0,
+            index_head_dim=hf.get("index_head_dim", 0) or 0,
+            index_topk=hf.get("index_topk", 0) or 0,
+            num_nextn_predict_layers=hf.get("num_nextn_predict_layers", 0) or 0,
+            full_attention_interval=hf.get("full_attention_interval", 0) or 0,
+            linear_num_key_heads=hf.get("linear_num_key_heads", 0) or 0,
+            linear_num_value_heads=hf.get("linear_num_value_heads", 0) or 0,
+            linear_key_head_dim=hf.get("linear_key_head_dim", 0) or 0,
+            linear_value_head_dim=hf.get("linear_value_head_dim", 0) or 0,
+            linear_conv_kernel_dim=hf.get("linear_conv_kernel_dim", 4) or 4,
+            partial_rotary_factor=hf.get("partial_rotary_factor", 1.0) or 1.0,
+            eos_token_id=(hf.get("eos_token_id")[0] if isinstance(hf.get("eos_token_id"), list)
+                          else hf.get("eos_token_id")),
+            name=a,
+        )
+        qc = hf.get("quantization_config") or {}
+        if qc.get("quant_method") == "fp8" and qc.get("weight_block_size"):
+            c.quant = "fp8_block"
+        return c
+
+
+@dataclass
+class CacheConfig:
+    block_size: int = 64
+    gpu_memory_utilization: float = 0.90
+    num_gpu_blocks: Optional[int] = None  # override the memory-derived block count
+    kv_dtype: torch.dtype = torch.bfloat16
+    enable_prefix_caching: bool = True
+
+
+@dataclass
+class SchedulerConfig:
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 4096
+    enable_chunked_prefill: bool = True
+    long_prefill_token_threshold: int = 0
+
+
+@dataclass
+class ParallelConfig:
+    tensor_parallel_size: int = 1
+    pipeline_parallel_size: int = 1
+    data_parallel_size: int = 1
+    enable_expert_parallel: bool = False
+    distributed_backend: str = "nccl"
+    use_custom_allreduce: bool = True
+
+
+@dataclass
+class EngineConfig:
+    model: ModelConfig = field(default_factory=ModelConfig)
+    cache: CacheConfig = field(default_factory=CacheConfig)
+    scheduler: SchedulerConfig = field(default_factory=SchedulerConfig)
+    parallel: ParallelConfig = field(default_factory=ParallelConfig)
+    device: str = "cuda"
+    seed: int = 0
+    load_format: str = "dummy"  # dummy (random N(0, init_std)) | safetensors
+    model_path: Optional[str] = None
+    init_std: float = 0.02
+    enforce_eager: bool = False
+    cuda_graph_sizes: Optional[list] = None
+    speculative_num_tokens: int = 0
+
+    def replace(self, **kw: Any) -> "EngineConfig":
+        return dataclasses.replace(self, **kw)

@@ -1,0 +1,199 @@
+"""Dense decoder family: Llama-2/3, Mistral-style and Qwen2/Qwen3 (QK-RMSNorm) models.
+
+One forward = per layer
+    qkv GEMM -> fused [QK-norm] + RoPE + paged KV insert -> paged attention -> o_proj GEMM
+    -> all-reduce + residual add + RMSNorm (one fused op) -> gate/up GEMM with SwiGLU epilogue
+    -> down GEMM -> all-reduce + residual add + next RMSNorm
+so every norm rides on the collective before it and SwiGLU never round-trips HBM.  Weights
+are sharded Megatron-style for tensor parallelism (heads / intermediate / vocab); the
+embedding is replicated so the first layer needs no collective.
+
+The reference runs upstream vLLM's model files with its custom ops swapped in
+(vllm_musa/model_executor/layers/*: RMSNorm, SiluAndMul, RotaryEmbedding, RowParallelLinear)
+and compile-time fusions (vllm_musa/_inductor/musa_allreduce_rms_fusion.py:254).  Here the
+fused graph is written directly.
+"""
+from __future__ import annotations
+
+import re
+from collections import defaultdict
+from typing import Iterable, Optional, Tuple
+
+import torch
+
+from .. import ops
+from ..attention import AttnMetadata, PagedAttention
+from ..config import ModelConfig
+from ..parallel.communicator import LocalCommunicator
+from ..parallel.state import ParallelState
+
+_LAYER_RE = re.compile(r"^model\.layers\.(\d+)\.(.+)$")
+
+
+def shard_rows(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    n = w.shape[0]
+    assert n % world == 0, f"cannot shard {n} rows over {world} ranks"
+    s = n // world
+    return w[rank * s:(rank + 1) * s]
+
+
+def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    n = w.shape[1]
+    assert n % world == 0, f"cannot shard {n} columns over {world} ranks"
+    s = n // world
+    return w[:, rank * s:(rank + 1) * s]
+
+
+def kv_head_range(num_kv_heads: int, rank: int, world: int) -> Tuple[int, int]:
+    """KV heads owned by ``rank``; heads are replicated when there are fewer than ranks."""
+    if num_kv_heads >= world:
+        per = num_kv_heads // world
+        return rank * per, per
+    return (rank * num_kv_heads) // world, 1
+
+
+class _Layer:
+    __slots__ = ("ln1", "ln2", "qkv_w", "o_w", "gu_w", "down_w", "q_norm", "k_norm")
+
+    def __init__(self):
+        for s in self.__slots__:
+            setattr(self, s, None)
+
+
+class DenseDecoderForCausalLM:
+    """Llama / Qwen2 / Qwen3 dense decoder (see module docstring)."""
+
+    def __init__(self, cfg: ModelConfig, pstate: Optional[ParallelState] = None,
+                 comm=None, device: str | torch.device = "cuda"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = cfg.dtype
+        self.pstate = pstate or ParallelState()
+        self.tp, self.rank = self.pstate.tp_size, self.pstate.tp_rank
+        self.comm = comm or LocalCommunicator(self.device)
+        if cfg.num_heads % self.tp:
+            raise ValueError("num_heads must be divisible by tensor_parallel_size")
+        self.hq = cfg.num_heads // self.tp
+        self.kv0, self.hkv = kv_head_range(cfg.num_kv_heads, self.rank, self.tp)
+        self.D = cfg.head_dim
+        if cfg.intermediate_size % self.tp:
+            raise ValueError("intermediate_size must be divisible by tensor_parallel_size")
+        self.I = cfg.intermediate_size // self.tp
+        self.I_pad = (self.I + 31) // 32 * 32
+        self.vocab_local = cfg.vocab_size // self.tp
+        if cfg.vocab_size % self.tp:
+            raise ValueError("vocab_size must be divisible by tensor_parallel_size")
+        self.vocab_start = self.rank * self.vocab_local
+        self.layers = [_Layer() for _ in range(cfg.num_layers)]
+        self.embed = None
+        self.final_norm = None
+        self.lm_head = None
+        self.attn = PagedAttention(self.hq, self.hkv, self.D)
+        self.cos_sin = ops.build_cos_sin_cache(cfg.rot_dim, cfg.max_position, cfg.rope_theta,
+                                               device=self.device, scaling=cfg.rope_scaling)
+        self._staging = defaultdict(dict)
+
+    # ------------------------------------------------------------------ weights
+    @property
+    def qkv_width(self) -> int:
+        return (self.hq + 2 * self.hkv) * self.D
+
+    def _to(self, t: torch.Tensor) -> torch.Tensor:
+        return t.to(device=self.device, dtype=self.dtype).contiguous()
+
+    def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
+        """Consume HF-named tensors; shard, fuse (qkv, interleaved gate/up) and keep them."""
+        cfg = self.cfg
+        for name, w in weights:
+            if name == "model.embed_tokens.weight":
+                self.embed = self._to(w)
+                if cfg.tie_word_embeddings:
+                    self.lm_head = self._to(shard_rows(w, self.rank, self.tp))
+            elif name == "lm_head.weight":
+                self.lm_head = self._to(shard_rows(w, self.rank, self.tp))
+            elif name == "model.norm.weight":
+                self.final_norm = self._to(w)
+            else:
+                m = _LAYER_RE.match(name)
+                if not m:
+                    continue
+                i, key = int(m.group(1)), m.group(2)
+                if i >= cfg.num_layers:
+                    continue
+                self._staging[i][key] = w
+                self._try_finalize(i)
+        missing = [i for i in range(cfg.num_layers) if self.layers[i].qkv_w is None]
+        if missing or self.embed is None or self.final_norm is None or self.lm_head is None:
+            raise RuntimeError(f"incomplete checkpoint: layers {missing[:8]} ... embed/norm/lm_head "
+                               f"present={self.embed is not None},{self.final_norm is not None},"
+                               f"{self.lm_head is not None}")
+        self._staging.clear()
+
+    def _try_finalize(self, i: int) -> None:
+        need = ["input_layernorm.weight", "post_attention_layernorm.weight",
+                "self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
+                "mlp.down_proj.weight"]
+        if self.cfg.qk_norm:
+            need += ["self_attn.q_norm.weight", "self_attn.k_norm.weight"]
+        st = self._staging[i]
+        if not all(k in st for k in need):
+            return
+        L, D, r, t = self.layers[i], self.D, self.rank, self.tp
+        q = shard_rows(st["self_attn.q_proj.weight"], r, t)
+        k = st["self_attn.k_proj.weight"][self.kv0 * D:(self.kv0 + self.hkv) * D]
+        v = st["self_attn.v_proj.weight"][self.kv0 * D:(self.kv0 + self.hkv) * D]
+        L.qkv_w = self._to(torch.cat([q, k, v], 0))
+        L.o_w = self._to(shard_cols(st["self_attn.o_proj.weight"], r, t))
+        g = shard_rows(st["mlp.gate_proj.weight"], r, t)
+        u = shard_rows(st["mlp.up_proj.weight"], r, t)
+        L.gu_w = self._to(ops.interleave_gate_up(g, u))
+        dn = shard_cols(st["mlp.down_proj.weight"], r, t)
+        if self.I_pad != self.I:
+            dn = torch.cat([dn, torch.zeros(dn.shape[0], self.I_pad - self.I, dtype=dn.dtype,
+                                            device=dn.device)], 1)
+        L.down_w = self._to(dn)
+        L.ln1 = self._to(st["input_layernorm.weight"])
+        L.ln2 = self._to(st["post_attention_layernorm.weight"])
+        if self.cfg.qk_norm:
+            L.q_norm = self._to(st["self_attn.q_norm.weight"])
+            L.k_norm = self._to(st["self_attn.k_norm.weight"])
+        del self._staging[i]
+
+    def linear_shapes(self) -> list:
+        """(N, K) of every GEMM weight, for workspace planning."""
+        L = self.layers[0]
+        return [tuple(L.qkv_w.shape), tuple(L.o_w.shape), tuple(L.gu_w.shape),
+                tuple(L.down_w.shape), tuple(self.lm_head.shape)]
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, input_ids: torch.Tensor, meta: AttnMetadata,
+                kv_caches: list) -> torch.Tensor:
+        """input_ids int32 [T] -> final normalised hidden states [T, H]."""
+        cfg, eps = self.cfg, self.cfg.rms_norm_eps
+        h = ops.embedding(input_ids, self.embed)
+        residual = h
+        x = ops.rms_norm(h, self.layers[0].ln1, eps)
+        n = len(self.layers)
+        for i, L in enumerate(self.layers):
+            kc, vc = kv_caches[i]
+            qkv = ops.linear(x, L.qkv_w)
+            ops.rope_kv(qkv, meta.positions, self.cos_sin, kc, vc, meta.slot_mapping, self.hq,
+                        self.hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm, eps)
+            a = self.attn.forward(qkv, kc, vc, meta)
+            o = ops.linear(a, L.o_w)
+            x, residual = self.comm.allreduce_add_rmsnorm(o, residual, L.ln2, eps)
+            act = ops.linear_silu_mul(x, L.gu_w)
+            d = ops.linear(act, L.down_w)
+            nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
+            x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
+        return x
+
+    def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """[S, H] -> this rank's vocab shard of the logits, fp32 [S, V/tp]."""
+        return ops.linear(hidden, self.lm_head, out_dtype=torch.float32)
+
+    # ------------------------------------------------------------------ KV cache geometry
+    def kv_cache_spec(self) -> dict:
+        return {"num_layers": self.cfg.num_layers, "num_kv_heads": self.hkv,
+                "head_dim": self.D, "dtype": self.dtype}

@@ -1,0 +1,39 @@
+"""Model registry: architecture name -> implementation class."""
+from __future__ import annotations
+
+from ..config import ModelConfig
+
+_REGISTRY = {}
+
+
+def register_model(arch: str):
+    def deco(cls):
+        _REGISTRY[arch] = cls
+        return cls
+    return deco
+
+
+def get_model_class(cfg: ModelConfig):
+    _populate()
+    if cfg.arch not in _REGISTRY:
+        raise NotImplementedError(f"architecture {cfg.arch!r} is not supported; "
+                                  f"supported: {sorted(_REGISTRY)}")
+    return _REGISTRY[cfg.arch]
+
+
+def supported_architectures() -> list:
+    _populate()
+    return sorted(_REGISTRY)
+
+
+def _populate():
+    if _REGISTRY:
+        return
+    from .llama import DenseDecoderForCausalLM
+    _REGISTRY["llama"] = DenseDecoderForCausalLM
+    _REGISTRY["qwen3"] = DenseDecoderForCausalLM
+    try:
+        from .qwen3_moe import Qwen3MoeForCausalLM
+        _REGISTRY["qwen3_moe"] = Qwen3MoeForCausalLM
+    except ImportError:  # pragma: no cover - optional while families are added
+        pass

@@ -1,0 +1,129 @@
+"""Paged attention over the [num_blocks, Hkv, block_size, D] KV cache.
+
+CUDA: csrc/attention/paged_attention.cu (TMA page loads, split-KV decode, chunked-prefill
+kernel).  CPU: a direct PyTorch restatement used by the tiny CPU configuration and as the
+numerics oracle (reference: the MATE FA3 varlen path behind
+vllm_musa/v1/attention/backends/flash_attn.py:1186-1537).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+_WS: dict = {}
+
+
+def decode_workspace(device: torch.device, B: int, Hq: int, D: int, splits: int):
+    """Split-KV partial buffers (fp32 O and log-sum-exp), reused across calls."""
+    need_o, need_l = B * Hq * splits * D, B * Hq * splits
+    key = (device.type, device.index)
+    ws = _WS.get(key)
+    if ws is None or ws[0].numel() < need_o or ws[1].numel() < need_l:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("decode workspace must be reserved before CUDA-graph capture")
+        ws = (torch.empty(max(need_o, 1 << 16), dtype=torch.float32, device=device),
+              torch.empty(max(need_l, 1 << 12), dtype=torch.float32, device=device))
+        _WS[key] = ws
+    return ws
+
+
+def num_decode_splits(B: int, Hkv: int, max_seq_len: int) -> int:
+    return int(_ext.require().decode_num_splits(B, Hkv, max_seq_len))
+
+
+def _gather_kv(cache: torch.Tensor, table: torch.Tensor, n: int) -> torch.Tensor:
+    # -> [n, Hkv, D]
+    bs = cache.shape[2]
+    nb = (n + bs - 1) // bs
+    blocks = cache[table[:nb].long()]            # [nb, Hkv, bs, D]
+    return blocks.permute(0, 2, 1, 3).reshape(nb * bs, cache.shape[1], cache.shape[3])[:n]
+
+
+def _attend_ref(q, k, v, q_pos, scale, window):
+    # q [Tq, Hq, D], k/v [S, Hkv, D]; causal by absolute position
+    Hq, Hkv = q.shape[1], k.shape[1]
+    G = Hq // Hkv
+    k = k.float().repeat_interleave(G, dim=1)
+    v = v.float().repeat_interleave(G, dim=1)
+    s = torch.einsum("thd,shd->hts", q.float(), k) * scale
+    kv_pos = torch.arange(k.shape[0])
+    mask = kv_pos[None, :] > q_pos[:, None]
+    if window > 0:
+        mask |= kv_pos[None, :] <= q_pos[:, None] - window
+    s = s.masked_fill(mask[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hts,shd->thd", p, v)
+
+
+def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 block_tables: torch.Tensor, seq_lens: torch.Tensor, num_q_heads: int,
+                 num_kv_heads: int, scale: float, max_seq_len: int,
+                 out: torch.Tensor | None = None, num_splits: int | None = None) -> torch.Tensor:
+    """One query token per sequence.  q: [B, >= Hq*D] (row stride may exceed Hq*D)."""
+    B = q.shape[0]
+    D = k_cache.shape[-1]
+    Hq = num_q_heads
+    if out is None:
+        out = torch.empty(B, Hq * D, dtype=q.dtype, device=q.device)
+    if B == 0:
+        return out
+    if q.is_cuda:
+        if num_splits is None:
+            num_splits = num_decode_splits(B, num_kv_heads, max_seq_len)
+        ws_o = ws_l = None
+        if num_splits > 1:
+            ws_o, ws_l = decode_workspace(q.device, B, Hq, D, num_splits)
+        _ext.ops().paged_decode(q, out, k_cache, v_cache, block_tables, seq_lens, Hq,
+                                num_kv_heads, max_seq_len, scale, num_splits, ws_o, ws_l)
+        return out
+    for b in range(B):
+        n = int(seq_lens[b])
+        if n == 0:
+            out[b].zero_()
+            continue
+        k = _gather_kv(k_cache, block_tables[b], n)
+        v = _gather_kv(v_cache, block_tables[b], n)
+        qb = q[b, :Hq * D].view(1, Hq, D)
+        o = _attend_ref(qb, k, v, torch.tensor([n - 1]), scale, 0)
+        out[b] = o.reshape(Hq * D).to(out.dtype)
+    return out
+
+
+def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  cu_q: torch.Tensor, seq_lens: torch.Tensor, block_tables: torch.Tensor,
+                  num_q_heads: int, num_kv_heads: int, scale: float, window: int = 0,
+                  out: torch.Tensor | None = None,
+                  tile_scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of each request's new tokens over its whole cached sequence.
+
+    q: [T, >= Hq*D] for the prefill tokens (request r owns rows cu_q[r]:cu_q[r+1]); the K/V
+    of those tokens must already be in the cache.
+    """
+    T = q.shape[0]
+    D = k_cache.shape[-1]
+    Hq = num_q_heads
+    R = seq_lens.shape[0]
+    if out is None:
+        out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
+    if T == 0 or R == 0:
+        return out
+    if q.is_cuda:
+        if tile_scratch is None:
+            tile_scratch = torch.empty(R + 1, dtype=torch.int32, device=q.device)
+        _ext.ops().paged_prefill(q, out, k_cache, v_cache, cu_q, seq_lens, block_tables,
+                                 tile_scratch, Hq, num_kv_heads, scale, window)
+        return out
+    cu = cu_q.tolist()
+    for r in range(R):
+        a, b = cu[r], cu[r + 1]
+        if b == a:
+            continue
+        n = int(seq_lens[r])
+        k = _gather_kv(k_cache, block_tables[r], n)
+        v = _gather_kv(v_cache, block_tables[r], n)
+        qr = q[a:b, :Hq * D].reshape(b - a, Hq, D)
+        pos = torch.arange(n - (b - a), n)
+        o = _attend_ref(qr, k, v, pos, scale, window)
+        out[a:b] = o.reshape(b - a, Hq * D).to(out.dtype)
+    return out

@@ -1,0 +1,72 @@
+"""Token sampling: greedy / temperature (Gumbel-max) with top-k, top-p and min-p filters.
+
+CUDA: csrc/sampling/sampling.cu (radix-select thresholds, Philox Gumbel noise keyed by
+(seed, step, vocab index) so vocab-parallel shards agree).  CPU: a PyTorch restatement with
+the same filtering semantics (random draws come from torch's generator, so only greedy
+results are bit-comparable across devices).  Reference: vllm_musa/v1/sample/
+topk_topp_sampler.py:351, csrc/musa/sampler.mu:124, top_p_mask_logits.mu:149.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+
+def _filter_ref(l: torch.Tensor, k: int, p: float, mp: float) -> torch.Tensor:
+    keep = torch.ones_like(l, dtype=torch.bool)
+    if 0 < k < l.numel():
+        kth = torch.topk(l, k).values[-1]
+        keep &= l >= kth
+    m = l.max()
+    if mp > 0:
+        keep &= l >= m + torch.log(torch.tensor(mp))
+    if p < 1.0:
+        e = torch.where(keep, torch.exp(l - m), torch.zeros_like(l))
+        vals, order = torch.sort(e, descending=True)
+        cum = torch.cumsum(vals, 0)
+        target = p * cum[-1]
+        # smallest prefix whose mass reaches the target; keep ties of the threshold value
+        cut = int(torch.searchsorted(cum, target).clamp(max=l.numel() - 1))
+        thr = vals[cut]
+        keep &= e >= thr
+    return keep
+
+
+def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor | None = None,
+                  top_k: torch.Tensor | None = None, top_p: torch.Tensor | None = None,
+                  min_p: torch.Tensor | None = None, seeds: torch.Tensor | None = None,
+                  steps: torch.Tensor | None = None, vocab_offset: int = 0,
+                  return_values: bool = False, generator: torch.Generator | None = None):
+    """logits [R, V] fp32 -> token ids [R] int64 (global ids = vocab_offset + local index).
+
+    temperature <= 0 means greedy.  With ``return_values`` also returns the winning score
+    (logit for greedy, perturbed logit otherwise) for merging vocab shards.
+    """
+    R = logits.shape[0]
+    if logits.is_cuda:
+        out_idx = torch.empty(R, dtype=torch.int64, device=logits.device)
+        out_val = torch.empty(R, dtype=torch.float32, device=logits.device) if return_values else None
+        if R:
+            _ext.ops().sample(logits, temperature, top_k, top_p, min_p, seeds, steps,
+                              vocab_offset, out_idx, out_val)
+        return (out_idx, out_val) if return_values else out_idx
+    ids = torch.empty(R, dtype=torch.int64)
+    vals = torch.empty(R, dtype=torch.float32)
+    for r in range(R):
+        l = logits[r].float()
+        T = float(temperature[r]) if temperature is not None else 0.0
+        if T <= 0:
+            i = int(torch.argmax(l))
+            ids[r], vals[r] = i + vocab_offset, l[i]
+            continue
+        l = l / T
+        keep = _filter_ref(l, int(top_k[r]) if top_k is not None else 0,
+                           float(top_p[r]) if top_p is not None else 1.0,
+                           float(min_p[r]) if min_p is not None else 0.0)
+        u = torch.rand(l.shape, generator=generator).clamp(1e-7, 1 - 1e-7)
+        g = -torch.log(-torch.log(u))
+        sc = torch.where(keep, l + g, torch.full_like(l, float("-inf")))
+        i = int(torch.argmax(sc))
+        ids[r], vals[r] = i + vocab_offset, sc[i]
+    return (ids, vals) if return_values else ids

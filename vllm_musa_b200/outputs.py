@@ -1,0 +1,44 @@
+"""Request outputs returned by the engine / ``LLM.generate`` (vLLM-compatible fields)."""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+
+@dataclass
+class CompletionOutput:
+    index: int
+    token_ids: List[int]
+    text: str = ""
+    finish_reason: Optional[str] = None
+    cumulative_logprob: Optional[float] = None
+
+
+@dataclass
+class RequestMetrics:
+    arrival_time: float = 0.0
+    first_token_time: Optional[float] = None
+    finished_time: Optional[float] = None
+
+    @property
+    def ttft(self) -> Optional[float]:
+        if self.first_token_time is None:
+            return None
+        return self.first_token_time - self.arrival_time
+
+
+@dataclass
+class RequestOutput:
+    request_id: str
+    prompt_token_ids: List[int]
+    outputs: List[CompletionOutput]
+    finished: bool
+    prompt: Optional[str] = None
+    metrics: RequestMetrics = field(default_factory=RequestMetrics)
+
+    def tpot(self) -> Optional[float]:
+        m = self.metrics
+        n = len(self.outputs[0].token_ids) if self.outputs else 0
+        if m.first_token_time is None or m.finished_time is None or n < 2:
+            return None
+        return (m.finished_time - m.first_token_time) / (n - 1)

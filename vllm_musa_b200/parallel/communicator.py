@@ -1,0 +1,68 @@
+"""Tensor-parallel communicator: the collectives the model layers call.
+
+``allreduce_add_rmsnorm`` is the hot one: every row-parallel projection (o_proj, down_proj)
+ends in it.  With TP == 1 it is the fused residual-add + RMSNorm kernel; with TP > 1 the
+NVSwitch peer-memory kernel (parallel/custom_ar.py) performs all-reduce + residual-add +
+RMSNorm in one launch when available, otherwise NCCL all-reduce followed by the fused norm.
+Reference: MusaJitCustomAllreduce (vllm_musa/distributed/device_communicators/
+musa_jit_custom_all_reduce.py:1762-1938) and the fused ops in
+vllm_musa/fused_allreduce_rmsnorm_ops.py:25-214.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from .state import ParallelState
+
+
+class TPCommunicator:
+    def __init__(self, st: ParallelState, device: torch.device, custom: Optional[object] = None):
+        self.st = st
+        self.device = device
+        self.world = st.tp_size
+        self.group = st.tp_group
+        self.custom = custom  # CustomAllReduce (NVSwitch P2P) or None
+
+    # -- plain collectives ----------------------------------------------------------------
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return x
+        if self.custom is not None and self.custom.can_run(x):
+            return self.custom.all_reduce(x)
+        dist.all_reduce(x, group=self.group)
+        return x
+
+    def all_gather(self, x: torch.Tensor, dim: int = 0) -> torch.Tensor:
+        if self.world == 1:
+            return x
+        out = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        if dim == 0:
+            return out.reshape((-1,) + tuple(x.shape[1:]))
+        return torch.cat(list(out.unbind(0)), dim=dim)
+
+    # -- fused ------------------------------------------------------------------------------
+    def allreduce_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                              eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+        """residual <- AR(x) + residual; x <- RMSNorm(residual) * weight (x, residual in place)."""
+        if self.world > 1:
+            if self.custom is not None and self.custom.can_run(x):
+                return self.custom.allreduce_add_rmsnorm(x, residual, weight, eps)
+            dist.all_reduce(x, group=self.group)
+        return ops.fused_add_rms_norm(x, residual, weight, eps)
+
+    def close(self) -> None:
+        if self.custom is not None:
+            self.custom.close()
+            self.custom = None
+
+
+class LocalCommunicator(TPCommunicator):
+    """Single-GPU / CPU stand-in with the same interface."""
+
+    def __init__(self, device: torch.device):
+        super().__init__(ParallelState(), device)

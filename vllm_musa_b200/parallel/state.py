@@ -1,0 +1,102 @@
+"""Process groups for tensor / expert / data parallelism (one process per GPU).
+
+Reference: the reference relies on upstream vLLM's parallel_state with the ``mccl`` backend
+(vllm_musa/platform.py:251) plus Gloo CPU groups for IPC-handle exchange
+(vllm_musa/distributed/device_communicators/musa_jit_custom_all_reduce.py:383-421).  Here:
+``torch.distributed`` with NCCL for device collectives and a Gloo group for host-side
+consensus; every rank reads RANK / WORLD_SIZE / LOCAL_RANK from the launcher (torchrun).
+"""
+from __future__ import annotations
+
+import datetime
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class ParallelState:
+    world_size: int = 1
+    rank: int = 0
+    local_rank: int = 0
+    tp_size: int = 1
+    tp_rank: int = 0
+    tp_group: Optional[object] = None     # device (NCCL) group
+    tp_cpu_group: Optional[object] = None  # Gloo group for host consensus
+    dp_size: int = 1
+    dp_rank: int = 0
+    ep_size: int = 1
+    ep_rank: int = 0
+    ep_group: Optional[object] = None
+    comm: Optional[object] = None          # TP communicator (parallel.communicator)
+
+    @property
+    def is_driver(self) -> bool:
+        return self.rank == 0
+
+
+_STATE = ParallelState()
+
+
+def get_parallel_state() -> ParallelState:
+    return _STATE
+
+
+def set_parallel_state(st: ParallelState) -> None:
+    global _STATE
+    _STATE = st
+
+
+def init_distributed(tp_size: int = 1, ep: bool = False, backend: Optional[str] = None,
+                     timeout_s: float = 300.0) -> ParallelState:
+    """Initialise torch.distributed from the environment and build the TP/EP/DP groups.
+
+    World = tp_size * dp_size; ranks [k*tp, (k+1)*tp) form TP group k.  EP reuses the TP ranks
+    (experts sharded over the same GPUs that shard attention).  Single process: no groups.
+    """
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
+    st = ParallelState(world_size=world, rank=rank, local_rank=local_rank)
+    if world == 1 and tp_size == 1:
+        set_parallel_state(st)
+        return st
+    if world % tp_size != 0:
+        raise ValueError(f"world size {world} not divisible by tensor_parallel_size {tp_size}")
+    if backend is None:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29511")
+        kw = {}
+        if backend == "nccl":
+            torch.cuda.set_device(local_rank)
+            kw["device_id"] = torch.device("cuda", local_rank)
+        dist.init_process_group(backend=backend, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
+    st.tp_size = tp_size
+    st.dp_size = world // tp_size
+    st.dp_rank = rank // tp_size
+    st.tp_rank = rank % tp_size
+    for k in range(st.dp_size):
+        ranks = list(range(k * tp_size, (k + 1) * tp_size))
+        g = dist.new_group(ranks, backend=backend) if tp_size < world else dist.group.WORLD
+        cg = dist.new_group(ranks, backend="gloo")
+        if rank in ranks:
+            st.tp_group, st.tp_cpu_group = g, cg
+    if ep:
+        st.ep_size, st.ep_rank, st.ep_group = st.tp_size, st.tp_rank, st.tp_group
+    set_parallel_state(st)
+    return st
+
+
+def destroy_distributed() -> None:
+    global _STATE
+    if _STATE.comm is not None and hasattr(_STATE.comm, "close"):
+        _STATE.comm.close()
+    if dist.is_initialized():
+        dist.destroy_process_group()
+    _STATE = ParallelState()

@@ -1,0 +1,47 @@
+"""Sampler over (possibly vocab-sharded) logits.
+
+Each tensor-parallel rank holds the logits of its vocab shard.  Instead of all-gathering the
+full [S, V] logits (the reference's path: patch 0069 IPC all-gather, then top-k/top-p,
+vllm_musa/distributed/device_communicators/musa_jit_custom_all_reduce.py:1941-1956), every
+rank reduces its shard to one (score, token) candidate per row with the Gumbel-max sampler,
+ranks exchange the [S] candidates, and the max wins: identical on every rank because the
+Gumbel noise is a function of (seed, step, global token id).  Rows that use top-k / top-p /
+min-p need global order statistics, so those batches gather the full logits first.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import ops
+
+
+class Sampler:
+    def __init__(self, comm=None, vocab_start: int = 0, tp_size: int = 1):
+        self.comm = comm
+        self.vocab_start = vocab_start
+        self.tp = tp_size
+
+    def __call__(self, logits: torch.Tensor, temperature: Optional[torch.Tensor],
+                 top_k: Optional[torch.Tensor], top_p: Optional[torch.Tensor],
+                 min_p: Optional[torch.Tensor], seeds: Optional[torch.Tensor],
+                 steps: Optional[torch.Tensor], any_filter: bool = False,
+                 generator: Optional[torch.Generator] = None) -> torch.Tensor:
+        if self.tp == 1:
+            return ops.sample_tokens(logits, temperature, top_k, top_p, min_p, seeds, steps,
+                                     generator=generator)
+        if any_filter:
+            full = self.comm.all_gather(logits, dim=1)
+            return ops.sample_tokens(full, temperature, top_k, top_p, min_p, seeds, steps,
+                                     generator=generator)
+        ids, vals = ops.sample_tokens(logits, temperature, None, None, None, seeds, steps,
+                                      vocab_offset=self.vocab_start, return_values=True)
+        all_vals = self.comm.all_gather(vals.unsqueeze(0), dim=0)   # [tp, S]
+        all_ids = self.comm.all_gather(ids.unsqueeze(0), dim=0)
+        if logits.is_cuda:
+            out = torch.empty_like(ids)
+            torch.ops.b200.merge_candidates(all_vals.contiguous(), all_ids.contiguous(), out)
+            return out
+        best = torch.argmax(all_vals, dim=0)
+        return all_ids.gather(0, best.unsqueeze(0)).squeeze(0)

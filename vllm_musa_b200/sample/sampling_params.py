@@ -1,0 +1,41 @@
+"""Sampling parameters (the vLLM ``SamplingParams`` surface the reference's users rely on)."""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+
+@dataclass
+class SamplingParams:
+    n: int = 1
+    temperature: float = 1.0
+    top_p: float = 1.0
+    top_k: int = 0          # 0 or -1: disabled
+    min_p: float = 0.0
+    seed: Optional[int] = None
+    max_tokens: int = 16
+    min_tokens: int = 0
+    stop_token_ids: List[int] = field(default_factory=list)
+    stop: List[str] = field(default_factory=list)
+    ignore_eos: bool = False
+    detokenize: bool = True
+
+    def __post_init__(self):
+        if self.top_k is None or self.top_k < 0:
+            self.top_k = 0
+        if self.temperature < 0:
+            raise ValueError("temperature must be >= 0")
+        if not 0.0 < self.top_p <= 1.0:
+            raise ValueError("top_p must be in (0, 1]")
+        if not 0.0 <= self.min_p <= 1.0:
+            raise ValueError("min_p must be in [0, 1]")
+        if self.max_tokens < 1:
+            raise ValueError("max_tokens must be >= 1")
+        if self.n < 1:
+            raise ValueError("n must be >= 1")
+        if self.temperature < 1e-5:
+            self.temperature = 0.0  # greedy
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature == 0.0
