@@ -113,6 +113,7 @@ void run_act_and_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int
                                                    reinterpret_cast<const __nv_bfloat16*>(x), ld_x,
                                                    I, limit);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 void run_silu_mul_fp8_quant(void* out, float* scales, const void* x, int64_t ld_x, int rows, int I,
@@ -124,6 +125,7 @@ void run_silu_mul_fp8_quant(void* out, float* scales, const void* x, int64_t ld_
       reinterpret_cast<__nv_fp8_e4m3*>(out), scales, reinterpret_cast<const __nv_bfloat16*>(x),
       ld_x, rows, I);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, int rows, int K,
@@ -135,6 +137,7 @@ void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, 
       reinterpret_cast<__nv_fp8_e4m3*>(out), scales, reinterpret_cast<const __nv_bfloat16*>(x),
       ld_x, rows, K);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace act

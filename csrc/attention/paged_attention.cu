@@ -638,10 +638,12 @@ void run_decode(const DecodeArgs& a, cudaStream_t stream) {
     B200_REQUIRE(false, "decode: head_dim must be 64, 128 or 256");
 #undef B200_DEC
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
   if (p.num_splits > 1) {
     attn_combine_kernel<<<dim3(a.B, a.Hq), 128, 0, stream>>>(a.ws_o, a.ws_lse, p.o, a.ld_o, a.Hq,
                                                              p.num_splits, a.D);
     B200_CUDA_OK(cudaGetLastError());
+  count_launch();
   }
 }
 
@@ -659,6 +661,7 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
                                      (uint64_t)a.Hq * a.D, a.T, a.ld_q, 64, CH,
                                      CU_TENSOR_MAP_SWIZZLE_128B);
   tile_offsets_kernel<<<1, 32, 0, stream>>>(a.cu_q, a.R, a.tile_offsets);
+  count_launch();
   PrefillParams p;
   p.o = reinterpret_cast<__nv_bfloat16*>(a.o);
   p.ld_o = a.ld_o;
@@ -693,6 +696,7 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
     B200_REQUIRE(false, "prefill: head_dim must be 64, 128 or 256");
 #undef B200_PRE
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace attn

@@ -125,6 +125,7 @@ void run_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
   }
 #undef B200_ROPE_LAUNCH
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace rope

@@ -4,6 +4,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <stdexcept>
 #include <string>
 
@@ -23,6 +24,13 @@
   } while (0)
 
 namespace b200 {
+// Number of kernels this library has launched (or recorded into a CUDA graph) in this process.
+inline std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> c{0};
+  return c;
+}
+inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_order_relaxed); }
+
 inline int num_sms() {
   static int n = -1;
   if (n < 0) {

@@ -393,6 +393,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   const int grid = std::min(p.total_units, num_sms());
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 template <int EPI>
@@ -482,6 +483,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
                                                                   (int)a.ldc, p.splits);
   }
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace gemm

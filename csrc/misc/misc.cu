@@ -35,6 +35,7 @@ void run_embedding(void* out, const void* table, const int32_t* ids, int T, int 
       reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(table), ids, H8, vocab,
       vocab_start);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 void run_gather_rows(void* out, const void* in, int64_t ld_in, const int32_t* idx, int R, int H,
@@ -47,6 +48,7 @@ void run_gather_rows(void* out, const void* in, int64_t ld_in, const int32_t* id
       reinterpret_cast<uint4*>(out), reinterpret_cast<const uint8_t*>(in), ld_in * elem_bytes,
       idx, W16);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace misc

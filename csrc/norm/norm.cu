@@ -117,6 +117,7 @@ static void launch_vpt(const RmsNormArgs& a, cudaStream_t s) {
     B200_REQUIRE(false, "rms_norm: hidden size too large");
 #undef B200_NORM_LAUNCH
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 void run_rms_norm(const RmsNormArgs& a, cudaStream_t s) {
@@ -146,6 +147,7 @@ void run_rms_norm_gated(void* out, const void* x, const void* z, const void* w, 
       reinterpret_cast<const __nv_bfloat16*>(z), reinterpret_cast<const __nv_bfloat16*>(w), rows,
       H, group, eps);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace norm

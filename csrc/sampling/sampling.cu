@@ -252,6 +252,7 @@ void run_sample(const SampleArgs& a, cudaStream_t s) {
                                           a.top_k, a.top_p, a.min_p, a.seeds, a.steps, a.out_val,
                                           a.out_idx);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 void run_merge_candidates(const float* vals, const int64_t* idx, int S, int R, int64_t* out,
@@ -259,6 +260,7 @@ void run_merge_candidates(const float* vals, const int64_t* idx, int S, int R, i
   if (R == 0) return;
   merge_candidates_kernel<<<(R + 255) / 256, 256, 0, s>>>(vals, idx, S, R, out);
   B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace sampling

@@ -12,6 +12,8 @@
 #include <mutex>
 
 #include "b200_kernels.h"
+#include "common/host_check.h"
+#include "comm/custom_ar.h"
 
 namespace {
 
@@ -413,6 +415,44 @@ void gather_rows(Tensor& out, const Tensor& x, const Tensor& idx) {
 
 Tensor error_word(const Tensor& like) { return error_word_for(like.device()); }
 
+// ------------------------------------------------------------------------------------- comm
+// Fused all-reduce: `bufs` holds per-rank device addresses as int64:
+//   [0:W) staging slot, [W:2W) output slot, [2W:3W) flag region (this call's parity).
+void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64_t epochs_ptr,
+                     int64_t rank, int64_t world, int64_t T, int64_t H, int64_t blocks,
+                     int64_t parity, bool two_shot, const c10::optional<Tensor>& residual,
+                     const c10::optional<Tensor>& weight, double eps) {
+  TORCH_CHECK((int64_t)bufs.size() == 3 * world, "fused_allreduce: buffer table size");
+  const c10::cuda::CUDAGuard g(like.device());
+  b200::comm::ArParams a{};
+  a.rank = rank;
+  a.world = world;
+  a.T = T;
+  a.H = H;
+  a.blocks = blocks;
+  a.parity = parity;
+  a.two_shot = two_shot;
+  for (int p = 0; p < world; ++p) {
+    a.staging[p] = reinterpret_cast<const void*>(bufs[p]);
+    a.out[p] = reinterpret_cast<void*>(bufs[world + p]);
+    a.flags[p] = reinterpret_cast<uint32_t*>(bufs[2 * world + p]);
+  }
+  a.epochs = reinterpret_cast<uint32_t*>(epochs_ptr);
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->scalar_type() == at::kBFloat16 &&
+                    residual->size(0) >= T && residual->size(1) == H,
+                "fused_allreduce: residual");
+    a.residual = residual->data_ptr();
+  }
+  if (weight.has_value()) {
+    TORCH_CHECK(weight->numel() == H && weight->scalar_type() == at::kBFloat16, "weight");
+    a.weight = weight->data_ptr();
+  }
+  a.eps = eps;
+  a.err = err_ptr(like);
+  guarded([&] { b200::comm::run_fused_allreduce(a, stream_of(like)); });
+}
+
 }  // namespace
 
 TORCH_LIBRARY(b200, m) {
@@ -473,6 +513,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &gemm_plan, "automatic (bn, splits, workspace_floats) for a bf16 GEMM");
   m.def("decode_num_splits", &decode_num_splits, "split-KV count for a decode batch");
   m.def("error_word", &error_word, "per-device error word of the bounded waits");
+  m.def("fused_allreduce", &fused_allreduce, "NVSwitch all-reduce (+ residual + RMSNorm)");
+  m.def("ipc_malloc", [](size_t n) { return (int64_t)reinterpret_cast<uintptr_t>(b200::comm::ipc_malloc(n)); });
+  m.def("ipc_free", [](int64_t p) { b200::comm::ipc_free(reinterpret_cast<void*>(p)); });
+  m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(b200::comm::ipc_handle(reinterpret_cast<void*>(p))); });
+  m.def("ipc_open", [](const std::string& h) { return (int64_t)reinterpret_cast<uintptr_t>(b200::comm::ipc_open(h)); });
+  m.def("ipc_close", [](int64_t p) { b200::comm::ipc_close(reinterpret_cast<void*>(p)); });
+  m.def("comm_flag_bytes", []() { return (int64_t)(b200::comm::kFlagBytes + b200::comm::kEpochBytes); });
+  m.def("comm_max_blocks", []() { return (int64_t)b200::comm::kMaxBlocks; });
+  m.def("launch_count", []() { return (long long)b200::launch_counter().load(); },
+        "kernels launched (or recorded into CUDA graphs) by this library so far");
   m.attr("BUILT_ARCH") = "sm_100a";
   register_runtime(m);
 }

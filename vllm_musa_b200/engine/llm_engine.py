@@ -1,0 +1,258 @@
+"""The serving engine: requests in, tokens out.
+
+    add_request() -> C++ Scheduler (admission, KV blocks, chunked prefill, preemption)
+    step()        -> Scheduler.schedule() fills the pinned step buffers
+                  -> ModelRunner.execute() (H2D, forward / CUDA-graph replay, sample, D2H)
+                  -> Scheduler.update() appends tokens, applies stop conditions
+Tensor parallelism is SPMD: every rank (one process per GPU, launched by torchrun) runs
+its own engine on the same requests; the schedulers stay in lock-step because every rank
+draws the same tokens (vocab-parallel sampler, parallel/sampler).  The reference gets this
+layer from upstream vLLM's V1 EngineCore.
+"""
+from __future__ import annotations
+
+import itertools
+import logging
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from ..config import EngineConfig
+from ..models.registry import get_model_class
+from ..models.weights import dummy_weights, safetensors_weights
+from ..outputs import CompletionOutput, RequestMetrics, RequestOutput
+from ..parallel.communicator import LocalCommunicator, TPCommunicator
+from ..parallel.state import get_parallel_state, init_distributed
+from ..sample.sampler import Sampler
+from ..sample.sampling_params import SamplingParams
+from .model_runner import ModelRunner
+
+log = logging.getLogger("vllm_musa_b200")
+
+_REASONS = {1: "length", 2: "stop", 3: "abort"}
+
+
+@dataclass
+class _Req:
+    request_id: str
+    int_id: int
+    prompt_token_ids: List[int]
+    params: SamplingParams
+    arrival: float
+    prompt: Optional[str] = None
+    parent: Optional[str] = None
+    index: int = 0
+    tokens: List[int] = field(default_factory=list)
+    first_token_time: Optional[float] = None
+
+
+def _mix_seed(a: int, b: int) -> int:
+    x = (a * 0x9E3779B97F4A7C15 + b * 0xBF58476D1CE4E5B9 + 0x94D049BB133111EB) & (2**64 - 1)
+    x ^= x >> 31
+    return x & 0x7FFFFFFFFFFFFFFF
+
+
+class LLMEngine:
+    def __init__(self, config: EngineConfig, tokenizer=None):
+        self.config = config
+        self.tokenizer = tokenizer
+        mcfg = config.model
+        tp = config.parallel.tensor_parallel_size
+        device = torch.device(config.device)
+        if device.type == "cuda":
+            ops._ext.require()
+        st = get_parallel_state()
+        if tp > 1 and st.tp_size != tp:
+            st = init_distributed(tp_size=tp, ep=config.parallel.enable_expert_parallel,
+                                  backend="nccl" if device.type == "cuda" else "gloo")
+        if device.type == "cuda":
+            device = torch.device("cuda", st.local_rank if st.world_size > 1 else
+                                  (device.index or 0))
+            torch.cuda.set_device(device)
+        self.device = device
+        self.pstate = st
+        if st.tp_size > 1:
+            custom = None
+            if device.type == "cuda" and config.parallel.use_custom_allreduce:
+                from ..parallel.custom_ar import maybe_create_custom_allreduce
+                custom = maybe_create_custom_allreduce(st, device)
+            self.comm = TPCommunicator(st, device, custom)
+            st.comm = self.comm
+        else:
+            self.comm = LocalCommunicator(device)
+        cls = get_model_class(mcfg)
+        self.model = cls(mcfg, st, self.comm, device)
+        t0 = time.time()
+        if config.load_format == "dummy":
+            gdev = "cuda" if device.type == "cuda" else "cpu"
+            self.model.load_weights(dummy_weights(mcfg, config.seed, config.init_std,
+                                                  device=str(device) if gdev == "cuda" else "cpu"))
+        else:
+            self.model.load_weights(safetensors_weights(config.model_path))
+        log.info("weights ready in %.1fs", time.time() - t0)
+        self.sampler = Sampler(self.comm, getattr(self.model, "vocab_start", 0), st.tp_size)
+        self.runner = ModelRunner(config, self.model, self.sampler, device)
+        num_blocks = self.runner.profile_and_allocate_kv()
+        if st.tp_size > 1:
+            # every rank must run with the same block count (lock-step schedulers)
+            t = torch.tensor([num_blocks], dtype=torch.int64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=st.tp_cpu_group)
+            if int(t) != num_blocks:
+                num_blocks = int(t)
+                self.runner.allocate_kv(num_blocks)
+        self.num_blocks = num_blocks
+        from .. import _C_runtime
+        sc = _C_runtime.SchedulerConfig()
+        sc.block_size = config.cache.block_size
+        sc.max_num_seqs = config.scheduler.max_num_seqs
+        sc.max_num_batched_tokens = config.scheduler.max_num_batched_tokens
+        sc.max_model_len = config.scheduler.max_model_len
+        sc.max_blocks_per_seq = self.runner.max_blocks
+        sc.chunked_prefill = config.scheduler.enable_chunked_prefill
+        sc.prefix_caching = config.cache.enable_prefix_caching
+        sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
+        self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
+        self.runner.capture_graphs()
+        self._ids = itertools.count()
+        self._reqs: Dict[int, _Req] = {}
+        self._by_name: Dict[str, int] = {}
+        self._parents: Dict[str, dict] = {}
+        self.step_end_times: List[float] = []
+        self.stream_outputs = False
+        self.num_steps = 0
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, request_id: str, prompt_token_ids: List[int],
+                    params: Optional[SamplingParams] = None, arrival_time: Optional[float] = None,
+                    prompt: Optional[str] = None) -> None:
+        params = params or SamplingParams()
+        arrival = time.time() if arrival_time is None else arrival_time
+        if params.n > 1:
+            self._parents[request_id] = {"n": params.n, "done": {}, "prompt_ids": prompt_token_ids,
+                                         "prompt": prompt, "arrival": arrival}
+            for k in range(params.n):
+                child = SamplingParams(**{**params.__dict__, "n": 1})
+                if params.seed is not None:
+                    child.seed = params.seed + k
+                self._add_one(f"{request_id}#{k}", prompt_token_ids, child, arrival, prompt,
+                              parent=request_id, index=k)
+            return
+        self._add_one(request_id, prompt_token_ids, params, arrival, prompt)
+
+    def _add_one(self, name, prompt_ids, params, arrival, prompt, parent=None, index=0):
+        if name in self._by_name:
+            raise ValueError(f"duplicate request id {name!r}")
+        iid = next(self._ids)
+        from .. import _C_runtime
+        sp = _C_runtime.SamplingCfg()
+        sp.max_tokens = params.max_tokens
+        sp.min_tokens = params.min_tokens
+        sp.ignore_eos = params.ignore_eos
+        eos = self.config.model.eos_token_id
+        sp.eos_id = -1 if eos is None else int(eos)
+        sp.stop_ids = list(params.stop_token_ids)
+        sp.temperature = params.temperature
+        sp.top_k = params.top_k
+        sp.top_p = params.top_p
+        sp.min_p = params.min_p
+        sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
+        self.scheduler.add_request(iid, list(map(int, prompt_ids)), sp)
+        self._reqs[iid] = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
+        self._by_name[name] = iid
+
+    def abort_request(self, request_id: str) -> None:
+        names = [request_id] + [n for n in self._by_name if n.startswith(request_id + "#")]
+        for n in names:
+            iid = self._by_name.get(n)
+            if iid is not None:
+                self.scheduler.abort_request(iid)
+                self._by_name.pop(n, None)
+                self._reqs.pop(iid, None)
+                self.scheduler.forget(iid)
+        self._parents.pop(request_id, None)
+
+    def has_unfinished_requests(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    # ------------------------------------------------------------------ stepping
+    def step(self) -> List[RequestOutput]:
+        plan = self.scheduler.schedule()
+        if plan.num_reqs == 0:
+            return []
+        sampled = self.runner.execute(plan)
+        finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
+        now = time.time()
+        self.step_end_times.append(now)
+        self.num_steps += 1
+        outs: List[RequestOutput] = []
+        if self.stream_outputs:
+            vals = sampled.tolist()
+            for k, iid in enumerate(plan.sample_req_ids):
+                r = self._reqs.get(iid)
+                if r is not None:
+                    r.tokens.append(vals[k])
+                    if r.first_token_time is None:
+                        r.first_token_time = now
+            done = {iid for iid, _ in finished}
+            for iid in plan.sample_req_ids:
+                if iid not in done and iid in self._reqs:
+                    outs.append(self._make_output(self._reqs[iid], None, False))
+        for iid, reason in finished:
+            r = self._reqs.pop(iid, None)
+            if r is None:
+                continue
+            self._by_name.pop(r.request_id, None)
+            o = self._finish(r, _REASONS.get(reason, "stop"))
+            if o is not None:
+                outs.append(o)
+        return outs
+
+    def _step_time(self, step: int) -> Optional[float]:
+        # scheduler steps are 1-based and one engine step == one scheduler step
+        if step is None or step < 1 or step > len(self.step_end_times):
+            return None
+        return self.step_end_times[step - 1]
+
+    def _finish(self, r: _Req, reason: str) -> Optional[RequestOutput]:
+        info = self.scheduler.request_info(r.int_id)
+        toks = self.scheduler.output_tokens(r.int_id)
+        self.scheduler.forget(r.int_id)
+        r.tokens = list(toks)
+        first = self._step_time(info["first_token_step"]) if info else None
+        last = self._step_time(info["finish_step"]) if info else None
+        out = self._make_output(r, reason, True, first, last)
+        if r.parent is None:
+            return out
+        par = self._parents.get(r.parent)
+        if par is None:
+            return None
+        par["done"][r.index] = out
+        if len(par["done"]) < par["n"]:
+            return None
+        del self._parents[r.parent]
+        comps = [par["done"][k].outputs[0] for k in range(par["n"])]
+        ftimes = [par["done"][k].metrics.first_token_time for k in range(par["n"])]
+        ltimes = [par["done"][k].metrics.finished_time for k in range(par["n"])]
+        m = RequestMetrics(par["arrival"], min([t for t in ftimes if t] or [None]) if any(ftimes) else None,
+                           max([t for t in ltimes if t] or [None]) if any(ltimes) else None)
+        return RequestOutput(r.parent, par["prompt_ids"], comps, True, par["prompt"], m)
+
+    def _make_output(self, r: _Req, reason, finished, first=None, last=None) -> RequestOutput:
+        text = ""
+        if self.tokenizer is not None and r.params.detokenize:
+            try:
+                text = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
+            except Exception:  # pragma: no cover - tokenizer specific
+                text = ""
+        comp = CompletionOutput(r.index, list(r.tokens), text, reason)
+        m = RequestMetrics(r.arrival, first if first is not None else r.first_token_time, last)
+        return RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
+
+    # ------------------------------------------------------------------ lifecycle
+    def shutdown(self) -> None:
+        self.runner.release_graphs()
+        if self.comm is not None and hasattr(self.comm, "close"):
+            self.comm.close()

@@ -1,0 +1,329 @@
+"""GPU model runner: step buffers, KV cache, CUDA graphs, forward + sampling.
+
+Per engine step:
+  1. the C++ scheduler has written the step's inputs into pinned host buffers;
+  2. the used prefix of each buffer is copied host->device (async, on the compute stream);
+  3. decode-only steps replay a captured CUDA graph of the padded batch size (forward +
+     LM head + sampler in one replay); prefill / mixed steps run eagerly;
+  4. the sampled token ids come back device->host into a pinned buffer.
+The reference uses vLLM's GPUModelRunner with its static graph wrapper and graph-capture
+hooks (vllm_musa/platform.py:908-910, v1/worker/*); this runner is written for this engine.
+"""
+from __future__ import annotations
+
+import logging
+import time
+from typing import Optional
+
+import torch
+
+from .. import ops
+from ..attention import AttnMetadata
+from ..config import EngineConfig
+
+log = logging.getLogger("vllm_musa_b200")
+
+_I32, _F32, _I64 = torch.int32, torch.float32, torch.int64
+
+
+class StepBuffers:
+    """Fixed-capacity step inputs: pinned host side + device side (same tensors on CPU)."""
+
+    FIELDS = [("input_ids", "tok", _I32), ("positions", "tok", _I32),
+              ("slot_mapping", "tok", _I32), ("cu_q", "req1", _I32), ("seq_lens", "req", _I32),
+              ("block_tables", "bt", _I32), ("logits_idx", "req", _I32),
+              ("temperature", "req", _F32), ("top_k", "req", _I32), ("top_p", "req", _F32),
+              ("min_p", "req", _F32), ("seeds", "req", _I64), ("steps", "req", _I32)]
+
+    def __init__(self, max_tokens: int, max_reqs: int, max_blocks: int, device: torch.device):
+        self.max_tokens, self.max_reqs, self.max_blocks = max_tokens, max_reqs, max_blocks
+        self.device = device
+        pin = device.type == "cuda"
+        sizes = {"tok": max_tokens, "req": max_reqs, "req1": max_reqs + 1,
+                 "bt": max_reqs * max_blocks}
+        self.h, self.d = {}, {}
+        for name, kind, dt in self.FIELDS:
+            self.h[name] = torch.zeros(sizes[kind], dtype=dt, pin_memory=pin)
+            self.d[name] = self.h[name] if not pin else torch.zeros(sizes[kind], dtype=dt,
+                                                                    device=device)
+        self.sampled_h = torch.zeros(max_reqs, dtype=_I64, pin_memory=pin)
+
+    def pointers(self) -> dict:
+        p = {name: self.h[name].data_ptr() for name, _, _ in self.FIELDS}
+        p["max_tokens"], p["max_reqs"] = self.max_tokens, self.max_reqs
+        return p
+
+    def bt2d(self, which: str = "d") -> torch.Tensor:
+        return getattr(self, which)["block_tables"].view(self.max_reqs, self.max_blocks)
+
+    def upload(self, n_tok: int, n_req: int, n_sample: int, sampling: bool) -> int:
+        """Copy the used prefixes host->device.  Returns the number of bytes copied."""
+        if self.device.type != "cuda":
+            return 0
+        nbytes = 0
+
+        def cp(name, n):
+            nonlocal nbytes
+            if n > 0:
+                self.d[name][:n].copy_(self.h[name][:n], non_blocking=True)
+                nbytes += n * self.h[name].element_size()
+
+        for name in ("input_ids", "positions", "slot_mapping"):
+            cp(name, n_tok)
+        cp("cu_q", n_req + 1)
+        cp("seq_lens", n_req)
+        cp("block_tables", n_req * self.max_blocks)
+        cp("logits_idx", n_sample)
+        if sampling:
+            for name in ("temperature", "top_k", "top_p", "min_p", "seeds", "steps"):
+                cp(name, n_sample)
+        return nbytes
+
+
+class ModelRunner:
+    def __init__(self, cfg: EngineConfig, model, sampler, device: torch.device):
+        self.cfg = cfg
+        self.model = model
+        self.sampler = sampler
+        self.device = device
+        sc = cfg.scheduler
+        self.block_size = cfg.cache.block_size
+        self.max_blocks = (sc.max_model_len + self.block_size - 1) // self.block_size
+        self.buf = StepBuffers(sc.max_num_batched_tokens, sc.max_num_seqs, self.max_blocks, device)
+        self.kv_caches: list = []
+        self.kv_tensor: Optional[torch.Tensor] = None
+        self.num_blocks = 0
+        self.tile_scratch = torch.zeros(sc.max_num_seqs + 1, dtype=_I32, device=device)
+        self.graphs: dict = {}
+        self.graph_launches: dict = {}     # our kernels recorded in each decode graph
+        self.graph_launches_replayed = 0   # ... summed over replays
+        self.graph_pool = None
+        self.use_graphs = device.type == "cuda" and not cfg.enforce_eager
+        self.timing = False
+        self.step_times: list = []  # (kind, start_event, end_event)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.gen = torch.Generator(device="cpu").manual_seed(cfg.seed) if device.type == "cpu" else None
+        self.record_logits = False  # debugging / tests: keep every step's logits (eager only)
+        self.logits_log: list = []
+
+    # ------------------------------------------------------------------ memory / KV cache
+    def kv_bytes_per_block(self) -> int:
+        spec = self.model.kv_cache_spec()
+        elt = torch.tensor([], dtype=spec["dtype"]).element_size()
+        return spec["num_layers"] * 2 * spec["num_kv_heads"] * self.block_size * spec["head_dim"] * elt
+
+    def profile_and_allocate_kv(self) -> int:
+        """Measure the activation peak of a full-budget prefill, then size the KV cache."""
+        cc = self.cfg.cache
+        if cc.num_gpu_blocks is not None or self.device.type != "cuda":
+            n = cc.num_gpu_blocks or max(64, 4 * self.cfg.scheduler.max_num_seqs)
+            self.allocate_kv(n)
+            return n
+        spec = self.model.kv_cache_spec()
+        tmp = [(torch.zeros(1, spec["num_kv_heads"], self.block_size, spec["head_dim"],
+                            dtype=spec["dtype"], device=self.device),) * 2
+               for _ in range(spec["num_layers"])]
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        T = self.cfg.scheduler.max_num_batched_tokens
+        R = min(self.cfg.scheduler.max_num_seqs, max(1, T // 1024))
+        b = self.buf
+        per = T // R
+        b.d["input_ids"][:T].zero_()
+        b.d["positions"][:T].copy_(torch.arange(T, device=self.device) % per)
+        b.d["slot_mapping"][:T].fill_(-1)
+        b.d["cu_q"][:R + 1].copy_(torch.arange(R + 1, device=self.device) * per)
+        b.d["cu_q"][R] = T
+        b.d["seq_lens"][:R].fill_(per)
+        b.d["seq_lens"][R - 1] = T - per * (R - 1)
+        b.bt2d()[:R].zero_()
+        b.d["logits_idx"][:R].copy_(b.d["cu_q"][1:R + 1] - 1)
+        meta = AttnMetadata(T, 0, R, b.d["positions"][:T], b.d["slot_mapping"][:T],
+                            b.d["seq_lens"][:R], b.bt2d()[:R], b.d["cu_q"][:R + 1],
+                            max_seq_len=T, tile_scratch=self.tile_scratch)
+        self.kv_caches = tmp
+        self._forward_sample(T, R, R, meta, sampling=False, any_filter=False)
+        torch.cuda.synchronize()
+        peak = torch.cuda.max_memory_allocated() - base
+        self.kv_caches = []
+        del tmp
+        torch.cuda.empty_cache()
+        free, total = torch.cuda.mem_get_info()
+        graph_reserve = (1 << 30) if self.use_graphs else 0
+        budget = free - (1.0 - cc.gpu_memory_utilization) * total - peak - graph_reserve
+        n = int(budget // self.kv_bytes_per_block())
+        if n < 16:
+            raise RuntimeError(f"not enough GPU memory for the KV cache (budget {budget/2**30:.1f} GiB)")
+        log.info("KV cache: %d blocks of %d tokens (%.1f GiB); activation peak %.2f GiB",
+                 n, self.block_size, n * self.kv_bytes_per_block() / 2**30, peak / 2**30)
+        self.allocate_kv(n)
+        return n
+
+    def allocate_kv(self, num_blocks: int) -> None:
+        spec = self.model.kv_cache_spec()
+        self.num_blocks = num_blocks
+        self.kv_tensor = torch.zeros(spec["num_layers"], 2, num_blocks, spec["num_kv_heads"],
+                                     self.block_size, spec["head_dim"], dtype=spec["dtype"],
+                                     device=self.device)
+        self.kv_caches = [(self.kv_tensor[i, 0], self.kv_tensor[i, 1])
+                          for i in range(spec["num_layers"])]
+
+    # ------------------------------------------------------------------ forward
+    def _forward_sample(self, T: int, R: int, S: int, meta: AttnMetadata, sampling: bool,
+                        any_filter: bool, decode_only: bool = False) -> torch.Tensor:
+        b = self.buf
+        hidden = self.model.forward(b.d["input_ids"][:T], meta, self.kv_caches)
+        rows = hidden if decode_only else ops.gather_rows(hidden, b.d["logits_idx"][:S])
+        logits = self.model.compute_logits(rows)
+        if self.record_logits:
+            self.logits_log.append(logits.detach().float().cpu())
+        if sampling:
+            return self.sampler(logits, b.d["temperature"][:S], b.d["top_k"][:S],
+                                b.d["top_p"][:S], b.d["min_p"][:S], b.d["seeds"][:S],
+                                b.d["steps"][:S], any_filter=any_filter, generator=self.gen)
+        return self.sampler(logits, None, None, None, None, None, None)
+
+    def _meta(self, T: int, R: int, nd: int, npf: int, max_seq_len: int,
+              decode_splits: Optional[int] = None) -> AttnMetadata:
+        b = self.buf
+        return AttnMetadata(T, nd, npf, b.d["positions"][:T], b.d["slot_mapping"][:T],
+                            b.d["seq_lens"][:R], b.bt2d()[:R], b.d["cu_q"][:R + 1],
+                            max_seq_len=max_seq_len, decode_splits=decode_splits,
+                            tile_scratch=self.tile_scratch)
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def graph_sizes(self) -> list:
+        if self.cfg.cuda_graph_sizes:
+            sizes = sorted(set(int(s) for s in self.cfg.cuda_graph_sizes))
+        else:
+            mx = self.cfg.scheduler.max_num_seqs
+            sizes = [1, 2, 4, 8] + list(range(16, 257, 16)) + list(range(288, 1025, 32))
+            sizes = [s for s in sizes if s <= mx]
+            if mx not in sizes:
+                sizes.append(mx)
+        return [s for s in sizes if s <= self.buf.max_reqs]
+
+    def _pad_decode_inputs(self, B: int) -> None:
+        b = self.buf
+        b.d["seq_lens"][:B].zero_()
+        b.d["slot_mapping"][:B].fill_(-1)
+        b.d["input_ids"][:B].zero_()
+        b.d["positions"][:B].zero_()
+        b.d["cu_q"][:B + 1].copy_(torch.arange(B + 1, dtype=_I32, device=self.device))
+        b.d["logits_idx"][:B].copy_(torch.arange(B, dtype=_I32, device=self.device))
+        b.d["temperature"][:B].zero_()
+        b.d["top_k"][:B].zero_()
+        b.d["top_p"][:B].fill_(1.0)
+        b.d["min_p"][:B].zero_()
+
+    def reserve_workspaces(self) -> None:
+        """Size the split-K GEMM and split-KV workspaces for every shape the runner can see."""
+        if self.device.type != "cuda":
+            return
+        mod = ops._ext.require()
+        Ms = sorted(set(self.graph_sizes() + [self.cfg.scheduler.max_num_batched_tokens,
+                                                self.cfg.scheduler.max_num_seqs]))
+        need = 0
+        for (N, K) in self.model.linear_shapes():
+            for M in Ms + [1, 2, 4, 8, 16, 32, 64, 128]:
+                need = max(need, mod.gemm_plan(M, N, K)[2])
+        ops.gemm.reserve_workspace(self.device, need)
+        spec = self.model.kv_cache_spec()
+        hq = getattr(self.model, "hq", spec["num_kv_heads"])
+        worst = 0
+        for B in range(1, self.cfg.scheduler.max_num_seqs + 1):
+            s = ops.attention.num_decode_splits(B, spec["num_kv_heads"], self.cfg.scheduler.max_model_len)
+            worst = max(worst, B * s)
+        if worst:
+            ops.attention.decode_workspace(self.device, worst, hq, spec["head_dim"], 1)
+
+    def capture_graphs(self) -> None:
+        if not self.use_graphs:
+            return
+        t0 = time.time()
+        mod = ops._ext.require()
+        self.reserve_workspaces()
+        self.graph_pool = torch.cuda.graph_pool_handle()
+        max_len = self.cfg.scheduler.max_model_len
+        hkv = self.model.kv_cache_spec()["num_kv_heads"]
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for B in sorted(self.graph_sizes(), reverse=True):
+                self._pad_decode_inputs(B)
+                splits = ops.attention.num_decode_splits(B, hkv, max_len)
+                meta = self._meta(B, B, B, 0, max_len, splits)
+                for _ in range(2):
+                    self._forward_sample(B, B, B, meta, sampling=True, any_filter=False,
+                                         decode_only=True)
+                g = torch.cuda.CUDAGraph()
+                c0 = mod.launch_count()
+                with torch.cuda.graph(g, pool=self.graph_pool, stream=stream):
+                    out = self._forward_sample(B, B, B, meta, sampling=True, any_filter=False,
+                                               decode_only=True)
+                self.graph_launches[B] = mod.launch_count() - c0
+                self.graphs[B] = (g, out)
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        log.info("captured %d decode CUDA graphs in %.1fs", len(self.graphs), time.time() - t0)
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        self.graph_pool = None
+
+    # ------------------------------------------------------------------ step
+    def execute(self, plan) -> torch.Tensor:
+        """Run one scheduled step; returns the sampled ids (host int64 tensor, [num_samples])."""
+        T, R, S = plan.num_tokens, plan.num_reqs, plan.num_samples
+        nd, npf = plan.num_decodes, plan.num_prefills
+        b = self.buf
+        cuda = self.device.type == "cuda"
+        decode_only = npf == 0 and nd == R and S == R
+        B = None
+        if decode_only and self.graphs and not self.record_logits and \
+                not (plan.any_filter and self.sampler.tp > 1):
+            for s in sorted(self.graphs):
+                if s >= R:
+                    B = s
+                    break
+        ev = None
+        if self.timing and cuda:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        if B is not None:
+            h = b.h
+            if B > R:
+                h["slot_mapping"][T:B] = -1
+                h["seq_lens"][R:B] = 0
+                h["input_ids"][T:B] = 0
+                h["positions"][T:B] = 0
+                h["logits_idx"][S:B] = 0
+                h["temperature"][S:B] = 0
+                h["top_k"][S:B] = 0
+                h["top_p"][S:B] = 1.0
+                h["min_p"][S:B] = 0
+            self.h2d_bytes += b.upload(B, B, B, True)
+            g, out = self.graphs[B]
+            g.replay()
+            self.graph_launches_replayed += self.graph_launches[B]
+            ids = out[:S]
+        else:
+            sampling = not plan.all_greedy
+            self.h2d_bytes += b.upload(T, R, S, sampling)
+            meta = self._meta(T, R, nd, npf, plan.max_seq_len)
+            ids = self._forward_sample(T, R, S, meta, sampling=sampling,
+                                       any_filter=plan.any_filter, decode_only=decode_only)
+        out_h = b.sampled_h[:S]
+        if cuda:
+            out_h.copy_(ids, non_blocking=True)
+            self.d2h_bytes += S * 8
+            if ev is not None:
+                ev[1].record()
+                self.step_times.append(("decode" if decode_only else "mixed", ev[0], ev[1]))
+            torch.cuda.current_stream().synchronize()
+        else:
+            out_h.copy_(ids)
+        return out_h

@@ -1,0 +1,119 @@
+"""Offline inference API: ``LLM(...).generate(prompts, sampling_params)``.
+
+Same call shape as vLLM's ``LLM`` (the surface the reference's users drive through
+``vllm serve`` / ``LLM()``): prompts may be strings (tokenised with the model's tokenizer),
+token-id lists, or ``{"prompt_token_ids": [...]}`` / ``{"prompt": "..."}`` dicts.
+With ``tensor_parallel_size > 1`` run one process per GPU under ``torchrun``; every rank
+calls ``generate`` with the same prompts and receives the same outputs.
+"""
+from __future__ import annotations
+
+import os
+from typing import List, Optional, Sequence, Union
+
+from ..config import CacheConfig, EngineConfig, ModelConfig, ParallelConfig, SchedulerConfig
+from ..engine.llm_engine import LLMEngine
+from ..models.presets import PRESETS, get_preset
+from ..outputs import RequestOutput
+from ..sample.sampling_params import SamplingParams
+
+PromptType = Union[str, List[int], dict]
+
+
+def _load_tokenizer(path: Optional[str]):
+    if not path or not os.path.isdir(path):
+        return None
+    try:
+        from transformers import AutoTokenizer
+        return AutoTokenizer.from_pretrained(path)
+    except Exception:  # pragma: no cover - optional
+        return None
+
+
+class LLM:
+    def __init__(self, model: Union[str, ModelConfig, None] = None, *,
+                 tensor_parallel_size: int = 1, enable_expert_parallel: bool = False,
+                 max_model_len: Optional[int] = None, max_num_seqs: int = 256,
+                 max_num_batched_tokens: int = 8192, block_size: int = 64,
+                 gpu_memory_utilization: float = 0.90, num_gpu_blocks: Optional[int] = None,
+                 enable_prefix_caching: bool = True, enable_chunked_prefill: bool = True,
+                 enforce_eager: bool = False, seed: int = 0, load_format: Optional[str] = None,
+                 device: str = "cuda", dtype=None, tokenizer=None,
+                 cuda_graph_sizes: Optional[list] = None, num_layers: Optional[int] = None,
+                 **unused):
+        path = None
+        if isinstance(model, ModelConfig):
+            mcfg = model
+        elif isinstance(model, str) and model.lower() in PRESETS:
+            mcfg = get_preset(model)
+        elif isinstance(model, str):
+            path = model
+            mcfg = ModelConfig.from_hf(model)
+        else:
+            raise ValueError("model must be a preset name, a checkpoint directory or a ModelConfig")
+        if dtype is not None:
+            mcfg.dtype = dtype
+        if num_layers is not None:
+            mcfg.num_layers = num_layers
+        if load_format is None:
+            load_format = "safetensors" if path else "dummy"
+        mlen = max_model_len or min(mcfg.max_position, 8192)
+        cfg = EngineConfig(
+            model=mcfg,
+            cache=CacheConfig(block_size=block_size, gpu_memory_utilization=gpu_memory_utilization,
+                              num_gpu_blocks=num_gpu_blocks,
+                              enable_prefix_caching=enable_prefix_caching),
+            scheduler=SchedulerConfig(max_num_seqs=max_num_seqs,
+                                      max_num_batched_tokens=max(max_num_batched_tokens, max_num_seqs),
+                                      max_model_len=mlen,
+                                      enable_chunked_prefill=enable_chunked_prefill),
+            parallel=ParallelConfig(tensor_parallel_size=tensor_parallel_size,
+                                    enable_expert_parallel=enable_expert_parallel),
+            device=device, seed=seed, load_format=load_format, model_path=path,
+            enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes)
+        tok = tokenizer if tokenizer is not None else _load_tokenizer(path)
+        self.engine = LLMEngine(cfg, tok)
+        self._counter = 0
+
+    def get_tokenizer(self):
+        return self.engine.tokenizer
+
+    def _prompt_ids(self, p: PromptType):
+        if isinstance(p, dict):
+            if "prompt_token_ids" in p:
+                return list(p["prompt_token_ids"]), p.get("prompt")
+            p = p["prompt"]
+        if isinstance(p, str):
+            tok = self.engine.tokenizer
+            if tok is None:
+                raise ValueError("string prompts need a tokenizer (checkpoint directory); "
+                                 "pass token ids for preset / random-weight models")
+            return tok.encode(p), p
+        return list(p), None
+
+    def generate(self, prompts: Union[PromptType, Sequence[PromptType]],
+                 sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
+                 use_tqdm: bool = False) -> List[RequestOutput]:
+        if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and
+                                                isinstance(prompts[0], int)):
+            prompts = [prompts]
+        if sampling_params is None:
+            sampling_params = SamplingParams()
+        if isinstance(sampling_params, SamplingParams):
+            sampling_params = [sampling_params] * len(prompts)
+        order = []
+        for p, sp in zip(prompts, sampling_params):
+            ids, text = self._prompt_ids(p)
+            rid = str(self._counter)
+            self._counter += 1
+            self.engine.add_request(rid, ids, sp, prompt=text)
+            order.append(rid)
+        done = {}
+        while self.engine.has_unfinished_requests():
+            for o in self.engine.step():
+                if o.finished:
+                    done[o.request_id] = o
+        return [done[r] for r in order]
+
+    def shutdown(self):
+        self.engine.shutdown()
