@@ -1,0 +1,248 @@
+// NVSwitch peer-memory all-reduce fused with residual-add + RMSNorm, for tensor parallelism.
+//
+// Every rank owns an IPC-exported buffer holding (a) two staging slots that the preceding
+// row-parallel GEMM writes its partial sums into, (b) two output slots, (c) barrier flags.
+// Peers map each other's buffers (cudaIpcOpenMemHandle) and the kernels below read / write
+// them with plain 16-byte loads and stores over NVLink: no NCCL call, no staging copy, and
+// never a TMA (let alone multicast TMA) load from peer memory.
+//
+//  one-shot (small T):   start barrier; every rank reduces ALL rows from all peers' staging,
+//                        adds the (replicated) residual, normalises, writes its local output.
+//  two-shot (larger T):  start barrier; rank r reduces only its row chunk from all peers,
+//                        adds the residual rows it owns (the residual stream stays
+//                        row-sharded: rank r is the only writer of its rows), normalises, and
+//                        stores the normalised rows into EVERY rank's output slot (the
+//                        all-gather rides on posted P2P stores); end barrier.
+// Barriers are per block: block b of every rank bumps its own epoch counter, publishes it to
+// each peer's flag slot [phase][b][rank] with a release store, and spins (acquire loads,
+// bounded by a clock budget) until all peers' slots for block b reach the epoch.  Slots
+// alternate by call parity, so one start barrier also proves every peer finished the
+// previous call (which is what frees the other parity's buffers).  On a timeout the kernel
+// records kErrPeerTimeout in the error word and returns without touching the data.
+//
+// Reference counterpart: vllm_musa/jit_kernel/csrc/distributed/custom_all_reduce.mu:151-1126
+// (flag barrier, 1-stage / 2-stage / 2-shot reduce, fused AR + RMSNorm variants) driven by
+// vllm_musa/distributed/device_communicators/musa_jit_custom_all_reduce.py:440-1760.
+#include <algorithm>
+
+#include "../b200_kernels.h"
+#include "../common/common.cuh"
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include "custom_ar.h"
+
+namespace b200 {
+namespace comm {
+
+B200_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+B200_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Block-level barrier among the `world` ranks for block `b`.  Thread p (< world) signals
+// rank p and waits for rank p's signal.  Returns false on timeout.
+B200_DEVICE bool block_barrier(const ArParams& a, int phase, uint32_t epoch) {
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  const int b = blockIdx.x;
+  if (threadIdx.x < a.world) {
+    const int p = threadIdx.x;
+    uint32_t* peer_slot = a.flags[p] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + a.rank;
+    __threadfence_system();
+    st_release_sys(peer_slot, epoch);
+    const uint32_t* my_slot = a.flags[a.rank] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + p;
+    const long long t0 = clock64();
+    while ((int32_t)(ld_acquire_sys(my_slot) - epoch) < 0) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        record_error(a.err, kErrPeerTimeout);
+        ok_all = 0;
+        break;
+      }
+      if (error_raised(a.err)) {
+        ok_all = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return ok_all != 0;
+}
+
+// One row: sum the row over all ranks' staging, add residual, normalise.  VPT vectors of 8
+// bf16 per thread.  Writes residual (if any) and returns normalised values in `o`.
+template <int VPT, bool kNorm>
+B200_DEVICE void reduce_row(const ArParams& a, int row, float (&o)[VPT][8], float* red) {
+  const int nvec = a.H / 8;
+  float v[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+  for (int p = 0; p < a.world; ++p) {
+    const uint4* src = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const __nv_bfloat16*>(a.staging[p]) + (size_t)row * a.H);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        float f[8];
+        unpack8(src[c], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+      }
+    }
+  }
+  float ss = 0.f;
+  if (a.residual) {
+    uint4* rr = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.residual) +
+                                         (size_t)row * a.H);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        float r[8];
+        unpack8(rr[c], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+        const uint4 pk = pack8(v[i]);
+        rr[c] = pk;
+        unpack8(pk, v[i]);
+      }
+    }
+  }
+  if constexpr (kNorm) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+    ss = block_sum(ss, red);
+    const float inv = rsqrtf(ss / a.H + a.eps);
+    const uint4* wr = reinterpret_cast<const uint4*>(a.weight);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+        float w[8];
+        unpack8(wr[c], w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[i][j] = v[i][j] * inv * w[j];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[i][j] = v[i][j];
+  }
+}
+
+template <int VPT, bool kNorm, bool kTwoShot>
+__global__ void __launch_bounds__(1024) fused_ar_kernel(ArParams a) {
+  __shared__ float red[32];
+  __shared__ uint32_t epoch_s;
+  if (threadIdx.x == 0) {
+    epoch_s = a.epochs[blockIdx.x] + 1;
+    a.epochs[blockIdx.x] = epoch_s;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_s;
+  if (!block_barrier(a, a.parity, epoch)) return;
+  const int nvec = a.H / 8;
+  int r0 = 0, r1 = a.T;
+  if (kTwoShot) {
+    const int per = (a.T + a.world - 1) / a.world;
+    r0 = min(a.T, a.rank * per);
+    r1 = min(a.T, r0 + per);
+  }
+  for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+    float o[VPT][8];
+    reduce_row<VPT, kNorm>(a, row, o, red);
+    const int nout = kTwoShot ? a.world : 1;
+    for (int q = 0; q < nout; ++q) {
+      const int dst_rank = kTwoShot ? (a.rank + q) % a.world : a.rank;
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out[dst_rank]) +
+                                            (size_t)row * a.H);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < nvec) dst[c] = pack8(o[i]);
+      }
+    }
+  }
+  if (kTwoShot) block_barrier(a, 2 + a.parity, epoch);
+}
+
+template <bool kNorm, bool kTwoShot>
+static void launch(const ArParams& a, int threads, int vpt, int blocks, cudaStream_t s) {
+#define B200_AR(V) fused_ar_kernel<V, kNorm, kTwoShot><<<blocks, threads, 0, s>>>(a)
+  if (vpt <= 1)
+    B200_AR(1);
+  else if (vpt <= 2)
+    B200_AR(2);
+  else if (vpt <= 4)
+    B200_AR(4);
+  else
+    B200_AR(8);
+#undef B200_AR
+}
+
+void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
+  B200_REQUIRE(a.world >= 2 && a.world <= kMaxRanks, "custom all-reduce: world size");
+  B200_REQUIRE(a.H % 8 == 0 && a.H / 8 <= 1024 * 8, "custom all-reduce: hidden size");
+  B200_REQUIRE(a.blocks >= 1 && a.blocks <= kMaxBlocks, "custom all-reduce: block count");
+  if (a.T == 0) return;
+  const int nvec = a.H / 8;
+  int threads = 128;
+  while (threads < 1024 && (nvec + threads - 1) / threads > 2) threads *= 2;
+  const int vpt = (nvec + threads - 1) / threads;
+  B200_REQUIRE(vpt <= 8, "custom all-reduce: hidden size too large");
+  const bool norm = a.weight != nullptr;
+  if (a.two_shot) {
+    if (norm)
+      launch<true, true>(a, threads, vpt, a.blocks, s);
+    else
+      launch<false, true>(a, threads, vpt, a.blocks, s);
+  } else {
+    if (norm)
+      launch<true, false>(a, threads, vpt, a.blocks, s);
+    else
+      launch<false, false>(a, threads, vpt, a.blocks, s);
+  }
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
+// ------------------------------------------------------------------------------ IPC helpers
+void* ipc_malloc(size_t bytes) {
+  void* p = nullptr;
+  B200_CUDA_OK(cudaMalloc(&p, bytes));
+  B200_CUDA_OK(cudaMemset(p, 0, bytes));
+  return p;
+}
+void ipc_free(void* p) { B200_CUDA_OK(cudaFree(p)); }
+std::string ipc_handle(void* p) {
+  cudaIpcMemHandle_t h;
+  B200_CUDA_OK(cudaIpcGetMemHandle(&h, p));
+  return std::string(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+void* ipc_open(const std::string& handle) {
+  B200_REQUIRE(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  B200_CUDA_OK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+void ipc_close(void* p) { B200_CUDA_OK(cudaIpcCloseMemHandle(p)); }
+
+}  // namespace comm
+}  // namespace b200
