@@ -519,6 +519,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(b200::comm::ipc_handle(reinterpret_cast<void*>(p))); });
   m.def("ipc_open", [](const std::string& h) { return (int64_t)reinterpret_cast<uintptr_t>(b200::comm::ipc_open(h)); });
   m.def("ipc_close", [](int64_t p) { b200::comm::ipc_close(reinterpret_cast<void*>(p)); });
+  m.def("tensor_from_ptr",
+        [](int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtype, int64_t device) {
+          // non-owning view of device memory this library manages (IPC buffers)
+          return torch::from_blob(reinterpret_cast<void*>(ptr), shape, [](void*) {},
+                                  at::TensorOptions().dtype(dtype).device(at::kCUDA, device));
+        });
   m.def("comm_flag_bytes", []() { return (int64_t)(b200::comm::kFlagBytes + b200::comm::kEpochBytes); });
   m.def("comm_max_blocks", []() { return (int64_t)b200::comm::kMaxBlocks; });
   m.def("launch_count", []() { return (long long)b200::launch_counter().load(); },

@@ -78,7 +78,9 @@ class LLMEngine:
             custom = None
             if device.type == "cuda" and config.parallel.use_custom_allreduce:
                 from ..parallel.custom_ar import maybe_create_custom_allreduce
-                custom = maybe_create_custom_allreduce(st, device)
+                custom = maybe_create_custom_allreduce(
+                    st, device, max_tokens=config.scheduler.max_num_batched_tokens,
+                    hidden=mcfg.hidden_size)
             self.comm = TPCommunicator(st, device, custom)
             st.comm = self.comm
         else:

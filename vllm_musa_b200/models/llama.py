@@ -171,6 +171,8 @@ class DenseDecoderForCausalLM:
                 kv_caches: list) -> torch.Tensor:
         """input_ids int32 [T] -> final normalised hidden states [T, H]."""
         cfg, eps = self.cfg, self.cfg.rms_norm_eps
+        T = input_ids.shape[0]
+        self.comm.begin_forward()
         h = ops.embedding(input_ids, self.embed)
         residual = h
         x = ops.rms_norm(h, self.layers[0].ln1, eps)
@@ -181,10 +183,10 @@ class DenseDecoderForCausalLM:
             ops.rope_kv(qkv, meta.positions, self.cos_sin, kc, vc, meta.slot_mapping, self.hq,
                         self.hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm, eps)
             a = self.attn.forward(qkv, kc, vc, meta)
-            o = ops.linear(a, L.o_w)
+            o = ops.linear(a, L.o_w, out=self.comm.out_buffer(T))
             x, residual = self.comm.allreduce_add_rmsnorm(o, residual, L.ln2, eps)
             act = ops.linear_silu_mul(x, L.gu_w)
-            d = ops.linear(act, L.down_w)
+            d = ops.linear(act, L.down_w, out=self.comm.out_buffer(T))
             nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
             x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
         return x

@@ -39,11 +39,28 @@ class TPCommunicator:
     def all_gather(self, x: torch.Tensor, dim: int = 0) -> torch.Tensor:
         if self.world == 1:
             return x
-        out = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
-        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        if x.is_cuda:
+            out = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+            dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        else:
+            parts = [torch.empty_like(x) for _ in range(self.world)]
+            dist.all_gather(parts, x.contiguous(), group=self.group)
+            out = torch.stack(parts)
         if dim == 0:
             return out.reshape((-1,) + tuple(x.shape[1:]))
         return torch.cat(list(out.unbind(0)), dim=dim)
+
+    # -- buffers ----------------------------------------------------------------------------
+    def begin_forward(self) -> None:
+        """Called once at the start of every forward pass (resets the slot parity)."""
+        if self.custom is not None:
+            self.custom.begin_forward()
+
+    def out_buffer(self, T: int) -> Optional[torch.Tensor]:
+        """Where a row-parallel GEMM should write its [T, hidden] partial sums (None: anywhere)."""
+        if self.custom is not None and T <= self.custom.max_tokens:
+            return self.custom.staging_view(T)
+        return None
 
     # -- fused ------------------------------------------------------------------------------
     def allreduce_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,

@@ -1,0 +1,144 @@
+"""NVSwitch peer-memory communicator (CUDA IPC) for tensor-parallel all-reduce + RMSNorm.
+
+Per rank one cudaMalloc'd buffer, exported with cudaIpcGetMemHandle and opened by every peer:
+
+    [staging 0][staging 1][output 0][output 1][flags: 4 x 128 blocks x 8 ranks][epochs]
+
+The row-parallel GEMM (o_proj / down_proj) writes its partial sums straight into this rank's
+staging slot (``staging_view``); ``allreduce_add_rmsnorm`` then launches one kernel
+(csrc/comm/custom_ar.cu) that reduces over the peers' staging slots with NVLink loads, adds
+the residual, normalises and (two-shot) scatters the normalised rows into every rank's output
+slot with NVLink stores.  Slots alternate by call parity; each forward pass has an even
+number of calls and starts at parity 0, so consecutive calls always alternate.
+
+Set-up is fail-closed like the reference's (vllm_musa/distributed/device_communicators/
+musa_jit_custom_all_reduce.py:1762-1938, MIN consensus over a CPU group): if any rank cannot
+allocate, export or open a buffer, every rank falls back to NCCL.
+"""
+from __future__ import annotations
+
+import logging
+import os
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+
+log = logging.getLogger("vllm_musa_b200")
+
+ONE_SHOT_MAX_BYTES = int(os.environ.get("B200_AR_ONE_SHOT_MAX_BYTES", str(256 * 1024)))
+
+
+class CustomAllReduce:
+    def __init__(self, st, device: torch.device, max_tokens: int, hidden: int):
+        mod = _ext.require()
+        self.mod = mod
+        self.world, self.rank = st.tp_size, st.tp_rank
+        self.device = device
+        self.hidden = hidden
+        self.max_tokens = max_tokens
+        self.slot = (max_tokens * hidden * 2 + 255) // 256 * 256
+        self.flag_off = 4 * self.slot
+        total = self.flag_off + mod.comm_flag_bytes()
+        self.max_blocks = int(mod.comm_max_blocks())
+        self.base = mod.ipc_malloc(total)
+        self.opened = []
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mod.ipc_handle(self.base), group=st.tp_cpu_group)
+        self.peer_base = []
+        for p in range(self.world):
+            if p == self.rank:
+                self.peer_base.append(self.base)
+            else:
+                addr = mod.ipc_open(handles[p])
+                self.opened.append(addr)
+                self.peer_base.append(addr)
+        self.epochs = self.base + self.flag_off + (mod.comm_flag_bytes() - 128 * 4)
+        dev = device.index
+        self._staging = [mod.tensor_from_ptr(self.base + k * self.slot, [max_tokens, hidden],
+                                             torch.bfloat16, dev) for k in range(2)]
+        self._out = [mod.tensor_from_ptr(self.base + (2 + k) * self.slot, [max_tokens, hidden],
+                                         torch.bfloat16, dev) for k in range(2)]
+        self._bufs = []
+        for k in range(2):
+            staging = [b + k * self.slot for b in self.peer_base]
+            out = [b + (2 + k) * self.slot for b in self.peer_base]
+            flags = [b + self.flag_off for b in self.peer_base]
+            self._bufs.append(staging + out + flags)
+        self.parity = 0
+
+    # ------------------------------------------------------------------ interface
+    def begin_forward(self) -> None:
+        self.parity = 0
+
+    def can_run(self, x: torch.Tensor) -> bool:
+        return (x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] == self.hidden and
+                x.shape[0] <= self.max_tokens)
+
+    def staging_view(self, T: int) -> torch.Tensor:
+        return self._staging[self.parity][:T]
+
+    def _plan(self, T: int):
+        two_shot = T * self.hidden * 2 > ONE_SHOT_MAX_BYTES and T >= self.world
+        rows = (T + self.world - 1) // self.world if two_shot else T
+        return two_shot, max(1, min(rows, self.max_blocks))
+
+    def _run(self, x, residual, weight, eps):
+        T = x.shape[0]
+        if x.data_ptr() != self._staging[self.parity].data_ptr():
+            self._staging[self.parity][:T].copy_(x)
+        two_shot, blocks = self._plan(T)
+        self.mod.fused_allreduce(x, self._bufs[self.parity], self.epochs, self.rank, self.world,
+                                 T, self.hidden, blocks, self.parity, two_shot, residual, weight,
+                                 eps)
+        out = self._out[self.parity][:T]
+        self.parity ^= 1
+        return out
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        out = self._run(x, None, None, 0.0)
+        if out.data_ptr() != x.data_ptr():
+            x.copy_(out)
+        return x
+
+    def allreduce_add_rmsnorm(self, x, residual, weight, eps):
+        return self._run(x, residual, weight, eps), residual
+
+    def close(self) -> None:
+        for a in self.opened:
+            try:
+                self.mod.ipc_close(a)
+            except Exception:  # pragma: no cover - teardown
+                pass
+        self.opened = []
+        if self.base:
+            try:
+                torch.cuda.synchronize(self.device)
+                self.mod.ipc_free(self.base)
+            except Exception:  # pragma: no cover
+                pass
+            self.base = 0
+
+
+def maybe_create_custom_allreduce(st, device, max_tokens: int = 8192, hidden: int = 0
+                                  ) -> Optional[CustomAllReduce]:
+    """Build the communicator on every TP rank, or on none (MIN consensus over Gloo)."""
+    if st.tp_size < 2 or st.tp_size > 8 or hidden <= 0:
+        return None
+    if os.environ.get("B200_DISABLE_CUSTOM_AR", "0") == "1":
+        return None
+    comm, ok = None, 1
+    try:
+        comm = CustomAllReduce(st, device, max_tokens, hidden)
+    except Exception as e:  # fail closed
+        log.warning("custom all-reduce unavailable on rank %d: %s", st.rank, e)
+        ok = 0
+    t = torch.tensor([ok], dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=st.tp_cpu_group)
+    if int(t) == 0:
+        if comm is not None:
+            comm.close()
+        return None
+    return comm
