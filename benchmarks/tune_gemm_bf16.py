@@ -1,0 +1,108 @@
+"""Sweep the tcgen05 BF16 GEMM's plans (tile width BN x split-K) for a model's linear shapes
+and write the fastest plan per (N, K, M) to vllm_musa_b200/tuning/gemm_bf16.json.
+
+Timing: CUDA events on the launching stream, warm-up first, L2 flushed (a 256 MiB write)
+before every timed launch, median of --reps.  Also reports cuBLAS (torch.matmul) for the same
+shape as a yardstick and the achieved TB/s of weight streaming (decode) / TFLOP/s.
+
+    python benchmarks/tune_gemm_bf16.py --model llama3-8b --tp 1 [--write]
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from vllm_musa_b200 import ops  # noqa: E402
+from vllm_musa_b200.models.presets import get_preset  # noqa: E402
+from vllm_musa_b200.tuning import path_of  # noqa: E402
+
+M_BUCKETS = [1, 8, 16, 32, 64, 128, 192, 256, 384, 512, 1024, 2048, 4096, 8192]
+
+
+def model_shapes(name, tp):
+    c = get_preset(name)
+    H, D = c.hidden_size, c.head_dim
+    hq, hkv = c.num_heads // tp, max(1, c.num_kv_heads // tp)
+    I = c.intermediate_size // tp
+    I_pad = (I + 31) // 32 * 32
+    return {"qkv": ((hq + 2 * hkv) * D, H, 0), "o": (H, hq * D, 0), "gate_up": (2 * I_pad, H, 1),
+            "down": (H, I_pad, 0), "lm_head": (c.vocab_size // tp, H, 2)}
+
+
+def timed(fn, flush, reps):
+    for _ in range(3):
+        fn()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e) * 1e3)
+    return statistics.median(ts)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--reps", type=int, default=7)
+    ap.add_argument("--m", type=str, default=",".join(map(str, M_BUCKETS)))
+    ap.add_argument("--write", action="store_true")
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args()
+    mod = ops._ext.require()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ops.gemm.reserve_workspace(torch.device("cuda"), 64 << 20)
+    entries, report = [], []
+    for lname, (N, K, mode) in model_shapes(a.model, a.tp).items():
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        for M in map(int, a.m.split(",")):
+            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            out = torch.empty(M, N // 2 if mode == 1 else N, device="cuda",
+                              dtype=torch.float32 if mode == 2 else torch.bfloat16)
+            auto = mod.gemm_plan(M, N, K)
+            t_auto = timed(lambda: ops.gemm._run(x, w, out, mode, auto[0], auto[1]), flush, a.reps)
+            best = (t_auto, auto[0], auto[1])
+            kb = (K + 63) // 64
+            for bn in (64, 128, 256):
+                for s in (1, 2, 3, 4, 6, 8, 12, 16):
+                    if s > 1 and kb // s < 4:
+                        continue
+                    if s * M * N > (64 << 20):
+                        continue
+                    t = timed(lambda: ops.gemm._run(x, w, out, mode, bn, s), flush, a.reps)
+                    if t < best[0]:
+                        best = (t, bn, s)
+            t_cublas = timed(lambda: torch.matmul(x, w.t()), flush, a.reps)
+            tb = (N * K * 2 + M * K * 2 + M * N * 2) / (best[0] * 1e-6) / 1e12
+            tf = 2 * M * N * K / (best[0] * 1e-6) / 1e12
+            report.append(dict(layer=lname, M=M, N=N, K=K, auto=list(auto[:2]), t_auto_us=round(t_auto, 1),
+                               best_bn=best[1], best_splits=best[2], t_best_us=round(best[0], 1),
+                               cublas_us=round(t_cublas, 1), TBps=round(tb, 2), TFLOPs=round(tf, 1)))
+            print(json.dumps(report[-1]), flush=True)
+            entries.append({"n": N, "k": K, "m": M, "bn": best[1], "splits": best[2],
+                            "us": round(best[0], 2)})
+    table = {"device": torch.cuda.get_device_name(), "model": a.model, "tp": a.tp,
+             "entries": entries}
+    if a.write:
+        path = a.out or path_of("gemm_bf16")
+        old = {"entries": []}
+        if os.path.exists(path):
+            old = json.load(open(path))
+        keep = [e for e in old["entries"] if (e["n"], e["k"]) not in {(x["n"], x["k"]) for x in entries}]
+        table["entries"] = keep + entries
+        with open(path, "w") as f:
+            json.dump(table, f, indent=1)
+        print("wrote", path)
+
+
+if __name__ == "__main__":
+    main()

@@ -46,11 +46,21 @@ B200_DEVICE float uniform_open(uint32_t bits) {
   return ((float)(bits >> 8) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
 }
 
+// Gumbel(0,1) from 32 random bits: G = -log(E), E = -log(u) ~ Exp(1).  The inner log is the
+// accurate one (u near 1 gives the largest G, which decides the argmax); the outer log's
+// argument E is away from the ill-conditioned point, so the fast log is accurate enough.
+B200_DEVICE float gumbel_from_bits(uint32_t b) { return -__logf(-logf(uniform_open(b))); }
+
+B200_DEVICE U4 philox_group(uint64_t seed, uint32_t step, uint32_t group) {
+  return philox(U4{group, step, 0x5a4d5153u, 0u}, (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+
+// Noise of global token `idx`: component (idx & 3) of the Philox block of group idx >> 2.
 B200_DEVICE float gumbel(uint64_t seed, uint32_t step, uint32_t idx) {
-  const U4 r = philox(U4{idx >> 2, step, 0x5a4d5153u, 0u}, (uint32_t)seed, (uint32_t)(seed >> 32));
+  const U4 r = philox_group(seed, step, idx >> 2);
   const uint32_t sel = idx & 3;
   const uint32_t b = sel == 0 ? r.x : sel == 1 ? r.y : sel == 2 ? r.z : r.w;
-  return -logf(-logf(uniform_open(b)));
+  return gumbel_from_bits(b);
 }
 
 B200_DEVICE uint32_t fkey(float f) {
@@ -196,12 +206,35 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t seed = seeds ? (uint64_t)seeds[row] : 0ull;
   const uint32_t step = steps ? (uint32_t)steps[row] : 0u;
   Cand best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float l = x[i] * inv_t;
-    if (fkey(l) < floor_key) continue;
-    const int gi = vocab_offset + i;
-    const float sc = greedy ? l : l + gumbel(seed, step, (uint32_t)gi);
-    best = better(best, Cand{sc, gi});
+  const bool vec = ((vocab_offset | V) & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  if (vec) {
+    // four consecutive tokens per thread: one 16-byte load and one Philox block per group
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const uint32_t g0 = (uint32_t)vocab_offset >> 2;
+    for (int j = threadIdx.x; j < V / 4; j += blockDim.x) {
+      const float4 v = x4[j];
+      const float l[4] = {v.x * inv_t, v.y * inv_t, v.z * inv_t, v.w * inv_t};
+      const int gi = vocab_offset + 4 * j;
+      if (greedy) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) best = better(best, Cand{l[e], gi + e});
+      } else {
+        const U4 r = philox_group(seed, step, g0 + j);
+        const uint32_t bits[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (fkey(l[e]) >= floor_key)
+            best = better(best, Cand{l[e] + gumbel_from_bits(bits[e]), gi + e});
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float l = x[i] * inv_t;
+      if (fkey(l) < floor_key) continue;
+      const int gi = vocab_offset + i;
+      const float sc = greedy ? l : l + gumbel(seed, step, (uint32_t)gi);
+      best = better(best, Cand{sc, gi});
+    }
   }
   // block argmax
 #pragma unroll

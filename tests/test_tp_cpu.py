@@ -52,3 +52,36 @@ def test_tp2_greedy_matches_tp1():
     two = _run(2)
     assert two[0] == two[1], "ranks diverged"
     assert two[0] == one
+
+
+def test_tp2_spawned_followers_match_tp1():
+    """LLM(tensor_parallel_size=2) without a launcher: the driver spawns a follower rank and
+    broadcasts request operations each step."""
+    import subprocess
+    import sys
+    code = r'''
+import torch, os
+torch.set_num_threads(1)
+from vllm_musa_b200 import LLM, SamplingParams
+from vllm_musa_b200.models.presets import tiny_llama
+llm = LLM(tiny_llama(), device="cpu", tensor_parallel_size=2, block_size=16, seed=0,
+          num_gpu_blocks=64, max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64)
+g = torch.Generator().manual_seed(0)
+prompts = torch.randint(0, 1024, (3, 20), generator=g).tolist()
+outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
+print("TOKENS", [o.outputs[0].token_ids for o in outs])
+outs2 = llm.generate(prompts[:1], SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True))
+print("TOKENS2", [o.outputs[0].token_ids for o in outs2])
+llm.shutdown()
+'''
+    env = dict(os.environ)
+    env.pop("WORLD_SIZE", None)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                       env=env, cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stderr[-4000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("TOKENS ")][0]
+    toks = eval(line[len("TOKENS "):])
+    one = _run(1)[0]
+    assert toks == one
+    line2 = [l for l in r.stdout.splitlines() if l.startswith("TOKENS2 ")][0]
+    assert eval(line2[len("TOKENS2 "):])[0] == one[0][:4]

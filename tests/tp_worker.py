@@ -1,0 +1,106 @@
+"""Worker for the multi-GPU tests (run under torchrun by tests/test_tp_gpu.py).
+
+--mode ar   : fused all-reduce + residual + RMSNorm kernel vs NCCL all-reduce + PyTorch math,
+              one-shot and two-shot sizes, several calls in a row (parity / epoch reuse).
+--mode llm  : greedy generation of a small Llama-architecture model at TP = WORLD_SIZE;
+              writes tokens and first-step logits (gathered to full vocab) as JSON.
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def small_cfg():
+    from vllm_musa_b200.config import ModelConfig
+    return ModelConfig(arch="llama", vocab_size=4096, hidden_size=1024, num_layers=3,
+                       num_heads=16, num_kv_heads=4, head_dim=64, intermediate_size=2816,
+                       rms_norm_eps=1e-6, rope_theta=1e4, max_position=2048, name="tp-test")
+
+
+def mode_ar(out_path):
+    from vllm_musa_b200 import ops
+    from vllm_musa_b200.parallel.custom_ar import maybe_create_custom_allreduce
+    from vllm_musa_b200.parallel.state import init_distributed
+    world = int(os.environ["WORLD_SIZE"])
+    st = init_distributed(tp_size=world)
+    dev = torch.device("cuda", st.local_rank)
+    H = 4096
+    ar = maybe_create_custom_allreduce(st, dev, max_tokens=2048, hidden=H)
+    assert ar is not None, "custom all-reduce did not initialise"
+    errs = []
+    g = torch.Generator(device="cpu").manual_seed(123)
+    w = (torch.randn(H, generator=g) * 0.1 + 1).to(torch.bfloat16).to(dev)
+    for it, T in enumerate([1, 7, 32, 256, 1000, 2048, 5]):
+        ar.begin_forward() if it % 2 == 0 else None
+        gen = torch.Generator(device="cpu").manual_seed(1000 * it + st.rank)
+        x = torch.randn(T, H, generator=gen).to(torch.bfloat16).to(dev)
+        gres = torch.Generator(device="cpu").manual_seed(77 + it)
+        res = torch.randn(T, H, generator=gres).to(torch.bfloat16).to(dev)
+        # reference: NCCL sum then fused norm math in fp32
+        ref_sum = x.float().clone()
+        dist.all_reduce(ref_sum, group=st.tp_group)
+        ref_res = (ref_sum + res.float()).to(torch.bfloat16)
+        ref_out = ops.norm._rms_ref(ref_res, w, 1e-6, False)
+        stg = ar.staging_view(T)
+        stg.copy_(x)
+        out, res2 = ar.allreduce_add_rmsnorm(stg, res.clone(), w, 1e-6)
+        torch.cuda.synchronize()
+        two_shot, _ = ar._plan(T)
+        if two_shot:
+            per = (T + world - 1) // world
+            r0, r1 = min(T, st.rank * per), min(T, st.rank * per + per)
+            dres = (res2[r0:r1].float() - ref_res[r0:r1].float()).abs().max().item() if r1 > r0 else 0.0
+        else:
+            dres = (res2.float() - ref_res.float()).abs().max().item()
+        dout = (out.float() - ref_out.float()).abs().max().item()
+        errs.append({"T": T, "two_shot": two_shot, "dout": dout, "dres": dres})
+    ops._ext.check_device_errors()
+    ar.close()
+    if st.rank == 0:
+        with open(out_path, "w") as f:
+            json.dump(errs, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def mode_llm(out_path, tp, eager):
+    from vllm_musa_b200 import LLM, SamplingParams
+    from vllm_musa_b200.parallel.state import destroy_distributed, get_parallel_state
+    llm = LLM(small_cfg(), tensor_parallel_size=tp, block_size=64, seed=0, num_gpu_blocks=256,
+              max_model_len=1024, max_num_seqs=16, max_num_batched_tokens=1024,
+              enforce_eager=eager, cuda_graph_sizes=[1, 2, 4, 8, 16])
+    llm.engine.runner.record_logits = True
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (7, 100, 300, 64)]
+    outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True))
+    first = llm.engine.runner.logits_log[0].cuda()
+    st = get_parallel_state()
+    if st.tp_size > 1:
+        parts = [torch.empty_like(first) for _ in range(st.tp_size)]
+        dist.all_gather(parts, first, group=st.tp_group)
+        first = torch.cat(parts, dim=1)
+    res = {"tokens": [o.outputs[0].token_ids for o in outs], "logits0": first.cpu().tolist(),
+           "rank": st.rank}
+    with open(f"{out_path}.{st.rank}", "w") as f:
+        json.dump(res, f)
+    llm.shutdown()
+    destroy_distributed()
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["ar", "llm"], required=True)
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--eager", action="store_true")
+    a = ap.parse_args()
+    if a.mode == "ar":
+        mode_ar(a.out)
+    else:
+        mode_llm(a.out, a.tp, a.eager)

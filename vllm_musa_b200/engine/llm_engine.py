@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import itertools
 import logging
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
@@ -125,6 +126,12 @@ class LLMEngine:
         self.step_end_times: List[float] = []
         self.stream_outputs = False
         self.num_steps = 0
+        # multi-process TP without torchrun: the driver broadcasts request ops every step
+        self.role = os.environ.get("B200_SPMD_ROLE", "replicated") if st.tp_size > 1 else "single"
+        self.sync = None
+        if self.role in ("driver", "follower"):
+            from .executor import StepSync
+            self.sync = StepSync(st.tp_cpu_group, st.tp_rank)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_token_ids: List[int],
@@ -132,6 +139,10 @@ class LLMEngine:
                     prompt: Optional[str] = None) -> None:
         params = params or SamplingParams()
         arrival = time.time() if arrival_time is None else arrival_time
+        if self.sync is not None:
+            if self.role == "follower":
+                raise RuntimeError("requests are added on the driver rank only")
+            self.sync.record(("add", request_id, list(prompt_token_ids), params, arrival, prompt))
         if params.n > 1:
             self._parents[request_id] = {"n": params.n, "done": {}, "prompt_ids": prompt_token_ids,
                                          "prompt": prompt, "arrival": arrival}
@@ -166,6 +177,8 @@ class LLMEngine:
         self._by_name[name] = iid
 
     def abort_request(self, request_id: str) -> None:
+        if self.sync is not None and self.role == "driver":
+            self.sync.record(("abort", request_id))
         names = [request_id] + [n for n in self._by_name if n.startswith(request_id + "#")]
         for n in names:
             iid = self._by_name.get(n)
@@ -181,6 +194,18 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ stepping
     def step(self) -> List[RequestOutput]:
+        if self.sync is not None:
+            ops_ = self.sync.exchange()
+            if self.role == "follower":
+                for op in ops_:
+                    if op[0] == "add":
+                        self._follower_add(*op[1:])
+                    elif op[0] == "abort":
+                        self.abort_request(op[1])
+                    elif op[0] == "shutdown":
+                        self._stop = True
+            if not self.scheduler.has_unfinished():
+                return []
         plan = self.scheduler.schedule()
         if plan.num_reqs == 0:
             return []
@@ -253,8 +278,28 @@ class LLMEngine:
         m = RequestMetrics(r.arrival, first if first is not None else r.first_token_time, last)
         return RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
 
+    def _follower_add(self, request_id, prompt_ids, params, arrival, prompt):
+        sync, self.sync = self.sync, None  # apply locally without re-recording
+        try:
+            self.add_request(request_id, prompt_ids, params, arrival, prompt)
+        finally:
+            self.sync = sync
+
+    def follow(self) -> None:
+        """Follower rank main loop: mirror the driver's steps until it shuts down."""
+        self._stop = False
+        while not self._stop:
+            self.step()
+
+    def stop_followers(self) -> None:
+        if self.sync is not None and self.role == "driver":
+            self.sync.record(("shutdown",))
+            self.sync.exchange()
+            self.sync = None
+
     # ------------------------------------------------------------------ lifecycle
     def shutdown(self) -> None:
+        self.stop_followers()
         self.runner.release_graphs()
         if self.comm is not None and hasattr(self.comm, "close"):
             self.comm.close()

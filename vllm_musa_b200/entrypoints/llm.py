@@ -72,6 +72,11 @@ class LLM:
             device=device, seed=seed, load_format=load_format, model_path=path,
             enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes)
         tok = tokenizer if tokenizer is not None else _load_tokenizer(path)
+        self.executor = None
+        if tensor_parallel_size > 1 and "WORLD_SIZE" not in os.environ:
+            # no launcher: spawn follower ranks and drive them from this process
+            from ..engine.executor import MultiprocExecutor
+            self.executor = MultiprocExecutor(cfg, tensor_parallel_size)
         self.engine = LLMEngine(cfg, tok)
         self._counter = 0
 
@@ -117,3 +122,8 @@ class LLM:
 
     def shutdown(self):
         self.engine.shutdown()
+        if self.executor is not None:
+            from ..parallel.state import destroy_distributed
+            destroy_distributed()
+            self.executor.shutdown()
+            self.executor = None

@@ -10,6 +10,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _ext
+from .. import tuning
 
 _WS: dict = {}
 
@@ -31,14 +32,23 @@ def reserve_workspace(device: torch.device, numel: int) -> None:
     _workspace(device, numel)
 
 
+def plan_for(M: int, N: int, K: int, bn: int = 0, splits: int = 0) -> tuple:
+    """(bn, splits, workspace_floats): forced plan, else the measured table, else the
+    kernel's cost model (bn = splits = 0 lets the launcher decide)."""
+    if bn <= 0 and splits <= 0:
+        hit = tuning.gemm_table().lookup(M, N, K)
+        if hit is not None:
+            bn, splits = hit
+    if bn > 0 or splits > 0:
+        return bn, splits, (splits if splits > 1 else 0) * M * N
+    _, s, need = _ext.require().gemm_plan(M, N, K)
+    return 0, 0, need
+
+
 def _run(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, mode: int, bn: int = 0,
          splits: int = 0) -> torch.Tensor:
-    mod = _ext.require()
     M, N, K = x.shape[0], w.shape[0], x.shape[1]
-    if bn > 0 or splits > 0:
-        need = (splits if splits > 1 else 0) * M * N
-    else:
-        _, s, need = mod.gemm_plan(M, N, K)
+    bn, splits, need = plan_for(M, N, K, bn, splits)
     ws = _workspace(x.device, need) if need > 0 else None
     torch.ops.b200.gemm_bf16(x, w, out, mode, bn, splits, ws)
     return out
