@@ -1,8 +1,9 @@
 """Sweep the tcgen05 BF16 GEMM's plans (tile width BN x split-K) for a model's linear shapes
 and write the fastest plan per (N, K, M) to vllm_musa_b200/tuning/gemm_bf16.json.
 
-Timing: CUDA events on the launching stream, warm-up first, L2 flushed (a 256 MiB write)
-before every timed launch, median of --reps.  Also reports cuBLAS (torch.matmul) for the same
+Timing: CUDA events on the launching stream after warm-up; launches cycle through copies of
+the weight whose total exceeds L2 (every launch reads its weight from HBM), averaged over a
+back-to-back loop; median of --reps.  Also reports cuBLAS (torch.matmul) for the same
 shape as a yardstick and the achieved TB/s of weight streaming (decode) / TFLOP/s.
 
     python benchmarks/tune_gemm_bf16.py --model llama3-8b --tp 1 [--write]
@@ -34,18 +35,25 @@ def model_shapes(name, tp):
             "down": (H, I_pad, 0), "lm_head": (c.vocab_size // tp, H, 2)}
 
 
-def timed(fn, flush, reps):
-    for _ in range(3):
-        fn()
+L2_BYTES = 126 << 20
+
+
+def timed(fn, ws, reps):
+    """Median per-launch time of ``fn(w)`` cycling through weight copies ``ws`` whose total
+    size exceeds L2, so every launch streams its weights from HBM (as consecutive layers do
+    in a decode step); each sample averages a back-to-back loop of launches."""
+    for w in ws:
+        fn(w)
+    loop = max(8, len(ws))
     ts = []
     for _ in range(reps):
-        flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        fn()
+        for i in range(loop):
+            fn(ws[i % len(ws)])
         e.record()
         torch.cuda.synchronize()
-        ts.append(s.elapsed_time(e) * 1e3)
+        ts.append(s.elapsed_time(e) * 1e3 / loop)
     return statistics.median(ts)
 
 
@@ -59,17 +67,17 @@ def main():
     ap.add_argument("--out", default=None)
     a = ap.parse_args()
     mod = ops._ext.require()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     ops.gemm.reserve_workspace(torch.device("cuda"), 64 << 20)
     entries, report = [], []
     for lname, (N, K, mode) in model_shapes(a.model, a.tp).items():
-        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        copies = max(2, -(-3 * L2_BYTES // (N * K * 2)))
+        ws = [(torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
         for M in map(int, a.m.split(",")):
             x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
             out = torch.empty(M, N // 2 if mode == 1 else N, device="cuda",
                               dtype=torch.float32 if mode == 2 else torch.bfloat16)
             auto = mod.gemm_plan(M, N, K)
-            t_auto = timed(lambda: ops.gemm._run(x, w, out, mode, auto[0], auto[1]), flush, a.reps)
+            t_auto = timed(lambda w: ops.gemm._run(x, w, out, mode, auto[0], auto[1]), ws, a.reps)
             best = (t_auto, auto[0], auto[1])
             kb = (K + 63) // 64
             for bn in (64, 128, 256):
@@ -78,10 +86,10 @@ def main():
                         continue
                     if s * M * N > (64 << 20):
                         continue
-                    t = timed(lambda: ops.gemm._run(x, w, out, mode, bn, s), flush, a.reps)
+                    t = timed(lambda w: ops.gemm._run(x, w, out, mode, bn, s), ws, a.reps)
                     if t < best[0]:
                         best = (t, bn, s)
-            t_cublas = timed(lambda: torch.matmul(x, w.t()), flush, a.reps)
+            t_cublas = timed(lambda w: torch.matmul(x, w.t()), ws, a.reps)
             tb = (N * K * 2 + M * K * 2 + M * N * 2) / (best[0] * 1e-6) / 1e12
             tf = 2 * M * N * K / (best[0] * 1e-6) / 1e12
             report.append(dict(layer=lname, M=M, N=N, K=K, auto=list(auto[:2]), t_auto_us=round(t_auto, 1),

@@ -1,0 +1,91 @@
+"""OpenAI-compatible server on the tiny CPU model: completions (token ids and text through a
+toy tokenizer), streaming, chat, n > 1, stop strings, models / health / metrics."""
+import json
+
+import pytest
+import torch
+
+from vllm_musa_b200 import LLM
+from vllm_musa_b200.engine.async_llm import AsyncLLM
+from vllm_musa_b200.entrypoints.openai.api_server import build_app
+from vllm_musa_b200.models.presets import tiny_llama
+
+
+class ToyTokenizer:
+    """Byte-level toy tokenizer over the tiny model's 1024-token vocabulary."""
+    chat_template = None
+
+    def encode(self, text):
+        return [b % 1024 for b in text.encode()]
+
+    def decode(self, ids, skip_special_tokens=True):
+        return "".join(chr(32 + (i % 90)) for i in ids)
+
+
+@pytest.fixture(scope="module")
+def client():
+    from fastapi.testclient import TestClient
+    llm = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=128,
+              max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256,
+              tokenizer=ToyTokenizer())
+    alm = AsyncLLM(llm.engine)
+    app = build_app(alm, "tiny", 256)
+    with TestClient(app) as c:
+        yield c, llm
+    alm.shutdown()
+
+
+def test_models_health_metrics(client):
+    c, _ = client
+    assert c.get("/health").status_code == 200
+    assert c.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    assert "b200_request_success_total" in c.get("/metrics").text
+
+
+def test_completion_token_ids_matches_offline(client):
+    c, llm = client
+    prompt = list(range(10, 40))
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 6, "temperature": 0,
+                                        "ignore_eos": True}).json()
+    assert r["usage"]["completion_tokens"] == 6
+    ref = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=64,
+              max_model_len=256, max_num_seqs=4, max_num_batched_tokens=256)
+    from vllm_musa_b200 import SamplingParams
+    want = ref.generate([prompt], SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+    assert r["choices"][0]["token_ids"] == want[0].outputs[0].token_ids
+
+
+def test_text_prompt_n2_and_stop(client):
+    c, _ = client
+    r = c.post("/v1/completions", json={"prompt": "hello", "max_tokens": 5, "n": 2,
+                                        "temperature": 1.0, "seed": 3, "ignore_eos": True}).json()
+    assert len(r["choices"]) == 2 and all(len(ch["text"]) == 5 for ch in r["choices"])
+    full = c.post("/v1/completions", json={"prompt": "hello", "max_tokens": 8, "temperature": 0,
+                                           "ignore_eos": True}).json()["choices"][0]["text"]
+    stop = full[3:5]
+    r = c.post("/v1/completions", json={"prompt": "hello", "max_tokens": 8, "temperature": 0,
+                                        "ignore_eos": True, "stop": [stop]}).json()
+    assert r["choices"][0]["text"] == full[:full.find(stop)]
+    assert r["choices"][0]["finish_reason"] == "stop"
+
+
+def test_streaming_and_chat(client):
+    c, _ = client
+    with c.stream("POST", "/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4,
+                                                  "temperature": 0, "ignore_eos": True,
+                                                  "stream": True}) as r:
+        events = [l for l in r.iter_lines() if l.startswith("data: ")]
+    assert events[-1] == "data: [DONE]"
+    text = "".join(json.loads(e[6:])["choices"][0]["text"] for e in events[:-1])
+    assert len(text) == 4
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                             "max_tokens": 3, "temperature": 0,
+                                             "ignore_eos": True}).json()
+    assert r["choices"][0]["message"]["role"] == "assistant"
+    assert r["usage"]["completion_tokens"] == 3
+
+
+def test_bad_request(client):
+    c, _ = client
+    r = c.post("/v1/completions", json={"prompt": list(range(300)), "max_tokens": 4})
+    assert r.status_code == 400

@@ -1,0 +1,265 @@
+"""OpenAI-compatible HTTP server (``/v1/completions``, ``/v1/chat/completions``,
+``/v1/models``, ``/health``, ``/metrics``), the role ``vllm serve`` plays for the reference
+(usage: docs/usage.md of the reference).
+
+    python -m vllm_musa_b200.entrypoints.openai.api_server --model /path/or/preset --port 8000
+    b200-vllm serve llama3-8b --tensor-parallel-size 8
+
+Tensor parallelism: without a launcher the server process spawns its follower ranks; under
+``torchrun`` rank 0 serves HTTP and the other ranks follow it.
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import logging
+import os
+import time
+import uuid
+from typing import List, Optional
+
+from .protocol import (ChatChoice, ChatCompletionRequest, ChatCompletionResponse, ChatMessage,
+                       CompletionChoice, CompletionRequest, CompletionResponse, ErrorResponse,
+                       ModelCard, ModelList, Usage)
+
+log = logging.getLogger("vllm_musa_b200")
+
+
+def _chat_prompt(tokenizer, messages: List[ChatMessage]) -> List[int]:
+    msgs = [m.model_dump() for m in messages]
+    if tokenizer is None:
+        raise ValueError("chat completions need a tokenizer (serve a checkpoint directory)")
+    if getattr(tokenizer, "chat_template", None):
+        ids = tokenizer.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)
+        return list(ids["input_ids"] if isinstance(ids, dict) else ids)
+    text = "".join(f"{m['role']}: {m['content']}\n" for m in msgs) + "assistant:"
+    return tokenizer.encode(text)
+
+
+def build_app(llm, model_name: str, max_model_len: int):
+    """FastAPI app over an ``AsyncLLM``."""
+    from fastapi import FastAPI, Request
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    from ...sample.sampling_params import SamplingParams
+    from ...engine.async_llm import AsyncLLM  # noqa: F401  (type)
+
+    app = FastAPI(title="vllm_musa_b200 OpenAI-compatible server")
+    tok = llm.tokenizer
+    default_max = 16
+
+    def err(msg: str, code: int = 400):
+        return JSONResponse(ErrorResponse(message=msg, code=code).model_dump(), status_code=code)
+
+    def encode_prompts(prompt) -> List[tuple]:
+        if isinstance(prompt, str):
+            if tok is None:
+                raise ValueError("text prompts need a tokenizer; send token ids instead")
+            return [(tok.encode(prompt), prompt)]
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+            return [(list(prompt), None)]
+        out = []
+        for p in prompt:
+            out += encode_prompts(p)
+        return out
+
+    def check_len(ids, params: SamplingParams):
+        if len(ids) + 1 > max_model_len:
+            raise ValueError(f"prompt has {len(ids)} tokens; max_model_len is {max_model_len}")
+        params.max_tokens = min(params.max_tokens, max_model_len - len(ids))
+
+    @app.get("/health")
+    async def health():
+        return PlainTextResponse("ok")
+
+    @app.get("/version")
+    async def version():
+        from ... import __version__
+        return {"version": __version__}
+
+    @app.get("/v1/models")
+    async def models():
+        return ModelList(data=[ModelCard(id=model_name, max_model_len=max_model_len)]).model_dump()
+
+    @app.get("/metrics")
+    async def metrics():
+        s = llm.stats
+        eng = llm.engine
+        lines = [
+            "# TYPE b200_request_success_total counter",
+            f"b200_request_success_total {s['finished']}",
+            "# TYPE b200_prompt_tokens_total counter",
+            f"b200_prompt_tokens_total {s['prompt_tokens']}",
+            "# TYPE b200_generation_tokens_total counter",
+            f"b200_generation_tokens_total {s['generation_tokens']}",
+            "# TYPE b200_num_requests_running gauge",
+            f"b200_num_requests_running {eng.scheduler.num_running()}",
+            "# TYPE b200_num_requests_waiting gauge",
+            f"b200_num_requests_waiting {eng.scheduler.num_waiting()}",
+            "# TYPE b200_kv_cache_free_blocks gauge",
+            f"b200_kv_cache_free_blocks {eng.scheduler.num_free_blocks()}",
+        ]
+        for name, vals in (("time_to_first_token_seconds", s["ttft"]),
+                           ("time_per_output_token_seconds", s["tpot"])):
+            lines.append(f"# TYPE b200_{name} summary")
+            lines.append(f"b200_{name}_count {len(vals)}")
+            lines.append(f"b200_{name}_sum {sum(vals):.6f}")
+        return PlainTextResponse("\n".join(lines) + "\n")
+
+    async def run_one(ids, params, rid):
+        final = None
+        async for o in llm.generate(ids, params, rid):
+            final = o
+        return final
+
+    @app.post("/v1/completions")
+    async def completions(req: CompletionRequest):
+        try:
+            prompts = encode_prompts(req.prompt)
+            base = req.sampling_params(default_max)
+            jobs = []
+            for pi, (ids, text) in enumerate(prompts):
+                for k in range(base.n):
+                    p = SamplingParams(**{**base.__dict__, "n": 1})
+                    if base.seed is not None:
+                        p.seed = base.seed + k
+                    check_len(ids, p)
+                    jobs.append((pi * base.n + k, ids, text, p))
+        except ValueError as e:
+            return err(str(e))
+        rid = f"cmpl-{uuid.uuid4().hex}"
+        if req.stream:
+            async def gen():
+                qs = []
+                for idx, ids, text, p in jobs:
+                    qs.append((idx, llm.generate(ids, p, f"{rid}-{idx}")))
+                for idx, it in qs:
+                    sent = ""
+                    async for o in it:
+                        c = o.outputs[0]
+                        delta = c.text[len(sent):]
+                        sent = c.text
+                        chunk = {"id": rid, "object": "text_completion", "created": int(time.time()),
+                                 "model": model_name,
+                                 "choices": [{"index": idx, "text": delta,
+                                              "token_ids": c.token_ids[-1:] if c.token_ids else [],
+                                              "finish_reason": c.finish_reason if o.finished else None}]}
+                        yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}") for idx, ids, _, p in jobs])
+        choices, n_prompt, n_gen = [], 0, 0
+        for (idx, ids, text, _), o in zip(jobs, outs):
+            c = o.outputs[0]
+            body = (text or "") + c.text if req.echo else c.text
+            choices.append(CompletionChoice(index=idx, text=body, token_ids=c.token_ids,
+                                            finish_reason=c.finish_reason))
+            n_prompt += len(ids)
+            n_gen += len(c.token_ids)
+        return CompletionResponse(id=rid, model=model_name, choices=choices,
+                                  usage=Usage(prompt_tokens=n_prompt, completion_tokens=n_gen,
+                                              total_tokens=n_prompt + n_gen)).model_dump()
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: ChatCompletionRequest):
+        try:
+            ids = _chat_prompt(tok, req.messages)
+            p = req.sampling_params(req.max_completion_tokens or default_max)
+            if req.max_completion_tokens:
+                p.max_tokens = req.max_completion_tokens
+            check_len(ids, p)
+        except ValueError as e:
+            return err(str(e))
+        rid = f"chatcmpl-{uuid.uuid4().hex}"
+        if req.stream:
+            async def gen():
+                sent = ""
+                async for o in llm.generate(ids, SamplingParams(**{**p.__dict__, "n": 1}), rid):
+                    c = o.outputs[0]
+                    delta = c.text[len(sent):]
+                    sent = c.text
+                    chunk = {"id": rid, "object": "chat.completion.chunk", "created": int(time.time()),
+                             "model": model_name,
+                             "choices": [{"index": 0, "delta": {"role": "assistant", "content": delta},
+                                          "finish_reason": c.finish_reason if o.finished else None}]}
+                    yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        outs = await asyncio.gather(*[
+            run_one(ids, SamplingParams(**{**p.__dict__, "n": 1,
+                                           "seed": (p.seed + k) if p.seed is not None else None}),
+                    f"{rid}-{k}") for k in range(p.n)])
+        choices = [ChatChoice(index=k, message=ChatMessage(role="assistant", content=o.outputs[0].text),
+                              finish_reason=o.outputs[0].finish_reason) for k, o in enumerate(outs)]
+        n_gen = sum(len(o.outputs[0].token_ids) for o in outs)
+        return ChatCompletionResponse(id=rid, model=model_name, choices=choices,
+                                      usage=Usage(prompt_tokens=len(ids), completion_tokens=n_gen,
+                                                  total_tokens=len(ids) + n_gen)).model_dump()
+
+    return app
+
+
+def make_arg_parser(p: Optional[argparse.ArgumentParser] = None) -> argparse.ArgumentParser:
+    p = p or argparse.ArgumentParser(description="vllm_musa_b200 OpenAI-compatible server")
+    p.add_argument("--model", default="llama3-8b", help="checkpoint directory or preset name")
+    p.add_argument("--served-model-name", default=None)
+    p.add_argument("--host", default="0.0.0.0")
+    p.add_argument("--port", type=int, default=8000)
+    p.add_argument("--tensor-parallel-size", "-tp", type=int, default=1)
+    p.add_argument("--enable-expert-parallel", action="store_true")
+    p.add_argument("--max-model-len", type=int, default=None)
+    p.add_argument("--max-num-seqs", type=int, default=256)
+    p.add_argument("--max-num-batched-tokens", type=int, default=8192)
+    p.add_argument("--block-size", type=int, default=64)
+    p.add_argument("--gpu-memory-utilization", type=float, default=0.90)
+    p.add_argument("--enforce-eager", action="store_true")
+    p.add_argument("--no-enable-prefix-caching", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--device", default="cuda")
+    p.add_argument("--num-gpu-blocks", type=int, default=None)
+    return p
+
+
+def build_llm(args):
+    from ..llm import LLM
+    return LLM(args.model, tensor_parallel_size=args.tensor_parallel_size,
+               enable_expert_parallel=args.enable_expert_parallel,
+               max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs,
+               max_num_batched_tokens=args.max_num_batched_tokens, block_size=args.block_size,
+               gpu_memory_utilization=args.gpu_memory_utilization,
+               enforce_eager=args.enforce_eager,
+               enable_prefix_caching=not args.no_enable_prefix_caching, seed=args.seed,
+               device=args.device, num_gpu_blocks=args.num_gpu_blocks)
+
+
+def run_server(args) -> None:
+    import uvicorn
+
+    from ...engine.async_llm import AsyncLLM
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        os.environ["B200_SPMD_ROLE"] = "driver" if rank == 0 else "follower"
+    llm = build_llm(args)
+    if world > 1 and rank != 0:
+        llm.engine.follow()
+        llm.shutdown()
+        return
+    alm = AsyncLLM(llm.engine)
+    name = args.served_model_name or args.model
+    app = build_app(alm, name, llm.engine.config.scheduler.max_model_len)
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+    finally:
+        alm.shutdown()
+        llm.shutdown()
+
+
+def main(argv=None):
+    logging.basicConfig(level=logging.INFO)
+    run_server(make_arg_parser().parse_args(argv))
+
+
+if __name__ == "__main__":
+    main()

@@ -47,6 +47,7 @@ def plan_for(M: int, N: int, K: int, bn: int = 0, splits: int = 0) -> tuple:
 
 def _run(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, mode: int, bn: int = 0,
          splits: int = 0) -> torch.Tensor:
+    _ext.require()  # registers torch.ops.b200
     M, N, K = x.shape[0], w.shape[0], x.shape[1]
     bn, splits, need = plan_for(M, N, K, bn, splits)
     ws = _workspace(x.device, need) if need > 0 else None
