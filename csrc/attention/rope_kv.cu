@@ -4,6 +4,7 @@
 //   q heads: [RMSNorm] -> RoPE -> written back in place (attention reads q from the buffer)
 //   k heads: [RMSNorm] -> RoPE -> written to k_cache at slot_mapping[t]
 //   v heads: copied to v_cache at slot_mapping[t]
+// With no cache (k_cache == nullptr) it only rotates: q and k are written back in place.
 // Cache layout is [num_blocks, Hkv, block_size, D] so that one page of one KV head is a
 // contiguous block_size*D run (a single bulk copy for the attention kernels).  RoPE supports
 // NeoX (rotate halves) and GPT-J (rotate pairs) styles and partial rotary (rot_dim < D); the
@@ -84,11 +85,12 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
   }
 
-  if (is_q) {
+  if (is_q || (is_k && k_cache == nullptr)) {  // rotate-only mode keeps k in place too
 #pragma unroll
     for (int j = 0; j < E; ++j) src[j] = f2bf(v[j]);
     return;
   }
+  if (k_cache == nullptr) return;
   if (slot < 0) return;  // padding token: nothing to cache
   const int kvh = is_k ? h - Hq : h - Hq - Hkv;
   const int64_t blk = slot / block_size, off = slot % block_size;

@@ -209,25 +209,33 @@ void group_quant_fp8(Tensor& out, Tensor& scales, const Tensor& x) {
 // ------------------------------------------------------------------------------------- rope+kv
 void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
              const c10::optional<Tensor>& q_norm_w, const c10::optional<Tensor>& k_norm_w,
-             Tensor& k_cache, Tensor& v_cache, const Tensor& slot_mapping, int64_t Hq, int64_t Hkv,
-             int64_t rot_dim, bool neox, double eps) {
+             const c10::optional<Tensor>& k_cache_opt, const c10::optional<Tensor>& v_cache_opt,
+             const Tensor& slot_mapping, int64_t Hq, int64_t Hkv, int64_t rot_dim, bool neox,
+             double eps, int64_t head_dim) {
   CHECK_CUDA(qkv);
   CHECK_BF16(qkv);
   CHECK_ROWMAJOR(qkv);
-  CHECK_BF16(k_cache);
-  CHECK_BF16(v_cache);
+  const bool cached = k_cache_opt.has_value();
+  TORCH_CHECK(cached == v_cache_opt.has_value(), "rope_kv: pass both caches or neither");
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.is_contiguous(), "positions int32");
   TORCH_CHECK(slot_mapping.scalar_type() == at::kInt && slot_mapping.is_contiguous(),
               "slot_mapping int32");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() &&
                   cos_sin.size(1) == rot_dim,
               "cos_sin must be fp32 [max_pos, rot_dim]");
-  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
-              "kv cache must be contiguous [blocks, Hkv, block_size, D]");
+  if (cached) {
+    const Tensor& k_cache = *k_cache_opt;
+    const Tensor& v_cache = *v_cache_opt;
+    CHECK_BF16(k_cache);
+    CHECK_BF16(v_cache);
+    TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
+                "kv cache must be contiguous [blocks, Hkv, block_size, D]");
+    TORCH_CHECK(k_cache.size(1) == Hkv, "rope_kv: cache heads");
+  }
   const int T = qkv.size(0);
-  const int D = k_cache.size(3);
+  const int D = cached ? k_cache_opt->size(3) : (int)head_dim;
+  TORCH_CHECK(D > 0, "rope_kv: head_dim required without a cache");
   TORCH_CHECK(qkv.size(1) >= (Hq + 2 * Hkv) * D, "rope_kv: qkv width");
-  TORCH_CHECK(k_cache.size(1) == Hkv, "rope_kv: cache heads");
   const c10::cuda::CUDAGuard g(qkv.device());
   b200::rope::RopeKvArgs a{};
   a.qkv = qkv.data_ptr();
@@ -236,14 +244,14 @@ void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
   a.cos_sin = cos_sin.data_ptr<float>();
   a.q_norm_w = q_norm_w.has_value() ? q_norm_w->data_ptr() : nullptr;
   a.k_norm_w = k_norm_w.has_value() ? k_norm_w->data_ptr() : nullptr;
-  a.k_cache = k_cache.data_ptr();
-  a.v_cache = v_cache.data_ptr();
+  a.k_cache = cached ? k_cache_opt->data_ptr() : nullptr;
+  a.v_cache = cached ? v_cache_opt->data_ptr() : nullptr;
   a.slot_mapping = slot_mapping.data_ptr<int32_t>();
   a.T = T;
   a.Hq = Hq;
   a.Hkv = Hkv;
   a.D = D;
-  a.block_size = k_cache.size(2);
+  a.block_size = cached ? k_cache_opt->size(2) : 1;
   a.rot_dim = rot_dim;
   a.neox = neox;
   a.eps = eps;
@@ -470,8 +478,8 @@ TORCH_LIBRARY(b200, m) {
   m.def("group_quant_fp8(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
   m.def(
       "rope_kv(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor? q_norm_w, Tensor? "
-      "k_norm_w, Tensor(b!) k_cache, Tensor(c!) v_cache, Tensor slot_mapping, int num_q_heads, "
-      "int num_kv_heads, int rot_dim, bool neox=True, float eps=1e-6) -> ()");
+      "k_norm_w, Tensor(b!)? k_cache, Tensor(c!)? v_cache, Tensor slot_mapping, int num_q_heads, "
+      "int num_kv_heads, int rot_dim, bool neox=True, float eps=1e-6, int head_dim=0) -> ()");
   m.def(
       "paged_decode(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor "
       "block_tables, Tensor seq_lens, int num_q_heads, int num_kv_heads, int max_seq_len, float "

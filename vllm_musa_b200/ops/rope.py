@@ -54,23 +54,27 @@ def _rotate_ref(x: torch.Tensor, cs: torch.Tensor, rot_dim: int, neox: bool) -> 
 
 
 def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
-            k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor,
-            num_q_heads: int, num_kv_heads: int, rot_dim: int, neox: bool = True,
-            q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
-            eps: float = 1e-6) -> None:
+            k_cache: torch.Tensor | None, v_cache: torch.Tensor | None,
+            slot_mapping: torch.Tensor, num_q_heads: int, num_kv_heads: int, rot_dim: int,
+            neox: bool = True, q_norm_w: torch.Tensor | None = None,
+            k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+            write_k: bool = False, head_dim: int | None = None) -> None:
     """In place on ``qkv`` [T, (Hq+2Hkv)*D]: q <- rope(norm(q)); cache[slot] <- rope(norm(k)), v.
 
     Caches are [num_blocks, Hkv, block_size, D]; slot = block * block_size + offset; slot < 0
-    skips the write.
+    skips the write.  Without caches (``write_k``) q and k are only rotated in place.
     """
     T = qkv.shape[0]
     if T == 0:
         return
+    if head_dim is None:
+        head_dim = k_cache.shape[-1] if k_cache is not None else qkv.shape[1] // (
+            num_q_heads + 2 * num_kv_heads)
     if qkv.is_cuda:
         _ext.ops().rope_kv(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache,
-                           slot_mapping, num_q_heads, num_kv_heads, rot_dim, neox, eps)
+                           slot_mapping, num_q_heads, num_kv_heads, rot_dim, neox, eps, head_dim)
         return
-    D = k_cache.shape[-1]
+    D = head_dim
     Hq, Hkv = num_q_heads, num_kv_heads
     q = qkv[:, :Hq * D].view(T, Hq, D).float()
     k = qkv[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D).float()
@@ -84,6 +88,9 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
         q = _rotate_ref(q, cs, rot_dim, neox)
         k = _rotate_ref(k, cs, rot_dim, neox)
     qkv[:, :Hq * D] = q.reshape(T, Hq * D).to(qkv.dtype)
+    if k_cache is None:
+        qkv[:, Hq * D:(Hq + Hkv) * D] = k.reshape(T, Hkv * D).to(qkv.dtype)
+        return
     bs = k_cache.shape[2]
     sl = slot_mapping.long()
     ok = sl >= 0
