@@ -77,27 +77,32 @@ def main():
             out = torch.empty(M, N // 2 if mode == 1 else N, device="cuda",
                               dtype=torch.float32 if mode == 2 else torch.bfloat16)
             auto = mod.gemm_plan(M, N, K)
-            t_auto = timed(lambda w: ops.gemm._run(x, w, out, mode, auto[0], auto[1]), ws, a.reps)
-            best = (t_auto, auto[0], auto[1])
+            t_auto = timed(lambda w: ops.gemm._run(x, w, out, mode, auto[0], auto[1], auto[3]),
+                           ws, a.reps)
+            best = (t_auto, auto[0], auto[1], auto[3])
             kb = (K + 63) // 64
-            for bn in (64, 128, 256):
-                for s in (1, 2, 3, 4, 6, 8, 12, 16):
-                    if s > 1 and kb // s < 4:
+            for mt in ((1, 2) if M > 128 else (1,)):
+                for bn in (256, 224, 208, 192, 176, 160, 144, 128, 112, 96, 64, 48, 32):
+                    if M >= 1024 and (bn % 64 or mt * bn * 2 > 512):
                         continue
-                    if s * M * N > (64 << 20):
-                        continue
-                    t = timed(lambda w: ops.gemm._run(x, w, out, mode, bn, s), ws, a.reps)
-                    if t < best[0]:
-                        best = (t, bn, s)
+                    for s in ((1,) if M >= 1024 else (1, 2, 3, 4, 6, 8)):
+                        if s > 1 and kb // s < 4:
+                            continue
+                        if s * M * N > (64 << 20):
+                            continue
+                        t = timed(lambda w: ops.gemm._run(x, w, out, mode, bn, s, mt), ws, a.reps)
+                        if t < best[0]:
+                            best = (t, bn, s, mt)
             t_cublas = timed(lambda w: torch.matmul(x, w.t()), ws, a.reps)
             tb = (N * K * 2 + M * K * 2 + M * N * 2) / (best[0] * 1e-6) / 1e12
             tf = 2 * M * N * K / (best[0] * 1e-6) / 1e12
-            report.append(dict(layer=lname, M=M, N=N, K=K, auto=list(auto[:2]), t_auto_us=round(t_auto, 1),
-                               best_bn=best[1], best_splits=best[2], t_best_us=round(best[0], 1),
+            report.append(dict(layer=lname, M=M, N=N, K=K, auto=[auto[0], auto[1], auto[3]],
+                               t_auto_us=round(t_auto, 1), best_bn=best[1], best_splits=best[2],
+                               best_mt=best[3], t_best_us=round(best[0], 1),
                                cublas_us=round(t_cublas, 1), TBps=round(tb, 2), TFLOPs=round(tf, 1)))
             print(json.dumps(report[-1]), flush=True)
             entries.append({"n": N, "k": K, "m": M, "bn": best[1], "splits": best[2],
-                            "us": round(best[0], 2)})
+                            "mt": best[3], "us": round(best[0], 2)})
     table = {"device": torch.cuda.get_device_name(), "model": a.model, "tp": a.tp,
              "entries": entries}
     if a.write:

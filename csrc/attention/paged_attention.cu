@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes);
   uint64_t* empty = full + STAGES;
 
+  pdl_launch_dependents();
   const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.Hq / p.Hkv;
@@ -373,6 +374,7 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* empty = full + STAGES;
   uint64_t* qbar = empty + STAGES;
 
+  pdl_launch_dependents();
   const int tile = p.max_tiles - 1 - blockIdx.x;  // longest-context tiles first
   const int head = blockIdx.y;
   const int total_tiles = p.tile_offsets[p.R];

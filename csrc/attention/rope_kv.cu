@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(kWarps * 32)
                    int* err) {
   constexpr int E = D / 32;  // elements per lane
   __shared__ float stage[kWarps][D];
+  pdl_launch_dependents();
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
   const int64_t gid = (int64_t)blockIdx.x * kWarps + warp;

@@ -26,17 +26,51 @@ struct GemmArgs {
   int M, N, K;
   int mode;
   int bn, splits;  // 0 = automatic
-  float* workspace;
+  int mt;          // 128-row halves per CTA (1 or 2); 0 = automatic
+  float* workspace;  // split-K partials
   int64_t workspace_numel;
+  int* counters;     // split-K per-tile arrival counters (zero-initialised, self-resetting)
+  int64_t counters_numel;
   int* err;
 };
 struct GemmPlan {
   int bn, splits;
   int64_t workspace_floats;
+  int mt;
 };
 GemmPlan plan_bf16(int M, int N, int K);
 void run_bf16(const GemmArgs& a, cudaStream_t s);
+struct GroupedGemmArgs {
+  const void* A;  // [max_rows, K] expert-sorted rows
+  int64_t lda;
+  const void* B;  // [num_experts * N, K] stacked expert weights
+  int64_t ldb;
+  void* C;        // [max_rows, N] (N/2 with SwiGLU)
+  int64_t ldc;
+  int max_rows, N, K, num_experts, mode, bn;
+  const int32_t* tile_expert;
+  const int32_t* num_tiles;
+  int* err;
+};
+void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t s);
 }  // namespace gemm
+
+// ------------------------------------------------------------------------------- MoE
+namespace moe {
+void run_topk_softmax(const float* logits, int T, int E, int k, bool renorm, int32_t* ids,
+                      float* w, cudaStream_t s);
+void run_grouped_topk(const float* logits, const float* bias, int T, int E, int k, int n_group,
+                      int topk_group, bool sigmoid, bool renorm, float scale, int32_t* ids,
+                      float* w, cudaStream_t s);
+int align_max_rows(int n, int E);
+void run_moe_align(const int32_t* ids, int n, int E, int max_rows, int32_t* sorted_ids,
+                   int32_t* tile_expert, int32_t* offsets, int32_t* pos, int32_t* num_tiles,
+                   cudaStream_t s);
+void run_moe_gather(const void* x, int64_t ldx, const int32_t* sorted_ids, const int32_t* num_tiles,
+                    int max_rows, int k, int H, void* out, cudaStream_t s);
+void run_moe_combine(const void* y, const int32_t* pos, const float* w, int T, int k, int H,
+                     const void* shared, void* out, int64_t ldo, cudaStream_t s);
+}  // namespace moe
 
 // ------------------------------------------------------------------------------- norms
 namespace norm {

@@ -146,7 +146,7 @@ B200_DEVICE void reduce_row(const ArParams& a, int row, float (&o)[VPT][8], floa
 }
 
 template <int VPT, bool kNorm, bool kTwoShot>
-__global__ void __launch_bounds__(1024) fused_ar_kernel(ArParams a) {
+__global__ void __launch_bounds__(512) fused_ar_kernel(ArParams a) {
   __shared__ float red[32];
   __shared__ uint32_t epoch_s;
   if (threadIdx.x == 0) {
@@ -202,7 +202,7 @@ void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
   if (a.T == 0) return;
   const int nvec = a.H / 8;
   int threads = 128;
-  while (threads < 1024 && (nvec + threads - 1) / threads > 2) threads *= 2;
+  while (threads < 512 && (nvec + threads - 1) / threads > 2) threads *= 2;
   const int vpt = (nvec + threads - 1) / threads;
   B200_REQUIRE(vpt <= 8, "custom all-reduce: hidden size too large");
   const bool norm = a.weight != nullptr;

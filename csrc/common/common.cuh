@@ -249,6 +249,13 @@ B200_DEVICE void cp_async_wait() {
 
 B200_DEVICE int elect_one_lane() { return (threadIdx.x & 31) == 0; }
 
+// Programmatic dependent launch: allow the next kernel of the stream (if it was launched with
+// programmatic serialization, e.g. the GEMMs) to begin its prologue now.  It still waits for
+// this grid to finish (griddepcontrol.wait) before reading what this grid writes.
+B200_DEVICE void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace b200
 
 #include "host_check.h"

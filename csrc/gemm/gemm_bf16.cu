@@ -6,21 +6,29 @@
 // (reference: setup.py:258 links mublasLt; vllm_musa/kernels/fp8_block_gemm.py:18 is its
 // Triton GEMM) with a hand-written tcgen05 kernel:
 //
-//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage (128B swizzle), ring of
-//               STAGES shared-memory slots guarded by full/empty mbarriers.
-//   warp 1      allocates TMEM (2 x BN fp32 columns: double-buffered accumulators), one
-//               elected lane issues tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit.
-//   warps 2..5  epilogue: tcgen05.ld accumulator rows -> fused epilogue -> global.
+//   warp 0      TMA producer: per stage an MT*128 x 64 A tile and a BN x 64 B tile (128-byte
+//               swizzle) into a ring of shared-memory slots guarded by full/empty mbarriers.
+//   warp 1      allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=BN, K=16; MT
+//               of them per k-step, one per 128-row half, all reading the same B tile) and
+//               tcgen05.commit.  Accumulators are double-buffered when 2*MT*BN <= 512 columns.
+//   warps 2..5  epilogue: tcgen05.ld accumulator rows (16 columns at a time) -> fused
+//               epilogue -> global.
 //
-// Work units (m-tile, n-tile, k-split) are scheduled persistently (grid <= #SMs) in grouped
-// order so that a wave shares B tiles through L2.  Epilogues:
+// BN is a runtime multiple of 16 (16..256) and MT is 1 or 2, so the planner can pick a tile
+// count close to a whole number of waves over the 148 SMs (decode-sized M is at the
+// compute / bandwidth ridge, where a 1.5-wave tail costs a third of the runtime).  Work units
+// (m-tile, n-tile, k-split) are scheduled persistently in grouped order so a wave shares B
+// tiles through L2.  Epilogues:
 //   kStore     C = acc (bf16)
-//   kSiluMul   B rows are interleaved in groups of 64 (32 gate rows, 32 up rows); output
-//              C[:, g*32 + c] = silu(acc[g*64 + c]) * acc[g*64 + 32 + c]  (N/2 columns)
+//   kSiluMul   B rows interleaved in groups of 16 (8 gate rows, 8 up rows); output
+//              C[:, g*8 + c] = silu(acc[g*16 + c]) * acc[g*16 + 8 + c]  (N/2 columns)
 //   kF32       C = acc (fp32, used for logits)
-//   kSplitK    partial sums to an fp32 workspace [splits, M, N]; a reduce kernel finishes.
-// Every mbarrier wait is bounded (see common.cuh); a timeout leaves an error code and the
-// kernel drains, frees TMEM and returns.
+// Split-K (any epilogue): units write fp32 partials [splits, M, N]; the CTA that completes an
+// output tile last (per-tile arrival counter) sums them and applies the epilogue, so there is
+// no separate reduce launch.  Launched with programmatic dependent launch: the producer
+// prefetches its first weight tiles into L2, then waits for the previous kernel.
+// Every mbarrier wait is bounded (common.cuh); a timeout leaves an error code and the kernel
+// drains, frees TMEM and returns.
 #include <algorithm>
 #include <vector>
 
@@ -36,26 +44,42 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle atom
 constexpr int kThreads = 192;
 constexpr int kGroupN = 8;
+constexpr int kMaxStages = 8;
+constexpr int kSmemBudget = 227 * 1024;
+constexpr int kSmemOverhead = 1024 /*align*/ + 512 /*barriers, tmem slot*/;
 
-enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2, kSplitK = 3 };
+enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2 };
 
 struct Params {
   int M, N, K;
+  int bn, stages, acc_bufs, tmem_cols;
   int num_m, num_n, num_kb, splits, kb_per_split;
   int total_units;
-  void* C;       // output (bf16 or fp32) or fp32 workspace for split-K
-  int ldc;       // elements
+  void* C;  // output (bf16 or fp32) or fp32 workspace for split-K
+  int ldc;  // elements
   int* err;
+  // grouped (MoE) mode: m-tile i uses expert tile_expert[i]'s weights (B rows expert*N ...);
+  // the live m-tile count is read from the device (*num_tiles)
+  const int32_t* tile_expert;
+  const int32_t* num_tiles;
+  // split-K: fp32 partials [splits, M, N] and one arrival counter per output tile (zero
+  // between launches: the CTA that completes a tile resets it)
+  float* ws;
+  int* counters;
 };
 
-template <int BN>
-struct Smem {
-  static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int kBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-};
+B200_DEVICE void epi_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+B200_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+B200_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+B200_DEVICE void tma_prefetch_l2_2d(const void* desc, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+B200_HOST_DEVICE int a_tile_bytes(int mt) { return mt * BM * BK * 2; }
+B200_HOST_DEVICE int b_tile_bytes(int bn) { return bn * BK * 2; }
 
 B200_DEVICE void unit_coords(int u, const Params& p, int& m, int& n, int& ks) {
   const int tiles = p.num_m * p.num_n;
@@ -72,26 +96,67 @@ B200_DEVICE void unit_coords(int u, const Params& p, int& m, int& n, int& ks) {
 
 B200_DEVICE float silu(float x) { return x / (1.f + __expf(-x)); }
 
-template <int BN, int EPI>
+// Final epilogue of 16 accumulator columns [col, col+16) of one row.
+template <int EPI>
+B200_DEVICE void store_chunk16(const Params& p, int row, int col, const float (&f)[16]) {
+  if constexpr (EPI == kSiluMul) {
+    // 8 gate columns then the matching 8 up columns -> 8 outputs at col/2
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = silu(f[j]) * f[8 + j];
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc +
+                              col / 2) = pack8(o);
+  } else if constexpr (EPI == kStore) {
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      if (col + 8 * v < p.N) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = f[8 * v + j];
+        *reinterpret_cast<uint4*>(C + 8 * v) = pack8(o);
+      }
+    }
+  } else {
+    float* C = reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col;
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      if (col + 4 * v < p.N)
+        *reinterpret_cast<float4*>(C + 4 * v) =
+            make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
+  }
+}
+
+template <int MT, int EPI, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, Params p) {
-  using S = Smem<BN>;
-  constexpr int STAGES = S::kStages;
+  // Programmatic dependent launch: let the next kernel in the stream start its prologue as
+  // soon as SMs free up; it waits (griddepcontrol.wait) before reading what we write.
+  pdl_trigger();
+  if constexpr (GROUPED) {
+    pdl_wait();  // the live tile count is produced by the preceding kernel
+    p.num_m = *p.num_tiles;
+    p.total_units = p.num_m * p.num_n;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * S::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  const int STAGES = p.stages;
+  const int A_BYTES = a_tile_bytes(MT);
+  const int B_BYTES = b_tile_bytes(p.bn);
+  const int STAGE_BYTES = A_BYTES + B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* acc_full = bars + 2 * STAGES;
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* acc_full = bars + 2 * kMaxStages;
+  uint64_t* acc_empty = bars + 2 * kMaxStages + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int BN = p.bn;
+  const int ACC_COLS = MT * BN;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -107,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, 2 * BN);
+    tc::tmem_alloc(tmem_slot, p.tmem_cols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -121,6 +186,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      if (!GROUPED && (int)blockIdx.x < p.total_units) {
+        // weights do not depend on the previous kernel: start pulling the first unit's B
+        // tiles into L2 while that kernel drains
+        int m, n, ks;
+        unit_coords(blockIdx.x, p, m, n, ks);
+        const int kb0 = ks * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + 2 * STAGES);
+        for (int kb = kb0; kb < kb1; ++kb) tma_prefetch_l2_2d(&tmB, kb * BK, n * BN);
+      }
+      pdl_wait();
       for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
         int m, n, ks;
         unit_coords(u, p, m, n, ks);
@@ -131,9 +206,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-          tma_load_2d(sA + stage * S::kABytes, &tmA, &full[stage], kb * BK, m * BM);
-          tma_load_2d(sB + stage * S::kBBytes, &tmB, &full[stage], kb * BK, n * BN);
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(st, &tmA, &full[stage], kb * BK, m * BM * MT);
+          const int brow = GROUPED ? p.tile_expert[m] * p.N + n * BN : n * BN;
+          tma_load_2d(st + A_BYTES, &tmB, &full[stage], kb * BK, brow);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -155,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_f16<true>(BM, BN);
+      const uint32_t idesc = tc::idesc_f16<true>(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -168,20 +245,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err)) break;
         tc::fence_after_sync();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err)) {
             ok = false;
             break;
           }
           tc::fence_after_sync();
-          const uint64_t adesc = tc::smem_desc_kmajor_sw128(smem_u32(sA + stage * S::kABytes));
-          const uint64_t bdesc = tc::smem_desc_kmajor_sw128(smem_u32(sB + stage * S::kBBytes));
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t bdesc = tc::smem_desc_kmajor_sw128(sa + A_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // +32 bytes along K inside the 128-byte swizzle atom -> +2 in the >>4 address field
-            tc::mma_f16_ss(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc,
-                           (kb > kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const uint64_t adesc = tc::smem_desc_kmajor_sw128(sa + mt * BM * 128);
+              // +32 bytes along K inside the 128-byte swizzle atom -> +2 in the >>4 field
+              tc::mma_f16_ss(d_tmem + mt * BN, adesc + 2 * k, bdesc + 2 * k, idesc,
+                             (kb > kb0 || k > 0) ? 1u : 0u);
+            }
           }
           tc::mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -191,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc::mma_commit(&acc_full[acc]);
-        if (++acc == 2) {
+        if (++acc == p.acc_bufs) {
           acc = 0;
           acc_phase ^= 1;
         }
@@ -199,8 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
+    __shared__ int s_last;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    const bool split = p.splits > 1;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
@@ -208,74 +290,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       unit_coords(u, p, m, n, ks);
       if (!mbar_wait(&acc_full[acc], acc_phase, p.err)) break;
       tc::fence_after_sync();
-      const int row = m * BM + row_in_tile;
-      const bool row_ok = row < p.M;
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if constexpr (EPI == kSiluMul) {
-        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int row = (m * MT + mt) * BM + q * 32 + lane;
+        const bool row_ok = row < p.M;
+        const uint32_t t_row =
+            tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS + mt * BN;
 #pragma unroll 1
-        for (int g = 0; g < BN / 64; ++g) {
-          uint32_t rg[32], ru[32];
-          tc::tmem_ld_32x32b_x32(t_row + g * 64, rg);
-          tc::tmem_ld_32x32b_x32(t_row + g * 64 + 32, ru);
+        for (int c = 0; c < BN; c += 32) {
+          const bool two = c + 16 < BN;
+          uint32_t r[2][16];
+          tc::tmem_ld_32x32b_x16(t_row + c, r[0]);
+          if (two) tc::tmem_ld_32x32b_x16(t_row + c + 16, r[1]);
           tc::tmem_ld_wait();
-          const int col = (n * BN + g * 64) / 2;  // output column base
-          if (row_ok && col < p.N / 2) {
-            uint4* dst = reinterpret_cast<uint4*>(C + (size_t)row * p.ldc + col);
+          if (!row_ok) continue;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              float f[8];
+          for (int h = 0; h < 2; ++h) {
+            const int col = n * BN + c + 16 * h;
+            if ((h == 1 && !two) || col >= p.N) continue;
+            if (split) {
+              float* w = p.ws + ((size_t)ks * p.M + row) * p.N + col;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float gv = __uint_as_float(rg[v * 8 + j]);
-                const float uv = __uint_as_float(ru[v * 8 + j]);
-                f[j] = silu(gv) * uv;
-              }
-              dst[v] = pack8(f);
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tc::tmem_ld_32x32b_x32(t_row + c * 32, r);
-          tc::tmem_ld_wait();
-          const int col = n * BN + c * 32;
-          if (!row_ok || col >= p.N) continue;
-          if constexpr (EPI == kStore) {
-            __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
-            uint4* dst = reinterpret_cast<uint4*>(C + (size_t)row * p.ldc + col);
-            const int nvec = min(4, (p.N - col) / 8);
+              for (int v = 0; v < 4; ++v)
+                reinterpret_cast<float4*>(w)[v] =
+                    make_float4(__uint_as_float(r[h][4 * v]), __uint_as_float(r[h][4 * v + 1]),
+                                __uint_as_float(r[h][4 * v + 2]), __uint_as_float(r[h][4 * v + 3]));
+            } else {
+              float f[16];
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              if (v < nvec) {
-                float f[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[v * 8 + j]);
-                dst[v] = pack8(f);
-              }
-            }
-          } else {
-            float* C = reinterpret_cast<float*>(p.C);
-            if constexpr (EPI == kSplitK) C += (size_t)ks * p.M * p.ldc;
-            float4* dst = reinterpret_cast<float4*>(C + (size_t)row * p.ldc + col);
-            const int nvec = min(8, (p.N - col) / 4);
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              if (v < nvec)
-                dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+              for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(r[h][j]);
+              store_chunk16<EPI>(p, row, col, f);
             }
           }
         }
       }
+      // accumulator drained: hand TMEM back to the MMA warp
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      if (++acc == 2) {
+      if (++acc == p.acc_bufs) {
         acc = 0;
         acc_phase ^= 1;
+      }
+      if (split) {
+        // the last CTA to finish this output tile sums the partials and applies the epilogue
+        __threadfence();
+        epi_barrier();
+        const int tile = m * p.num_n + n;
+        if (warp == 2 && lane == 0) s_last = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+        epi_barrier();
+        if (s_last) {
+          __threadfence();
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int row = (m * MT + mt) * BM + q * 32 + lane;
+            if (row >= p.M) continue;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+              const int col = n * BN + c;
+              if (col >= p.N) break;
+              float f[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) f[j] = 0.f;
+              for (int sp = 0; sp < p.splits; ++sp) {
+                const float4* w =
+                    reinterpret_cast<const float4*>(p.ws + ((size_t)sp * p.M + row) * p.N + col);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                  const float4 t = __ldcg(w + v);
+                  f[4 * v] += t.x;
+                  f[4 * v + 1] += t.y;
+                  f[4 * v + 2] += t.z;
+                  f[4 * v + 3] += t.w;
+                }
+              }
+              store_chunk16<EPI>(p, row, col, f);
+            }
+          }
+          epi_barrier();
+          if (warp == 2 && lane == 0) p.counters[tile] = 0;
+        }
       }
     }
   }
@@ -283,137 +377,186 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (warp == 1) tc::tmem_dealloc(tmem_base, 2 * BN);
-}
-
-// Sum split-K partials [splits, M, N] fp32 -> bf16 C (or fp32 C).
-template <bool kOutF32>
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ C, int M,
-                                     int N, int ldc, int splits) {
-  const size_t total4 = (size_t)M * N / 4;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t e = i * 4;
-    const int row = e / N, col = e % N;
-    float4 acc = reinterpret_cast<const float4*>(ws)[i];
-    for (int s = 1; s < splits; ++s) {
-      const float4 t = reinterpret_cast<const float4*>(ws + (size_t)s * M * N)[i];
-      acc.x += t.x;
-      acc.y += t.y;
-      acc.z += t.z;
-      acc.w += t.w;
-    }
-    if constexpr (kOutF32) {
-      *reinterpret_cast<float4*>(reinterpret_cast<float*>(C) + (size_t)row * ldc + col) = acc;
-    } else {
-      __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col;
-      uint2 v;
-      v.x = pack_bf16x2(acc.x, acc.y);
-      v.y = pack_bf16x2(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(c) = v;
-    }
-  }
-}
-
-template <bool kOutF32>
-__global__ void splitk_reduce_silu_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ C,
-                                          int M, int N, int ldc, int splits) {
-  // N = interleaved width; output width N/2
-  const size_t total = (size_t)M * (N / 2);
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const int row = i / (N / 2), oc = i % (N / 2);
-    const int g = oc / 32, c = oc % 32;
-    const int cg = g * 64 + c, cu = g * 64 + 32 + c;
-    float gv = 0.f, uv = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float* w = ws + (size_t)s * M * N + (size_t)row * N;
-      gv += w[cg];
-      uv += w[cu];
-    }
-    C[(size_t)row * ldc + oc] = __float2bfloat16_rn(silu(gv) * uv);
-  }
+  if (warp == 1) tc::tmem_dealloc(tmem_base, p.tmem_cols);
 }
 
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
 struct Plan {
-  int bn, splits;
+  int mt, bn, splits;
 };
 
-// Cost model: per-CTA time of one k-block is max(load time, MMA time) at the per-SM share of
-// HBM bandwidth / tensor throughput; total = waves * k-blocks-per-unit * per-kb time, plus the
-// split-K workspace round trip.
+static int stages_for(int mt, int bn) {
+  const int stage = a_tile_bytes(mt) + b_tile_bytes(bn);
+  return std::min(kMaxStages, (kSmemBudget - kSmemOverhead) / stage);
+}
+
+// Cost model.  A unit's time is the largest of (a) its MMA time, (b) filling shared memory
+// with its A and B tiles through L2 at its share of L2 bandwidth (capped per SM), and (c)
+// pulling its B tiles (the weights) from HBM at its share of DRAM bandwidth (capped per SM);
+// the slowest SM runs ceil(units / SMs) units and the GEMM cannot beat its DRAM bytes at
+// full bandwidth.  Split-K adds the fp32 workspace round trip.  Constants are B200 figures
+// (~4000 bf16 MAC/clk/SM at ~1.8 GHz under load, ~6.5 TB/s HBM, ~16 TB/s L2).
+static double plan_cost(int M, int N, int K, int mt, int bn, int s, int sms) {
+  const int num_m = (M + BM * mt - 1) / (BM * mt);
+  const int num_n = (N + bn - 1) / bn;
+  const int num_kb = (K + BK - 1) / BK;
+  const int kps = (num_kb + s - 1) / s;
+  const long units = (long)num_m * num_n * s;
+  const long per_sm = (units + sms - 1) / sms;
+  const long active = std::min<long>(units, sms);
+  const double clk = 1.8e9, mac_per_clk = 4000.0;
+  const double mma_t = (double)kps * mt * BM * bn * BK / mac_per_clk / clk;
+  const double fill_bytes = (double)(mt * BM + bn) * kps * BK * 2;
+  const double fill_t = fill_bytes / std::min(1.6e13 / active, 1.2e11);
+  const double dram_bytes = (double)bn * kps * BK * 2;
+  const double dram_t = dram_bytes / std::min(6.5e12 / active, 9.0e10);
+  const double total_bytes = (double)N * K * 2 + (double)M * K * 2 + (double)M * N * 2;
+  double t = std::max(per_sm * std::max(mma_t, std::max(fill_t, dram_t)), total_bytes / 6.5e12);
+  t += per_sm * 0.6e-6 + 2.0e-6;  // per-unit epilogue / pipeline fill, launch
+  if (s > 1) t += (double)M * N * 4 * (s + 1) / 6.0e12 + 3e-6;
+  return t;
+}
+
 static Plan choose_plan(int M, int N, int K) {
   const int sms = num_sms();
-  const int num_m = (M + BM - 1) / BM;
-  const int num_kb = (K + BK - 1) / BK;
-  Plan best{256, 1};
+  Plan best{1, 256, 1};
   double best_cost = 1e30;
-  const int bns[3] = {256, 128, 64};
-  for (int bi = 0; bi < 3; ++bi) {
-    const int bn = bns[bi];
-    const int num_n = (N + bn - 1) / bn;
-    const int tiles = num_m * num_n;
-    for (int s = 1; s <= 16; ++s) {
-      if (s > 1 && (num_kb + s - 1) / s < 4) break;
-      const int kps = (num_kb + s - 1) / s;
-      const long units = (long)tiles * s;
-      const long waves = (units + sms - 1) / sms;
-      const long active = std::min<long>(units, sms);
-      const double bytes = (double)(BM + bn) * BK * 2;
-      const double per_sm_bw = 6.5e12 / active * 0.9;
-      const double mma_t = (double)BM * bn * BK * 2 / (1.4e15 / sms);
-      const double reuse = active > 1 ? 0.5 : 1.0;  // neighbours share tiles through L2
-      const double load_t = bytes * reuse / per_sm_bw;
-      double cost = waves * kps * std::max(load_t, mma_t) + waves * 1.5e-6;
-      if (s > 1) cost += (double)M * N * 4 * (s + 1) / 6.0e12 + 3e-6;
-      if (cost < best_cost * 0.97) {
-        best_cost = cost;
-        best = {bn, s};
+  const int num_kb = (K + BK - 1) / BK;
+  for (int mt = 1; mt <= 2; ++mt) {
+    if (mt == 2 && (M <= BM || M > 1024)) continue;  // MT=2 measured slower at large M
+    for (int bn = 256; bn >= 16; bn -= 16) {
+      if (2 * mt * bn > 512 && M > 1024) continue;  // large M wants double-buffered TMEM
+      for (int s = 1; s <= 16; ++s) {
+        if (s > 1 && (num_kb + s - 1) / s < 4) break;
+        if (s > 1 && (long)s * M * N > (64l << 20)) break;
+        const double c = plan_cost(M, N, K, mt, bn, s, sms);
+        if (c < best_cost * 0.995) {
+          best_cost = c;
+          best = {mt, bn, s};
+        }
       }
     }
   }
   return best;
 }
 
-template <int BN, int EPI>
+// Launch with programmatic stream serialization (the kernel calls griddepcontrol.wait before
+// touching anything the previous kernel wrote).
+template <typename K>
+static void launch_pdl(K kern, int grid, int smem, cudaStream_t stream, const CUtensorMap& ta,
+                       const CUtensorMap& tb, const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200_CUDA_OK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+}
+
+template <int MT, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                    cudaStream_t stream) {
-  auto kern = gemm_bf16_kernel<BN, EPI>;
-  const int smem = Smem<BN>::kBytes;
+  auto kern = gemm_bf16_kernel<MT, EPI>;
   static uint32_t attr_set = 0;  // bit per device
   int dev;
   B200_CUDA_OK(cudaGetDevice(&dev));
   if (!(attr_set & (1u << dev))) {
-    B200_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    B200_CUDA_OK(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget));
     attr_set |= 1u << dev;
   }
+  const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) + kSmemOverhead;
   const int grid = std::min(p.total_units, num_sms());
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
-  B200_CUDA_OK(cudaGetLastError());
+  launch_pdl(kern, grid, smem, stream, ta, tb, p);
   count_launch();
 }
 
 template <int EPI>
-static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+static void dispatch_mt(int mt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                         cudaStream_t s) {
-  if (bn == 256)
-    launch<256, EPI>(ta, tb, p, s);
-  else if (bn == 128)
-    launch<128, EPI>(ta, tb, p, s);
+  if (mt == 2)
+    launch<2, EPI>(ta, tb, p, s);
   else
-    launch<64, EPI>(ta, tb, p, s);
+    launch<1, EPI>(ta, tb, p, s);
+}
+
+// Grouped (MoE) GEMM: A = expert-sorted rows [max_rows, K] (segments padded to 128 rows),
+// B = stacked expert weights [E * N, K]; C = [max_rows, N] (or N/2 with SwiGLU).
+void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
+  const int N = a.N, K = a.K;
+  B200_REQUIRE(K % 8 == 0 && N % 16 == 0, "grouped gemm: K % 8 == 0 and N % 16 == 0");
+  B200_REQUIRE(a.max_rows % BM == 0, "grouped gemm: max_rows must be a multiple of 128");
+  if (a.max_rows == 0) return;
+  int bn = a.bn > 0 ? a.bn : 0;
+  if (bn == 0) {
+    // fill the SMs with (tiles x n-tiles) units assuming ~E live tiles
+    const int tiles = std::max(1, std::min(a.max_rows / BM, a.num_experts));
+    bn = 256;
+    while (bn > 64 && (long)tiles * ((N + bn - 1) / bn) < num_sms()) bn -= 64;
+  }
+  Params p;
+  p.M = a.max_rows;
+  p.N = N;
+  p.K = K;
+  p.bn = bn;
+  p.stages = stages_for(1, bn);
+  p.acc_bufs = 2 * bn <= 512 ? 2 : 1;
+  int cols = 32;
+  while (cols < p.acc_bufs * bn) cols <<= 1;
+  p.tmem_cols = cols;
+  p.num_m = a.max_rows / BM;  // upper bound; the kernel reads the live count
+  p.num_n = (N + bn - 1) / bn;
+  p.num_kb = (K + BK - 1) / BK;
+  p.splits = 1;
+  p.kb_per_split = p.num_kb;
+  p.total_units = p.num_m * p.num_n;
+  p.err = a.err;
+  p.ldc = (int)a.ldc;
+  p.C = a.C;
+  p.tile_expert = a.tile_expert;
+  p.num_tiles = a.num_tiles;
+  p.ws = nullptr;
+  p.counters = nullptr;
+  const CUtensorMap ta = make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                     K, a.max_rows, a.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tb =
+      make_tma_2d(const_cast<void*>(a.B), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K,
+                  (uint64_t)a.num_experts * N, a.ldb, BK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  auto go = [&](auto kern) {
+    static uint32_t attr = 0;
+    int dev;
+    B200_CUDA_OK(cudaGetDevice(&dev));
+    if (!(attr & (1u << dev))) {
+      B200_CUDA_OK(
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget));
+      attr |= 1u << dev;
+    }
+    const int smem = p.stages * (a_tile_bytes(1) + b_tile_bytes(bn)) + kSmemOverhead;
+    const int grid = std::min(p.total_units, num_sms());
+    launch_pdl(kern, grid, smem, stream, ta, tb, p);
+  };
+  if (a.mode == kModeSiluMul)
+    go(gemm_bf16_kernel<1, kSiluMul, true>);
+  else
+    go(gemm_bf16_kernel<1, kStore, true>);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
 }
 
 GemmPlan plan_bf16(int M, int N, int K) {
-  Plan p = choose_plan(M, N, K);
+  const Plan p = choose_plan(M, N, K);
   const int num_kb = (K + BK - 1) / BK;
   int s = std::max(1, std::min<int>(p.splits, num_kb));
   const int kps = (num_kb + s - 1) / s;
   s = (num_kb + kps - 1) / kps;
-  return GemmPlan{p.bn, s, s > 1 ? (int64_t)s * M * N : 0};
+  return GemmPlan{p.bn, s, s > 1 ? (int64_t)s * M * N : 0, p.mt};
 }
 
 void run_bf16(const GemmArgs& a, cudaStream_t stream) {
@@ -426,16 +569,26 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
                "gemm_bf16: operands must be 16-byte aligned");
   if (M == 0) return;
   const bool silu = a.mode == kModeSiluMul;
-  B200_REQUIRE(!silu || N % 64 == 0, "gemm_bf16 silu: N must be a multiple of 64");
-  GemmPlan plan = plan_bf16(M, N, K);
+  B200_REQUIRE(!silu || N % 16 == 0, "gemm_bf16 silu: N must be a multiple of 16");
+  Plan plan = choose_plan(M, N, K);
   if (a.bn > 0) plan.bn = a.bn;
   if (a.splits > 0) plan.splits = a.splits;
-  B200_REQUIRE(plan.bn == 64 || plan.bn == 128 || plan.bn == 256, "gemm_bf16: bn");
+  if (a.mt > 0) plan.mt = a.mt;
+  B200_REQUIRE(plan.bn >= 16 && plan.bn <= 256 && plan.bn % 16 == 0,
+               "gemm_bf16: bn must be a multiple of 16 in [16, 256]");
+  B200_REQUIRE(plan.mt == 1 || plan.mt == 2, "gemm_bf16: mt must be 1 or 2");
   Params p;
   p.M = M;
   p.N = N;
   p.K = K;
-  p.num_m = (M + BM - 1) / BM;
+  p.bn = plan.bn;
+  p.stages = stages_for(plan.mt, plan.bn);
+  const int acc_cols = plan.mt * plan.bn;
+  p.acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
+  int cols = 32;
+  while (cols < p.acc_bufs * acc_cols) cols <<= 1;
+  p.tmem_cols = cols;
+  p.num_m = (M + BM * plan.mt - 1) / (BM * plan.mt);
   p.num_n = (N + plan.bn - 1) / plan.bn;
   p.num_kb = (K + BK - 1) / BK;
   p.splits = std::max(1, std::min<int>(plan.splits, p.num_kb));
@@ -445,45 +598,32 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.err = a.err;
   p.ldc = (int)a.ldc;
 
-  const CUtensorMap ta = make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                                     K, M, a.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap ta =
+      make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, a.lda, BK,
+                  BM * plan.mt, CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tb = make_tma_2d(const_cast<void*>(a.B), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                                      K, N, a.ldb, BK, plan.bn, CU_TENSOR_MAP_SWIZZLE_128B);
 
-  if (p.splits == 1) {
-    p.C = a.C;
-    if (a.mode == kModeStore)
-      dispatch_bn<kStore>(plan.bn, ta, tb, p, stream);
-    else if (a.mode == kModeSiluMul)
-      dispatch_bn<kSiluMul>(plan.bn, ta, tb, p, stream);
-    else
-      dispatch_bn<kF32>(plan.bn, ta, tb, p, stream);
-    return;
+  p.C = a.C;
+  p.tile_expert = nullptr;
+  p.num_tiles = nullptr;
+  p.ws = nullptr;
+  p.counters = nullptr;
+  if (p.splits > 1) {
+    const int64_t need = (int64_t)p.splits * M * N;
+    B200_REQUIRE(a.workspace != nullptr && a.workspace_numel >= need,
+                 "gemm_bf16: split-K workspace too small");
+    B200_REQUIRE(a.counters != nullptr && a.counters_numel >= (int64_t)p.num_m * p.num_n,
+                 "gemm_bf16: split-K tile counters too small");
+    p.ws = a.workspace;
+    p.counters = a.counters;
   }
-  const int64_t need = (int64_t)p.splits * M * N;
-  B200_REQUIRE(a.workspace != nullptr && a.workspace_numel >= need,
-               "gemm_bf16: split-K workspace too small");
-  p.C = a.workspace;
-  p.ldc = N;
-  dispatch_bn<kSplitK>(plan.bn, ta, tb, p, stream);
-  const int threads = 256;
-  if (silu) {
-    const size_t total = (size_t)M * (N / 2);
-    const int blocks = (int)std::min<size_t>((total + threads - 1) / threads, 148 * 16);
-    splitk_reduce_silu_kernel<false><<<blocks, threads, 0, stream>>>(
-        a.workspace, reinterpret_cast<__nv_bfloat16*>(a.C), M, N, (int)a.ldc, p.splits);
-  } else {
-    const size_t total4 = (size_t)M * N / 4;
-    const int blocks = (int)std::min<size_t>((total4 + threads - 1) / threads, 148 * 16);
-    if (a.mode == kModeF32)
-      splitk_reduce_kernel<true><<<blocks, threads, 0, stream>>>(a.workspace, a.C, M, N,
-                                                                 (int)a.ldc, p.splits);
-    else
-      splitk_reduce_kernel<false><<<blocks, threads, 0, stream>>>(a.workspace, a.C, M, N,
-                                                                  (int)a.ldc, p.splits);
-  }
-  B200_CUDA_OK(cudaGetLastError());
-  count_launch();
+  if (a.mode == kModeStore)
+    dispatch_mt<kStore>(plan.mt, ta, tb, p, stream);
+  else if (a.mode == kModeSiluMul)
+    dispatch_mt<kSiluMul>(plan.mt, ta, tb, p, stream);
+  else
+    dispatch_mt<kF32>(plan.mt, ta, tb, p, stream);
 }
 
 }  // namespace gemm

@@ -12,6 +12,7 @@ namespace misc {
 __global__ void embedding_kernel(uint4* __restrict__ out, const uint4* __restrict__ table,
                                  const int32_t* __restrict__ ids, int H8, int64_t vocab,
                                  int64_t vocab_start) {
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   const int64_t id = (int64_t)ids[t] - vocab_start;
   const bool ok = id >= 0 && id < vocab;

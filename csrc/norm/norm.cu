@@ -19,6 +19,7 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ out, int64_t ld_out,
                                __nv_bfloat16* __restrict__ residual, int64_t ld_res,
                                const __nv_bfloat16* __restrict__ w, int H, float eps) {
   __shared__ float red[32];
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int nvec = H / 8;
   uint4* xr = reinterpret_cast<uint4*>(x + row * ld_x);

@@ -50,7 +50,8 @@ void guarded(F&& f) {
 
 // ------------------------------------------------------------------------------------- GEMM
 void gemm_bf16(const Tensor& A, const Tensor& B, Tensor& C, int64_t mode, int64_t bn,
-               int64_t splits, const c10::optional<Tensor>& workspace) {
+               int64_t splits, const c10::optional<Tensor>& workspace, int64_t mt,
+               const c10::optional<Tensor>& counters) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CUDA(C);
@@ -77,10 +78,16 @@ void gemm_bf16(const Tensor& A, const Tensor& B, Tensor& C, int64_t mode, int64_
   a.mode = mode;
   a.bn = bn;
   a.splits = splits;
+  a.mt = mt;
   if (workspace.has_value()) {
     TORCH_CHECK(workspace->scalar_type() == at::kFloat && workspace->is_cuda(), "workspace");
     a.workspace = workspace->data_ptr<float>();
     a.workspace_numel = workspace->numel();
+  }
+  if (counters.has_value()) {
+    TORCH_CHECK(counters->scalar_type() == at::kInt && counters->is_cuda(), "counters");
+    a.counters = counters->data_ptr<int>();
+    a.counters_numel = counters->numel();
   }
   a.err = err_ptr(A);
   guarded([&] { b200::gemm::run_bf16(a, stream_of(A)); });
@@ -88,7 +95,7 @@ void gemm_bf16(const Tensor& A, const Tensor& B, Tensor& C, int64_t mode, int64_
 
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
   const auto p = b200::gemm::plan_bf16(M, N, K);
-  return {p.bn, p.splits, p.workspace_floats};
+  return {p.bn, p.splits, p.workspace_floats, p.mt};
 }
 
 // ------------------------------------------------------------------------------------- norms
@@ -423,6 +430,106 @@ void gather_rows(Tensor& out, const Tensor& x, const Tensor& idx) {
 
 Tensor error_word(const Tensor& like) { return error_word_for(like.device()); }
 
+// ------------------------------------------------------------------------------------- MoE
+void gemm_grouped_bf16(const Tensor& A, const Tensor& B, Tensor& C, const Tensor& tile_expert,
+                       const Tensor& num_tiles, int64_t num_experts, int64_t mode, int64_t bn) {
+  CHECK_CUDA(A);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  CHECK_ROWMAJOR(C);
+  TORCH_CHECK(B.size(0) % num_experts == 0, "grouped gemm: B rows must be E * N");
+  const int N = B.size(0) / num_experts;
+  TORCH_CHECK(A.size(1) == B.size(1), "grouped gemm: K mismatch");
+  TORCH_CHECK(C.size(0) == A.size(0) && C.size(1) == (mode == 1 ? N / 2 : N), "grouped gemm: C");
+  TORCH_CHECK(tile_expert.scalar_type() == at::kInt && num_tiles.scalar_type() == at::kInt,
+              "grouped gemm: int32 tile metadata");
+  const c10::cuda::CUDAGuard g(A.device());
+  b200::gemm::GroupedGemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.max_rows = A.size(0);
+  a.N = N;
+  a.K = A.size(1);
+  a.num_experts = num_experts;
+  a.mode = mode;
+  a.bn = bn;
+  a.tile_expert = tile_expert.data_ptr<int32_t>();
+  a.num_tiles = num_tiles.data_ptr<int32_t>();
+  a.err = err_ptr(A);
+  guarded([&] { b200::gemm::run_grouped_bf16(a, stream_of(A)); });
+}
+
+void topk_softmax(const Tensor& logits, Tensor& ids, Tensor& w, bool renorm) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "router logits fp32");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && w.scalar_type() == at::kFloat, "ids/w dtypes");
+  const c10::cuda::CUDAGuard g(logits.device());
+  guarded([&] {
+    b200::moe::run_topk_softmax(logits.data_ptr<float>(), logits.size(0), logits.size(1),
+                                ids.size(1), renorm, ids.data_ptr<int32_t>(), w.data_ptr<float>(),
+                                stream_of(logits));
+  });
+}
+
+void grouped_topk(const Tensor& logits, const c10::optional<Tensor>& bias, Tensor& ids, Tensor& w,
+                  int64_t n_group, int64_t topk_group, bool sigmoid, bool renorm, double scale) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "router logits fp32");
+  const c10::cuda::CUDAGuard g(logits.device());
+  guarded([&] {
+    b200::moe::run_grouped_topk(logits.data_ptr<float>(),
+                                bias.has_value() ? bias->data_ptr<float>() : nullptr,
+                                logits.size(0), logits.size(1), ids.size(1), n_group, topk_group,
+                                sigmoid, renorm, scale, ids.data_ptr<int32_t>(),
+                                w.data_ptr<float>(), stream_of(logits));
+  });
+}
+
+void moe_align(const Tensor& ids, int64_t E, Tensor& sorted_ids, Tensor& tile_expert,
+               Tensor& offsets, Tensor& pos, Tensor& num_tiles) {
+  CHECK_CUDA(ids);
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "moe_align: int32 ids");
+  const c10::cuda::CUDAGuard g(ids.device());
+  guarded([&] {
+    b200::moe::run_moe_align(ids.data_ptr<int32_t>(), ids.numel(), E, sorted_ids.numel(),
+                             sorted_ids.data_ptr<int32_t>(), tile_expert.data_ptr<int32_t>(),
+                             offsets.data_ptr<int32_t>(), pos.data_ptr<int32_t>(),
+                             num_tiles.data_ptr<int32_t>(), stream_of(ids));
+  });
+}
+
+void moe_gather(const Tensor& x, const Tensor& sorted_ids, const Tensor& num_tiles, int64_t k,
+                Tensor& out) {
+  CHECK_CUDA(x);
+  CHECK_ROWMAJOR(x);
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::moe::run_moe_gather(x.data_ptr(), x.stride(0), sorted_ids.data_ptr<int32_t>(),
+                              num_tiles.data_ptr<int32_t>(), out.size(0), k, x.size(1),
+                              out.data_ptr(), stream_of(x));
+  });
+}
+
+void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w,
+                 const c10::optional<Tensor>& shared, Tensor& out) {
+  CHECK_CUDA(y);
+  TORCH_CHECK(y.is_contiguous() && pos.is_contiguous() && w.is_contiguous(), "moe_combine");
+  CHECK_ROWMAJOR(out);
+  const c10::cuda::CUDAGuard g(y.device());
+  guarded([&] {
+    b200::moe::run_moe_combine(y.data_ptr(), pos.data_ptr<int32_t>(), w.data_ptr<float>(),
+                               pos.size(0), pos.size(1), y.size(1),
+                               shared.has_value() ? shared->data_ptr() : nullptr, out.data_ptr(),
+                               out.stride(0), stream_of(y));
+  });
+}
+
 // ------------------------------------------------------------------------------------- comm
 // Fused all-reduce: `bufs` holds per-rank device addresses as int64:
 //   [0:W) staging slot, [W:2W) output slot, [2W:3W) flag region (this call's parity).
@@ -466,7 +573,7 @@ void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64
 TORCH_LIBRARY(b200, m) {
   m.def(
       "gemm_bf16(Tensor A, Tensor B, Tensor(a!) C, int mode=0, int bn=0, int splits=0, "
-      "Tensor? workspace=None) -> ()");
+      "Tensor? workspace=None, int mt=0, Tensor(b!)? counters=None) -> ()");
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps, bool gemma=False) -> ()");
   m.def(
       "fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor weight, float eps, "
@@ -495,6 +602,18 @@ TORCH_LIBRARY(b200, m) {
   m.def("merge_candidates(Tensor vals, Tensor idx, Tensor(a!) out) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor table, Tensor ids, int vocab_start=0) -> ()");
   m.def("gather_rows(Tensor(a!) out, Tensor x, Tensor idx) -> ()");
+  m.def(
+      "gemm_grouped_bf16(Tensor A, Tensor B, Tensor(a!) C, Tensor tile_expert, Tensor num_tiles, "
+      "int num_experts, int mode=0, int bn=0) -> ()");
+  m.def("topk_softmax(Tensor logits, Tensor(a!) ids, Tensor(b!) w, bool renorm=True) -> ()");
+  m.def(
+      "grouped_topk(Tensor logits, Tensor? bias, Tensor(a!) ids, Tensor(b!) w, int n_group, "
+      "int topk_group, bool sigmoid, bool renorm, float scale) -> ()");
+  m.def(
+      "moe_align(Tensor ids, int num_experts, Tensor(a!) sorted_ids, Tensor(b!) tile_expert, "
+      "Tensor(c!) offsets, Tensor(d!) pos, Tensor(e!) num_tiles) -> ()");
+  m.def("moe_gather(Tensor x, Tensor sorted_ids, Tensor num_tiles, int k, Tensor(a!) out) -> ()");
+  m.def("moe_combine(Tensor y, Tensor pos, Tensor w, Tensor? shared, Tensor(a!) out) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(b200, CUDA, m) {
@@ -512,6 +631,12 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("merge_candidates", &merge_candidates);
   m.impl("embedding", &embedding);
   m.impl("gather_rows", &gather_rows);
+  m.impl("gemm_grouped_bf16", &gemm_grouped_bf16);
+  m.impl("topk_softmax", &topk_softmax);
+  m.impl("grouped_topk", &grouped_topk);
+  m.impl("moe_align", &moe_align);
+  m.impl("moe_gather", &moe_gather);
+  m.impl("moe_combine", &moe_combine);
 }
 
 void register_runtime(pybind11::module_& m);  // csrc/runtime/bindings.cpp
@@ -520,6 +645,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vllm_musa_b200 native extension (sm_100a kernels + host runtime)";
   m.def("gemm_plan", &gemm_plan, "automatic (bn, splits, workspace_floats) for a bf16 GEMM");
   m.def("decode_num_splits", &decode_num_splits, "split-KV count for a decode batch");
+  m.def("moe_max_rows", [](int64_t n, int64_t E) { return (int64_t)b200::moe::align_max_rows(n, E); },
+        "rows of the expert-sorted buffer for n assignments over E experts");
   m.def("error_word", &error_word, "per-device error word of the bounded waits");
   m.def("fused_allreduce", &fused_allreduce, "NVSwitch all-reduce (+ residual + RMSNorm)");
   m.def("ipc_malloc", [](size_t n) { return (int64_t)reinterpret_cast<uintptr_t>(b200::comm::ipc_malloc(n)); });

@@ -35,14 +35,28 @@ def test_gemm_bf16(M, N, K):
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item() / 4 + 1e-2)
 
 
-@pytest.mark.parametrize("bn,splits", [(64, 1), (128, 1), (256, 1), (128, 3), (256, 4), (64, 8)])
-def test_gemm_bf16_forced_plans(bn, splits):
-    M, N, K = 250, 768, 2048
+@pytest.mark.parametrize("bn,splits,mt", [(64, 1, 1), (128, 1, 1), (256, 1, 1), (128, 3, 1),
+                                          (256, 4, 1), (64, 8, 1), (208, 1, 1), (48, 2, 1),
+                                          (128, 1, 2), (256, 1, 2), (176, 3, 2), (16, 1, 2)])
+def test_gemm_bf16_forced_plans(bn, splits, mt):
+    M, N, K = 250, 768 + 16, 2048
     a, b = _bf(M, K, seed=3), _bf(N, K, seed=4, scale=0.05)
     ref = a.float() @ b.float().t()
     out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
-    ops.gemm._run(a, b, out, 0, bn, splits)
+    ops.gemm._run(a, b, out, 0, bn, splits, mt)
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("bn,splits,mt", [(208, 1, 1), (128, 1, 2), (96, 2, 2), (256, 1, 2)])
+def test_gemm_silu_forced_plans(bn, splits, mt):
+    M, I, K = 300, 1024, 1024
+    x = _bf(M, K, seed=17)
+    g, u = _bf(I, K, seed=18, scale=0.05), _bf(I, K, seed=19, scale=0.05)
+    w = ops.interleave_gate_up(g, u)
+    out = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
+    ops.gemm._run(x, w, out, 1, bn, splits, mt)
+    ref = torch.nn.functional.silu(x.float() @ g.float().t()) * (x.float() @ u.float().t())
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 
 
 def test_gemm_fp32_out_and_strided_a():

@@ -229,7 +229,7 @@ class ModelRunner:
         need = 0
         for (N, K) in self.model.linear_shapes():
             for M in Ms + [1, 2, 4, 8, 16, 32, 64, 128]:
-                need = max(need, ops.gemm.plan_for(M, N, K)[2], mod.gemm_plan(M, N, K)[2])
+                need = max(need, ops.gemm.plan_for(M, N, K)[3], mod.gemm_plan(M, N, K)[2])
         ops.gemm.reserve_workspace(self.device, need)
         spec = self.model.kv_cache_spec()
         hq = getattr(self.model, "hq", spec["num_kv_heads"])

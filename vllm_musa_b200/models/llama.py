@@ -53,7 +53,9 @@ def kv_head_range(num_kv_heads: int, rank: int, world: int) -> Tuple[int, int]:
 
 
 class _Layer:
-    __slots__ = ("ln1", "ln2", "qkv_w", "o_w", "gu_w", "down_w", "q_norm", "k_norm")
+    __slots__ = ("ln1", "ln2", "qkv_w", "o_w", "gu_w", "down_w", "q_norm", "k_norm", "router_w",
+                 "router_bias", "experts_gu", "experts_down", "shared_gu", "shared_down",
+                 "shared_gate", "extra")
 
     def __init__(self):
         for s in self.__slots__:
@@ -79,7 +81,7 @@ class DenseDecoderForCausalLM:
         if cfg.intermediate_size % self.tp:
             raise ValueError("intermediate_size must be divisible by tensor_parallel_size")
         self.I = cfg.intermediate_size // self.tp
-        self.I_pad = (self.I + 31) // 32 * 32
+        self.I_pad = (self.I + 7) // 8 * 8  # gate/up interleave groups of 8
         self.vocab_local = cfg.vocab_size // self.tp
         if cfg.vocab_size % self.tp:
             raise ValueError("vocab_size must be divisible by tensor_parallel_size")
@@ -129,11 +131,30 @@ class DenseDecoderForCausalLM:
                                f"{self.lm_head is not None}")
         self._staging.clear()
 
+    def _mlp_keys(self, i: int) -> list:
+        return ["mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight"]
+
+    def _finalize_mlp(self, i: int, L, st: dict) -> None:
+        L.gu_w, L.down_w = self._dense_mlp_weights(st["mlp.gate_proj.weight"],
+                                                   st["mlp.up_proj.weight"],
+                                                   st["mlp.down_proj.weight"])
+
+    def _dense_mlp_weights(self, gate, up, down):
+        """TP-shard a SwiGLU MLP: interleaved gate/up rows, down columns padded to I_pad."""
+        r, t = self.rank, self.tp
+        I = gate.shape[0] // t
+        I_pad = (I + 7) // 8 * 8
+        gu = ops.interleave_gate_up(shard_rows(gate, r, t), shard_rows(up, r, t))
+        dn = shard_cols(down, r, t)
+        if I_pad != I:
+            dn = torch.cat([dn, torch.zeros(dn.shape[0], I_pad - I, dtype=dn.dtype,
+                                            device=dn.device)], 1)
+        return self._to(gu), self._to(dn)
+
     def _try_finalize(self, i: int) -> None:
         need = ["input_layernorm.weight", "post_attention_layernorm.weight",
                 "self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
-                "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
-                "mlp.down_proj.weight"]
+                "self_attn.o_proj.weight"] + self._mlp_keys(i)
         if self.cfg.qk_norm:
             need += ["self_attn.q_norm.weight", "self_attn.k_norm.weight"]
         st = self._staging[i]
@@ -145,14 +166,7 @@ class DenseDecoderForCausalLM:
         v = st["self_attn.v_proj.weight"][self.kv0 * D:(self.kv0 + self.hkv) * D]
         L.qkv_w = self._to(torch.cat([q, k, v], 0))
         L.o_w = self._to(shard_cols(st["self_attn.o_proj.weight"], r, t))
-        g = shard_rows(st["mlp.gate_proj.weight"], r, t)
-        u = shard_rows(st["mlp.up_proj.weight"], r, t)
-        L.gu_w = self._to(ops.interleave_gate_up(g, u))
-        dn = shard_cols(st["mlp.down_proj.weight"], r, t)
-        if self.I_pad != self.I:
-            dn = torch.cat([dn, torch.zeros(dn.shape[0], self.I_pad - self.I, dtype=dn.dtype,
-                                            device=dn.device)], 1)
-        L.down_w = self._to(dn)
+        self._finalize_mlp(i, L, st)
         L.ln1 = self._to(st["input_layernorm.weight"])
         L.ln2 = self._to(st["post_attention_layernorm.weight"])
         if self.cfg.qk_norm:
@@ -161,10 +175,13 @@ class DenseDecoderForCausalLM:
         del self._staging[i]
 
     def linear_shapes(self) -> list:
-        """(N, K) of every GEMM weight, for workspace planning."""
-        L = self.layers[0]
-        return [tuple(L.qkv_w.shape), tuple(L.o_w.shape), tuple(L.gu_w.shape),
-                tuple(L.down_w.shape), tuple(self.lm_head.shape)]
+        """(N, K) of every dense GEMM weight, for workspace planning."""
+        out = {tuple(self.lm_head.shape)}
+        for L in self.layers:
+            for w in (L.qkv_w, L.o_w, L.gu_w, L.down_w):
+                if w is not None:
+                    out.add(tuple(w.shape))
+        return sorted(out)
 
     # ------------------------------------------------------------------ forward
     def forward(self, input_ids: torch.Tensor, meta: AttnMetadata,
@@ -185,11 +202,15 @@ class DenseDecoderForCausalLM:
             a = self.attn.forward(qkv, kc, vc, meta)
             o = ops.linear(a, L.o_w, out=self.comm.out_buffer(T))
             x, residual = self.comm.allreduce_add_rmsnorm(o, residual, L.ln2, eps)
-            act = ops.linear_silu_mul(x, L.gu_w)
-            d = ops.linear(act, L.down_w, out=self.comm.out_buffer(T))
+            d = self._mlp(i, L, x, T)
             nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
             x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
         return x
+
+    def _mlp(self, i: int, L, x: torch.Tensor, T: int) -> torch.Tensor:
+        """Dense SwiGLU MLP; returns this rank's partial sum (all-reduced by the caller)."""
+        act = ops.linear_silu_mul(x, L.gu_w)
+        return ops.linear(act, L.down_w, out=self.comm.out_buffer(T))
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """[S, H] -> this rank's vocab shard of the logits, fp32 [S, V/tp]."""

@@ -1,0 +1,79 @@
+"""Qwen3-MoE family (Qwen3-30B-A3B and relatives): Qwen3 attention (QK-RMSNorm, GQA) with a
+softmax top-k routed expert MLP in every layer, optional shared expert.
+
+Experts are tensor-parallel sharded on their intermediate dimension (every rank holds all
+experts, 1/tp of each), so the MoE output is a partial sum that rides on the same fused
+all-reduce + residual + RMSNorm as the dense layers.  The expert computation is the fused MoE
+path of ops/moe.py (device-side routing and expert-sorted layout, grouped tcgen05 GEMMs with
+SwiGLU epilogue, weighted combine written straight into the all-reduce staging buffer).
+Reference counterparts: vllm_musa/model_executor/layers/fused_moe/* (dispatcher, router),
+upstream vLLM's qwen3_moe model it patches.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..ops import moe as moe_ops
+from .llama import DenseDecoderForCausalLM, shard_cols, shard_rows
+
+
+class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
+    def __init__(self, cfg, pstate=None, comm=None, device="cuda"):
+        super().__init__(cfg, pstate, comm, device)
+        if cfg.moe_intermediate_size % self.tp:
+            raise ValueError("moe_intermediate_size must be divisible by tensor_parallel_size")
+        self.E = cfg.num_experts
+        self.topk = cfg.num_experts_per_tok
+        self.I_e = cfg.moe_intermediate_size // self.tp
+
+    def _is_moe(self, i: int) -> bool:
+        return self.cfg.num_experts > 0 and i >= self.cfg.first_k_dense
+
+    def _mlp_keys(self, i):
+        if not self._is_moe(i):
+            return super()._mlp_keys(i)
+        keys = ["mlp.gate.weight"]
+        for e in range(self.cfg.num_experts):
+            keys += [f"mlp.experts.{e}.gate_proj.weight", f"mlp.experts.{e}.up_proj.weight",
+                     f"mlp.experts.{e}.down_proj.weight"]
+        if self.cfg.shared_expert_intermediate_size:
+            keys += ["mlp.shared_expert.gate_proj.weight", "mlp.shared_expert.up_proj.weight",
+                     "mlp.shared_expert.down_proj.weight", "mlp.shared_expert_gate.weight"]
+        return keys
+
+    def _finalize_mlp(self, i, L, st):
+        if not self._is_moe(i):
+            return super()._finalize_mlp(i, L, st)
+        r, t = self.rank, self.tp
+        L.router_w = self._to(st["mlp.gate.weight"])
+        gus, downs = [], []
+        for e in range(self.E):
+            g = shard_rows(st[f"mlp.experts.{e}.gate_proj.weight"], r, t)
+            u = shard_rows(st[f"mlp.experts.{e}.up_proj.weight"], r, t)
+            gus.append(ops.interleave_gate_up(g, u))
+            downs.append(shard_cols(st[f"mlp.experts.{e}.down_proj.weight"], r, t))
+        L.experts_gu = self._to(torch.cat(gus, 0))      # [E * 2I, H]
+        L.experts_down = self._to(torch.cat(downs, 0))  # [E * H, I]
+        if self.cfg.shared_expert_intermediate_size:
+            L.shared_gu, L.shared_down = self._dense_mlp_weights(
+                st["mlp.shared_expert.gate_proj.weight"], st["mlp.shared_expert.up_proj.weight"],
+                st["mlp.shared_expert.down_proj.weight"])
+            L.shared_gate = self._to(st["mlp.shared_expert_gate.weight"])
+
+    def _mlp(self, i, L, x, T):
+        if not self._is_moe(i):
+            return super()._mlp(i, L, x, T)
+        logits = ops.linear(x, L.router_w, out_dtype=torch.float32)
+        ids, w = moe_ops.topk_softmax(logits, self.topk, self.cfg.norm_topk_prob)
+        shared = None
+        if L.shared_gu is not None:
+            shared = ops.linear(ops.linear_silu_mul(x, L.shared_gu), L.shared_down)
+            if L.shared_gate is not None:
+                gate = torch.sigmoid(ops.linear(x, L.shared_gate, out_dtype=torch.float32))
+                shared = (shared.float() * gate).to(shared.dtype)
+        return moe_ops.fused_moe(x, L.experts_gu, L.experts_down, ids, w, self.E, shared,
+                                 out=self.comm.out_buffer(T))
+
+    def linear_shapes(self):
+        return [s for s in super().linear_shapes()]

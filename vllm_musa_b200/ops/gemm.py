@@ -2,7 +2,7 @@
 
 ``linear(x, w)`` = x @ w.T with w in nn.Linear layout [N, K].  ``linear_silu_mul`` applies
 SwiGLU in the GEMM epilogue; its weight must be laid out by :func:`interleave_gate_up`
-(groups of 32 gate rows followed by the matching 32 up rows).
+(groups of 8 gate rows followed by the matching 8 up rows).
 """
 from __future__ import annotations
 
@@ -13,6 +13,8 @@ from . import _ext
 from .. import tuning
 
 _WS: dict = {}
+_COUNTERS: dict = {}
+MAX_TILES = 1 << 16
 
 
 def _workspace(device: torch.device, numel: int) -> torch.Tensor:
@@ -27,31 +29,47 @@ def _workspace(device: torch.device, numel: int) -> torch.Tensor:
     return ws
 
 
+def _counters(device: torch.device) -> torch.Tensor:
+    """Per-tile split-K arrival counters: zeroed once, reset by the kernel after every use."""
+    key = (device.type, device.index)
+    c = _COUNTERS.get(key)
+    if c is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("split-K counters must be allocated before CUDA-graph capture")
+        c = torch.zeros(MAX_TILES, dtype=torch.int32, device=device)
+        _COUNTERS[key] = c
+    return c
+
+
 def reserve_workspace(device: torch.device, numel: int) -> None:
-    """Pre-size the split-K workspace (call before CUDA-graph capture)."""
+    """Pre-size the split-K workspace and counters (call before CUDA-graph capture)."""
     _workspace(device, numel)
+    _counters(device)
 
 
-def plan_for(M: int, N: int, K: int, bn: int = 0, splits: int = 0) -> tuple:
-    """(bn, splits, workspace_floats): forced plan, else the measured table, else the
-    kernel's cost model (bn = splits = 0 lets the launcher decide)."""
-    if bn <= 0 and splits <= 0:
+def plan_for(M: int, N: int, K: int, bn: int = 0, splits: int = 0, mt: int = 0) -> tuple:
+    """(bn, splits, mt, workspace_floats): forced plan, else the measured table, else the
+    kernel's cost model (zeros let the launcher decide)."""
+    if bn <= 0 and splits <= 0 and mt <= 0:
         hit = tuning.gemm_table().lookup(M, N, K)
         if hit is not None:
-            bn, splits = hit
-    if bn > 0 or splits > 0:
-        return bn, splits, (splits if splits > 1 else 0) * M * N
-    _, s, need = _ext.require().gemm_plan(M, N, K)
-    return 0, 0, need
+            bn, splits, mt = hit
+    if bn > 0 or splits > 0 or mt > 0:
+        if splits <= 0:
+            splits = 1
+        return bn, splits, mt, (splits if splits > 1 else 0) * M * N
+    pl = _ext.require().gemm_plan(M, N, K)
+    return 0, 0, 0, pl[2]
 
 
 def _run(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, mode: int, bn: int = 0,
-         splits: int = 0) -> torch.Tensor:
+         splits: int = 0, mt: int = 0) -> torch.Tensor:
     _ext.require()  # registers torch.ops.b200
     M, N, K = x.shape[0], w.shape[0], x.shape[1]
-    bn, splits, need = plan_for(M, N, K, bn, splits)
+    bn, splits, mt, need = plan_for(M, N, K, bn, splits, mt)
     ws = _workspace(x.device, need) if need > 0 else None
-    torch.ops.b200.gemm_bf16(x, w, out, mode, bn, splits, ws)
+    cnt = _counters(x.device) if need > 0 else None
+    torch.ops.b200.gemm_bf16(x, w, out, mode, bn, splits, ws, mt, cnt)
     return out
 
 
@@ -74,8 +92,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     return y
 
 
-def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 32) -> torch.Tensor:
-    """[I, K] gate and up -> [2I, K] with rows (gate[32g:32g+32], up[32g:32g+32]) per group.
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 8) -> torch.Tensor:
+    """[I, K] gate and up -> [2I, K] with rows (gate[8g:8g+8], up[8g:8g+8]) per group.
 
     I is zero-padded to a multiple of ``group``; padded channels contribute silu(0)*0 = 0.
     """
@@ -88,7 +106,7 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 32) ->
     return torch.stack([gate.reshape(G, group, K), up.reshape(G, group, K)], 1).reshape(-1, K)
 
 
-def deinterleave_gate_up(w: torch.Tensor, group: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
+def deinterleave_gate_up(w: torch.Tensor, group: int = 8) -> tuple[torch.Tensor, torch.Tensor]:
     K = w.shape[1]
     v = w.reshape(-1, 2, group, K)
     return v[:, 0].reshape(-1, K), v[:, 1].reshape(-1, K)

@@ -1,0 +1,120 @@
+"""Mixture-of-experts ops: routing, expert-sorted layout, grouped GEMMs, weighted combine.
+
+CUDA path (csrc/moe/moe.cu + the grouped mode of csrc/gemm/gemm_bf16.cu):
+    ids, w   = topk_softmax(router_logits)            (or grouped_topk)
+    sorted   = moe_align(ids)     every expert's rows padded to 128, counts stay on device
+    xs       = moe_gather(x)      [max_rows, H] expert-contiguous activations
+    h        = grouped GEMM(xs, W_gate_up, SwiGLU epilogue)   [max_rows, I]
+    y        = grouped GEMM(h, W_down)                         [max_rows, H]
+    out      = moe_combine(y, w)  (+ shared-expert output)
+No host synchronisation anywhere, so decode MoE layers run inside CUDA graphs.
+CPU path: a per-expert loop in PyTorch (reference semantics).  Reference counterpart:
+vllm_musa/model_executor/layers/fused_moe/fused_moe.py:2214-2765 (dispatcher and backends).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _ext
+from .gemm import deinterleave_gate_up
+
+
+def topk_softmax(logits: torch.Tensor, k: int, renorm: bool = True):
+    T, E = logits.shape
+    if logits.is_cuda:
+        ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+        if T:
+            _ext.ops().topk_softmax(logits.float().contiguous(), ids, w, renorm)
+        return ids, w
+    p = torch.softmax(logits.float(), -1)
+    w, ids = torch.topk(p, k, dim=-1)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return ids.to(torch.int32), w
+
+
+def grouped_topk(logits: torch.Tensor, k: int, n_group: int, topk_group: int,
+                 bias: Optional[torch.Tensor] = None, sigmoid: bool = True, renorm: bool = True,
+                 scale: float = 1.0):
+    T, E = logits.shape
+    if logits.is_cuda:
+        ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+        if T:
+            _ext.ops().grouped_topk(logits.float().contiguous(),
+                                    bias.float().contiguous() if bias is not None else None,
+                                    ids, w, n_group, topk_group, sigmoid, renorm, scale)
+        return ids, w
+    s = torch.sigmoid(logits.float()) if sigmoid else torch.softmax(logits.float(), -1)
+    b = s + (bias.float() if bias is not None else 0.0)
+    g = b.view(T, n_group, E // n_group)
+    gscore = g.topk(min(2, E // n_group), dim=-1).values.sum(-1)
+    keep = torch.zeros(T, n_group, dtype=torch.bool)
+    keep.scatter_(1, gscore.topk(topk_group, dim=-1).indices, True)
+    b = b.masked_fill(~keep.repeat_interleave(E // n_group, dim=1), float("-inf"))
+    ids = b.topk(k, dim=-1).indices
+    w = s.gather(1, ids)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return ids.to(torch.int32), w * scale
+
+
+def _fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared):
+    T, H = x.shape
+    I2 = w_gu.shape[0] // num_experts
+    out = torch.zeros(T, H, dtype=torch.float32)
+    xf = x.float()
+    for e in range(num_experts):
+        tok, slot = torch.nonzero(ids == e, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        g, u = deinterleave_gate_up(w_gu[e * I2:(e + 1) * I2])
+        h = F.silu(xf[tok] @ g.float().t()) * (xf[tok] @ u.float().t())
+        h = h.to(x.dtype).float()
+        d = w_down[e * H:(e + 1) * H].float()
+        y = (h @ d.t()).to(x.dtype).float()
+        out.index_add_(0, tok, y * w[tok, slot].unsqueeze(1).float())
+    if shared is not None:
+        out += shared.float()
+    return out.to(x.dtype)
+
+
+def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: torch.Tensor,
+              w: torch.Tensor, num_experts: int, shared: Optional[torch.Tensor] = None,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x [T, H]; w_gu [E * 2I, H] (gate/up interleaved per expert); w_down [E * H, I];
+    ids/w [T, k] -> [T, H] = sum_j w[:, j] * expert_{ids[:, j]}(x) (+ shared)."""
+    T, H = x.shape
+    k = ids.shape[1]
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    if not x.is_cuda:
+        out.copy_(_fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared))
+        return out
+    mod = _ext.require()
+    E = num_experts
+    n = T * k
+    max_rows = int(mod.moe_max_rows(n, E))
+    dev = x.device
+    sorted_ids = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    tile_expert = torch.empty(max_rows // 128, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, k, dtype=torch.int32, device=dev)
+    num_tiles = torch.empty(1, dtype=torch.int32, device=dev)
+    ops = torch.ops.b200
+    ops.moe_align(ids.contiguous(), E, sorted_ids, tile_expert, offsets, pos, num_tiles)
+    xs = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
+    ops.moe_gather(x, sorted_ids, num_tiles, k, xs)
+    I = w_gu.shape[0] // E // 2
+    h = torch.empty(max_rows, I, dtype=x.dtype, device=dev)
+    ops.gemm_grouped_bf16(xs, w_gu, h, tile_expert, num_tiles, E, 1, 0)
+    y = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
+    ops.gemm_grouped_bf16(h, w_down, y, tile_expert, num_tiles, E, 0, 0)
+    ops.moe_combine(y, pos, w.contiguous(), shared, out)
+    return out

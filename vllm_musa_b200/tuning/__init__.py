@@ -5,7 +5,8 @@ and its offline-measured fp8_block_splitk.json.  Here the tables are measured on
 sweep scripts under benchmarks/ and consulted at run time by the kernel wrappers.
 
 Table ``gemm_bf16``: {"device": str, "entries": [{"n": N, "k": K, "m": M, "bn": BN,
-"splits": S, "us": t}, ...]}: the fastest plan measured for each (N, K) at each M bucket.
+"splits": S, "mt": MT, "us": t}, ...]}: the fastest plan measured for each (N, K) at each M
+bucket (BN a multiple of 16 up to 256, MT = 128-row halves per CTA).
 """
 from __future__ import annotations
 
@@ -18,7 +19,8 @@ from typing import Optional
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 _SCHEMAS = {
-    "gemm_bf16": {"entry_keys": {"n", "k", "m", "bn", "splits"}, "bn": {64, 128, 256}},
+    "gemm_bf16": {"entry_keys": {"n", "k", "m", "bn", "splits"},
+                  "bn": set(range(16, 257, 16))},
 }
 
 
@@ -61,7 +63,7 @@ class GemmPlanTable:
         self.by_nk = {}
         for e in (table or {}).get("entries", []):
             self.by_nk.setdefault((int(e["n"]), int(e["k"])), []).append(
-                (int(e["m"]), int(e["bn"]), int(e["splits"])))
+                (int(e["m"]), int(e["bn"]), int(e["splits"]), int(e.get("mt", 1))))
         for v in self.by_nk.values():
             v.sort()
 
@@ -72,8 +74,8 @@ class GemmPlanTable:
         i = bisect.bisect_left([r[0] for r in rows], M)
         if i == len(rows):
             return None  # larger than anything measured: cost model decides
-        _, bn, s = rows[i]
-        return bn, s
+        _, bn, s, mt = rows[i]
+        return bn, s, mt
 
 
 @lru_cache(maxsize=None)
