@@ -566,19 +566,9 @@ static CUtensorMap cache_map(void* base, int64_t rows, int D, int box_rows) {
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// Raise the dynamic shared-memory limit of a kernel once per (kernel, device).
 template <typename K>
 static void set_smem(K kern, int bytes) {
-  static std::mutex mu;
-  static std::set<std::pair<const void*, int>> done;
-  int dev;
-  B200_CUDA_OK(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lk(mu);
-  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), dev);
-  if (!done.count(key)) {
-    B200_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done.insert(key);
-  }
+  ensure_dynamic_smem(reinterpret_cast<const void*>(kern), bytes);
 }
 
 int decode_num_splits(int B, int Hkv, int max_seq_len) {

@@ -55,6 +55,19 @@ struct GroupedGemmArgs {
 void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t s);
 }  // namespace gemm
 
+// ------------------------------------------------------------------------------- GDN
+namespace gdn {
+void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,
+                       const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
+                       int T, int C, void* out, int64_t ldo, cudaStream_t s);
+void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld_ba,
+                       const float* A_log, const float* dt_bias, float* state,
+                       const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
+                       int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s);
+void run_sigmoid_gate(void* out, int64_t ldo, const void* gate, int64_t ldg, int T, int W,
+                      cudaStream_t s);
+}  // namespace gdn
+
 // ------------------------------------------------------------------------------- MoE
 namespace moe {
 void run_topk_softmax(const float* logits, int T, int E, int k, bool renorm, int32_t* ids,
@@ -87,8 +100,9 @@ struct RmsNormArgs {
   bool gemma;
 };
 void run_rms_norm(const RmsNormArgs& a, cudaStream_t s);
-void run_rms_norm_gated(void* out, const void* x, const void* z, const void* w, int rows, int H,
-                        int group, float eps, cudaStream_t s);
+void run_rms_norm_gated(void* out, int64_t ldo, const void* x, int64_t ldx, const void* z,
+                        int64_t ldz, const void* w, int rows, int H, int group, float eps,
+                        cudaStream_t s);
 }  // namespace norm
 
 // ------------------------------------------------------------------------------- activations

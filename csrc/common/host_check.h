@@ -5,8 +5,11 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <mutex>
+#include <set>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #define B200_REQUIRE(cond, msg)                                                           \
   do {                                                                                    \
@@ -30,6 +33,23 @@ inline std::atomic<long long>& launch_counter() {
   return c;
 }
 inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_order_relaxed); }
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel address, device).
+inline void ensure_dynamic_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  B200_CUDA_OK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.insert({kernel, dev}).second) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) {
+      done.erase({kernel, dev});
+      B200_CUDA_OK(e);
+    }
+  }
+}
 
 inline int num_sms() {
   static int n = -1;

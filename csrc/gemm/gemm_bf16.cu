@@ -45,7 +45,7 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle atom
 constexpr int kThreads = 192;
 constexpr int kGroupN = 8;
 constexpr int kMaxStages = 8;
-constexpr int kSmemBudget = 227 * 1024;
+constexpr int kSmemBudget = 226 * 1024;  // dynamic opt-in; leaves room for static smem
 constexpr int kSmemOverhead = 1024 /*align*/ + 512 /*barriers, tmem slot*/;
 
 enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2 };
@@ -312,9 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               float* w = p.ws + ((size_t)ks * p.M + row) * p.N + col;
 #pragma unroll
               for (int v = 0; v < 4; ++v)
-                reinterpret_cast<float4*>(w)[v] =
-                    make_float4(__uint_as_float(r[h][4 * v]), __uint_as_float(r[h][4 * v + 1]),
-                                __uint_as_float(r[h][4 * v + 2]), __uint_as_float(r[h][4 * v + 3]));
+                if (col + 4 * v < p.N)  // N % 4 == 0: a float4 is either in or out of the row
+                  reinterpret_cast<float4*>(w)[v] = make_float4(
+                      __uint_as_float(r[h][4 * v]), __uint_as_float(r[h][4 * v + 1]),
+                      __uint_as_float(r[h][4 * v + 2]), __uint_as_float(r[h][4 * v + 3]));
             } else {
               float f[16];
 #pragma unroll
@@ -357,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     reinterpret_cast<const float4*>(p.ws + ((size_t)sp * p.M + row) * p.N + col);
 #pragma unroll
                 for (int v = 0; v < 4; ++v) {
+                  if (col + 4 * v >= p.N) break;
                   const float4 t = __ldcg(w + v);
                   f[4 * v] += t.x;
                   f[4 * v + 1] += t.y;
@@ -457,21 +459,27 @@ static void launch_pdl(K kern, int grid, int smem, cudaStream_t stream, const CU
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B200_CUDA_OK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the launch error so later launches do not report it
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(kern));
+    throw std::runtime_error(
+        std::string("b200: gemm launch failed: ") + cudaGetErrorString(e) +
+        " grid=" + std::to_string(grid) + " smem=" + std::to_string(smem) +
+        " max_dyn_smem=" + std::to_string(fa.maxDynamicSharedSizeBytes) +
+        " static_smem=" + std::to_string(fa.sharedSizeBytes) + " regs=" +
+        std::to_string(fa.numRegs) + " M=" + std::to_string(p.M) + " N=" + std::to_string(p.N) +
+        " K=" + std::to_string(p.K) + " bn=" + std::to_string(p.bn) +
+        " stages=" + std::to_string(p.stages) + " units=" + std::to_string(p.total_units));
+  }
 }
 
 template <int MT, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                    cudaStream_t stream) {
   auto kern = gemm_bf16_kernel<MT, EPI>;
-  static uint32_t attr_set = 0;  // bit per device
-  int dev;
-  B200_CUDA_OK(cudaGetDevice(&dev));
-  if (!(attr_set & (1u << dev))) {
-    B200_CUDA_OK(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget));
-    attr_set |= 1u << dev;
-  }
+  ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
   const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) + kSmemOverhead;
   const int grid = std::min(p.total_units, num_sms());
   launch_pdl(kern, grid, smem, stream, ta, tb, p);
@@ -530,14 +538,7 @@ void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
       make_tma_2d(const_cast<void*>(a.B), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K,
                   (uint64_t)a.num_experts * N, a.ldb, BK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   auto go = [&](auto kern) {
-    static uint32_t attr = 0;
-    int dev;
-    B200_CUDA_OK(cudaGetDevice(&dev));
-    if (!(attr & (1u << dev))) {
-      B200_CUDA_OK(
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget));
-      attr |= 1u << dev;
-    }
+    ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
     const int smem = p.stages * (a_tile_bytes(1) + b_tile_bytes(bn)) + kSmemOverhead;
     const int grid = std::min(p.total_units, num_sms());
     launch_pdl(kern, grid, smem, stream, ta, tb, p);

@@ -66,9 +66,9 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ out, int64_t ld_out,
 
 // Gated RMSNorm: out = RMSNorm_group(x) * w * silu(z), statistics per group of `group` elems.
 // One warp per (row, group) when group <= 256 elements; generic loop otherwise.
-__global__ void rmsnorm_gated_kernel(__nv_bfloat16* __restrict__ out,
-                                     const __nv_bfloat16* __restrict__ x,
-                                     const __nv_bfloat16* __restrict__ z,
+__global__ void rmsnorm_gated_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo,
+                                     const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                     const __nv_bfloat16* __restrict__ z, int64_t ldz,
                                      const __nv_bfloat16* __restrict__ w, int rows, int H,
                                      int group, float eps) {
   const int warps = blockDim.x / 32;
@@ -77,9 +77,9 @@ __global__ void rmsnorm_gated_kernel(__nv_bfloat16* __restrict__ out,
   if (gid >= rows * groups_per_row) return;
   const int row = gid / groups_per_row, g = gid % groups_per_row;
   const int lane = threadIdx.x & 31;
-  const __nv_bfloat16* xp = x + (size_t)row * H + g * group;
-  const __nv_bfloat16* zp = z + (size_t)row * H + g * group;
-  __nv_bfloat16* op = out + (size_t)row * H + g * group;
+  const __nv_bfloat16* xp = x + (size_t)row * ldx + g * group;
+  const __nv_bfloat16* zp = z + (size_t)row * ldz + g * group;
+  __nv_bfloat16* op = out + (size_t)row * ldo + g * group;
   float ss = 0.f;
   for (int i = lane; i < group; i += 32) {
     const float t = bf2f(xp[i]);
@@ -137,16 +137,17 @@ void run_rms_norm(const RmsNormArgs& a, cudaStream_t s) {
   }
 }
 
-void run_rms_norm_gated(void* out, const void* x, const void* z, const void* w, int rows, int H,
-                        int group, float eps, cudaStream_t s) {
+void run_rms_norm_gated(void* out, int64_t ldo, const void* x, int64_t ldx, const void* z,
+                        int64_t ldz, const void* w, int rows, int H, int group, float eps,
+                        cudaStream_t s) {
   B200_REQUIRE(H % group == 0, "rms_norm_gated: H must be a multiple of the group size");
   const int total = rows * (H / group);
   if (total == 0) return;
   const int threads = 256;
   rmsnorm_gated_kernel<<<(total + 7) / 8, threads, 0, s>>>(
-      reinterpret_cast<__nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(x),
-      reinterpret_cast<const __nv_bfloat16*>(z), reinterpret_cast<const __nv_bfloat16*>(w), rows,
-      H, group, eps);
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+      reinterpret_cast<const __nv_bfloat16*>(z), ldz, reinterpret_cast<const __nv_bfloat16*>(w),
+      rows, H, group, eps);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
 }

@@ -23,6 +23,7 @@ static StepBuffers buffers_from(py::dict d) {
   b.min_p = reinterpret_cast<float*>(d["min_p"].cast<uintptr_t>());
   b.seeds = reinterpret_cast<int64_t*>(d["seeds"].cast<uintptr_t>());
   b.steps = p32("steps");
+  b.state_slots = d.contains("state_slots") ? p32("state_slots") : nullptr;
   b.max_tokens = d["max_tokens"].cast<int>();
   b.max_reqs = d["max_reqs"].cast<int>();
   return b;
@@ -101,6 +102,7 @@ void register_runtime(py::module_& m) {
         d["finish_step"] = r->finish_step;
         d["num_preemptions"] = r->num_preemptions;
         d["num_blocks"] = (int)r->blocks.size();
+        d["state_slot"] = r->state_slot;
         return d;
       });
 }

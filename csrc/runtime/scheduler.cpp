@@ -90,6 +90,7 @@ uint64_t Scheduler::block_hash(uint64_t parent, const int32_t* toks, int n) cons
 
 Scheduler::Scheduler(const SchedulerConfig& cfg, int num_blocks, const StepBuffers& buf)
     : cfg_(cfg), pool_(num_blocks), buf_(buf) {
+  for (int s = cfg_.max_num_seqs - 1; s >= 0; --s) free_slots_.push_back(s);
   if (cfg_.block_size <= 0) throw std::runtime_error("scheduler: block_size must be > 0");
   if ((int64_t)cfg_.max_blocks_per_seq * cfg_.block_size < cfg_.max_model_len)
     throw std::runtime_error("scheduler: block-table width cannot hold max_model_len");
@@ -114,6 +115,13 @@ void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt,
   waiting_.push_back(id);
 }
 
+void Scheduler::release_slot(Request& r) {
+  if (r.state_slot >= 0) {
+    free_slots_.push_back(r.state_slot);
+    r.state_slot = -1;
+  }
+}
+
 void Scheduler::free_request_blocks(Request& r) {
   // reverse order: the tail blocks (least likely shared) are handed out first
   for (auto it = r.blocks.rbegin(); it != r.blocks.rend(); ++it) pool_.release(*it);
@@ -131,6 +139,7 @@ bool Scheduler::abort_request(int64_t id) {
     running_.erase(std::remove(running_.begin(), running_.end(), id), running_.end());
   }
   free_request_blocks(r);
+  release_slot(r);
   r.status = kFinished;
   r.reason = kAbort;
   r.finish_step = step_;
@@ -139,6 +148,7 @@ bool Scheduler::abort_request(int64_t id) {
 
 void Scheduler::preempt(Request& r) {
   free_request_blocks(r);
+  release_slot(r);
   r.num_computed = 0;
   r.num_cached_prefix = 0;
   r.status = kWaiting;
@@ -237,6 +247,10 @@ StepPlan Scheduler::schedule() {
     if (!ensure_blocks(r, r.num_computed + q)) break;
     waiting_.pop_front();
     r.status = kRunning;
+    if (r.state_slot < 0 && !free_slots_.empty()) {
+      r.state_slot = free_slots_.back();
+      free_slots_.pop_back();
+    }
     running_.push_back(r.id);
     items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size()});
     budget -= q;
@@ -262,6 +276,7 @@ StepPlan Scheduler::schedule() {
     buf_.cu_q[i + 1] = t;
     const int seq_len = it.start + it.q;
     buf_.seq_lens[i] = seq_len;
+    if (buf_.state_slots) buf_.state_slots[i] = r.state_slot;
     plan.max_seq_len = std::max(plan.max_seq_len, seq_len);
     std::copy(r.blocks.begin(), r.blocks.end(),
               buf_.block_tables + (int64_t)i * cfg_.max_blocks_per_seq);
@@ -324,6 +339,7 @@ std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, i
       r.reason = why;
       r.finish_step = step_;
       free_request_blocks(r);
+      release_slot(r);
       finished.emplace_back(r.id, (int)why);
     }
   }

@@ -47,6 +47,7 @@ struct Request {
   Status status = kWaiting;
   FinishReason reason = kNotFinished;
   SamplingCfg sp;
+  int32_t state_slot = -1;      // per-request recurrent-state slot (hybrid models)
   int64_t first_token_step = -1;
   int64_t finish_step = -1;
   int num_preemptions = 0;
@@ -106,6 +107,7 @@ struct StepBuffers {
   float* min_p;           // [max_reqs]
   int64_t* seeds;         // [max_reqs]
   int32_t* steps;         // [max_reqs]  output index of the token being drawn
+  int32_t* state_slots;   // [max_reqs]  recurrent-state slot of every scheduled request
   int max_tokens, max_reqs;
 };
 
@@ -160,6 +162,8 @@ class Scheduler {
   std::deque<int64_t> waiting_;
   std::vector<int64_t> running_;
   std::vector<int64_t> last_sample_ids_;
+  std::vector<int32_t> free_slots_;
+  void release_slot(Request& r);
   int64_t step_ = 0;
 };
 

@@ -1,0 +1,286 @@
+// Gated DeltaNet (Qwen3-Next linear-attention layers) for sm_100a.
+//
+//  causal_conv1d   depthwise causal convolution (kernel 4) + SiLU over the packed [q | k | v]
+//                  channels of a varlen batch.  Token t of request r reads inputs t-3..t; the
+//                  ones before the request's first new token come from its conv state slot
+//                  (the last 3 inputs of its previous chunk; zeros for a fresh request).
+//  conv_state_update  writes each request's last 3 inputs back into its slot.
+//  gdn_recurrent   the gated delta rule, token by token:
+//                      S <- exp(g_t) S;  u = beta_t (v_t - S^T k_t);  S <- S + k_t u^T;
+//                      o_t = S^T q_t
+//                  with q, k L2-normalised (q also scaled by 1/sqrt(dk)), g_t =
+//                  -exp(A_log) softplus(a_t + dt_bias), beta_t = sigmoid(b_t).  One CTA per
+//                  (request, value head); the 128 x 128 fp32 state lives in registers (4
+//                  threads per value column, 32 key rows each) for the whole chunk, tokens are
+//                  staged through shared memory 16 at a time.  Prefill chunks and decode steps
+//                  use the same kernel; the state slot carries across engine steps.
+// State layout: [slots, Hv, dv, dk] fp32 (value-major, so each thread's 32 key rows are one
+// contiguous 128-byte run).
+//
+// Reference counterparts: vllm_musa/model_executor/layers/mamba/gdn/qwen_gdn_linear_attn.py
+// :296-557 (MATE gated_delta_rule_decode / chunk_gated_delta_rule, no source in the
+// reference), vllm_musa/jit_kernel/tilelang/causal_conv1d.py:101-989,
+// vllm_musa/jit_kernel/fused_gdn_gating.py:22.
+#include "../b200_kernels.h"
+#include "../common/common.cuh"
+
+namespace b200 {
+namespace gdn {
+
+constexpr int kDK = 128, kDV = 128;
+constexpr int kThreads = 512;  // 128 value columns x 4 key quarters
+constexpr int kTok = 16;       // tokens staged per round (24 KB of shared memory)
+
+B200_DEVICE int find_req(const int32_t* cu, int R, int t) {
+  int lo = 0, hi = R - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// ------------------------------------------------------------------------------ conv1d
+__global__ void causal_conv1d_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                     const __nv_bfloat16* __restrict__ w,  // [C, 4]
+                                     const __nv_bfloat16* __restrict__ state,  // [slots, C, 3]
+                                     const int32_t* __restrict__ cu_q,
+                                     const int32_t* __restrict__ seq_lens,
+                                     const int32_t* __restrict__ slots, int R, int C,
+                                     __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  pdl_launch_dependents();
+  const int t = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int r = find_req(cu_q, R, t);
+  const int q0 = cu_q[r];
+  const int q_len = cu_q[r + 1] - q0;
+  const bool hist = seq_lens[r] - q_len > 0;
+  const __nv_bfloat16* st = state + ((size_t)slots[r] * C + c) * 3;
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int tau = t - 3 + j;  // absolute token index in the batch
+    float xin;
+    if (tau >= q0) {
+      xin = bf2f(x[(size_t)tau * ldx + c]);
+    } else {
+      const int back = q0 - tau;  // 1..3 tokens before the chunk
+      xin = hist ? bf2f(st[3 - back]) : 0.f;
+    }
+    acc += xin * bf2f(w[c * 4 + j]);
+  }
+  out[(size_t)t * ldo + c] = f2bf(acc / (1.f + __expf(-acc)));
+}
+
+__global__ void conv_state_update_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                         __nv_bfloat16* __restrict__ state,
+                                         const int32_t* __restrict__ cu_q,
+                                         const int32_t* __restrict__ seq_lens,
+                                         const int32_t* __restrict__ slots, int R, int C) {
+  const int r = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C || r >= R) return;
+  const int q0 = cu_q[r], L = cu_q[r + 1] - q0;
+  const bool hist = seq_lens[r] - L > 0;
+  __nv_bfloat16* st = state + ((size_t)slots[r] * C + c) * 3;
+  float old[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) old[j] = hist ? bf2f(st[j]) : 0.f;
+  float nw[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int rel = L - 3 + j;  // index into this chunk (negative: from the old state)
+    nw[j] = rel >= 0 ? bf2f(x[(size_t)(q0 + rel) * ldx + c]) : old[3 + rel];
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) st[j] = f2bf(nw[j]);
+}
+
+// ------------------------------------------------------------------------------ recurrence
+struct RecParams {
+  const __nv_bfloat16* qkv;  // [T, >= 2*Hk*dk + Hv*dv] conv output
+  int64_t ld_qkv;
+  const __nv_bfloat16* ba;   // [T, >= 2*Hv]: b then a
+  int64_t ld_ba;
+  const float* A_log;        // [Hv]
+  const float* dt_bias;      // [Hv]
+  float* state;              // [slots, Hv, dv, dk]
+  const int32_t* cu_q;
+  const int32_t* seq_lens;
+  const int32_t* slots;
+  __nv_bfloat16* out;        // [T, Hv*dv]
+  int64_t ld_out;
+  int R, Hk, Hv;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) gdn_recurrent_kernel(RecParams p) {
+  pdl_launch_dependents();
+  __shared__ float sq[kTok][kDK], sk[kTok][kDK], sv[kTok][kDV];
+  __shared__ float sg[kTok], sb[kTok];
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int vcol = tid >> 2, kq = tid & 3;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int q0 = p.cu_q[r];
+  const int L = p.cu_q[r + 1] - q0;
+  const bool hist = p.seq_lens[r] - L > 0;
+  const int hk = h / (p.Hv / p.Hk);
+  float* gstate = p.state + (((size_t)p.slots[r] * p.Hv + h) * kDV + vcol) * kDK + kq * 32;
+  float S[32];
+  if (hist) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v4 = reinterpret_cast<const float4*>(gstate)[i];
+      S[4 * i] = v4.x;
+      S[4 * i + 1] = v4.y;
+      S[4 * i + 2] = v4.z;
+      S[4 * i + 3] = v4.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) S[i] = 0.f;
+  }
+  const float A = -__expf(p.A_log[h]);
+  const float dtb = p.dt_bias[h];
+  const float qscale = rsqrtf((float)kDK);
+  const int qoff = hk * kDK, koff = p.Hk * kDK + hk * kDK, voff = 2 * p.Hk * kDK + h * kDV;
+  for (int base = 0; base < L; base += kTok) {
+    const int nt = min(kTok, L - base);
+    __syncthreads();  // previous round done with the staging buffers
+    // stage + L2-normalise q and k (one warp per token), v, gates
+    for (int j = warp; j < nt; j += kThreads / 32) {
+      const __nv_bfloat16* row = p.qkv + (size_t)(q0 + base + j) * p.ld_qkv;
+      float qv[4], kv[4];
+      float sqq = 0.f, skk = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qv[e] = bf2f(row[qoff + lane * 4 + e]);
+        kv[e] = bf2f(row[koff + lane * 4 + e]);
+        sqq += qv[e] * qv[e];
+        skk += kv[e] * kv[e];
+      }
+      sqq = warp_sum(sqq);
+      skk = warp_sum(skk);
+      const float iq = rsqrtf(sqq + 1e-6f) * qscale, ik = rsqrtf(skk + 1e-6f);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sq[j][lane * 4 + e] = qv[e] * iq;
+        sk[j][lane * 4 + e] = kv[e] * ik;
+        sv[j][lane * 4 + e] = bf2f(row[voff + lane * 4 + e]);
+      }
+      if (lane == 0) {
+        const __nv_bfloat16* ba = p.ba + (size_t)(q0 + base + j) * p.ld_ba;
+        const float b = bf2f(ba[h]), a = bf2f(ba[p.Hv + h]);
+        const float x = a + dtb;
+        const float sp = x > 20.f ? x : log1pf(__expf(x));  // softplus
+        sg[j] = __expf(A * sp);
+        sb[j] = 1.f / (1.f + __expf(-b));
+      }
+    }
+    __syncthreads();
+    for (int j = 0; j < nt; ++j) {
+      const float decay = sg[j], beta = sb[j];
+      const float* kk = &sk[j][kq * 32];
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        S[i] *= decay;
+        dot += S[i] * kk[i];
+      }
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      const float u = (sv[j][vcol] - dot) * beta;
+      const float* qq = &sq[j][kq * 32];
+      float o = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        S[i] += kk[i] * u;
+        o += S[i] * qq[i];
+      }
+      o += __shfl_xor_sync(0xffffffffu, o, 1);
+      o += __shfl_xor_sync(0xffffffffu, o, 2);
+      if (kq == 0) p.out[(size_t)(q0 + base + j) * p.ld_out + h * kDV + vcol] = f2bf(o);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    reinterpret_cast<float4*>(gstate)[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+}
+
+// Attention output gate (Qwen3-Next gated attention): out *= sigmoid(gate), both [T, W].
+__global__ void sigmoid_gate_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo,
+                                    const __nv_bfloat16* __restrict__ gate, int64_t ldg, int W) {
+  pdl_launch_dependents();
+  const int t = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= W) return;
+  float o[8], g[8];
+  uint4* op = reinterpret_cast<uint4*>(out + (size_t)t * ldo + c);
+  unpack8(*op, o);
+  unpack8(*reinterpret_cast<const uint4*>(gate + (size_t)t * ldg + c), g);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = o[j] / (1.f + __expf(-g[j]));
+  *op = pack8(o);
+}
+
+// ------------------------------------------------------------------------------ launchers
+void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,
+                       const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
+                       int T, int C, void* out, int64_t ldo, cudaStream_t s) {
+  if (T == 0 || R == 0) return;
+  const int threads = 128;
+  causal_conv1d_kernel<<<dim3((C + threads - 1) / threads, T), threads, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<const __nv_bfloat16*>(w),
+      reinterpret_cast<const __nv_bfloat16*>(state), cu_q, seq_lens, slots, R, C,
+      reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+  conv_state_update_kernel<<<dim3((C + threads - 1) / threads, R), threads, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<__nv_bfloat16*>(state),
+      cu_q, seq_lens, slots, R, C);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
+void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld_ba,
+                       const float* A_log, const float* dt_bias, float* state,
+                       const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
+                       int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s) {
+  B200_REQUIRE(Hv % Hk == 0, "gdn: value heads must be a multiple of key heads");
+  if (R == 0) return;
+  RecParams p;
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv);
+  p.ld_qkv = ld_qkv;
+  p.ba = reinterpret_cast<const __nv_bfloat16*>(ba);
+  p.ld_ba = ld_ba;
+  p.A_log = A_log;
+  p.dt_bias = dt_bias;
+  p.state = state;
+  p.cu_q = cu_q;
+  p.seq_lens = seq_lens;
+  p.slots = slots;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.R = R;
+  p.Hk = Hk;
+  p.Hv = Hv;
+  gdn_recurrent_kernel<<<dim3(R, Hv), kThreads, 0, s>>>(p);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
+void run_sigmoid_gate(void* out, int64_t ldo, const void* gate, int64_t ldg, int T, int W,
+                      cudaStream_t s) {
+  B200_REQUIRE(W % 8 == 0, "sigmoid_gate: width % 8");
+  if (T == 0) return;
+  const int threads = 128;
+  sigmoid_gate_kernel<<<dim3((W / 8 + threads - 1) / threads, T), threads, 0, s>>>(
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(gate),
+      ldg, W);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace gdn
+}  // namespace b200

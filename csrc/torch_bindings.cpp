@@ -152,14 +152,18 @@ void rms_norm_gated(Tensor& out, const Tensor& x, const Tensor& z, const Tensor&
   CHECK_BF16(x);
   CHECK_BF16(z);
   CHECK_BF16(w);
-  TORCH_CHECK(x.is_contiguous() && z.is_contiguous() && out.is_contiguous(), "rms_norm_gated");
+  CHECK_ROWMAJOR(x);
+  CHECK_ROWMAJOR(z);
+  CHECK_ROWMAJOR(out);
   TORCH_CHECK(w.numel() == group, "rms_norm_gated: weight must have `group` elements");
   const c10::cuda::CUDAGuard g(x.device());
-  const int H = x.size(-1);
-  const int rows = x.numel() / H;
+  const int H = x.size(1);
+  const int rows = x.size(0);
+  TORCH_CHECK(z.size(1) == H && out.size(1) == H && z.size(0) == rows, "rms_norm_gated: shapes");
   guarded([&] {
-    b200::norm::run_rms_norm_gated(out.data_ptr(), x.data_ptr(), z.data_ptr(), w.data_ptr(), rows,
-                                   H, group, eps, stream_of(x));
+    b200::norm::run_rms_norm_gated(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0),
+                                   z.data_ptr(), z.stride(0), w.data_ptr(), rows, H, group, eps,
+                                   stream_of(x));
   });
 }
 
@@ -430,6 +434,63 @@ void gather_rows(Tensor& out, const Tensor& x, const Tensor& idx) {
 
 Tensor error_word(const Tensor& like) { return error_word_for(like.device()); }
 
+// ------------------------------------------------------------------------------------- GDN
+void causal_conv1d(const Tensor& x, const Tensor& w, Tensor& state, const Tensor& cu_q,
+                   const Tensor& seq_lens, const Tensor& slots, Tensor& out) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(w.is_contiguous() && w.dim() == 2 && w.size(1) == 4, "conv weight [C, 4]");
+  TORCH_CHECK(state.is_contiguous() && state.dim() == 3 && state.size(2) == 3 &&
+                  state.scalar_type() == at::kBFloat16,
+              "conv state [slots, C, 3] bf16");
+  const int C = w.size(0);
+  TORCH_CHECK(state.size(1) == C && x.size(1) >= C && out.size(1) >= C, "conv widths");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::gdn::run_causal_conv1d(x.data_ptr(), x.stride(0), w.data_ptr(), state.data_ptr(),
+                                 cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                                 slots.data_ptr<int32_t>(), seq_lens.numel(), x.size(0), C,
+                                 out.data_ptr(), out.stride(0), stream_of(x));
+  });
+}
+
+void gdn_recurrent(const Tensor& qkv, const Tensor& ba, const Tensor& A_log, const Tensor& dt_bias,
+                   Tensor& state, const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots,
+                   int64_t Hk, int64_t Hv, Tensor& out) {
+  CHECK_CUDA(qkv);
+  CHECK_BF16(qkv);
+  CHECK_ROWMAJOR(qkv);
+  CHECK_ROWMAJOR(ba);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4 &&
+                  state.size(1) == Hv && state.size(2) == 128 && state.size(3) == 128,
+              "gdn state [slots, Hv, 128, 128] fp32");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
+              "A_log / dt_bias fp32");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  guarded([&] {
+    b200::gdn::run_gdn_recurrent(qkv.data_ptr(), qkv.stride(0), ba.data_ptr(), ba.stride(0),
+                                 A_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                                 state.data_ptr<float>(), cu_q.data_ptr<int32_t>(),
+                                 seq_lens.data_ptr<int32_t>(), slots.data_ptr<int32_t>(),
+                                 seq_lens.numel(), Hk, Hv, out.data_ptr(), out.stride(0),
+                                 stream_of(qkv));
+  });
+}
+
+void sigmoid_gate(Tensor& out, const Tensor& gate) {
+  CHECK_CUDA(out);
+  CHECK_ROWMAJOR(out);
+  CHECK_ROWMAJOR(gate);
+  const c10::cuda::CUDAGuard g(out.device());
+  guarded([&] {
+    b200::gdn::run_sigmoid_gate(out.data_ptr(), out.stride(0), gate.data_ptr(), gate.stride(0),
+                                out.size(0), out.size(1), stream_of(out));
+  });
+}
+
 // ------------------------------------------------------------------------------------- MoE
 void gemm_grouped_bf16(const Tensor& A, const Tensor& B, Tensor& C, const Tensor& tile_expert,
                        const Tensor& num_tiles, int64_t num_experts, int64_t mode, int64_t bn) {
@@ -614,6 +675,13 @@ TORCH_LIBRARY(b200, m) {
       "Tensor(c!) offsets, Tensor(d!) pos, Tensor(e!) num_tiles) -> ()");
   m.def("moe_gather(Tensor x, Tensor sorted_ids, Tensor num_tiles, int k, Tensor(a!) out) -> ()");
   m.def("moe_combine(Tensor y, Tensor pos, Tensor w, Tensor? shared, Tensor(a!) out) -> ()");
+  m.def(
+      "causal_conv1d(Tensor x, Tensor w, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, "
+      "Tensor slots, Tensor(b!) out) -> ()");
+  m.def(
+      "gdn_recurrent(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
+      "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out) -> ()");
+  m.def("sigmoid_gate(Tensor(a!) out, Tensor gate) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(b200, CUDA, m) {
@@ -637,6 +705,9 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("moe_align", &moe_align);
   m.impl("moe_gather", &moe_gather);
   m.impl("moe_combine", &moe_combine);
+  m.impl("causal_conv1d", &causal_conv1d);
+  m.impl("gdn_recurrent", &gdn_recurrent);
+  m.impl("sigmoid_gate", &sigmoid_gate);
 }
 
 void register_runtime(pybind11::module_& m);  // csrc/runtime/bindings.cpp

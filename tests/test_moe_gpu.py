@@ -37,6 +37,30 @@ def test_grouped_topk(T, E, k, ng, tg):
     torch.testing.assert_close(w.cpu().sort(-1).values, rw.sort(-1).values, rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("E,N,K,tiles", [(8, 256, 128, 3), (4, 512, 256, 5), (16, 128, 512, 16)])
+def test_grouped_gemm(mode, E, N, K, tiles):
+    """Grouped GEMM alone: tile t (128 rows) multiplies expert tile_expert[t]'s weights."""
+    g = torch.Generator().manual_seed(E * N + K + mode)
+    max_rows = (tiles + 2) * 128  # trailing tiles beyond num_tiles are never written
+    A = (torch.randn(max_rows, K, generator=g) * 0.5).to(torch.bfloat16)
+    B = (torch.randn(E * N, K, generator=g) * 0.05).to(torch.bfloat16)
+    te = torch.randint(0, E, (max_rows // 128,), generator=g, dtype=torch.int32)
+    nt = torch.tensor([tiles], dtype=torch.int32)
+    width = N // 2 if mode == 1 else N
+    C = torch.zeros(max_rows, width, dtype=torch.bfloat16, device="cuda")
+    torch.ops.b200.gemm_grouped_bf16(A.cuda(), B.cuda(), C, te.cuda(), nt.cuda(), E, mode, 0)
+    torch.cuda.synchronize()
+    for t in range(tiles):
+        a = A[t * 128:(t + 1) * 128].float()
+        w = B[int(te[t]) * N:(int(te[t]) + 1) * N].float()
+        y = a @ w.t()
+        if mode == 1:  # interleaved groups of 8 gate rows then 8 up rows
+            y = y.view(128, N // 16, 2, 8)
+            y = (torch.nn.functional.silu(y[:, :, 0]) * y[:, :, 1]).reshape(128, N // 2)
+        torch.testing.assert_close(C[t * 128:(t + 1) * 128].float().cpu(), y, atol=3e-2, rtol=3e-2)
+
+
 @pytest.mark.parametrize("T,E,k,H,I", [(1, 8, 2, 256, 128), (7, 128, 8, 512, 256),
                                         (300, 128, 8, 256, 128), (64, 16, 4, 1024, 512)])
 def test_fused_moe(T, E, k, H, I):

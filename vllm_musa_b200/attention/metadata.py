@@ -28,6 +28,7 @@ class AttnMetadata:
     decode_splits: Optional[int] = None
     tile_scratch: Optional[torch.Tensor] = None
     sliding_window: int = 0
+    state_slots: Optional[torch.Tensor] = None  # int32 [R] recurrent-state slot per request
 
     @property
     def prefill_cu_q(self) -> torch.Tensor:

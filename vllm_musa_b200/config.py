@@ -160,6 +160,7 @@ class ModelConfig:
             linear_value_head_dim=hf.get("linear_value_head_dim", 0) or 0,
             linear_conv_kernel_dim=hf.get("linear_conv_kernel_dim", 4) or 4,
             partial_rotary_factor=hf.get("partial_rotary_factor", 1.0) or 1.0,
+            attn_output_gate=arch == "qwen3_next",
             eos_token_id=(hf.get("eos_token_id")[0] if isinstance(hf.get("eos_token_id"), list)
                           else hf.get("eos_token_id")),
             name=a,

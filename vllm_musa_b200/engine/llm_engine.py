@@ -115,7 +115,9 @@ class LLMEngine:
         sc.max_model_len = config.scheduler.max_model_len
         sc.max_blocks_per_seq = self.runner.max_blocks
         sc.chunked_prefill = config.scheduler.enable_chunked_prefill
-        sc.prefix_caching = config.cache.enable_prefix_caching
+        # recurrent-state (hybrid) models cannot resume from cached KV blocks alone
+        sc.prefix_caching = (config.cache.enable_prefix_caching
+                             and not hasattr(self.model, "allocate_state"))
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
         self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
         self.runner.capture_graphs()

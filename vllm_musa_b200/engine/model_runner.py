@@ -33,7 +33,8 @@ class StepBuffers:
               ("slot_mapping", "tok", _I32), ("cu_q", "req1", _I32), ("seq_lens", "req", _I32),
               ("block_tables", "bt", _I32), ("logits_idx", "req", _I32),
               ("temperature", "req", _F32), ("top_k", "req", _I32), ("top_p", "req", _F32),
-              ("min_p", "req", _F32), ("seeds", "req", _I64), ("steps", "req", _I32)]
+              ("min_p", "req", _F32), ("seeds", "req", _I64), ("steps", "req", _I32),
+              ("state_slots", "req", _I32)]
 
     def __init__(self, max_tokens: int, max_reqs: int, max_blocks: int, device: torch.device):
         self.max_tokens, self.max_reqs, self.max_blocks = max_tokens, max_reqs, max_blocks
@@ -72,6 +73,7 @@ class StepBuffers:
             cp(name, n_tok)
         cp("cu_q", n_req + 1)
         cp("seq_lens", n_req)
+        cp("state_slots", n_req)
         cp("block_tables", n_req * self.max_blocks)
         cp("logits_idx", n_sample)
         if sampling:
@@ -104,6 +106,11 @@ class ModelRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.gen = torch.Generator(device="cpu").manual_seed(cfg.seed) if device.type == "cpu" else None
+        # recurrent-state slot written by padded CUDA-graph rows (one spare slot past the
+        # scheduler's range, so padding never touches a live request's state)
+        self.dummy_state_slot = sc.max_num_seqs
+        if hasattr(model, "allocate_state"):
+            model.allocate_state(sc.max_num_seqs + 1)
         self.record_logits = False  # debugging / tests: keep every step's logits (eager only)
         self.logits_log: list = []
 
@@ -141,9 +148,11 @@ class ModelRunner:
         b.d["seq_lens"][R - 1] = T - per * (R - 1)
         b.bt2d()[:R].zero_()
         b.d["logits_idx"][:R].copy_(b.d["cu_q"][1:R + 1] - 1)
+        b.d["state_slots"][:R].copy_(torch.arange(R, dtype=_I32, device=self.device))
         meta = AttnMetadata(T, 0, R, b.d["positions"][:T], b.d["slot_mapping"][:T],
                             b.d["seq_lens"][:R], b.bt2d()[:R], b.d["cu_q"][:R + 1],
-                            max_seq_len=T, tile_scratch=self.tile_scratch)
+                            max_seq_len=T, tile_scratch=self.tile_scratch,
+                            state_slots=b.d["state_slots"][:R])
         self.kv_caches = tmp
         self._forward_sample(T, R, R, meta, sampling=False, any_filter=False)
         torch.cuda.synchronize()
@@ -192,7 +201,7 @@ class ModelRunner:
         return AttnMetadata(T, nd, npf, b.d["positions"][:T], b.d["slot_mapping"][:T],
                             b.d["seq_lens"][:R], b.bt2d()[:R], b.d["cu_q"][:R + 1],
                             max_seq_len=max_seq_len, decode_splits=decode_splits,
-                            tile_scratch=self.tile_scratch)
+                            tile_scratch=self.tile_scratch, state_slots=b.d["state_slots"][:R])
 
     # ------------------------------------------------------------------ CUDA graphs
     def graph_sizes(self) -> list:
@@ -218,6 +227,7 @@ class ModelRunner:
         b.d["top_k"][:B].zero_()
         b.d["top_p"][:B].fill_(1.0)
         b.d["min_p"][:B].zero_()
+        b.d["state_slots"][:B].fill_(self.dummy_state_slot)
 
     def reserve_workspaces(self) -> None:
         """Size the split-K GEMM and split-KV workspaces for every shape the runner can see."""
@@ -305,6 +315,8 @@ class ModelRunner:
                 h["top_k"][S:B] = 0
                 h["top_p"][S:B] = 1.0
                 h["min_p"][S:B] = 0
+                h["cu_q"][R + 1:B + 1] = torch.arange(R + 1, B + 1, dtype=_I32)
+                h["state_slots"][R:B] = self.dummy_state_slot
             self.h2d_bytes += b.upload(B, B, B, True)
             g, out = self.graphs[B]
             g.replay()

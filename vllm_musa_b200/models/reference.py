@@ -79,3 +79,109 @@ class ReferenceDecoder:
             step_logits.append(lg)
             toks.append(int(lg.argmax()))
         return toks[len(prompt):], step_logits
+
+
+class HybridReferenceDecoder(ReferenceDecoder):
+    """Whole-sequence fp32 reference of the Qwen3-Next hybrid decoder from HF-named weights.
+
+    Layer i is full attention when (i + 1) % full_attention_interval == 0, else a Gated
+    DeltaNet layer; every layer ends in a routed MoE with a sigmoid-gated shared expert.  All
+    RMSNorm weights except the gated output norm are stored zero-centred, y = norm(x) * (1 + w).
+    Weight layouts follow the HF checkpoint: ``in_proj_qkvz`` rows grouped per key head as
+    [q | k | v (rep heads) | z (rep heads)], ``in_proj_ba`` per key head as [b (rep) | a (rep)],
+    ``q_proj`` per attention head as [q | gate].  The delta rule runs token by token.
+    """
+
+    def _rms1(self, x, w):
+        return self._rms(x, 1.0 + w)
+
+    def _moe(self, p, x):
+        cfg, w = self.cfg, self.w
+        probs = torch.softmax(x @ w[p + "mlp.gate.weight"].t(), -1)
+        top_w, top_i = probs.topk(cfg.num_experts_per_tok, -1)
+        if cfg.norm_topk_prob:
+            top_w = top_w / top_w.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for t in range(x.shape[0]):
+            for j in range(top_i.shape[1]):
+                q = f"{p}mlp.experts.{int(top_i[t, j])}."
+                h = F.silu(x[t] @ w[q + "gate_proj.weight"].t()) * (x[t] @ w[q + "up_proj.weight"].t())
+                out[t] += top_w[t, j] * (h @ w[q + "down_proj.weight"].t())
+        if cfg.shared_expert_intermediate_size:
+            q = p + "mlp.shared_expert."
+            s = (F.silu(x @ w[q + "gate_proj.weight"].t()) * (x @ w[q + "up_proj.weight"].t())) @ \
+                w[q + "down_proj.weight"].t()
+            out = out + torch.sigmoid(x @ w[p + "mlp.shared_expert_gate.weight"].t()) * s
+        return out
+
+    def _gated_attention(self, p, x, pos, mask):
+        cfg, w, D = self.cfg, self.w, self.D
+        S = x.shape[0]
+        qg = (x @ w[p + "self_attn.q_proj.weight"].t()).view(S, cfg.num_heads, 2 * D)
+        q, gate = qg[..., :D], qg[..., D:].reshape(S, -1)
+        k = (x @ w[p + "self_attn.k_proj.weight"].t()).view(S, cfg.num_kv_heads, D)
+        v = (x @ w[p + "self_attn.v_proj.weight"].t()).view(S, cfg.num_kv_heads, D)
+        q = self._rope(self._rms1(q, w[p + "self_attn.q_norm.weight"]), pos)
+        k = self._rope(self._rms1(k, w[p + "self_attn.k_norm.weight"]), pos)
+        G = cfg.num_heads // cfg.num_kv_heads
+        k, v = k.repeat_interleave(G, 1), v.repeat_interleave(G, 1)
+        s = torch.einsum("qhd,khd->hqk", q, k) / D ** 0.5
+        s = s.masked_fill(mask[None], float("-inf"))
+        a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(S, -1)
+        return (a * torch.sigmoid(gate)) @ w[p + "self_attn.o_proj.weight"].t()
+
+    def _gated_deltanet(self, p, x):
+        cfg, w = self.cfg, self.w
+        S = x.shape[0]
+        Hk, Hv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        dk, dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        rep = Hv // Hk
+        qkvz = (x @ w[p + "linear_attn.in_proj_qkvz.weight"].t()).view(S, Hk, 2 * dk + 2 * rep * dv)
+        q = qkvz[..., :dk].reshape(S, Hk * dk)
+        k = qkvz[..., dk:2 * dk].reshape(S, Hk * dk)
+        v = qkvz[..., 2 * dk:2 * dk + rep * dv].reshape(S, Hv * dv)
+        z = qkvz[..., 2 * dk + rep * dv:].reshape(S, Hv, dv)
+        ba = (x @ w[p + "linear_attn.in_proj_ba.weight"].t()).view(S, Hk, 2 * rep)
+        b, a = ba[..., :rep].reshape(S, Hv), ba[..., rep:].reshape(S, Hv)
+        mixed = torch.cat([q, k, v], -1)  # [S, C]
+        cw = w[p + "linear_attn.conv1d.weight"]  # [C, 1, K]
+        Kc = cw.shape[-1]
+        y = F.conv1d(F.pad(mixed.t().unsqueeze(0), (Kc - 1, 0)), cw, groups=cw.shape[0])[0]
+        mixed = F.silu(y).t()
+        q = mixed[:, :Hk * dk].view(S, Hk, dk).repeat_interleave(rep, 1)
+        k = mixed[:, Hk * dk:2 * Hk * dk].view(S, Hk, dk).repeat_interleave(rep, 1)
+        v = mixed[:, 2 * Hk * dk:].view(S, Hv, dv)
+        q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) * dk ** -0.5
+        k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+        beta = torch.sigmoid(b)
+        g = -torch.exp(w[p + "linear_attn.A_log"]) * F.softplus(a + w[p + "linear_attn.dt_bias"])
+        state = torch.zeros(Hv, dk, dv)
+        o = torch.empty(S, Hv, dv)
+        for t in range(S):
+            state = state * torch.exp(g[t]).view(Hv, 1, 1)
+            mem = (state * k[t].unsqueeze(-1)).sum(-2)
+            delta = (v[t] - mem) * beta[t].unsqueeze(-1)
+            state = state + k[t].unsqueeze(-1) * delta.unsqueeze(-2)
+            o[t] = (state * q[t].unsqueeze(-1)).sum(-2)
+        o = self._rms(o, w[p + "linear_attn.norm.weight"]) * F.silu(z)
+        return o.reshape(S, -1) @ w[p + "linear_attn.out_proj.weight"].t()
+
+    @torch.no_grad()
+    def logits(self, tokens: List[int]) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        S = len(tokens)
+        pos = torch.arange(S)
+        mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
+        h = w["model.embed_tokens.weight"][torch.tensor(tokens)]
+        interval = cfg.full_attention_interval or 4
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            x = self._rms1(h, w[p + "input_layernorm.weight"])
+            if (i + 1) % interval == 0:
+                h = h + self._gated_attention(p, x, pos, mask)
+            else:
+                h = h + self._gated_deltanet(p, x)
+            h = h + self._moe(p, self._rms1(h, w[p + "post_attention_layernorm.weight"]))
+        h = self._rms1(h, w["model.norm.weight"])
+        head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
+        return h @ head.t()

@@ -32,8 +32,7 @@ def _populate():
     from .llama import DenseDecoderForCausalLM
     _REGISTRY["llama"] = DenseDecoderForCausalLM
     _REGISTRY["qwen3"] = DenseDecoderForCausalLM
-    try:
-        from .qwen3_moe import Qwen3MoeForCausalLM
-        _REGISTRY["qwen3_moe"] = Qwen3MoeForCausalLM
-    except ImportError:  # pragma: no cover - optional while families are added
-        pass
+    from .qwen3_moe import Qwen3MoeForCausalLM
+    from .qwen3_next import Qwen3NextForCausalLM
+    _REGISTRY["qwen3_moe"] = Qwen3MoeForCausalLM
+    _REGISTRY["qwen3_next"] = Qwen3NextForCausalLM

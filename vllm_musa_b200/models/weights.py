@@ -36,17 +36,33 @@ def hf_param_shapes(cfg: ModelConfig) -> list:
     out = [("model.embed_tokens.weight", (V, H), "w")]
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
-        out += [
-            (p + "input_layernorm.weight", (H,), "norm"),
-            (p + "self_attn.q_proj.weight", (cfg.num_heads * D, H), "w"),
-            (p + "self_attn.k_proj.weight", (cfg.num_kv_heads * D, H), "w"),
-            (p + "self_attn.v_proj.weight", (cfg.num_kv_heads * D, H), "w"),
-            (p + "self_attn.o_proj.weight", (H, cfg.num_heads * D), "w"),
-        ]
-        if cfg.qk_norm:
-            out += [(p + "self_attn.q_norm.weight", (D,), "norm"),
-                    (p + "self_attn.k_norm.weight", (D,), "norm")]
-        out.append((p + "post_attention_layernorm.weight", (H,), "norm"))
+        hybrid = cfg.arch == "qwen3_next"
+        norm = "norm0" if hybrid else "norm"  # Qwen3-Next stores (1 + w) norms as w
+        out.append((p + "input_layernorm.weight", (H,), norm))
+        if hybrid and (i + 1) % (cfg.full_attention_interval or 4):
+            Hk, Hv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+            dk, dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+            conv_dim = 2 * Hk * dk + Hv * dv
+            q = p + "linear_attn."
+            out += [(q + "in_proj_qkvz.weight", (2 * Hk * dk + 2 * Hv * dv, H), "w"),
+                    (q + "in_proj_ba.weight", (2 * Hv, H), "w"),
+                    (q + "conv1d.weight", (conv_dim, 1, cfg.linear_conv_kernel_dim), "conv"),
+                    (q + "dt_bias", (Hv,), "norm"),
+                    (q + "A_log", (Hv,), "a_log"),
+                    (q + "norm.weight", (dv,), "norm"),
+                    (q + "out_proj.weight", (H, Hv * dv), "w")]
+        else:
+            qrows = cfg.num_heads * D * (2 if cfg.attn_output_gate else 1)
+            out += [
+                (p + "self_attn.q_proj.weight", (qrows, H), "w"),
+                (p + "self_attn.k_proj.weight", (cfg.num_kv_heads * D, H), "w"),
+                (p + "self_attn.v_proj.weight", (cfg.num_kv_heads * D, H), "w"),
+                (p + "self_attn.o_proj.weight", (H, cfg.num_heads * D), "w"),
+            ]
+            if cfg.qk_norm:
+                out += [(p + "self_attn.q_norm.weight", (D,), norm),
+                        (p + "self_attn.k_norm.weight", (D,), norm)]
+        out.append((p + "post_attention_layernorm.weight", (H,), norm))
         if cfg.is_moe:
             E, I = cfg.num_experts, cfg.moe_intermediate_size
             out.append((p + "mlp.gate.weight", (E, H), "w"))
@@ -64,7 +80,7 @@ def hf_param_shapes(cfg: ModelConfig) -> list:
             I = cfg.intermediate_size
             out += [(p + "mlp.gate_proj.weight", (I, H), "w"), (p + "mlp.up_proj.weight", (I, H), "w"),
                     (p + "mlp.down_proj.weight", (H, I), "w")]
-    out.append(("model.norm.weight", (H,), "norm"))
+    out.append(("model.norm.weight", (H,), "norm0" if cfg.arch == "qwen3_next" else "norm"))
     if not cfg.tie_word_embeddings:
         out.append(("lm_head.weight", (V, H), "w"))
     return out
@@ -80,6 +96,14 @@ def dummy_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02, device: st
     for name, shape, kind in (shapes or hf_param_shapes(cfg)):
         if kind == "norm":
             yield name, torch.ones(shape, dtype=dtype, device=device)
+        elif kind == "norm0":
+            yield name, torch.zeros(shape, dtype=dtype, device=device)
+        elif kind == "a_log":  # decay rates A = 1..16 (log-spaced), as HF initialises them
+            yield name, torch.log(torch.linspace(1.0, 16.0, shape[0])).to(dtype).to(device)
+        elif kind == "conv":
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            t.normal_(0.0, 0.3, generator=gen)
+            yield name, t.to(dtype)
         else:
             t = torch.empty(shape, dtype=torch.float32, device=device)
             t.normal_(0.0, std, generator=gen)

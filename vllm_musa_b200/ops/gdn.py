@@ -1,0 +1,89 @@
+"""Gated DeltaNet ops (Qwen3-Next linear attention): causal conv1d with per-request state,
+the gated delta-rule recurrence with per-request state, and the sigmoid output gate.
+
+CUDA: csrc/scan/gdn.cu.  CPU: the same math in PyTorch (token loop), which is also the
+numerics oracle of the GPU tests.  States: conv [slots, C, 3] (last three inputs), recurrent
+[slots, Hv, dv, dk] fp32 (value-major).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import _ext
+
+
+def causal_conv1d(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, cu_q: torch.Tensor,
+                  seq_lens: torch.Tensor, slots: torch.Tensor,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, >= C] (first C channels used); w [C, 4]; updates ``state`` in place."""
+    C = w.shape[0]
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty(T, C, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    if x.is_cuda:
+        _ext.ops().causal_conv1d(x, w, state, cu_q, seq_lens, slots, out)
+        return out
+    cu = cu_q.tolist()
+    for r in range(len(cu) - 1):
+        a, b = cu[r], cu[r + 1]
+        L = b - a
+        slot = int(slots[r])
+        hist = state[slot].float() if int(seq_lens[r]) - L > 0 else torch.zeros(C, 3)
+        xs = torch.cat([hist, x[a:b, :C].float().t()], dim=1)  # [C, 3 + L]
+        y = F.conv1d(xs.unsqueeze(0), w.float().unsqueeze(1), groups=C)[0]  # [C, L]
+        out[a:b] = F.silu(y).t().to(out.dtype)
+        state[slot] = xs[:, -3:].to(state.dtype)
+    return out
+
+
+def gdn_recurrent(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
+                  state: torch.Tensor, cu_q: torch.Tensor, seq_lens: torch.Tensor,
+                  slots: torch.Tensor, Hk: int, Hv: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gated delta rule over each request's new tokens.  qkv [T, 2*Hk*128 + Hv*128] (conv
+    output: q | k | v), ba [T, 2*Hv] (b | a); state [slots, Hv, 128, 128] updated in place."""
+    T = qkv.shape[0]
+    D = 128
+    if out is None:
+        out = torch.empty(T, Hv * D, dtype=qkv.dtype, device=qkv.device)
+    if T == 0:
+        return out
+    if qkv.is_cuda:
+        _ext.ops().gdn_recurrent(qkv, ba, A_log, dt_bias, state, cu_q, seq_lens, slots, Hk, Hv,
+                                 out)
+        return out
+    rep = Hv // Hk
+    cu = cu_q.tolist()
+    for r in range(len(cu) - 1):
+        a, b = cu[r], cu[r + 1]
+        L = b - a
+        slot = int(slots[r])
+        S = state[slot].float().clone() if int(seq_lens[r]) - L > 0 else torch.zeros(Hv, D, D)
+        q = qkv[a:b, :Hk * D].float().view(L, Hk, D).repeat_interleave(rep, 1)
+        k = qkv[a:b, Hk * D:2 * Hk * D].float().view(L, Hk, D).repeat_interleave(rep, 1)
+        v = qkv[a:b, 2 * Hk * D:2 * Hk * D + Hv * D].float().view(L, Hv, D)
+        q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) / D ** 0.5
+        k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+        bb = torch.sigmoid(ba[a:b, :Hv].float())
+        g = -torch.exp(A_log.float()) * F.softplus(ba[a:b, Hv:2 * Hv].float() + dt_bias.float())
+        for t in range(L):
+            S = S * torch.exp(g[t]).view(Hv, 1, 1)               # S[h, v, k]
+            kv = torch.einsum("hvk,hk->hv", S, k[t])
+            u = (v[t] - kv) * bb[t].view(Hv, 1)
+            S = S + u.unsqueeze(-1) * k[t].unsqueeze(1)
+            out[a + t] = torch.einsum("hvk,hk->hv", S, q[t]).reshape(-1).to(out.dtype)
+        state[slot] = S.to(state.dtype)
+    return out
+
+
+def sigmoid_gate(out: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """out *= sigmoid(gate) in place (both [T, W], rows may be strided)."""
+    if out.is_cuda:
+        if out.shape[0]:
+            _ext.ops().sigmoid_gate(out, gate)
+        return out
+    out.copy_((out.float() * torch.sigmoid(gate.float())).to(out.dtype))
+    return out

@@ -44,8 +44,8 @@ def rms_norm_gated(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, group
                    eps: float) -> torch.Tensor:
     """RMSNorm over groups of ``group`` channels, times weight, times silu(z) (GDN output)."""
     if x.is_cuda:
-        out = torch.empty_like(x)
-        _ext.ops().rms_norm_gated(out, x.contiguous(), z.contiguous(), weight, group, eps)
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        _ext.ops().rms_norm_gated(out, x, z, weight, group, eps)
         return out
     shp = x.shape
     xf = x.float().reshape(-1, group)
