@@ -70,19 +70,20 @@ void run_sigmoid_gate(void* out, int64_t ldo, const void* gate, int64_t ldg, int
 
 // ------------------------------------------------------------------------------- MoE
 namespace moe {
-void run_topk_softmax(const float* logits, int T, int E, int k, bool renorm, int32_t* ids,
-                      float* w, cudaStream_t s);
+void run_topk_softmax(const float* logits, int64_t ld, int T, int E, int k, bool renorm,
+                      int32_t* ids, float* w, cudaStream_t s);
 void run_grouped_topk(const float* logits, const float* bias, int T, int E, int k, int n_group,
                       int topk_group, bool sigmoid, bool renorm, float scale, int32_t* ids,
                       float* w, cudaStream_t s);
 int align_max_rows(int n, int E);
-void run_moe_align(const int32_t* ids, int n, int E, int max_rows, int32_t* sorted_ids,
+void run_moe_align(const int32_t* ids, int n, int E, int e0, int max_rows, int32_t* sorted_ids,
                    int32_t* tile_expert, int32_t* offsets, int32_t* pos, int32_t* num_tiles,
                    cudaStream_t s);
 void run_moe_gather(const void* x, int64_t ldx, const int32_t* sorted_ids, const int32_t* num_tiles,
                     int max_rows, int k, int H, void* out, cudaStream_t s);
 void run_moe_combine(const void* y, const int32_t* pos, const float* w, int T, int k, int H,
-                     const void* shared, void* out, int64_t ldo, cudaStream_t s);
+                     const void* shared, const float* shared_gate, int64_t ld_gate, void* out,
+                     int64_t ldo, cudaStream_t s);
 }  // namespace moe
 
 // ------------------------------------------------------------------------------- norms

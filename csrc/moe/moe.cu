@@ -29,8 +29,8 @@ constexpr int kTile = 128;
 
 // ------------------------------------------------------------------------------ top-k softmax
 template <int EPL>  // experts per lane
-__global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int k,
-                                    bool renorm, int32_t* __restrict__ ids,
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int64_t ld, int T, int E,
+                                    int k, bool renorm, int32_t* __restrict__ ids,
                                     float* __restrict__ w) {
   const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (t >= T) return;
@@ -40,7 +40,7 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int
 #pragma unroll
   for (int i = 0; i < EPL; ++i) {
     const int e = lane * EPL + i;
-    v[i] = e < E ? logits[(size_t)t * E + e] : -INFINITY;
+    v[i] = e < E ? logits[(size_t)t * ld + e] : -INFINITY;
     mx = fmaxf(mx, v[i]);
   }
   mx = warp_max(mx);
@@ -224,7 +224,7 @@ __global__ void grouped_topk_kernel(const float* __restrict__ logits,
 // ------------------------------------------------------------------------------ align / sort
 // Single CTA of 1024 threads: histogram, padded exclusive scan, stable placement.
 __global__ void __launch_bounds__(1024)
-    moe_align_kernel(const int32_t* __restrict__ ids, int n, int E, int max_rows,
+    moe_align_kernel(const int32_t* __restrict__ ids, int n, int E, int e0, int max_rows,
                      int32_t* __restrict__ sorted_ids, int32_t* __restrict__ tile_expert,
                      int32_t* __restrict__ offsets, int32_t* __restrict__ pos,
                      int32_t* __restrict__ num_tiles) {
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(1024)
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i];
+    const int e = ids[i] - e0;  // local expert index (expert parallelism)
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(1024)
   // placement: the slot inside an expert's segment is taken with an atomic; rows are
   // computed independently, so the order inside a segment does not change any result.
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int e = ids[i];
+    const int e = ids[i] - e0;
     if (e >= 0 && e < E) {
       const int p = start[e] + atomicAdd(&cursor[e], 1);
       sorted_ids[p] = i;
@@ -294,12 +294,17 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ pos,
                                    const float* __restrict__ w, int T, int k, int H,
                                    const __nv_bfloat16* __restrict__ shared,
+                                   const float* __restrict__ shared_gate, int64_t ld_gate,
                                    __nv_bfloat16* __restrict__ out, int64_t ldo) {
   const int t = blockIdx.x;
+  // sigmoid-gated shared expert (Qwen2/3-MoE style): the gate logit rides in the router GEMM
+  const float sg = shared_gate ? 1.f / (1.f + __expf(-shared_gate[(size_t)t * ld_gate])) : 1.f;
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
     float acc[8];
     if (shared) {
       unpack8(reinterpret_cast<const uint4*>(shared + (size_t)t * H)[c], acc);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] *= sg;
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -318,13 +323,14 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
 }
 
 // ------------------------------------------------------------------------------ launchers
-void run_topk_softmax(const float* logits, int T, int E, int k, bool renorm, int32_t* ids,
-                      float* w, cudaStream_t s) {
+void run_topk_softmax(const float* logits, int64_t ld, int T, int E, int k, bool renorm,
+                      int32_t* ids, float* w, cudaStream_t s) {
   B200_REQUIRE(E <= 512 && k <= 32 && k <= E, "topk_softmax: E <= 512, k <= 32");
   if (T == 0) return;
   const int warps = 8, blocks = (T + warps - 1) / warps;
   const int epl = (E + 31) / 32;
-#define B200_TK(N) topk_softmax_kernel<N><<<blocks, warps * 32, 0, s>>>(logits, T, E, k, renorm, ids, w)
+#define B200_TK(N) \
+  topk_softmax_kernel<N><<<blocks, warps * 32, 0, s>>>(logits, ld, T, E, k, renorm, ids, w)
   if (epl <= 2) B200_TK(2);
   else if (epl <= 4) B200_TK(4);
   else if (epl <= 8) B200_TK(8);
@@ -356,12 +362,12 @@ void run_grouped_topk(const float* logits, const float* bias, int T, int E, int 
 
 int align_max_rows(int n, int E) { return ((n + E * (kTile - 1)) + kTile - 1) / kTile * kTile; }
 
-void run_moe_align(const int32_t* ids, int n, int E, int max_rows, int32_t* sorted_ids,
+void run_moe_align(const int32_t* ids, int n, int E, int e0, int max_rows, int32_t* sorted_ids,
                    int32_t* tile_expert, int32_t* offsets, int32_t* pos, int32_t* num_tiles,
                    cudaStream_t s) {
   B200_REQUIRE(max_rows >= align_max_rows(n, E), "moe_align: max_rows too small");
   const int smem = (3 * E + 1) * sizeof(int32_t);
-  moe_align_kernel<<<1, 1024, smem, s>>>(ids, n, E, max_rows, sorted_ids, tile_expert, offsets,
+  moe_align_kernel<<<1, 1024, smem, s>>>(ids, n, E, e0, max_rows, sorted_ids, tile_expert, offsets,
                                          pos, num_tiles);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
@@ -379,11 +385,13 @@ void run_moe_gather(const void* x, int64_t ldx, const int32_t* sorted_ids, const
 }
 
 void run_moe_combine(const void* y, const int32_t* pos, const float* w, int T, int k, int H,
-                     const void* shared, void* out, int64_t ldo, cudaStream_t s) {
+                     const void* shared, const float* shared_gate, int64_t ld_gate, void* out,
+                     int64_t ldo, cudaStream_t s) {
   B200_REQUIRE(H % 8 == 0, "moe_combine: H % 8");
   if (T == 0) return;
   moe_combine_kernel<<<T, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(y), pos, w, T, k, H,
                                        reinterpret_cast<const __nv_bfloat16*>(shared),
+                                       shared_gate, ld_gate,
                                        reinterpret_cast<__nv_bfloat16*>(out), ldo);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();

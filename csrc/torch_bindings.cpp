@@ -528,13 +528,13 @@ void gemm_grouped_bf16(const Tensor& A, const Tensor& B, Tensor& C, const Tensor
 
 void topk_softmax(const Tensor& logits, Tensor& ids, Tensor& w, bool renorm) {
   CHECK_CUDA(logits);
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "router logits fp32");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "router logits fp32");
   TORCH_CHECK(ids.scalar_type() == at::kInt && w.scalar_type() == at::kFloat, "ids/w dtypes");
   const c10::cuda::CUDAGuard g(logits.device());
   guarded([&] {
-    b200::moe::run_topk_softmax(logits.data_ptr<float>(), logits.size(0), logits.size(1),
-                                ids.size(1), renorm, ids.data_ptr<int32_t>(), w.data_ptr<float>(),
-                                stream_of(logits));
+    b200::moe::run_topk_softmax(logits.data_ptr<float>(), logits.stride(0), logits.size(0),
+                                logits.size(1), ids.size(1), renorm, ids.data_ptr<int32_t>(),
+                                w.data_ptr<float>(), stream_of(logits));
   });
 }
 
@@ -553,12 +553,13 @@ void grouped_topk(const Tensor& logits, const c10::optional<Tensor>& bias, Tenso
 }
 
 void moe_align(const Tensor& ids, int64_t E, Tensor& sorted_ids, Tensor& tile_expert,
-               Tensor& offsets, Tensor& pos, Tensor& num_tiles) {
+               Tensor& offsets, Tensor& pos, Tensor& num_tiles, int64_t expert_offset) {
   CHECK_CUDA(ids);
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "moe_align: int32 ids");
   const c10::cuda::CUDAGuard g(ids.device());
   guarded([&] {
-    b200::moe::run_moe_align(ids.data_ptr<int32_t>(), ids.numel(), E, sorted_ids.numel(),
+    b200::moe::run_moe_align(ids.data_ptr<int32_t>(), ids.numel(), E, expert_offset,
+                             sorted_ids.numel(),
                              sorted_ids.data_ptr<int32_t>(), tile_expert.data_ptr<int32_t>(),
                              offsets.data_ptr<int32_t>(), pos.data_ptr<int32_t>(),
                              num_tiles.data_ptr<int32_t>(), stream_of(ids));
@@ -578,16 +579,23 @@ void moe_gather(const Tensor& x, const Tensor& sorted_ids, const Tensor& num_til
 }
 
 void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w,
-                 const c10::optional<Tensor>& shared, Tensor& out) {
+                 const c10::optional<Tensor>& shared, Tensor& out,
+                 const c10::optional<Tensor>& shared_gate) {
   CHECK_CUDA(y);
   TORCH_CHECK(y.is_contiguous() && pos.is_contiguous() && w.is_contiguous(), "moe_combine");
   CHECK_ROWMAJOR(out);
+  if (shared.has_value()) TORCH_CHECK(shared->is_contiguous(), "moe_combine: shared contiguous");
+  if (shared_gate.has_value())
+    TORCH_CHECK(shared_gate->scalar_type() == at::kFloat && shared.has_value(),
+                "moe_combine: fp32 shared gate needs a shared output");
   const c10::cuda::CUDAGuard g(y.device());
   guarded([&] {
     b200::moe::run_moe_combine(y.data_ptr(), pos.data_ptr<int32_t>(), w.data_ptr<float>(),
                                pos.size(0), pos.size(1), y.size(1),
-                               shared.has_value() ? shared->data_ptr() : nullptr, out.data_ptr(),
-                               out.stride(0), stream_of(y));
+                               shared.has_value() ? shared->data_ptr() : nullptr,
+                               shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
+                               shared_gate.has_value() ? shared_gate->stride(0) : 0,
+                               out.data_ptr(), out.stride(0), stream_of(y));
   });
 }
 
@@ -672,9 +680,10 @@ TORCH_LIBRARY(b200, m) {
       "int topk_group, bool sigmoid, bool renorm, float scale) -> ()");
   m.def(
       "moe_align(Tensor ids, int num_experts, Tensor(a!) sorted_ids, Tensor(b!) tile_expert, "
-      "Tensor(c!) offsets, Tensor(d!) pos, Tensor(e!) num_tiles) -> ()");
+      "Tensor(c!) offsets, Tensor(d!) pos, Tensor(e!) num_tiles, int expert_offset=0) -> ()");
   m.def("moe_gather(Tensor x, Tensor sorted_ids, Tensor num_tiles, int k, Tensor(a!) out) -> ()");
-  m.def("moe_combine(Tensor y, Tensor pos, Tensor w, Tensor? shared, Tensor(a!) out) -> ()");
+  m.def("moe_combine(Tensor y, Tensor pos, Tensor w, Tensor? shared, Tensor(a!) out, "
+      "Tensor? shared_gate=None) -> ()");
   m.def(
       "causal_conv1d(Tensor x, Tensor w, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, "
       "Tensor slots, Tensor(b!) out) -> ()");

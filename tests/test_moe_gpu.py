@@ -72,9 +72,13 @@ def test_fused_moe(T, E, k, H, I):
     w_dn = (torch.randn(E * H, I, generator=g) * 0.05).to(torch.bfloat16)
     ids, w = moe_ops.topk_softmax(torch.randn(T, E, generator=g), k)
     shared = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
-    ref = moe_ops.fused_moe(x, w_gu, w_dn, ids, w, E, shared)
+    # router-GEMM-shaped logits whose column E is the shared expert's gate
+    logits = torch.randn(T, E + 8, generator=g)
+    gate = logits[:, E:E + 1] if T % 2 else None
+    ref = moe_ops.fused_moe(x, w_gu, w_dn, ids, w, E, shared, shared_gate=gate)
+    lg = logits.cuda()
     out = moe_ops.fused_moe(x.cuda(), w_gu.cuda(), w_dn.cuda(), ids.cuda(), w.cuda(), E,
-                            shared.cuda())
+                            shared.cuda(), shared_gate=lg[:, E:E + 1] if T % 2 else None)
     torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=3e-2, atol=3e-2)
 
 
@@ -85,7 +89,7 @@ def test_tiny_moe_engine_graph_vs_eager():
                       num_heads=8, num_kv_heads=2, head_dim=64, intermediate_size=1024,
                       rms_norm_eps=1e-6, rope_theta=1e4, max_position=1024, qk_norm=True,
                       num_experts=32, num_experts_per_tok=4, moe_intermediate_size=256,
-                      name="tiny-moe-gpu")
+                      shared_expert_intermediate_size=256, name="tiny-moe-gpu")
     g = torch.Generator().manual_seed(4)
     prompts = [torch.randint(0, 2048, (n,), generator=g).tolist() for n in (5, 77, 200)]
     sp = SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True)

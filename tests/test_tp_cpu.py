@@ -16,28 +16,43 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, temperature):
+def _model(name):
+    if name == "tiny-llama":
+        from vllm_musa_b200.models.presets import tiny_llama
+        return tiny_llama()
+    if name == "tiny-moe":
+        from test_moe_cpu import tiny_moe
+        return tiny_moe(shared=64)
+    from test_qwen3_next_cpu import tiny_next
+    return tiny_next()
+
+
+def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     torch.set_num_threads(1)
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     from vllm_musa_b200 import LLM, SamplingParams
-    from vllm_musa_b200.models.presets import tiny_llama
     from vllm_musa_b200.parallel.state import destroy_distributed
-    llm = LLM(tiny_llama(), device="cpu", tensor_parallel_size=world, block_size=16, seed=0,
-              num_gpu_blocks=64, max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64)
+    cfg = _model(model)
+    llm = LLM(cfg, device="cpu", tensor_parallel_size=world, block_size=16, seed=0,
+              num_gpu_blocks=64, max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64,
+              enable_expert_parallel=ep)
     g = torch.Generator().manual_seed(0)
-    prompts = torch.randint(0, 1024, (3, 20), generator=g).tolist()
+    prompts = torch.randint(0, min(1024, cfg.vocab_size), (3, 20), generator=g).tolist()
     outs = llm.generate(prompts, SamplingParams(temperature=temperature, max_tokens=8,
                                                 ignore_eos=True, seed=7 if temperature else None))
     q.put((rank, [o.outputs[0].token_ids for o in outs]))
     destroy_distributed()
 
 
-def _run(world, temperature=0.0):
+def _run(world, temperature=0.0, model="tiny-llama", ep=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, temperature)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, temperature, model, ep))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(world))
@@ -50,6 +65,17 @@ def _run(world, temperature=0.0):
 def test_tp2_greedy_matches_tp1():
     one = _run(1)[0]
     two = _run(2)
+    assert two[0] == two[1], "ranks diverged"
+    assert two[0] == one
+
+
+@pytest.mark.parametrize("model,ep", [("tiny-moe", False), ("tiny-moe", True),
+                                      ("tiny-next", False), ("tiny-next", True)])
+def test_tp2_moe_and_hybrid_match_tp1(model, ep):
+    """TP=2 attention with tensor-sharded experts, or with expert parallelism (each rank keeps
+    half of the experts whole), reproduces the single-rank tokens."""
+    one = _run(1, model=model)[0]
+    two = _run(2, model=model, ep=ep)
     assert two[0] == two[1], "ranks diverged"
     assert two[0] == one
 

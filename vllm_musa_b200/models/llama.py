@@ -120,7 +120,7 @@ class DenseDecoderForCausalLM:
                 if not m:
                     continue
                 i, key = int(m.group(1)), m.group(2)
-                if i >= cfg.num_layers:
+                if i >= cfg.num_layers or not self._wanted(i, key):
                     continue
                 self._staging[i][key] = w
                 self._try_finalize(i)
@@ -130,6 +130,11 @@ class DenseDecoderForCausalLM:
                                f"present={self.embed is not None},{self.final_norm is not None},"
                                f"{self.lm_head is not None}")
         self._staging.clear()
+
+    def _wanted(self, i: int, key: str) -> bool:
+        """Whether this rank keeps layer ``i``'s tensor ``key`` (expert parallelism drops the
+        experts other ranks own before they are staged)."""
+        return True
 
     def _mlp_keys(self, i: int) -> list:
         return ["mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight"]

@@ -25,7 +25,19 @@ class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
             raise ValueError("moe_intermediate_size must be divisible by tensor_parallel_size")
         self.E = cfg.num_experts
         self.topk = cfg.num_experts_per_tok
-        self.I_e = cfg.moe_intermediate_size // self.tp
+        # Expert parallelism (attention stays tensor-parallel): rank r owns a contiguous slice
+        # of whole experts; the routed partial sums join the shared expert's TP partial sum in
+        # the fused all-reduce + residual + RMSNorm that follows the MoE block.
+        self.ep = self.pstate.ep_size > 1
+        if self.ep:
+            if cfg.num_experts % self.pstate.ep_size:
+                raise ValueError("num_experts must be divisible by the expert-parallel size")
+            self.E_local = cfg.num_experts // self.pstate.ep_size
+            self.e0 = self.pstate.ep_rank * self.E_local
+            self.I_e = cfg.moe_intermediate_size
+        else:
+            self.E_local, self.e0 = self.E, 0
+            self.I_e = cfg.moe_intermediate_size // self.tp
 
     def _is_moe(self, i: int) -> bool:
         return self.cfg.num_experts > 0 and i >= self.cfg.first_k_dense
@@ -34,7 +46,7 @@ class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
         if not self._is_moe(i):
             return super()._mlp_keys(i)
         keys = ["mlp.gate.weight"]
-        for e in range(self.cfg.num_experts):
+        for e in range(self.e0, self.e0 + self.E_local):
             keys += [f"mlp.experts.{e}.gate_proj.weight", f"mlp.experts.{e}.up_proj.weight",
                      f"mlp.experts.{e}.down_proj.weight"]
         if self.cfg.shared_expert_intermediate_size:
@@ -42,38 +54,52 @@ class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
                      "mlp.shared_expert.down_proj.weight", "mlp.shared_expert_gate.weight"]
         return keys
 
+    def _wanted(self, i, key):
+        if key.startswith("mlp.experts.") and self._is_moe(i):
+            e = int(key.split(".")[2])
+            return self.e0 <= e < self.e0 + self.E_local
+        return True
+
     def _finalize_mlp(self, i, L, st):
         if not self._is_moe(i):
             return super()._finalize_mlp(i, L, st)
         r, t = self.rank, self.tp
-        L.router_w = self._to(st["mlp.gate.weight"])
+        router = st["mlp.gate.weight"]
+        if "mlp.shared_expert_gate.weight" in st:
+            # the shared expert's gate logit rides in the router GEMM as row E (padded to a
+            # multiple of 8 rows); the combine kernel applies its sigmoid
+            sg = st["mlp.shared_expert_gate.weight"].reshape(1, -1)
+            router = torch.cat([router, sg, torch.zeros(7, sg.shape[1], dtype=sg.dtype)], 0)
+            L.shared_gate = True
+        L.router_w = self._to(router)
         gus, downs = [], []
-        for e in range(self.E):
-            g = shard_rows(st[f"mlp.experts.{e}.gate_proj.weight"], r, t)
-            u = shard_rows(st[f"mlp.experts.{e}.up_proj.weight"], r, t)
+        er, et = (0, 1) if self.ep else (r, t)  # EP keeps whole experts
+        for e in range(self.e0, self.e0 + self.E_local):
+            g = shard_rows(st[f"mlp.experts.{e}.gate_proj.weight"], er, et)
+            u = shard_rows(st[f"mlp.experts.{e}.up_proj.weight"], er, et)
             gus.append(ops.interleave_gate_up(g, u))
-            downs.append(shard_cols(st[f"mlp.experts.{e}.down_proj.weight"], r, t))
+            downs.append(shard_cols(st[f"mlp.experts.{e}.down_proj.weight"], er, et))
         L.experts_gu = self._to(torch.cat(gus, 0))      # [E * 2I, H]
         L.experts_down = self._to(torch.cat(downs, 0))  # [E * H, I]
         if self.cfg.shared_expert_intermediate_size:
             L.shared_gu, L.shared_down = self._dense_mlp_weights(
                 st["mlp.shared_expert.gate_proj.weight"], st["mlp.shared_expert.up_proj.weight"],
                 st["mlp.shared_expert.down_proj.weight"])
-            L.shared_gate = self._to(st["mlp.shared_expert_gate.weight"])
 
     def _mlp(self, i, L, x, T):
         if not self._is_moe(i):
             return super()._mlp(i, L, x, T)
         logits = ops.linear(x, L.router_w, out_dtype=torch.float32)
-        ids, w = moe_ops.topk_softmax(logits, self.topk, self.cfg.norm_topk_prob)
-        shared = None
+        E = self.E
+        ids, w = moe_ops.topk_softmax(logits[:, :E], self.topk, self.cfg.norm_topk_prob)
+        shared = gate = None
         if L.shared_gu is not None:
             shared = ops.linear(ops.linear_silu_mul(x, L.shared_gu), L.shared_down)
-            if L.shared_gate is not None:
-                gate = torch.sigmoid(ops.linear(x, L.shared_gate, out_dtype=torch.float32))
-                shared = (shared.float() * gate).to(shared.dtype)
-        return moe_ops.fused_moe(x, L.experts_gu, L.experts_down, ids, w, self.E, shared,
-                                 out=self.comm.out_buffer(T))
+            if L.shared_gate:
+                gate = logits[:, E:E + 1]
+        return moe_ops.fused_moe(x, L.experts_gu, L.experts_down, ids, w, self.E_local, shared,
+                                 out=self.comm.out_buffer(T), expert_offset=self.e0,
+                                 shared_gate=gate)
 
     def linear_shapes(self):
         return [s for s in super().linear_shapes()]

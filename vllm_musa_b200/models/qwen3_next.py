@@ -139,7 +139,8 @@ class Qwen3NextForCausalLM(Qwen3MoeForCausalLM):
                 self.final_norm = self._to(w.float() + 1.0)
             else:
                 m = _LAYER_RE.match(name)
-                if not m or int(m.group(1)) >= cfg.num_layers:
+                if not m or int(m.group(1)) >= cfg.num_layers or \
+                        not self._wanted(int(m.group(1)), m.group(2)):
                     continue
                 self._staging[int(m.group(1))][m.group(2)] = w
                 self._try_finalize(int(m.group(1)))

@@ -28,7 +28,9 @@ def topk_softmax(logits: torch.Tensor, k: int, renorm: bool = True):
         ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
         w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
         if T:
-            _ext.ops().topk_softmax(logits.float().contiguous(), ids, w, renorm)
+            lg = logits if logits.dtype == torch.float32 and logits.stride(1) == 1 else \
+                logits.float().contiguous()
+            _ext.ops().topk_softmax(lg, ids, w, renorm)
         return ids, w
     p = torch.softmax(logits.float(), -1)
     w, ids = torch.topk(p, k, dim=-1)
@@ -63,13 +65,14 @@ def grouped_topk(logits: torch.Tensor, k: int, n_group: int, topk_group: int,
     return ids.to(torch.int32), w * scale
 
 
-def _fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared):
+def _fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared, expert_offset=0,
+                   shared_gate=None):
     T, H = x.shape
     I2 = w_gu.shape[0] // num_experts
     out = torch.zeros(T, H, dtype=torch.float32)
     xf = x.float()
     for e in range(num_experts):
-        tok, slot = torch.nonzero(ids == e, as_tuple=True)
+        tok, slot = torch.nonzero(ids == e + expert_offset, as_tuple=True)
         if tok.numel() == 0:
             continue
         g, u = deinterleave_gate_up(w_gu[e * I2:(e + 1) * I2])
@@ -79,15 +82,23 @@ def _fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared):
         y = (h @ d.t()).to(x.dtype).float()
         out.index_add_(0, tok, y * w[tok, slot].unsqueeze(1).float())
     if shared is not None:
-        out += shared.float()
+        s = shared.float()
+        if shared_gate is not None:
+            s = s * torch.sigmoid(shared_gate.float().reshape(T, 1))
+        out += s
     return out.to(x.dtype)
 
 
 def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: torch.Tensor,
               w: torch.Tensor, num_experts: int, shared: Optional[torch.Tensor] = None,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, expert_offset: int = 0,
+              shared_gate: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x [T, H]; w_gu [E * 2I, H] (gate/up interleaved per expert); w_down [E * H, I];
-    ids/w [T, k] -> [T, H] = sum_j w[:, j] * expert_{ids[:, j]}(x) (+ shared)."""
+    ids/w [T, k] -> [T, H] = sum_j w[:, j] * expert_{ids[:, j]}(x) (+ shared).
+
+    With expert parallelism this rank holds experts [expert_offset, expert_offset + E); routed
+    slots naming other experts contribute nothing here (their owners add them).
+    ``shared_gate`` [T, 1] fp32 logits (any row stride) scale ``shared`` by their sigmoid."""
     T, H = x.shape
     k = ids.shape[1]
     if out is None:
@@ -95,7 +106,8 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
     if T == 0:
         return out
     if not x.is_cuda:
-        out.copy_(_fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared))
+        out.copy_(_fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared, expert_offset,
+                                 shared_gate))
         return out
     mod = _ext.require()
     E = num_experts
@@ -108,7 +120,8 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
     pos = torch.empty(T, k, dtype=torch.int32, device=dev)
     num_tiles = torch.empty(1, dtype=torch.int32, device=dev)
     ops = torch.ops.b200
-    ops.moe_align(ids.contiguous(), E, sorted_ids, tile_expert, offsets, pos, num_tiles)
+    ops.moe_align(ids.contiguous(), E, sorted_ids, tile_expert, offsets, pos, num_tiles,
+                  expert_offset)
     xs = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
     ops.moe_gather(x, sorted_ids, num_tiles, k, xs)
     I = w_gu.shape[0] // E // 2
@@ -116,5 +129,5 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
     ops.gemm_grouped_bf16(xs, w_gu, h, tile_expert, num_tiles, E, 1, 0)
     y = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
     ops.gemm_grouped_bf16(h, w_down, y, tile_expert, num_tiles, E, 0, 0)
-    ops.moe_combine(y, pos, w.contiguous(), shared, out)
+    ops.moe_combine(y, pos, w.contiguous(), shared, out, shared_gate)
     return out
