@@ -55,6 +55,36 @@ struct GroupedGemmArgs {
 void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t s);
 }  // namespace gemm
 
+namespace gemm_fp8 {
+// C[M, N] bf16 = sum over 128-wide K blocks of sa[m, kb] * sb[n / 128, kb] * (A . B^T)[kb]
+struct Fp8GemmArgs {
+  const void* A;  // [M, K] e4m3, row stride lda (elements = bytes)
+  int64_t lda;
+  const void* B;  // [N, K] e4m3, row stride ldb
+  int64_t ldb;
+  const float* sa;  // [M, ceil(K/128)] per-token group scales, row stride sa_ld
+  int64_t sa_ld;
+  const float* sb;  // [ceil(N/128), ceil(K/128)] block scales, row stride sb_ld
+  int64_t sb_ld;
+  void* C;  // [M, N] bf16, row stride ldc
+  int64_t ldc;
+  int M, N, K;
+  int splits;  // 0 = planner
+  float* workspace;
+  long workspace_numel;
+  int* counters;
+  long counters_numel;
+  int* err;
+};
+struct Fp8Plan {
+  int splits;
+  long workspace_floats;
+  int counters;
+};
+Fp8Plan plan_fp8(int M, int N, int K);
+void run_fp8(const Fp8GemmArgs& a, cudaStream_t stream);
+}  // namespace gemm_fp8
+
 // ------------------------------------------------------------------------------- GDN
 namespace gdn {
 void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,

@@ -9,6 +9,7 @@
 //              [61,64) layout (0 none, 2 = 128B swizzle, 4 = 64B, 6 = 32B)
 //   instr desc (kind::f16): [4,6) D fmt (1=f32), [7,10) A fmt (0 f16, 1 bf16), [10,13) B fmt,
 //              [15] A major (0=K), [16] B major, [17,23) N>>3, [24,29) M>>4
+//   (kind::f8f6f4 uses the same fields with A/B formats 0 = e4m3, 1 = e5m2)
 #pragma once
 #include "common.cuh"
 
@@ -66,6 +67,15 @@ B200_HOST_DEVICE constexpr uint32_t idesc_f16(int M, int N) {
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::f8f6f4 with fp32 accumulation, both operands K-major
+// e4m3 (format code 0 in the A/B format fields; K = 32 per instruction).
+B200_HOST_DEVICE constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4)                                   // D = f32
+         | (0u << 7) | (0u << 10)                    // A, B = E4M3
+         | (0u << 15) | (0u << 16)                   // both K-major
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // ---------------------------------------------------------------------------------------------
 // MMA issue (single thread) and commit
 // ---------------------------------------------------------------------------------------------
@@ -75,6 +85,16 @@ B200_DEVICE void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, u
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+B200_DEVICE void mma_f8f6f4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

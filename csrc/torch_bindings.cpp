@@ -98,6 +98,61 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
   return {p.bn, p.splits, p.workspace_floats, p.mt};
 }
 
+void gemm_fp8(const Tensor& A, const Tensor& sa, const Tensor& B, const Tensor& sb, Tensor& C,
+              int64_t splits, const c10::optional<Tensor>& workspace,
+              const c10::optional<Tensor>& counters) {
+  CHECK_CUDA(A);
+  CHECK_CUDA(B);
+  TORCH_CHECK(A.scalar_type() == at::kFloat8_e4m3fn && B.scalar_type() == at::kFloat8_e4m3fn,
+              "gemm_fp8: e4m3 operands");
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  CHECK_ROWMAJOR(C);
+  TORCH_CHECK(C.scalar_type() == at::kBFloat16, "gemm_fp8: bf16 output");
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sb.scalar_type() == at::kFloat &&
+                  sa.stride(1) == 1 && sb.stride(1) == 1,
+              "gemm_fp8: fp32 row-major scales");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  const int kb = (K + 127) / 128;
+  TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "gemm_fp8: shapes");
+  TORCH_CHECK(sa.size(0) >= M && sa.size(1) >= kb, "gemm_fp8: activation scales [M, K/128]");
+  TORCH_CHECK(sb.size(0) >= (N + 127) / 128 && sb.size(1) >= kb,
+              "gemm_fp8: weight scales [N/128, K/128]");
+  const c10::cuda::CUDAGuard g(A.device());
+  b200::gemm_fp8::Fp8GemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.sa = sa.data_ptr<float>();
+  a.sa_ld = sa.stride(0);
+  a.sb = sb.data_ptr<float>();
+  a.sb_ld = sb.stride(0);
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.splits = splits;
+  if (workspace.has_value()) {
+    TORCH_CHECK(workspace->scalar_type() == at::kFloat && workspace->is_cuda(), "workspace");
+    a.workspace = workspace->data_ptr<float>();
+    a.workspace_numel = workspace->numel();
+  }
+  if (counters.has_value()) {
+    TORCH_CHECK(counters->scalar_type() == at::kInt && counters->is_cuda(), "counters");
+    a.counters = counters->data_ptr<int>();
+    a.counters_numel = counters->numel();
+  }
+  a.err = err_ptr(A);
+  guarded([&] { b200::gemm_fp8::run_fp8(a, stream_of(A)); });
+}
+
+std::vector<int64_t> gemm_fp8_plan(int64_t M, int64_t N, int64_t K) {
+  const auto p = b200::gemm_fp8::plan_fp8(M, N, K);
+  return {p.splits, p.workspace_floats, p.counters};
+}
+
 // ------------------------------------------------------------------------------------- norms
 void rms_norm(Tensor& out, const Tensor& x, const Tensor& w, double eps, bool gemma) {
   CHECK_CUDA(x);
@@ -672,6 +727,9 @@ TORCH_LIBRARY(b200, m) {
   m.def("embedding(Tensor(a!) out, Tensor table, Tensor ids, int vocab_start=0) -> ()");
   m.def("gather_rows(Tensor(a!) out, Tensor x, Tensor idx) -> ()");
   m.def(
+      "gemm_fp8(Tensor A, Tensor sa, Tensor B, Tensor sb, Tensor(a!) C, int splits=0, "
+      "Tensor? workspace=None, Tensor? counters=None) -> ()");
+  m.def(
       "gemm_grouped_bf16(Tensor A, Tensor B, Tensor(a!) C, Tensor tile_expert, Tensor num_tiles, "
       "int num_experts, int mode=0, int bn=0) -> ()");
   m.def("topk_softmax(Tensor logits, Tensor(a!) ids, Tensor(b!) w, bool renorm=True) -> ()");
@@ -712,6 +770,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("topk_softmax", &topk_softmax);
   m.impl("grouped_topk", &grouped_topk);
   m.impl("moe_align", &moe_align);
+  m.impl("gemm_fp8", &gemm_fp8);
   m.impl("moe_gather", &moe_gather);
   m.impl("moe_combine", &moe_combine);
   m.impl("causal_conv1d", &causal_conv1d);
@@ -724,6 +783,7 @@ void register_runtime(pybind11::module_& m);  // csrc/runtime/bindings.cpp
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vllm_musa_b200 native extension (sm_100a kernels + host runtime)";
   m.def("gemm_plan", &gemm_plan, "automatic (bn, splits, workspace_floats) for a bf16 GEMM");
+  m.def("gemm_fp8_plan", &gemm_fp8_plan, "automatic (splits, workspace_floats, counters) for fp8");
   m.def("decode_num_splits", &decode_num_splits, "split-KV count for a decode batch");
   m.def("moe_max_rows", [](int64_t n, int64_t E) { return (int64_t)b200::moe::align_max_rows(n, E); },
         "rows of the expert-sorted buffer for n assignments over E experts");

@@ -69,7 +69,7 @@ class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
             # the shared expert's gate logit rides in the router GEMM as row E (padded to a
             # multiple of 8 rows); the combine kernel applies its sigmoid
             sg = st["mlp.shared_expert_gate.weight"].reshape(1, -1)
-            router = torch.cat([router, sg, torch.zeros(7, sg.shape[1], dtype=sg.dtype)], 0)
+            router = torch.cat([router, sg, sg.new_zeros(7, sg.shape[1])], 0)
             L.shared_gate = True
         L.router_w = self._to(router)
         gus, downs = [], []
