@@ -75,6 +75,10 @@ struct Fp8GemmArgs {
   int* counters;
   long counters_numel;
   int* err;
+  // grouped (MoE) mode: B = [num_experts * N, K], sb = [num_experts * ceil(N/128), K/128]
+  const int32_t* tile_expert = nullptr;
+  const int32_t* num_tiles = nullptr;
+  int num_experts = 0;
 };
 struct Fp8Plan {
   int splits;
@@ -206,6 +210,59 @@ int decode_num_splits(int B, int Hkv, int max_seq_len);
 void run_decode(const DecodeArgs& a, cudaStream_t s);
 void run_prefill(const PrefillArgs& a, cudaStream_t s);
 }  // namespace attn
+
+namespace mla {
+// Absorbed multi-head latent attention over a [slots, 576] bf16 latent cache (c_kv | k_pe).
+struct MlaArgs {
+  const void* q_lat;  // (t, h, c<512) at t*ql_t + h*ql_h + c
+  int64_t ql_t, ql_h;
+  const void* q_pe;   // (t, h, c<64) at t*qp_t + h*qp_h + c
+  int64_t qp_t, qp_h;
+  const void* cache;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int block_size;
+  const int32_t* cu_q;
+  const int32_t* seq_lens;
+  int R;
+  const int32_t* indices;  // [T, topk] token positions (-1 = none) or null for the causal prefix
+  int64_t idx_ld;
+  int topk;
+  void* out;  // (t, h, c<512) bf16 at t*o_t + h*o_h + c
+  int64_t o_t, o_h;
+  float* ws_o;    // [splits, T, Hq, 512] when splits > 1
+  float* ws_lse;  // [splits, T, Hq]
+  int T, Hq, splits;
+  float scale;
+};
+void run_prep(void* q, int64_t ld_q, int Hq, const void* kv, int64_t ld_kv, const void* kv_norm_w,
+              float eps, const int32_t* positions, const float* cos_sin, void* cache,
+              const int32_t* slots, int T, cudaStream_t s);
+void run_attention(const MlaArgs& a, cudaStream_t s);
+
+// DeepSeek-V3.2 lightning indexer.
+struct IndexerArgs {
+  const void* q;  // [T, 64 * 128] bf16 (RoPE applied), row stride ld_q
+  int64_t ld_q;
+  const float* w;  // [T, 64] head weights, row stride ld_w
+  int64_t ld_w;
+  const void* cache;  // [slots, 128] bf16 index keys
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int block_size;
+  const int32_t* cu_q;
+  const int32_t* seq_lens;
+  int R, T;
+  float* scores;  // [T, ld_s]
+  int64_t ld_s;
+};
+void run_indexer_k_prep(const void* k, int64_t ld_k, const void* ln_w, const void* ln_b, float eps,
+                        const int32_t* positions, const float* cos_sin, void* cache,
+                        const int32_t* slots, int T, cudaStream_t s);
+void run_indexer_scores(const IndexerArgs& a, cudaStream_t s);
+void run_topk(const float* scores, int64_t ld_s, const int32_t* cu_q, const int32_t* seq_lens,
+              int R, int T, int k, int32_t* out, int64_t ld_o, cudaStream_t s);
+}  // namespace mla
 
 // ------------------------------------------------------------------------------- sampling
 namespace sampling {

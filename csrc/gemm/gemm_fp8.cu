@@ -52,6 +52,10 @@ struct Params {
   float* ws;      // split-K partials [splits, M, N]
   int* counters;  // one per output tile, zero between launches
   int* err;
+  // grouped (MoE) mode: m-tile i multiplies expert tile_expert[i] (B rows e*N.., scale rows
+  // e*ceil(N/128)..); the live m-tile count is read from the device
+  const int32_t* tile_expert;
+  const int32_t* num_tiles;
 };
 
 B200_DEVICE void epi_barrier() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -88,6 +92,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     Params p, int stages) {
   pdl_trigger();
+  if (p.tile_expert) {
+    pdl_wait();  // the live tile count comes from the preceding alignment kernel
+    p.num_m = *p.num_tiles;
+    p.total_units = p.num_m * p.num_n;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -142,7 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = smem + stage * kStageBytes;
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           tma_load_2d(st, &tmA, &full[stage], kb * BK, m * BM);
-          tma_load_2d(st + BM * BK, &tmB, &full[stage], kb * BK, n * BN);
+          const int brow = p.tile_expert ? p.tile_expert[m] * p.N + n * BN : n * BN;
+          tma_load_2d(st + BM * BK, &tmB, &full[stage], kb * BK, brow);
           if (++stage == stages) {
             stage = 0;
             phase ^= 1;
@@ -213,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
       const float* sa_row = p.sa + (size_t)(row_ok ? row : 0) * p.sa_ld;
-      const float* sb_row = p.sb + (size_t)n * p.sb_ld;
+      const int nb = p.tile_expert ? p.tile_expert[m] * ((p.N + BN - 1) / BN) + n : n;
+      const float* sb_row = p.sb + (size_t)nb * p.sb_ld;
       float acc[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = 0.f;
@@ -328,7 +339,9 @@ void run_fp8(const Fp8GemmArgs& a, cudaStream_t stream) {
   p.num_m = (M + BM - 1) / BM;
   p.num_n = (N + BN - 1) / BN;
   p.num_kb = (K + BK - 1) / BK;
-  int s = a.splits > 0 ? std::min(a.splits, p.num_kb) : plan_fp8(M, N, K).splits;
+  int s = a.tile_expert ? 1
+          : a.splits > 0 ? std::min(a.splits, p.num_kb)
+                         : plan_fp8(M, N, K).splits;
   p.kb_per_split = (p.num_kb + s - 1) / s;
   s = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.splits = s;
@@ -342,6 +355,12 @@ void run_fp8(const Fp8GemmArgs& a, cudaStream_t stream) {
   p.err = a.err;
   p.ws = a.workspace;
   p.counters = a.counters;
+  p.tile_expert = a.tile_expert;
+  p.num_tiles = a.num_tiles;
+  if (a.tile_expert) {
+    B200_REQUIRE(s == 1 && a.num_tiles && M % BM == 0 && a.num_experts > 0,
+                 "gemm_fp8 grouped: no split-K, rows a multiple of 128");
+  }
   if (s > 1) {
     B200_REQUIRE(a.workspace && a.workspace_numel >= (long)s * M * N,
                  "gemm_fp8: split-K workspace too small");
@@ -350,8 +369,10 @@ void run_fp8(const Fp8GemmArgs& a, cudaStream_t stream) {
   }
   const CUtensorMap ta = make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K,
                                      M, a.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-  const CUtensorMap tb = make_tma_2d(const_cast<void*>(a.B), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K,
-                                     N, a.ldb, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tb =
+      make_tma_2d(const_cast<void*>(a.B), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K,
+                  (uint64_t)(a.tile_expert ? a.num_experts : 1) * N, a.ldb, BK, BN,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
   const int stages = kMaxStages;
   ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_fp8_kernel), kSmemBytes);
   cudaLaunchConfig_t cfg = {};

@@ -100,7 +100,8 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
 
 void gemm_fp8(const Tensor& A, const Tensor& sa, const Tensor& B, const Tensor& sb, Tensor& C,
               int64_t splits, const c10::optional<Tensor>& workspace,
-              const c10::optional<Tensor>& counters) {
+              const c10::optional<Tensor>& counters, const c10::optional<Tensor>& tile_expert,
+              const c10::optional<Tensor>& num_tiles, int64_t num_experts) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   TORCH_CHECK(A.scalar_type() == at::kFloat8_e4m3fn && B.scalar_type() == at::kFloat8_e4m3fn,
@@ -112,12 +113,16 @@ void gemm_fp8(const Tensor& A, const Tensor& sa, const Tensor& B, const Tensor& 
   TORCH_CHECK(sa.scalar_type() == at::kFloat && sb.scalar_type() == at::kFloat &&
                   sa.stride(1) == 1 && sb.stride(1) == 1,
               "gemm_fp8: fp32 row-major scales");
-  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  const bool grouped = tile_expert.has_value();
+  const int E = grouped ? num_experts : 1;
+  TORCH_CHECK(!grouped || (num_tiles.has_value() && E > 0 && B.size(0) % E == 0),
+              "gemm_fp8: grouped mode needs num_tiles and B rows = E * N");
+  const int M = A.size(0), N = B.size(0) / E, K = A.size(1);
   const int kb = (K + 127) / 128;
   TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "gemm_fp8: shapes");
   TORCH_CHECK(sa.size(0) >= M && sa.size(1) >= kb, "gemm_fp8: activation scales [M, K/128]");
-  TORCH_CHECK(sb.size(0) >= (N + 127) / 128 && sb.size(1) >= kb,
-              "gemm_fp8: weight scales [N/128, K/128]");
+  TORCH_CHECK(sb.size(0) >= E * ((N + 127) / 128) && sb.size(1) >= kb,
+              "gemm_fp8: weight scales [E * N/128, K/128]");
   const c10::cuda::CUDAGuard g(A.device());
   b200::gemm_fp8::Fp8GemmArgs a{};
   a.A = A.data_ptr();
@@ -143,6 +148,13 @@ void gemm_fp8(const Tensor& A, const Tensor& sa, const Tensor& B, const Tensor& 
     TORCH_CHECK(counters->scalar_type() == at::kInt && counters->is_cuda(), "counters");
     a.counters = counters->data_ptr<int>();
     a.counters_numel = counters->numel();
+  }
+  if (grouped) {
+    TORCH_CHECK(tile_expert->scalar_type() == at::kInt && num_tiles->scalar_type() == at::kInt,
+                "gemm_fp8: int32 tile metadata");
+    a.tile_expert = tile_expert->data_ptr<int32_t>();
+    a.num_tiles = num_tiles->data_ptr<int32_t>();
+    a.num_experts = E;
   }
   a.err = err_ptr(A);
   guarded([&] { b200::gemm_fp8::run_fp8(a, stream_of(A)); });
@@ -323,6 +335,141 @@ void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
   a.eps = eps;
   a.err = err_ptr(qkv);
   guarded([&] { b200::rope::run_rope_kv(a, stream_of(qkv)); });
+}
+
+// ------------------------------------------------------------------------------------- MLA
+void mla_prep(Tensor& q, const Tensor& kv, const Tensor& kv_norm_w, double eps,
+              const Tensor& positions, const Tensor& cos_sin, Tensor& cache,
+              const Tensor& slot_mapping, int64_t Hq) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_BF16(kv);
+  TORCH_CHECK(q.stride(1) == 1 && kv.stride(1) == 1 && q.size(1) >= Hq * 192 && kv.size(1) >= 576,
+              "mla_prep: q [T, Hq*192], kv [T, 576] row-major");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 576 && cache.scalar_type() == at::kBFloat16,
+              "mla_prep: bf16 latent cache [..., 576]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == 64, "mla_prep: cos_sin [P, 64]");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slot_mapping.scalar_type() == at::kInt,
+              "mla_prep: int32 positions / slots");
+  const c10::cuda::CUDAGuard g(q.device());
+  guarded([&] {
+    b200::mla::run_prep(q.data_ptr(), q.stride(0), Hq, kv.data_ptr(), kv.stride(0),
+                        kv_norm_w.data_ptr(), eps, positions.data_ptr<int32_t>(),
+                        cos_sin.data_ptr<float>(), cache.data_ptr(), slot_mapping.data_ptr<int32_t>(),
+                        q.size(0), stream_of(q));
+  });
+}
+
+void mla_attention(const Tensor& q_lat, const Tensor& q_pe, const Tensor& cache,
+                   const Tensor& block_tables, const Tensor& cu_q, const Tensor& seq_lens,
+                   const c10::optional<Tensor>& indices, Tensor& out, double scale, int64_t splits,
+                   const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse) {
+  CHECK_CUDA(q_lat);
+  TORCH_CHECK(q_lat.dim() == 3 && q_pe.dim() == 3 && out.dim() == 3, "mla_attention: [T, H, C] views");
+  TORCH_CHECK(q_lat.stride(2) == 1 && q_pe.stride(2) == 1 && out.stride(2) == 1 &&
+                  q_lat.size(2) == 512 && q_pe.size(2) == 64 && out.size(2) == 512,
+              "mla_attention: inner dims 512 / 64 contiguous");
+  TORCH_CHECK(q_lat.scalar_type() == at::kBFloat16 && q_pe.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16,
+              "mla_attention: bf16");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 576, "mla_attention: cache [..., 576]");
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.stride(1) == 1, "mla_attention: block tables");
+  const int bs = cache.dim() == 3 ? cache.size(1) : cache.size(-2);
+  b200::mla::MlaArgs a{};
+  a.q_lat = q_lat.data_ptr();
+  a.ql_t = q_lat.stride(0);
+  a.ql_h = q_lat.stride(1);
+  a.q_pe = q_pe.data_ptr();
+  a.qp_t = q_pe.stride(0);
+  a.qp_h = q_pe.stride(1);
+  a.cache = cache.data_ptr();
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.bt_stride = block_tables.stride(0);
+  a.block_size = bs;
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.R = seq_lens.size(0);
+  if (indices.has_value()) {
+    TORCH_CHECK(indices->scalar_type() == at::kInt && indices->stride(1) == 1, "mla: int32 indices");
+    a.indices = indices->data_ptr<int32_t>();
+    a.idx_ld = indices->stride(0);
+    a.topk = indices->size(1);
+  }
+  a.out = out.data_ptr();
+  a.o_t = out.stride(0);
+  a.o_h = out.stride(1);
+  a.T = q_lat.size(0);
+  a.Hq = q_lat.size(1);
+  a.splits = splits;
+  a.scale = scale;
+  if (splits > 1) {
+    TORCH_CHECK(ws_o.has_value() && ws_lse.has_value() &&
+                    ws_o->numel() >= splits * a.T * a.Hq * 512 && ws_lse->numel() >= splits * a.T * a.Hq,
+                "mla_attention: split workspace too small");
+    a.ws_o = ws_o->data_ptr<float>();
+    a.ws_lse = ws_lse->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard g(q_lat.device());
+  guarded([&] { b200::mla::run_attention(a, stream_of(q_lat)); });
+}
+
+void indexer_k_prep(const Tensor& k, const Tensor& ln_w, const Tensor& ln_b, double eps,
+                    const Tensor& positions, const Tensor& cos_sin, Tensor& cache,
+                    const Tensor& slot_mapping) {
+  CHECK_CUDA(k);
+  CHECK_BF16(k);
+  TORCH_CHECK(k.stride(1) == 1 && k.size(1) >= 128, "indexer_k_prep: k [T, 128]");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 128, "indexer_k_prep: cache [..., 128]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == 64, "indexer: cos_sin [P, 64]");
+  const c10::cuda::CUDAGuard g(k.device());
+  guarded([&] {
+    b200::mla::run_indexer_k_prep(k.data_ptr(), k.stride(0), ln_w.data_ptr(), ln_b.data_ptr(), eps,
+                                  positions.data_ptr<int32_t>(), cos_sin.data_ptr<float>(),
+                                  cache.data_ptr(), slot_mapping.data_ptr<int32_t>(), k.size(0),
+                                  stream_of(k));
+  });
+}
+
+void indexer_scores(const Tensor& q, const Tensor& w, const Tensor& cache,
+                    const Tensor& block_tables, const Tensor& cu_q, const Tensor& seq_lens,
+                    Tensor& scores) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  TORCH_CHECK(q.stride(1) == 1 && q.size(1) >= 64 * 128, "indexer_scores: q [T, 64*128]");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.stride(1) == 1 && w.size(1) >= 64,
+              "indexer_scores: fp32 weights [T, 64]");
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.stride(1) == 1, "indexer_scores: fp32 out");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 128, "indexer_scores: cache [..., 128]");
+  b200::mla::IndexerArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = q.stride(0);
+  a.w = w.data_ptr<float>();
+  a.ld_w = w.stride(0);
+  a.cache = cache.data_ptr();
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.bt_stride = block_tables.stride(0);
+  a.block_size = cache.dim() == 3 ? cache.size(1) : cache.size(-2);
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.R = seq_lens.size(0);
+  a.T = q.size(0);
+  a.scores = scores.data_ptr<float>();
+  a.ld_s = scores.size(1);
+  TORCH_CHECK(scores.stride(0) == scores.size(1), "indexer_scores: contiguous scores");
+  const c10::cuda::CUDAGuard g(q.device());
+  guarded([&] { b200::mla::run_indexer_scores(a, stream_of(q)); });
+}
+
+void mla_topk(const Tensor& scores, const Tensor& cu_q, const Tensor& seq_lens, Tensor& out) {
+  CHECK_CUDA(scores);
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.stride(1) == 1, "topk: fp32 scores");
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.stride(1) == 1, "topk: int32 out");
+  const c10::cuda::CUDAGuard g(scores.device());
+  guarded([&] {
+    b200::mla::run_topk(scores.data_ptr<float>(), scores.stride(0), cu_q.data_ptr<int32_t>(),
+                        seq_lens.data_ptr<int32_t>(), seq_lens.size(0), scores.size(0), out.size(1),
+                        out.data_ptr<int32_t>(), out.stride(0), stream_of(scores));
+  });
 }
 
 // ------------------------------------------------------------------------------------- attention
@@ -727,8 +874,23 @@ TORCH_LIBRARY(b200, m) {
   m.def("embedding(Tensor(a!) out, Tensor table, Tensor ids, int vocab_start=0) -> ()");
   m.def("gather_rows(Tensor(a!) out, Tensor x, Tensor idx) -> ()");
   m.def(
+      "mla_prep(Tensor(a!) q, Tensor kv, Tensor kv_norm_w, float eps, Tensor positions, "
+      "Tensor cos_sin, Tensor(b!) cache, Tensor slot_mapping, int Hq) -> ()");
+  m.def(
+      "mla_attention(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_tables, Tensor cu_q, "
+      "Tensor seq_lens, Tensor? indices, Tensor(a!) out, float scale, int splits, "
+      "Tensor? ws_o=None, Tensor? ws_lse=None) -> ()");
+  m.def(
+      "indexer_k_prep(Tensor k, Tensor ln_w, Tensor ln_b, float eps, Tensor positions, "
+      "Tensor cos_sin, Tensor(a!) cache, Tensor slot_mapping) -> ()");
+  m.def(
+      "indexer_scores(Tensor q, Tensor w, Tensor cache, Tensor block_tables, Tensor cu_q, "
+      "Tensor seq_lens, Tensor(a!) scores) -> ()");
+  m.def("mla_topk(Tensor scores, Tensor cu_q, Tensor seq_lens, Tensor(a!) out) -> ()");
+  m.def(
       "gemm_fp8(Tensor A, Tensor sa, Tensor B, Tensor sb, Tensor(a!) C, int splits=0, "
-      "Tensor? workspace=None, Tensor? counters=None) -> ()");
+      "Tensor? workspace=None, Tensor? counters=None, Tensor? tile_expert=None, "
+      "Tensor? num_tiles=None, int num_experts=0) -> ()");
   m.def(
       "gemm_grouped_bf16(Tensor A, Tensor B, Tensor(a!) C, Tensor tile_expert, Tensor num_tiles, "
       "int num_experts, int mode=0, int bn=0) -> ()");
@@ -771,6 +933,11 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("grouped_topk", &grouped_topk);
   m.impl("moe_align", &moe_align);
   m.impl("gemm_fp8", &gemm_fp8);
+  m.impl("mla_prep", &mla_prep);
+  m.impl("mla_attention", &mla_attention);
+  m.impl("indexer_k_prep", &indexer_k_prep);
+  m.impl("indexer_scores", &indexer_scores);
+  m.impl("mla_topk", &mla_topk);
   m.impl("moe_gather", &moe_gather);
   m.impl("moe_combine", &moe_combine);
   m.impl("causal_conv1d", &causal_conv1d);

@@ -37,6 +37,35 @@ def test_gemm_fp8_gpu(M, N, K, splits):
     torch.cuda.synchronize()
     _ext.check_device_errors()
     torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
-    # the full path: on-device activation quantisation + GEMM
+    # the full path: on-device activation quantisation + GEMM (the GPU quantiser may round a
+    # few values to the neighbouring e4m3 code, so its own output is the reference input)
     y = fp8.linear_fp8(x.cuda(), wq.cuda(), ws.cuda())
-    torch.testing.assert_close(y.float().cpu(), ref, rtol=5e-2, atol=5e-2)
+    gq, gs = fp8.group_quant_fp8(x.cuda())
+    ref2 = fp8.gemm_fp8_ref(gq.cpu(), gs.cpu(), wq, ws)
+    torch.testing.assert_close(y.float().cpu(), ref2, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,E,k,H,I,off", [(1, 8, 2, 256, 128, 0), (77, 16, 4, 512, 256, 8),
+                                            (300, 32, 8, 1024, 256, 0)])
+def test_fused_moe_fp8_gpu(T, E, k, H, I, off):
+    from vllm_musa_b200.ops import moe as moe_ops
+    g = torch.Generator().manual_seed(T + E + off)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    gus, gss, dws, dss = [], [], [], []
+    for _ in range(E):
+        q, s = fp8.quantize_weight_block(torch.randn(2 * I, H, generator=g) * 0.05)
+        gus.append(q)
+        gss.append(s)
+        q, s = fp8.quantize_weight_block(torch.randn(H, I, generator=g) * 0.05)
+        dws.append(q)
+        dss.append(s)
+    w_gu, s_gu, w_dn, s_dn = torch.cat(gus), torch.cat(gss), torch.cat(dws), torch.cat(dss)
+    ids, w = moe_ops.topk_softmax(torch.randn(T, 2 * E, generator=g), k)  # half are other ranks'
+    shared = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
+    ref = moe_ops.fused_moe_fp8(x, w_gu, s_gu, w_dn, s_dn, ids, w, E, shared, expert_offset=off)
+    out = moe_ops.fused_moe_fp8(x.cuda(), w_gu.cuda(), s_gu.cuda(), w_dn.cuda(), s_dn.cuda(),
+                                ids.cuda(), w.cuda(), E, shared.cuda(), expert_offset=off)
+    torch.cuda.synchronize()
+    # activations are re-quantised to e4m3 twice on the GPU path: compare at fp8 resolution
+    torch.testing.assert_close(out.float().cpu(), ref.float(), rtol=6e-2, atol=6e-2)

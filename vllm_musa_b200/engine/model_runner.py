@@ -116,6 +116,8 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ memory / KV cache
     def kv_bytes_per_block(self) -> int:
+        if hasattr(self.model, "kv_bytes_per_block"):  # model-defined caches (e.g. MLA)
+            return self.model.kv_bytes_per_block(self.block_size)
         spec = self.model.kv_cache_spec()
         elt = torch.tensor([], dtype=spec["dtype"]).element_size()
         return spec["num_layers"] * 2 * spec["num_kv_heads"] * self.block_size * spec["head_dim"] * elt
@@ -128,9 +130,12 @@ class ModelRunner:
             self.allocate_kv(n)
             return n
         spec = self.model.kv_cache_spec()
-        tmp = [(torch.zeros(1, spec["num_kv_heads"], self.block_size, spec["head_dim"],
-                            dtype=spec["dtype"], device=self.device),) * 2
-               for _ in range(spec["num_layers"])]
+        if hasattr(self.model, "allocate_kv_cache"):
+            tmp = self.model.allocate_kv_cache(1, self.block_size)
+        else:
+            tmp = [(torch.zeros(1, spec["num_kv_heads"], self.block_size, spec["head_dim"],
+                                dtype=spec["dtype"], device=self.device),) * 2
+                   for _ in range(spec["num_layers"])]
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         torch.cuda.reset_peak_memory_stats()
@@ -174,6 +179,10 @@ class ModelRunner:
     def allocate_kv(self, num_blocks: int) -> None:
         spec = self.model.kv_cache_spec()
         self.num_blocks = num_blocks
+        if hasattr(self.model, "allocate_kv_cache"):
+            self.kv_tensor = None
+            self.kv_caches = self.model.allocate_kv_cache(num_blocks, self.block_size)
+            return
         self.kv_tensor = torch.zeros(spec["num_layers"], 2, num_blocks, spec["num_kv_heads"],
                                      self.block_size, spec["head_dim"], dtype=spec["dtype"],
                                      device=self.device)
@@ -241,6 +250,8 @@ class ModelRunner:
             for M in Ms + [1, 2, 4, 8, 16, 32, 64, 128]:
                 need = max(need, ops.gemm.plan_for(M, N, K)[3], mod.gemm_plan(M, N, K)[2])
         ops.gemm.reserve_workspace(self.device, need)
+        if hasattr(self.model, "reserve_workspaces"):
+            self.model.reserve_workspaces(max(self.graph_sizes() + [1]))
         spec = self.model.kv_cache_spec()
         hq = getattr(self.model, "hq", spec["num_kv_heads"])
         worst = 0

@@ -185,3 +185,122 @@ class HybridReferenceDecoder(ReferenceDecoder):
         h = self._rms1(h, w["model.norm.weight"])
         head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
         return h @ head.t()
+
+
+class DeepseekReferenceDecoder(ReferenceDecoder):
+    """Whole-sequence fp32 reference of the DeepSeek-V3 / V3.2 decoder from HF-named weights:
+    MLA in its expanded form (per-head keys and values from kv_b_proj, no absorption), the
+    V3.2 lightning indexer as an explicit causal top-k mask, sigmoid grouped-top-k MoE with
+    the score-correction bias and shared experts.  Latent RoPE is the interleaved form."""
+
+    def __init__(self, cfg, weights):
+        super().__init__(cfg, weights)
+        rot = cfg.qk_rope_head_dim
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rot, 2, dtype=torch.float64) / rot))
+        f = torch.outer(torch.arange(cfg.max_position, dtype=torch.float64), inv)
+        self.cos, self.sin = f.cos().float(), f.sin().float()
+
+    def _rope_il(self, x, pos):
+        c, s = self.cos[pos], self.sin[pos]
+        while c.dim() < x.dim():
+            c, s = c.unsqueeze(-2), s.unsqueeze(-2)
+        out = torch.empty_like(x)
+        out[..., 0::2] = x[..., 0::2] * c - x[..., 1::2] * s
+        out[..., 1::2] = x[..., 1::2] * c + x[..., 0::2] * s
+        return out
+
+    def _rope_nx(self, x, pos):
+        c, s = self.cos[pos], self.sin[pos]
+        while c.dim() < x.dim():
+            c, s = c.unsqueeze(-2), s.unsqueeze(-2)
+        h = x.shape[-1] // 2
+        return torch.cat([x[..., :h] * c - x[..., h:] * s, x[..., h:] * c + x[..., :h] * s], -1)
+
+    def _attention(self, p, x, pos):
+        cfg, w = self.cfg, self.w
+        S, Hq = x.shape[0], cfg.num_heads
+        nope, rope, vd = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+        a = p + "self_attn."
+        if cfg.q_lora_rank:
+            q_a = self._rms(x @ w[a + "q_a_proj.weight"].t(), w[a + "q_a_layernorm.weight"])
+            q = (q_a @ w[a + "q_b_proj.weight"].t()).view(S, Hq, nope + rope)
+        else:
+            q = (x @ w[a + "q_proj.weight"].t()).view(S, Hq, nope + rope)
+        kv = x @ w[a + "kv_a_proj_with_mqa.weight"].t()
+        c = self._rms(kv[:, :cfg.kv_lora_rank], w[a + "kv_a_layernorm.weight"])
+        k_pe = self._rope_il(kv[:, cfg.kv_lora_rank:], pos)                   # [S, 64]
+        q = torch.cat([q[..., :nope], self._rope_il(q[..., nope:], pos)], -1)
+        kvb = (c @ w[a + "kv_b_proj.weight"].t()).view(S, Hq, nope + vd)
+        k = torch.cat([kvb[..., :nope], k_pe.unsqueeze(1).expand(S, Hq, rope)], -1)
+        v = kvb[..., nope:]
+        scale = (nope + rope) ** -0.5
+        s = torch.einsum("qhd,khd->hqk", q, k) * scale
+        allow = torch.tril(torch.ones(S, S, dtype=torch.bool))
+        if cfg.index_topk:
+            allow = allow & self._indexer_mask(a, x, q_a, pos, allow)
+        s = s.masked_fill(~allow[None], float("-inf"))
+        o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(S, -1)
+        return o @ w[a + "o_proj.weight"].t()
+
+    def _indexer_mask(self, a, x, q_a, pos, causal):
+        cfg, w = self.cfg, self.w
+        S, nh, dh = x.shape[0], cfg.index_n_heads, cfg.index_head_dim
+        i = a + "indexer."
+        q = (q_a @ w[i + "wq_b.weight"].t()).view(S, nh, dh)
+        q = torch.cat([self._rope_nx(q[..., :64], pos), q[..., 64:]], -1)
+        k = F.layer_norm(x @ w[i + "wk.weight"].t(), (dh,), w[i + "k_norm.weight"],
+                         w[i + "k_norm.bias"], 1e-6)
+        k = torch.cat([self._rope_nx(k[..., :64], pos), k[..., 64:]], -1)
+        hw = (x @ w[i + "weights_proj.weight"].t()) * (nh ** -0.5 * dh ** -0.5)
+        sc = (hw.unsqueeze(-1) * torch.relu(torch.einsum("thd,sd->ths", q, k))).sum(1)
+        sc = sc.masked_fill(~causal, float("-inf"))
+        mask = torch.zeros(S, S, dtype=torch.bool)
+        for t in range(S):
+            n = min(cfg.index_topk, t + 1)
+            mask[t, sc[t, :t + 1].topk(n).indices] = True
+        return mask
+
+    def _moe(self, p, x):
+        cfg, w = self.cfg, self.w
+        T = x.shape[0]
+        logits = x @ w[p + "mlp.gate.weight"].t()
+        scores = torch.sigmoid(logits) if cfg.scoring_func == "sigmoid" else torch.softmax(logits, -1)
+        choice = scores + w.get(p + "mlp.gate.e_score_correction_bias", torch.zeros(cfg.num_experts))
+        g = choice.view(T, cfg.n_group, -1).topk(2, -1).values.sum(-1)
+        keep = torch.zeros_like(g).scatter_(1, g.topk(cfg.topk_group, -1).indices, 1.0)
+        keep = keep.repeat_interleave(cfg.num_experts // cfg.n_group, 1)
+        ids = choice.masked_fill(keep == 0, float("-inf")).topk(cfg.num_experts_per_tok, -1).indices
+        wts = scores.gather(1, ids)
+        if cfg.norm_topk_prob:
+            wts = wts / wts.sum(-1, keepdim=True)
+        wts = wts * cfg.routed_scaling_factor
+        out = torch.zeros_like(x)
+        for t in range(T):
+            for j in range(ids.shape[1]):
+                q = f"{p}mlp.experts.{int(ids[t, j])}."
+                h = F.silu(x[t] @ w[q + "gate_proj.weight"].t()) * (x[t] @ w[q + "up_proj.weight"].t())
+                out[t] += wts[t, j] * (h @ w[q + "down_proj.weight"].t())
+        if cfg.shared_expert_intermediate_size:
+            q = p + "mlp.shared_experts."
+            out += (F.silu(x @ w[q + "gate_proj.weight"].t()) * (x @ w[q + "up_proj.weight"].t())) @ \
+                w[q + "down_proj.weight"].t()
+        return out
+
+    @torch.no_grad()
+    def logits(self, tokens: List[int]) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        S = len(tokens)
+        pos = torch.arange(S)
+        h = w["model.embed_tokens.weight"][torch.tensor(tokens)]
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            h = h + self._attention(p, self._rms(h, w[p + "input_layernorm.weight"]), pos)
+            x = self._rms(h, w[p + "post_attention_layernorm.weight"])
+            if cfg.num_experts and i >= cfg.first_k_dense:
+                h = h + self._moe(p, x)
+            else:
+                h = h + (F.silu(x @ w[p + "mlp.gate_proj.weight"].t()) *
+                         (x @ w[p + "mlp.up_proj.weight"].t())) @ w[p + "mlp.down_proj.weight"].t()
+        h = self._rms(h, w["model.norm.weight"])
+        head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
+        return h @ head.t()

@@ -36,3 +36,6 @@ def _populate():
     from .qwen3_next import Qwen3NextForCausalLM
     _REGISTRY["qwen3_moe"] = Qwen3MoeForCausalLM
     _REGISTRY["qwen3_next"] = Qwen3NextForCausalLM
+    from .deepseek_v2 import DeepseekV2ForCausalLM
+    for arch in ("deepseek_v2", "deepseek_v3", "deepseek_v32"):
+        _REGISTRY[arch] = DeepseekV2ForCausalLM

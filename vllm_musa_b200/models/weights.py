@@ -34,6 +34,8 @@ def hf_param_shapes(cfg: ModelConfig) -> list:
     """Ordered (name, shape, kind) list of the dense/MoE decoder parameters (HF names)."""
     H, D, V = cfg.hidden_size, cfg.head_dim, cfg.vocab_size
     out = [("model.embed_tokens.weight", (V, H), "w")]
+    if cfg.arch.startswith("deepseek"):
+        return out + _deepseek_shapes(cfg)
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
         hybrid = cfg.arch == "qwen3_next"
@@ -81,6 +83,55 @@ def hf_param_shapes(cfg: ModelConfig) -> list:
             out += [(p + "mlp.gate_proj.weight", (I, H), "w"), (p + "mlp.up_proj.weight", (I, H), "w"),
                     (p + "mlp.down_proj.weight", (H, I), "w")]
     out.append(("model.norm.weight", (H,), "norm0" if cfg.arch == "qwen3_next" else "norm"))
+    if not cfg.tie_word_embeddings:
+        out.append(("lm_head.weight", (V, H), "w"))
+    return out
+
+
+def _deepseek_shapes(cfg: ModelConfig) -> list:
+    """DeepSeek-V2/V3/V3.2 HF names (MLA, optional lightning indexer, grouped MoE)."""
+    H, V, Hq = cfg.hidden_size, cfg.vocab_size, cfg.num_heads
+    nope, rope, vd = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+    out = []
+    for i in range(cfg.num_layers):
+        p = f"model.layers.{i}."
+        a = p + "self_attn."
+        out.append((p + "input_layernorm.weight", (H,), "norm"))
+        if cfg.q_lora_rank:
+            out += [(a + "q_a_proj.weight", (cfg.q_lora_rank, H), "w"),
+                    (a + "q_a_layernorm.weight", (cfg.q_lora_rank,), "norm"),
+                    (a + "q_b_proj.weight", (Hq * (nope + rope), cfg.q_lora_rank), "w")]
+        else:
+            out.append((a + "q_proj.weight", (Hq * (nope + rope), H), "w"))
+        out += [(a + "kv_a_proj_with_mqa.weight", (cfg.kv_lora_rank + rope, H), "w"),
+                (a + "kv_a_layernorm.weight", (cfg.kv_lora_rank,), "norm"),
+                (a + "kv_b_proj.weight", (Hq * (nope + vd), cfg.kv_lora_rank), "w"),
+                (a + "o_proj.weight", (H, Hq * vd), "w")]
+        if cfg.index_topk:
+            x = a + "indexer."
+            out += [(x + "wq_b.weight", (cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank), "w"),
+                    (x + "wk.weight", (cfg.index_head_dim, H), "w"),
+                    (x + "k_norm.weight", (cfg.index_head_dim,), "norm"),
+                    (x + "k_norm.bias", (cfg.index_head_dim,), "norm0"),
+                    (x + "weights_proj.weight", (cfg.index_n_heads, H), "w")]
+        out.append((p + "post_attention_layernorm.weight", (H,), "norm"))
+        if cfg.num_experts and i >= cfg.first_k_dense:
+            E, I = cfg.num_experts, cfg.moe_intermediate_size
+            out += [(p + "mlp.gate.weight", (E, H), "w"),
+                    (p + "mlp.gate.e_score_correction_bias", (E,), "norm0")]
+            for e in range(E):
+                q = f"{p}mlp.experts.{e}."
+                out += [(q + "gate_proj.weight", (I, H), "w"), (q + "up_proj.weight", (I, H), "w"),
+                        (q + "down_proj.weight", (H, I), "w")]
+            if cfg.shared_expert_intermediate_size:
+                Is, q = cfg.shared_expert_intermediate_size, p + "mlp.shared_experts."
+                out += [(q + "gate_proj.weight", (Is, H), "w"), (q + "up_proj.weight", (Is, H), "w"),
+                        (q + "down_proj.weight", (H, Is), "w")]
+        else:
+            I = cfg.intermediate_size
+            out += [(p + "mlp.gate_proj.weight", (I, H), "w"), (p + "mlp.up_proj.weight", (I, H), "w"),
+                    (p + "mlp.down_proj.weight", (H, I), "w")]
+    out.append(("model.norm.weight", (H,), "norm"))
     if not cfg.tie_word_embeddings:
         out.append(("lm_head.weight", (V, H), "w"))
     return out

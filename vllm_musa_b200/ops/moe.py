@@ -131,3 +131,71 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
     ops.gemm_grouped_bf16(h, w_down, y, tile_expert, num_tiles, E, 0, 0)
     ops.moe_combine(y, pos, w.contiguous(), shared, out, shared_gate)
     return out
+
+
+def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_offset):
+    from .fp8 import dequantize_weight_block
+    T, H = x.shape
+    I2 = w_gu.shape[0] // E
+    out = torch.zeros(T, H, dtype=torch.float32)
+    xf = x.float()
+    for e in range(E):
+        tok, slot = torch.nonzero(ids == e + expert_offset, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        gu = dequantize_weight_block(w_gu[e * I2:(e + 1) * I2], s_gu[e * I2 // 128:(e + 1) * I2 // 128])
+        dn = dequantize_weight_block(w_down[e * H:(e + 1) * H],
+                                     s_down[e * (H // 128):(e + 1) * (H // 128)])
+        hg = xf[tok] @ gu.t()
+        h = F.silu(hg[:, :I2 // 2]) * hg[:, I2 // 2:]
+        out.index_add_(0, tok, (h @ dn.t()) * w[tok, slot].unsqueeze(1).float())
+    if shared is not None:
+        out += shared.float()
+    return out.to(x.dtype)
+
+
+def fused_moe_fp8(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, w_down: torch.Tensor,
+                  s_down: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, num_experts: int,
+                  shared: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                  expert_offset: int = 0) -> torch.Tensor:
+    """Block-FP8 routed experts (DeepSeek): w_gu e4m3 [E * 2I, H] with rows [gate (I) ; up (I)]
+    per expert and 128x128 scales s_gu [E * 2I/128, H/128]; w_down e4m3 [E * H, I], s_down
+    [E * H/128, I/128].
+
+        align -> gather -> 1x128 quant -> grouped FP8 GEMM (gate|up) -> SwiGLU + 1x128 quant
+        -> grouped FP8 GEMM (down) -> weighted combine (+ shared)
+    Every step is a device kernel with device-side counts (graph-capturable)."""
+    T, H = x.shape
+    k = ids.shape[1]
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    if not x.is_cuda:
+        out.copy_(_fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, num_experts, shared,
+                                     expert_offset))
+        return out
+    from .activation import group_quant_fp8, silu_mul_fp8_quant
+    mod = _ext.require()
+    E = num_experts
+    max_rows = int(mod.moe_max_rows(T * k, E))
+    dev = x.device
+    sorted_ids = torch.empty(max_rows, dtype=torch.int32, device=dev)
+    tile_expert = torch.empty(max_rows // 128, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, k, dtype=torch.int32, device=dev)
+    num_tiles = torch.empty(1, dtype=torch.int32, device=dev)
+    ops = torch.ops.b200
+    ops.moe_align(ids.contiguous(), E, sorted_ids, tile_expert, offsets, pos, num_tiles,
+                  expert_offset)
+    xs = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
+    ops.moe_gather(x, sorted_ids, num_tiles, k, xs)
+    xq, xsc = group_quant_fp8(xs)
+    I2 = w_gu.shape[0] // E
+    hg = torch.empty(max_rows, I2, dtype=x.dtype, device=dev)
+    ops.gemm_fp8(xq, xsc, w_gu, s_gu, hg, 1, None, None, tile_expert, num_tiles, E)
+    hq, hsc = silu_mul_fp8_quant(hg)
+    y = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
+    ops.gemm_fp8(hq, hsc, w_down, s_down, y, 1, None, None, tile_expert, num_tiles, E)
+    ops.moe_combine(y, pos, w.contiguous(), shared, out, None)
+    return out
