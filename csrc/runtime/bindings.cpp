@@ -65,7 +65,9 @@ void register_runtime(py::module_& m) {
       .def_readonly("num_preempted", &StepPlan::num_preempted)
       .def_readonly("all_greedy", &StepPlan::all_greedy)
       .def_readonly("any_filter", &StepPlan::any_filter)
-      .def_readonly("sample_req_ids", &StepPlan::sample_req_ids);
+      .def_readonly("sample_req_ids", &StepPlan::sample_req_ids)
+      .def_readonly("sample_counts", &StepPlan::sample_counts)
+      .def_readonly("num_spec_tokens", &StepPlan::num_spec_tokens);
 
   py::class_<Scheduler>(m, "Scheduler")
       .def(py::init([](const SchedulerConfig& c, int num_blocks, py::dict bufs) {
@@ -86,6 +88,12 @@ void register_runtime(py::module_& m) {
       .def("step_index", &Scheduler::step_index)
       .def("output_tokens", &Scheduler::output_tokens)
       .def("forget", &Scheduler::forget)
+      .def("propose_ngram", &Scheduler::propose_ngram, py::arg("k"), py::arg("n_min") = 1,
+           py::arg("n_max") = 4)
+      .def("set_draft", &Scheduler::set_draft)
+      .def("decode_request_ids", &Scheduler::decode_request_ids)
+      .def("spec_accepted", &Scheduler::spec_accepted)
+      .def("spec_proposed", &Scheduler::spec_proposed)
       .def("prefix_cache_hits", &Scheduler::prefix_cache_hits)
       .def("prefix_cache_queries", &Scheduler::prefix_cache_queries)
       .def("request_info", [](const Scheduler& s, int64_t id) -> py::object {

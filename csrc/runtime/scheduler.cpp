@@ -188,8 +188,9 @@ void Scheduler::admit_prefix(Request& r) {
 void Scheduler::register_full_blocks(Request& r) {
   if (!cfg_.prefix_caching) return;
   const int bs = cfg_.block_size;
+  const int known = std::min(r.num_computed, (int)r.tokens.size());
   while ((int)r.block_hashes.size() < (int)r.blocks.size() &&
-         ((int)r.block_hashes.size() + 1) * bs <= r.num_computed) {
+         ((int)r.block_hashes.size() + 1) * bs <= known) {
     const int j = (int)r.block_hashes.size();
     const uint64_t parent = j == 0 ? 0 : r.block_hashes[j - 1];
     const uint64_t h = block_hash(parent, r.tokens.data() + j * bs, bs);
@@ -206,6 +207,7 @@ StepPlan Scheduler::schedule() {
     Request* r;
     int start, q;
     bool samples;
+    int spec;  // draft tokens appended to a decode
   };
   std::vector<Item> items;
   items.reserve(running_.size() + 16);
@@ -219,6 +221,14 @@ StepPlan Scheduler::schedule() {
     int q = std::min(remaining, budget);
     if (cfg_.long_prefill_threshold > 0 && q > 1) q = std::min(q, cfg_.long_prefill_threshold);
     if (!cfg_.chunked_prefill && q < remaining) continue;
+    int spec = 0;
+    if (remaining == 1 && !r.draft.empty()) {
+      // verify drafts: never past the model length or the request's token budget
+      const int room = std::min(cfg_.max_model_len - (int)r.tokens.size(),
+                                r.sp.max_tokens - r.num_output() - 1);
+      spec = std::max(0, std::min({(int)r.draft.size(), budget - 1, room}));
+      q += spec;
+    }
     bool self_preempted = false;
     while (!ensure_blocks(r, r.num_computed + q)) {
       const int64_t victim = running_.back();
@@ -232,7 +242,8 @@ StepPlan Scheduler::schedule() {
       }
     }
     if (self_preempted) break;
-    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size()});
+    items.push_back({&r, r.num_computed, q, r.num_computed + q - spec == (int)r.tokens.size(),
+                     spec});
     budget -= q;
   }
 
@@ -252,7 +263,7 @@ StepPlan Scheduler::schedule() {
       free_slots_.pop_back();
     }
     running_.push_back(r.id);
-    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size()});
+    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size(), 0});
     budget -= q;
   }
 
@@ -263,12 +274,13 @@ StepPlan Scheduler::schedule() {
   int t = 0, s = 0;
   buf_.cu_q[0] = 0;
   last_sample_ids_.clear();
+  last_sample_counts_.clear();
   for (size_t i = 0; i < items.size(); ++i) {
     Item& it = items[i];
     Request& r = *it.r;
     for (int j = 0; j < it.q; ++j) {
       const int pos = it.start + j;
-      buf_.input_ids[t] = r.tokens[pos];
+      buf_.input_ids[t] = j < it.q - it.spec ? r.tokens[pos] : r.draft[j - (it.q - it.spec)];
       buf_.positions[t] = pos;
       buf_.slot_mapping[t] = r.blocks[pos / bs] * bs + pos % bs;
       ++t;
@@ -287,18 +299,32 @@ StepPlan Scheduler::schedule() {
       plan.num_prefill_tokens += it.q;
     }
     if (it.samples) {
-      buf_.logits_idx[s] = t - 1;
-      buf_.temperature[s] = r.sp.temperature;
-      buf_.top_k[s] = r.sp.top_k;
-      buf_.top_p[s] = r.sp.top_p;
-      buf_.min_p[s] = r.sp.min_p;
-      buf_.seeds[s] = r.sp.seed;
-      buf_.steps[s] = r.num_output();
+      // one row per position that predicts a new token: the pending token's position and,
+      // under verification, every draft position
+      for (int j = 0; j <= it.spec; ++j) {
+        buf_.logits_idx[s] = t - 1 - it.spec + j;
+        buf_.temperature[s] = r.sp.temperature;
+        buf_.top_k[s] = r.sp.top_k;
+        buf_.top_p[s] = r.sp.top_p;
+        buf_.min_p[s] = r.sp.min_p;
+        buf_.seeds[s] = r.sp.seed;
+        buf_.steps[s] = r.num_output() + j;  // same noise as without speculation
+        ++s;
+      }
       if (r.sp.temperature > 0.f) plan.all_greedy = false;
       if (r.sp.temperature > 0.f && (r.sp.top_k > 0 || r.sp.top_p < 1.f || r.sp.min_p > 0.f))
         plan.any_filter = true;
       last_sample_ids_.push_back(r.id);
-      ++s;
+      last_sample_counts_.push_back(1 + it.spec);
+      plan.sample_counts.push_back(1 + it.spec);
+    }
+    plan.num_spec_tokens += it.spec;
+    if (it.spec > 0) {
+      r.spec_start = it.start;
+      r.draft.resize(it.spec);  // the drafts under verification
+      spec_proposed_ += it.spec;
+    } else {
+      r.draft.clear();
     }
     r.num_computed = seq_len;
     register_full_blocks(r);
@@ -311,29 +337,52 @@ StepPlan Scheduler::schedule() {
 }
 
 std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, int n) {
-  if (n != (int)last_sample_ids_.size())
-    throw std::runtime_error("scheduler.update: expected " +
-                             std::to_string(last_sample_ids_.size()) + " tokens, got " +
-                             std::to_string(n));
+  int rows = 0;
+  for (int c : last_sample_counts_) rows += c;
+  if (n != rows)
+    throw std::runtime_error("scheduler.update: expected " + std::to_string(rows) +
+                             " sampled rows, got " + std::to_string(n));
   std::vector<std::pair<int64_t, int>> finished;
-  for (int k = 0; k < n; ++k) {
+  int row = 0;
+  for (size_t k = 0; k < last_sample_ids_.size(); ++k) {
+    const int cnt = last_sample_counts_[k];
+    const int64_t* y = sampled + row;
+    row += cnt;
     auto itr = reqs_.find(last_sample_ids_[k]);
     if (itr == reqs_.end()) continue;
     Request& r = itr->second;
     if (r.status != kRunning) continue;  // aborted or preempted while in flight
-    const int32_t tok = (int32_t)sampled[k];
-    r.tokens.push_back(tok);
-    if (r.first_token_step < 0) r.first_token_step = step_;
-    const int out = r.num_output();
+    // tokens this step contributes: accepted drafts, then the token drawn at the first
+    // position whose draft was rejected (or after the last draft)
+    int accept = 0;
+    const int d = cnt - 1;
+    while (accept < d && (int32_t)y[accept] == r.draft[accept]) ++accept;
+    if (d > 0) {
+      spec_accepted_ += accept;
+      // KV is valid for the pending token and the accepted drafts only
+      r.num_computed = r.spec_start + 1 + accept;
+      r.draft.clear();
+      r.spec_start = -1;
+    }
     FinishReason why = kNotFinished;
-    const bool may_stop = out >= r.sp.min_tokens;
-    if (may_stop && !r.sp.ignore_eos && tok == r.sp.eos_id) why = kStop;
-    if (may_stop && why == kNotFinished &&
-        std::find(r.sp.stop_ids.begin(), r.sp.stop_ids.end(), tok) != r.sp.stop_ids.end())
-      why = kStop;
-    if (why == kNotFinished &&
-        (out >= r.sp.max_tokens || (int)r.tokens.size() >= cfg_.max_model_len))
-      why = kLength;
+    for (int j = 0; j <= accept && why == kNotFinished; ++j) {
+      const int32_t tok = (int32_t)y[j];
+      r.tokens.push_back(tok);
+      if (r.first_token_step < 0) r.first_token_step = step_;
+      const int out = r.num_output();
+      const bool may_stop = out >= r.sp.min_tokens;
+      if (may_stop && !r.sp.ignore_eos && tok == r.sp.eos_id) why = kStop;
+      if (may_stop && why == kNotFinished &&
+          std::find(r.sp.stop_ids.begin(), r.sp.stop_ids.end(), tok) != r.sp.stop_ids.end())
+        why = kStop;
+      if (why == kNotFinished &&
+          (out >= r.sp.max_tokens || (int)r.tokens.size() >= cfg_.max_model_len))
+        why = kLength;
+    }
+    if (d > 0) {
+      r.num_computed = std::min(r.num_computed, (int)r.tokens.size() - 1);
+      register_full_blocks(r);
+    }
     if (why != kNotFinished) {
       r.status = kFinished;
       r.reason = why;
@@ -349,7 +398,47 @@ std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, i
                    running_.end());
   }
   last_sample_ids_.clear();
+  last_sample_counts_.clear();
   return finished;
+}
+
+std::vector<int64_t> Scheduler::decode_request_ids() const {
+  std::vector<int64_t> out;
+  for (int64_t id : running_) {
+    const Request& r = reqs_.at(id);
+    if ((int)r.tokens.size() - r.num_computed == 1) out.push_back(id);
+  }
+  return out;
+}
+
+void Scheduler::set_draft(int64_t id, const std::vector<int32_t>& draft) {
+  auto it = reqs_.find(id);
+  if (it == reqs_.end() || it->second.status != kRunning) return;
+  it->second.draft = draft;
+}
+
+int Scheduler::propose_ngram(int k, int n_min, int n_max) {
+  int total = 0;
+  for (int64_t id : running_) {
+    Request& r = reqs_.at(id);
+    r.draft.clear();
+    const int L = (int)r.tokens.size();
+    if (L - r.num_computed != 1 || k <= 0) continue;
+    const int32_t* tk = r.tokens.data();
+    for (int n = std::min(n_max, L - 1); n >= n_min && r.draft.empty(); --n) {
+      // latest earlier occurrence of the last n tokens
+      for (int st = L - n - 1; st >= 0; --st) {
+        if (std::equal(tk + st, tk + st + n, tk + L - n)) {
+          const int from = st + n;
+          const int cnt = std::min(k, L - from);
+          r.draft.assign(tk + from, tk + from + cnt);
+          break;
+        }
+      }
+    }
+    total += (int)r.draft.size();
+  }
+  return total;
 }
 
 std::vector<int32_t> Scheduler::output_tokens(int64_t id) const {

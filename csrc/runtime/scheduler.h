@@ -48,6 +48,8 @@ struct Request {
   FinishReason reason = kNotFinished;
   SamplingCfg sp;
   int32_t state_slot = -1;      // per-request recurrent-state slot (hybrid models)
+  std::vector<int32_t> draft;   // speculative tokens proposed for the next step
+  int spec_start = -1;          // first position of the in-flight verification step
   int64_t first_token_step = -1;
   int64_t finish_step = -1;
   int num_preemptions = 0;
@@ -122,7 +124,9 @@ struct StepPlan {
   int num_preempted = 0;
   bool all_greedy = true;
   bool any_filter = false;  // some row uses top-k / top-p / min-p
+  int num_spec_tokens = 0;  // draft tokens under verification this step
   std::vector<int64_t> sample_req_ids;
+  std::vector<int32_t> sample_counts;  // sampling rows per request (1 + drafts)
 };
 
 class Scheduler {
@@ -132,9 +136,21 @@ class Scheduler {
   bool abort_request(int64_t id);
   // Plan the next step and fill the step buffers.  Returns an empty plan when idle.
   StepPlan schedule();
-  // Append the tokens drawn for the last plan's sampling rows (same order).  Returns the
-  // (id, reason) pairs of the requests that finished; their blocks are already released.
+  // Append the tokens drawn for the last plan's sampling rows (same order).  A request under
+  // speculative verification owns 1 + d consecutive rows (the token drawn at each of its
+  // positions); its drafts are accepted while they equal the drawn token, and the first
+  // mismatch (or the row after the last draft) contributes the drawn token.  With drafts
+  // fixed before sampling this is exact rejection sampling.  Returns the (id, reason) pairs of
+  // the requests that finished; their blocks are already released.
   std::vector<std::pair<int64_t, int>> update(const int64_t* sampled, int n);
+  // Propose up to k draft tokens per running decode request by prompt lookup: the longest
+  // suffix n-gram (n_max down to n_min) that occurred earlier in the request's tokens is
+  // followed by its continuation.  Returns the number of drafts set.
+  int propose_ngram(int k, int n_min, int n_max);
+  void set_draft(int64_t id, const std::vector<int32_t>& draft);
+  std::vector<int64_t> decode_request_ids() const;  // running requests with one token pending
+  int64_t spec_accepted() const { return spec_accepted_; }
+  int64_t spec_proposed() const { return spec_proposed_; }
 
   bool has_unfinished() const { return !waiting_.empty() || !running_.empty(); }
   int num_waiting() const { return (int)waiting_.size(); }
@@ -162,6 +178,8 @@ class Scheduler {
   std::deque<int64_t> waiting_;
   std::vector<int64_t> running_;
   std::vector<int64_t> last_sample_ids_;
+  std::vector<int32_t> last_sample_counts_;
+  int64_t spec_accepted_ = 0, spec_proposed_ = 0;
   std::vector<int32_t> free_slots_;
   void release_slot(Request& r);
   int64_t step_ = 0;

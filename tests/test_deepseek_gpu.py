@@ -49,7 +49,9 @@ def test_tiny_deepseek_logits_track_reference(quant):
     got = llm.engine.runner.logits_log[0][0]
     llm.shutdown()
     ref_cfg = _cfg(torch.float32, None)
-    ref = DeepseekReferenceDecoder(ref_cfg, dict(dummy_weights(ref_cfg, seed=0, std=0.02)))
+    # the engine draws its random weights with the CUDA generator: use the same stream
+    W = {k: v.cpu() for k, v in dummy_weights(ref_cfg, seed=0, std=0.02, device="cuda")}
+    ref = DeepseekReferenceDecoder(ref_cfg, W)
     want = ref.logits(prompt)[-1]
     err = (got - want).abs().max() / want.abs().max()
     assert err < (0.15 if quant else 0.06), float(err)

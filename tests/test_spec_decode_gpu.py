@@ -1,0 +1,37 @@
+"""Speculative decoding on B200 (tiny Llama, bf16): drafts verified in multi-token steps
+(prefill attention kernel) give the same tokens as plain decoding up to bf16 near-ties, and
+verification steps run whole requests' drafts at once."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_oracle_drafts_cut_steps_and_keep_tokens():
+    from vllm_musa_b200 import LLM, SamplingParams
+    from vllm_musa_b200.models.presets import tiny_llama
+    cfg = tiny_llama()
+    cfg.dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (20, 64, 100)]
+    sp = SamplingParams(temperature=0.0, max_tokens=32, ignore_eos=True)
+    kw = dict(block_size=64, seed=0, num_gpu_blocks=64, max_model_len=512, max_num_seqs=8,
+              max_num_batched_tokens=256, enforce_eager=True)
+    plain = [o.outputs[0].token_ids for o in LLM(cfg, **kw).generate(prompts, sp)]
+    llm = LLM(cfg, **kw)
+    eng = llm.engine
+    for i, p in enumerate(prompts):
+        eng.add_request(f"r{i}", p, sp)
+    iids = {eng._by_name[f"r{i}"]: i for i in range(3)}
+    outs = {}
+    while eng.has_unfinished_requests():
+        for iid in eng.scheduler.decode_request_ids():
+            done = len(eng.scheduler.output_tokens(iid))
+            eng.scheduler.set_draft(iid, plain[iids[iid]][done:done + 4])
+        for o in eng.step():
+            outs[o.request_id] = o.outputs[0].token_ids
+    got = [outs[f"r{i}"] for i in range(3)]
+    agree = sum(a == b for x, y in zip(got, plain) for a, b in zip(x, y)) / sum(map(len, plain))
+    assert agree > 0.9, agree
+    assert eng.num_steps < 32  # several tokens accepted per verification step
+    assert eng.scheduler.spec_accepted() > 0

@@ -200,6 +200,24 @@ class ParallelConfig:
 
 
 @dataclass
+class SpeculativeConfig:
+    """Speculative decoding.  ``ngram``: prompt lookup (drafts copied from the continuation of
+    the latest earlier occurrence of the context's suffix n-gram, n in [prompt_lookup_min,
+    prompt_lookup_max]); ``mtp``: the checkpoint's multi-token-prediction layer (DeepSeek)."""
+    method: Optional[str] = None  # None | "ngram" | "mtp"
+    num_speculative_tokens: int = 0
+    prompt_lookup_min: int = 1
+    prompt_lookup_max: int = 4
+
+    @staticmethod
+    def from_dict(d: Optional[dict]) -> "SpeculativeConfig":
+        if not d:
+            return SpeculativeConfig()
+        return SpeculativeConfig(**{k: v for k, v in d.items()
+                                    if k in SpeculativeConfig.__dataclass_fields__})
+
+
+@dataclass
 class EngineConfig:
     model: ModelConfig = field(default_factory=ModelConfig)
     cache: CacheConfig = field(default_factory=CacheConfig)
@@ -212,7 +230,7 @@ class EngineConfig:
     init_std: float = 0.02
     enforce_eager: bool = False
     cuda_graph_sizes: Optional[list] = None
-    speculative_num_tokens: int = 0
+    speculative: SpeculativeConfig = field(default_factory=SpeculativeConfig)
 
     def replace(self, **kw: Any) -> "EngineConfig":
         return dataclasses.replace(self, **kw)

@@ -128,6 +128,7 @@ class LLMEngine:
         self.step_end_times: List[float] = []
         self.stream_outputs = False
         self.num_steps = 0
+        self.drafter = None  # model-based speculative proposer (MTP), set up by the runner
         # multi-process TP without torchrun: the driver broadcasts request ops every step
         self.role = os.environ.get("B200_SPMD_ROLE", "replicated") if st.tp_size > 1 else "single"
         self.sync = None
@@ -208,6 +209,12 @@ class LLMEngine:
                         self._stop = True
             if not self.scheduler.has_unfinished():
                 return []
+        spec = self.config.speculative
+        if spec.method == "ngram" and spec.num_speculative_tokens > 0:
+            self.scheduler.propose_ngram(spec.num_speculative_tokens, spec.prompt_lookup_min,
+                                         spec.prompt_lookup_max)
+        elif spec.method == "mtp" and self.drafter is not None:
+            self.drafter.propose(self.scheduler)
         plan = self.scheduler.schedule()
         if plan.num_reqs == 0:
             return []
@@ -217,12 +224,13 @@ class LLMEngine:
         self.step_end_times.append(now)
         self.num_steps += 1
         outs: List[RequestOutput] = []
+        if self.drafter is not None:
+            self.drafter.after_step(plan, sampled)
         if self.stream_outputs:
-            vals = sampled.tolist()
-            for k, iid in enumerate(plan.sample_req_ids):
+            for iid in plan.sample_req_ids:
                 r = self._reqs.get(iid)
                 if r is not None:
-                    r.tokens.append(vals[k])
+                    r.tokens = list(self.scheduler.output_tokens(iid))
                     if r.first_token_time is None:
                         r.first_token_time = now
             done = {iid for iid, _ in finished}

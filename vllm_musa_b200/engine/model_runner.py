@@ -31,23 +31,25 @@ class StepBuffers:
 
     FIELDS = [("input_ids", "tok", _I32), ("positions", "tok", _I32),
               ("slot_mapping", "tok", _I32), ("cu_q", "req1", _I32), ("seq_lens", "req", _I32),
-              ("block_tables", "bt", _I32), ("logits_idx", "req", _I32),
-              ("temperature", "req", _F32), ("top_k", "req", _I32), ("top_p", "req", _F32),
-              ("min_p", "req", _F32), ("seeds", "req", _I64), ("steps", "req", _I32),
+              ("block_tables", "bt", _I32), ("logits_idx", "smp", _I32),
+              ("temperature", "smp", _F32), ("top_k", "smp", _I32), ("top_p", "smp", _F32),
+              ("min_p", "smp", _F32), ("seeds", "smp", _I64), ("steps", "smp", _I32),
               ("state_slots", "req", _I32)]
+    # sampling rows: one per request, or 1 + drafts under speculative verification; never
+    # more than the step's tokens
 
     def __init__(self, max_tokens: int, max_reqs: int, max_blocks: int, device: torch.device):
         self.max_tokens, self.max_reqs, self.max_blocks = max_tokens, max_reqs, max_blocks
         self.device = device
         pin = device.type == "cuda"
         sizes = {"tok": max_tokens, "req": max_reqs, "req1": max_reqs + 1,
-                 "bt": max_reqs * max_blocks}
+                 "bt": max_reqs * max_blocks, "smp": max(max_tokens, max_reqs)}
         self.h, self.d = {}, {}
         for name, kind, dt in self.FIELDS:
             self.h[name] = torch.zeros(sizes[kind], dtype=dt, pin_memory=pin)
             self.d[name] = self.h[name] if not pin else torch.zeros(sizes[kind], dtype=dt,
                                                                     device=device)
-        self.sampled_h = torch.zeros(max_reqs, dtype=_I64, pin_memory=pin)
+        self.sampled_h = torch.zeros(max(max_tokens, max_reqs), dtype=_I64, pin_memory=pin)
 
     def pointers(self) -> dict:
         p = {name: self.h[name].data_ptr() for name, _, _ in self.FIELDS}

@@ -11,7 +11,8 @@ from __future__ import annotations
 import os
 from typing import List, Optional, Sequence, Union
 
-from ..config import CacheConfig, EngineConfig, ModelConfig, ParallelConfig, SchedulerConfig
+from ..config import (CacheConfig, EngineConfig, ModelConfig, ParallelConfig, SchedulerConfig,
+                      SpeculativeConfig)
 from ..engine.llm_engine import LLMEngine
 from ..models.presets import PRESETS, get_preset
 from ..outputs import RequestOutput
@@ -40,7 +41,7 @@ class LLM:
                  enforce_eager: bool = False, seed: int = 0, load_format: Optional[str] = None,
                  device: str = "cuda", dtype=None, tokenizer=None,
                  cuda_graph_sizes: Optional[list] = None, num_layers: Optional[int] = None,
-                 **unused):
+                 speculative_config: Optional[dict] = None, **unused):
         path = None
         if isinstance(model, ModelConfig):
             mcfg = model
@@ -70,7 +71,8 @@ class LLM:
             parallel=ParallelConfig(tensor_parallel_size=tensor_parallel_size,
                                     enable_expert_parallel=enable_expert_parallel),
             device=device, seed=seed, load_format=load_format, model_path=path,
-            enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes)
+            enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes,
+            speculative=SpeculativeConfig.from_dict(speculative_config))
         tok = tokenizer if tokenizer is not None else _load_tokenizer(path)
         self.executor = None
         if tensor_parallel_size > 1 and "WORLD_SIZE" not in os.environ:

@@ -133,12 +133,19 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
     return out
 
 
+def _fq(x: torch.Tensor) -> torch.Tensor:
+    """x rounded through per-token 1x128 e4m3 quantisation (what the GPU path feeds its GEMMs)."""
+    from .activation import group_quant_fp8
+    q, s = group_quant_fp8(x)
+    return q.float() * s.repeat_interleave(128, 1)
+
+
 def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_offset):
     from .fp8 import dequantize_weight_block
     T, H = x.shape
     I2 = w_gu.shape[0] // E
     out = torch.zeros(T, H, dtype=torch.float32)
-    xf = x.float()
+    xf = _fq(x.to(torch.bfloat16))
     for e in range(E):
         tok, slot = torch.nonzero(ids == e + expert_offset, as_tuple=True)
         if tok.numel() == 0:
@@ -146,9 +153,10 @@ def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_
         gu = dequantize_weight_block(w_gu[e * I2:(e + 1) * I2], s_gu[e * I2 // 128:(e + 1) * I2 // 128])
         dn = dequantize_weight_block(w_down[e * H:(e + 1) * H],
                                      s_down[e * (H // 128):(e + 1) * (H // 128)])
-        hg = xf[tok] @ gu.t()
-        h = F.silu(hg[:, :I2 // 2]) * hg[:, I2 // 2:]
-        out.index_add_(0, tok, (h @ dn.t()) * w[tok, slot].unsqueeze(1).float())
+        hg = (xf[tok] @ gu.t()).to(torch.bfloat16).float()
+        h = _fq((F.silu(hg[:, :I2 // 2]) * hg[:, I2 // 2:]).to(torch.bfloat16))
+        y = (h @ dn.t()).to(torch.bfloat16).float()
+        out.index_add_(0, tok, y * w[tok, slot].unsqueeze(1).float())
     if shared is not None:
         out += shared.float()
     return out.to(x.dtype)

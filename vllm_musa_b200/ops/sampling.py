@@ -33,6 +33,33 @@ def _filter_ref(l: torch.Tensor, k: int, p: float, mp: float) -> torch.Tensor:
     return keep
 
 
+_M64 = (1 << 64) - 1
+
+
+def _mix64(z: torch.Tensor) -> torch.Tensor:
+    """SplitMix64 finaliser on int64 lanes (wrapping arithmetic; logical shifts emulated)."""
+    def srl(x, n):
+        return (x >> n) & ((1 << (64 - n)) - 1)
+
+    def wrap(v):
+        v &= _M64
+        return v - (1 << 64) if v >= (1 << 63) else v
+
+    z = (z ^ srl(z, 30)) * wrap(0xBF58476D1CE4E5B9)
+    z = (z ^ srl(z, 27)) * wrap(0x94D049BB133111EB)
+    return z ^ srl(z, 31)
+
+
+def _keyed_uniform(seed: int, step: int, idx: torch.Tensor) -> torch.Tensor:
+    """U(0,1) noise that is a pure function of (seed, step, global token id): the CPU
+    counterpart of the kernel's counter-based generator, so a token drawn at output index
+    `step` does not depend on batching, chunking, speculation or the vocab split."""
+    key = (seed * 0x9E3779B97F4A7C15 + step * 0xD1B54A32D192ED03) & _M64
+    key = key - (1 << 64) if key >= (1 << 63) else key
+    z = _mix64(idx * 0x2545F4914F6CDD1D + key)
+    return (((z >> 11) & ((1 << 53) - 1)).double() / float(1 << 53)).float()
+
+
 def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor | None = None,
                   top_k: torch.Tensor | None = None, top_p: torch.Tensor | None = None,
                   min_p: torch.Tensor | None = None, seeds: torch.Tensor | None = None,
@@ -64,7 +91,12 @@ def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor | None = None,
         keep = _filter_ref(l, int(top_k[r]) if top_k is not None else 0,
                            float(top_p[r]) if top_p is not None else 1.0,
                            float(min_p[r]) if min_p is not None else 0.0)
-        u = torch.rand(l.shape, generator=generator).clamp(1e-7, 1 - 1e-7)
+        if seeds is not None and steps is not None:
+            idx = torch.arange(l.shape[0], dtype=torch.int64) + vocab_offset
+            u = _keyed_uniform(int(seeds[r]), int(steps[r]), idx)
+        else:
+            u = torch.rand(l.shape, generator=generator)
+        u = u.clamp(1e-7, 1 - 1e-7)
         g = -torch.log(-torch.log(u))
         sc = torch.where(keep, l + g, torch.full_like(l, float("-inf")))
         i = int(torch.argmax(sc))
