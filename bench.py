@@ -16,7 +16,12 @@ on the compute stream; the maximum over ranks is reported.
   e2e       output tokens / CUDA-event time of the LLM.generate() call (host scheduling
             included), with the per-step host->device / device->host byte counts
 
-Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Other BASELINE configurations (same metric, their own model and workload; the default is
+configuration 2):  --config 3  Qwen3-30B-A3B MoE, 128 x 2048 -> 512, experts expert-parallel
+over the GPUs;  --config 5  Qwen3-Next-80B-A3B hybrid, 32 x 32768 -> 512;  --config 4
+DeepSeek-V3.2 (fp8), 64 x 8192 -> 1024 (needs the memory of 8 GPUs).
+
+Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
         torchrun --nproc-per-node N bench.py --gpus N ...
 """
 from __future__ import annotations
@@ -35,20 +40,37 @@ REFERENCE_UNAVAILABLE = (
     "ModuleNotFoundError: No module named 'torchada')")
 
 
+# BASELINE.json configurations 2..5: preset, concurrent requests, input / output lengths
+CONFIGS = {
+    2: dict(model="llama3-8b", requests=256, input=1024, output=256, ep=False),
+    3: dict(model="qwen3-30b-a3b", requests=128, input=2048, output=512, ep=True),
+    4: dict(model="deepseek-v3.2", requests=64, input=8192, output=1024, ep=True),
+    5: dict(model="qwen3-next-80b-a3b", requests=32, input=32768, output=512, ep=False),
+}
+
+
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", default="llama3-8b")
-    ap.add_argument("--num-requests", type=int, default=256)
-    ap.add_argument("--input-len", type=int, default=1024)
-    ap.add_argument("--output-len", type=int, default=256)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--model", default=None)
+    ap.add_argument("--num-requests", type=int, default=None)
+    ap.add_argument("--input-len", type=int, default=None)
+    ap.add_argument("--output-len", type=int, default=None)
     ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
     ap.add_argument("--num-layers", type=int, default=None, help="debug only: fewer layers")
     ap.add_argument("--enforce-eager", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    c = CONFIGS[a.config]
+    a.model = a.model or c["model"]
+    a.num_requests = a.num_requests or c["requests"]
+    a.input_len = a.input_len or c["input"]
+    a.output_len = a.output_len or c["output"]
+    a.ep = c["ep"]
+    return a
 
 
 def main():
@@ -75,7 +97,8 @@ def main():
     llm = LLM(args.model, tensor_parallel_size=args.gpus, max_num_seqs=n_req,
               max_num_batched_tokens=args.max_num_batched_tokens,
               max_model_len=in_len + out_len + 64, block_size=64, seed=0,
-              enforce_eager=args.enforce_eager, num_layers=args.num_layers)
+              enforce_eager=args.enforce_eager, num_layers=args.num_layers,
+              enable_expert_parallel=args.ep and args.gpus > 1)
     eng = llm.engine
     vocab = eng.config.model.vocab_size
     sp = SamplingParams(temperature=1.0, top_p=1.0, max_tokens=out_len, ignore_eos=True)
@@ -151,10 +174,11 @@ def main():
                 "random-init N(0,0.02) weights",
         "config": {"model": eng.config.model.name + (f" ({args.num_layers} layers)" if args.num_layers else ""),
                    "global_batch": n_req, "seq_len": in_len, "output_len": out_len,
-                   "parallelism": f"tp{args.gpus}", "sampling": "temperature 1.0, ignore_eos",
+                   "parallelism": f"tp{args.gpus}" + (f"+ep{args.gpus}" if args.ep and args.gpus > 1 else ""),
+                   "sampling": "temperature 1.0, ignore_eos",
                    "max_num_batched_tokens": args.max_num_batched_tokens,
-                   "l2": "inputs larger than L2: every step streams the 16 GB of weights and the "
-                         "KV cache from HBM"},
+                   "l2": "inputs larger than L2: every step streams the model's weights (GBs) and "
+                         "the KV cache from HBM"},
         "p50_ttft_ms": round(statistics.median(ttfts), 1) if ttfts else None,
         "p50_tpot_ms": round(statistics.median(tpots), 3) if tpots else None,
         "engine_steps_per_step": engine_steps / K,

@@ -1,0 +1,224 @@
+"""Per-kernel timings of the hot sm_100a kernels against the measured roofline.
+
+Each case times one kernel (CUDA events on the launching stream, after warm-up, averaged over
+a back-to-back loop) on inputs larger than L2 (126 MB) or cycling through copies whose total
+exceeds it, and reports achieved bytes/s and FLOP/s with their fractions of the measured
+copy bandwidth / cuBLAS bf16 peak in MEASURED_PEAKS.json ("of measured").
+
+    python benchmarks/kernel_bench.py                 # every case
+    python benchmarks/kernel_bench.py --only gemm_decode,attn_decode --iters 20
+
+The same command with --iters small is what the committed ncu summaries under profiles/ were
+captured on (one kernel, few launches).
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from vllm_musa_b200 import ops  # noqa: E402
+from vllm_musa_b200.ops import _ext  # noqa: E402
+
+L2 = 126 << 20
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"] * 1e9, d["bf16_tflops"] * 1e12
+    return 6.65e12, 1.59e15
+
+
+def timed(fn, iters):
+    for _ in range(3):
+        fn(0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1e3 / iters  # us
+
+
+def copies(make, nbytes):
+    n = max(2, -(-3 * L2 // max(nbytes, 1)))
+    return [make() for _ in range(n)]
+
+
+def report(name, shape, us, nbytes, flops):
+    bw, pk = peaks()
+    rec = {"kernel": name, "shape": shape, "us": round(us, 2),
+           "TBps": round(nbytes / us / 1e6, 3), "TFLOPs": round(flops / us / 1e6, 1),
+           "frac_hbm_of_measured": round(nbytes / (us * 1e-6) / bw, 3),
+           "frac_bf16_of_measured": round(flops / (us * 1e-6) / pk, 3)}
+    print(json.dumps(rec), flush=True)
+
+
+def bf16(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------------------------ cases
+def gemm(M, N, K, iters, name):
+    ws = copies(lambda: bf16(N, K, scale=0.02), N * K * 2)
+    x = bf16(M, K)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    us = timed(lambda i: ops.linear(x, ws[i % len(ws)], out=out), iters)
+    report(name, [M, N, K], us, (M * K + N * K + M * N) * 2, 2 * M * N * K)
+
+
+def case_gemm_decode(it):
+    gemm(256, 28672, 4096, it, "gemm_bf16_decode_gate_up")
+    gemm(256, 4096, 14336, it, "gemm_bf16_decode_down")
+
+
+def case_gemm_prefill(it):
+    gemm(8192, 28672, 4096, it, "gemm_bf16_prefill_gate_up")
+    gemm(8192, 4096, 4096, it, "gemm_bf16_prefill_o")
+
+
+def case_gemm_fp8(it):
+    from vllm_musa_b200.ops import fp8
+    for M, N, K in ((64, 24576, 7168), (4096, 7168, 2048)):
+        mk = lambda: fp8.quantize_weight_block(torch.randn(N, K, device="cuda") * 0.02)  # noqa
+        ws = copies(mk, N * K)
+        xq, xs = fp8.group_quant_fp8(bf16(M, K))
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        us = timed(lambda i: fp8.gemm_fp8(xq, xs, *ws[i % len(ws)], out), it)
+        report("gemm_fp8_block", [M, N, K], us, M * K + N * K + M * N * 2, 2 * M * N * K)
+
+
+def _paged(B, ctx, Hkv, D, bs=64):
+    per = -(-ctx // bs)
+    nblk = B * per
+    k = bf16(nblk, Hkv, bs, D)
+    v = bf16(nblk, Hkv, bs, D)
+    bt = torch.randperm(nblk, device="cuda", dtype=torch.int32).view(B, per)
+    return k, v, bt
+
+
+def case_attn_decode(it):
+    B, ctx, Hq, Hkv, D = 256, 1152, 32, 8, 128
+    k, v, bt = _paged(B, ctx, Hkv, D)
+    q = bf16(B, Hq * D)
+    seq = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq * D, dtype=torch.bfloat16, device="cuda")
+    splits = ops.attention.num_decode_splits(B, Hkv, ctx)
+    ops.attention.decode_workspace(q.device, B, Hq, D, splits)
+    us = timed(lambda i: ops.paged_decode(q, k, v, bt, seq, Hq, Hkv, D ** -0.5, ctx, out=out,
+                                          num_splits=splits), it)
+    report("paged_decode", [B, ctx, Hq, Hkv, D], us, 2 * B * ctx * Hkv * D * 2,
+           4 * B * ctx * Hq * D)
+
+
+def case_attn_prefill(it):
+    R, L, Hq, Hkv, D = 8, 1024, 32, 8, 128
+    k, v, bt = _paged(R, L, Hkv, D)
+    T = R * L
+    qkv = bf16(T, (Hq + 2 * Hkv) * D)
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")
+    seq = torch.full((R,), L, dtype=torch.int32, device="cuda")
+    out = torch.empty(T, Hq * D, dtype=torch.bfloat16, device="cuda")
+    us = timed(lambda i: ops.paged_prefill(qkv, k, v, cu, seq, bt, Hq, Hkv, D ** -0.5,
+                                           out=out), it)
+    report("paged_prefill", [R, L, Hq, Hkv, D], us, (T * (Hq + 2 * Hkv) * D + T * Hq * D) * 2,
+           2 * R * L * L * Hq * D)  # causal: half of 4*L^2*Hq*D
+
+
+def case_mla_decode(it):
+    from vllm_musa_b200.ops import mla
+    B, ctx, H, bs = 64, 8192, 16, 64
+    per = ctx // bs
+    cache = bf16(B * per, bs, 576)
+    bt = torch.randperm(B * per, device="cuda", dtype=torch.int32).view(B, per)
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    seq = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    q_lat, q_pe = bf16(B, H, 512), bf16(B, H, 64)
+    out = torch.empty(B, H, 512, dtype=torch.bfloat16, device="cuda")
+    for sparse in (False, True):
+        idx = None
+        keys = ctx
+        if sparse:
+            keys = 2048
+            idx = torch.stack([torch.randperm(ctx, device="cuda")[:keys] for _ in range(B)]).to(torch.int32)
+        splits = max(1, min(16, 296 // B))
+        ws = (torch.empty(splits * B * H * 512, device="cuda"), torch.empty(splits * B * H, device="cuda"))
+        us = timed(lambda i: mla.mla_attention(q_lat, q_pe, cache, bt, cu, seq, idx, out,
+                                               192 ** -0.5, splits, ws), it)
+        report("mla_decode_sparse2048" if sparse else "mla_decode_dense", [B, keys, H], us,
+               B * keys * 576 * 2, 2 * B * keys * H * (576 + 512))
+
+
+def case_gdn_decode(it):
+    from vllm_musa_b200.ops import gdn
+    B, Hk, Hv = 256, 16, 32
+    state = torch.randn(B, Hv, 128, 128, device="cuda") * 0.01
+    qkv = bf16(B, (2 * Hk + Hv) * 128)
+    ba = bf16(B, 2 * Hv)
+    A, dt = torch.zeros(Hv, device="cuda"), torch.zeros(Hv, device="cuda")
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    seq = torch.full((B,), 100, dtype=torch.int32, device="cuda")
+    slots = torch.arange(B, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hv * 128, dtype=torch.bfloat16, device="cuda")
+    us = timed(lambda i: gdn.gdn_recurrent(qkv, ba, A, dt, state, cu, seq, slots, Hk, Hv, out), it)
+    report("gdn_recurrent_decode", [B, Hk, Hv], us, 2 * B * Hv * 128 * 128 * 4,
+           4 * B * Hv * 128 * 128)
+
+
+def case_moe(it):
+    from vllm_musa_b200.ops import moe
+    T, E, k, H, I = 256, 128, 8, 2048, 768
+    w_gu = bf16(E * 2 * I, H, scale=0.02)
+    w_dn = bf16(E * H, I, scale=0.02)
+    x = bf16(T, H)
+    ids, w = moe.topk_softmax(torch.randn(T, E, device="cuda"), k)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    us = timed(lambda i: moe.fused_moe(x, w_gu, w_dn, ids, w, E, None, out=out), it)
+    report("fused_moe_decode", [T, E, k, H, I], us, (w_gu.numel() + w_dn.numel()) * 2,
+           2 * T * k * 3 * H * I)
+
+
+def case_rmsnorm(it):
+    T, H = 32768, 4096
+    x, r = bf16(T, H), bf16(T, H)
+    w = bf16(H)
+    us = timed(lambda i: ops.fused_add_rms_norm(x, r, w, 1e-5), it)
+    report("fused_add_rms_norm", [T, H], us, 4 * T * H * 2, 0)
+
+
+def case_sample(it):
+    B, V = 256, 128256
+    logits = torch.randn(B, V, device="cuda")
+    t = torch.ones(B, device="cuda")
+    seeds = torch.arange(B, dtype=torch.int64, device="cuda")
+    steps = torch.zeros(B, dtype=torch.int32, device="cuda")
+    us = timed(lambda i: ops.sample_tokens(logits, t, None, None, None, seeds, steps), it)
+    report("gumbel_sample", [B, V], us, B * V * 4, 0)
+
+
+CASES = {n[5:]: f for n, f in globals().items() if n.startswith("case_")}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=",".join(CASES))
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    _ext.require()
+    ops.gemm.reserve_workspace(torch.device("cuda"), 64 << 20)
+    for name in a.only.split(","):
+        CASES[name](a.iters)
+    torch.cuda.synchronize()
+    _ext.check_device_errors()
+
+
+if __name__ == "__main__":
+    main()

@@ -54,4 +54,4 @@ def test_tiny_deepseek_logits_track_reference(quant):
     ref = DeepseekReferenceDecoder(ref_cfg, W)
     want = ref.logits(prompt)[-1]
     err = (got - want).abs().max() / want.abs().max()
-    assert err < (0.15 if quant else 0.06), float(err)
+    assert err < (0.25 if quant else 0.06), float(err)  # fp8: weights and activations rounded
