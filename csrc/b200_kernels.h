@@ -15,7 +15,7 @@ namespace b200 {
 
 // ------------------------------------------------------------------------------- GEMM
 namespace gemm {
-enum Mode : int { kModeStore = 0, kModeSiluMul = 1, kModeF32 = 2 };
+enum Mode : int { kModeStore = 0, kModeSiluMul = 1, kModeF32 = 2, kModeScatter = 3 };
 struct GemmArgs {
   const void* A;  // [M, K] bf16, row stride lda
   int64_t lda;
@@ -32,6 +32,11 @@ struct GemmArgs {
   int* counters;     // split-K per-tile arrival counters (zero-initialised, self-resetting)
   int64_t counters_numel;
   int* err;
+  // kModeScatter (GEMM -> reduce-scatter): output row r belongs to rank o = r / rs_rows and is
+  // stored (bf16, over NVLink when o is a peer) at peers[o] + (rs_rank * rs_rows + r - o *
+  // rs_rows) * ldc: every rank's receive slot holds one rs_rows-row block per source rank.
+  void* peers[8] = {};
+  int rs_rows = 0, rs_rank = 0, rs_world = 0;
 };
 struct GemmPlan {
   int bn, splits;

@@ -77,7 +77,7 @@ B200_DEVICE bool block_barrier(const ArParams& a, int phase, uint32_t epoch) {
 // One row: sum the row over all ranks' staging, add residual, normalise.  VPT vectors of 8
 // bf16 per thread.  Writes residual (if any) and returns normalised values in `o`.
 template <int VPT, bool kNorm>
-B200_DEVICE void reduce_row(const ArParams& a, int row, float (&o)[VPT][8], float* red) {
+B200_DEVICE void reduce_row(const ArParams& a, int row, int r0, float (&o)[VPT][8], float* red) {
   const int nvec = a.H / 8;
   float v[VPT][8];
 #pragma unroll
@@ -85,8 +85,13 @@ B200_DEVICE void reduce_row(const ArParams& a, int row, float (&o)[VPT][8], floa
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
   for (int p = 0; p < a.world; ++p) {
-    const uint4* src = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const __nv_bfloat16*>(a.staging[p]) + (size_t)row * a.H);
+    // peers' staging (row-major [T, H]) or, after an epilogue reduce-scatter, block p of the
+    // local staging slot
+    const __nv_bfloat16* base =
+        a.rs_rows > 0 ? reinterpret_cast<const __nv_bfloat16*>(a.staging[a.rank]) +
+                            ((size_t)p * a.rs_rows + (row - r0)) * a.H
+                      : reinterpret_cast<const __nv_bfloat16*>(a.staging[p]) + (size_t)row * a.H;
+    const uint4* src = reinterpret_cast<const uint4*>(base);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(512) fused_ar_kernel(ArParams a) {
   }
   for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
     float o[VPT][8];
-    reduce_row<VPT, kNorm>(a, row, o, red);
+    reduce_row<VPT, kNorm>(a, row, r0, o, red);
     const int nout = kTwoShot ? a.world : 1;
     for (int q = 0; q < nout; ++q) {
       const int dst_rank = kTwoShot ? (a.rank + q) % a.world : a.rank;
@@ -199,6 +204,8 @@ void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
   B200_REQUIRE(a.world >= 2 && a.world <= kMaxRanks, "custom all-reduce: world size");
   B200_REQUIRE(a.H % 8 == 0 && a.H / 8 <= 1024 * 8, "custom all-reduce: hidden size");
   B200_REQUIRE(a.blocks >= 1 && a.blocks <= kMaxBlocks, "custom all-reduce: block count");
+  B200_REQUIRE(a.rs_rows == 0 || (a.two_shot && a.rs_rows == (a.T + a.world - 1) / a.world),
+               "custom all-reduce: epilogue reduce-scatter needs two-shot with ceil(T/world) rows");
   if (a.T == 0) return;
   const int nvec = a.H / 8;
   int threads = 128;

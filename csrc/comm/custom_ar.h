@@ -25,6 +25,10 @@ struct ArParams {
   const void* weight;              // RMSNorm weight (nullptr: no norm, plain all-reduce)
   float eps;
   int* err;
+  // > 0: the reduce-scatter already happened in the producing GEMM's epilogue (two-shot
+  // only): this rank's staging slot holds `world` blocks of rs_rows rows, block p = rank p's
+  // partial sums of the rows this rank owns, so the reduction reads local memory only.
+  int rs_rows = 0;
 };
 
 void run_fused_allreduce(const ArParams& a, cudaStream_t s);

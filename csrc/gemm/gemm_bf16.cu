@@ -23,6 +23,9 @@
 //   kSiluMul   B rows interleaved in groups of 16 (8 gate rows, 8 up rows); output
 //              C[:, g*8 + c] = silu(acc[g*16 + c]) * acc[g*16 + 8 + c]  (N/2 columns)
 //   kF32       C = acc (fp32, used for logits)
+//   kScatter   C = acc (bf16) stored into the owning rank's receive slot, a peer's memory
+//              reached with plain 16-byte stores over NVLink (the reduce-scatter of a
+//              row-parallel projection rides on the epilogue; see run_bf16)
 // Split-K (any epilogue): units write fp32 partials [splits, M, N]; the CTA that completes an
 // output tile last (per-tile arrival counter) sums them and applies the epilogue, so there is
 // no separate reduce launch.  Launched with programmatic dependent launch: the producer
@@ -48,7 +51,7 @@ constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 226 * 1024;  // dynamic opt-in; leaves room for static smem
 constexpr int kSmemOverhead = 1024 /*align*/ + 512 /*barriers, tmem slot*/;
 
-enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2 };
+enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2, kScatter = 3 };
 
 struct Params {
   int M, N, K;
@@ -66,6 +69,9 @@ struct Params {
   // between launches: the CTA that completes a tile resets it)
   float* ws;
   int* counters;
+  // kScatter: receive slots of every rank (peer VAs), rows per owner, this rank
+  void* peers[8];
+  int rs_rows, rs_rank;
 };
 
 B200_DEVICE void epi_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -106,8 +112,15 @@ B200_DEVICE void store_chunk16(const Params& p, int row, int col, const float (&
     for (int j = 0; j < 8; ++j) o[j] = silu(f[j]) * f[8 + j];
     *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc +
                               col / 2) = pack8(o);
-  } else if constexpr (EPI == kStore) {
-    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col;
+  } else if constexpr (EPI == kStore || EPI == kScatter) {
+    __nv_bfloat16* C;
+    if constexpr (EPI == kScatter) {
+      const int owner = row / p.rs_rows;
+      C = reinterpret_cast<__nv_bfloat16*>(p.peers[owner]) +
+          ((size_t)p.rs_rank * p.rs_rows + (row - owner * p.rs_rows)) * p.ldc + col;
+    } else {
+      C = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col;
+    }
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
       if (col + 8 * v < p.N) {
@@ -376,6 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // peer stores of the scatter epilogue are made visible system-wide before the kernel ends
+  if constexpr (EPI == kScatter) __threadfence_system();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -532,6 +547,8 @@ void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
   p.num_tiles = a.num_tiles;
   p.ws = nullptr;
   p.counters = nullptr;
+  p.rs_rows = p.rs_rank = 0;
+  for (int i = 0; i < 8; ++i) p.peers[i] = nullptr;
   const CUtensorMap ta = make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                                      K, a.max_rows, a.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tb =
@@ -610,6 +627,17 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.num_tiles = nullptr;
   p.ws = nullptr;
   p.counters = nullptr;
+  for (int i = 0; i < 8; ++i) p.peers[i] = a.peers[i];
+  p.rs_rows = a.rs_rows;
+  p.rs_rank = a.rs_rank;
+  if (a.mode == kModeScatter) {
+    B200_REQUIRE(a.rs_world >= 1 && a.rs_world <= 8 && a.rs_rows > 0 &&
+                     (int64_t)a.rs_rows * a.rs_world >= M && a.rs_rank < a.rs_world,
+                 "gemm_bf16 scatter: bad reduce-scatter geometry");
+    for (int i = 0; i < a.rs_world; ++i)
+      B200_REQUIRE(a.peers[i] != nullptr && reinterpret_cast<uintptr_t>(a.peers[i]) % 16 == 0,
+                   "gemm_bf16 scatter: receive slots must be 16-byte aligned");
+  }
   if (p.splits > 1) {
     const int64_t need = (int64_t)p.splits * M * N;
     B200_REQUIRE(a.workspace != nullptr && a.workspace_numel >= need,
@@ -623,6 +651,8 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     dispatch_mt<kStore>(plan.mt, ta, tb, p, stream);
   else if (a.mode == kModeSiluMul)
     dispatch_mt<kSiluMul>(plan.mt, ta, tb, p, stream);
+  else if (a.mode == kModeScatter)
+    dispatch_mt<kScatter>(plan.mt, ta, tb, p, stream);
   else
     dispatch_mt<kF32>(plan.mt, ta, tb, p, stream);
 }

@@ -807,7 +807,7 @@ void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w,
 void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64_t epochs_ptr,
                      int64_t rank, int64_t world, int64_t T, int64_t H, int64_t blocks,
                      int64_t parity, bool two_shot, const c10::optional<Tensor>& residual,
-                     const c10::optional<Tensor>& weight, double eps) {
+                     const c10::optional<Tensor>& weight, double eps, int64_t rs_rows) {
   TORCH_CHECK((int64_t)bufs.size() == 3 * world, "fused_allreduce: buffer table size");
   const c10::cuda::CUDAGuard g(like.device());
   b200::comm::ArParams a{};
@@ -835,8 +835,52 @@ void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64
     a.weight = weight->data_ptr();
   }
   a.eps = eps;
+  a.rs_rows = rs_rows;
   a.err = err_ptr(like);
   guarded([&] { b200::comm::run_fused_allreduce(a, stream_of(like)); });
+}
+
+// Row-parallel GEMM whose epilogue performs the reduce-scatter: C rows go to their owner
+// rank's receive slot (`recv` = every rank's slot address, peers included).
+void gemm_bf16_rs(const Tensor& A, const Tensor& B, const std::vector<int64_t>& recv,
+                  int64_t rs_rows, int64_t rank, int64_t bn, int64_t splits, int64_t mt,
+                  const c10::optional<Tensor>& workspace, const c10::optional<Tensor>& counters) {
+  CHECK_CUDA(A);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  TORCH_CHECK(A.size(1) == B.size(1), "gemm_bf16_rs: K mismatch");
+  TORCH_CHECK(recv.size() >= 1 && recv.size() <= 8, "gemm_bf16_rs: 1..8 ranks");
+  const c10::cuda::CUDAGuard g(A.device());
+  b200::gemm::GemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.C = reinterpret_cast<void*>(recv[rank]);
+  a.ldc = B.size(0);
+  a.M = A.size(0);
+  a.N = B.size(0);
+  a.K = A.size(1);
+  a.mode = b200::gemm::kModeScatter;
+  a.bn = bn;
+  a.splits = splits;
+  a.mt = mt;
+  for (size_t i = 0; i < recv.size(); ++i) a.peers[i] = reinterpret_cast<void*>(recv[i]);
+  a.rs_rows = rs_rows;
+  a.rs_rank = rank;
+  a.rs_world = recv.size();
+  if (workspace.has_value()) {
+    a.workspace = workspace->data_ptr<float>();
+    a.workspace_numel = workspace->numel();
+  }
+  if (counters.has_value()) {
+    a.counters = counters->data_ptr<int>();
+    a.counters_numel = counters->numel();
+  }
+  a.err = err_ptr(A);
+  guarded([&] { b200::gemm::run_bf16(a, stream_of(A)); });
 }
 
 }  // namespace
@@ -955,7 +999,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_max_rows", [](int64_t n, int64_t E) { return (int64_t)b200::moe::align_max_rows(n, E); },
         "rows of the expert-sorted buffer for n assignments over E experts");
   m.def("error_word", &error_word, "per-device error word of the bounded waits");
-  m.def("fused_allreduce", &fused_allreduce, "NVSwitch all-reduce (+ residual + RMSNorm)");
+  m.def("fused_allreduce", &fused_allreduce, "NVSwitch all-reduce (+ residual + RMSNorm)",
+        py::arg("like"), py::arg("bufs"), py::arg("epochs_ptr"), py::arg("rank"),
+        py::arg("world"), py::arg("T"), py::arg("H"), py::arg("blocks"), py::arg("parity"),
+        py::arg("two_shot"), py::arg("residual"), py::arg("weight"), py::arg("eps"),
+        py::arg("rs_rows") = 0);
+  m.def("gemm_bf16_rs", &gemm_bf16_rs,
+        "row-parallel GEMM with the reduce-scatter in its epilogue (NVLink stores)",
+        py::arg("A"), py::arg("B"), py::arg("recv"), py::arg("rs_rows"), py::arg("rank"),
+        py::arg("bn") = 0, py::arg("splits") = 0, py::arg("mt") = 0,
+        py::arg("workspace") = py::none(), py::arg("counters") = py::none());
   m.def("ipc_malloc", [](size_t n) { return (int64_t)reinterpret_cast<uintptr_t>(b200::comm::ipc_malloc(n)); });
   m.def("ipc_free", [](int64_t p) { b200::comm::ipc_free(reinterpret_cast<void*>(p)); });
   m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(b200::comm::ipc_handle(reinterpret_cast<void*>(p))); });

@@ -41,6 +41,17 @@ def test_fused_allreduce_rmsnorm_2gpu(tmp_path):
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_gemm_reduce_scatter_fused_2gpu(tmp_path):
+    out = str(tmp_path / "rs.json")
+    _torchrun(2, ["--mode", "gemm_rs", "--out", out], 29631)
+    res = json.load(open(out))
+    assert any(r["fused"] for r in res)
+    for r in res:
+        if r["fused"]:
+            assert r["dres"] < 0.1 and r["dout"] < 0.15, r
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("eager", [True, False])
 def test_tp2_engine_matches_tp1(tmp_path, eager):
     p1, p2 = str(tmp_path / "tp1"), str(tmp_path / "tp2")

@@ -69,6 +69,55 @@ def mode_ar(out_path):
     dist.destroy_process_group()
 
 
+def mode_gemm_rs(out_path):
+    """Row-parallel GEMM with the reduce-scatter in its tcgen05 epilogue (NVLink stores into
+    the owners' staging slots) + local reduce / residual / RMSNorm / all-gather, against NCCL
+    all-reduce of a plain GEMM."""
+    from vllm_musa_b200 import ops
+    from vllm_musa_b200.parallel.custom_ar import maybe_create_custom_allreduce
+    from vllm_musa_b200.parallel.state import init_distributed
+    world = int(os.environ["WORLD_SIZE"])
+    st = init_distributed(tp_size=world)
+    dev = torch.device("cuda", st.local_rank)
+    H, K = 4096, 1024
+    ar = maybe_create_custom_allreduce(st, dev, max_tokens=2048, hidden=H)
+    assert ar is not None
+    ops.gemm.reserve_workspace(dev, 64 << 20)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    nw = (torch.randn(H, generator=g) * 0.1 + 1).to(torch.bfloat16).to(dev)
+    errs = []
+    for it, T in enumerate([300, 1000, 2048, 77, 513]):
+        ar.begin_forward()
+        gen = torch.Generator(device="cpu").manual_seed(100 * it + st.rank)
+        x = (torch.randn(T, K, generator=gen)).to(torch.bfloat16).to(dev)
+        w = (torch.randn(H, K, generator=gen) * 0.03).to(torch.bfloat16).to(dev)
+        gres = torch.Generator(device="cpu").manual_seed(7 + it)
+        res = torch.randn(T, H, generator=gres).to(torch.bfloat16).to(dev)
+        ref_sum = ops.linear(x, w).float()
+        dist.all_reduce(ref_sum, group=st.tp_group)
+        ref_res = (ref_sum + res.float()).to(torch.bfloat16)
+        ref_out = ops.norm._rms_ref(ref_res, nw, 1e-6, False)
+        fused = ar.can_fuse_gemm(T)
+        r2 = res.clone()
+        out, r2 = ar.linear_allreduce_add_rmsnorm(x, w, r2, nw, 1e-6) if fused else (None, None)
+        torch.cuda.synchronize()
+        if not fused:
+            errs.append({"T": T, "fused": False})
+            continue
+        per = (T + world - 1) // world
+        r0, r1 = min(T, st.rank * per), min(T, st.rank * per + per)
+        dres = (r2[r0:r1].float() - ref_res[r0:r1].float()).abs().max().item() if r1 > r0 else 0.0
+        dout = (out.float() - ref_out.float()).abs().max().item()
+        errs.append({"T": T, "fused": True, "dout": dout, "dres": dres})
+    ops._ext.check_device_errors()
+    ar.close()
+    if st.rank == 0:
+        with open(out_path, "w") as f:
+            json.dump(errs, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def mode_llm(out_path, tp, eager):
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.parallel.state import destroy_distributed, get_parallel_state
@@ -95,12 +144,14 @@ def mode_llm(out_path, tp, eager):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["ar", "llm"], required=True)
+    ap.add_argument("--mode", choices=["ar", "gemm_rs", "llm"], required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
     a = ap.parse_args()
     if a.mode == "ar":
         mode_ar(a.out)
+    elif a.mode == "gemm_rs":
+        mode_gemm_rs(a.out)
     else:
         mode_llm(a.out, a.tp, a.eager)

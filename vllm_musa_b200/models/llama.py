@@ -205,12 +205,19 @@ class DenseDecoderForCausalLM:
             ops.rope_kv(qkv, meta.positions, self.cos_sin, kc, vc, meta.slot_mapping, self.hq,
                         self.hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm, eps)
             a = self.attn.forward(qkv, kc, vc, meta)
-            o = ops.linear(a, L.o_w, out=self.comm.out_buffer(T))
-            x, residual = self.comm.allreduce_add_rmsnorm(o, residual, L.ln2, eps)
-            d = self._mlp(i, L, x, T)
+            x, residual = self.comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
             nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
-            x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
+            x, residual = self._mlp_allreduce(i, L, x, T, residual, nxt, eps)
         return x
+
+    def _mlp_allreduce(self, i, L, x, T, residual, nxt, eps):
+        """MLP + all-reduce + residual + next norm; the dense down projection fuses its
+        reduce-scatter into the GEMM epilogue."""
+        if L.gu_w is not None and L.down_w is not None:
+            act = ops.linear_silu_mul(x, L.gu_w)
+            return self.comm.linear_allreduce_add_rmsnorm(act, L.down_w, residual, nxt, eps)
+        d = self._mlp(i, L, x, T)
+        return self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
 
     def _mlp(self, i: int, L, x: torch.Tensor, T: int) -> torch.Tensor:
         """Dense SwiGLU MLP; returns this rank's partial sum (all-reduced by the caller)."""

@@ -29,6 +29,11 @@ from ..ops import _ext
 log = logging.getLogger("vllm_musa_b200")
 
 ONE_SHOT_MAX_BYTES = int(os.environ.get("B200_AR_ONE_SHOT_MAX_BYTES", str(256 * 1024)))
+FUSE_GEMM_RS = os.environ.get("B200_FUSE_GEMM_RS", "1") == "1"
+
+
+def self_world_pad(st) -> int:
+    return st.tp_size
 
 
 class CustomAllReduce:
@@ -39,7 +44,8 @@ class CustomAllReduce:
         self.device = device
         self.hidden = hidden
         self.max_tokens = max_tokens
-        self.slot = (max_tokens * hidden * 2 + 255) // 256 * 256
+        # rows + world: the epilogue reduce-scatter lays out world blocks of ceil(T/world) rows
+        self.slot = ((max_tokens + self_world_pad(st)) * hidden * 2 + 255) // 256 * 256
         self.flag_off = 4 * self.slot
         total = self.flag_off + mod.comm_flag_bytes()
         self.max_blocks = int(mod.comm_max_blocks())
@@ -105,6 +111,33 @@ class CustomAllReduce:
 
     def allreduce_add_rmsnorm(self, x, residual, weight, eps):
         return self._run(x, residual, weight, eps), residual
+
+    def can_fuse_gemm(self, T: int) -> bool:
+        """Row-parallel GEMM + all-reduce as one reduce-scatter-in-epilogue GEMM and a local
+        reduce + norm + all-gather kernel: used whenever the two-shot algorithm is (larger T)."""
+        return FUSE_GEMM_RS and 0 < T <= self.max_tokens and self._plan(T)[0]
+
+    def linear_allreduce_add_rmsnorm(self, x, w, residual, weight, eps):
+        """residual <- sum_ranks(x @ w^T) + residual; returns (RMSNorm(residual) * weight,
+        residual).  The GEMM epilogue stores each row block straight into its owner's staging
+        slot over NVLink (reduce-scatter fused with the tcgen05 tiles); the all-reduce kernel
+        then reduces local memory only and all-gathers the normalised rows."""
+        from ..ops import gemm as gemm_ops
+        T = x.shape[0]
+        rows = (T + self.world - 1) // self.world
+        recv = self._bufs[self.parity][:self.world]
+        M, N, K = T, w.shape[0], w.shape[1]
+        bn, splits, mt, need = gemm_ops.plan_for(M, N, K)
+        ws = gemm_ops._workspace(x.device, need) if need > 0 else None
+        cnt = gemm_ops._counters(x.device) if need > 0 else None
+        self.mod.gemm_bf16_rs(x, w, recv, rows, self.rank, bn, splits, mt, ws, cnt)
+        _, blocks = self._plan(T)
+        self.mod.fused_allreduce(x, self._bufs[self.parity], self.epochs, self.rank, self.world,
+                                 T, self.hidden, blocks, self.parity, True, residual, weight,
+                                 eps, rows)
+        out = self._out[self.parity][:T]
+        self.parity ^= 1
+        return out, residual
 
     def close(self) -> None:
         for a in self.opened:
