@@ -149,7 +149,7 @@ def case_mla_decode(it):
         if sparse:
             keys = 2048
             idx = torch.stack([torch.randperm(ctx, device="cuda")[:keys] for _ in range(B)]).to(torch.int32)
-        splits = max(1, min(16, 296 // B))
+        splits = mla.choose_splits(B * ((H + 15) // 16), keys)
         ws = (torch.empty(splits * B * H * 512, device="cuda"), torch.empty(splits * B * H, device="cuda"))
         us = timed(lambda i: mla.mla_attention(q_lat, q_pe, cache, bt, cu, seq, idx, out,
                                                192 ** -0.5, splits, ws), it)

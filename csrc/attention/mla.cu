@@ -9,13 +9,13 @@
 // per query token (DeepSeek sparse attention: the indexer's top-k).
 //
 //   mla_prep_kernel       q_pe RoPE in place; c_kv RMSNorm + k_pe RoPE + cache insert.
-//   mla_attn_kernel       grid (query token, 16-head group, KV split).  4 warps; per 64-key tile
+//   mla_attn_kernel       grid (query token, 16-head group, KV split).  8 warps; per 64-key tile
 //                         (cp.async gather through the block table or the index list) warp w
-//                         scores keys 16w..16w+15 for the 16 heads (mma.sync m16n8k16 over the
+//                         scores keys 8w..8w+7 for the 16 heads (mma.sync m16n8k16 over the
 //                         576-wide rows), the tile's scores meet in shared memory for the online
-//                         softmax, and warp w accumulates output columns 128w..128w+127 over
-//                         all 64 keys (the 512-wide fp32 row block is split across warps so it
-//                         stays in registers).  Split partials are merged by mla_combine_kernel.
+//                         softmax, and warp w accumulates output columns 64w..64w+63 over all
+//                         64 keys (the 512-wide fp32 row block is split across warps so it stays
+//                         in registers).  Split partials are merged by mla_combine_kernel.
 //   indexer_k_prep_kernel LayerNorm + RoPE of the indexer key, insert into the index cache.
 //   indexer_score_kernel  score(t, j) = sum_h w[t, h] * relu(q[t, h] . k[j]) for 64 heads x 128
 //                         dims, 64 keys per step, causal prefix only (others -inf).
@@ -40,7 +40,9 @@ constexpr int kLat = 512, kPe = 64, kRow = kLat + kPe;  // 576
 constexpr int kCB = kRow / 64;                          // 9 column blocks of 64 (128 bytes)
 constexpr int kTile = 64;
 constexpr int kHeads = 16;  // heads per CTA (one m16 tile)
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kCols = kLat / kWarps;  // output columns per warp (64)
 constexpr int kQBytes = kCB * kHeads * 128;    // 18 KB
 constexpr int kKBytes = kCB * kTile * 128;     // 72 KB per buffer
 constexpr int kSStride = kTile + 8;            // padded fp32 score row
@@ -205,9 +207,9 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
   }
   cp_async_commit();
 
-  float o[16][4];
+  float o[kCols / 8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
+  for (int i = 0; i < kCols / 8; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[i][j] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
@@ -224,34 +226,28 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
     __syncthreads();  // this tile (and Q) landed
 
     const uint32_t sK = smem_u32(kbuf + buf * kKBytes);
-    // ---- scores of keys 16w .. 16w+15 for the 16 heads
-    float s[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s[nt][j] = 0.f;
+    // ---- scores of keys 8w .. 8w+7 for the 16 heads
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
     {
-      const int tok = warp * 16 + (m8 >> 1) * 8 + r8;
+      // x2: matrices (keys 0-7 of this warp, k chunk c0) and (same keys, chunk c0+1)
+      const int tok = warp * 8 + r8;
 #pragma unroll 4
       for (int ks = 0; ks < kRow / 16; ++ks) {
         const int cb = ks >> 2, c0 = (ks & 3) * 2;
         uint32_t qa[4];
         mma::ldsm_x4(mma::sw128(sQ + cb * (kHeads * 128), (m8 & 1) * 8 + r8, c0 + (m8 >> 1)),
                      qa[0], qa[1], qa[2], qa[3]);
-        uint32_t b0, b1, b2, b3;
-        mma::ldsm_x4(mma::sw128(sK + cb * (kTile * 128), tok, c0 + (m8 & 1)), b0, b1, b2, b3);
-        mma::mma_bf16(s[0], qa, b0, b1);
-        mma::mma_bf16(s[1], qa, b2, b3);
+        uint32_t b0, b1;
+        mma::ldsm_x2(mma::sw128(sK + cb * (kTile * 128), tok, c0 + (m8 & 1)), b0, b1);
+        mma::mma_bf16(s, qa, b0, b1);
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int key = warp * 16 + nt * 8 + 2 * tq + (j & 1);
-        const int row = g + (j >> 1) * 8;
-        sS[row * kSStride + key] = sOff[buf * kTile + key] >= 0 ? s[nt][j] * p.scale_log2 : -INFINITY;
-      }
+    for (int j = 0; j < 4; ++j) {
+      const int key = warp * 8 + 2 * tq + (j & 1);
+      const int row = g + (j >> 1) * 8;
+      sS[row * kSStride + key] = sOff[buf * kTile + key] >= 0 ? s[j] * p.scale_log2 : -INFINITY;
+    }
     __syncthreads();
     // ---- online softmax over the 64-key tile (each warp computes the same row statistics)
     float pv[2][16];
@@ -286,12 +282,12 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
       lrow[rr] = lrow[rr] * corr + sum;
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt) {
+      for (int dt = 0; dt < kCols / 8; ++dt) {
         o[dt][2 * rr] *= corr;
         o[dt][2 * rr + 1] *= corr;
       }
     }
-    // ---- O[:, 128w .. 128w+127] += P(16 x 64) . V(64 x 128), V = c_kv columns of the tile
+    // ---- O[:, 64w .. 64w+63] += P(16 x 64) . V(64 x 64), V = c_kv columns of the tile
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t pa[4];
@@ -301,8 +297,8 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
       pa[3] = pack_bf16x2(pv[1][4 * kk + 2], pv[1][4 * kk + 3]);
       const int tok = kk * 16 + (m8 & 1) * 8 + r8;
 #pragma unroll
-      for (int dn = 0; dn < 8; ++dn) {  // 16-wide column slices of this warp's 128 columns
-        const int col16 = warp * 8 + dn;  // global 16-column slice (0..31)
+      for (int dn = 0; dn < kCols / 16; ++dn) {  // 16-wide column slices of this warp's columns
+        const int col16 = warp * (kCols / 16) + dn;  // global 16-column slice (0..31)
         const int cb = col16 >> 2, cc = (col16 & 3) * 2;
         uint32_t b0, b1, b2, b3;
         mma::ldsm_x4_t(mma::sw128(sK + cb * (kTile * 128), tok, cc + (m8 >> 1)), b0, b1, b2, b3);
@@ -320,17 +316,17 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
     if (h >= p.Hq) continue;
     const float inv = lrow[rr] > 0.f ? 1.f / lrow[rr] : 0.f;
     if (p.splits == 1) {
-      __nv_bfloat16* dst = p.out + (size_t)t * p.o_t + (size_t)h * p.o_h + warp * 128;
+      __nv_bfloat16* dst = p.out + (size_t)t * p.o_t + (size_t)h * p.o_h + warp * kCols;
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt) {
+      for (int dt = 0; dt < kCols / 8; ++dt) {
         const int col = dt * 8 + 2 * tq;
         *reinterpret_cast<uint32_t*>(dst + col) =
             pack_bf16x2(o[dt][2 * rr] * inv, o[dt][2 * rr + 1] * inv);
       }
     } else {
-      float* dst = p.ws_o + (((size_t)split * p.T + t) * p.Hq + h) * kLat + warp * 128;
+      float* dst = p.ws_o + (((size_t)split * p.T + t) * p.Hq + h) * kLat + warp * kCols;
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt) {
+      for (int dt = 0; dt < kCols / 8; ++dt) {
         const int col = dt * 8 + 2 * tq;
         *reinterpret_cast<float2*>(dst + col) =
             make_float2(o[dt][2 * rr] * inv, o[dt][2 * rr + 1] * inv);
@@ -369,6 +365,7 @@ __global__ void mla_combine_kernel(const float* __restrict__ ws_o, const float* 
 
 // --------------------------------------------------------------------------------- indexer
 constexpr int kIdxHeads = 64, kIdxDim = 128, kIdxPe = 64;
+constexpr int kIdxThreads = 128;  // 4 warps x 16 heads
 constexpr int kIdxChunk = 16;  // key tiles (of 64) per CTA
 constexpr int kIdxQBytes = kIdxHeads * kIdxDim * 2;  // 16 KB (2 column blocks)
 constexpr int kIdxKBytes = kTile * kIdxDim * 2;      // 16 KB
@@ -433,7 +430,7 @@ struct IdxParams {
   int64_t ld_s;
 };
 
-__global__ void __launch_bounds__(kThreads) indexer_score_kernel(IdxParams p) {
+__global__ void __launch_bounds__(kIdxThreads) indexer_score_kernel(IdxParams p) {
   pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -454,11 +451,11 @@ __global__ void __launch_bounds__(kThreads) indexer_score_kernel(IdxParams p) {
   float* srow = p.scores + (size_t)t * p.ld_s;
   // positions this CTA owns but that are past the prefix read as -inf
   const int own_end = min((int)p.ld_s, (tile0 + kIdxChunk) * kTile);
-  for (int j = max(tile0 * kTile, tiles * kTile) + tid; j < own_end; j += kThreads) srow[j] = -INFINITY;
+  for (int j = max(tile0 * kTile, tiles * kTile) + tid; j < own_end; j += kIdxThreads) srow[j] = -INFINITY;
   if (tile0 >= tile1) return;
   const int32_t* bt = p.block_tables + (size_t)r * p.bt_stride;
 
-  for (int i = tid; i < kIdxHeads * 16; i += kThreads) {
+  for (int i = tid; i < kIdxHeads * 16; i += kIdxThreads) {
     const int row = i >> 4, w = i & 15, cb = w >> 3, c = w & 7;
     cp_async16(smem + cb * (kIdxHeads * 128) + row * 128 + ((c ^ (row & 7)) << 4),
                p.q + (size_t)t * p.ld_q + row * kIdxDim + cb * 64 + c * 8);
@@ -474,7 +471,7 @@ __global__ void __launch_bounds__(kThreads) indexer_score_kernel(IdxParams p) {
   };
   auto issue = [&](int buf) {
     uint8_t* kb = kbuf + buf * kIdxKBytes;
-    for (int i = tid; i < kTile * 16; i += kThreads) {
+    for (int i = tid; i < kTile * 16; i += kIdxThreads) {
       const int row = i >> 4, w = i & 15, cb = w >> 3, c = w & 7;
       const int64_t off = sOff[buf * kTile + row];
       cp_async16(kb + cb * (kTile * 128) + row * 128 + ((c ^ (row & 7)) << 4),
@@ -694,7 +691,7 @@ void run_indexer_scores(const IndexerArgs& a, cudaStream_t s) {
   p.ld_s = a.ld_s;
   const int chunks = (int)((a.ld_s + kTile * kIdxChunk - 1) / (kTile * kIdxChunk));
   ensure_dynamic_smem(reinterpret_cast<const void*>(indexer_score_kernel), kIdxSmem);
-  indexer_score_kernel<<<dim3(a.T, chunks), kThreads, kIdxSmem, s>>>(p);
+  indexer_score_kernel<<<dim3(a.T, chunks), kIdxThreads, kIdxSmem, s>>>(p);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
 }

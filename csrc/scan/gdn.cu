@@ -9,10 +9,13 @@
 //                      S <- exp(g_t) S;  u = beta_t (v_t - S^T k_t);  S <- S + k_t u^T;
 //                      o_t = S^T q_t
 //                  with q, k L2-normalised (q also scaled by 1/sqrt(dk)), g_t =
-//                  -exp(A_log) softplus(a_t + dt_bias), beta_t = sigmoid(b_t).  One CTA per
-//                  (request, value head); the 128 x 128 fp32 state lives in registers (4
-//                  threads per value column, 32 key rows each) for the whole chunk, tokens are
-//                  staged through shared memory 16 at a time.  Prefill chunks and decode steps
+//                  -exp(A_log) softplus(a_t + dt_bias), beta_t = sigmoid(b_t).  The rows of S
+//                  for different value columns evolve independently, so one CTA owns 32 value
+//                  columns of one (request, value head): four CTAs per head keep several CTAs
+//                  resident per SM (the decode step is a load-update-store of 64 KB of state
+//                  per head).  The state slice lives in registers (4 threads per value column,
+//                  32 key rows each) for the whole chunk; tokens are staged through shared
+//                  memory 16 at a time.  Prefill chunks and decode steps
 //                  use the same kernel; the state slot carries across engine steps.
 // State layout: [slots, Hv, dv, dk] fp32 (value-major, so each thread's 32 key rows are one
 // contiguous 128-byte run).
@@ -28,7 +31,8 @@ namespace b200 {
 namespace gdn {
 
 constexpr int kDK = 128, kDV = 128;
-constexpr int kThreads = 512;  // 128 value columns x 4 key quarters
+constexpr int kVSplit = 4;                   // CTAs per (request, head): 32 value columns each
+constexpr int kThreads = 128;                // 32 value columns x 4 key quarters
 constexpr int kTok = 16;       // tokens staged per round (24 KB of shared memory)
 
 B200_DEVICE int find_req(const int32_t* cu, int R, int t) {
@@ -114,13 +118,14 @@ struct RecParams {
   int R, Hk, Hv;
 };
 
-__global__ void __launch_bounds__(kThreads, 1) gdn_recurrent_kernel(RecParams p) {
+__global__ void __launch_bounds__(kThreads, 4) gdn_recurrent_kernel(RecParams p) {
   pdl_launch_dependents();
-  __shared__ float sq[kTok][kDK], sk[kTok][kDK], sv[kTok][kDV];
+  __shared__ float sq[kTok][kDK], sk[kTok][kDK], sv[kTok][kDV / kVSplit];
   __shared__ float sg[kTok], sb[kTok];
   const int r = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x;
-  const int vcol = tid >> 2, kq = tid & 3;
+  const int vloc = tid >> 2, kq = tid & 3;
+  const int vcol = blockIdx.z * (kDV / kVSplit) + vloc;
   const int warp = tid >> 5, lane = tid & 31;
   const int q0 = p.cu_q[r];
   const int L = p.cu_q[r + 1] - q0;
@@ -167,8 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_recurrent_kernel(RecParams p)
       for (int e = 0; e < 4; ++e) {
         sq[j][lane * 4 + e] = qv[e] * iq;
         sk[j][lane * 4 + e] = kv[e] * ik;
-        sv[j][lane * 4 + e] = bf2f(row[voff + lane * 4 + e]);
       }
+      sv[j][lane] = bf2f(row[voff + blockIdx.z * (kDV / kVSplit) + lane]);
       if (lane == 0) {
         const __nv_bfloat16* ba = p.ba + (size_t)(q0 + base + j) * p.ld_ba;
         const float b = bf2f(ba[h]), a = bf2f(ba[p.Hv + h]);
@@ -190,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_recurrent_kernel(RecParams p)
       }
       dot += __shfl_xor_sync(0xffffffffu, dot, 1);
       dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-      const float u = (sv[j][vcol] - dot) * beta;
+      const float u = (sv[j][vloc] - dot) * beta;
       const float* qq = &sq[j][kq * 32];
       float o = 0.f;
 #pragma unroll
@@ -265,7 +270,7 @@ void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t 
   p.R = R;
   p.Hk = Hk;
   p.Hv = Hv;
-  gdn_recurrent_kernel<<<dim3(R, Hv), kThreads, 0, s>>>(p);
+  gdn_recurrent_kernel<<<dim3(R, Hv, kVSplit), kThreads, 0, s>>>(p);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
 }

@@ -379,7 +379,7 @@ class DeepseekV2ForCausalLM:
             return 1
         groups = T * ((self.hq + 15) // 16)
         keys = self.cfg.index_topk if self.sparse else self.cfg.max_position
-        return max(1, min(8, -(-296 // groups), keys // 256))
+        return mla_ops.choose_splits(groups, keys)
 
     def _ws(self, T: int, splits: int):
         if splits == 1:

@@ -19,6 +19,20 @@ from . import _ext
 LAT, PE = 512, 64
 
 
+def choose_splits(groups: int, max_keys: int, sms: int = 148) -> int:
+    """KV splits for `groups` (query token x 16-head group) CTAs: one CTA per SM, so minimise
+    whole waves per unit of work (ceil(groups * s / sms) / s) plus a small per-split merge cost,
+    keeping at least 256 keys per split."""
+    best, best_cost = 1, None
+    for s in range(1, 17):
+        if s > 1 and max_keys // s < 256:
+            break
+        cost = -(-groups * s // sms) / s + 0.005 * s
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    return best
+
+
 def _rope_gptj(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """x [..., 64] rotated in interleaved pairs (2i, 2i+1) with frequency i."""
     x0, x1 = x[..., 0::2], x[..., 1::2]
