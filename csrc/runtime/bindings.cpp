@@ -67,7 +67,8 @@ void register_runtime(py::module_& m) {
       .def_readonly("any_filter", &StepPlan::any_filter)
       .def_readonly("sample_req_ids", &StepPlan::sample_req_ids)
       .def_readonly("sample_counts", &StepPlan::sample_counts)
-      .def_readonly("num_spec_tokens", &StepPlan::num_spec_tokens);
+      .def_readonly("num_spec_tokens", &StepPlan::num_spec_tokens)
+      .def_readonly("req_ids", &StepPlan::req_ids);
 
   py::class_<Scheduler>(m, "Scheduler")
       .def(py::init([](const SchedulerConfig& c, int num_blocks, py::dict bufs) {
@@ -92,6 +93,8 @@ void register_runtime(py::module_& m) {
            py::arg("n_max") = 4)
       .def("set_draft", &Scheduler::set_draft)
       .def("decode_request_ids", &Scheduler::decode_request_ids)
+      .def("tokens_range", &Scheduler::tokens_range)
+      .def("num_tokens", &Scheduler::num_tokens)
       .def("spec_accepted", &Scheduler::spec_accepted)
       .def("spec_proposed", &Scheduler::spec_proposed)
       .def("prefix_cache_hits", &Scheduler::prefix_cache_hits)

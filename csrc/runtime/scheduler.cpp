@@ -319,6 +319,7 @@ StepPlan Scheduler::schedule() {
       plan.sample_counts.push_back(1 + it.spec);
     }
     plan.num_spec_tokens += it.spec;
+    plan.req_ids.push_back(r.id);
     if (it.spec > 0) {
       r.spec_start = it.start;
       r.draft.resize(it.spec);  // the drafts under verification
@@ -400,6 +401,20 @@ std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, i
   last_sample_ids_.clear();
   last_sample_counts_.clear();
   return finished;
+}
+
+std::vector<int32_t> Scheduler::tokens_range(int64_t id, int start, int n) const {
+  auto it = reqs_.find(id);
+  if (it == reqs_.end()) return {};
+  const auto& t = it->second.tokens;
+  const int a = std::max(0, std::min(start, (int)t.size()));
+  const int b = std::max(a, std::min(start + n, (int)t.size()));
+  return std::vector<int32_t>(t.begin() + a, t.begin() + b);
+}
+
+int Scheduler::num_tokens(int64_t id) const {
+  auto it = reqs_.find(id);
+  return it == reqs_.end() ? 0 : (int)it->second.tokens.size();
 }
 
 std::vector<int64_t> Scheduler::decode_request_ids() const {

@@ -127,6 +127,7 @@ struct StepPlan {
   int num_spec_tokens = 0;  // draft tokens under verification this step
   std::vector<int64_t> sample_req_ids;
   std::vector<int32_t> sample_counts;  // sampling rows per request (1 + drafts)
+  std::vector<int64_t> req_ids;        // every scheduled request, in step-buffer order
 };
 
 class Scheduler {
@@ -149,6 +150,9 @@ class Scheduler {
   int propose_ngram(int k, int n_min, int n_max);
   void set_draft(int64_t id, const std::vector<int32_t>& draft);
   std::vector<int64_t> decode_request_ids() const;  // running requests with one token pending
+  // tokens[start, start + n) of a request (clipped to what exists), and its token count
+  std::vector<int32_t> tokens_range(int64_t id, int start, int n) const;
+  int num_tokens(int64_t id) const;
   int64_t spec_accepted() const { return spec_accepted_; }
   int64_t spec_proposed() const { return spec_proposed_; }
 

@@ -83,3 +83,26 @@ def test_ngram_accepts_drafts_on_repetition():
     assert outs[-1].outputs[0].token_ids == plain[0]
     assert eng.scheduler.spec_accepted() == eng.scheduler.spec_proposed() > 0
     assert eng.num_steps < 24 - 10  # several tokens per step
+
+
+def test_mtp_spec_decode_matches_plain_deepseek():
+    """DeepSeek multi-token prediction: the MTP layer (checkpoint layer num_layers) drafts one
+    token per step from the main model's hidden states; verified outputs equal plain
+    decoding."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_deepseek_cpu import tiny_ds
+    cfg = tiny_ds(True, 128)
+    cfg.num_nextn_predict_layers = 1
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (30, 70)]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    kw = dict(device="cpu", block_size=16, seed=0, num_gpu_blocks=64, max_model_len=128,
+              max_num_seqs=4, max_num_batched_tokens=64)
+    plain = [o.outputs[0].token_ids for o in LLM(cfg, **kw).generate(prompts, sp)]
+    llm = LLM(cfg, speculative_config={"method": "mtp", "num_speculative_tokens": 1}, **kw)
+    outs = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    assert outs == plain
+    assert llm.engine.drafter.proposed > 0
+    assert llm.engine.scheduler.spec_proposed() > 0

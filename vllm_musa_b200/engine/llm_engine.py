@@ -98,6 +98,7 @@ class LLMEngine:
         log.info("weights ready in %.1fs", time.time() - t0)
         self.sampler = Sampler(self.comm, getattr(self.model, "vocab_start", 0), st.tp_size)
         self.runner = ModelRunner(config, self.model, self.sampler, device)
+        self.drafter = None  # model-based speculative proposer (MTP)
         num_blocks = self.runner.profile_and_allocate_kv()
         if st.tp_size > 1:
             # every rank must run with the same block count (lock-step schedulers)
@@ -120,6 +121,9 @@ class LLMEngine:
                              and not hasattr(self.model, "allocate_state"))
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
         self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
+        if config.speculative.method == "mtp":
+            from .spec_decode import MTPDrafter
+            self.drafter = MTPDrafter(self, config.speculative.num_speculative_tokens or 1)
         self.runner.capture_graphs()
         self._ids = itertools.count()
         self._reqs: Dict[int, _Req] = {}
@@ -128,7 +132,6 @@ class LLMEngine:
         self.step_end_times: List[float] = []
         self.stream_outputs = False
         self.num_steps = 0
-        self.drafter = None  # model-based speculative proposer (MTP), set up by the runner
         # multi-process TP without torchrun: the driver broadcasts request ops every step
         self.role = os.environ.get("B200_SPMD_ROLE", "replicated") if st.tp_size > 1 else "single"
         self.sync = None

@@ -99,6 +99,8 @@ class ModelRunner:
         self.num_blocks = 0
         self.tile_scratch = torch.zeros(sc.max_num_seqs + 1, dtype=_I32, device=device)
         self.graphs: dict = {}
+        self.graph_hidden: dict = {}       # hidden-state output of each decode graph
+        self.last_hidden: Optional[torch.Tensor] = None
         self.graph_launches: dict = {}     # our kernels recorded in each decode graph
         self.graph_launches_replayed = 0   # ... summed over replays
         self.graph_pool = None
@@ -196,6 +198,7 @@ class ModelRunner:
                         any_filter: bool, decode_only: bool = False) -> torch.Tensor:
         b = self.buf
         hidden = self.model.forward(b.d["input_ids"][:T], meta, self.kv_caches)
+        self.last_hidden = hidden  # final hidden states of the step (the MTP drafter reads them)
         rows = hidden if decode_only else ops.gather_rows(hidden, b.d["logits_idx"][:S])
         logits = self.model.compute_logits(rows)
         if self.record_logits:
@@ -289,12 +292,14 @@ class ModelRunner:
                                                decode_only=True)
                 self.graph_launches[B] = mod.launch_count() - c0
                 self.graphs[B] = (g, out)
+                self.graph_hidden[B] = self.last_hidden
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
         log.info("captured %d decode CUDA graphs in %.1fs", len(self.graphs), time.time() - t0)
 
     def release_graphs(self) -> None:
         self.graphs.clear()
+        self.graph_hidden.clear()
         self.graph_pool = None
 
     # ------------------------------------------------------------------ step
@@ -333,6 +338,7 @@ class ModelRunner:
             self.h2d_bytes += b.upload(B, B, B, True)
             g, out = self.graphs[B]
             g.replay()
+            self.last_hidden = self.graph_hidden[B][:T]
             self.graph_launches_replayed += self.graph_launches[B]
             ids = out[:S]
         else:

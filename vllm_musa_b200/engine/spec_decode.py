@@ -1,0 +1,90 @@
+"""Model-based speculative proposers.
+
+``MTPDrafter`` drives DeepSeek's multi-token-prediction layer (the checkpoint's layer
+``num_layers``).  After every engine step it runs the MTP layer over each request's positions
+whose next token is now known: position p combines the embedding of token p+1 with the main
+model's final hidden state at p, writes the MTP layer's latent KV for p (same block table and
+slots as the main model), and its logits predict token p+2.  The prediction made at the
+position just before the request's pending token becomes the draft the scheduler verifies in
+the next step (exact acceptance, see csrc/runtime/scheduler.cpp).  Positions of rejected
+drafts are skipped: their main-model KV and hidden states are stale and get overwritten.
+
+Reference counterparts: vllm_musa/v1/spec_decode/utils.py:4-124 (eagle / MTP input
+preparation kernels) and patches/vllm__v1__spec_decode__eagle.patch.py (drafter wiring).
+"""
+from __future__ import annotations
+
+import torch
+
+from ..attention.metadata import AttnMetadata
+
+
+class MTPDrafter:
+    def __init__(self, engine, num_tokens: int = 1):
+        model = engine.model
+        if getattr(model, "mtp", None) is None:
+            raise ValueError("speculative method 'mtp' needs a checkpoint with an MTP layer "
+                             "(num_nextn_predict_layers > 0)")
+        if num_tokens != 1:
+            raise ValueError("the MTP drafter proposes one token per step")
+        self.engine = engine
+        self.model = model
+        self.runner = engine.runner
+        self.proposed = 0
+
+    def propose(self, scheduler) -> None:
+        """Drafts were set right after the previous step; nothing to do before scheduling."""
+
+    @torch.no_grad()
+    def after_step(self, plan, sampled) -> None:
+        sch = self.engine.scheduler
+        b = self.runner.buf
+        h = b.h
+        hidden = self.runner.last_hidden
+        if hidden is None or plan.num_reqs == 0:
+            return
+        cu = h["cu_q"][:plan.num_reqs + 1].tolist()
+        pos_all = h["positions"][:plan.num_tokens]
+        rows, next_ids, cus, lens, req_rows, who = [], [], [0], [], [], []
+        for i, rid in enumerate(plan.req_ids):
+            n_tok = sch.num_tokens(rid)
+            if n_tok == 0:
+                continue  # finished and forgotten
+            start = int(pos_all[cu[i]])
+            q = cu[i + 1] - cu[i]
+            last = min(start + q - 1, n_tok - 2)  # positions whose next token is known
+            if last < start:
+                continue
+            nxt = sch.tokens_range(rid, start + 1, last - start + 1)
+            rows.extend(range(cu[i], cu[i] + (last - start + 1)))
+            next_ids.extend(nxt)
+            cus.append(cus[-1] + len(nxt))
+            lens.append(last + 1)
+            req_rows.append(i)
+            who.append((rid, last == n_tok - 2))
+        if not rows:
+            return
+        dev = hidden.device
+        rows_t = torch.tensor(rows, dtype=torch.long, device=dev)
+        T = len(rows)
+        ids = torch.tensor(next_ids, dtype=torch.int32, device=dev)
+        positions = b.d["positions"][:plan.num_tokens][rows_t].contiguous()
+        slots = b.d["slot_mapping"][:plan.num_tokens][rows_t].contiguous()
+        rr = torch.tensor(req_rows, dtype=torch.long, device=dev)
+        bt = b.bt2d()[:plan.num_reqs][rr].contiguous()
+        cu_t = torch.tensor(cus, dtype=torch.int32, device=dev)
+        sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+        R = len(req_rows)
+        meta = AttnMetadata(T, 0, R, positions, slots, sl, bt, cu_t, max_seq_len=max(lens),
+                            tile_scratch=self.runner.tile_scratch,
+                            state_slots=b.d["state_slots"][:R])
+        prev = hidden[rows_t]
+        cache = self.runner.kv_caches[self.model.cfg.num_layers]
+        x = self.model.forward_mtp(ids, prev, meta, cache)
+        last_rows = torch.tensor([c - 1 for c in cus[1:]], dtype=torch.long, device=dev)
+        logits = self.model.compute_logits_mtp(x[last_rows])
+        draft = self.runner.sampler(logits, None, None, None, None, None, None).cpu().tolist()
+        for k, (rid, ready) in enumerate(who):
+            if ready:
+                sch.set_draft(rid, [int(draft[k])])
+                self.proposed += 1

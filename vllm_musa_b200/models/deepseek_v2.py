@@ -62,7 +62,9 @@ class Lin:
 class _Layer:
     __slots__ = ("ln1", "ln2", "w_a", "q_a_norm", "kv_a_norm", "w_qb", "w_kb", "w_vb", "o", "idx_ln_w",
                  "idx_ln_b", "gu", "down", "router_w", "router_bias", "experts_gu", "experts_gu_s",
-                 "experts_down", "experts_down_s", "shared_gu", "shared_down")
+                 "experts_down", "experts_down_s", "shared_gu", "shared_down",
+                 # multi-token-prediction layer only
+                 "enorm", "hnorm", "eh_proj", "head_norm", "head")
 
     def __init__(self):
         for s in self.__slots__:
@@ -126,6 +128,9 @@ class DeepseekV2ForCausalLM:
             self.scale *= m * m
         self._staging = defaultdict(dict)
         self._mla_ws = None
+        # DeepSeek multi-token prediction: checkpoint layer index num_layers (loaded if present)
+        self.mtp: Optional[_Layer] = None
+        self._mtp_staging: dict = {}
 
     # ------------------------------------------------------------------ weights
     def _to(self, t):
@@ -336,8 +341,13 @@ class DeepseekV2ForCausalLM:
                 if not m:
                     continue
                 i, key = int(m.group(1)), m.group(2)
+                if i == cfg.num_layers and cfg.num_nextn_predict_layers > 0:
+                    if self._wanted(i, key) and key != "embed_tokens.weight":
+                        self._mtp_staging[key] = w
+                        self._try_finalize_mtp()
+                    continue
                 if i >= cfg.num_layers or not self._wanted(i, key):
-                    continue  # (MTP layers beyond num_layers are loaded by the drafter)
+                    continue
                 self._staging[i][key] = w
                 self._try_finalize(i)
         if cfg.tie_word_embeddings and self.lm_head is None and self.embed is not None:
@@ -346,11 +356,56 @@ class DeepseekV2ForCausalLM:
         if missing or self.embed is None or self.final_norm is None or self.lm_head is None:
             raise RuntimeError(f"incomplete checkpoint: layers {missing[:8]}")
         self._staging.clear()
+        self._mtp_staging = {}
+
+    def _try_finalize_mtp(self):
+        st = self._mtp_staging
+        i = self.cfg.num_layers
+        need = ["enorm.weight", "hnorm.weight", "eh_proj.weight", "shared_head.norm.weight",
+                "shared_head.head.weight", "input_layernorm.weight",
+                "post_attention_layernorm.weight"] + self._attn_keys() + self._mlp_keys(i)
+        if self.mtp is not None or not all(k in st for k in need) or \
+                any(self._needs_scale(st, k) for k in need):
+            return
+        L = _Layer()
+        self._finalize_attention(L, st)
+        self._finalize_mlp(i, L, st)
+        L.ln1 = self._to(st["input_layernorm.weight"])
+        L.ln2 = self._to(st["post_attention_layernorm.weight"])
+        L.enorm = self._to(st["enorm.weight"])
+        L.hnorm = self._to(st["hnorm.weight"])
+        L.eh_proj = self._lin(*self._raw(st, "eh_proj"))
+        L.head_norm = self._to(st["shared_head.norm.weight"])
+        L.head = self._to(shard_rows(st["shared_head.head.weight"], self.rank, self.tp))
+        self.mtp = L
+        self._mtp_staging = {}
+
+    def forward_mtp(self, next_ids, prev_hidden, meta, cache):
+        """One multi-token-prediction step: position p combines the embedding of token p+1
+        with the main model's final hidden state at p, runs the MTP decoder layer (own latent
+        cache, same block tables), and returns hidden states whose logits predict token p+2."""
+        L, eps = self.mtp, self.cfg.rms_norm_eps
+        T = next_ids.shape[0]
+        self.comm.begin_forward()
+        e = ops.rms_norm(ops.embedding(next_ids, self.embed), L.enorm, eps)
+        hp = ops.rms_norm(prev_hidden, L.hnorm, eps)
+        x = L.eh_proj(torch.cat([e, hp], -1).contiguous())
+        residual = x
+        x = ops.rms_norm(x, L.ln1, eps)
+        a = self._attention(L, x, meta, cache, T)
+        o = L.o(a, out=self.comm.out_buffer(T))
+        x, residual = self.comm.allreduce_add_rmsnorm(o, residual, L.ln2, eps)
+        d = self._mlp(self.cfg.num_layers, L, x, T)
+        x, residual = self.comm.allreduce_add_rmsnorm(d, residual, L.head_norm, eps)
+        return x
+
+    def compute_logits_mtp(self, hidden):
+        return ops.linear(hidden, self.mtp.head, out_dtype=torch.float32)
 
     def linear_shapes(self):
         """(N, K) of the bf16 GEMMs (split-K workspace planning)."""
         out = {tuple(self.lm_head.shape)}
-        for L in self.layers:
+        for L in self.layers + ([self.mtp] if self.mtp is not None else []):
             for lin in (L.w_a, L.w_qb, L.o, L.gu, L.down, L.shared_gu, L.shared_down):
                 if lin is not None and not lin.fp8:
                     out.add(tuple(lin.w.shape))
@@ -364,10 +419,12 @@ class DeepseekV2ForCausalLM:
     def kv_bytes_per_block(self, block_size: int) -> int:
         elt = torch.tensor([], dtype=self.dtype).element_size()
         per = 576 + (self.idx_dim if self.sparse else 0)
-        return self.cfg.num_layers * block_size * per * elt
+        n = self.cfg.num_layers + (1 if self.mtp is not None else 0)
+        return n * block_size * per * elt
 
     def allocate_kv_cache(self, num_blocks: int, block_size: int) -> list:
-        n = self.cfg.num_layers
+        """One latent (+ index) cache per layer, plus one for the MTP layer when loaded."""
+        n = self.cfg.num_layers + (1 if self.mtp is not None else 0)
         lat = torch.zeros(n, num_blocks, block_size, 576, dtype=self.dtype, device=self.device)
         idx = torch.zeros(n, num_blocks, block_size, self.idx_dim, dtype=self.dtype,
                           device=self.device) if self.sparse else None

@@ -89,12 +89,19 @@ def hf_param_shapes(cfg: ModelConfig) -> list:
 
 
 def _deepseek_shapes(cfg: ModelConfig) -> list:
-    """DeepSeek-V2/V3/V3.2 HF names (MLA, optional lightning indexer, grouped MoE)."""
+    """DeepSeek-V2/V3/V3.2 HF names (MLA, optional lightning indexer, grouped MoE, and the
+    multi-token-prediction layer at index num_layers)."""
     H, V, Hq = cfg.hidden_size, cfg.vocab_size, cfg.num_heads
     nope, rope, vd = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
     out = []
-    for i in range(cfg.num_layers):
+    n_mtp = 1 if cfg.num_nextn_predict_layers > 0 else 0
+    for i in range(cfg.num_layers + n_mtp):
         p = f"model.layers.{i}."
+        if i == cfg.num_layers:
+            out += [(p + "enorm.weight", (H,), "norm"), (p + "hnorm.weight", (H,), "norm"),
+                    (p + "eh_proj.weight", (H, 2 * H), "w"),
+                    (p + "shared_head.norm.weight", (H,), "norm"),
+                    (p + "shared_head.head.weight", (V, H), "w")]
         a = p + "self_attn."
         out.append((p + "input_layernorm.weight", (H,), "norm"))
         if cfg.q_lora_rank:
