@@ -97,3 +97,9 @@ def test_rope_rotate_only_cpu_matches_reference():
     torch.testing.assert_close(a[:, :Hq * D], q.reshape(T, -1))
     torch.testing.assert_close(a[:, Hq * D:(Hq + Hk) * D], k.reshape(T, -1))
     torch.testing.assert_close(a[:, (Hq + Hk) * D:], qkv[:, (Hq + Hk) * D:])
+
+
+def test_custom_op_preload_list_imports():
+    from vllm_musa_b200 import plugin
+    assert "vllm_musa_b200.ops" in plugin.CUSTOM_OP_MODULES
+    plugin.preload_custom_op_modules()

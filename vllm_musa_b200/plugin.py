@@ -104,6 +104,22 @@ def make_custom_op_classes():
     return B200SiluAndMul, B200RotaryEmbedding
 
 
+# Modules that register torch.ops.b200.* and the IR providers; they must be imported before
+# vLLM traces or compiles a model so the ops exist in every process (workers included).
+# Reference counterpart: vllm_musa/custom_op_modules.py:5-27.
+CUSTOM_OP_MODULES = ("vllm_musa_b200.ops", "vllm_musa_b200.ir_providers")
+
+
+def preload_custom_op_modules() -> None:
+    import importlib
+    for name in CUSTOM_OP_MODULES:
+        importlib.import_module(name)
+    import torch
+    from .ops import _ext
+    if torch.cuda.is_available():
+        _ext.ops()  # load the extension: registers torch.ops.b200.*
+
+
 def register_custom_ops() -> None:
     global _REGISTERED
     if _REGISTERED:
@@ -114,6 +130,7 @@ def register_custom_ops() -> None:
     except Exception as e:  # vLLM not importable: nothing to register into
         log.info("vLLM not available, skipping plugin registration: %s", e)
         return
+    preload_custom_op_modules()
     register_ir_providers(ir)
     silu, rope = make_custom_op_classes()
     CustomOp.register_oot(silu, name="SiluAndMul")
