@@ -297,4 +297,32 @@ void run_gather_rows(void* out, const void* in, int64_t ld_in, const int32_t* id
                      int elem_bytes, cudaStream_t s);
 }  // namespace misc
 
+namespace ep {
+// Expert-parallel all-to-all (csrc/comm/ep_a2a.cu).  Pointer arrays hold every rank's address
+// of the same buffer (peer VAs from CUDA IPC).
+struct A2AParams {
+  int rank, world;
+  int Tc, row0;      // this rank's shard: rows [row0, row0 + Tc) of x
+  int H, k, E_local;
+  int cap;           // receive rows per source rank
+  int rs_rows;       // rows per block of the all-reduce staging slot (= ceil(T / world))
+  const void* x;     // [T, H] bf16 hidden states (replicated)
+  int64_t ldx;
+  const int32_t* ids;  // [Tc, k] global expert ids of the shard tokens
+  const float* w;      // [Tc, k] routing weights
+  int* send_cnt;       // [world] local counters (zero between calls)
+  void* recv_x[8];         // [world * cap, H] bf16
+  int32_t* recv_ids[8];    // [world * cap, k] local expert ids (-1: not served here)
+  float* recv_w[8];        // [world * cap, k]
+  int32_t* recv_tok[8];    // [world * cap] shard row of the token at its source
+  int32_t* recv_cnt[8];    // [world] rows received from each source
+  uint32_t* flags[8];      // [kMaxRanks] arrival epochs
+  uint32_t* epoch;         // local call counter
+  void* staging[8];        // all-reduce staging slots (this call's parity)
+  int* err;
+};
+void run_dispatch(const A2AParams& p, cudaStream_t s);
+void run_return(const A2AParams& p, const void* y, const int32_t* pos, cudaStream_t s);
+}  // namespace ep
+
 }  // namespace b200

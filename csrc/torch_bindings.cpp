@@ -840,6 +840,70 @@ void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64
   guarded([&] { b200::comm::run_fused_allreduce(a, stream_of(like)); });
 }
 
+// Expert-parallel all-to-all: `ints` = [rank, world, Tc, row0, H, k, E_local, cap, rs_rows];
+// `ptrs` = [send_cnt, epoch, then per rank (world entries each): recv_x, recv_ids, recv_w,
+// recv_tok, recv_cnt, flags, staging].
+static b200::ep::A2AParams a2a_params(const Tensor& like, const std::vector<int64_t>& ints,
+                                      const std::vector<int64_t>& ptrs) {
+  TORCH_CHECK(ints.size() == 9, "ep a2a: 9 integer parameters");
+  b200::ep::A2AParams p{};
+  p.rank = ints[0];
+  p.world = ints[1];
+  p.Tc = ints[2];
+  p.row0 = ints[3];
+  p.H = ints[4];
+  p.k = ints[5];
+  p.E_local = ints[6];
+  p.cap = ints[7];
+  p.rs_rows = ints[8];
+  TORCH_CHECK(p.world >= 1 && p.world <= 8 && (int64_t)ptrs.size() == 2 + 7 * p.world,
+              "ep a2a: pointer table size");
+  p.send_cnt = reinterpret_cast<int*>(ptrs[0]);
+  p.epoch = reinterpret_cast<uint32_t*>(ptrs[1]);
+  for (int r = 0; r < p.world; ++r) {
+    p.recv_x[r] = reinterpret_cast<void*>(ptrs[2 + r]);
+    p.recv_ids[r] = reinterpret_cast<int32_t*>(ptrs[2 + p.world + r]);
+    p.recv_w[r] = reinterpret_cast<float*>(ptrs[2 + 2 * p.world + r]);
+    p.recv_tok[r] = reinterpret_cast<int32_t*>(ptrs[2 + 3 * p.world + r]);
+    p.recv_cnt[r] = reinterpret_cast<int32_t*>(ptrs[2 + 4 * p.world + r]);
+    p.flags[r] = reinterpret_cast<uint32_t*>(ptrs[2 + 5 * p.world + r]);
+    p.staging[r] = reinterpret_cast<void*>(ptrs[2 + 6 * p.world + r]);
+  }
+  p.err = err_ptr(like);
+  return p;
+}
+
+void ep_dispatch(const Tensor& x, const Tensor& ids, const Tensor& w,
+                 const std::vector<int64_t>& ints, const std::vector<int64_t>& ptrs) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  TORCH_CHECK(x.stride(1) == 1, "ep_dispatch: row-major x");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && w.scalar_type() == at::kFloat &&
+                  w.is_contiguous(),
+              "ep_dispatch: int32 ids / fp32 weights [Tc, k]");
+  auto p = a2a_params(x, ints, ptrs);
+  TORCH_CHECK(ids.size(0) >= p.Tc && ids.size(1) == p.k && x.size(1) == p.H, "ep_dispatch: shapes");
+  p.x = x.data_ptr();
+  p.ldx = x.stride(0);
+  p.ids = ids.data_ptr<int32_t>();
+  p.w = w.data_ptr<float>();
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] { b200::ep::run_dispatch(p, stream_of(x)); });
+}
+
+void ep_return(const Tensor& y, const Tensor& pos, const std::vector<int64_t>& ints,
+               const std::vector<int64_t>& ptrs) {
+  CHECK_CUDA(y);
+  CHECK_BF16(y);
+  TORCH_CHECK(y.is_contiguous() && pos.scalar_type() == at::kInt && pos.is_contiguous(),
+              "ep_return: contiguous y, int32 pos");
+  auto p = a2a_params(y, ints, ptrs);
+  TORCH_CHECK(y.size(1) == p.H && pos.size(0) == (int64_t)p.world * p.cap && pos.size(1) == p.k,
+              "ep_return: shapes");
+  const c10::cuda::CUDAGuard g(y.device());
+  guarded([&] { b200::ep::run_return(p, y.data_ptr(), pos.data_ptr<int32_t>(), stream_of(y)); });
+}
+
 // Row-parallel GEMM whose epilogue performs the reduce-scatter: C rows go to their owner
 // rank's receive slot (`recv` = every rank's slot address, peers included).
 void gemm_bf16_rs(const Tensor& A, const Tensor& B, const std::vector<int64_t>& recv,
@@ -1004,6 +1068,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("world"), py::arg("T"), py::arg("H"), py::arg("blocks"), py::arg("parity"),
         py::arg("two_shot"), py::arg("residual"), py::arg("weight"), py::arg("eps"),
         py::arg("rs_rows") = 0);
+  m.def("ep_dispatch", &ep_dispatch, "expert-parallel dispatch over NVLink (+ count exchange)");
+  m.def("ep_return", &ep_return, "expert-parallel combine into the sources' staging slots");
   m.def("gemm_bf16_rs", &gemm_bf16_rs,
         "row-parallel GEMM with the reduce-scatter in its epilogue (NVLink stores)",
         py::arg("A"), py::arg("B"), py::arg("recv"), py::arg("rs_rows"), py::arg("rank"),

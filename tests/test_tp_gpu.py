@@ -41,6 +41,25 @@ def test_fused_allreduce_rmsnorm_2gpu(tmp_path):
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("eager", [True, False])
+def test_moe_ep2_all_to_all_matches_tp1(tmp_path, eager):
+    """Qwen3-MoE with expert parallelism over 2 GPUs through the NVSwitch all-to-all
+    (dispatch / grouped experts / return into the staging blocks / local-source reduce)."""
+    p1, p2 = str(tmp_path / "m1"), str(tmp_path / "m2")
+    extra = ["--eager"] if eager else []
+    _torchrun(1, ["--mode", "llm", "--model", "moe", "--out", p1, "--tp", "1"] + extra, 29641)
+    _torchrun(2, ["--mode", "llm", "--model", "moe", "--ep", "--out", p2, "--tp", "2"] + extra,
+              29651)
+    a = json.load(open(p1 + ".0"))
+    b0, b1 = json.load(open(p2 + ".0")), json.load(open(p2 + ".1"))
+    assert b0["tokens"] == b1["tokens"], "EP ranks diverged"
+    la, lb = torch.tensor(a["logits0"]), torch.tensor(b0["logits0"])
+    assert (la - lb).abs().max().item() < 0.05
+    same_first = sum(x[0] == y[0] for x, y in zip(a["tokens"], b0["tokens"]))
+    assert same_first >= 3
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
 def test_gemm_reduce_scatter_fused_2gpu(tmp_path):
     out = str(tmp_path / "rs.json")
     _torchrun(2, ["--mode", "gemm_rs", "--out", out], 29631)

@@ -118,12 +118,25 @@ def mode_gemm_rs(out_path):
     dist.destroy_process_group()
 
 
-def mode_llm(out_path, tp, eager):
+def moe_cfg():
+    from vllm_musa_b200.config import ModelConfig
+    return ModelConfig(arch="qwen3_moe", vocab_size=4096, hidden_size=1024, num_layers=3,
+                       num_heads=16, num_kv_heads=4, head_dim=64, intermediate_size=2816,
+                       rms_norm_eps=1e-6, rope_theta=1e4, max_position=2048, qk_norm=True,
+                       num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
+                       name="tp-moe-test")
+
+
+def mode_llm(out_path, tp, eager, model="dense", ep=False):
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.parallel.state import destroy_distributed, get_parallel_state
-    llm = LLM(small_cfg(), tensor_parallel_size=tp, block_size=64, seed=0, num_gpu_blocks=256,
+    cfg = moe_cfg() if model == "moe" else small_cfg()
+    llm = LLM(cfg, tensor_parallel_size=tp, block_size=64, seed=0, num_gpu_blocks=256,
               max_model_len=1024, max_num_seqs=16, max_num_batched_tokens=1024,
-              enforce_eager=eager, cuda_graph_sizes=[1, 2, 4, 8, 16])
+              enforce_eager=eager, cuda_graph_sizes=[1, 2, 4, 8, 16],
+              enable_expert_parallel=ep)
+    if ep and tp > 1:
+        assert llm.engine.comm.ep_a2a is not None, "EP all-to-all did not initialise"
     llm.engine.runner.record_logits = True
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (7, 100, 300, 64)]
@@ -136,6 +149,8 @@ def mode_llm(out_path, tp, eager):
         first = torch.cat(parts, dim=1)
     res = {"tokens": [o.outputs[0].token_ids for o in outs], "logits0": first.cpu().tolist(),
            "rank": st.rank}
+    ops_ext = __import__("vllm_musa_b200.ops._ext", fromlist=["check_device_errors"])
+    ops_ext.check_device_errors()
     with open(f"{out_path}.{st.rank}", "w") as f:
         json.dump(res, f)
     llm.shutdown()
@@ -148,10 +163,12 @@ if __name__ == "__main__":
     ap.add_argument("--out", required=True)
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--model", default="dense")
+    ap.add_argument("--ep", action="store_true")
     a = ap.parse_args()
     if a.mode == "ar":
         mode_ar(a.out)
     elif a.mode == "gemm_rs":
         mode_gemm_rs(a.out)
     else:
-        mode_llm(a.out, a.tp, a.eager)
+        mode_llm(a.out, a.tp, a.eager, a.model, a.ep)

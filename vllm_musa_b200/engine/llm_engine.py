@@ -83,6 +83,12 @@ class LLMEngine:
                     st, device, max_tokens=config.scheduler.max_num_batched_tokens,
                     hidden=mcfg.hidden_size)
             self.comm = TPCommunicator(st, device, custom)
+            if custom is not None and st.ep_size > 1 and mcfg.num_experts and \
+                    mcfg.num_experts % st.ep_size == 0:
+                from ..parallel.ep_a2a import maybe_create_ep_a2a
+                self.comm.ep_a2a = maybe_create_ep_a2a(
+                    st, device, custom, config.scheduler.max_num_batched_tokens,
+                    mcfg.hidden_size, mcfg.num_experts_per_tok, mcfg.num_experts // st.ep_size)
             st.comm = self.comm
         else:
             self.comm = LocalCommunicator(device)

@@ -86,6 +86,26 @@ class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
                 st["mlp.shared_expert.gate_proj.weight"], st["mlp.shared_expert.up_proj.weight"],
                 st["mlp.shared_expert.down_proj.weight"])
 
+    def _mlp_allreduce(self, i, L, x, T, residual, nxt, eps):
+        """MoE layers under expert parallelism with the NVSwitch all-to-all: route this rank's
+        token shard, dispatch / experts / return into the owners' staging blocks, then the
+        local-source two-shot reduce (+ residual, norm, all-gather).  Layers with a
+        (tensor-sharded) shared expert keep the replicated-token path."""
+        a2a = getattr(self.comm, "ep_a2a", None)
+        if not (self._is_moe(i) and self.ep and a2a is not None and x.is_cuda and
+                L.shared_gu is None and a2a.can_run(T)):
+            return super()._mlp_allreduce(i, L, x, T, residual, nxt, eps)
+        per = (T + self.tp - 1) // self.tp
+        r0 = min(T, self.rank * per)
+        xs = x[r0:min(T, r0 + per)]
+        logits = ops.linear(xs, L.router_w, out_dtype=torch.float32)
+        ids, w = moe_ops.topk_softmax(logits[:, :self.E], self.topk, self.cfg.norm_topk_prob)
+
+        def experts(rx, rids):
+            return moe_ops.moe_experts(rx, L.experts_gu, L.experts_down, rids, self.E_local)
+
+        return a2a.moe_allreduce_add_rmsnorm(x, ids, w, experts, None, residual, nxt, eps)
+
     def _mlp(self, i, L, x, T):
         if not self._is_moe(i):
             return super()._mlp(i, L, x, T)

@@ -109,10 +109,21 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
         out.copy_(_fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared, expert_offset,
                                  shared_gate))
         return out
+    y, pos = moe_experts(x, w_gu, w_down, ids, num_experts, expert_offset)
+    torch.ops.b200.moe_combine(y, pos, w.contiguous(), shared, out, shared_gate)
+    return out
+
+
+def moe_experts(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: torch.Tensor,
+                num_experts: int, expert_offset: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Routed experts without the combine (CUDA): align -> gather -> grouped GEMM (SwiGLU) ->
+    grouped GEMM.  Returns (y [max_rows, H] expert outputs in expert-sorted order, pos [T, k]:
+    the row of y holding (token t, slot j), -1 when that expert is not served here)."""
+    T, H = x.shape
+    k = ids.shape[1]
     mod = _ext.require()
     E = num_experts
-    n = T * k
-    max_rows = int(mod.moe_max_rows(n, E))
+    max_rows = int(mod.moe_max_rows(T * k, E))
     dev = x.device
     sorted_ids = torch.empty(max_rows, dtype=torch.int32, device=dev)
     tile_expert = torch.empty(max_rows // 128, dtype=torch.int32, device=dev)
@@ -129,8 +140,7 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
     ops.gemm_grouped_bf16(xs, w_gu, h, tile_expert, num_tiles, E, 1, 0)
     y = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
     ops.gemm_grouped_bf16(h, w_down, y, tile_expert, num_tiles, E, 0, 0)
-    ops.moe_combine(y, pos, w.contiguous(), shared, out, shared_gate)
-    return out
+    return y, pos
 
 
 def _fq(x: torch.Tensor) -> torch.Tensor:

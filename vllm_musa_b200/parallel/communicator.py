@@ -26,6 +26,7 @@ class TPCommunicator:
         self.world = st.tp_size
         self.group = st.tp_group
         self.custom = custom  # CustomAllReduce (NVSwitch P2P) or None
+        self.ep_a2a = None    # EPAllToAll (expert-parallel dispatch/combine) or None
 
     # -- plain collectives ----------------------------------------------------------------
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
@@ -86,6 +87,9 @@ class TPCommunicator:
         return self.allreduce_add_rmsnorm(o, residual, weight, eps)
 
     def close(self) -> None:
+        if self.ep_a2a is not None:
+            self.ep_a2a.close()
+            self.ep_a2a = None
         if self.custom is not None:
             self.custom.close()
             self.custom = None

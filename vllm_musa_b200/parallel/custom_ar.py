@@ -112,6 +112,23 @@ class CustomAllReduce:
     def allreduce_add_rmsnorm(self, x, residual, weight, eps):
         return self._run(x, residual, weight, eps), residual
 
+    def staging_blocks(self, rows: int) -> torch.Tensor:
+        """This call's staging slot viewed as world blocks of `rows` rows (epilogue / expert
+        return targets of the local-source reduce)."""
+        return self._staging[self.parity][:self.world * rows]
+
+    def reduce_blocks_add_rmsnorm(self, T, residual, weight, eps, like):
+        """Two-shot reduce of the world blocks already stored in this rank's staging slot
+        (+ residual, RMSNorm, all-gather of the normalised rows)."""
+        rows = (T + self.world - 1) // self.world
+        _, blocks = self._plan(T)
+        self.mod.fused_allreduce(like, self._bufs[self.parity], self.epochs, self.rank,
+                                 self.world, T, self.hidden, blocks, self.parity, True, residual,
+                                 weight, eps, rows)
+        out = self._out[self.parity][:T]
+        self.parity ^= 1
+        return out, residual
+
     def can_fuse_gemm(self, T: int) -> bool:
         """Row-parallel GEMM + all-reduce as one reduce-scatter-in-epilogue GEMM and a local
         reduce + norm + all-gather kernel: used whenever the two-shot algorithm is (larger T)."""
