@@ -70,6 +70,9 @@ def mode_ar(out_path):
 
 
 def mode_gemm_rs(out_path):
+    os.environ["B200_FUSE_GEMM_RS"] = "1"
+    import vllm_musa_b200.parallel.custom_ar as car
+    car.FUSE_GEMM_RS = True
     """Row-parallel GEMM with the reduce-scatter in its tcgen05 epilogue (NVLink stores into
     the owners' staging slots) + local reduce / residual / RMSNorm / all-gather, against NCCL
     all-reduce of a plain GEMM."""
