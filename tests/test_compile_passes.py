@@ -1,0 +1,68 @@
+"""Graph fusion passes on CPU: traced graphs with all_reduce -> fused_add_rms_norm and
+silu_and_mul -> group_quant_fp8 chains are rewritten to the fused ops, the rewritten module
+computes the same values, and chains whose intermediate has other users are left alone."""
+import torch
+import torch.fx as fx
+
+from vllm_musa_b200.compile import B200PassManager
+from vllm_musa_b200.compile import passes as P  # noqa: F401  (registers torch.ops.b200fx)
+
+ops = torch.ops.b200fx
+
+
+class Block(torch.nn.Module):
+    def forward(self, x, residual, w, gu):
+        a = ops.all_reduce(x)
+        y, r = ops.fused_add_rms_norm(a, residual, w, 1e-6)
+        h = ops.silu_and_mul(gu)
+        q, s = ops.group_quant_fp8(h)
+        return y, r, q, s
+
+
+class Shared(torch.nn.Module):
+    def forward(self, x, residual, w):
+        a = ops.all_reduce(x)
+        y, r = ops.fused_add_rms_norm(a, residual, w, 1e-6)
+        return y, r, a * 2  # the all-reduce output has another user: no fusion
+
+
+def _names(gm):
+    return [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+
+
+def test_fusions_rewrite_and_preserve_values():
+    g = torch.Generator().manual_seed(0)
+    x, res = torch.randn(5, 256, generator=g), torch.randn(5, 256, generator=g)
+    w, gu = torch.rand(256, generator=g), torch.randn(5, 512, generator=g)
+    gm = fx.symbolic_trace(Block())
+    ref = gm(x, res, w, gu)
+    pm = B200PassManager()
+    assert pm(gm.graph) == 2
+    gm.recompile()
+    names = " ".join(_names(gm))
+    assert "allreduce_add_rms_norm" in names and "silu_mul_fp8_quant" in names
+    assert "b200fx.all_reduce" not in names and "group_quant_fp8" not in names
+    out = gm(x, res, w, gu)
+    torch.testing.assert_close(out[0], ref[0])
+    torch.testing.assert_close(out[1], ref[1])
+    torch.testing.assert_close(out[2].float(), ref[2].float())
+    torch.testing.assert_close(out[3], ref[3])
+    assert pm.stats == {"allreduce_rmsnorm": 1, "silu_mul_quant": 1}
+
+
+def test_no_fusion_when_intermediate_is_shared():
+    gm = fx.symbolic_trace(Shared())
+    pm = B200PassManager().configure(None)
+    assert pm(gm.graph) == 0
+    assert len(pm.uuid()) == 64
+
+
+def test_vllm_pass_manager_hook():
+    import pytest
+    pm_mod = pytest.importorskip("vllm.compilation.passes.pass_manager")
+    from vllm_musa_b200.compile.vllm_pass_manager import B200PostGradPassManager, b200_passes
+    from vllm_musa_b200.platform import B200Platform
+    assert issubclass(B200PostGradPassManager, pm_mod.PostGradPassManager)
+    assert B200Platform.get_pass_manager_cls().endswith("B200PostGradPassManager")
+    ps = b200_passes()
+    assert len(ps) == 2 and all(p.is_applicable_for_range(None) for p in ps)

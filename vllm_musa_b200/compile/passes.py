@@ -1,0 +1,192 @@
+"""Post-grad style graph passes: pattern-match unfused op chains in a torch.fx graph and replace
+them with the fused ops of this package.
+
+* ``AllReduceRMSNormFusionPass``  all_reduce(x) -> fused_add_rms_norm(x, residual, w, eps)
+  becomes one ``allreduce_add_rms_norm`` (the NVSwitch all-reduce + residual + RMSNorm kernel).
+* ``SiluMulQuantFusionPass``      silu_and_mul(x) -> group_quant_fp8(y) becomes one
+  ``silu_mul_fp8_quant`` (SwiGLU + 1x128 e4m3 quantisation in one kernel).
+
+Ops are matched by qualified name, so graphs traced from this package's ``torch.ops.b200fx.*``
+ops and graphs holding vLLM's equivalents (``vllm.all_reduce``, ``_C.fused_add_rms_norm``,
+``_C.silu_and_mul``, ``_C.per_token_group_fp8_quant``) are both rewritten.  A pass is a callable
+on ``torch.fx.Graph`` with a ``uuid()`` (the interface vLLM's pass manager and Inductor's
+custom post-grad pass hook expect).
+
+Reference counterparts: vllm_musa/compilation/passes/pass_manager.py:59-83 (pass manager),
+vllm_musa/_inductor/musa_allreduce_rms_fusion.py:103-844 (AR + RMSNorm fusion),
+compilation/passes/silu_deepgemm_fusion.py:19-85 (SiLU + quant fusion).
+"""
+from __future__ import annotations
+
+import hashlib
+from typing import Callable, Iterable, List, Optional
+
+import torch
+import torch.fx as fx
+
+# --------------------------------------------------------------------------------------------
+# Traceable ops (CPU implementations; CUDA tensors dispatch to the package's kernels)
+# --------------------------------------------------------------------------------------------
+_LIB = torch.library.Library("b200fx", "DEF")
+_LIB.define("all_reduce(Tensor x) -> Tensor")
+_LIB.define("fused_add_rms_norm(Tensor x, Tensor residual, Tensor w, float eps) -> (Tensor, Tensor)")
+_LIB.define("allreduce_add_rms_norm(Tensor x, Tensor residual, Tensor w, float eps) -> (Tensor, Tensor)")
+_LIB.define("silu_and_mul(Tensor x) -> Tensor")
+_LIB.define("group_quant_fp8(Tensor x) -> (Tensor, Tensor)")
+_LIB.define("silu_mul_fp8_quant(Tensor x) -> (Tensor, Tensor)")
+
+_COMM: Optional[object] = None  # TP communicator used by the fused all-reduce op
+
+
+def set_communicator(comm) -> None:
+    global _COMM
+    _COMM = comm
+
+
+def _all_reduce(x):
+    if _COMM is None or getattr(_COMM, "world", 1) == 1:
+        return x.clone()
+    return _COMM.all_reduce(x.clone())
+
+
+def _fused_add_rms_norm(x, residual, w, eps):
+    from .. import ops
+    r = (x.float() + residual.float()).to(x.dtype)
+    return ops.rms_norm(r, w, eps), r
+
+
+def _allreduce_add_rms_norm(x, residual, w, eps):
+    if _COMM is not None and getattr(_COMM, "world", 1) > 1:
+        out, res = _COMM.allreduce_add_rmsnorm(x.clone(), residual.clone(), w, eps)
+        return out.clone(), res
+    return _fused_add_rms_norm(x, residual, w, eps)
+
+
+def _silu_and_mul(x):
+    from .. import ops
+    return ops.silu_and_mul(x)
+
+
+def _group_quant(x):
+    from ..ops.activation import group_quant_fp8
+    return group_quant_fp8(x)
+
+
+def _silu_mul_quant(x):
+    from ..ops.activation import silu_mul_fp8_quant
+    return silu_mul_fp8_quant(x)
+
+
+for _name, _fn in (("all_reduce", _all_reduce), ("fused_add_rms_norm", _fused_add_rms_norm),
+                   ("allreduce_add_rms_norm", _allreduce_add_rms_norm),
+                   ("silu_and_mul", _silu_and_mul), ("group_quant_fp8", _group_quant),
+                   ("silu_mul_fp8_quant", _silu_mul_quant)):
+    _LIB.impl(_name, _fn, "CompositeExplicitAutograd")
+
+# --------------------------------------------------------------------------------------------
+# Matching helpers
+# --------------------------------------------------------------------------------------------
+ALL_REDUCE = ("b200fx.all_reduce", "vllm.all_reduce")
+ADD_RMS = ("b200fx.fused_add_rms_norm", "_C.fused_add_rms_norm")
+SILU_MUL = ("b200fx.silu_and_mul", "_C.silu_and_mul")
+GROUP_QUANT = ("b200fx.group_quant_fp8", "_C.per_token_group_fp8_quant")
+
+
+def _qual(target) -> str:
+    name = getattr(target, "_qualified_op_name", None) or getattr(target, "__name__", "")
+    if hasattr(target, "_schema"):
+        name = str(target._schema.name).replace("::", ".")
+    elif hasattr(target, "_qualified_op_name"):
+        name = target._qualified_op_name.replace("::", ".")
+    return name
+
+
+def _is(node: fx.Node, names: Iterable[str]) -> bool:
+    return node.op == "call_function" and any(_qual(node.target).startswith(n) for n in names)
+
+
+class _Pass:
+    name = "pass"
+
+    def uuid(self) -> str:
+        src = self.__class__.__name__ + self.name
+        return hashlib.sha256(src.encode()).hexdigest()
+
+    def __call__(self, graph: fx.Graph) -> int:
+        raise NotImplementedError
+
+
+class AllReduceRMSNormFusionPass(_Pass):
+    """all_reduce(x) whose only user is fused_add_rms_norm(ar, residual, w, eps)."""
+    name = "allreduce_rmsnorm"
+
+    def __call__(self, graph: fx.Graph) -> int:
+        n = 0
+        for node in list(graph.nodes):
+            if not _is(node, ADD_RMS):
+                continue
+            src = node.args[0]
+            if not isinstance(src, fx.Node) or not _is(src, ALL_REDUCE) or len(src.users) != 1:
+                continue
+            with graph.inserting_before(node):
+                fused = graph.call_function(torch.ops.b200fx.allreduce_add_rms_norm.default,
+                                            (src.args[0],) + tuple(node.args[1:]))
+            node.replace_all_uses_with(fused)
+            graph.erase_node(node)
+            graph.erase_node(src)
+            n += 1
+        return n
+
+
+class SiluMulQuantFusionPass(_Pass):
+    """group_quant_fp8(silu_and_mul(x)) with the activation used only by the quantiser."""
+    name = "silu_mul_quant"
+
+    def __call__(self, graph: fx.Graph) -> int:
+        n = 0
+        for node in list(graph.nodes):
+            if not _is(node, GROUP_QUANT):
+                continue
+            act = node.args[0]
+            if not isinstance(act, fx.Node) or not _is(act, SILU_MUL) or len(act.users) != 1:
+                continue
+            with graph.inserting_before(node):
+                fused = graph.call_function(torch.ops.b200fx.silu_mul_fp8_quant.default,
+                                            (act.args[0],))
+            node.replace_all_uses_with(fused)
+            graph.erase_node(node)
+            graph.erase_node(act)
+            n += 1
+        return n
+
+
+class B200PassManager(_Pass):
+    """Runs the fusion passes in order; ``configure`` picks them from a config-like object
+    (attributes ``fuse_allreduce_rms`` / ``fuse_act_quant``, default on)."""
+    name = "b200_pass_manager"
+
+    def __init__(self, passes: Optional[List[Callable]] = None):
+        self.passes = passes if passes is not None else [AllReduceRMSNormFusionPass(),
+                                                         SiluMulQuantFusionPass()]
+        self.stats = {}
+
+    def configure(self, config=None) -> "B200PassManager":
+        ps = []
+        if getattr(config, "fuse_allreduce_rms", True):
+            ps.append(AllReduceRMSNormFusionPass())
+        if getattr(config, "fuse_act_quant", True):
+            ps.append(SiluMulQuantFusionPass())
+        self.passes = ps
+        return self
+
+    def uuid(self) -> str:
+        return hashlib.sha256("".join(p.uuid() for p in self.passes).encode()).hexdigest()
+
+    def __call__(self, graph: fx.Graph) -> int:
+        total = 0
+        for p in self.passes:
+            k = p(graph)
+            self.stats[p.name] = self.stats.get(p.name, 0) + k
+            total += k
+        graph.lint()
+        return total

@@ -48,6 +48,10 @@ class B200Platform(_Base):
         return IrOpPriorityConfig.with_default(["native"], rms_norm=base, fused_add_rms_norm=base)
 
     @classmethod
+    def get_pass_manager_cls(cls) -> str:
+        return "vllm_musa_b200.compile.vllm_pass_manager.B200PostGradPassManager"
+
+    @classmethod
     def use_custom_allreduce(cls) -> bool:
         return True
 
