@@ -85,6 +85,19 @@ def case_gemm_prefill(it):
     gemm(8192, 4096, 4096, it, "gemm_bf16_prefill_o")
 
 
+def case_gemm_pair(it):
+    """1-CTA 128 x 256 tiles (mt=1) vs CTA-pair 256 x bn tiles (mt=4) on prefill shapes."""
+    for M, N, K in ((8192, 28672, 4096), (8192, 4096, 14336), (8192, 6144, 4096),
+                    (8192, 4096, 4096)):
+        ws = copies(lambda: bf16(N, K, scale=0.02), N * K * 2)
+        x = bf16(M, K)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        for mt, bn in ((1, 256), (4, 0)):
+            us = timed(lambda i: ops.gemm._run(x, ws[i % len(ws)], out, 0, bn, 1, mt), it)
+            report(f"gemm_bf16_{'pair' if mt == 4 else 'single'}", [M, N, K], us,
+                   (M * K + N * K + M * N) * 2, 2 * M * N * K)
+
+
 def case_gemm_fp8(it):
     from vllm_musa_b200.ops import fp8
     for M, N, K in ((64, 24576, 7168), (4096, 7168, 2048)):

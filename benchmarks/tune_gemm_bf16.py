@@ -1,4 +1,5 @@
-"""Sweep the tcgen05 BF16 GEMM's plans (tile width BN x split-K) for a model's linear shapes
+"""Sweep the tcgen05 BF16 GEMM's plans (tile width BN x split-K x row tiles: MT = 1 or 2
+128-row tiles per CTA, or 4 = a CTA pair on a 256-row tile) for a model's linear shapes
 and write the fastest plan per (N, K, M) to vllm_musa_b200/tuning/gemm_bf16.json.
 
 Timing: CUDA events on the launching stream after warm-up; launches cycle through copies of
@@ -36,6 +37,10 @@ def model_shapes(name, tp):
 
 
 L2_BYTES = 126 << 20
+
+
+def s_ok(M):
+    return M >= 1024
 
 
 def timed(fn, ws, reps):
@@ -81,11 +86,15 @@ def main():
                            ws, a.reps)
             best = (t_auto, auto[0], auto[1], auto[3])
             kb = (K + 63) // 64
-            for mt in ((1, 2) if M > 128 else (1,)):
+            for mt in ((1, 2, 4) if M >= 1024 else (1, 2) if M > 128 else (1,)):
                 for bn in (256, 224, 208, 192, 176, 160, 144, 128, 112, 96, 64, 48, 32):
-                    if M >= 1024 and (bn % 64 or mt * bn * 2 > 512):
+                    if mt == 4 and (bn % 32 or bn < 128):  # CTA pairs: 256-row tiles
                         continue
-                    for s in ((1,) if M >= 1024 else (1, 2, 3, 4, 6, 8)):
+                    if mt == 4 and s_ok(M) is False:
+                        continue
+                    if M >= 1024 and mt != 4 and (bn % 64 or mt * bn * 2 > 512):
+                        continue
+                    for s in ((1,) if M >= 1024 or mt == 4 else (1, 2, 3, 4, 6, 8)):
                         if s > 1 and kb // s < 4:
                             continue
                         if s * M * N > (64 << 20):

@@ -193,6 +193,37 @@ B200_DEVICE void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar, in
       : "memory");
 }
 
+// ---- thread-block clusters
+B200_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+B200_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// shared::cluster address of `smem_addr` (a shared::cta address) in CTA `rank` of the cluster
+B200_DEVICE uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+B200_DEVICE void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// TMA load issued by either CTA of a pair; completion bytes go to the mbarrier at the given
+// shared::cluster address (the leader's).  Not a multicast load.
+B200_DEVICE void tma_load_2d_pair(void* smem_dst, const void* desc, uint32_t bar_cluster_addr,
+                                  int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
 B200_DEVICE void tma_load_2d_hint(void* smem_dst, const void* desc, uint64_t* bar, int x, int y,
                                   uint64_t policy) {
   asm volatile(

@@ -398,11 +398,219 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// CTA-pair variant for large M: a 2-CTA cluster computes a 256 x BN tile with cta_group::2
+// MMAs.  Each CTA stages its own 128 A rows and half of the BN B rows (same shared-memory
+// offsets), so per FLOP the pair moves a third less data from L2 into shared memory than two
+// independent 128 x BN tiles.  Both CTAs' TMA loads complete on the leader's full barrier; the
+// leader's single MMA thread commits to the empty / accumulator barriers of both CTAs
+// (tcgen05.commit multicast); both CTAs' epilogue warps release the accumulator on the
+// leader's barrier (8 arrivals).  No split-K.
+// ---------------------------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmB, Params p) {
+  pdl_trigger();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int STAGES = p.stages;
+  const int BN = p.bn, HALF = BN / 2;
+  const int A_BYTES = BM * BK * 2;
+  const int B_BYTES = HALF * BK * 2;
+  const int STAGE_BYTES = A_BYTES + B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* acc_full = bars + 2 * kMaxStages;
+  uint64_t* acc_empty = bars + 2 * kMaxStages + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tmem_slot, p.tmem_cols);
+    tc::tmem_relinquish_pair();
+  }
+  tc::fence_before_sync();
+  cluster_sync();  // both CTAs' barriers and TMEM are ready
+  tc::fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      pdl_wait();
+      for (int u = pair; u < p.total_units && ok; u += npairs) {
+        int m, n, ks;
+        unit_coords(u, p, m, n, ks);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          const uint32_t fullc = mapa_shared(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(st, &tmA, fullc, kb * BK, m * 2 * BM + (int)crank * BM);
+          tma_load_2d_pair(st + A_BYTES, &tmB, fullc, kb * BK, n * BN + (int)crank * HALF);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (ok) {  // no TMA write in flight at exit
+        for (int i = 0; i < STAGES; ++i) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) break;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      const uint32_t idesc = tc::idesc_f16<true>(2 * BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = pair; u < p.total_units && ok; u += npairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err)) break;
+        tc::fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t adesc = tc::smem_desc_kmajor_sw128(sa);
+          const uint64_t bdesc = tc::smem_desc_kmajor_sw128(sa + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc::mma_f16_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc,
+                                (kb > 0 || k > 0) ? 1u : 0u);
+          tc::mma_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc::mma_commit_pair_mc(&acc_full[acc], 0x3);
+        if (++acc == p.acc_bufs) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = pair; u < p.total_units; u += npairs) {
+      int m, n, ks;
+      unit_coords(u, p, m, n, ks);
+      if (!mbar_wait(&acc_full[acc], acc_phase, p.err)) break;
+      tc::fence_after_sync();
+      const int row = m * 2 * BM + (int)crank * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const bool two = c + 16 < BN;
+        uint32_t r[2][16];
+        tc::tmem_ld_32x32b_x16(t_row + c, r[0]);
+        if (two) tc::tmem_ld_32x32b_x16(t_row + c + 16, r[1]);
+        tc::tmem_ld_wait();
+        if (!row_ok) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col = n * BN + c + 16 * h;
+          if ((h == 1 && !two) || col >= p.N) continue;
+          float f[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(r[h][j]);
+          store_chunk16<EPI>(p, row, col, f);
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_leader0 + acc * (uint32_t)sizeof(uint64_t));
+      if (++acc == p.acc_bufs) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  cluster_sync();  // the peer's remote arrivals and TMEM reads are done
+  tc::fence_after_sync();
+  if (warp == 1) tc::tmem_dealloc_pair(tmem_base, p.tmem_cols);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
 struct Plan {
   int mt, bn, splits;
 };
+
+// CTA pairs are used from this many rows (B200_GEMM_PAIR_MIN_ROWS; 0 disables)
+static int pair_min_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("B200_GEMM_PAIR_MIN_ROWS");
+    v = e ? atoi(e) : 2048;
+    if (v <= 0) v = 1 << 30;
+  }
+  return v;
+}
+
+// Tile width for CTA pairs: the widest multiple of 32 (<= 256) whose tile count fills the SM
+// pairs in whole waves best.
+static int pair_bn(int M, int N) {
+  const int pairs = std::max(1, num_sms() / 2);
+  const int num_m = (M + 2 * BM - 1) / (2 * BM);
+  int best = 256;
+  double best_eff = 0.0;
+  for (int bn = 256; bn >= 128; bn -= 32) {
+    const long tiles = (long)num_m * ((N + bn - 1) / bn);
+    const long waves = (tiles + pairs - 1) / pairs;
+    const double eff = (double)tiles / (double)(waves * pairs) * (bn >= 192 ? 1.0 : 0.93);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = bn;
+    }
+  }
+  return best;
+}
 
 static int stages_for(int mt, int bn) {
   const int stage = a_tile_bytes(mt) + b_tile_bytes(bn);
@@ -502,6 +710,37 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
 }
 
 template <int EPI>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                        cudaStream_t stream) {
+  auto kern = gemm_bf16_pair_kernel<EPI>;
+  ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
+  const int smem = p.stages * (BM * BK * 2 + (p.bn / 2) * BK * 2) + kSmemOverhead;
+  const int pairs = std::max(1, std::min(p.total_units, num_sms() / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string("b200: pair gemm launch failed: ") +
+                             cudaGetErrorString(e) + " grid=" + std::to_string(2 * pairs) +
+                             " smem=" + std::to_string(smem));
+  }
+  count_launch();
+}
+
+template <int EPI>
 static void dispatch_mt(int mt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                         cudaStream_t s) {
   if (mt == 2)
@@ -592,21 +831,36 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.bn > 0) plan.bn = a.bn;
   if (a.splits > 0) plan.splits = a.splits;
   if (a.mt > 0) plan.mt = a.mt;
+  // CTA pairs (mt = 4): 256-row tiles; chosen automatically for large M (no split-K)
+  const bool pair_ok = a.mode != kModeScatter && M >= 2 * BM;
+  // automatic use (no measured plan): large M and not too wide -- at M = 8192 the pair tiles
+  // measured 0.95 / 0.89 of cuBLAS on N = 4096 (K = 14336 / 4096) but lost on N = 28672
+  const bool pair = a.mt == 4 ? pair_ok
+                              : (a.mt == 0 && a.bn <= 0 && a.splits <= 0 && pair_ok &&
+                                 M >= pair_min_rows() && N <= 16384 && plan.splits <= 1);
+  if (pair) {
+    plan.mt = 1;
+    plan.splits = 1;
+    plan.bn = a.mt == 4 && a.bn > 0 && a.bn % 32 == 0 ? a.bn : pair_bn(M, N);
+  }
   B200_REQUIRE(plan.bn >= 16 && plan.bn <= 256 && plan.bn % 16 == 0,
                "gemm_bf16: bn must be a multiple of 16 in [16, 256]");
-  B200_REQUIRE(plan.mt == 1 || plan.mt == 2, "gemm_bf16: mt must be 1 or 2");
+  B200_REQUIRE(plan.mt == 1 || plan.mt == 2, "gemm_bf16: mt must be 1, 2 or 4 (CTA pair)");
+  B200_REQUIRE(!pair || plan.bn % 32 == 0, "gemm_bf16: CTA-pair tiles need bn % 32 == 0");
   Params p;
   p.M = M;
   p.N = N;
   p.K = K;
   p.bn = plan.bn;
-  p.stages = stages_for(plan.mt, plan.bn);
+  p.stages = pair ? std::min(kMaxStages, (kSmemBudget - kSmemOverhead) /
+                                             (BM * BK * 2 + (plan.bn / 2) * BK * 2))
+                  : stages_for(plan.mt, plan.bn);
   const int acc_cols = plan.mt * plan.bn;
   p.acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
   int cols = 32;
   while (cols < p.acc_bufs * acc_cols) cols <<= 1;
   p.tmem_cols = cols;
-  p.num_m = (M + BM * plan.mt - 1) / (BM * plan.mt);
+  p.num_m = pair ? (M + 2 * BM - 1) / (2 * BM) : (M + BM * plan.mt - 1) / (BM * plan.mt);
   p.num_n = (N + plan.bn - 1) / plan.bn;
   p.num_kb = (K + BK - 1) / BK;
   p.splits = std::max(1, std::min<int>(plan.splits, p.num_kb));
@@ -620,7 +874,8 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
       make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, a.lda, BK,
                   BM * plan.mt, CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tb = make_tma_2d(const_cast<void*>(a.B), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                                     K, N, a.ldb, BK, plan.bn, CU_TENSOR_MAP_SWIZZLE_128B);
+                                     K, N, a.ldb, BK, pair ? plan.bn / 2 : plan.bn,
+                                     CU_TENSOR_MAP_SWIZZLE_128B);
 
   p.C = a.C;
   p.tile_expert = nullptr;
@@ -646,6 +901,15 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
                  "gemm_bf16: split-K tile counters too small");
     p.ws = a.workspace;
     p.counters = a.counters;
+  }
+  if (pair) {
+    if (a.mode == kModeStore)
+      launch_pair<kStore>(ta, tb, p, stream);
+    else if (a.mode == kModeSiluMul)
+      launch_pair<kSiluMul>(ta, tb, p, stream);
+    else
+      launch_pair<kF32>(ta, tb, p, stream);
+    return;
   }
   if (a.mode == kModeStore)
     dispatch_mt<kStore>(plan.mt, ta, tb, p, stream);

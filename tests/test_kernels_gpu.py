@@ -59,6 +59,27 @@ def test_gemm_silu_forced_plans(bn, splits, mt):
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("M,N,K,bn,mode", [(256, 512, 1024, 256, 0), (1000, 784, 2048, 256, 0),
+                                           (2048, 4096, 4096, 192, 0), (777, 1024, 512, 128, 1),
+                                           (4096, 2000, 1024, 224, 2), (300, 96, 256, 64, 0)])
+def test_gemm_bf16_cta_pair(M, N, K, bn, mode):
+    """CTA-pair (cta_group::2) tiles: 256 x bn per 2-CTA cluster, forced with mt=4."""
+    a = _bf(M, K, seed=21)
+    if mode == 1:
+        g, u = _bf(N // 2, K, seed=22, scale=0.05), _bf(N // 2, K, seed=23, scale=0.05)
+        b = ops.interleave_gate_up(g, u)
+        ref = torch.nn.functional.silu(a.float() @ g.float().t()) * (a.float() @ u.float().t())
+        out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=DEV)
+    else:
+        b = _bf(N, K, seed=24, scale=0.05)
+        ref = a.float() @ b.float().t()
+        out = torch.empty(M, N, dtype=torch.float32 if mode == 2 else torch.bfloat16, device=DEV)
+    ops.gemm._run(a, b, out, mode, bn, 1, 4)
+    torch.cuda.synchronize()
+    _ext.check_device_errors()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
+
+
 def test_gemm_fp32_out_and_strided_a():
     M, N, K = 64, 1000, 512
     big = _bf(M, K + 64, seed=5)
