@@ -50,6 +50,8 @@ constexpr int kGroupN = 8;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 226 * 1024;  // dynamic opt-in; leaves room for static smem
 constexpr int kSmemOverhead = 1024 /*align*/ + 512 /*barriers, tmem slot*/;
+constexpr int kScatterWarpBytes = 32 * 128;  // kScatter epilogue staging per epilogue warp
+constexpr int kScatterBytes = 4 * kScatterWarpBytes;
 
 enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2, kScatter = 3 };
 
@@ -309,6 +311,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool row_ok = row < p.M;
         const uint32_t t_row =
             tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS + mt * BN;
+        if constexpr (EPI == kScatter) {
+          if (!split) {
+            // Stage 32 rows x 64 columns in this warp's scratch, then store each row's 128
+            // contiguous bytes with 8 lanes (4 rows per warp instruction): NVLink carries
+            // whole 128-byte segments instead of 32-byte row pieces.
+            uint8_t* scr = smem + STAGES * STAGE_BYTES + 512 + (warp - 2) * kScatterWarpBytes;
+            const int base_row = (m * MT + mt) * BM + q * 32;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 64) {
+              const int ncol = min(64, BN - c);
+              uint32_t r[4][16];
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+                if (16 * h < ncol) tc::tmem_ld_32x32b_x16(t_row + c + 16 * h, r[h]);
+              tc::tmem_ld_wait();
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                if (16 * h >= ncol) continue;
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                  float f[8];
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[h][8 * j + e]);
+                  const int ch = 2 * h + j;
+                  *reinterpret_cast<uint4*>(scr + lane * 128 + ((ch ^ (lane & 7)) << 4)) = pack8(f);
+                }
+              }
+              __syncwarp();
+              const int chunks = ncol / 8;
+              for (int i = lane; i < 32 * chunks; i += 32) {
+                const int rl = i / chunks, ch = i - rl * chunks;
+                const int rrow = base_row + rl;
+                const int col = n * BN + c + ch * 8;
+                if (rrow < p.M && col < p.N) {
+                  const int owner = rrow / p.rs_rows;
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.peers[owner]) +
+                                       ((size_t)p.rs_rank * p.rs_rows + (rrow - owner * p.rs_rows)) *
+                                           p.ldc + col;
+                  *reinterpret_cast<uint4*>(dst) =
+                      *reinterpret_cast<const uint4*>(scr + rl * 128 + ((ch ^ (rl & 7)) << 4));
+                }
+              }
+              __syncwarp();
+            }
+            continue;
+          }
+        }
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           const bool two = c + 16 < BN;
@@ -703,7 +752,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
                    cudaStream_t stream) {
   auto kern = gemm_bf16_kernel<MT, EPI>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
-  const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) + kSmemOverhead;
+  const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) + kSmemOverhead +
+                   (EPI == kScatter ? kScatterBytes : 0);
   const int grid = std::min(p.total_units, num_sms());
   launch_pdl(kern, grid, smem, stream, ta, tb, p);
   count_launch();
@@ -855,6 +905,9 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.stages = pair ? std::min(kMaxStages, (kSmemBudget - kSmemOverhead) /
                                              (BM * BK * 2 + (plan.bn / 2) * BK * 2))
                   : stages_for(plan.mt, plan.bn);
+  if (a.mode == kModeScatter)  // room for the coalescing scratch of the scatter epilogue
+    p.stages = std::min(p.stages, (kSmemBudget - kSmemOverhead - kScatterBytes) /
+                                      (a_tile_bytes(plan.mt) + b_tile_bytes(plan.bn)));
   const int acc_cols = plan.mt * plan.bn;
   p.acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
   int cols = 32;
