@@ -102,16 +102,33 @@ def main():
                         t = timed(lambda w: ops.gemm._run(x, w, out, mode, bn, s, mt), ws, a.reps)
                         if t < best[0]:
                             best = (t, bn, s, mt)
+            # swapped plans (C^T = W X^T): tokens in the MMA's N dimension, one token tile
+            swap_best = None
+            if mode in (0, 1) and M <= 256 and M % 8 == 0:
+                sbn = (M + 15) // 16 * 16
+                for smt in (1, 2):
+                    for s in (1, 2, 3, 4, 6, 8):
+                        if s > 1 and kb // s < 4:
+                            continue
+                        t = timed(lambda w: ops.gemm._run(x, w, out, mode, sbn, s, smt, swap=True),
+                                  ws, a.reps)
+                        if swap_best is None or t < swap_best[0]:
+                            swap_best = (t, sbn, s, smt)
             t_cublas = timed(lambda w: torch.matmul(x, w.t()), ws, a.reps)
             tb = (N * K * 2 + M * K * 2 + M * N * 2) / (best[0] * 1e-6) / 1e12
             tf = 2 * M * N * K / (best[0] * 1e-6) / 1e12
             report.append(dict(layer=lname, M=M, N=N, K=K, auto=[auto[0], auto[1], auto[3]],
                                t_auto_us=round(t_auto, 1), best_bn=best[1], best_splits=best[2],
                                best_mt=best[3], t_best_us=round(best[0], 1),
+                               swap_us=round(swap_best[0], 1) if swap_best else None,
                                cublas_us=round(t_cublas, 1), TBps=round(tb, 2), TFLOPs=round(tf, 1)))
             print(json.dumps(report[-1]), flush=True)
             entries.append({"n": N, "k": K, "m": M, "bn": best[1], "splits": best[2],
                             "mt": best[3], "us": round(best[0], 2)})
+            if swap_best is not None:
+                entries.append({"n": N, "k": K, "m": M, "bn": swap_best[1],
+                                "splits": swap_best[2], "mt": swap_best[3], "swap": 1,
+                                "us": round(swap_best[0], 2)})
     table = {"device": torch.cuda.get_device_name(), "model": a.model, "tp": a.tp,
              "entries": entries}
     if a.write:
@@ -119,7 +136,8 @@ def main():
         old = {"entries": []}
         if os.path.exists(path):
             old = json.load(open(path))
-        keep = [e for e in old["entries"] if (e["n"], e["k"]) not in {(x["n"], x["k"]) for x in entries}]
+        keep = [e for e in old["entries"]
+                if (e["n"], e["k"]) not in {(x["n"], x["k"]) for x in entries}]
         table["entries"] = keep + entries
         with open(path, "w") as f:
             json.dump(table, f, indent=1)

@@ -15,7 +15,11 @@ namespace b200 {
 
 // ------------------------------------------------------------------------------- GEMM
 namespace gemm {
-enum Mode : int { kModeStore = 0, kModeSiluMul = 1, kModeF32 = 2, kModeScatter = 3 };
+// kModeStoreT / kModeSiluT ("swap-AB", for decode-sized token counts): A is the WEIGHT [N, K]
+// and B the activations [M, K]; the kernel computes C^T tiles and stores C [M, N] (N/2 for
+// SiLU) transposed, so the tokens occupy the MMA's N dimension.
+enum Mode : int { kModeStore = 0, kModeSiluMul = 1, kModeF32 = 2, kModeScatter = 3,
+                  kModeStoreT = 4, kModeSiluT = 5 };
 struct GemmArgs {
   const void* A;  // [M, K] bf16, row stride lda
   int64_t lda;

@@ -53,7 +53,13 @@ constexpr int kSmemOverhead = 1024 /*align*/ + 512 /*barriers, tmem slot*/;
 constexpr int kScatterWarpBytes = 32 * 128;  // kScatter epilogue staging per epilogue warp
 constexpr int kScatterBytes = 4 * kScatterWarpBytes;
 
-enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2, kScatter = 3 };
+enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2, kScatter = 3, kStoreT = 4, kSiluT = 5 };
+
+// Transposed ("swap-AB") epilogues compute C^T = W . X^T so a decode-sized token count sits in
+// the MMA's N dimension (one 128 x M tile per 128 weight rows, the efficient tcgen05 shape) and
+// write C[token][feature] through a per-warp shared-memory transpose.
+template <int EPI>
+constexpr bool kTransposed = EPI == kStoreT || EPI == kSiluT;
 
 struct Params {
   int M, N, K;
@@ -103,6 +109,48 @@ B200_DEVICE void unit_coords(int u, const Params& p, int& m, int& n, int& ks) {
 }
 
 B200_DEVICE float silu(float x) { return x / (1.f + __expf(-x)); }
+
+// Transposed store of a 32 x 32 block held one accumulator row per lane: f[j] = C^T(base_row +
+// lane, c0 + j).  Writes C[(c0 + lane) * ldc + feature] with 16-byte stores after a shared-
+// memory transpose (scr: 2 KB per warp).  kSiluT: rows are gate/up interleaved in groups of 16
+// (8 gate rows, then their 8 up rows); the 32-row block yields 16 outputs at base_row / 2.
+// Warp-collective: every lane calls it.
+template <int EPI>
+B200_DEVICE void store_t32(const Params& p, uint8_t* scr, int base_row, int c0,
+                           const float (&f)[32], int lane) {
+  __nv_bfloat16* s = reinterpret_cast<__nv_bfloat16*>(scr);
+  const int t = c0 + lane;
+  if constexpr (EPI == kStoreT) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s[j * 32 + lane] = f2bf(f[j]);
+    __syncwarp();
+    if (t < p.N) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)t * p.ldc + base_row;
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        if (base_row + 8 * v < p.M)
+          reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(s + lane * 32)[v];
+    }
+  } else {
+    const bool gate = (lane & 8) == 0;
+    const int o = (lane & 7) + ((lane >> 4) << 3);  // output index within the block (0..15)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float up = __shfl_xor_sync(0xffffffffu, f[j], 8);
+      if (gate) s[j * 16 + o] = f2bf(silu(f[j]) * up);
+    }
+    __syncwarp();
+    if (t < p.N) {
+      __nv_bfloat16* dst =
+          reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)t * p.ldc + base_row / 2;
+#pragma unroll
+      for (int v = 0; v < 2; ++v)
+        if (base_row + 16 * v < p.M)
+          reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(s + lane * 16)[v];
+    }
+  }
+  __syncwarp();
+}
 
 // Final epilogue of 16 accumulator columns [col, col+16) of one row.
 template <int EPI>
@@ -311,6 +359,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool row_ok = row < p.M;
         const uint32_t t_row =
             tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS + mt * BN;
+        if constexpr (kTransposed<EPI>) {
+          if (!split) {
+            uint8_t* scr = smem + STAGES * STAGE_BYTES + 512 + (warp - 2) * kScatterWarpBytes;
+            const int base_row = (m * MT + mt) * BM + q * 32;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+              const bool two = c + 16 < BN;
+              uint32_t r[2][16];
+              tc::tmem_ld_32x32b_x16(t_row + c, r[0]);
+              if (two) tc::tmem_ld_32x32b_x16(t_row + c + 16, r[1]);
+              tc::tmem_ld_wait();
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                f[j] = __uint_as_float(r[0][j]);
+                f[16 + j] = two ? __uint_as_float(r[1][j]) : 0.f;
+              }
+              store_t32<EPI>(p, scr, base_row, n * BN + c, f, lane);
+            }
+            continue;
+          }
+        }
         if constexpr (EPI == kScatter) {
           if (!split) {
             // Stage 32 rows x 64 columns in this warp's scratch, then store each row's 128
@@ -402,7 +472,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = m * p.num_n + n;
         if (warp == 2 && lane == 0) s_last = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
         epi_barrier();
-        if (s_last) {
+        if (s_last && kTransposed<EPI>) {
+          __threadfence();
+          uint8_t* scr = smem + STAGES * STAGE_BYTES + 512 + (warp - 2) * kScatterWarpBytes;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int base_row = (m * MT + mt) * BM + q * 32;
+            const int row = base_row + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+              const int col0 = n * BN + c;
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = 0.f;
+              if (row < p.M) {
+                for (int sp = 0; sp < p.splits; ++sp) {
+                  const float* w = p.ws + ((size_t)sp * p.M + row) * p.N + col0;
+#pragma unroll
+                  for (int v = 0; v < 8; ++v) {
+                    if (col0 + 4 * v < p.N && c + 4 * v < BN) {
+                      const float4 x = __ldcg(reinterpret_cast<const float4*>(w) + v);
+                      f[4 * v] += x.x;
+                      f[4 * v + 1] += x.y;
+                      f[4 * v + 2] += x.z;
+                      f[4 * v + 3] += x.w;
+                    }
+                  }
+                }
+              }
+              store_t32<EPI>(p, scr, base_row, col0, f, lane);
+            }
+          }
+          epi_barrier();
+          if (warp == 2 && lane == 0) p.counters[tile] = 0;
+        } else if (s_last) {
           __threadfence();
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
@@ -753,7 +856,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   auto kern = gemm_bf16_kernel<MT, EPI>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
   const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) + kSmemOverhead +
-                   (EPI == kScatter ? kScatterBytes : 0);
+                   (EPI == kScatter || kTransposed<EPI> ? kScatterBytes : 0);
   const int grid = std::min(p.total_units, num_sms());
   launch_pdl(kern, grid, smem, stream, ta, tb, p);
   count_launch();
@@ -868,7 +971,10 @@ GemmPlan plan_bf16(int M, int N, int K) {
 
 void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   const int M = a.M, N = a.N, K = a.K;
+  // (swapped modes: N is the token count, M the weight rows; both must be multiples of 8)
   B200_REQUIRE(K % 8 == 0 && N % 8 == 0, "gemm_bf16: K and N must be multiples of 8");
+  B200_REQUIRE((a.mode != kModeStoreT && a.mode != kModeSiluT) || M % 8 == 0,
+               "gemm_bf16 swapped: weight rows must be a multiple of 8");
   B200_REQUIRE((a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0,
                "gemm_bf16: row strides must be 16-byte multiples");
   B200_REQUIRE(reinterpret_cast<uintptr_t>(a.A) % 16 == 0 &&
@@ -882,7 +988,10 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.splits > 0) plan.splits = a.splits;
   if (a.mt > 0) plan.mt = a.mt;
   // CTA pairs (mt = 4): 256-row tiles; chosen automatically for large M (no split-K)
-  const bool pair_ok = a.mode != kModeScatter && M >= 2 * BM;
+  const bool transposed = a.mode == kModeStoreT || a.mode == kModeSiluT;
+  B200_REQUIRE(a.mode != kModeSiluT || M % 16 == 0,
+               "gemm_bf16 swapped SiLU: weight rows must be a multiple of 16");
+  const bool pair_ok = a.mode != kModeScatter && !transposed && M >= 2 * BM;
   // automatic use (no measured plan): large M and not too wide -- at M = 8192 the pair tiles
   // measured 0.95 / 0.89 of cuBLAS on N = 4096 (K = 14336 / 4096) but lost on N = 28672
   const bool pair = a.mt == 4 ? pair_ok
@@ -905,7 +1014,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.stages = pair ? std::min(kMaxStages, (kSmemBudget - kSmemOverhead) /
                                              (BM * BK * 2 + (plan.bn / 2) * BK * 2))
                   : stages_for(plan.mt, plan.bn);
-  if (a.mode == kModeScatter)  // room for the coalescing scratch of the scatter epilogue
+  if (a.mode == kModeScatter || transposed)  // room for the epilogue's shared-memory staging
     p.stages = std::min(p.stages, (kSmemBudget - kSmemOverhead - kScatterBytes) /
                                       (a_tile_bytes(plan.mt) + b_tile_bytes(plan.bn)));
   const int acc_cols = plan.mt * plan.bn;
@@ -970,6 +1079,10 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     dispatch_mt<kSiluMul>(plan.mt, ta, tb, p, stream);
   else if (a.mode == kModeScatter)
     dispatch_mt<kScatter>(plan.mt, ta, tb, p, stream);
+  else if (a.mode == kModeStoreT)
+    dispatch_mt<kStoreT>(plan.mt, ta, tb, p, stream);
+  else if (a.mode == kModeSiluT)
+    dispatch_mt<kSiluT>(plan.mt, ta, tb, p, stream);
   else
     dispatch_mt<kF32>(plan.mt, ta, tb, p, stream);
 }

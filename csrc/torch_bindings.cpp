@@ -62,7 +62,12 @@ void gemm_bf16(const Tensor& A, const Tensor& B, Tensor& C, int64_t mode, int64_
   CHECK_ROWMAJOR(C);
   TORCH_CHECK(A.size(1) == B.size(1), "gemm_bf16: K mismatch");
   const int M = A.size(0), N = B.size(0), K = A.size(1);
-  TORCH_CHECK(C.size(0) == M && C.size(1) == (mode == 1 ? N / 2 : N), "gemm_bf16: C shape");
+  if (mode == 4 || mode == 5) {  // swapped: A = weight [features, K], B = activations [tokens, K]
+    TORCH_CHECK(C.size(0) == N && C.size(1) == (mode == 5 ? M / 2 : M), "gemm_bf16: C^T shape");
+    TORCH_CHECK(C.stride(1) == 1, "gemm_bf16: C row-major");
+  } else {
+    TORCH_CHECK(C.size(0) == M && C.size(1) == (mode == 1 ? N / 2 : N), "gemm_bf16: C shape");
+  }
   TORCH_CHECK(C.scalar_type() == (mode == 2 ? at::kFloat : at::kBFloat16), "gemm_bf16: C dtype");
   const c10::cuda::CUDAGuard g(A.device());
   b200::gemm::GemmArgs a{};

@@ -80,6 +80,30 @@ def test_gemm_bf16_cta_pair(M, N, K, bn, mode):
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("M,N,K,bn,splits,mt,mode", [
+    (256, 4096, 1024, 256, 1, 1, 0), (64, 1024, 2048, 64, 4, 1, 0), (8, 768, 512, 16, 2, 1, 0),
+    (256, 2048, 4096, 256, 3, 2, 0), (128, 1024, 1024, 128, 1, 1, 1), (40, 784, 1024, 48, 2, 1, 1),
+    (200, 1056, 512, 208, 1, 2, 1)])
+def test_gemm_bf16_swapped(M, N, K, bn, splits, mt, mode):
+    """Swap-AB plans: C^T = W X^T computed with the tokens in the MMA's N dimension and stored
+    transposed through shared memory (with and without split-K, store and SwiGLU)."""
+    a = _bf(M, K, seed=31)
+    if mode == 1:
+        g, u = _bf(N // 2, K, seed=32, scale=0.05), _bf(N // 2, K, seed=33, scale=0.05)
+        b = ops.interleave_gate_up(g, u)
+        ref = torch.nn.functional.silu(a.float() @ g.float().t()) * (a.float() @ u.float().t())
+        out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=DEV)
+    else:
+        b = _bf(N, K, seed=34, scale=0.05)
+        ref = a.float() @ b.float().t()
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm.reserve_workspace(a.device, 16 << 20)
+    ops.gemm._run(a, b, out, mode, bn, splits, mt, swap=True)
+    torch.cuda.synchronize()
+    _ext.check_device_errors()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
+
+
 def test_gemm_fp32_out_and_strided_a():
     M, N, K = 64, 1000, 512
     big = _bf(M, K + 64, seed=5)

@@ -63,9 +63,24 @@ def plan_for(M: int, N: int, K: int, bn: int = 0, splits: int = 0, mt: int = 0) 
 
 
 def _run(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, mode: int, bn: int = 0,
-         splits: int = 0, mt: int = 0) -> torch.Tensor:
+         splits: int = 0, mt: int = 0, swap: bool = False) -> torch.Tensor:
+    """mode 0 store / 1 SwiGLU / 2 fp32.  ``swap`` (or a measured swapped plan for a decode-
+    sized M) runs C^T = W X^T with the tokens in the MMA's N dimension (modes 0 and 1)."""
     _ext.require()  # registers torch.ops.b200
     M, N, K = x.shape[0], w.shape[0], x.shape[1]
+    if mode in (0, 1) and M % 8 == 0 and (mode == 0 or N % 16 == 0):
+        sp = None
+        if swap:
+            sp = (bn, splits, mt)
+        elif bn <= 0 and splits <= 0 and mt <= 0 and M <= 256:
+            sp = tuning.gemm_table().swap_plan(M, N, K)
+        if sp is not None:
+            sbn, ss, smt = sp
+            need = ss * M * N if ss > 1 else 0
+            ws = _workspace(x.device, need) if need > 0 else None
+            cnt = _counters(x.device) if need > 0 else None
+            torch.ops.b200.gemm_bf16(w, x, out, mode + 4, sbn, ss, ws, smt, cnt)
+            return out
     bn, splits, mt, need = plan_for(M, N, K, bn, splits, mt)
     ws = _workspace(x.device, need) if need > 0 else None
     cnt = _counters(x.device) if need > 0 else None

@@ -58,25 +58,38 @@ def load(name: str) -> Optional[dict]:
 
 
 class GemmPlanTable:
-    """(N, K, M) -> (bn, splits): exact (N, K) match, smallest measured M bucket >= M."""
+    """(N, K, M) -> plan: exact (N, K) match, smallest measured M bucket >= M.  Entries with
+    ``"swap": 1`` are plans of the swapped problem (C^T = W X^T, tokens in the MMA's N)."""
 
     def __init__(self, table: Optional[dict]):
         self.by_nk = {}
         for e in (table or {}).get("entries", []):
-            self.by_nk.setdefault((int(e["n"]), int(e["k"])), []).append(
-                (int(e["m"]), int(e["bn"]), int(e["splits"]), int(e.get("mt", 1))))
+            key = (int(e["n"]), int(e["k"]), int(e.get("swap", 0)))
+            self.by_nk.setdefault(key, []).append(
+                (int(e["m"]), int(e["bn"]), int(e["splits"]), int(e.get("mt", 1)),
+                 float(e.get("us", 0.0))))
         for v in self.by_nk.values():
             v.sort()
 
-    def lookup(self, M: int, N: int, K: int):
-        rows = self.by_nk.get((N, K))
+    def entry(self, M: int, N: int, K: int, swap: bool = False):
+        rows = self.by_nk.get((N, K, int(swap)))
         if not rows:
             return None
         i = bisect.bisect_left([r[0] for r in rows], M)
         if i == len(rows):
             return None  # larger than anything measured: cost model decides
-        _, bn, s, mt = rows[i]
-        return bn, s, mt
+        return rows[i]
+
+    def lookup(self, M: int, N: int, K: int):
+        e = self.entry(M, N, K)
+        return None if e is None else e[1:4]
+
+    def swap_plan(self, M: int, N: int, K: int):
+        """(bn, splits, mt) of the swapped problem when it was measured faster, else None."""
+        s, d = self.entry(M, N, K, True), self.entry(M, N, K, False)
+        if s is None or (d is not None and d[0] == s[0] and d[4] <= s[4]):
+            return None
+        return s[1:4]
 
 
 @lru_cache(maxsize=None)
