@@ -228,6 +228,69 @@ void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
   count_launch();
 }
 
+// ------------------------------------------------------------------------------ sampling
+__global__ void __launch_bounds__(256) cand_exchange_kernel(CandParams a) {
+  __shared__ uint32_t epoch_s;
+  __shared__ int ok_all;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < a.R) {
+    for (int p = 0; p < a.world; ++p) {
+      a.vals[p][(size_t)a.rank * a.R + r] = a.my_vals[r];
+      a.ids[p][(size_t)a.rank * a.R + r] = a.my_ids[r];
+    }
+  }
+  __threadfence_system();
+  if (threadIdx.x == 0) {
+    epoch_s = a.epochs[blockIdx.x] + 1;
+    a.epochs[blockIdx.x] = epoch_s;
+    ok_all = 1;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_s;
+  if (threadIdx.x < a.world) {
+    const int p = threadIdx.x;
+    const size_t phase = 4 + a.parity;
+    uint32_t* peer_slot = a.flags[p] + (phase * kMaxBlocks + blockIdx.x) * kMaxRanks + a.rank;
+    st_release_sys(peer_slot, epoch);
+    const uint32_t* my_slot = a.flags[a.rank] + (phase * kMaxBlocks + blockIdx.x) * kMaxRanks + p;
+    const long long t0 = clock64();
+    while ((int32_t)(ld_acquire_sys(my_slot) - epoch) < 0) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        record_error(a.err, kErrPeerTimeout);
+        ok_all = 0;
+        break;
+      }
+      if (error_raised(a.err)) {
+        ok_all = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok_all || r >= a.R) return;
+  float bv = -INFINITY;
+  int64_t bi = a.my_ids[r];
+  for (int p = 0; p < a.world; ++p) {
+    const float v = a.vals[a.rank][(size_t)p * a.R + r];
+    const int64_t i = a.ids[a.rank][(size_t)p * a.R + r];
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  a.out[r] = bi;
+}
+
+void run_exchange_candidates(const CandParams& a, cudaStream_t s) {
+  B200_REQUIRE(a.world >= 2 && a.world <= kMaxRanks, "candidate exchange: world size");
+  if (a.R == 0) return;
+  const int blocks = (a.R + 255) / 256;
+  B200_REQUIRE(blocks <= kMaxBlocks, "candidate exchange: too many rows");
+  cand_exchange_kernel<<<blocks, 256, 0, s>>>(a);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
 // ------------------------------------------------------------------------------ IPC helpers
 void* ipc_malloc(size_t bytes) {
   void* p = nullptr;

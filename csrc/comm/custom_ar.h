@@ -10,8 +10,9 @@ namespace comm {
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 128;
-// flags region: [4 phases][kMaxBlocks][kMaxRanks] uint32, then the local epoch counters.
-constexpr size_t kFlagBytes = 4 * kMaxBlocks * kMaxRanks * sizeof(uint32_t);
+// flags region: [6 phases][kMaxBlocks][kMaxRanks] uint32 (all-reduce start / end barriers by
+// parity, sampling exchange by parity), then the local epoch counters.
+constexpr size_t kFlagBytes = 6 * kMaxBlocks * kMaxRanks * sizeof(uint32_t);
 constexpr size_t kEpochBytes = kMaxBlocks * sizeof(uint32_t);
 
 struct ArParams {
@@ -32,6 +33,22 @@ struct ArParams {
 };
 
 void run_fused_allreduce(const ArParams& a, cudaStream_t s);
+
+// Vocab-parallel sampling exchange: every rank's per-row (score, token) candidate is stored into
+// every peer's candidate region [src rank][row]; after a per-block epoch barrier each rank picks
+// the row maxima (ties -> smaller token id) from local memory.
+struct CandParams {
+  int rank, world, R, parity;
+  float* vals[kMaxRanks];      // this call's candidate score region of every rank [world][R]
+  int64_t* ids[kMaxRanks];     // this call's candidate id region of every rank [world][R]
+  uint32_t* flags[kMaxRanks];  // flag region of every rank (phases 4 / 5 by parity)
+  uint32_t* epochs;            // local per-block epoch counters (own slice)
+  const float* my_vals;        // [R] this rank's candidates
+  const int64_t* my_ids;
+  int64_t* out;                // [R] merged tokens
+  int* err;
+};
+void run_exchange_candidates(const CandParams& a, cudaStream_t s);
 void* ipc_malloc(size_t bytes);
 void ipc_free(void* p);
 std::string ipc_handle(void* p);

@@ -909,6 +909,35 @@ void ep_return(const Tensor& y, const Tensor& pos, const std::vector<int64_t>& i
   guarded([&] { b200::ep::run_return(p, y.data_ptr(), pos.data_ptr<int32_t>(), stream_of(y)); });
 }
 
+// Vocab-parallel sampling: exchange per-row candidates over NVLink and merge.
+// ptrs = [vals of every rank (world), ids of every rank (world), flags of every rank (world)]
+void exchange_candidates(const Tensor& vals, const Tensor& ids, Tensor& out,
+                         const std::vector<int64_t>& ptrs, int64_t epochs_ptr, int64_t rank,
+                         int64_t world, int64_t parity) {
+  CHECK_CUDA(vals);
+  TORCH_CHECK(vals.scalar_type() == at::kFloat && ids.scalar_type() == at::kLong &&
+                  out.scalar_type() == at::kLong && vals.is_contiguous() && ids.is_contiguous(),
+              "exchange_candidates: fp32 scores, int64 ids");
+  TORCH_CHECK((int64_t)ptrs.size() == 3 * world, "exchange_candidates: pointer table");
+  b200::comm::CandParams a{};
+  a.rank = rank;
+  a.world = world;
+  a.R = vals.size(0);
+  a.parity = parity;
+  for (int p = 0; p < world; ++p) {
+    a.vals[p] = reinterpret_cast<float*>(ptrs[p]);
+    a.ids[p] = reinterpret_cast<int64_t*>(ptrs[world + p]);
+    a.flags[p] = reinterpret_cast<uint32_t*>(ptrs[2 * world + p]);
+  }
+  a.epochs = reinterpret_cast<uint32_t*>(epochs_ptr);
+  a.my_vals = vals.data_ptr<float>();
+  a.my_ids = ids.data_ptr<int64_t>();
+  a.out = out.data_ptr<int64_t>();
+  a.err = err_ptr(vals);
+  const c10::cuda::CUDAGuard g(vals.device());
+  guarded([&] { b200::comm::run_exchange_candidates(a, stream_of(vals)); });
+}
+
 // Row-parallel GEMM whose epilogue performs the reduce-scatter: C rows go to their owner
 // rank's receive slot (`recv` = every rank's slot address, peers included).
 void gemm_bf16_rs(const Tensor& A, const Tensor& B, const std::vector<int64_t>& recv,
@@ -1074,6 +1103,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("two_shot"), py::arg("residual"), py::arg("weight"), py::arg("eps"),
         py::arg("rs_rows") = 0);
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel dispatch over NVLink (+ count exchange)");
+  m.def("exchange_candidates", &exchange_candidates,
+        "vocab-parallel sampling: per-row candidates exchanged over NVLink and merged");
   m.def("ep_return", &ep_return, "expert-parallel combine into the sources' staging slots");
   m.def("gemm_bf16_rs", &gemm_bf16_rs,
         "row-parallel GEMM with the reduce-scatter in its epilogue (NVLink stores)",

@@ -60,6 +60,13 @@ def test_moe_ep2_all_to_all_matches_tp1(tmp_path, eager):
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_sampling_candidate_exchange_2gpu(tmp_path):
+    out = str(tmp_path / "cand.json")
+    _torchrun(2, ["--mode", "cand", "--out", out], 29661)
+    assert json.load(open(out))["mismatches"] == 0
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
 def test_gemm_reduce_scatter_fused_2gpu(tmp_path):
     out = str(tmp_path / "rs.json")
     _torchrun(2, ["--mode", "gemm_rs", "--out", out], 29631)

@@ -121,6 +121,40 @@ def mode_gemm_rs(out_path):
     dist.destroy_process_group()
 
 
+def mode_cand(out_path):
+    """Vocab-parallel sampling candidate exchange (NVLink stores + epoch barrier + merge in one
+    kernel) against NCCL all-gather + argmax, with ties broken toward the smaller token id."""
+    from vllm_musa_b200.parallel.custom_ar import maybe_create_custom_allreduce
+    from vllm_musa_b200.parallel.state import init_distributed
+    world = int(os.environ["WORLD_SIZE"])
+    st = init_distributed(tp_size=world)
+    dev = torch.device("cuda", st.local_rank)
+    ar = maybe_create_custom_allreduce(st, dev, max_tokens=512, hidden=1024)
+    assert ar is not None
+    bad = 0
+    for it, R in enumerate([1, 5, 256, 300, 512, 2]):
+        g = torch.Generator(device="cpu").manual_seed(10 * it + st.rank)
+        vals = torch.randint(0, 4, (R,), generator=g).float().to(dev)  # many ties across ranks
+        ids = (torch.randint(0, 1000, (R,), generator=g) + 1000 * st.rank).to(dev)
+        got = ar.merge_candidates(vals, ids)
+        av = [torch.empty_like(vals) for _ in range(world)]
+        ai = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(av, vals, group=st.tp_group)
+        dist.all_gather(ai, ids, group=st.tp_group)
+        V, I = torch.stack(av).cpu(), torch.stack(ai).cpu()
+        key = torch.where(V == V.max(0).values, I, torch.full_like(I, 1 << 40))
+        ref = key.min(0).values
+        bad += int((got.cpu() != ref).sum())
+    from vllm_musa_b200 import ops
+    ops._ext.check_device_errors()
+    ar.close()
+    if st.rank == 0:
+        with open(out_path, "w") as f:
+            json.dump({"mismatches": bad}, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def moe_cfg():
     from vllm_musa_b200.config import ModelConfig
     return ModelConfig(arch="qwen3_moe", vocab_size=4096, hidden_size=1024, num_layers=3,
@@ -162,7 +196,7 @@ def mode_llm(out_path, tp, eager, model="dense", ep=False):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["ar", "gemm_rs", "llm"], required=True)
+    ap.add_argument("--mode", choices=["ar", "gemm_rs", "cand", "llm"], required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
@@ -173,5 +207,7 @@ if __name__ == "__main__":
         mode_ar(a.out)
     elif a.mode == "gemm_rs":
         mode_gemm_rs(a.out)
+    elif a.mode == "cand":
+        mode_cand(a.out)
     else:
         mode_llm(a.out, a.tp, a.eager, a.model, a.ep)

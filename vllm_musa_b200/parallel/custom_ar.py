@@ -50,7 +50,14 @@ class CustomAllReduce:
         # rows + world: the epilogue reduce-scatter lays out world blocks of ceil(T/world) rows
         self.slot = ((max_tokens + self_world_pad(st)) * hidden * 2 + 255) // 256 * 256
         self.flag_off = 4 * self.slot
-        total = self.flag_off + mod.comm_flag_bytes()
+        # sampling candidates: [2 parities][world][max_tokens] fp32 scores + int64 ids
+        self.cand_rows = max_tokens
+        self.cand_off = self.flag_off + (mod.comm_flag_bytes() + 255) // 256 * 256
+        n = self.world * max_tokens
+        self.cand_ids_off = (n * 4 + 255) // 256 * 256   # int64 ids after the fp32 scores
+        self.cand_parity_bytes = self.cand_ids_off + (n * 8 + 255) // 256 * 256
+        cand_bytes = 2 * self.cand_parity_bytes
+        total = self.cand_off + cand_bytes
         self.max_blocks = int(mod.comm_max_blocks())
         self.base = mod.ipc_malloc(total)
         self.opened = []
@@ -77,6 +84,7 @@ class CustomAllReduce:
             flags = [b + self.flag_off for b in self.peer_base]
             self._bufs.append(staging + out + flags)
         self.parity = 0
+        self.cand_parity = 0
 
     # ------------------------------------------------------------------ interface
     def begin_forward(self) -> None:
@@ -131,6 +139,28 @@ class CustomAllReduce:
         out = self._out[self.parity][:T]
         self.parity ^= 1
         return out, residual
+
+    def merge_candidates(self, vals: torch.Tensor, ids: torch.Tensor) -> Optional[torch.Tensor]:
+        """Vocab-parallel sampling: each rank's per-row (score, token) goes into every peer's
+        candidate region by NVLink stores; one kernel barriers and merges (no NCCL).
+
+        Returns None when the batch does not fit the region (caller falls back to NCCL).
+        A rank can only overwrite a peer's region in its next call after a collective of the
+        forward pass in between has seen that peer finish this call, and the two parities
+        alternate as well, so no end-of-call barrier is needed."""
+        R = vals.shape[0]
+        if R > self.cand_rows or R > 128 * 256:
+            return None
+        k = self.cand_parity
+        vals_ptrs = [b + self.cand_off + k * self.cand_parity_bytes for b in self.peer_base]
+        ids_ptrs = [v + self.cand_ids_off for v in vals_ptrs]
+        flags = [b + self.flag_off for b in self.peer_base]
+        out = torch.empty_like(ids)
+        self.mod.exchange_candidates(vals.contiguous(), ids.contiguous(), out,
+                                     vals_ptrs + ids_ptrs + flags, self.epochs, self.rank,
+                                     self.world, k)
+        self.cand_parity ^= 1
+        return out
 
     def can_fuse_gemm(self, T: int) -> bool:
         """Row-parallel GEMM + all-reduce as one reduce-scatter-in-epilogue GEMM and a local

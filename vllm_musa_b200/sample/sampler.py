@@ -4,7 +4,9 @@ Each tensor-parallel rank holds the logits of its vocab shard.  Instead of all-g
 full [S, V] logits (the reference's path: patch 0069 IPC all-gather, then top-k/top-p,
 vllm_musa/distributed/device_communicators/musa_jit_custom_all_reduce.py:1941-1956), every
 rank reduces its shard to one (score, token) candidate per row with the Gumbel-max sampler,
-ranks exchange the [S] candidates, and the max wins: identical on every rank because the
+ranks exchange the [S] candidates (one kernel storing them into every peer's candidate region
+over NVLink, then an epoch barrier and the merge, when the P2P communicator is up; NCCL
+all-gather otherwise), and the max wins: identical on every rank because the
 Gumbel noise is a function of (seed, step, global token id).  Rows that use top-k / top-p /
 min-p need global order statistics, so those batches gather the full logits first.
 """
@@ -37,6 +39,11 @@ class Sampler:
                                      generator=generator)
         ids, vals = ops.sample_tokens(logits, temperature, None, None, None, seeds, steps,
                                       vocab_offset=self.vocab_start, return_values=True)
+        custom = getattr(self.comm, "custom", None)
+        if logits.is_cuda and custom is not None:
+            merged = custom.merge_candidates(vals, ids)  # NVLink exchange + merge, one kernel
+            if merged is not None:
+                return merged
         all_vals = self.comm.all_gather(vals.unsqueeze(0), dim=0)   # [tp, S]
         all_ids = self.comm.all_gather(ids.unsqueeze(0), dim=0)
         if logits.is_cuda:
