@@ -40,7 +40,8 @@ L2_BYTES = 126 << 20
 
 
 def s_ok(M):
-    return M >= 1024
+    """CTA-pair plans (256-row tiles) are tried above one 128-row tile."""
+    return M > 128
 
 
 def timed(fn, ws, reps):
@@ -86,7 +87,7 @@ def main():
                            ws, a.reps)
             best = (t_auto, auto[0], auto[1], auto[3])
             kb = (K + 63) // 64
-            for mt in ((1, 2, 4) if M >= 1024 else (1, 2) if M > 128 else (1,)):
+            for mt in ((1, 2, 4) if M > 128 else (1,)):
                 for bn in (256, 224, 208, 192, 176, 160, 144, 128, 112, 96, 64, 48, 32):
                     if mt == 4 and (bn % 32 or bn < 128):  # CTA pairs: 256-row tiles
                         continue
@@ -94,7 +95,8 @@ def main():
                         continue
                     if M >= 1024 and mt != 4 and (bn % 64 or mt * bn * 2 > 512):
                         continue
-                    for s in ((1,) if M >= 1024 or mt == 4 else (1, 2, 3, 4, 6, 8)):
+                    for s in ((1,) if M >= 1024 else (1, 2, 3, 4) if mt == 4 else
+                              (1, 2, 3, 4, 6, 8)):
                         if s > 1 and kb // s < 4:
                             continue
                         if s * M * N > (64 << 20):
@@ -136,8 +138,8 @@ def main():
         old = {"entries": []}
         if os.path.exists(path):
             old = json.load(open(path))
-        keep = [e for e in old["entries"]
-                if (e["n"], e["k"]) not in {(x["n"], x["k"]) for x in entries}]
+        fresh = {(x["n"], x["k"], x["m"]) for x in entries}
+        keep = [e for e in old["entries"] if (e["n"], e["k"], e["m"]) not in fresh]
         table["entries"] = keep + entries
         with open(path, "w") as f:
             json.dump(table, f, indent=1)

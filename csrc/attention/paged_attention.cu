@@ -645,6 +645,10 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
   B200_REQUIRE(a.block_size % 16 == 0 && (a.block_size <= 64 || a.block_size % 64 == 0),
                "prefill: block_size must be 16, 32, 64 or a multiple of 64");
   B200_REQUIRE((a.ld_q * 2) % 16 == 0, "prefill: q row stride must be a multiple of 16 bytes");
+  if (prefill_tc_enabled(a.D)) {
+    run_prefill_tc(a, stream);
+    return;
+  }
   const int box_rows = std::min(a.block_size, CH);
   const int64_t cache_rows = (int64_t)a.num_blocks * a.Hkv * a.block_size;
   const CUtensorMap tk = cache_map(a.k_cache, cache_rows, a.D, box_rows);

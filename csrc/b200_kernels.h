@@ -215,6 +215,10 @@ struct PrefillArgs {
   float scale;
   int* err;
 };
+// head_dim 128 prefill on tcgen05 (prefill_tc.cu); B200_ATTN_TC=0 selects the mma.sync kernel.
+bool prefill_tc_enabled(int D);
+void set_prefill_tc(bool on);
+void run_prefill_tc(const PrefillArgs& a, cudaStream_t stream);
 int decode_num_splits(int B, int Hkv, int max_seq_len);
 void run_decode(const DecodeArgs& a, cudaStream_t s);
 void run_prefill(const PrefillArgs& a, cudaStream_t s);

@@ -71,6 +71,14 @@ B200_DEVICE uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
+// 2^x with the PTX ex2.approx.ftz instruction (the SFU's base-2 exponential; results below
+// the normal range flush to zero, which softmax weights can afford).
+B200_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 B200_DEVICE uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

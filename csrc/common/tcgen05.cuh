@@ -8,7 +8,7 @@
 //              offset>>4, [46,48) version=1, [49,52) base offset, [52] lbo mode,
 //              [61,64) layout (0 none, 2 = 128B swizzle, 4 = 64B, 6 = 32B)
 //   instr desc (kind::f16): [4,6) D fmt (1=f32), [7,10) A fmt (0 f16, 1 bf16), [10,13) B fmt,
-//              [15] A major (0=K), [16] B major, [17,23) N>>3, [24,29) M>>4
+//              [15] A major (0=K), [16] B major (1=MN), [17,23) N>>3, [24,29) M>>4
 //   (kind::f8f6f4 uses the same fields with A/B formats 0 = e4m3, 1 = e5m2)
 #pragma once
 #include "common.cuh"
@@ -57,6 +57,18 @@ B200_DEVICE uint64_t smem_desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// MN-major operand with 128-byte swizzle (rows of 64 contiguous 16-bit MN elements, one row
+// per K index): 8-row K groups are `sbo` bytes apart, 64-element MN groups `lbo` bytes apart.
+B200_DEVICE uint64_t smem_desc_mnmajor_sw128(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)kSwizzle128B << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation, both operands K-major.
 template <bool kBf16>
 B200_HOST_DEVICE constexpr uint32_t idesc_f16(int M, int N) {
@@ -99,6 +111,18 @@ B200_DEVICE void mma_f8f6f4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc
       : "memory");
 }
 
+// A from tensor memory (lane = row, two 16-bit K elements per 32-bit column), B from shared
+// memory through its descriptor.
+B200_DEVICE void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once every previously issued MMA of this thread has completed.
 B200_DEVICE void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -135,6 +159,21 @@ B200_DEVICE void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 B200_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// registers -> TMEM: thread t of the warp writes 32 consecutive 32-bit columns of lane (base+t).
+B200_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+B200_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------
 // CTA-pair (cta_group::2) variants: one MMA spans the TMEM of both CTAs of a 2-CTA cluster

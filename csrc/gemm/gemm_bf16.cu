@@ -556,7 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // independent 128 x BN tiles.  Both CTAs' TMA loads complete on the leader's full barrier; the
 // leader's single MMA thread commits to the empty / accumulator barriers of both CTAs
 // (tcgen05.commit multicast); both CTAs' epilogue warps release the accumulator on the
-// leader's barrier (8 arrivals).  No split-K.
+// leader's barrier (8 arrivals).  Split-K as in the one-CTA kernel, per 128-row half tile
+// (decode-sized M = 256: one row tile, the K splits fill the SM pairs).
 // ---------------------------------------------------------------------------------------------
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -615,7 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = pair; u < p.total_units && ok; u += npairs) {
         int m, n, ks;
         unit_coords(u, p, m, n, ks);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int kb0 = ks * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) {
             ok = false;
             break;
@@ -650,10 +652,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int u = pair; u < p.total_units && ok; u += npairs) {
+        int m, n, ks;
+        unit_coords(u, p, m, n, ks);
+        const int kb0 = ks * p.kb_per_split, kb1 = min(p.num_kb, kb0 + p.kb_per_split);
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err)) break;
         tc::fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err)) {
             ok = false;
             break;
@@ -665,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             tc::mma_f16_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc,
-                                (kb > 0 || k > 0) ? 1u : 0u);
+                                (kb > kb0 || k > 0) ? 1u : 0u);
           tc::mma_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
@@ -681,7 +686,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    __shared__ int s_last;
     const int q = warp & 3;
+    const bool split = p.splits > 1;
     const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -705,6 +712,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 2; ++h) {
           const int col = n * BN + c + 16 * h;
           if ((h == 1 && !two) || col >= p.N) continue;
+          if (split) {
+            float* w = p.ws + ((size_t)ks * p.M + row) * p.N + col;
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col + 4 * v < p.N)
+                reinterpret_cast<float4*>(w)[v] = make_float4(
+                    __uint_as_float(r[h][4 * v]), __uint_as_float(r[h][4 * v + 1]),
+                    __uint_as_float(r[h][4 * v + 2]), __uint_as_float(r[h][4 * v + 3]));
+            continue;
+          }
           float f[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(r[h][j]);
@@ -717,6 +734,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (++acc == p.acc_bufs) {
         acc = 0;
         acc_phase ^= 1;
+      }
+      if (split) {
+        // per 128-row half tile: the last of the K splits to finish sums the partials
+        __threadfence();
+        epi_barrier();
+        const int tile = (m * 2 + (int)crank) * p.num_n + n;
+        if (warp == 2 && lane == 0) s_last = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+        epi_barrier();
+        if (s_last) {
+          __threadfence();
+          if (row_ok) {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+              const int col = n * BN + c;
+              if (col >= p.N) break;
+              float f[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) f[j] = 0.f;
+              for (int sp = 0; sp < p.splits; ++sp) {
+                const float4* w =
+                    reinterpret_cast<const float4*>(p.ws + ((size_t)sp * p.M + row) * p.N + col);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                  if (col + 4 * v >= p.N) break;
+                  const float4 t = __ldcg(w + v);
+                  f[4 * v] += t.x;
+                  f[4 * v + 1] += t.y;
+                  f[4 * v + 2] += t.z;
+                  f[4 * v + 3] += t.w;
+                }
+              }
+              store_chunk16<EPI>(p, row, col, f);
+            }
+          }
+          epi_barrier();
+          if (warp == 2 && lane == 0) p.counters[tile] = 0;
+        }
       }
     }
   }
@@ -991,15 +1045,16 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   const bool transposed = a.mode == kModeStoreT || a.mode == kModeSiluT;
   B200_REQUIRE(a.mode != kModeSiluT || M % 16 == 0,
                "gemm_bf16 swapped SiLU: weight rows must be a multiple of 16");
-  const bool pair_ok = a.mode != kModeScatter && !transposed && M >= 2 * BM;
+  const bool pair_ok = a.mode != kModeScatter && !transposed && M > BM;
   // automatic use (no measured plan): large M and not too wide -- at M = 8192 the pair tiles
   // measured 0.95 / 0.89 of cuBLAS on N = 4096 (K = 14336 / 4096) but lost on N = 28672
   const bool pair = a.mt == 4 ? pair_ok
                               : (a.mt == 0 && a.bn <= 0 && a.splits <= 0 && pair_ok &&
-                                 M >= pair_min_rows() && N <= 16384 && plan.splits <= 1);
+                                 M >= std::max(2 * BM, pair_min_rows()) && N <= 16384 &&
+                                 plan.splits <= 1);
   if (pair) {
     plan.mt = 1;
-    plan.splits = 1;
+    plan.splits = a.mt == 4 && a.splits > 0 ? a.splits : 1;
     plan.bn = a.mt == 4 && a.bn > 0 && a.bn % 32 == 0 ? a.bn : pair_bn(M, N);
   }
   B200_REQUIRE(plan.bn >= 16 && plan.bn <= 256 && plan.bn % 16 == 0,
@@ -1059,7 +1114,8 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     const int64_t need = (int64_t)p.splits * M * N;
     B200_REQUIRE(a.workspace != nullptr && a.workspace_numel >= need,
                  "gemm_bf16: split-K workspace too small");
-    B200_REQUIRE(a.counters != nullptr && a.counters_numel >= (int64_t)p.num_m * p.num_n,
+    B200_REQUIRE(a.counters != nullptr &&
+                     a.counters_numel >= (int64_t)p.num_m * p.num_n * (pair ? 2 : 1),
                  "gemm_bf16: split-K tile counters too small");
     p.ws = a.workspace;
     p.counters = a.counters;

@@ -59,11 +59,13 @@ def test_gemm_silu_forced_plans(bn, splits, mt):
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("M,N,K,bn,mode", [(256, 512, 1024, 256, 0), (1000, 784, 2048, 256, 0),
-                                           (2048, 4096, 4096, 192, 0), (777, 1024, 512, 128, 1),
-                                           (4096, 2000, 1024, 224, 2), (300, 96, 256, 64, 0)])
-def test_gemm_bf16_cta_pair(M, N, K, bn, mode):
-    """CTA-pair (cta_group::2) tiles: 256 x bn per 2-CTA cluster, forced with mt=4."""
+@pytest.mark.parametrize("M,N,K,bn,mode,splits", [
+    (256, 512, 1024, 256, 0, 1), (1000, 784, 2048, 256, 0, 1), (2048, 4096, 4096, 192, 0, 1),
+    (777, 1024, 512, 128, 1, 1), (4096, 2000, 1024, 224, 2, 1), (300, 96, 256, 64, 0, 1),
+    (256, 4096, 4096, 256, 0, 4), (200, 1024, 2048, 128, 1, 3), (512, 2000, 1024, 192, 2, 2)])
+def test_gemm_bf16_cta_pair(M, N, K, bn, mode, splits):
+    """CTA-pair (cta_group::2) tiles: 256 x bn per 2-CTA cluster, forced with mt=4, with and
+    without split-K."""
     a = _bf(M, K, seed=21)
     if mode == 1:
         g, u = _bf(N // 2, K, seed=22, scale=0.05), _bf(N // 2, K, seed=23, scale=0.05)
@@ -74,7 +76,7 @@ def test_gemm_bf16_cta_pair(M, N, K, bn, mode):
         b = _bf(N, K, seed=24, scale=0.05)
         ref = a.float() @ b.float().t()
         out = torch.empty(M, N, dtype=torch.float32 if mode == 2 else torch.bfloat16, device=DEV)
-    ops.gemm._run(a, b, out, mode, bn, 1, 4)
+    ops.gemm._run(a, b, out, mode, bn, splits, 4)
     torch.cuda.synchronize()
     _ext.check_device_errors()
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
@@ -236,6 +238,38 @@ def test_paged_prefill_chunked(D, Hq, Hkv, bs, window):
     scale = 1.0 / math.sqrt(D)
     ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale, window)
     out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale, window)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("bs,window,qscale", [(64, 0, 1.0), (16, 0, 4.0), (128, 0, 8.0),
+                                               (64, 300, 4.0)])
+@pytest.mark.parametrize("tc", [True, False])
+def test_paged_prefill_long(bs, window, qscale, tc):
+    """Long prompts and cached contexts on both head_dim-128 prefill kernels (tcgen05 with TMEM
+    S/P/O, and the mma.sync one): several 128-key blocks, partial tiles, large logits (lazy
+    rescaling of O in TMEM), sliding window."""
+    D, Hq, Hkv = 128, 16, 4
+    reqs = [(0, 1024), (300, 700), (2000, 257), (0, 129), (127, 1)]
+    R = len(reqs)
+    lens = [c + n for c, n in reqs]
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=41)
+    bt = _random_tables(R, lens, bs, nb, seed=5)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([n for _, n in reqs]), 0)), dtype=torch.int32)
+    T = int(cu[-1])
+    q = (_bf(T, (Hq + 2 * Hkv) * D, seed=42).float() * qscale).to(torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale, window)
+    mod = _ext.require()
+    mod.set_prefill_tc(tc)
+    try:
+        out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale,
+                                window)
+        torch.cuda.synchronize()
+    finally:
+        mod.set_prefill_tc(True)
+    _ext.check_device_errors()
     torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
 
 
