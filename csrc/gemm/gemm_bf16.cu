@@ -1052,6 +1052,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
                               : (a.mt == 0 && a.bn <= 0 && a.splits <= 0 && pair_ok &&
                                  M >= std::max(2 * BM, pair_min_rows()) && N <= 16384 &&
                                  plan.splits <= 1);
+  if (!pair && plan.mt == 4) plan.mt = 1;  // a CTA-pair plan for an epilogue pairs lack
   if (pair) {
     plan.mt = 1;
     plan.splits = a.mt == 4 && a.splits > 0 ? a.splits : 1;
