@@ -147,6 +147,11 @@ void run_rms_norm(const RmsNormArgs& a, cudaStream_t s);
 void run_rms_norm_gated(void* out, int64_t ldo, const void* x, int64_t ldx, const void* z,
                         int64_t ldz, const void* w, int rows, int H, int group, float eps,
                         cudaStream_t s);
+// (residual += x;) y = RMSNorm(residual or x) * w -> e4m3 [rows, H] + fp32 1x128 scales
+// (+ bf16 y when `out` is non-null).
+void run_rms_norm_quant_fp8(void* q, int64_t ld_q, float* scales, void* out, int64_t ld_out,
+                            const void* x, int64_t ld_x, void* residual, int64_t ld_res,
+                            const void* weight, int rows, int H, float eps, cudaStream_t s);
 }  // namespace norm
 
 // ------------------------------------------------------------------------------- activations

@@ -94,6 +94,124 @@ __global__ void rmsnorm_gated_kernel(__nv_bfloat16* __restrict__ out, int64_t ld
   }
 }
 
+// (residual add +) RMSNorm + per-token 1x128 e4m3 quantisation in one pass: the normalised
+// row stays in registers; each 128-element group is 16 consecutive 8-element vectors held by
+// 16 consecutive lanes (blockDim is a multiple of 16), so the group amax is a half-warp
+// shuffle reduction.  Writes e4m3 [rows, H] + fp32 scales [rows, H/128] (scale = amax / 448)
+// and, when `out` is non-null, the bf16 normalised row as well (consumers that need both).
+// Reference counterpart: csrc/musa/quantization/fused_add_rms_norm_per_token_group_fp8_quant.cu:59
+// (hidden fixed at 4096 there; any multiple of 128 here).
+template <int VPT, bool kAdd>
+__global__ void rmsnorm_quant_kernel(__nv_fp8_e4m3* __restrict__ q, int64_t ld_q,
+                                     float* __restrict__ scales, __nv_bfloat16* __restrict__ out,
+                                     int64_t ld_out, const __nv_bfloat16* __restrict__ x,
+                                     int64_t ld_x, __nv_bfloat16* __restrict__ residual,
+                                     int64_t ld_res, const __nv_bfloat16* __restrict__ w, int H,
+                                     float eps) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  const int row = blockIdx.x;
+  const int nvec = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ld_x);
+  uint4* rr = kAdd ? reinterpret_cast<uint4*>(residual + row * ld_res) : nullptr;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    if (c < nvec) {
+      unpack8(xr[c], v[i]);
+      if constexpr (kAdd) {
+        float r[8];
+        unpack8(rr[c], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+        const uint4 packed = pack8(v[i]);
+        rr[c] = packed;
+        unpack8(packed, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / H + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  const int groups = H / 128;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    const bool live = c < nvec;
+    float o[8];
+    float amax = 0.f;
+    if (live) {
+      float wf[8];
+      unpack8(wr[c], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * wf[j];
+      const uint4 ob = pack8(o);
+      if (out != nullptr) reinterpret_cast<uint4*>(out + row * ld_out)[c] = ob;
+      unpack8(ob, o);  // quantise the bf16-rounded value, like norm-then-quant would
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(o[j]));
+    }
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1)
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (!live) continue;
+    const float scale = fmaxf(amax, 1e-10f) / 448.f;
+    const float qi = 1.f / scale;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_fp8_e4m3 a(o[j] * qi), b(o[4 + j] * qi);
+      lo |= (uint32_t)(*reinterpret_cast<const uint8_t*>(&a)) << (8 * j);
+      hi |= (uint32_t)(*reinterpret_cast<const uint8_t*>(&b)) << (8 * j);
+    }
+    reinterpret_cast<uint2*>(q + row * ld_q)[c] = make_uint2(lo, hi);
+    if ((c & 15) == 0) scales[(size_t)row * groups + c / 16] = scale;
+  }
+}
+
+void run_rms_norm_quant_fp8(void* q, int64_t ld_q, float* scales, void* out, int64_t ld_out,
+                            const void* x, int64_t ld_x, void* residual, int64_t ld_res,
+                            const void* weight, int rows, int H, float eps, cudaStream_t s) {
+  B200_REQUIRE(H % 128 == 0, "rms_norm_quant_fp8: hidden size must be a multiple of 128");
+  B200_REQUIRE(ld_q % 8 == 0, "rms_norm_quant_fp8: fp8 row stride must be a multiple of 8");
+  if (rows == 0) return;
+  const int nvec = H / 8;
+  int threads = 128;
+  while (threads < 1024 && (nvec + threads - 1) / threads > 4) threads *= 2;
+  const int vpt = (nvec + threads - 1) / threads;
+#define B200_NQ(V, ADD)                                                                         \
+  rmsnorm_quant_kernel<V, ADD><<<rows, threads, 0, s>>>(                                         \
+      reinterpret_cast<__nv_fp8_e4m3*>(q), ld_q, scales, reinterpret_cast<__nv_bfloat16*>(out), \
+      ld_out, reinterpret_cast<const __nv_bfloat16*>(x), ld_x,                                   \
+      reinterpret_cast<__nv_bfloat16*>(residual), ld_res,                                        \
+      reinterpret_cast<const __nv_bfloat16*>(weight), H, eps)
+#define B200_NQV(ADD)            \
+  if (vpt <= 1)                  \
+    B200_NQ(1, ADD);             \
+  else if (vpt <= 2)             \
+    B200_NQ(2, ADD);             \
+  else if (vpt <= 4)             \
+    B200_NQ(4, ADD);             \
+  else                           \
+    B200_NQ(8, ADD);
+  B200_REQUIRE(vpt <= 8, "rms_norm_quant_fp8: hidden size too large");
+  if (residual) {
+    B200_NQV(true)
+  } else {
+    B200_NQV(false)
+  }
+#undef B200_NQV
+#undef B200_NQ
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
 template <bool kAdd, bool kGemma>
 static void launch_vpt(const RmsNormArgs& a, cudaStream_t s) {
   const int nvec = a.H / 8;

@@ -218,6 +218,40 @@ void fused_add_rms_norm(Tensor& x, Tensor& residual, const Tensor& w, double eps
   guarded([&] { b200::norm::run_rms_norm(a, stream_of(x)); });
 }
 
+void rms_norm_quant_fp8(Tensor& q, Tensor& scales, std::optional<Tensor> out, Tensor& x,
+                       std::optional<Tensor> residual, const Tensor& w, double eps) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_ROWMAJOR(x);
+  CHECK_ROWMAJOR(q);
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn, "rms_norm_quant_fp8: q must be e4m3");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.is_contiguous(),
+              "rms_norm_quant_fp8: scales must be contiguous fp32");
+  const int64_t rows = x.size(0), H = x.size(1);
+  TORCH_CHECK(q.size(0) == rows && q.size(1) == H, "rms_norm_quant_fp8: q shape");
+  TORCH_CHECK(scales.numel() >= rows * (H / 128), "rms_norm_quant_fp8: scales too small");
+  TORCH_CHECK(w.is_contiguous() && w.numel() == H, "rms_norm_quant_fp8: weight");
+  if (out) {
+    CHECK_BF16(*out);
+    CHECK_ROWMAJOR(*out);
+    TORCH_CHECK(out->size(0) == rows && out->size(1) == H, "rms_norm_quant_fp8: out shape");
+  }
+  if (residual) {
+    CHECK_BF16(*residual);
+    CHECK_ROWMAJOR(*residual);
+    TORCH_CHECK(residual->sizes() == x.sizes(), "rms_norm_quant_fp8: residual shape");
+  }
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::norm::run_rms_norm_quant_fp8(
+        q.data_ptr(), q.stride(0), scales.data_ptr<float>(), out ? out->data_ptr() : nullptr,
+        out ? out->stride(0) : 0, x.data_ptr(), x.stride(0),
+        residual ? residual->data_ptr() : nullptr, residual ? residual->stride(0) : 0,
+        w.data_ptr(), (int)rows, (int)H, (float)eps, stream_of(x));
+  });
+}
+
 void rms_norm_gated(Tensor& out, const Tensor& x, const Tensor& z, const Tensor& w, int64_t group,
                     double eps) {
   CHECK_CUDA(x);
@@ -992,6 +1026,9 @@ TORCH_LIBRARY(b200, m) {
       "fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor weight, float eps, "
       "bool gemma=False) -> ()");
   m.def(
+      "rms_norm_quant_fp8(Tensor(a!) q, Tensor(b!) scales, Tensor(c!)? out, Tensor(d!) x, "
+      "Tensor(e!)? residual, Tensor weight, float eps) -> ()");
+  m.def(
       "rms_norm_gated(Tensor(a!) out, Tensor x, Tensor z, Tensor weight, int group, float eps) -> ()");
   m.def("act_and_mul(Tensor(a!) out, Tensor x, int kind=0, float limit=0.0) -> ()");
   m.def("silu_mul_fp8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
@@ -1060,6 +1097,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
   m.impl("fused_add_rms_norm", &fused_add_rms_norm);
   m.impl("rms_norm_gated", &rms_norm_gated);
+  m.impl("rms_norm_quant_fp8", &rms_norm_quant_fp8);
   m.impl("act_and_mul", &act_and_mul);
   m.impl("silu_mul_fp8_quant", &silu_mul_fp8_quant);
   m.impl("group_quant_fp8", &group_quant_fp8);

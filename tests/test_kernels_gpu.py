@@ -335,3 +335,24 @@ def test_embedding_and_gather():
     x = _bf(50, 4096, seed=2)
     idx = torch.tensor([0, 49, 3, 3], dtype=torch.int32, device=DEV)
     assert torch.equal(ops.gather_rows(x, idx), x[idx.long()])
+
+
+@pytest.mark.parametrize("rows,H,add,want", [(1, 7168, True, False), (37, 4096, False, True),
+                                             (256, 1536, True, True), (5, 128, False, False)])
+def test_rms_norm_quant_fp8(rows, H, add, want):
+    """Fused (residual add +) RMSNorm + 1x128 e4m3 quantisation against the PyTorch path."""
+    x = _bf(rows, H, seed=61, scale=2.0)
+    w = (_bf(H, 1, seed=62).view(H) * 0.2 + 1).to(torch.bfloat16)
+    res = _bf(rows, H, seed=63) if add else None
+    q, s, y = ops.rms_norm_quant_fp8(x, w, 1e-6, residual=res.clone() if add else None,
+                                     want_bf16=want)
+    rq, rs, ry = ops.rms_norm_quant_fp8(x.cpu(), w.cpu(), 1e-6,
+                                        residual=res.cpu().clone() if add else None,
+                                        want_bf16=True)
+    torch.cuda.synchronize()
+    _ext.check_device_errors()
+    torch.testing.assert_close(s.cpu(), rs, rtol=1e-2, atol=1e-6)
+    deq = q.cpu().float().view(rows, H // 128, 128) * s.cpu().unsqueeze(-1)
+    torch.testing.assert_close(deq.view(rows, H), ry.float(), rtol=0.07, atol=0.02)
+    if want:
+        torch.testing.assert_close(y.cpu().float(), ry.float(), rtol=1e-2, atol=1e-2)

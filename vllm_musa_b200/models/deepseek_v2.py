@@ -58,6 +58,10 @@ class Lin:
             return fp8_ops.linear_fp8(x, self.w, self.s, out)
         return ops.linear(x, self.w, out=out)
 
+    def quantized(self, q, sq, out=None):
+        """fp8 layer on an input already quantised per token (1x128 e4m3 + scales)."""
+        return fp8_ops.gemm_fp8(q, sq, self.w, self.s, out)
+
 
 class _Layer:
     __slots__ = ("ln1", "ln2", "w_a", "q_a_norm", "kv_a_norm", "w_qb", "w_kb", "w_vb", "o", "idx_ln_w",
@@ -460,21 +464,33 @@ class DeepseekV2ForCausalLM:
         self.comm.begin_forward()
         h = ops.embedding(input_ids, self.embed)
         residual = h
-        x = ops.rms_norm(h, self.layers[0].ln1, eps)
         n = len(self.layers)
+        # the attention input's only consumer is the fused q_a / kv_a projection: with fp8
+        # weights the norm quantises it in the same pass (1x128 e4m3 groups)
+        xq = None
+        if self.layers[0].w_a.fp8:
+            q0, s0, _ = ops.rms_norm_quant_fp8(h, self.layers[0].ln1, eps)
+            x, xq = h, (q0, s0)
+        else:
+            x = ops.rms_norm(h, self.layers[0].ln1, eps)
         for i, L in enumerate(self.layers):
-            a = self._attention(L, x, meta, kv_caches[i], T)
+            a = self._attention(L, x, meta, kv_caches[i], T, xq)
             o = L.o(a, out=self.comm.out_buffer(T))
             x, residual = self.comm.allreduce_add_rmsnorm(o, residual, L.ln2, eps)
             d = self._mlp(i, L, x, T)
-            nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
-            x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
+            if i + 1 < n and self.layers[i + 1].w_a.fp8:
+                x, residual, xq = self.comm.allreduce_add_rmsnorm_quant(
+                    d, residual, self.layers[i + 1].ln1, eps)
+            else:
+                nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
+                x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
+                xq = None
         return x
 
-    def _attention(self, L, x, meta, cache, T):
+    def _attention(self, L, x, meta, cache, T, xq=None):
         hq, eps = self.hq, self.cfg.rms_norm_eps
         lat_cache, idx_cache = cache
-        a = L.w_a(x)
+        a = L.w_a(x) if xq is None else L.w_a.quantized(*xq)
         kv = a[:, self.a_off["kv"]:self.a_off["kv"] + 576]
         if self.q_lora:
             q_a = ops.rms_norm(a[:, :self.q_lora], L.q_a_norm, eps)
@@ -489,7 +505,7 @@ class DeepseekV2ForCausalLM:
         indices = None
         if self.sparse:
             indices = self._indexer(L, q, a, meta, idx_cache, T)
-        o_lat = torch.empty(hq, T, 512, dtype=x.dtype, device=x.device)
+        o_lat = torch.empty(hq, T, 512, dtype=a.dtype, device=a.device)
         splits = self._splits(T)
         mla_ops.mla_attention(q_lat.transpose(0, 1), q3[:, :, 128:], lat_cache, meta.block_tables,
                               meta.cu_q, meta.seq_lens, indices, o_lat.transpose(0, 1),

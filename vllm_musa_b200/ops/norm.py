@@ -40,6 +40,30 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Te
     return x, residual
 
 
+def rms_norm_quant_fp8(x: torch.Tensor, weight: torch.Tensor, eps: float,
+                       residual: torch.Tensor | None = None, want_bf16: bool = False):
+    """(residual <- x + residual;) y = RMSNorm(residual or x) * w, quantised per token in 1x128
+    e4m3 groups in the same pass.  Returns (q [rows, H] e4m3, scales [rows, H/128] fp32, y bf16
+    or None).  Reference: csrc/musa/quantization/fused_add_rms_norm_per_token_group_fp8_quant.cu:59."""
+    rows, H = x.shape
+    if x.is_cuda:
+        q = torch.empty(rows, H, dtype=torch.float8_e4m3fn, device=x.device)
+        sc = torch.empty(rows, H // 128, dtype=torch.float32, device=x.device)
+        y = torch.empty_like(x) if want_bf16 else None
+        _ext.ops().rms_norm_quant_fp8(q, sc, y, x, residual, weight, eps)
+        return q, sc, y
+    if residual is not None:
+        s = (x.float() + residual.float()).to(x.dtype)
+        residual.copy_(s)
+        y = _rms_ref(s, weight, eps, False)
+    else:
+        y = _rms_ref(x, weight, eps, False)
+    g = y.float().view(rows, H // 128, 128)
+    sc = g.abs().amax(-1).clamp_min(1e-10) / 448.0
+    q = (g / sc.unsqueeze(-1)).view(rows, H).to(torch.float8_e4m3fn)
+    return q, sc, (y if want_bf16 else None)
+
+
 def rms_norm_gated(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, group: int,
                    eps: float) -> torch.Tensor:
     """RMSNorm over groups of ``group`` channels, times weight, times silu(z) (GDN output)."""

@@ -73,6 +73,18 @@ class TPCommunicator:
             dist.all_reduce(x, group=self.group)
         return ops.fused_add_rms_norm(x, residual, weight, eps)
 
+    def allreduce_add_rmsnorm_quant(self, x: torch.Tensor, residual: torch.Tensor,
+                                    weight: torch.Tensor, eps: float):
+        """Like ``allreduce_add_rmsnorm`` for a normalised output consumed by an fp8 GEMM:
+        returns (x, residual, (q, scales)) with x's rows quantised per token (1x128 e4m3).  One
+        GPU: residual add, RMSNorm and quantisation in one kernel (x is left unnormalised);
+        TP: the fused all-reduce + norm, then the group quantisation."""
+        if self.world > 1:
+            x, residual = self.allreduce_add_rmsnorm(x, residual, weight, eps)
+            return x, residual, ops.activation.group_quant_fp8(x)
+        q, sc, _ = ops.rms_norm_quant_fp8(x, weight, eps, residual=residual)
+        return x, residual, (q, sc)
+
     def linear_allreduce_add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor,
                                      residual: torch.Tensor, weight: torch.Tensor, eps: float
                                      ) -> tuple[torch.Tensor, torch.Tensor]:
