@@ -257,20 +257,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(s_col + 32 * c, s[c]);
       tc::tmem_ld_wait();
       const int kv0 = (first_blk + j) * kBK;
-      const bool need_mask = kv0 + kBK - 1 > my_pos || p.window > 0;
-      float mx = -INFINITY;
+      if (kv0 + kBK - 1 > my_pos || p.window > 0) {  // diagonal / window blocks only
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int kv = kv0 + 32 * c + i;
+            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window))
+              s[c][i] = __float_as_uint(-INFINITY);
+          }
+      }
+      // row max of the raw scores with 8 independent chains (one warp per scheduler: a
+      // single dependent chain of 128 max operations would dominate the block)
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(s[c][i]) * p.scale_log2;
-          if (need_mask) {
-            const int kv = kv0 + 32 * c + i;
-            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window)) v = -INFINITY;
-          }
-          s[c][i] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(s[c][i]));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mx8[k] = fmaxf(mx8[k], mx8[k + 4]);
+      const float mx = fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])) * p.scale_log2;
       const float m_new = fmaxf(m_ref, mx);
       float factor = 1.f;
       bool resc = false;
@@ -299,19 +307,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tmem_st_32x32b_x32(lane_base + kColO + 32 * c, o);
         }
       }
-      const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      float sum = 0.f;
+      // p = 2^(s * scale - m): one FMA + one ex2 per score, sums in 8 independent chains
+      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+      float sum8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
       uint32_t pk[2][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float a = ex2_approx(__uint_as_float(s[c][i]) - mu);
-          const float e = ex2_approx(__uint_as_float(s[c][i + 1]) - mu);
-          sum += a + e;
+          const float a = ex2_approx(fmaf(__uint_as_float(s[c][i]), p.scale_log2, neg_m));
+          const float e = ex2_approx(fmaf(__uint_as_float(s[c][i + 1]), p.scale_log2, neg_m));
+          sum8[(i >> 1) & 7] += a + e;
           pk[c >> 1][(c & 1) * 16 + i / 2] = pack_bf16x2(a, e);  // low half = even key
         }
-      l += sum;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sum8[k] += sum8[k + 4];
+      l += (sum8[0] + sum8[1]) + (sum8[2] + sum8[3]);
       tc::tmem_st_32x32b_x32(s_col, pk[0]);
       tc::tmem_st_32x32b_x32(s_col + 32, pk[1]);
       tc::tmem_st_wait();

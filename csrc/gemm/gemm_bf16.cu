@@ -465,8 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc = 0;
         acc_phase ^= 1;
       }
-      if (split) {
+      if (split && p.counters != nullptr) {
         // the last CTA to finish this output tile sums the partials and applies the epilogue
+        // (no counters: a separate reduction kernel does it after the grid)
         __threadfence();
         epi_barrier();
         const int tile = m * p.num_n + n;
@@ -735,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc = 0;
         acc_phase ^= 1;
       }
-      if (split) {
+      if (split && p.counters != nullptr) {
         // per 128-row half tile: the last of the K splits to finish sums the partials
         __threadfence();
         epi_barrier();
@@ -779,6 +780,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // the peer's remote arrivals and TMEM reads are done
   tc::fence_after_sync();
   if (warp == 1) tc::tmem_dealloc_pair(tmem_base, p.tmem_cols);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Split-K reduction as its own grid (programmatic dependent launch after the GEMM): one thread
+// per (row, 16 columns), consecutive threads on consecutive column chunks of a row, so every
+// split's partial rows are read with coalesced 16-byte loads; then the GEMM's epilogue.  Used
+// where the in-kernel last-arriver fixup would serialise behind one CTA per tile (CTA-pair
+// tiles with one unit per CTA).
+// ---------------------------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(Params p) {
+  pdl_wait();  // every split's partials are written
+  pdl_trigger();
+  const int chunks = (p.N + 15) / 16;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)p.M * chunks) return;
+  const int row = (int)(idx / chunks), col = (int)(idx % chunks) * 16;
+  float f[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) f[j] = 0.f;
+  for (int sp = 0; sp < p.splits; ++sp) {
+    const float4* w = reinterpret_cast<const float4*>(p.ws + ((size_t)sp * p.M + row) * p.N + col);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      if (col + 4 * v < p.N) {
+        const float4 t = __ldcg(w + v);
+        f[4 * v] += t.x;
+        f[4 * v + 1] += t.y;
+        f[4 * v + 2] += t.z;
+        f[4 * v + 3] += t.w;
+      }
+    }
+  }
+  store_chunk16<EPI>(p, row, col, f);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -945,6 +980,34 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Para
                              " smem=" + std::to_string(smem));
   }
   count_launch();
+}
+
+template <int EPI>
+static void launch_splitk_reduce(const Params& p, cudaStream_t stream) {
+  const long threads = (long)p.M * ((p.N + 15) / 16);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200_CUDA_OK(cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<EPI>, p));
+  count_launch();
+}
+
+// Split-K partials reduced by a separate grid for one-CTA tiles too (B200_GEMM_SPLITK_REDUCE=1);
+// CTA-pair tiles always use it.
+static bool splitk_reduce_kernel_on() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("B200_GEMM_SPLITK_REDUCE");
+    v = (e && atoi(e) != 0) ? 1 : 0;
+  }
+  return v == 1;
 }
 
 template <int EPI>
@@ -1121,6 +1184,10 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     p.ws = a.workspace;
     p.counters = a.counters;
   }
+  // deferred split-K reduction (separate grid): the GEMM only writes partials
+  const bool deferred = p.splits > 1 && (pair || (splitk_reduce_kernel_on() && !transposed &&
+                                                   a.mode != kModeScatter));
+  if (deferred) p.counters = nullptr;
   if (pair) {
     if (a.mode == kModeStore)
       launch_pair<kStore>(ta, tb, p, stream);
@@ -1128,9 +1195,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
       launch_pair<kSiluMul>(ta, tb, p, stream);
     else
       launch_pair<kF32>(ta, tb, p, stream);
-    return;
-  }
-  if (a.mode == kModeStore)
+  } else if (a.mode == kModeStore)
     dispatch_mt<kStore>(plan.mt, ta, tb, p, stream);
   else if (a.mode == kModeSiluMul)
     dispatch_mt<kSiluMul>(plan.mt, ta, tb, p, stream);
@@ -1142,6 +1207,14 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     dispatch_mt<kSiluT>(plan.mt, ta, tb, p, stream);
   else
     dispatch_mt<kF32>(plan.mt, ta, tb, p, stream);
+  if (deferred) {
+    if (a.mode == kModeStore)
+      launch_splitk_reduce<kStore>(p, stream);
+    else if (a.mode == kModeSiluMul)
+      launch_splitk_reduce<kSiluMul>(p, stream);
+    else
+      launch_splitk_reduce<kF32>(p, stream);
+  }
 }
 
 }  // namespace gemm
