@@ -290,23 +290,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         m_ref = m_new;
         l *= factor;
       }
-      if (__any_sync(0xffffffffu, resc)) {
-        // O must hold PV_{j-1} before it is rescaled (j >= 1: m_ref was finite)
-        if (!warp_wait(o_done, (j - 1) & 1, p.err)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tc::tmem_ld_32x32b_x32(lane_base + kColO + 32 * c, o);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          tc::tmem_st_32x32b_x32(lane_base + kColO + 32 * c, o);
-        }
-      }
       // p = 2^(s * scale - m): one FMA + one ex2 per score, sums in 8 independent chains
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
       float sum8[8];
@@ -325,6 +308,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int k = 0; k < 4; ++k) sum8[k] += sum8[k + 4];
       l += (sum8[0] + sum8[1]) + (sum8[2] + sum8[3]);
+      // Every iteration confirms PV_{j-1} (one o_done phase per PV, waited in order: a parity
+      // wait is only exact when the barrier is at most one phase ahead of the waiter); O is
+      // then stable and may be rescaled before PV_j accumulates into it.
+      if (j > 0 && !warp_wait(o_done, (j - 1) & 1, p.err)) {
+        ok = false;
+        break;
+      }
+      if (__any_sync(0xffffffffu, resc)) {
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tc::tmem_ld_32x32b_x32(lane_base + kColO + 32 * c, o);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tc::tmem_st_32x32b_x32(lane_base + kColO + 32 * c, o);
+        }
+      }
       tc::tmem_st_32x32b_x32(s_col, pk[0]);
       tc::tmem_st_32x32b_x32(s_col + 32, pk[1]);
       tc::tmem_st_wait();

@@ -8,7 +8,8 @@
 // Cache layout is [num_blocks, Hkv, block_size, D] so that one page of one KV head is a
 // contiguous block_size*D run (a single bulk copy for the attention kernels).  RoPE supports
 // NeoX (rotate halves) and GPT-J (rotate pairs) styles and partial rotary (rot_dim < D); the
-// cos/sin cache is [max_pos, rot_dim] fp32 = [cos(rot_dim/2) | sin(rot_dim/2)].
+// cos/sin cache is [max_pos, rot_dim] fp32 = [cos(rot_dim/2) | sin(rot_dim/2)].  Multimodal
+// RoPE (M-RoPE) takes positions [3, T] and picks each frequency's row by section.
 //
 // Reference counterparts: vllm_musa/jit_kernel/csrc/norm/qk_mrope.mu:168-1311 (Qwen3 fused
 // QK-norm + RoPE + cache), vllm_musa/jit_kernel/csrc/rope/rotary_embedding.mu:124-708 (RoPE),
@@ -22,6 +23,18 @@ namespace rope {
 
 constexpr int kWarps = 4;
 
+// Which position row (0 temporal, 1 height, 2 width) rotary frequency f uses.  Sectioned
+// (Qwen2-VL style): the first s0 frequencies temporal, the next s1 height, the rest width.
+// Interleaved (Qwen3-VL style): f % 3 == 1 height while f < 3 * s1, f % 3 == 2 width while
+// f < 3 * s2, otherwise temporal.
+B200_DEVICE int mrope_component(const MropeSpec& mr, int f) {
+  if (mr.mode == 1) return f < mr.s0 ? 0 : (f < mr.s0 + mr.s1 ? 1 : 2);
+  const int r = f % 3;
+  if (r == 1 && f < 3 * mr.s1) return 1;
+  if (r == 2 && f < 3 * mr.s2) return 2;
+  return 0;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kWarps * 32)
     rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld_qkv,
@@ -30,7 +43,7 @@ __global__ void __launch_bounds__(kWarps * 32)
                    const __nv_bfloat16* __restrict__ k_norm_w, __nv_bfloat16* __restrict__ k_cache,
                    __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ slot_mapping,
                    int T, int Hq, int Hkv, int block_size, int rot_dim, int neox, float eps,
-                   int* err) {
+                   int* err, MropeSpec mr) {
   constexpr int E = D / 32;  // elements per lane
   __shared__ float stage[kWarps][D];
   pdl_launch_dependents();
@@ -63,13 +76,19 @@ __global__ void __launch_bounds__(kWarps * 32)
 #pragma unroll
       for (int j = 0; j < E; ++j) stage[warp][lane * E + j] = v[j];
       __syncwarp();
-      const int64_t pos = positions[t];
-      const float* cs = cos_sin + pos * rot_dim;
       const int half = rot_dim / 2;
+      const float* cs = cos_sin + (int64_t)positions[t] * rot_dim;
 #pragma unroll
       for (int j = 0; j < E; ++j) {
         const int i = lane * E + j;
         if (i < rot_dim) {
+          if (mr.mode != 0) {
+            // multimodal RoPE: frequency f takes its position from the temporal / height /
+            // width row of `positions` ([3, pos_stride])
+            const int f = neox ? (i < half ? i : i - half) : i / 2;
+            const int comp = mrope_component(mr, f);
+            cs = cos_sin + (int64_t)positions[comp * mr.pos_stride + t] * rot_dim;
+          }
           if (neox) {
             const int f = i < half ? i : i - half;
             const float c = cs[f], s = cs[half + f];
@@ -104,6 +123,11 @@ __global__ void __launch_bounds__(kWarps * 32)
 void run_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
   if (a.T == 0) return;
   B200_REQUIRE(a.rot_dim % 2 == 0 && a.rot_dim <= a.D, "rope_kv: rot_dim");
+  B200_REQUIRE(a.mrope.mode == 0 ||
+                   (a.mrope.mode == 1 && a.mrope.s0 + a.mrope.s1 + a.mrope.s2 == a.rot_dim / 2) ||
+                   (a.mrope.mode == 2 && a.mrope.pos_stride >= a.T),
+               "rope_kv: M-RoPE sections must cover rot_dim / 2 frequencies");
+  B200_REQUIRE(a.mrope.mode == 0 || a.mrope.pos_stride >= a.T, "rope_kv: M-RoPE position rows");
   const int64_t warps = (int64_t)a.T * (a.Hq + 2 * a.Hkv);
   const int blocks = (int)((warps + kWarps - 1) / kWarps);
 #define B200_ROPE_LAUNCH(DD)                                                                     \
@@ -112,7 +136,8 @@ void run_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
       reinterpret_cast<const __nv_bfloat16*>(a.q_norm_w),                                        \
       reinterpret_cast<const __nv_bfloat16*>(a.k_norm_w),                                        \
       reinterpret_cast<__nv_bfloat16*>(a.k_cache), reinterpret_cast<__nv_bfloat16*>(a.v_cache), \
-      a.slot_mapping, a.T, a.Hq, a.Hkv, a.block_size, a.rot_dim, a.neox ? 1 : 0, a.eps, a.err)
+      a.slot_mapping, a.T, a.Hq, a.Hkv, a.block_size, a.rot_dim, a.neox ? 1 : 0, a.eps, a.err, \
+      a.mrope)
   switch (a.D) {
     case 64:
       B200_ROPE_LAUNCH(64);

@@ -166,6 +166,12 @@ void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, 
 
 // ------------------------------------------------------------------------------- rope + kv
 namespace rope {
+// Multimodal RoPE: mode 0 off, 1 sectioned (s0 | s1 | s2 frequencies), 2 interleaved;
+// positions are [3, pos_stride] int32 (temporal, height, width rows).
+struct MropeSpec {
+  int mode = 0, s0 = 0, s1 = 0, s2 = 0;
+  int64_t pos_stride = 0;
+};
 struct RopeKvArgs {
   void* qkv;
   int64_t ld_qkv;
@@ -180,6 +186,7 @@ struct RopeKvArgs {
   bool neox;
   float eps;
   int* err;
+  MropeSpec mrope;
 };
 void run_rope_kv(const RopeKvArgs& a, cudaStream_t s);
 }  // namespace rope

@@ -999,13 +999,15 @@ static void launch_splitk_reduce(const Params& p, cudaStream_t stream) {
   count_launch();
 }
 
-// Split-K partials reduced by a separate grid for one-CTA tiles too (B200_GEMM_SPLITK_REDUCE=1);
-// CTA-pair tiles always use it.
+// Split-K partials are reduced by the separate grid (measured 1.2-2.5x faster than the in-kernel
+// last-arriver fixup at decode sizes: e.g. M=128 N=4096 K=14336 32.7 vs 60.4 us);
+// B200_GEMM_SPLITK_REDUCE=0 keeps the in-kernel fixup for one-CTA tiles.  CTA-pair tiles always
+// use the grid; swapped (transposed-store) and reduce-scatter epilogues keep the fixup.
 static bool splitk_reduce_kernel_on() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("B200_GEMM_SPLITK_REDUCE");
-    v = (e && atoi(e) != 0) ? 1 : 0;
+    v = (e == nullptr || atoi(e) != 0) ? 1 : 0;
   }
   return v == 1;
 }

@@ -328,7 +328,8 @@ void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
              const c10::optional<Tensor>& q_norm_w, const c10::optional<Tensor>& k_norm_w,
              const c10::optional<Tensor>& k_cache_opt, const c10::optional<Tensor>& v_cache_opt,
              const Tensor& slot_mapping, int64_t Hq, int64_t Hkv, int64_t rot_dim, bool neox,
-             double eps, int64_t head_dim) {
+             double eps, int64_t head_dim, c10::optional<at::IntArrayRef> mrope_section,
+             bool mrope_interleaved) {
   CHECK_CUDA(qkv);
   CHECK_BF16(qkv);
   CHECK_ROWMAJOR(qkv);
@@ -373,6 +374,17 @@ void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
   a.neox = neox;
   a.eps = eps;
   a.err = err_ptr(qkv);
+  if (mrope_section.has_value()) {
+    const auto sec = *mrope_section;
+    TORCH_CHECK(sec.size() == 3, "rope_kv: mrope_section needs 3 entries");
+    TORCH_CHECK(positions.dim() == 2 && positions.size(0) == 3 && positions.size(1) >= T,
+                "rope_kv: M-RoPE positions must be [3, >= T]");
+    a.mrope.mode = mrope_interleaved ? 2 : 1;
+    a.mrope.s0 = sec[0];
+    a.mrope.s1 = sec[1];
+    a.mrope.s2 = sec[2];
+    a.mrope.pos_stride = positions.size(1);
+  }
   guarded([&] { b200::rope::run_rope_kv(a, stream_of(qkv)); });
 }
 
@@ -1036,7 +1048,8 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "rope_kv(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor? q_norm_w, Tensor? "
       "k_norm_w, Tensor(b!)? k_cache, Tensor(c!)? v_cache, Tensor slot_mapping, int num_q_heads, "
-      "int num_kv_heads, int rot_dim, bool neox=True, float eps=1e-6, int head_dim=0) -> ()");
+      "int num_kv_heads, int rot_dim, bool neox=True, float eps=1e-6, int head_dim=0, "
+      "int[]? mrope_section=None, bool mrope_interleaved=False) -> ()");
   m.def(
       "paged_decode(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor "
       "block_tables, Tensor seq_lens, int num_q_heads, int num_kv_heads, int max_seq_len, float "

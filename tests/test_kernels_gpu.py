@@ -356,3 +356,31 @@ def test_rms_norm_quant_fp8(rows, H, add, want):
     torch.testing.assert_close(deq.view(rows, H), ry.float(), rtol=0.07, atol=0.02)
     if want:
         torch.testing.assert_close(y.cpu().float(), ry.float(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("section,interleaved,neox", [([16, 24, 24], False, True),
+                                                      ([24, 20, 20], True, True),
+                                                      ([8, 12, 12], False, False)])
+def test_rope_kv_mrope(section, interleaved, neox):
+    """Multimodal RoPE in the fused rope/KV-insert kernel against the PyTorch reference."""
+    T, Hq, Hkv, D, bs = 37, 8, 2, 128, 16
+    rot = 2 * sum(section) if not interleaved else 128
+    cs = ops.build_cos_sin_cache(rot, 4096, 1e6)
+    g = torch.Generator().manual_seed(7)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
+    pos3 = torch.randint(0, 4096, (3, T + 5), generator=g, dtype=torch.int32)
+    nb = (T + bs - 1) // bs + 2
+    kc = torch.zeros(nb, Hkv, bs, D, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(nb * bs, generator=g)[:T].to(torch.int32)
+    ref_qkv, rk, rv = qkv.clone(), kc.clone(), vc.clone()
+    ops.rope_kv(ref_qkv, pos3, cs, rk, rv, slots, Hq, Hkv, rot, neox=neox,
+                mrope_section=section, mrope_interleaved=interleaved)
+    gq, gk, gv = qkv.to(DEV), kc.to(DEV), vc.to(DEV)
+    ops.rope_kv(gq, pos3.to(DEV), cs.to(DEV), gk, gv, slots.to(DEV), Hq, Hkv, rot, neox=neox,
+                mrope_section=section, mrope_interleaved=interleaved)
+    torch.cuda.synchronize()
+    _ext.check_device_errors()
+    torch.testing.assert_close(gq.cpu().float(), ref_qkv.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(gk.cpu().float(), rk.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(gv.cpu().float(), rv.float())

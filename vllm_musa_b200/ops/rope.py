@@ -39,6 +39,24 @@ def build_cos_sin_cache(rot_dim: int, max_pos: int, theta: float, device=None,
     return cs.to(device) if device is not None else cs
 
 
+def _mrope_cos_sin(cos_sin: torch.Tensor, positions: torch.Tensor, rot_dim: int,
+                   section: list, interleaved: bool) -> torch.Tensor:
+    """[T, rot_dim] cos | sin where frequency f uses position row comp(f) of [3, T]."""
+    half = rot_dim // 2
+    f = torch.arange(half)
+    if interleaved:
+        comp = torch.zeros(half, dtype=torch.long)
+        comp[(f % 3 == 1) & (f < 3 * section[1])] = 1
+        comp[(f % 3 == 2) & (f < 3 * section[2])] = 2
+    else:
+        assert sum(section) == half, "M-RoPE sections must cover rot_dim / 2 frequencies"
+        comp = torch.repeat_interleave(torch.arange(3), torch.tensor(section))
+    cs = cos_sin[positions.long()]                       # [3, T, rot_dim]
+    idx = torch.cat([comp, comp])                         # cos half then sin half
+    cols = torch.arange(rot_dim)
+    return cs[idx.to(cs.device), :, cols.to(cs.device)].transpose(0, 1).contiguous()
+
+
 def _rotate_ref(x: torch.Tensor, cs: torch.Tensor, rot_dim: int, neox: bool) -> torch.Tensor:
     # x [T, H, D] fp32; cs [T, rot_dim]
     half = rot_dim // 2
@@ -58,11 +76,16 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
             slot_mapping: torch.Tensor, num_q_heads: int, num_kv_heads: int, rot_dim: int,
             neox: bool = True, q_norm_w: torch.Tensor | None = None,
             k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
-            write_k: bool = False, head_dim: int | None = None) -> None:
+            write_k: bool = False, head_dim: int | None = None,
+            mrope_section: list | None = None, mrope_interleaved: bool = False) -> None:
     """In place on ``qkv`` [T, (Hq+2Hkv)*D]: q <- rope(norm(q)); cache[slot] <- rope(norm(k)), v.
 
     Caches are [num_blocks, Hkv, block_size, D]; slot = block * block_size + offset; slot < 0
     skips the write.  Without caches (``write_k``) q and k are only rotated in place.
+    M-RoPE (``mrope_section`` = [temporal, height, width] frequency counts): positions are
+    [3, >= T] and each rotary frequency takes its position from the row its section names
+    (``mrope_interleaved``: frequencies assigned round-robin, Qwen3-VL layout).
+    Reference: vllm_musa/jit_kernel/csrc/norm/qk_mrope.mu:168-1311.
     """
     T = qkv.shape[0]
     if T == 0:
@@ -72,7 +95,9 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
             num_q_heads + 2 * num_kv_heads)
     if qkv.is_cuda:
         _ext.ops().rope_kv(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache,
-                           slot_mapping, num_q_heads, num_kv_heads, rot_dim, neox, eps, head_dim)
+                           slot_mapping, num_q_heads, num_kv_heads, rot_dim, neox, eps, head_dim,
+                           list(mrope_section) if mrope_section is not None else None,
+                           mrope_interleaved)
         return
     D = head_dim
     Hq, Hkv = num_q_heads, num_kv_heads
@@ -84,7 +109,11 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
     if k_norm_w is not None:
         k = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + eps) * k_norm_w.float()
     if rot_dim > 0:
-        cs = cos_sin[positions.long()]
+        if mrope_section is not None:
+            cs = _mrope_cos_sin(cos_sin, positions[:, :T], rot_dim, mrope_section,
+                                mrope_interleaved)
+        else:
+            cs = cos_sin[positions.long()]
         q = _rotate_ref(q, cs, rot_dim, neox)
         k = _rotate_ref(k, cs, rot_dim, neox)
     qkv[:, :Hq * D] = q.reshape(T, Hq * D).to(qkv.dtype)
