@@ -1,26 +1,25 @@
 // Causal (chunked) prefill attention on the 5th-generation tensor cores, head_dim 128.
 //
 // CTA = (128-query tile of one request, one query head); query row i lives in TMEM lane i.
-// Two CTAs per SM (256 TMEM columns and ~99 KB of shared memory each), so the tensor core and
-// the SFU exponentials of one CTA overlap the other CTA's softmax / MMAs, and each SM
-// scheduler runs two softmax warps.  Warp roles (192 threads):
+// Warp roles (192 threads, one CTA per SM: 512 TMEM columns, ~162 KB shared memory):
 //   warp 0    TMA producer: the Q tile once (two 64-column halves, 128-byte swizzle), then the
-//             K and V blocks of 128 keys from the paged cache (one stage each: K_{j+1} streams
-//             in while the softmax of block j and PV_j run).
+//             K and V blocks of 128 keys from the paged cache into two 2-stage rings.
 //   warp 1    TMEM owner and single-thread MMA issuer:
 //               S_j  = Q K_j^T   M 128, N 128 keys, K 128 dims; Q and K K-major in smem
 //               O   += P_j V_j   M 128, N 128 dims, K 128 keys; P from TMEM, V MN-major in smem
+//             in the order S_0, S_1, PV_0, S_2, PV_1, ... so the tensor core computes S_{j+1}
+//             while the softmax warps work on S_j.
 //   warps 2-5 softmax and epilogue, one query row per thread (the TMEM lane quarter its warp
-//             may access).  Pass 1 reads the S row from TMEM in 32-column chunks for the row
-//             max (8 independent chains); pass 2 re-reads each chunk, applies the causal /
-//             sliding-window mask (diagonal blocks only), p = 2^(s*scale - m) with one FMA and
-//             one ex2, and writes P (bf16) back over the consumed S columns with tcgen05.st.
-//             O is rescaled in TMEM only when a row max grows by more than 2^8 (until then
-//             P <= 256).  At the end O / l is read out of TMEM and stored.
-// TMEM columns: O [0,128) | S / P [128,256).  Every mbarrier is waited phase by phase (a
-// parity wait is exact only while the barrier is at most one phase ahead of the waiter);
-// every wait is bounded (error word + early exit); the producer waits for its own copies in
-// flight before the CTA exits, the MMA thread for its MMAs before TMEM is freed.
+//             may access): tcgen05.ld of the S row, scale + causal / sliding-window mask, online
+//             max with lazy rescaling (O is rescaled in TMEM only when a row's running max grows
+//             by more than 2^8; until then P = 2^(s - stale max) <= 256), exp2, row sums in
+//             registers, P packed to bf16 and written back over the S columns (tcgen05.st).  At
+//             the end O / l is read out of TMEM and stored.
+// TMEM columns: O [0,128) | S/P buffer 0 [128,256) | 1 [256,384) | 2 [384,512).  With three S
+// buffers, S_{j+2} goes to the buffer of P_{j-1}, whose PV has completed by then, so the MMA
+// issuer never waits on the MMA it has just issued.
+// Every mbarrier wait is bounded (error word + early exit); the producer waits for its own
+// copies in flight before the CTA exits, the MMA thread for its MMAs before TMEM is freed.
 //
 // Reference counterpart: the MATE FA3 varlen prefill the reference calls through
 // vllm_musa/v1/attention/backends/flash_attn.py:1186-1537 (no kernel source in the reference).
@@ -38,9 +37,9 @@ namespace {
 constexpr int kBQ = 128, kBK = 128, kDim = 128;
 constexpr int kHalfBytes = 128 * 128;        // 128 rows x 64 bf16 columns (one swizzle span)
 constexpr int kTileBytes = 2 * kHalfBytes;   // 128 rows x 128 columns
+constexpr int kRing = 2;                     // K stages, V stages
 constexpr int kTcThreads = 192;
-constexpr int kTcSmem = kTileBytes * 3 + 1024 + 256;  // Q | K | V: two CTAs per SM
-constexpr uint32_t kTmemCols = 256;
+constexpr int kTcSmem = kTileBytes * (1 + 2 * kRing) + 1024 + 256;
 constexpr uint32_t kColO = 0, kColS = 128;
 constexpr float kRescaleLog2 = 8.f;
 
@@ -91,7 +90,7 @@ B200_DEVICE bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
   return __all_sync(0xffffffffu, ok);
 }
 
-__global__ void __launch_bounds__(kTcThreads, 2)
+__global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, TcParams p) {
@@ -100,18 +99,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                                              ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = smem + kTileBytes;
-  uint8_t* sV = sK + kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTileBytes);
+  uint8_t* sV = sK + kRing * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kRing * kTileBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;
-  uint64_t* v_empty = bars + 4;
-  uint64_t* s_full = bars + 5;   // S_j computed
-  uint64_t* p_full = bars + 6;   // P_j written (4 softmax warps)
-  uint64_t* o_done = bars + 7;   // PV_j completed (one phase per block)
-  uint64_t* fin = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;    // [3] S_j computed
+  uint64_t* p_full = bars + 12;   // [3] P_j written (4 softmax warps)
+  uint64_t* p_free = bars + 15;   // [3] PV_j completed: buffer reusable
+  uint64_t* o_done = bars + 18;   // one phase per PV
+  uint64_t* fin = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int tile = p.max_tiles - 1 - blockIdx.x;  // longest-context tiles first
   const int head = blockIdx.y;
@@ -136,18 +136,23 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(k_full, 1);
-    mbar_init(k_empty, 1);
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 3; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&p_free[b], 1);
+    }
     mbar_init(o_done, 1);
     mbar_init(fin, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -165,53 +170,69 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       tma_load_2d(sQ + kHalfBytes, &tmQ, q_full, head * kDim + 64, q0);
       int nk = 0, nv = 0;  // blocks whose loads were issued
       for (int j = 0; j < nblk; ++j) {
-        const uint32_t ph = (j & 1) ^ 1;  // the previous block's stage release
-        if (!mbar_wait(k_empty, ph, p.err)) break;
-        load_kv_block(&tmK, sK, k_full, bt, first_blk + j, seq_len, h, p.Hkv, p.block_size);
+        const int st = j & 1;
+        const uint32_t ph = ((j >> 1) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[st], ph, p.err)) break;
+        load_kv_block(&tmK, sK + st * kTileBytes, &k_full[st], bt, first_blk + j, seq_len, h,
+                      p.Hkv, p.block_size);
         ++nk;
-        if (!mbar_wait(v_empty, ph, p.err)) break;
-        load_kv_block(&tmV, sV, v_full, bt, first_blk + j, seq_len, h, p.Hkv, p.block_size);
+        if (!mbar_wait(&v_empty[st], ph, p.err)) break;
+        load_kv_block(&tmV, sV + st * kTileBytes, &v_full[st], bt, first_blk + j, seq_len, h,
+                      p.Hkv, p.block_size);
         ++nv;
       }
       // no copy may still be writing shared memory when the CTA exits
       mbar_wait(q_full, 0, p.err);
-      if (nk > 0) mbar_wait(k_full, (nk - 1) & 1, p.err);
-      if (nv > 0) mbar_wait(v_full, (nv - 1) & 1, p.err);
+      for (int j = nk > kRing ? nk - kRing : 0; j < nk; ++j)
+        mbar_wait(&k_full[j & 1], (j >> 1) & 1, p.err);
+      for (int j = nv > kRing ? nv - kRing : 0; j < nv; ++j)
+        mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_f16<true>(kBQ, kBK);
       const uint32_t id_o = tc::idesc_f16<true>(kBQ, kDim) | (1u << 16);  // V is MN-major
-      const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK), va = smem_u32(sV);
+      const uint32_t qa = smem_u32(sQ);
       auto issue_s = [&](int j) -> bool {
-        if (!mbar_wait(k_full, j & 1, p.err)) return false;
+        const int st = j & 1, b = j % 3;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, p.err)) return false;
+        if (j >= 3 && !mbar_wait(&p_free[b], ((j - 3) / 3) & 1, p.err)) return false;
         tc::fence_after_sync();
+        const uint32_t ka = smem_u32(sK + st * kTileBytes);
+        const uint32_t d = tmem + kColS + b * 128;
 #pragma unroll
         for (int k = 0; k < kDim / 16; ++k) {
           const uint32_t off = (k >> 2) * kHalfBytes;
-          tc::mma_f16_ss(tmem + kColS, tc::smem_desc_kmajor_sw128(qa + off) + 2 * (k & 3),
+          tc::mma_f16_ss(d, tc::smem_desc_kmajor_sw128(qa + off) + 2 * (k & 3),
                          tc::smem_desc_kmajor_sw128(ka + off) + 2 * (k & 3), id_s, k > 0);
         }
-        tc::mma_commit(k_empty);
-        tc::mma_commit(s_full);
+        tc::mma_commit(&k_empty[st]);
+        tc::mma_commit(&s_full[b]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j & 1, b = j % 3;
+        if (!mbar_wait(&p_full[b], (j / 3) & 1, p.err)) return false;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1, p.err)) return false;
+        tc::fence_after_sync();
+        const uint32_t va = smem_u32(sV + st * kTileBytes);
+        const uint32_t pa = tmem + kColS + b * 128;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)  // 16 keys: 8 packed P columns, 16 V rows
+          tc::mma_f16_ts(tmem + kColO, pa + 8 * k,
+                         tc::smem_desc_mnmajor_sw128(va + k * 16 * 128, kHalfBytes, 1024), id_o,
+                         (j > 0 || k > 0) ? 1u : 0u);
+        tc::mma_commit(&v_empty[st]);
+        tc::mma_commit(&p_free[b]);
+        tc::mma_commit(o_done);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, p.err);
       if (ok) ok = issue_s(0);
+      if (ok && nblk > 1) ok = issue_s(1);
       for (int j = 0; j < nblk && ok; ++j) {
-        if (!mbar_wait(p_full, j & 1, p.err) || !mbar_wait(v_full, j & 1, p.err)) break;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)  // 16 keys: 8 packed P columns, 16 V rows
-          tc::mma_f16_ts(tmem + kColO, tmem + kColS + 8 * k,
-                         tc::smem_desc_mnmajor_sw128(va + k * 16 * 128, kHalfBytes, 1024), id_o,
-                         (j > 0 || k > 0) ? 1u : 0u);
-        tc::mma_commit(v_empty);
-        tc::mma_commit(o_done);
-        if (j + 1 < nblk) {
-          // S_{j+1} overwrites the P_j columns: PV_j must have completed
-          ok = mbar_wait(o_done, j & 1, p.err) && issue_s(j + 1);
-        }
+        ok = issue_pv(j);
+        if (ok && j + 2 < nblk) ok = issue_s(j + 2);
       }
       tc::mma_commit(fin);  // every MMA issued above has completed
       mbar_wait(fin, 0, p.err);
@@ -220,37 +241,41 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    const uint32_t s_col = lane_base + kColS;
     const int my_pos = pos0 + row;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
-      if (!warp_wait(s_full, j & 1, p.err)) {
+      const int b = j % 3;
+      if (!warp_wait(&s_full[b], (j / 3) & 1, p.err)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
+      const uint32_t s_col = lane_base + kColS + b * 128;
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(s_col + 32 * c, s[c]);
+      tc::tmem_ld_wait();
       const int kv0 = (first_blk + j) * kBK;
-      const bool masked = kv0 + kBK - 1 > my_pos || p.window > 0;  // diagonal / window blocks
-      // pass 1: row max of the raw scores (8 independent chains)
+      if (kv0 + kBK - 1 > my_pos || p.window > 0) {  // diagonal / window blocks only
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int kv = kv0 + 32 * c + i;
+            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window))
+              s[c][i] = __float_as_uint(-INFINITY);
+          }
+      }
+      // row max of the raw scores with 8 independent chains (one warp per scheduler: a
+      // single dependent chain of 128 max operations would dominate the block)
       float mx8[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(s_col + 32 * c, sv);
-        tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(sv[i]);
-          if (masked) {
-            const int kv = kv0 + 32 * c + i;
-            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window)) v = -INFINITY;
-          }
-          mx8[i & 7] = fmaxf(mx8[i & 7], v);
-        }
-      }
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(s[c][i]));
 #pragma unroll
       for (int k = 0; k < 4; ++k) mx8[k] = fmaxf(mx8[k], mx8[k + 4]);
       const float mx = fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])) * p.scale_log2;
@@ -265,37 +290,27 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         m_ref = m_new;
         l *= factor;
       }
-      // pass 2: p = 2^(s * scale - m) (one FMA + one ex2 per score), P chunk c (16 packed
-      // columns) written over S columns that pass 2 has already read
+      // p = 2^(s * scale - m): one FMA + one ex2 per score, sums in 8 independent chains
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
       float sum8[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(s_col + 32 * c, sv);
-        tc::tmem_ld_wait();
-        uint32_t pk[16];
+      uint32_t pk[2][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          float s0 = __uint_as_float(sv[i]), s1 = __uint_as_float(sv[i + 1]);
-          if (masked) {
-            const int kv = kv0 + 32 * c + i;
-            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window)) s0 = -INFINITY;
-            if (kv + 1 > my_pos || (p.window > 0 && kv + 1 <= my_pos - p.window)) s1 = -INFINITY;
-          }
-          const float a = ex2_approx(fmaf(s0, p.scale_log2, neg_m));
-          const float e = ex2_approx(fmaf(s1, p.scale_log2, neg_m));
+          const float a = ex2_approx(fmaf(__uint_as_float(s[c][i]), p.scale_log2, neg_m));
+          const float e = ex2_approx(fmaf(__uint_as_float(s[c][i + 1]), p.scale_log2, neg_m));
           sum8[(i >> 1) & 7] += a + e;
-          pk[i / 2] = pack_bf16x2(a, e);  // low half = even key
+          pk[c >> 1][(c & 1) * 16 + i / 2] = pack_bf16x2(a, e);  // low half = even key
         }
-        tc::tmem_st_32x32b_x16(s_col + 16 * c, pk);
-      }
 #pragma unroll
       for (int k = 0; k < 4; ++k) sum8[k] += sum8[k + 4];
       l += (sum8[0] + sum8[1]) + (sum8[2] + sum8[3]);
-      // PV_{j-1} has completed (phase by phase); O is stable and may be rescaled before PV_j
+      // Every iteration confirms PV_{j-1} (one o_done phase per PV, waited in order: a parity
+      // wait is only exact when the barrier is at most one phase ahead of the waiter); O is
+      // then stable and may be rescaled before PV_j accumulates into it.
       if (j > 0 && !warp_wait(o_done, (j - 1) & 1, p.err)) {
         ok = false;
         break;
@@ -312,12 +327,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           tc::tmem_st_32x32b_x32(lane_base + kColO + 32 * c, o);
         }
       }
+      tc::tmem_st_32x32b_x32(s_col, pk[0]);
+      tc::tmem_st_32x32b_x32(s_col + 32, pk[1]);
       tc::tmem_st_wait();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[b]);
     }
-    if (ok && warp_wait(o_done, (nblk - 1) & 1, p.err)) {
+    if (ok && nblk > 0 && warp_wait(o_done, (nblk - 1) & 1, p.err)) {
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool valid = row < rows;
@@ -342,7 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
 }
 
 }  // namespace
