@@ -1,0 +1,147 @@
+"""Fused compute + collective paths over NVLink, timed on the device (CUDA events, max over
+ranks), against their NVLink roofline and against the NCCL path they replace.
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/collectives_bench.py
+
+Cases (hidden 4096, bf16, every rank holds its partial sums):
+  ar_norm    fused all-reduce + residual + RMSNorm (one-shot / two-shot by size) vs
+             NCCL all_reduce followed by the fused add + RMSNorm kernel
+  gemm_rs    row-parallel GEMM [T, K/N] x [H, K/N]^T whose epilogue stores into the owners'
+             staging slots + the local-source reduce (+ residual + RMSNorm + all-gather) vs
+             GEMM + fused all-reduce kernel
+  cand       vocab-parallel sampling candidate exchange (one kernel) vs two NCCL all_gathers
+
+Roofline: the bytes a rank must move over NVLink (one direction, the larger of send / receive)
+divided by the measured peer-copy bandwidth (770 GB/s per direction); for gemm_rs the slower of
+that and the GEMM's FLOPs at the measured bf16 peak.  Prints one JSON line per case and size on
+rank 0.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+LINK_BPS = 770e9     # measured peer copy, per direction per GPU
+BF16_FLOPS = 1.639e15  # measured cuBLAS bf16 burst
+
+
+def _time(fn, iters, group):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) * 1e3 / iters], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return float(t)
+
+
+def main():
+    from vllm_musa_b200 import ops
+    from vllm_musa_b200.parallel.custom_ar import maybe_create_custom_allreduce
+    from vllm_musa_b200.parallel.state import init_distributed
+    world = int(os.environ["WORLD_SIZE"])
+    st = init_distributed(tp_size=world)
+    dev = torch.device("cuda", st.local_rank)
+    H, eps = 4096, 1e-6
+    ar = maybe_create_custom_allreduce(st, dev, max_tokens=8192, hidden=H)
+    assert ar is not None, "P2P communicator did not initialise"
+    ops.gemm.reserve_workspace(dev, 64 << 20)
+    w = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    out = []
+
+    def emit(d):
+        if st.rank == 0:
+            d.update(world=world)
+            print(json.dumps(d), flush=True)
+            out.append(d)
+
+    for T in (1, 8, 64, 256, 1024, 4096):
+        x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+        res = torch.randn(T, H, device=dev).to(torch.bfloat16)
+        two_shot, _ = ar._plan(T)
+
+        def fused():
+            stg = ar.staging_view(T)
+            ar.allreduce_add_rmsnorm(stg, res, w, eps)
+
+        def nccl():
+            y = x.clone()
+            dist.all_reduce(y, group=st.tp_group)
+            ops.fused_add_rms_norm(y, res, w, eps)
+
+        it = 200 if T <= 256 else 50
+        tf, tn = _time(fused, it, st.tp_group), _time(nccl, it, st.tp_group)
+        nbytes = T * H * 2
+        # one-shot: read the other ranks' full slots; two-shot: read (N-1)/N of each peer's
+        # slot for the owned chunk, then write the owned normalised chunk to N-1 peers
+        link = (world - 1) * nbytes if not two_shot else (world - 1) * nbytes / world
+        roof = link / LINK_BPS * 1e6
+        emit(dict(case="ar_norm", T=T, H=H, two_shot=two_shot, us=round(tf, 2),
+                  nccl_us=round(tn, 2), speedup_vs_nccl=round(tn / tf, 2),
+                  roofline_us=round(roof, 2), frac_of_roofline=round(roof / tf, 3)))
+
+    K = 14336
+    for T in (256, 1024, 4096):
+        if not ar._plan(T)[0]:  # the epilogue reduce-scatter pairs with the two-shot kernel
+            continue
+        Kr = K // world
+        x = (torch.randn(T, Kr, device=dev) * 0.1).to(torch.bfloat16)
+        wt = (torch.randn(H, Kr, device=dev) * 0.02).to(torch.bfloat16)
+        res = torch.randn(T, H, device=dev).to(torch.bfloat16)
+
+        def fused_rs():
+            ar.begin_forward()
+            ar.linear_allreduce_add_rmsnorm(x, wt, res, w, eps)
+
+        def unfused():
+            ar.begin_forward()
+            stg = ar.staging_view(T)
+            ops.linear(x, wt, out=stg)
+            ar.allreduce_add_rmsnorm(stg, res, w, eps)
+
+        it = 50
+        tf, tu = _time(fused_rs, it, st.tp_group), _time(unfused, it, st.tp_group)
+        flops = 2 * T * H * Kr
+        link = 2 * (world - 1) * T * H * 2 / world  # reduce-scatter out + all-gather out
+        roof = max(flops / BF16_FLOPS, link / LINK_BPS) * 1e6
+        emit(dict(case="gemm_rs", T=T, H=H, K_per_rank=Kr, us=round(tf, 2),
+                  unfused_us=round(tu, 2), speedup_vs_unfused=round(tu / tf, 2),
+                  roofline_us=round(roof, 2), frac_of_roofline=round(roof / tf, 3)))
+
+    for R in (8, 64, 256):
+        vals = torch.randn(R, device=dev)
+        ids = torch.randint(0, 1 << 20, (R,), device=dev)
+
+        def p2p():
+            ar.merge_candidates(vals, ids)
+
+        def nccl_gather():
+            av = [torch.empty_like(vals) for _ in range(world)]
+            ai = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(av, vals, group=st.tp_group)
+            dist.all_gather(ai, ids, group=st.tp_group)
+            torch.stack(av).argmax(0)
+
+        tp, tn = _time(p2p, 200, st.tp_group), _time(nccl_gather, 200, st.tp_group)
+        emit(dict(case="cand", rows=R, us=round(tp, 2), nccl_us=round(tn, 2),
+                  speedup_vs_nccl=round(tn / tp, 2)))
+    ops._ext.check_device_errors()
+    ar.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -79,6 +79,73 @@ def gdn_recurrent(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor, dt_b
     return out
 
 
+def _gdn_inputs(qkv, ba, A_log, dt_bias, a, b, Hk, Hv):
+    """Normalised q (scaled by 1/sqrt(dk)), k, v, beta, log-decay g for tokens [a, b)."""
+    D = 128
+    L = b - a
+    rep = Hv // Hk
+    q = qkv[a:b, :Hk * D].float().view(L, Hk, D).repeat_interleave(rep, 1)
+    k = qkv[a:b, Hk * D:2 * Hk * D].float().view(L, Hk, D).repeat_interleave(rep, 1)
+    v = qkv[a:b, 2 * Hk * D:2 * Hk * D + Hv * D].float().view(L, Hv, D)
+    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) / D ** 0.5
+    k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    beta = torch.sigmoid(ba[a:b, :Hv].float())
+    g = -torch.exp(A_log.float()) * F.softplus(ba[a:b, Hv:2 * Hv].float() + dt_bias.float())
+    return q, k, v, beta, g
+
+
+def gdn_chunk_step(S: torch.Tensor, q, k, v, beta, g):
+    """One chunk of the gated delta rule in matrix form (the algorithm of the chunked CUDA
+    kernels), for all heads: S [H, dv, dk] fp32 at the chunk start; q, k [C, H, dk], v [C, H,
+    dv], beta, g [C, H].  With G = cumsum(g), Gam = exp(G), u_t the delta-rule updates:
+        (I + diag(beta) L) U = diag(beta) (V - diag(Gam) K S^T),  L[t,i] = e^{G_t-G_i} k_t.k_i (i<t)
+        O = diag(Gam) Q S^T + tril(e^{G_t-G_i} q_t.k_i) U
+        S' = e^{G_C} S + U^T diag(e^{G_C - G}) K
+    Returns (O [C, H, dv], S')."""
+    C = q.shape[0]
+    G = torch.cumsum(g, 0)                                    # [C, H]
+    qh, kh, vh = q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1)   # [H, C, d]
+    Gh = G.t()                                                # [H, C]
+    causal = torch.tril(torch.ones(C, C))
+    strict = torch.tril(torch.ones(C, C), -1)
+    diff = (Gh.unsqueeze(2) - Gh.unsqueeze(1)).masked_fill(causal == 0, float("-inf"))
+    decay = torch.exp(diff)                                   # [H, t, i] = e^{G_t - G_i}, i <= t
+    Lm = (kh @ kh.transpose(1, 2)) * decay * strict           # [H, C, C]
+    bh = beta.t().unsqueeze(2)                                # [H, C, 1]
+    T = torch.eye(C).expand_as(Lm) + bh * Lm
+    gam = torch.exp(Gh).unsqueeze(2)                          # [H, C, 1]
+    rhs = bh * (vh - gam * (kh @ S.transpose(1, 2)))          # [H, C, dv]
+    U = torch.linalg.solve_triangular(T, rhs, upper=False, unitriangular=True)
+    Mq = (qh @ kh.transpose(1, 2)) * decay * causal
+    O = gam * (qh @ S.transpose(1, 2)) + Mq @ U               # [H, C, dv]
+    tail = torch.exp(Gh[:, -1:] - Gh).unsqueeze(2)            # [H, C, 1]
+    S2 = torch.exp(Gh[:, -1]).view(-1, 1, 1) * S + U.transpose(1, 2) @ (tail * kh)
+    return O.transpose(0, 1), S2
+
+
+def gdn_chunked_ref(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor,
+                    dt_bias: torch.Tensor, state: torch.Tensor, cu_q: torch.Tensor,
+                    seq_lens: torch.Tensor, slots: torch.Tensor, Hk: int, Hv: int,
+                    chunk: int = 64) -> torch.Tensor:
+    """The gated delta rule evaluated chunk by chunk (same results as ``gdn_recurrent``)."""
+    T = qkv.shape[0]
+    D = 128
+    out = torch.empty(T, Hv * D, dtype=qkv.dtype)
+    cu = cu_q.tolist()
+    for r in range(len(cu) - 1):
+        a, b = cu[r], cu[r + 1]
+        slot = int(slots[r])
+        S = state[slot].float().clone() if int(seq_lens[r]) - (b - a) > 0 else \
+            torch.zeros(Hv, D, D)
+        q, k, v, beta, g = _gdn_inputs(qkv, ba, A_log, dt_bias, a, b, Hk, Hv)
+        for c0 in range(0, b - a, chunk):
+            c1 = min(b - a, c0 + chunk)
+            O, S = gdn_chunk_step(S, q[c0:c1], k[c0:c1], v[c0:c1], beta[c0:c1], g[c0:c1])
+            out[a + c0:a + c1] = O.reshape(c1 - c0, Hv * D).to(out.dtype)
+        state[slot] = S.to(state.dtype)
+    return out
+
+
 def sigmoid_gate(out: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
     """out *= sigmoid(gate) in place (both [T, W], rows may be strided)."""
     if out.is_cuda:
