@@ -109,6 +109,14 @@ void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t 
                        int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s);
 void run_sigmoid_gate(void* out, int64_t ldo, const void* gate, int64_t ldg, int T, int W,
                       cudaStream_t s);
+// chunked prefill (gdn_chunked.cu): workspace of chunked_workspace_bytes(max_chunks, Hv) with
+// max_chunks = ceil(T / 64) + R, chunk_offsets [R + 1] int32, gam_c [max_chunks * Hv] fp32
+size_t chunked_workspace_bytes(int max_chunks, int Hv);
+void run_gdn_chunked(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld_ba,
+                     const float* A_log, const float* dt_bias, float* state, const int32_t* cu_q,
+                     const int32_t* seq_lens, const int32_t* slots, int32_t* chunk_offsets,
+                     void* ws, float* gam_c, int R, int T, int Hk, int Hv, void* out,
+                     int64_t ld_out, cudaStream_t s);
 }  // namespace gdn
 
 // ------------------------------------------------------------------------------- MoE

@@ -709,6 +709,43 @@ void causal_conv1d(const Tensor& x, const Tensor& w, Tensor& state, const Tensor
   });
 }
 
+void gdn_chunked(const Tensor& qkv, const Tensor& ba, const Tensor& A_log, const Tensor& dt_bias,
+                 Tensor& state, const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots,
+                 int64_t Hk, int64_t Hv, Tensor& out, Tensor& ws, Tensor& chunk_offsets,
+                 Tensor& gam_c) {
+  CHECK_CUDA(qkv);
+  CHECK_BF16(qkv);
+  CHECK_ROWMAJOR(qkv);
+  CHECK_ROWMAJOR(ba);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4 &&
+                  state.size(1) == Hv && state.size(2) == 128 && state.size(3) == 128,
+              "gdn state [slots, Hv, 128, 128] fp32");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
+              "A_log / dt_bias fp32");
+  const int R = seq_lens.numel(), T = qkv.size(0);
+  const int max_chunks = (T + 63) / 64 + R;
+  TORCH_CHECK(ws.is_contiguous() &&
+                  (size_t)ws.numel() * ws.element_size() >=
+                      b200::gdn::chunked_workspace_bytes(max_chunks, Hv),
+              "gdn_chunked: workspace too small");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ws.data_ptr()) % 16 == 0, "gdn_chunked: workspace alignment");
+  TORCH_CHECK(chunk_offsets.scalar_type() == at::kInt && chunk_offsets.numel() >= R + 1,
+              "gdn_chunked: chunk_offsets [R+1] int32");
+  TORCH_CHECK(gam_c.scalar_type() == at::kFloat && gam_c.numel() >= (int64_t)max_chunks * Hv,
+              "gdn_chunked: gam_c too small");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  guarded([&] {
+    b200::gdn::run_gdn_chunked(qkv.data_ptr(), qkv.stride(0), ba.data_ptr(), ba.stride(0),
+                               A_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                               state.data_ptr<float>(), cu_q.data_ptr<int32_t>(),
+                               seq_lens.data_ptr<int32_t>(), slots.data_ptr<int32_t>(),
+                               chunk_offsets.data_ptr<int32_t>(), ws.data_ptr(),
+                               gam_c.data_ptr<float>(), R, T, Hk, Hv, out.data_ptr(),
+                               out.stride(0), stream_of(qkv));
+  });
+}
+
 void gdn_recurrent(const Tensor& qkv, const Tensor& ba, const Tensor& A_log, const Tensor& dt_bias,
                    Tensor& state, const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots,
                    int64_t Hk, int64_t Hv, Tensor& out) {
@@ -1102,6 +1139,10 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "gdn_recurrent(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
       "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out) -> ()");
+  m.def(
+      "gdn_chunked(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
+      "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out, "
+      "Tensor(c!) ws, Tensor(d!) chunk_offsets, Tensor(e!) gam_c) -> ()");
   m.def("sigmoid_gate(Tensor(a!) out, Tensor gate) -> ()");
 }
 
@@ -1135,6 +1176,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("moe_combine", &moe_combine);
   m.impl("causal_conv1d", &causal_conv1d);
   m.impl("gdn_recurrent", &gdn_recurrent);
+  m.impl("gdn_chunked", &gdn_chunked);
   m.impl("sigmoid_gate", &sigmoid_gate);
 }
 

@@ -105,3 +105,31 @@ def test_tiny_qwen3_next_engine_graph_vs_eager():
         outs[eager] = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
         llm.shutdown()
     assert outs[True] == outs[False]
+
+
+@pytest.mark.parametrize("lens,ctx", [([64], [0]), ([200, 1, 77], [0, 9, 130]),
+                                      ([1000, 65], [64, 0])])
+def test_gdn_chunked_matches_recurrent(lens, ctx):
+    """Chunked prefill kernels (parallel chunk prep + tensor-core chunk scan) against the
+    token-recurrent kernel: outputs and the carried state."""
+    from vllm_musa_b200.ops import gdn
+    Hk, Hv = 2, 4
+    T = sum(lens)
+    g = torch.Generator().manual_seed(3)
+    qkv = torch.randn(T, 2 * Hk * 128 + Hv * 128, generator=g).to(torch.bfloat16).cuda()
+    ba = torch.randn(T, 2 * Hv, generator=g).to(torch.bfloat16).cuda()
+    A_log = (torch.randn(Hv, generator=g) * 0.5).cuda()
+    dt_bias = (torch.randn(Hv, generator=g) * 0.5).cuda()
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0)), dtype=torch.int32).cuda()
+    sl = torch.tensor([c + n for c, n in zip(ctx, lens)], dtype=torch.int32).cuda()
+    R = len(lens)
+    slots = torch.arange(R, dtype=torch.int32).flip(0).contiguous().cuda()
+    st0 = (torch.randn(R, Hv, 128, 128, generator=g) * 0.05).cuda()
+    s_ref, s_got = st0.clone(), st0.clone()
+    ref = gdn.gdn_recurrent(qkv, ba, A_log, dt_bias, s_ref, cu, sl, slots, Hk, Hv)
+    got = gdn.gdn_chunked(qkv, ba, A_log, dt_bias, s_got, cu, sl, slots, Hk, Hv)
+    torch.cuda.synchronize()
+    from vllm_musa_b200.ops import _ext
+    _ext.check_device_errors()
+    torch.testing.assert_close(got.float(), ref.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(s_got, s_ref, rtol=3e-2, atol=3e-2)

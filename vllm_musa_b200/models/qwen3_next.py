@@ -189,13 +189,32 @@ class Qwen3NextForCausalLM(Qwen3MoeForCausalLM):
             x, residual = self.comm.allreduce_add_rmsnorm(d, residual, nxt, eps)
         return x
 
+    def _delta_rule(self, conv, ba, e, state, meta):
+        """Gated delta rule over this step's tokens: decode rows (first in the batch) with the
+        token-recurrent kernel, prefill rows with the chunked kernels once they fill a chunk."""
+        nd, npf = meta.num_decodes, meta.num_prefills
+        T = conv.shape[0]
+        if npf == 0 or not conv.is_cuda:
+            return gdn_ops.gdn_recurrent(conv, ba, e["A_log"], e["dt_bias"], state, meta.cu_q,
+                                         meta.seq_lens, meta.state_slots, self.Hk_g, self.Hv_g)
+        out = torch.empty(T, self.Hv_g * 128, dtype=conv.dtype, device=conv.device)
+        sl, slots = meta.seq_lens, meta.state_slots
+        if nd > 0:
+            gdn_ops.gdn_recurrent(conv, ba, e["A_log"], e["dt_bias"], state, meta.cu_q[:nd + 1],
+                                  sl[:nd], slots[:nd], self.Hk_g, self.Hv_g, out=out)
+        cu_p = meta.cu_q[nd:nd + npf + 1]
+        fn = gdn_ops.gdn_chunked if T - nd >= gdn_ops.CHUNK_MIN_TOKENS else \
+            gdn_ops.gdn_recurrent
+        fn(conv, ba, e["A_log"], e["dt_bias"], state, cu_p, sl[nd:nd + npf],
+           slots[nd:nd + npf], self.Hk_g, self.Hv_g, out=out)
+        return out
+
     def _gdn(self, j, L, x, meta):
         e = L.extra
         qkvz = ops.linear(x, e["qkvz_w"])
         ba = ops.linear(x, e["ba_w"])
         conv = gdn_ops.causal_conv1d(qkvz, e["conv_w"], self.conv_state[j], meta.cu_q,
                                      meta.seq_lens, meta.state_slots)
-        o = gdn_ops.gdn_recurrent(conv, ba, e["A_log"], e["dt_bias"], self.ssm_state[j],
-                                  meta.cu_q, meta.seq_lens, meta.state_slots, self.Hk_g, self.Hv_g)
+        o = self._delta_rule(conv, ba, e, self.ssm_state[j], meta)
         z = qkvz[:, self.conv_dim:]
         return ops.rms_norm_gated(o, z, e["norm_w"], self.dv, self.cfg.rms_norm_eps)

@@ -146,6 +146,35 @@ def gdn_chunked_ref(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor,
     return out
 
 
+CHUNK_MIN_TOKENS = 64   # requests with at least this many new tokens use the chunked kernels
+_BLOCK_BYTES = 3 * 64 * 128 * 2 + 64 * 64 * 2 + 64 * 128 * 4
+
+
+def gdn_chunked(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
+                state: torch.Tensor, cu_q: torch.Tensor, seq_lens: torch.Tensor,
+                slots: torch.Tensor, Hk: int, Hv: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Same contract as ``gdn_recurrent``, evaluated 64 tokens at a time: a parallel per-chunk
+    kernel (triangular solve, decayed Q K^T / K K^T) and a tensor-core chunk scan carrying the
+    state (csrc/scan/gdn_chunked.cu).  CPU: ``gdn_chunked_ref``."""
+    T = qkv.shape[0]
+    if out is None:
+        out = torch.empty(T, Hv * 128, dtype=qkv.dtype, device=qkv.device)
+    if T == 0:
+        return out
+    if not qkv.is_cuda:
+        out.copy_(gdn_chunked_ref(qkv, ba, A_log, dt_bias, state, cu_q, seq_lens, slots, Hk, Hv))
+        return out
+    R = seq_lens.shape[0]
+    max_chunks = (T + 63) // 64 + R
+    ws = torch.empty(max_chunks * Hv * _BLOCK_BYTES, dtype=torch.uint8, device=qkv.device)
+    offs = torch.empty(R + 1, dtype=torch.int32, device=qkv.device)
+    gam = torch.empty(max_chunks * Hv, dtype=torch.float32, device=qkv.device)
+    _ext.ops().gdn_chunked(qkv, ba, A_log, dt_bias, state, cu_q, seq_lens, slots, Hk, Hv, out,
+                           ws, offs, gam)
+    return out
+
+
 def sigmoid_gate(out: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
     """out *= sigmoid(gate) in place (both [T, W], rows may be strided)."""
     if out.is_cuda:
