@@ -186,6 +186,134 @@ __global__ void __launch_bounds__(512) fused_ar_kernel(ArParams a) {
   if (kTwoShot) block_barrier(a, 2 + a.parity, epoch);
 }
 
+// Two-shot variant for many rows per rank (large T): one WARP per row and eight rows per
+// block, so every block keeps eight rows' peer loads in flight instead of walking one row at a
+// time with block-wide reductions.  Lane l owns the 8-element vectors l, l+32, ... of the row
+// (VPW of them); peer loads are issued CH vectors x NPEER ranks at a time (16 16-byte loads
+// per lane per round trip), accumulated in fp32, the residual added and rounded to bf16 (as
+// the unfused add would), the row normalised with a warp reduction and stored into every
+// rank's output slot.  Same barriers, flags and buffers as fused_ar_kernel.
+constexpr int kWarpRowThreads = 256;
+
+template <int VPW, int NPEER, bool kNorm>
+__global__ void __launch_bounds__(kWarpRowThreads) fused_ar_warp_kernel(ArParams a) {
+  constexpr int CH = 16 / NPEER;  // vectors per round trip (x NPEER loads in flight)
+  static_assert(VPW % CH == 0, "vectors per lane must be a multiple of the chunk");
+  __shared__ uint32_t epoch_s;
+  if (threadIdx.x == 0) {
+    epoch_s = a.epochs[blockIdx.x] + 1;
+    a.epochs[blockIdx.x] = epoch_s;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_s;
+  if (!block_barrier(a, a.parity, epoch)) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kWarpRowThreads / 32;
+  const int nvec = a.H / 8;
+  const int per = (a.T + NPEER - 1) / NPEER;
+  const int r0 = min(a.T, a.rank * per), r1 = min(a.T, r0 + per);
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (int row = r0 + blockIdx.x * kWarps + warp; row < r1; row += gridDim.x * kWarps) {
+    uint4 packed[VPW];
+#pragma unroll
+    for (int i0 = 0; i0 < VPW; i0 += CH) {
+      uint4 t[NPEER][CH];
+#pragma unroll
+      for (int p = 0; p < NPEER; ++p) {
+        const __nv_bfloat16* base =
+            a.rs_rows > 0 ? reinterpret_cast<const __nv_bfloat16*>(a.staging[a.rank]) +
+                                ((size_t)p * a.rs_rows + (row - r0)) * a.H
+                          : reinterpret_cast<const __nv_bfloat16*>(a.staging[p]) +
+                                (size_t)row * a.H;
+        const uint4* src = reinterpret_cast<const uint4*>(base);
+#pragma unroll
+        for (int k = 0; k < CH; ++k) {
+          const int c = lane + 32 * (i0 + k);
+          t[p][k] = c < nvec ? src[c] : zero;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const int c = lane + 32 * (i0 + k);
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < NPEER; ++p) {
+          float f[8];
+          unpack8(t[p][k], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += f[j];
+        }
+        if (a.residual && c < nvec) {
+          uint4* rr = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.residual) +
+                                               (size_t)row * a.H);
+          float r[8];
+          unpack8(rr[c], r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += r[j];
+          packed[i0 + k] = pack8(v);
+          rr[c] = packed[i0 + k];
+        } else {
+          packed[i0 + k] = pack8(v);
+        }
+      }
+    }
+    float inv = 1.f;
+    if constexpr (kNorm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPW; ++i) {
+        if (lane + 32 * i < nvec) {
+          float f[8];
+          unpack8(packed[i], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+        }
+      }
+      ss = warp_sum(ss);
+      inv = rsqrtf(ss / a.H + a.eps);
+    }
+#pragma unroll
+    for (int i = 0; i < VPW; ++i) {
+      const int c = lane + 32 * i;
+      if (c >= nvec) continue;
+      uint4 ov = packed[i];
+      if constexpr (kNorm) {
+        float f[8], w[8];
+        unpack8(packed[i], f);
+        unpack8(reinterpret_cast<const uint4*>(a.weight)[c], w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = f[j] * inv * w[j];
+        ov = pack8(f);
+      }
+#pragma unroll
+      for (int q = 0; q < NPEER; ++q) {
+        const int dst_rank = (a.rank + q) % NPEER;
+        reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out[dst_rank]) +
+                                 (size_t)row * a.H)[c] = ov;
+      }
+    }
+  }
+  block_barrier(a, 2 + a.parity, epoch);
+}
+
+template <int VPW, bool kNorm>
+static void launch_warp_rows(const ArParams& a, cudaStream_t s) {
+  if (a.world == 2)
+    fused_ar_warp_kernel<VPW, 2, kNorm><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
+  else if (a.world == 4)
+    fused_ar_warp_kernel<VPW, 4, kNorm><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
+  else
+    fused_ar_warp_kernel<VPW, 8, kNorm><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
+}
+
+template <bool kNorm>
+static void dispatch_warp_rows(const ArParams& a, int nvec, cudaStream_t s) {
+  if (nvec <= 32 * 8)
+    launch_warp_rows<8, kNorm>(a, s);
+  else
+    launch_warp_rows<16, kNorm>(a, s);
+}
+
 template <bool kNorm, bool kTwoShot>
 static void launch(const ArParams& a, int threads, int vpt, int blocks, cudaStream_t s) {
 #define B200_AR(V) fused_ar_kernel<V, kNorm, kTwoShot><<<blocks, threads, 0, s>>>(a)
@@ -213,7 +341,15 @@ void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
   const int vpt = (nvec + threads - 1) / threads;
   B200_REQUIRE(vpt <= 8, "custom all-reduce: hidden size too large");
   const bool norm = a.weight != nullptr;
-  if (a.two_shot) {
+  const int rows_per_rank = (a.T + a.world - 1) / a.world;
+  if (a.two_shot && rows_per_rank > a.blocks && nvec <= 32 * 16 &&  // rows held in registers
+      (a.world == 2 || a.world == 4 || a.world == 8)) {
+    // several rows per block: warp-per-row kernel keeps them all in flight
+    if (norm)
+      dispatch_warp_rows<true>(a, nvec, s);
+    else
+      dispatch_warp_rows<false>(a, nvec, s);
+  } else if (a.two_shot) {
     if (norm)
       launch<true, true>(a, threads, vpt, a.blocks, s);
     else
