@@ -1002,7 +1002,7 @@ static void launch_splitk_reduce(const Params& p, cudaStream_t stream) {
 // Split-K partials are reduced by the separate grid (measured 1.2-2.5x faster than the in-kernel
 // last-arriver fixup at decode sizes: e.g. M=128 N=4096 K=14336 32.7 vs 60.4 us);
 // B200_GEMM_SPLITK_REDUCE=0 keeps the in-kernel fixup for one-CTA tiles.  CTA-pair tiles always
-// use the grid; swapped (transposed-store) and reduce-scatter epilogues keep the fixup.
+// use the grid; swapped (transposed-store) epilogues keep the fixup.
 static bool splitk_reduce_kernel_on() {
   static int v = -1;
   if (v < 0) {
@@ -1187,8 +1187,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     p.counters = a.counters;
   }
   // deferred split-K reduction (separate grid): the GEMM only writes partials
-  const bool deferred = p.splits > 1 && (pair || (splitk_reduce_kernel_on() && !transposed &&
-                                                   a.mode != kModeScatter));
+  const bool deferred = p.splits > 1 && (pair || (splitk_reduce_kernel_on() && !transposed));
   if (deferred) p.counters = nullptr;
   if (pair) {
     if (a.mode == kModeStore)
@@ -1214,6 +1213,8 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
       launch_splitk_reduce<kStore>(p, stream);
     else if (a.mode == kModeSiluMul)
       launch_splitk_reduce<kSiluMul>(p, stream);
+    else if (a.mode == kModeScatter)  // partial sums reduced, then stored into the owners' slots
+      launch_splitk_reduce<kScatter>(p, stream);
     else
       launch_splitk_reduce<kF32>(p, stream);
   }
