@@ -186,6 +186,32 @@ def case_gdn_decode(it):
            4 * B * Hv * 128 * 128)
 
 
+def case_gdn_prefill(it):
+    """Gated delta rule over 2 x 4096 new tokens (Qwen3-Next 16 QK / 32 V heads at TP=1):
+    chunked kernels (prep + tensor-core scan) and, for comparison, the token recurrence."""
+    from vllm_musa_b200.ops import gdn
+    R, L, Hk, Hv = 2, 4096, 16, 32
+    T = R * L
+    state = torch.zeros(R, Hv, 128, 128, device="cuda")
+    qkv = bf16(T, (2 * Hk + Hv) * 128)
+    ba = bf16(T, 2 * Hv)
+    A, dt = torch.zeros(Hv, device="cuda"), torch.zeros(Hv, device="cuda")
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")
+    seq = torch.full((R,), L, dtype=torch.int32, device="cuda")
+    slots = torch.arange(R, dtype=torch.int32, device="cuda")
+    out = torch.empty(T, Hv * 128, dtype=torch.bfloat16, device="cuda")
+    # matrix-form FLOPs per chunk and head: K K^T, Q K^T (2 C^2 d), solve (C^2 2d),
+    # W S^T, Qg S^T, U^T Kt (3 C d^2), Mq U (C^2 d)
+    C, d = 64, 128
+    flops = 2 * (T // C) * Hv * (2 * C * C * d + C * C * 2 * d + 3 * C * d * d + C * C * d)
+    nbytes = T * (2 * Hk + Hv) * 128 * 2 + T * Hv * 128 * 2
+    us = timed(lambda i: gdn.gdn_chunked(qkv, ba, A, dt, state, cu, seq, slots, Hk, Hv, out), it)
+    report("gdn_chunked_prefill", [R, L, Hk, Hv], us, nbytes, flops)
+    us = timed(lambda i: gdn.gdn_recurrent(qkv, ba, A, dt, state, cu, seq, slots, Hk, Hv, out),
+               max(2, it // 4))
+    report("gdn_recurrent_prefill", [R, L, Hk, Hv], us, nbytes, flops)
+
+
 def case_moe(it):
     from vllm_musa_b200.ops import moe
     T, E, k, H, I = 256, 128, 8, 2048, 768
