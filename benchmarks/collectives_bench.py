@@ -11,6 +11,8 @@ Cases (hidden 4096, bf16, every rank holds its partial sums):
              GEMM + fused all-reduce kernel
   cand       vocab-parallel sampling candidate exchange (one kernel) vs two NCCL all_gathers
 
+Calls are captured into CUDA graphs and replayed (as the engine's decode steps are), so the
+times are device times without per-call host overhead.
 Roofline: the bytes a rank must move over NVLink (one direction, the larger of send / receive)
 divided by the measured peer-copy bandwidth (770 GB/s per direction); for gemm_rs the slower of
 that and the GEMM's FLOPs at the measured bf16 peak.  Prints one JSON line per case and size on
@@ -31,19 +33,43 @@ LINK_BPS = 770e9     # measured peer copy, per direction per GPU
 BF16_FLOPS = 1.639e15  # measured cuBLAS bf16 burst
 
 
-def _time(fn, iters, group):
+def _time(fn, iters, group, graph=True):
+    """Per-call device time, max over ranks.  With ``graph`` the calls are captured once into a
+    CUDA graph (20 back-to-back calls) and replayed, so host launch overhead (one Python
+    dispatch per call on each of N processes) does not enter the number, as in the engine's
+    captured decode steps."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    g = None
+    per = 20
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(per):
+                    fn()
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
     dist.barrier(group=group)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, iters // per) if graph else iters
     s.record()
-    for _ in range(iters):
-        fn()
+    for _ in range(reps):
+        if graph:
+            g.replay()
+        else:
+            fn()
     e.record()
     torch.cuda.synchronize()
-    t = torch.tensor([s.elapsed_time(e) * 1e3 / iters], device="cuda")
+    n = reps * (per if graph else 1)
+    t = torch.tensor([s.elapsed_time(e) * 1e3 / n], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    del g
     return float(t)
 
 
@@ -101,12 +127,10 @@ def main():
         wt = (torch.randn(H, Kr, device=dev) * 0.02).to(torch.bfloat16)
         res = torch.randn(T, H, device=dev).to(torch.bfloat16)
 
-        def fused_rs():
-            ar.begin_forward()
+        def fused_rs():  # consecutive calls alternate the buffer parity by themselves
             ar.linear_allreduce_add_rmsnorm(x, wt, res, w, eps)
 
         def unfused():
-            ar.begin_forward()
             stg = ar.staging_view(T)
             ops.linear(x, wt, out=stg)
             ar.allreduce_add_rmsnorm(stg, res, w, eps)
