@@ -128,6 +128,10 @@ struct AttnParams {
   float* ws_lse;               // [splits, T, Hq]
   int T, Hq, splits;
   float scale_log2;
+  // decode context parallelism: this rank's cache holds the tokens p with p % dcp_size ==
+  // dcp_rank at local index p / dcp_size; lse_out [T, Hq] receives log2-sum-exp of the scores
+  int dcp_size, dcp_rank;
+  float* lse_out;
 };
 
 B200_DEVICE int find_req(const int32_t* cu, int R, int t) {
@@ -153,7 +157,9 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = find_req(p.cu_q, p.R, t);
   const int q_len = p.cu_q[r + 1] - p.cu_q[r];
-  const int count = p.seq_lens[r] - q_len + (t - p.cu_q[r]) + 1;  // causal prefix length
+  int count = p.seq_lens[r] - q_len + (t - p.cu_q[r]) + 1;  // causal prefix length
+  if (p.dcp_size > 1)  // local tokens among the first `count` (dense mode only)
+    count = count > p.dcp_rank ? (count - p.dcp_rank + p.dcp_size - 1) / p.dcp_size : 0;
   // key range of this split (positions in the dense prefix or in the index list)
   // the index list holds min(topk, count) valid positions first (the top-k kernel's layout)
   const int n_keys = max(p.indices ? min(p.topk, count) : count, 0);
@@ -323,6 +329,8 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
         *reinterpret_cast<uint32_t*>(dst + col) =
             pack_bf16x2(o[dt][2 * rr] * inv, o[dt][2 * rr + 1] * inv);
       }
+      if (p.lse_out != nullptr && warp == 0 && tq == 0)
+        p.lse_out[(size_t)t * p.Hq + h] = lrow[rr] > 0.f ? mrow[rr] + log2f(lrow[rr]) : -INFINITY;
     } else {
       float* dst = p.ws_o + (((size_t)split * p.T + t) * p.Hq + h) * kLat + warp * kCols;
 #pragma unroll
@@ -340,7 +348,7 @@ __global__ void __launch_bounds__(kThreads) mla_attn_kernel(AttnParams p) {
 
 __global__ void mla_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
                                    int T, int Hq, int splits, __nv_bfloat16* __restrict__ out,
-                                   int64_t o_t, int64_t o_h) {
+                                   int64_t o_t, int64_t o_h, float* __restrict__ lse_out) {
   const int t = blockIdx.x, h = blockIdx.y;
   float mx = -INFINITY;
   for (int s = 0; s < splits; ++s) mx = fmaxf(mx, ws_lse[((size_t)s * T + t) * Hq + h]);
@@ -358,6 +366,8 @@ __global__ void mla_combine_kernel(const float* __restrict__ ws_o, const float* 
     acc[3] += w * v.w;
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  if (lse_out != nullptr && threadIdx.x == 0)
+    lse_out[(size_t)t * Hq + h] = wsum > 0.f ? mx + log2f(wsum) : -INFINITY;
   __nv_bfloat16* dst = out + (size_t)t * o_t + (size_t)h * o_h + threadIdx.x * 4;
   *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc[0] * inv, acc[1] * inv);
   *reinterpret_cast<uint32_t*>(dst + 2) = pack_bf16x2(acc[2] * inv, acc[3] * inv);
@@ -649,13 +659,19 @@ void run_attention(const MlaArgs& a, cudaStream_t s) {
   p.Hq = a.Hq;
   p.splits = a.splits;
   p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.dcp_size = a.dcp_size > 0 ? a.dcp_size : 1;
+  p.dcp_rank = a.dcp_rank;
+  p.lse_out = a.lse_out;
+  B200_REQUIRE(p.dcp_size == 1 || a.indices == nullptr,
+               "mla: decode context parallelism covers the dense (causal prefix) mode only");
+  B200_REQUIRE(p.dcp_rank >= 0 && p.dcp_rank < p.dcp_size, "mla: dcp rank");
   ensure_dynamic_smem(reinterpret_cast<const void*>(mla_attn_kernel), kSmem);
   mla_attn_kernel<<<dim3(a.T, (a.Hq + kHeads - 1) / kHeads, a.splits), kThreads, kSmem, s>>>(p);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
   if (a.splits > 1) {
     mla_combine_kernel<<<dim3(a.T, a.Hq), kLat / 4, 0, s>>>(a.ws_o, a.ws_lse, a.T, a.Hq, a.splits,
-                                                           p.out, a.o_t, a.o_h);
+                                                           p.out, a.o_t, a.o_h, a.lse_out);
     B200_CUDA_OK(cudaGetLastError());
     count_launch();
   }

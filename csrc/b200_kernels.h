@@ -267,6 +267,10 @@ struct MlaArgs {
   float* ws_lse;  // [splits, T, Hq]
   int T, Hq, splits;
   float scale;
+  // decode context parallelism (dense mode): the cache holds tokens p % dcp_size == dcp_rank at
+  // local index p / dcp_size; lse_out (optional) [T, Hq] log2-sum-exp of the scaled scores
+  int dcp_size = 1, dcp_rank = 0;
+  float* lse_out = nullptr;
 };
 void run_prep(void* q, int64_t ld_q, int Hq, const void* kv, int64_t ld_kv, const void* kv_norm_w,
               float eps, const int32_t* positions, const float* cos_sin, void* cache,

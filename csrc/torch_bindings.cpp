@@ -414,7 +414,8 @@ void mla_prep(Tensor& q, const Tensor& kv, const Tensor& kv_norm_w, double eps,
 void mla_attention(const Tensor& q_lat, const Tensor& q_pe, const Tensor& cache,
                    const Tensor& block_tables, const Tensor& cu_q, const Tensor& seq_lens,
                    const c10::optional<Tensor>& indices, Tensor& out, double scale, int64_t splits,
-                   const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse) {
+                   const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse,
+                   int64_t dcp_size, int64_t dcp_rank, const c10::optional<Tensor>& lse_out) {
   CHECK_CUDA(q_lat);
   TORCH_CHECK(q_lat.dim() == 3 && q_pe.dim() == 3 && out.dim() == 3, "mla_attention: [T, H, C] views");
   TORCH_CHECK(q_lat.stride(2) == 1 && q_pe.stride(2) == 1 && out.stride(2) == 1 &&
@@ -459,6 +460,14 @@ void mla_attention(const Tensor& q_lat, const Tensor& q_pe, const Tensor& cache,
                 "mla_attention: split workspace too small");
     a.ws_o = ws_o->data_ptr<float>();
     a.ws_lse = ws_lse->data_ptr<float>();
+  }
+  a.dcp_size = (int)dcp_size;
+  a.dcp_rank = (int)dcp_rank;
+  if (lse_out.has_value()) {
+    TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->is_contiguous() &&
+                    lse_out->numel() >= (int64_t)a.T * a.Hq,
+                "mla_attention: lse_out [T, H] fp32");
+    a.lse_out = lse_out->data_ptr<float>();
   }
   const c10::cuda::CUDAGuard g(q_lat.device());
   guarded([&] { b200::mla::run_attention(a, stream_of(q_lat)); });
@@ -1108,7 +1117,8 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "mla_attention(Tensor q_lat, Tensor q_pe, Tensor cache, Tensor block_tables, Tensor cu_q, "
       "Tensor seq_lens, Tensor? indices, Tensor(a!) out, float scale, int splits, "
-      "Tensor? ws_o=None, Tensor? ws_lse=None) -> ()");
+      "Tensor? ws_o=None, Tensor? ws_lse=None, int dcp_size=1, int dcp_rank=0, "
+      "Tensor(b!)? lse_out=None) -> ()");
   m.def(
       "indexer_k_prep(Tensor k, Tensor ln_w, Tensor ln_b, float eps, Tensor positions, "
       "Tensor cos_sin, Tensor(a!) cache, Tensor slot_mapping) -> ()");

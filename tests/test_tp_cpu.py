@@ -23,11 +23,17 @@ def _model(name):
     if name == "tiny-moe":
         from test_moe_cpu import tiny_moe
         return tiny_moe(shared=64)
+    if name in ("tiny-ds-dense", "tiny-ds-nomoe"):
+        from test_deepseek_cpu import tiny_ds
+        c = tiny_ds(sparse=False)
+        if name == "tiny-ds-nomoe":
+            c.first_k_dense = c.num_layers  # every layer a dense MLP: no expert routing
+        return c
     from test_qwen3_next_cpu import tiny_next
     return tiny_next()
 
 
-def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False):
+def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     torch.set_num_threads(1)
@@ -38,7 +44,7 @@ def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False):
     cfg = _model(model)
     llm = LLM(cfg, device="cpu", tensor_parallel_size=world, block_size=16, seed=0,
               num_gpu_blocks=64, max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64,
-              enable_expert_parallel=ep)
+              enable_expert_parallel=ep, decode_context_parallel_size=dcp)
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, min(1024, cfg.vocab_size), (3, 20), generator=g).tolist()
     outs = llm.generate(prompts, SamplingParams(temperature=temperature, max_tokens=8,
@@ -47,11 +53,11 @@ def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False):
     destroy_distributed()
 
 
-def _run(world, temperature=0.0, model="tiny-llama", ep=False):
+def _run(world, temperature=0.0, model="tiny-llama", ep=False, dcp=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, temperature, model, ep))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, temperature, model, ep, dcp))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -111,3 +117,15 @@ llm.shutdown()
     assert toks == one
     line2 = [l for l in r.stdout.splitlines() if l.startswith("TOKENS2 ")][0]
     assert eval(line2[len("TOKENS2 "):])[0] == one[0][:4]
+
+
+@pytest.mark.parametrize("dcp", [1, 2])
+def test_tp2_deepseek_mla_matches_tp1(dcp):
+    """DeepSeek MLA at TP=2 (vocab-sharded head: the sampler offsets each rank's candidates by
+    its vocab start) reproduces TP=1; with decode context parallelism (dcp=2) the latent cache
+    is sharded by token over the two ranks (every rank attends all heads over its tokens, then
+    an LSE-weighted reduce-scatter of the partials), through chunked prefill and decode."""
+    one = _run(1, model="tiny-ds-dense")[0]
+    two = _run(2, model="tiny-ds-dense", dcp=dcp)
+    assert two[0] == two[1], "ranks diverged"
+    assert two[0] == one

@@ -195,6 +195,9 @@ class ParallelConfig:
     pipeline_parallel_size: int = 1
     data_parallel_size: int = 1
     enable_expert_parallel: bool = False
+    # decode context parallelism: shard the (replicated) MLA latent cache by token over the
+    # tensor-parallel group; must equal tensor_parallel_size when > 1
+    decode_context_parallel_size: int = 1
     distributed_backend: str = "nccl"
     use_custom_allreduce: bool = True
 

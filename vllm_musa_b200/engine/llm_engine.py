@@ -103,6 +103,11 @@ class LLMEngine:
             self.model.load_weights(safetensors_weights(config.model_path))
         log.info("weights ready in %.1fs", time.time() - t0)
         self.sampler = Sampler(self.comm, getattr(self.model, "vocab_start", 0), st.tp_size)
+        dcp = config.parallel.decode_context_parallel_size
+        if dcp > 1:
+            if not hasattr(self.model, "enable_dcp"):
+                raise ValueError("decode context parallelism needs an MLA model (DeepSeek-V2/V3)")
+            self.model.enable_dcp(dcp, config.cache.block_size)
         self.runner = ModelRunner(config, self.model, self.sampler, device)
         self.drafter = None  # model-based speculative proposer (MTP)
         num_blocks = self.runner.profile_and_allocate_kv()
@@ -116,7 +121,8 @@ class LLMEngine:
         self.num_blocks = num_blocks
         from .. import _C_runtime
         sc = _C_runtime.SchedulerConfig()
-        sc.block_size = config.cache.block_size
+        # with decode context parallelism a scheduler block spans dcp ranks' cache blocks
+        sc.block_size = config.cache.block_size * dcp
         sc.max_num_seqs = config.scheduler.max_num_seqs
         sc.max_num_batched_tokens = config.scheduler.max_num_batched_tokens
         sc.max_model_len = config.scheduler.max_model_len

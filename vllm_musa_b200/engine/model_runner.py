@@ -91,8 +91,10 @@ class ModelRunner:
         self.sampler = sampler
         self.device = device
         sc = cfg.scheduler
-        self.block_size = cfg.cache.block_size
-        self.max_blocks = (sc.max_model_len + self.block_size - 1) // self.block_size
+        self.block_size = cfg.cache.block_size  # per-rank cache block
+        # block-table width in scheduler blocks (dcp ranks' cache blocks each)
+        span = self.block_size * cfg.parallel.decode_context_parallel_size
+        self.max_blocks = (sc.max_model_len + span - 1) // span
         self.buf = StepBuffers(sc.max_num_batched_tokens, sc.max_num_seqs, self.max_blocks, device)
         self.kv_caches: list = []
         self.kv_tensor: Optional[torch.Tensor] = None

@@ -34,7 +34,7 @@ def _load_tokenizer(path: Optional[str]):
 class LLM:
     def __init__(self, model: Union[str, ModelConfig, None] = None, *,
                  tensor_parallel_size: int = 1, enable_expert_parallel: bool = False,
-                 max_model_len: Optional[int] = None, max_num_seqs: int = 256,
+                 decode_context_parallel_size: int = 1, max_model_len: Optional[int] = None, max_num_seqs: int = 256,
                  max_num_batched_tokens: int = 8192, block_size: int = 64,
                  gpu_memory_utilization: float = 0.90, num_gpu_blocks: Optional[int] = None,
                  enable_prefix_caching: bool = True, enable_chunked_prefill: bool = True,
@@ -69,7 +69,8 @@ class LLM:
                                       max_model_len=mlen,
                                       enable_chunked_prefill=enable_chunked_prefill),
             parallel=ParallelConfig(tensor_parallel_size=tensor_parallel_size,
-                                    enable_expert_parallel=enable_expert_parallel),
+                                    enable_expert_parallel=enable_expert_parallel,
+                                    decode_context_parallel_size=decode_context_parallel_size),
             device=device, seed=seed, load_format=load_format, model_path=path,
             enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes,
             speculative=SpeculativeConfig.from_dict(speculative_config))

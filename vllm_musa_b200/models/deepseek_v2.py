@@ -123,6 +123,11 @@ class DeepseekV2ForCausalLM:
         self.vocab_local = cfg.vocab_size // self.tp
         self.layers = [_Layer() for _ in range(cfg.num_layers)]
         self.embed = self.final_norm = self.lm_head = None
+        if cfg.vocab_size % self.tp:
+            raise ValueError("vocab_size must be divisible by tensor_parallel_size")
+        # lm_head rows are vocab-sharded: rank r's logits start at token id r * V / tp (the
+        # vocab-parallel sampler adds this offset to its candidates)
+        self.vocab_start = self.rank * (cfg.vocab_size // self.tp)
         rs = cfg.rope_scaling or {}
         self.cos_sin = ops.build_cos_sin_cache(self.rope, cfg.max_position, cfg.rope_theta,
                                                self.device, scaling=cfg.rope_scaling)
@@ -132,6 +137,8 @@ class DeepseekV2ForCausalLM:
             self.scale *= m * m
         self._staging = defaultdict(dict)
         self._mla_ws = None
+        self.dcp, self.kv_block_size = 1, 0  # decode context parallelism (enable_dcp)
+        self._slots = None
         # DeepSeek multi-token prediction: checkpoint layer index num_layers (loaded if present)
         self.mtp: Optional[_Layer] = None
         self._mtp_staging: dict = {}
@@ -391,6 +398,7 @@ class DeepseekV2ForCausalLM:
         L, eps = self.mtp, self.cfg.rms_norm_eps
         T = next_ids.shape[0]
         self.comm.begin_forward()
+        self._slots = self._dcp_slots(meta.slot_mapping) if self.dcp > 1 else meta.slot_mapping
         e = ops.rms_norm(ops.embedding(next_ids, self.embed), L.enorm, eps)
         hp = ops.rms_norm(prev_hidden, L.hnorm, eps)
         x = L.eh_proj(torch.cat([e, hp], -1).contiguous())
@@ -438,20 +446,44 @@ class DeepseekV2ForCausalLM:
         """KV splits of the MLA kernel for T query tokens (static for a graph size)."""
         if T > 64 or self.device.type != "cuda":
             return 1
-        groups = T * ((self.hq + 15) // 16)
-        keys = self.cfg.index_topk if self.sparse else self.cfg.max_position
+        groups = T * ((self.hq * self.dcp + 15) // 16)
+        keys = self.cfg.index_topk if self.sparse else self.cfg.max_position // self.dcp
         return mla_ops.choose_splits(groups, keys)
 
     def _ws(self, T: int, splits: int):
         if splits == 1:
             return None
-        need = splits * T * self.hq * 512
+        heads = self.hq * self.dcp  # decode context parallelism attends every head
+        need = splits * T * heads * 512
         if self._mla_ws is None or self._mla_ws[0].numel() < need:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("MLA split workspace must be reserved before graph capture")
             self._mla_ws = (torch.empty(need, device=self.device),
-                            torch.empty(splits * T * self.hq, device=self.device))
+                            torch.empty(splits * T * heads, device=self.device))
         return self._mla_ws
+
+    # ------------------------------------------------------------------ decode context parallel
+    def enable_dcp(self, size: int, kv_block_size: int) -> None:
+        """Decode context parallelism over the tensor-parallel group (size == TP): the latent
+        cache is sharded by token (rank r keeps tokens p % size == r at local index p // size)
+        instead of replicated on every rank, so each rank holds 1 / size of every request's
+        context.  The scheduler's blocks then span kv_block_size * size tokens, kv_block_size
+        of them on each rank.  Dense MLA only (the V3.2 sparse indexer keeps its own cache)."""
+        if size > 1 and self.sparse:
+            raise ValueError("decode context parallelism supports dense MLA (no sparse indexer)")
+        if size > 1 and size != self.tp:
+            raise ValueError("decode_context_parallel_size must equal tensor_parallel_size")
+        self.dcp, self.kv_block_size = size, kv_block_size
+
+    def _dcp_slots(self, slot_mapping: torch.Tensor) -> torch.Tensor:
+        """Scheduler slot (virtual block * bs * dcp + offset) -> this rank's local slot, or -1
+        for tokens another rank stores."""
+        bs, n = self.kv_block_size, self.dcp
+        span = bs * n
+        off = torch.remainder(slot_mapping, span)
+        local = torch.div(slot_mapping, span, rounding_mode="floor") * bs + off // n
+        keep = (slot_mapping >= 0) & (off % n == self.rank)
+        return torch.where(keep, local, torch.full_like(local, -1)).to(slot_mapping.dtype)
 
     def reserve_workspaces(self, max_tokens: int) -> None:
         for T in range(1, min(max_tokens, 64) + 1):
@@ -462,6 +494,7 @@ class DeepseekV2ForCausalLM:
         cfg, eps = self.cfg, self.cfg.rms_norm_eps
         T = input_ids.shape[0]
         self.comm.begin_forward()
+        self._slots = self._dcp_slots(meta.slot_mapping) if self.dcp > 1 else meta.slot_mapping
         h = ops.embedding(input_ids, self.embed)
         residual = h
         n = len(self.layers)
@@ -499,17 +532,30 @@ class DeepseekV2ForCausalLM:
             q = a
         qh = q[:, :hq * 192]
         mla_ops.mla_prep(qh, kv, L.kv_a_norm, eps, meta.positions, self.cos_sin, lat_cache,
-                         meta.slot_mapping, hq)
+                         self._slots if self._slots is not None else meta.slot_mapping, hq)
         q3 = qh.view(T, hq, 192)
         q_lat = torch.bmm(q3[:, :, :128].transpose(0, 1), L.w_kb)  # [hq, T, 512]
         indices = None
         if self.sparse:
             indices = self._indexer(L, q, a, meta, idx_cache, T)
-        o_lat = torch.empty(hq, T, 512, dtype=a.dtype, device=a.device)
         splits = self._splits(T)
-        mla_ops.mla_attention(q_lat.transpose(0, 1), q3[:, :, 128:], lat_cache, meta.block_tables,
-                              meta.cu_q, meta.seq_lens, indices, o_lat.transpose(0, 1),
-                              self.scale, splits, self._ws(T, splits))
+        if self.dcp > 1:
+            # every rank attends ALL heads over its token shard, then an LSE-weighted
+            # reduce-scatter returns each rank its own heads
+            ql = self.comm.all_gather(q_lat.transpose(0, 1).contiguous(), dim=1)  # [T, H, 512]
+            qp = self.comm.all_gather(q3[:, :, 128:].contiguous(), dim=1)         # [T, H, 64]
+            H = ql.shape[1]
+            o_all = torch.empty(T, H, 512, dtype=a.dtype, device=a.device)
+            lse = torch.empty(T, H, dtype=torch.float32, device=a.device)
+            mla_ops.mla_attention(ql, qp, lat_cache, meta.block_tables, meta.cu_q, meta.seq_lens,
+                                  None, o_all, self.scale, splits, self._ws(T, splits),
+                                  dcp=(self.dcp, self.rank), lse_out=lse)
+            o_lat = mla_ops.dcp_combine(o_all, lse, self.comm).transpose(0, 1).contiguous()
+        else:
+            o_lat = torch.empty(hq, T, 512, dtype=a.dtype, device=a.device)
+            mla_ops.mla_attention(q_lat.transpose(0, 1), q3[:, :, 128:], lat_cache,
+                                  meta.block_tables, meta.cu_q, meta.seq_lens, indices,
+                                  o_lat.transpose(0, 1), self.scale, splits, self._ws(T, splits))
         o = torch.bmm(o_lat, L.w_vb)  # [hq, T, 128]
         return o.transpose(0, 1).reshape(T, hq * self.vdim)
 

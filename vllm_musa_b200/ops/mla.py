@@ -9,6 +9,7 @@ RoPE of the latent path is the interleaved (GPT-J) form; the indexer uses NeoX h
 """
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import torch
@@ -91,22 +92,37 @@ def _gather_rows(cache: torch.Tensor, bt_row: torch.Tensor, pos: torch.Tensor) -
     return cache.reshape(-1, cache.shape[-1])[slots]
 
 
+def dcp_local_count(count: int, dcp: tuple) -> int:
+    """Tokens p < count with p % size == rank (those this decode-context-parallel rank holds)."""
+    size, rank = dcp
+    return (count - rank + size - 1) // size if count > rank else 0
+
+
 def mla_attention(q_lat: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor,
                   block_tables: torch.Tensor, cu_q: torch.Tensor, seq_lens: torch.Tensor,
                   indices: Optional[torch.Tensor], out: torch.Tensor, scale: float,
-                  splits: int = 1, ws: Optional[tuple] = None) -> torch.Tensor:
+                  splits: int = 1, ws: Optional[tuple] = None, dcp: tuple = (1, 0),
+                  lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Absorbed MLA: q_lat [T, H, 512], q_pe [T, H, 64] (views with any token / head stride)
     -> out [T, H, 512] = softmax(q . [c_kv | k_pe]^T * scale) . c_kv over the causal prefix
-    (indices None) or the listed token positions (indices [T, topk], -1 = unused)."""
+    (indices None) or the listed token positions (indices [T, topk], -1 = unused).
+
+    ``dcp`` = (size, rank): decode context parallelism, dense mode only -- this rank's cache
+    holds the tokens p with p % size == rank at local index p // size, and the attention runs
+    over those.  ``lse_out`` [T, H] fp32 receives log2(sum exp2(score * scale * log2 e)) of the
+    keys attended (the weight of this partial in a cross-rank combine)."""
     T = q_lat.shape[0]
     if T == 0:
         return out
     if q_lat.is_cuda:
         wo, wl = ws if ws is not None else (None, None)
         _ext.ops().mla_attention(q_lat, q_pe, cache, block_tables, cu_q, seq_lens, indices, out,
-                                 scale, splits, wo, wl)
+                                 scale, splits, wo, wl, dcp[0], dcp[1], lse_out)
         return out
+    assert dcp[0] == 1 or indices is None, "decode context parallelism: dense mode only"
     for t, (r, count) in enumerate(_req_of_tokens(cu_q, seq_lens)):
+        if dcp[0] > 1:
+            count = dcp_local_count(count, dcp)
         if indices is None:
             pos = torch.arange(count)
         else:
@@ -114,12 +130,36 @@ def mla_attention(q_lat: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor,
             pos = pos[(pos >= 0) & (pos < count)]
         if pos.numel() == 0:
             out[t] = 0
+            if lse_out is not None:
+                lse_out[t] = float("-inf")
             continue
         kv = _gather_rows(cache, block_tables[r], pos).float()  # [n, 576]
         q = torch.cat([q_lat[t].float(), q_pe[t].float()], -1)  # [H, 576]
-        p = torch.softmax(q @ kv.t() * scale, -1)
+        sc = q @ kv.t() * scale
+        p = torch.softmax(sc, -1)
         out[t] = (p @ kv[:, :LAT]).to(out.dtype)
+        if lse_out is not None:
+            lse_out[t] = torch.logsumexp(sc, -1) / math.log(2.0)
     return out
+
+
+def dcp_combine(out: torch.Tensor, lse: torch.Tensor, comm) -> torch.Tensor:
+    """Cross-rank combine of decode-context-parallel partials: every rank holds out [T, H, C]
+    and lse [T, H] (log2 domain) for ALL heads over its token shard.  The log-sum-exp values
+    are all-gathered, each rank scales its partial by its softmax weight, and a reduce-scatter
+    over heads sums the weighted partials and leaves rank r its H / world heads.
+    Reference: vllm_musa/v1/attention/backends/flash_attn.py:179-237 (LSE-corrected
+    reduce-scatter), :1593-1726 (DCP attention)."""
+    world = comm.world
+    T, H, C = out.shape
+    lses = comm.all_gather(lse.unsqueeze(0), dim=0)            # [world, T, H]
+    m = lses.max(0).values
+    m = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+    wts = torch.exp2(lses - m)                                 # [world, T, H]
+    wsum = wts.sum(0)
+    mine = torch.where(wsum > 0, wts[comm.rank] / wsum.clamp_min(1e-30), torch.zeros_like(wsum))
+    part = (out.float() * mine.unsqueeze(-1))                  # [T, H, C]
+    return comm.reduce_scatter(part, dim=1).to(out.dtype)      # [T, H / world, C]
 
 
 def indexer_k_prep(k: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, eps: float,

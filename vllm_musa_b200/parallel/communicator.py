@@ -24,6 +24,7 @@ class TPCommunicator:
         self.st = st
         self.device = device
         self.world = st.tp_size
+        self.rank = st.tp_rank
         self.group = st.tp_group
         self.custom = custom  # CustomAllReduce (NVSwitch P2P) or None
         self.ep_a2a = None    # EPAllToAll (expert-parallel dispatch/combine) or None
@@ -50,6 +51,21 @@ class TPCommunicator:
         if dim == 0:
             return out.reshape((-1,) + tuple(x.shape[1:]))
         return torch.cat(list(out.unbind(0)), dim=dim)
+
+    def reduce_scatter(self, x: torch.Tensor, dim: int = 0) -> torch.Tensor:
+        """Sum over ranks, then rank r keeps the r-th of ``world`` equal slices along ``dim``."""
+        if self.world == 1:
+            return x
+        xt = x.movedim(dim, 0).contiguous()
+        n = xt.shape[0] // self.world
+        if x.is_cuda:
+            out = torch.empty((n,) + tuple(xt.shape[1:]), dtype=x.dtype, device=x.device)
+            dist.reduce_scatter_tensor(out, xt, group=self.group)
+        else:  # gloo has no reduce-scatter: all-reduce and keep this rank's slice
+            dist.all_reduce(xt, group=self.group)
+            r = dist.get_rank(self.group)
+            out = xt[r * n:(r + 1) * n].contiguous()
+        return out.movedim(0, dim)
 
     # -- buffers ----------------------------------------------------------------------------
     def begin_forward(self) -> None:
