@@ -121,3 +121,52 @@ def test_indexer_scores_and_topk():
             assert len(sel) == k and -1 not in sel
             thresh = got.cpu()[t, :count].topk(k).values[-1]
             assert (got.cpu()[t, row.long()] >= thresh).all()
+
+
+@pytest.mark.parametrize("dcp,splits", [(2, 1), (4, 3)])
+def test_mla_attention_dcp_partials_combine(dcp, splits):
+    """Decode context parallelism, emulated on one GPU: each virtual rank's cache holds the
+    tokens p % dcp == rank at local index p // dcp; the kernel attends those (dcp params) and
+    reports the log2-sum-exp; the LSE-weighted combine of the partials equals full attention."""
+    g = torch.Generator().manual_seed(7 + dcp)
+    bs, H = 16, 32
+    q_lens, hist = [1, 1, 5, 70, 1], [200, 0, 30, 0, 1000]
+    bt, cu, seq = _layout(q_lens, hist, bs, g, nblk=128)
+    T = int(cu[-1])
+    cache = (torch.randn(128, bs, 576, generator=g) * 0.5).to(torch.bfloat16)
+    q_lat = torch.randn(T, H, 512, generator=g).to(torch.bfloat16)
+    q_pe = torch.randn(T, H, 64, generator=g).to(torch.bfloat16)
+    scale = 192 ** -0.5
+    ref = torch.zeros(T, H, 512, dtype=torch.bfloat16)
+    mla.mla_attention(q_lat, q_pe, cache, bt, cu, seq, None, ref, scale)
+    flat = cache.view(-1, 576)
+    outs, lses = [], []
+    for r in range(dcp):
+        # local cache of virtual rank r: token p (p % dcp == r) at local index p // dcp
+        loc = torch.zeros(128, bs, 576, dtype=torch.bfloat16)
+        lbt = torch.zeros_like(bt)
+        nb = 0
+        for i, L in enumerate(seq.tolist()):
+            n_loc = (L - r + dcp - 1) // dcp if L > r else 0
+            for b in range((n_loc + bs - 1) // bs):
+                lbt[i, b] = nb
+                nb += 1
+            for li in range(n_loc):
+                p = li * dcp + r
+                src = int(bt[i, p // bs]) * bs + p % bs
+                loc[int(lbt[i, li // bs]), li % bs] = flat[src]
+        o = torch.empty(T, H, 512, dtype=torch.bfloat16, device="cuda")
+        lse = torch.empty(T, H, dtype=torch.float32, device="cuda")
+        ws = None
+        if splits > 1:
+            ws = (torch.empty(splits * T * H * 512, device="cuda"),
+                  torch.empty(splits * T * H, device="cuda"))
+        mla.mla_attention(q_lat.cuda(), q_pe.cuda(), loc.cuda(), lbt.cuda(), cu.cuda(),
+                          seq.cuda(), None, o, scale, splits, ws, dcp=(dcp, r), lse_out=lse)
+        outs.append(o.float().cpu())
+        lses.append(lse.cpu())
+    L = torch.stack(lses)                                   # [dcp, T, H]
+    m = L.max(0).values
+    w = torch.exp2(L - m)
+    comb = (torch.stack(outs) * w.unsqueeze(-1)).sum(0) / w.sum(0).unsqueeze(-1)
+    torch.testing.assert_close(comb, ref.float(), rtol=2e-2, atol=2e-2)
