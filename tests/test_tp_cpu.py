@@ -33,7 +33,7 @@ def _model(name):
     return tiny_next()
 
 
-def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp=1):
+def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp=1, dp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     torch.set_num_threads(1)
@@ -42,7 +42,8 @@ def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.parallel.state import destroy_distributed
     cfg = _model(model)
-    llm = LLM(cfg, device="cpu", tensor_parallel_size=world, block_size=16, seed=0,
+    llm = LLM(cfg, device="cpu", tensor_parallel_size=world // dp, data_parallel_size=dp,
+              block_size=16, seed=0,
               num_gpu_blocks=64, max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64,
               enable_expert_parallel=ep, decode_context_parallel_size=dcp)
     g = torch.Generator().manual_seed(0)
@@ -53,11 +54,12 @@ def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp
     destroy_distributed()
 
 
-def _run(world, temperature=0.0, model="tiny-llama", ep=False, dcp=1):
+def _run(world, temperature=0.0, model="tiny-llama", ep=False, dcp=1, dp=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, temperature, model, ep, dcp))
+    procs = [ctx.Process(target=_worker,
+                         args=(r, world, port, q, temperature, model, ep, dcp, dp))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -129,3 +131,13 @@ def test_tp2_deepseek_mla_matches_tp1(dcp):
     two = _run(2, model="tiny-ds-dense", dcp=dcp)
     assert two[0] == two[1], "ranks diverged"
     assert two[0] == one
+
+
+@pytest.mark.parametrize("world,dp", [(2, 2), (4, 2)])
+def test_data_parallel_replicas_match_single(world, dp):
+    """Data parallelism: dp engine replicas (each TP = world / dp) split the prompts and every
+    rank returns all outputs in prompt order, equal to the single-engine run."""
+    one = _run(1, temperature=0.7)[0]
+    res = _run(world, temperature=0.7, dp=dp)
+    for r in range(world):
+        assert res[r] == one

@@ -34,7 +34,8 @@ def _load_tokenizer(path: Optional[str]):
 class LLM:
     def __init__(self, model: Union[str, ModelConfig, None] = None, *,
                  tensor_parallel_size: int = 1, enable_expert_parallel: bool = False,
-                 decode_context_parallel_size: int = 1, max_model_len: Optional[int] = None, max_num_seqs: int = 256,
+                 decode_context_parallel_size: int = 1, data_parallel_size: int = 1,
+                 max_model_len: Optional[int] = None, max_num_seqs: int = 256,
                  max_num_batched_tokens: int = 8192, block_size: int = 64,
                  gpu_memory_utilization: float = 0.90, num_gpu_blocks: Optional[int] = None,
                  enable_prefix_caching: bool = True, enable_chunked_prefill: bool = True,
@@ -70,12 +71,27 @@ class LLM:
                                       enable_chunked_prefill=enable_chunked_prefill),
             parallel=ParallelConfig(tensor_parallel_size=tensor_parallel_size,
                                     enable_expert_parallel=enable_expert_parallel,
-                                    decode_context_parallel_size=decode_context_parallel_size),
+                                    decode_context_parallel_size=decode_context_parallel_size,
+                                    data_parallel_size=data_parallel_size),
             device=device, seed=seed, load_format=load_format, model_path=path,
             enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes,
             speculative=SpeculativeConfig.from_dict(speculative_config))
         tok = tokenizer if tokenizer is not None else _load_tokenizer(path)
         self.executor = None
+        self.dp_size, self.dp_rank = 1, 0
+        if data_parallel_size > 1:
+            # data parallelism: WORLD_SIZE = dp x tp ranks under one launcher; ranks
+            # [k*tp, (k+1)*tp) run engine replica k (its own TP group, KV cache and scheduler)
+            # and generate() splits the prompts over the replicas
+            world = int(os.environ.get("WORLD_SIZE", "1"))
+            if world != data_parallel_size * tensor_parallel_size:
+                raise ValueError("data_parallel_size > 1 needs WORLD_SIZE == "
+                                 "data_parallel_size * tensor_parallel_size (torchrun)")
+            from ..parallel.state import init_distributed
+            st = init_distributed(tp_size=tensor_parallel_size,
+                                  ep=enable_expert_parallel,
+                                  backend="nccl" if device == "cuda" else "gloo")
+            self.dp_size, self.dp_rank = st.dp_size, st.dp_rank
         if tensor_parallel_size > 1 and "WORLD_SIZE" not in os.environ:
             # no launcher: spawn follower ranks and drive them from this process
             from ..engine.executor import MultiprocExecutor
@@ -109,6 +125,8 @@ class LLM:
             sampling_params = SamplingParams()
         if isinstance(sampling_params, SamplingParams):
             sampling_params = [sampling_params] * len(prompts)
+        if self.dp_size > 1:
+            return self._generate_dp(prompts, sampling_params)
         order = []
         for p, sp in zip(prompts, sampling_params):
             ids, text = self._prompt_ids(p)
@@ -122,6 +140,29 @@ class LLM:
                 if o.finished:
                     done[o.request_id] = o
         return [done[r] for r in order]
+
+    def _generate_dp(self, prompts, sampling_params) -> List[RequestOutput]:
+        """Replica k serves prompts k, k + dp, ...; the outputs are exchanged over the world
+        group so every rank returns the full list in prompt order."""
+        import torch.distributed as dist
+        k, n = self.dp_rank, self.dp_size
+        mine = list(range(k, len(prompts), n))
+        saved, self.dp_size = self.dp_size, 1
+        try:
+            outs = self.generate([prompts[i] for i in mine], [sampling_params[i] for i in mine])
+        finally:
+            self.dp_size = saved
+        parts = [None] * dist.get_world_size()
+        dist.all_gather_object(parts, (k, mine, outs))
+        res: List[Optional[RequestOutput]] = [None] * len(prompts)
+        seen = set()
+        for rep, idx, o in parts:
+            if rep in seen:  # every TP rank of a replica returns the same outputs
+                continue
+            seen.add(rep)
+            for i, out in zip(idx, o):
+                res[i] = out
+        return res
 
     def shutdown(self):
         self.engine.shutdown()
