@@ -41,6 +41,7 @@ constexpr int kPrepThreads = 256;
 constexpr int kScanThreads = 128;
 constexpr int kCols = 32;    // value columns per scan CTA
 constexpr int kPadK = kD + 1;
+constexpr int kLdP = kD + 8;  // bf16 row stride (272 B) of the prep kernel's tensor-core copies
 
 // workspace block per (chunk, head)
 constexpr size_t kWBytes = kC * kD * 2, kQgBytes = kC * kD * 2, kKtBytes = kC * kD * 2;
@@ -91,6 +92,29 @@ B200_DEVICE uint8_t* block_of(const ChunkParams& p, int chunk, int h) {
   return p.ws + ((size_t)chunk * p.Hv + h) * kBlockBytes;
 }
 
+B200_DEVICE uint32_t s_addr(const void* p) { return smem_u32(p); }
+
+// A fragment (16 x 16 at (row0, k0)) of a row-major bf16 matrix with row stride ld elements
+B200_DEVICE void load_a(const __nv_bfloat16* base, int ld, int row0, int k0, int lane,
+                        uint32_t (&a)[4]) {
+  const __nv_bfloat16* p = base + (row0 + (lane & 15)) * ld + k0 + ((lane >> 4) << 3);
+  mma::ldsm_x4(s_addr(p), a[0], a[1], a[2], a[3]);
+}
+// B fragments of two n8 tiles (n0, n0+8) x k16 at k0 from an [n][k] (k contiguous) matrix
+B200_DEVICE void load_b_nk(const __nv_bfloat16* base, int ld, int n0, int k0, int lane,
+                           uint32_t& b0, uint32_t& b1, uint32_t& b2, uint32_t& b3) {
+  const __nv_bfloat16* p =
+      base + (n0 + (lane & 7) + ((lane >> 4) << 3)) * ld + k0 + (((lane >> 3) & 1) << 3);
+  mma::ldsm_x4(s_addr(p), b0, b1, b2, b3);
+}
+// B fragments of two n8 tiles x k16 from a [k][n] (n contiguous) matrix (transposing load)
+B200_DEVICE void load_b_kn(const __nv_bfloat16* base, int ld, int n0, int k0, int lane,
+                           uint32_t& b0, uint32_t& b1, uint32_t& b2, uint32_t& b3) {
+  const __nv_bfloat16* p =
+      base + (k0 + (lane & 7) + (((lane >> 3) & 1) << 3)) * ld + n0 + ((lane >> 4) << 3);
+  mma::ldsm_x4_t(s_addr(p), b0, b1, b2, b3);
+}
+
 // ------------------------------------------------------------------------------------ prep
 __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(ChunkParams p) {
   extern __shared__ float smf[];
@@ -100,6 +124,8 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(ChunkParam
   float* sL = sV + kC * kPadK;          // [64][65] beta_t e^{G_t-G_i} k_t.k_i (i<t)
   float* sG = sL + kC * (kC + 1);       // [64] cumulative log decay
   float* sB = sG + kC;                  // [64] beta
+  __nv_bfloat16* sKb = reinterpret_cast<__nv_bfloat16*>(sB + kC);  // [64][136] bf16 k
+  __nv_bfloat16* sQb = sKb + kC * kLdP;                              // [64][136] bf16 q
 
   const int chunk = blockIdx.x, h = blockIdx.y;
   const int total = p.chunk_offsets[p.R];
@@ -138,6 +164,8 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(ChunkParam
       sQ[t * kPadK + lane * 4 + e] = qv[e] * iq;
       sK[t * kPadK + lane * 4 + e] = kv[e] * ik;
       sV[t * kPadK + lane * 4 + e] = vv[e];
+      sQb[t * kLdP + lane * 4 + e] = f2bf(qv[e] * iq);
+      sKb[t * kLdP + lane * 4 + e] = f2bf(kv[e] * ik);
     }
   }
   // gates and the cumulative log decay (warp 0: two tokens per lane, then a scan)
@@ -183,25 +211,47 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(ChunkParam
   float* gU0 = reinterpret_cast<float*>(blk + kWBytes + kQgBytes + kKtBytes + kMqBytes);
   const float Gc = sG[C - 1];
 
-  // decayed K K^T (strictly lower, times beta_t) and Q K^T (lower incl. diagonal)
-  for (int e = tid; e < kC * kC; e += kPrepThreads) {
-    const int t = e / kC, i = e % kC;
-    float kk = 0.f, qk = 0.f;
-    if (i <= t) {
-      const float* kt = sK + t * kPadK;
-      const float* ki = sK + i * kPadK;
-      const float* qt = sQ + t * kPadK;
-#pragma unroll 8
-      for (int d = 0; d < kD; ++d) {
-        kk += kt[d] * ki[d];
-        qk += qt[d] * ki[d];
+  // decayed K K^T (strictly lower, times beta_t) and Q K^T (lower incl. diagonal) on the
+  // tensor cores (bf16 operands, fp32 accumulation): warp w owns rows [16 (w&3), +16) and
+  // columns [32 (w>>2), +32) of both 64 x 64 products
+  {
+    const int mt = warp & 3, nh = warp >> 2;
+    const int g = lane >> 2, tq = lane & 3;
+    float kk[4][4], qk[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kk[nt][e] = qk[nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < kD / 16; ++ks) {
+      uint32_t ak[4], aq[4];
+      load_a(sKb, kLdP, mt * 16, ks * 16, lane, ak);
+      load_a(sQb, kLdP, mt * 16, ks * 16, lane, aq);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        load_b_nk(sKb, kLdP, nh * 32 + np * 16, ks * 16, lane, b0, b1, b2, b3);
+        mma::mma_bf16(kk[2 * np], ak, b0, b1);
+        mma::mma_bf16(kk[2 * np + 1], ak, b2, b3);
+        mma::mma_bf16(qk[2 * np], aq, b0, b1);
+        mma::mma_bf16(qk[2 * np + 1], aq, b2, b3);
       }
-      const float dec = __expf(sG[t] - sG[i]);
-      kk *= dec * sB[t];
-      qk *= dec;
     }
-    sL[t * (kC + 1) + i] = i < t ? kk : 0.f;
-    gMq[t * kC + i] = f2bf(qk);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = mt * 16 + g + ((e >> 1) << 3);
+        const int i = nh * 32 + nt * 8 + 2 * tq + (e & 1);
+        float kv = 0.f, qv = 0.f;
+        if (i <= t) {
+          const float dec = __expf(sG[t] - sG[i]);
+          kv = kk[nt][e] * dec * sB[t];
+          qv = qk[nt][e] * dec;
+        }
+        sL[t * (kC + 1) + i] = i < t ? kv : 0.f;
+        gMq[t * kC + i] = f2bf(qv);
+      }
   }
   __syncthreads();
 
@@ -249,29 +299,6 @@ struct ScanSmem {
   __nv_bfloat16 S[kCols * kLdS];   // state slice [v][k] (bf16 copy for the products)
   __nv_bfloat16 Ut[kCols * kLdU];  // U^T [v][t]
 };
-
-B200_DEVICE uint32_t s_addr(const void* p) { return smem_u32(p); }
-
-// A fragment (16 x 16 at (row0, k0)) of a row-major bf16 matrix with row stride ld elements
-B200_DEVICE void load_a(const __nv_bfloat16* base, int ld, int row0, int k0, int lane,
-                        uint32_t (&a)[4]) {
-  const __nv_bfloat16* p = base + (row0 + (lane & 15)) * ld + k0 + ((lane >> 4) << 3);
-  mma::ldsm_x4(s_addr(p), a[0], a[1], a[2], a[3]);
-}
-// B fragments of two n8 tiles (n0, n0+8) x k16 at k0 from an [n][k] (k contiguous) matrix
-B200_DEVICE void load_b_nk(const __nv_bfloat16* base, int ld, int n0, int k0, int lane,
-                           uint32_t& b0, uint32_t& b1, uint32_t& b2, uint32_t& b3) {
-  const __nv_bfloat16* p =
-      base + (n0 + (lane & 7) + ((lane >> 4) << 3)) * ld + k0 + (((lane >> 3) & 1) << 3);
-  mma::ldsm_x4(s_addr(p), b0, b1, b2, b3);
-}
-// B fragments of two n8 tiles x k16 from a [k][n] (n contiguous) matrix (transposing load)
-B200_DEVICE void load_b_kn(const __nv_bfloat16* base, int ld, int n0, int k0, int lane,
-                           uint32_t& b0, uint32_t& b1, uint32_t& b2, uint32_t& b3) {
-  const __nv_bfloat16* p =
-      base + (k0 + (lane & 7) + (((lane >> 3) & 1) << 3)) * ld + n0 + ((lane >> 4) << 3);
-  mma::ldsm_x4_t(s_addr(p), b0, b1, b2, b3);
-}
 
 __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(ChunkParams p) {
   extern __shared__ uint8_t sm_raw[];
@@ -475,7 +502,8 @@ void run_gdn_chunked(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld
   chunk_offsets_kernel<<<1, 32, 0, s>>>(cu_q, R, chunk_offsets);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
-  const int prep_smem = (3 * kC * kPadK + kC * (kC + 1) + 2 * kC) * (int)sizeof(float);
+  const int prep_smem = (3 * kC * kPadK + kC * (kC + 1) + 2 * kC) * (int)sizeof(float) +
+                        2 * kC * kLdP * (int)sizeof(__nv_bfloat16);
   ensure_dynamic_smem(reinterpret_cast<const void*>(gdn_chunk_prep_kernel), prep_smem);
   gdn_chunk_prep_kernel<<<dim3(p.max_chunks, Hv), kPrepThreads, prep_smem, s>>>(p);
   B200_CUDA_OK(cudaGetLastError());
