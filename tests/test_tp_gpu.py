@@ -92,3 +92,23 @@ def test_tp2_engine_matches_tp1(tmp_path, eager):
     assert (la - lb).abs().max().item() < 0.05
     same_first = sum(x[0] == y[0] for x, y in zip(a["tokens"], b0["tokens"]))
     assert same_first >= 3
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("eager", [True, False])
+def test_deepseek_dcp2_matches_tp1(tmp_path, eager):
+    """DeepSeek MLA with decode context parallelism over 2 GPUs (latent cache sharded by token,
+    all heads per shard, LSE-weighted reduce-scatter) against TP=1: same first-step logits up
+    to bf16 noise and the same greedy first tokens."""
+    p1, p2 = str(tmp_path / "d1"), str(tmp_path / "d2")
+    extra = ["--eager"] if eager else []
+    _torchrun(1, ["--mode", "llm", "--model", "ds", "--out", p1, "--tp", "1"] + extra, 29671)
+    _torchrun(2, ["--mode", "llm", "--model", "ds", "--dcp", "2", "--out", p2, "--tp", "2"] +
+              extra, 29681)
+    a = json.load(open(p1 + ".0"))
+    b0, b1 = json.load(open(p2 + ".0")), json.load(open(p2 + ".1"))
+    assert b0["tokens"] == b1["tokens"], "DCP ranks diverged"
+    la, lb = torch.tensor(a["logits0"]), torch.tensor(b0["logits0"])
+    assert (la - lb).abs().max().item() < 0.05
+    same_first = sum(x[0] == y[0] for x, y in zip(a["tokens"], b0["tokens"]))
+    assert same_first >= 3

@@ -164,14 +164,28 @@ def moe_cfg():
                        name="tp-moe-test")
 
 
-def mode_llm(out_path, tp, eager, model="dense", ep=False):
+def ds_cfg():
+    """Small dense-MLA DeepSeek (no sparse indexer) for the decode-context-parallel check."""
+    from vllm_musa_b200.config import ModelConfig
+    return ModelConfig(arch="deepseek_v3", vocab_size=4096, hidden_size=1024, num_layers=3,
+                       num_heads=16, num_kv_heads=16, head_dim=192, intermediate_size=2048,
+                       rms_norm_eps=1e-6, rope_theta=1e4, max_position=2048,
+                       num_experts=16, num_experts_per_tok=2, moe_intermediate_size=256,
+                       shared_expert_intermediate_size=256, first_k_dense=1, n_group=4,
+                       topk_group=2, routed_scaling_factor=2.5, scoring_func="sigmoid",
+                       q_lora_rank=256, kv_lora_rank=512, qk_nope_head_dim=128,
+                       qk_rope_head_dim=64, v_head_dim=128, index_n_heads=0, index_head_dim=0,
+                       index_topk=0, rope_neox=False, name="tp-ds-test")
+
+
+def mode_llm(out_path, tp, eager, model="dense", ep=False, dcp=1):
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.parallel.state import destroy_distributed, get_parallel_state
-    cfg = moe_cfg() if model == "moe" else small_cfg()
+    cfg = moe_cfg() if model == "moe" else ds_cfg() if model == "ds" else small_cfg()
     llm = LLM(cfg, tensor_parallel_size=tp, block_size=64, seed=0, num_gpu_blocks=256,
               max_model_len=1024, max_num_seqs=16, max_num_batched_tokens=1024,
               enforce_eager=eager, cuda_graph_sizes=[1, 2, 4, 8, 16],
-              enable_expert_parallel=ep)
+              enable_expert_parallel=ep, decode_context_parallel_size=dcp)
     if ep and tp > 1:
         assert llm.engine.comm.ep_a2a is not None, "EP all-to-all did not initialise"
     llm.engine.runner.record_logits = True
@@ -202,6 +216,7 @@ if __name__ == "__main__":
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--model", default="dense")
     ap.add_argument("--ep", action="store_true")
+    ap.add_argument("--dcp", type=int, default=1)
     a = ap.parse_args()
     if a.mode == "ar":
         mode_ar(a.out)
@@ -210,4 +225,4 @@ if __name__ == "__main__":
     elif a.mode == "cand":
         mode_cand(a.out)
     else:
-        mode_llm(a.out, a.tp, a.eager, a.model, a.ep)
+        mode_llm(a.out, a.tp, a.eager, a.model, a.ep, a.dcp)
