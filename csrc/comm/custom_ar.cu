@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(512) fused_ar_kernel(ArParams a) {
   if (kTwoShot) block_barrier(a, 2 + a.parity, epoch);
 }
 
-// Two-shot variant for many rows per rank (large T): one WARP per row and eight rows per
+// Variant for many rows per rank (large T, two-shot or one-shot): one WARP per row and eight rows per
 // block, so every block keeps eight rows' peer loads in flight instead of walking one row at a
 // time with block-wide reductions.  Lane l owns the 8-element vectors l, l+32, ... of the row
 // (VPW of them); peer loads are issued CH vectors x NPEER ranks at a time (16 16-byte loads
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(512) fused_ar_kernel(ArParams a) {
 // rank's output slot.  Same barriers, flags and buffers as fused_ar_kernel.
 constexpr int kWarpRowThreads = 256;
 
-template <int VPW, int NPEER, bool kNorm>
+template <int VPW, int NPEER, bool kNorm, bool kTwoShot>
 __global__ void __launch_bounds__(kWarpRowThreads) fused_ar_warp_kernel(ArParams a) {
   constexpr int CH = 16 / NPEER;  // vectors per round trip (x NPEER loads in flight)
   static_assert(VPW % CH == 0, "vectors per lane must be a multiple of the chunk");
@@ -210,8 +210,9 @@ __global__ void __launch_bounds__(kWarpRowThreads) fused_ar_warp_kernel(ArParams
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kWarps = kWarpRowThreads / 32;
   const int nvec = a.H / 8;
-  const int per = (a.T + NPEER - 1) / NPEER;
-  const int r0 = min(a.T, a.rank * per), r1 = min(a.T, r0 + per);
+  // two-shot: this rank's row chunk, stored to every rank; one-shot: every row, stored locally
+  const int per = kTwoShot ? (a.T + NPEER - 1) / NPEER : a.T;
+  const int r0 = kTwoShot ? min(a.T, a.rank * per) : 0, r1 = min(a.T, r0 + per);
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   for (int row = r0 + blockIdx.x * kWarps + warp; row < r1; row += gridDim.x * kWarps) {
     uint4 packed[VPW];
@@ -286,32 +287,32 @@ __global__ void __launch_bounds__(kWarpRowThreads) fused_ar_warp_kernel(ArParams
         ov = pack8(f);
       }
 #pragma unroll
-      for (int q = 0; q < NPEER; ++q) {
+      for (int q = 0; q < (kTwoShot ? NPEER : 1); ++q) {
         const int dst_rank = (a.rank + q) % NPEER;
         reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out[dst_rank]) +
                                  (size_t)row * a.H)[c] = ov;
       }
     }
   }
-  block_barrier(a, 2 + a.parity, epoch);
+  if (kTwoShot) block_barrier(a, 2 + a.parity, epoch);
 }
 
-template <int VPW, bool kNorm>
+template <int VPW, bool kNorm, bool kTwoShot>
 static void launch_warp_rows(const ArParams& a, cudaStream_t s) {
   if (a.world == 2)
-    fused_ar_warp_kernel<VPW, 2, kNorm><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
+    fused_ar_warp_kernel<VPW, 2, kNorm, kTwoShot><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
   else if (a.world == 4)
-    fused_ar_warp_kernel<VPW, 4, kNorm><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
+    fused_ar_warp_kernel<VPW, 4, kNorm, kTwoShot><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
   else
-    fused_ar_warp_kernel<VPW, 8, kNorm><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
+    fused_ar_warp_kernel<VPW, 8, kNorm, kTwoShot><<<a.blocks, kWarpRowThreads, 0, s>>>(a);
 }
 
-template <bool kNorm>
+template <bool kNorm, bool kTwoShot>
 static void dispatch_warp_rows(const ArParams& a, int nvec, cudaStream_t s) {
   if (nvec <= 32 * 8)
-    launch_warp_rows<8, kNorm>(a, s);
+    launch_warp_rows<8, kNorm, kTwoShot>(a, s);
   else
-    launch_warp_rows<16, kNorm>(a, s);
+    launch_warp_rows<16, kNorm, kTwoShot>(a, s);
 }
 
 template <bool kNorm, bool kTwoShot>
@@ -341,14 +342,21 @@ void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
   const int vpt = (nvec + threads - 1) / threads;
   B200_REQUIRE(vpt <= 8, "custom all-reduce: hidden size too large");
   const bool norm = a.weight != nullptr;
-  const int rows_per_rank = (a.T + a.world - 1) / a.world;
-  if (a.two_shot && rows_per_rank > a.blocks && nvec <= 32 * 16 &&  // rows held in registers
+  const int rows_per_rank = a.two_shot ? (a.T + a.world - 1) / a.world : a.T;
+  if (rows_per_rank > a.blocks && nvec <= 32 * 16 &&  // rows held in registers
       (a.world == 2 || a.world == 4 || a.world == 8)) {
     // several rows per block: warp-per-row kernel keeps them all in flight
-    if (norm)
-      dispatch_warp_rows<true>(a, nvec, s);
-    else
-      dispatch_warp_rows<false>(a, nvec, s);
+    if (a.two_shot) {
+      if (norm)
+        dispatch_warp_rows<true, true>(a, nvec, s);
+      else
+        dispatch_warp_rows<false, true>(a, nvec, s);
+    } else {
+      if (norm)
+        dispatch_warp_rows<true, false>(a, nvec, s);
+      else
+        dispatch_warp_rows<false, false>(a, nvec, s);
+    }
   } else if (a.two_shot) {
     if (norm)
       launch<true, true>(a, threads, vpt, a.blocks, s);
