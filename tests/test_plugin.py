@@ -44,7 +44,7 @@ def test_env_flags_typed(monkeypatch):
     with pytest.raises(ValueError):
         envs.get("B200_AR_ONE_SHOT_MAX_BYTES")
     monkeypatch.delenv("B200_AR_ONE_SHOT_MAX_BYTES")
-    assert envs.snapshot()["B200_AR_ONE_SHOT_MAX_BYTES"] == 256 * 1024
+    assert envs.snapshot()["B200_AR_ONE_SHOT_MAX_BYTES"] == 0  # automatic (world-dependent)
 
 
 def test_native_arch_guard():

@@ -40,8 +40,9 @@ def _bool(s: str) -> bool:
 FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
     EnvFlag("B200_DISABLE_CUSTOM_AR", False, _bool,
             "use NCCL instead of the NVSwitch peer-memory all-reduce kernels"),
-    EnvFlag("B200_AR_ONE_SHOT_MAX_BYTES", 256 * 1024, int,
-            "largest message (bytes per rank) reduced one-shot; larger ones go two-shot"),
+    EnvFlag("B200_AR_ONE_SHOT_MAX_BYTES", 0, int,
+            "largest message (bytes per rank) reduced one-shot; larger ones go two-shot "
+            "(0: 2 MiB of peer reads, i.e. 2 MiB / (world - 1) per rank)"),
     EnvFlag("B200_DISABLE_TUNING", False, _bool, "ignore the measured tuning tables"),
     EnvFlag("B200_WORKER_TERMINATION_TIMEOUT_S", 10.0, float,
             "grace period before follower ranks are SIGTERM'd / SIGKILL'd at shutdown"),

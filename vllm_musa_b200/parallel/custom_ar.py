@@ -28,7 +28,12 @@ from ..ops import _ext
 
 log = logging.getLogger("vllm_musa_b200")
 
-ONE_SHOT_MAX_BYTES = int(os.environ.get("B200_AR_ONE_SHOT_MAX_BYTES", str(256 * 1024)))
+ONE_SHOT_MAX_BYTES = int(os.environ.get("B200_AR_ONE_SHOT_MAX_BYTES", "0"))
+# one-shot (every rank reads every peer's whole message, one barrier) while the peer reads stay
+# under this many bytes; two-shot (reduce-scatter + all-gather, two barriers) beyond.  Measured
+# at TP=2, H=4096 (CUDA-graph replay): 256 tokens 22.2 us one-shot vs 26.4 us two-shot,
+# 64 tokens 16.4 vs 25.2 us; 1024 tokens favour two-shot.
+ONE_SHOT_READ_BYTES = 2 << 20
 # The epilogue reduce-scatter stores 32-byte row pieces to peers, which NVLink moves less
 # efficiently than the two-shot kernel's warp-contiguous loads: measured at TP=2 decode
 # (256 tokens, Llama-3-8B) 9.31 ms/step fused vs 8.42 ms unfused, so it is opt-in.
@@ -98,7 +103,8 @@ class CustomAllReduce:
         return self._staging[self.parity][:T]
 
     def _plan(self, T: int):
-        two_shot = T * self.hidden * 2 > ONE_SHOT_MAX_BYTES and T >= self.world
+        limit = ONE_SHOT_MAX_BYTES or ONE_SHOT_READ_BYTES // max(1, self.world - 1)
+        two_shot = T * self.hidden * 2 > limit and T >= self.world
         rows = (T + self.world - 1) // self.world if two_shot else T
         return two_shot, max(1, min(rows, self.max_blocks))
 
@@ -162,10 +168,15 @@ class CustomAllReduce:
         self.cand_parity ^= 1
         return out
 
+    def local_source_ok(self, T: int) -> bool:
+        """The two-shot kernel's local-source mode (row blocks already scattered into this
+        rank's staging slot by a producer: the GEMM epilogue or the EP return) applies."""
+        return 0 < T <= self.max_tokens and self._plan(T)[0]
+
     def can_fuse_gemm(self, T: int) -> bool:
         """Row-parallel GEMM + all-reduce as one reduce-scatter-in-epilogue GEMM and a local
-        reduce + norm + all-gather kernel: used whenever the two-shot algorithm is (larger T)."""
-        return FUSE_GEMM_RS and 0 < T <= self.max_tokens and self._plan(T)[0]
+        reduce + norm + all-gather kernel (opt-in: B200_FUSE_GEMM_RS=1)."""
+        return FUSE_GEMM_RS and self.local_source_ok(T)
 
     def linear_allreduce_add_rmsnorm(self, x, w, residual, weight, eps):
         """residual <- sum_ranks(x @ w^T) + residual; returns (RMSNorm(residual) * weight,

@@ -73,7 +73,7 @@ class EPAllToAll:
 
     def can_run(self, T: int) -> bool:
         return T >= self.world and (T + self.world - 1) // self.world <= self.cap and \
-            self.ar.can_fuse_gemm(T)
+            self.ar.local_source_ok(T)
 
     def moe_allreduce_add_rmsnorm(self, x, router_ids, router_w, experts, shared_fn, residual,
                                   weight, eps):
