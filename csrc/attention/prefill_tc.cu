@@ -378,6 +378,10 @@ void set_prefill_tc(bool on) { g_prefill_tc = on ? 1 : 0; }
 
 void run_prefill_tc(const PrefillArgs& a, cudaStream_t stream) {
   B200_REQUIRE(a.D == kDim, "tensor-core prefill: head_dim must be 128");
+  if (prefill_tc2_supported(a.D, a.Hq, a.Hkv)) {
+    run_prefill_tc2(a, stream);
+    return;
+  }
   const int box_rows = a.block_size < 64 ? a.block_size : 64;
   const int64_t cache_rows = (int64_t)a.num_blocks * a.Hkv * a.block_size;
   const CUtensorMap tk = make_tma_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kDim,

@@ -238,6 +238,10 @@ struct PrefillArgs {
 // head_dim 128 prefill on tcgen05 (prefill_tc.cu); B200_ATTN_TC=0 selects the mma.sync kernel.
 bool prefill_tc_enabled(int D);
 void set_prefill_tc(bool on);
+// two query heads per CTA (even GQA group; prefill_tc2.cu); B200_ATTN_TC2=0 disables
+bool prefill_tc2_supported(int D, int Hq, int Hkv);
+void set_prefill_tc2(bool on);
+void run_prefill_tc2(const PrefillArgs& a, cudaStream_t stream);
 void run_prefill_tc(const PrefillArgs& a, cudaStream_t stream);
 int decode_num_splits(int B, int Hkv, int max_seq_len);
 void run_decode(const DecodeArgs& a, cudaStream_t s);

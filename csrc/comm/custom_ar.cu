@@ -342,8 +342,10 @@ void run_fused_allreduce(const ArParams& a, cudaStream_t s) {
   const int vpt = (nvec + threads - 1) / threads;
   B200_REQUIRE(vpt <= 8, "custom all-reduce: hidden size too large");
   const bool norm = a.weight != nullptr;
+  // warp-per-row kernel once blocks would walk several rows (one-shot: measured 25.4 us vs 22.2
+  // us for the block kernel at 256 rows, TP=2, so it takes over beyond two rows per block)
   const int rows_per_rank = a.two_shot ? (a.T + a.world - 1) / a.world : a.T;
-  if (rows_per_rank > a.blocks && nvec <= 32 * 16 &&  // rows held in registers
+  if (rows_per_rank > (a.two_shot ? 1 : 2) * a.blocks && nvec <= 32 * 16 &&  // rows in registers
       (a.world == 2 || a.world == 4 || a.world == 8)) {
     // several rows per block: warp-per-row kernel keeps them all in flight
     if (a.two_shot) {

@@ -1195,6 +1195,8 @@ void register_runtime(pybind11::module_& m);  // csrc/runtime/bindings.cpp
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vllm_musa_b200 native extension (sm_100a kernels + host runtime)";
   m.def("gemm_plan", &gemm_plan, "automatic (bn, splits, workspace_floats) for a bf16 GEMM");
+  m.def("set_prefill_tc2", [](bool on) { b200::attn::set_prefill_tc2(on); },
+        "allow (true) the two-heads-per-CTA tcgen05 prefill kernel for even GQA groups");
   m.def("set_prefill_tc", [](bool on) { b200::attn::set_prefill_tc(on); },
         "select the tcgen05 (true) or mma.sync (false) prefill attention kernel for head_dim 128");
   m.def("gemm_fp8_plan", &gemm_fp8_plan, "automatic (splits, workspace_floats, counters) for fp8");

@@ -243,11 +243,11 @@ def test_paged_prefill_chunked(D, Hq, Hkv, bs, window):
 
 @pytest.mark.parametrize("bs,window,qscale", [(64, 0, 1.0), (16, 0, 4.0), (128, 0, 8.0),
                                                (64, 300, 4.0)])
-@pytest.mark.parametrize("tc", [True, False])
+@pytest.mark.parametrize("tc", ["tc2", "tc", "sync"])
 def test_paged_prefill_long(bs, window, qscale, tc):
-    """Long prompts and cached contexts on both head_dim-128 prefill kernels (tcgen05 with TMEM
-    S/P/O, and the mma.sync one): several 128-key blocks, partial tiles, large logits (lazy
-    rescaling of O in TMEM), sliding window."""
+    """Long prompts and cached contexts on the head_dim-128 prefill kernels (tcgen05 with two
+    heads per CTA, tcgen05 with one head, and the mma.sync one): several 128-key blocks, partial
+    tiles, large logits (lazy rescaling of O in TMEM), sliding window."""
     D, Hq, Hkv = 128, 16, 4
     reqs = [(0, 1024), (300, 700), (2000, 257), (0, 129), (127, 1)]
     R = len(reqs)
@@ -262,13 +262,15 @@ def test_paged_prefill_long(bs, window, qscale, tc):
     scale = 1.0 / math.sqrt(D)
     ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale, window)
     mod = _ext.require()
-    mod.set_prefill_tc(tc)
+    mod.set_prefill_tc(tc != "sync")
+    mod.set_prefill_tc2(tc == "tc2")
     try:
         out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale,
                                 window)
         torch.cuda.synchronize()
     finally:
         mod.set_prefill_tc(True)
+        mod.set_prefill_tc2(True)
     _ext.check_device_errors()
     torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
 
