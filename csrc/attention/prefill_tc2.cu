@@ -15,8 +15,9 @@
 // TMEM (512 columns): O0 [0,128) | O1 [128,256) | S0/P0 [256,384) | S1/P1 [384,512).  P_h is
 // written over S_h, so S_h(j+1) is issued only after PV_h(j) completed (the MMA thread waits on
 // that head's o_done phase); the other head's work keeps the tensor core busy meanwhile.
-// Softmax: two passes over 32-column TMEM chunks (row max, then p = 2^(s*scale - m) with one
-// FMA and one ex2, P packed to bf16 and stored over consumed S columns); O rescaled in TMEM
+// Softmax: the S row read with four TMEM loads and one wait, row max in 8 independent chains,
+// p = 2^(s*scale - m) with one FMA and one ex2, P packed to bf16 and stored over the S columns
+// in 16-column pieces; O rescaled in TMEM
 // only when a row max grows by more than 2^8.  Every mbarrier is waited phase by phase (a
 // parity wait is exact only while the barrier is at most one phase ahead of the waiter) and
 // every wait is bounded (error word + early exit); the producer waits for its own copies in
@@ -256,25 +257,29 @@ __global__ void __launch_bounds__(kThreads2, 1)
       tc::fence_after_sync();
       const int kv0 = (first_blk + j) * kBK;
       const bool masked = kv0 + kBK - 1 > my_pos || p.window > 0;  // diagonal / window blocks
-      // pass 1: row max of the raw scores (8 independent chains)
+      // the whole S row in registers: four TMEM loads, one wait
+      uint32_t sv[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld_32x32b_x32(s_col + 32 * c, sv[c]);
+      tc::tmem_ld_wait();
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int kv = kv0 + 32 * c + i;
+            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window))
+              sv[c][i] = __float_as_uint(-INFINITY);
+          }
+      }
+      // row max of the raw scores (8 independent chains)
       float mx8[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(s_col + 32 * c, sv);
-        tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(sv[i]);
-          if (masked) {
-            const int kv = kv0 + 32 * c + i;
-            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window)) v = -INFINITY;
-          }
-          mx8[i & 7] = fmaxf(mx8[i & 7], v);
-        }
-      }
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sv[c][i]));
 #pragma unroll
       for (int k = 0; k < 4; ++k) mx8[k] = fmaxf(mx8[k], mx8[k + 4]);
       const float mx = fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])) * p.scale_log2;
@@ -289,27 +294,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
         m_ref = m_new;
         l *= factor;
       }
-      // pass 2: p = 2^(s * scale - m); P chunk c (16 packed columns) over consumed S columns
+      // p = 2^(s * scale - m) (one FMA + one ex2 per score); P chunk c (16 packed columns)
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
       float sum8[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(s_col + 32 * c, sv);
-        tc::tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          float s0 = __uint_as_float(sv[i]), s1 = __uint_as_float(sv[i + 1]);
-          if (masked) {
-            const int kv = kv0 + 32 * c + i;
-            if (kv > my_pos || (p.window > 0 && kv <= my_pos - p.window)) s0 = -INFINITY;
-            if (kv + 1 > my_pos || (p.window > 0 && kv + 1 <= my_pos - p.window)) s1 = -INFINITY;
-          }
-          const float a = ex2_approx(fmaf(s0, p.scale_log2, neg_m));
-          const float e = ex2_approx(fmaf(s1, p.scale_log2, neg_m));
+          const float a = ex2_approx(fmaf(__uint_as_float(sv[c][i]), p.scale_log2, neg_m));
+          const float e = ex2_approx(fmaf(__uint_as_float(sv[c][i + 1]), p.scale_log2, neg_m));
           sum8[(i >> 1) & 7] += a + e;
           pk[i / 2] = pack_bf16x2(a, e);  // low half = even key
         }
