@@ -231,7 +231,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       bool ok = mbar_wait(q_full, 0, p.err);
       if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
       for (int j = 0; j < nblk && ok; ++j) {
-        // S_h(j+1) overwrites P_h(j): it follows that head's PV_h(j) completion
+        // S_h(j+1) overwrites P_h(j): it follows that head's PV_h(j) completion.  Head 0's next
+        // S is issued before head 1's PV so each head's softmax chain stays short (measured
+        // 159.7 us vs 176.7 us with both PVs first, 8 x 1024 tokens, 32 / 8 heads)
         ok = issue_pv(0, j);
         if (ok && j + 1 < nblk) ok = mbar_wait(&o_done[0], j & 1, p.err) && issue_s(0, j + 1);
         if (ok) ok = issue_pv(1, j);
