@@ -172,6 +172,18 @@ void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, 
                          cudaStream_t s);
 }  // namespace act
 
+// ------------------------------------------------------------------------------- W4AFP8 MoE
+namespace w4a8 {
+// packed int4 [E, N, K/2] x bf16 scales [E, N, K/128] -> bf16 [E * N, K]; experts whose padded
+// row range (offsets[e], offsets[e + 1]) is empty are skipped (offsets may be null: expand all).
+void run_w4_dequant(void* out, const void* packed, const void* scales, const int32_t* offsets,
+                    int E, int N, int K, cudaStream_t s);
+// per-row e4m3 quantise -> dequantise round trip (optionally of SwiGLU(+clamp) of [gate | up]);
+// rows at or past num_tiles[0] * 128 are skipped when num_tiles is given.
+void run_row_fp8_qdq(void* out, const void* x, int64_t ld_x, int rows, int C, bool swiglu,
+                     float limit, const int32_t* num_tiles, cudaStream_t s);
+}  // namespace w4a8
+
 // ------------------------------------------------------------------------------- rope + kv
 namespace rope {
 // Multimodal RoPE: mode 0 off, 1 sectioned (s0 | s1 | s2 frequencies), 2 interleaved;

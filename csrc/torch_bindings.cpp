@@ -825,6 +825,49 @@ void gemm_grouped_bf16(const Tensor& A, const Tensor& B, Tensor& C, const Tensor
   guarded([&] { b200::gemm::run_grouped_bf16(a, stream_of(A)); });
 }
 
+void w4_dequant(Tensor& out, const Tensor& packed, const Tensor& scales,
+                const c10::optional<Tensor>& offsets) {
+  CHECK_CUDA(packed);
+  TORCH_CHECK(packed.dim() == 3 && packed.is_contiguous() && packed.scalar_type() == at::kChar,
+              "w4_dequant: packed int4 [E, N, K/2] int8");
+  const int E = packed.size(0), N = packed.size(1), K = packed.size(2) * 2;
+  TORCH_CHECK(K % 128 == 0, "w4_dequant: K must be a multiple of 128");
+  TORCH_CHECK(scales.is_contiguous() && scales.scalar_type() == at::kBFloat16 &&
+                  scales.numel() == (int64_t)E * N * (K / 128),
+              "w4_dequant: bf16 scales [E, N, K/128]");
+  CHECK_BF16(out);
+  TORCH_CHECK(out.is_contiguous() && out.numel() == (int64_t)E * N * K, "w4_dequant: out [E*N, K]");
+  if (offsets.has_value())
+    TORCH_CHECK(offsets->scalar_type() == at::kInt && offsets->numel() >= E + 1,
+                "w4_dequant: int32 offsets [E + 1]");
+  const c10::cuda::CUDAGuard g(packed.device());
+  guarded([&] {
+    b200::w4a8::run_w4_dequant(out.data_ptr(), packed.data_ptr(), scales.data_ptr(),
+                               offsets.has_value() ? offsets->data_ptr<int32_t>() : nullptr, E, N,
+                               K, stream_of(packed));
+  });
+}
+
+void row_fp8_qdq(Tensor& out, const Tensor& x, bool swiglu, double limit,
+                 const c10::optional<Tensor>& num_tiles) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  CHECK_BF16(out);
+  TORCH_CHECK(out.is_contiguous(), "row_fp8_qdq: contiguous out");
+  const int C = out.size(1);
+  TORCH_CHECK(C % 8 == 0 && x.size(1) == (swiglu ? 2 * C : C) && x.size(0) == out.size(0),
+              "row_fp8_qdq: shapes");
+  TORCH_CHECK((int64_t)C * 4 <= 200 * 1024, "row_fp8_qdq: row too long");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::w4a8::run_row_fp8_qdq(out.data_ptr(), x.data_ptr(), x.stride(0), x.size(0), C, swiglu,
+                                (float)limit,
+                                num_tiles.has_value() ? num_tiles->data_ptr<int32_t>() : nullptr,
+                                stream_of(x));
+  });
+}
+
 void topk_softmax(const Tensor& logits, Tensor& ids, Tensor& w, bool renorm) {
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "router logits fp32");
@@ -1141,6 +1184,8 @@ TORCH_LIBRARY(b200, m) {
       "moe_align(Tensor ids, int num_experts, Tensor(a!) sorted_ids, Tensor(b!) tile_expert, "
       "Tensor(c!) offsets, Tensor(d!) pos, Tensor(e!) num_tiles, int expert_offset=0) -> ()");
   m.def("moe_gather(Tensor x, Tensor sorted_ids, Tensor num_tiles, int k, Tensor(a!) out) -> ()");
+  m.def("w4_dequant(Tensor(a!) out, Tensor packed, Tensor scales, Tensor? offsets) -> ()");
+  m.def("row_fp8_qdq(Tensor(a!) out, Tensor x, bool swiglu, float limit, Tensor? num_tiles) -> ()");
   m.def("moe_combine(Tensor y, Tensor pos, Tensor w, Tensor? shared, Tensor(a!) out, "
       "Tensor? shared_gate=None) -> ()");
   m.def(
@@ -1183,6 +1228,8 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("indexer_scores", &indexer_scores);
   m.impl("mla_topk", &mla_topk);
   m.impl("moe_gather", &moe_gather);
+  m.impl("w4_dequant", &w4_dequant);
+  m.impl("row_fp8_qdq", &row_fp8_qdq);
   m.impl("moe_combine", &moe_combine);
   m.impl("causal_conv1d", &causal_conv1d);
   m.impl("gdn_recurrent", &gdn_recurrent);

@@ -19,6 +19,15 @@ class Block(torch.nn.Module):
         return y, r, q, s
 
 
+class NormQuant(torch.nn.Module):
+    """Input norm feeding an fp8 GEMM, then a residual norm feeding another."""
+    def forward(self, x, residual, w):
+        q0, s0 = ops.group_quant_fp8(ops.rms_norm(x, w, 1e-6))
+        y, r = ops.fused_add_rms_norm(x, residual, w, 1e-6)
+        q1, s1 = ops.group_quant_fp8(y)
+        return q0, s0, q1, s1, r * 2
+
+
 class Shared(torch.nn.Module):
     def forward(self, x, residual, w):
         a = ops.all_reduce(x)
@@ -47,7 +56,36 @@ def test_fusions_rewrite_and_preserve_values():
     torch.testing.assert_close(out[1], ref[1])
     torch.testing.assert_close(out[2].float(), ref[2].float())
     torch.testing.assert_close(out[3], ref[3])
-    assert pm.stats == {"allreduce_rmsnorm": 1, "silu_mul_quant": 1}
+    assert pm.stats == {"allreduce_rmsnorm": 1, "silu_mul_quant": 1, "rms_norm_quant": 0}
+
+
+def test_rms_norm_quant_fusion():
+    g = torch.Generator().manual_seed(1)
+    x, res = torch.randn(6, 256, generator=g), torch.randn(6, 256, generator=g)
+    w = torch.rand(256, generator=g) + 0.5
+    gm = fx.symbolic_trace(NormQuant())
+    ref = gm(x, res, w)
+    pm = B200PassManager()
+    assert pm(gm.graph) == 2
+    gm.graph.lint()
+    gm.recompile()
+    names = " ".join(_names(gm))
+    assert "b200fx.rms_norm_quant_fp8" in names and "add_rms_norm_quant_fp8" in names
+    assert "group_quant_fp8" not in names and "b200fx.fused_add_rms_norm" not in names
+    out = gm(x, res, w)
+    for o, r in zip(out, ref):
+        torch.testing.assert_close(o.float(), r.float())
+    assert pm.stats["rms_norm_quant"] == 2
+
+
+def test_rms_norm_quant_not_fused_when_norm_output_shared():
+    class M(torch.nn.Module):
+        def forward(self, x, residual, w):
+            y, r = ops.fused_add_rms_norm(x, residual, w, 1e-6)
+            q, s = ops.group_quant_fp8(y)
+            return q, s, y + r   # the bf16 normalised row is still needed
+    gm = fx.symbolic_trace(M())
+    assert B200PassManager([P.RMSNormQuantFusionPass()])(gm.graph) == 0
 
 
 def test_no_fusion_when_intermediate_is_shared():
@@ -65,4 +103,4 @@ def test_vllm_pass_manager_hook():
     assert issubclass(B200PostGradPassManager, pm_mod.PostGradPassManager)
     assert B200Platform.get_pass_manager_cls().endswith("B200PostGradPassManager")
     ps = b200_passes()
-    assert len(ps) == 2 and all(p.is_applicable_for_range(None) for p in ps)
+    assert len(ps) == 3 and all(p.is_applicable_for_range(None) for p in ps)

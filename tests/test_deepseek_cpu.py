@@ -41,3 +41,30 @@ def test_tiny_deepseek_matches_reference(sparse, q_lora, budget):
     for i, p in enumerate(prompts):
         toks, _ = ref.greedy(p, 4)
         assert outs[i].outputs[0].token_ids == toks, f"request {i} diverged"
+
+
+def test_tiny_deepseek_w4afp8_experts():
+    """W4AFP8: the engine keeps routed experts packed int4 and quantises activations per token;
+    its first-step logits match the fp32 reference run on the int4-rounded expert weights."""
+    from vllm_musa_b200.ops.w4afp8 import dequant_w4, quantize_w4
+    cfg = tiny_ds(False, 0)
+    cfg.moe_intermediate_size = 128  # int4 groups of 128 along every expert K
+    cfg.quant = "w4afp8"
+    prompt = _prompts(1, 40, seed=5)[0]
+    llm = LLM(cfg, device="cpu", block_size=16, seed=0, num_gpu_blocks=64, max_model_len=128,
+              max_num_seqs=4, max_num_batched_tokens=256)
+    L = llm.engine.runner.model.layers[1]
+    assert L.w4 is not None and L.w4[0].dtype == torch.int8 and L.experts_gu is None
+    llm.engine.runner.record_logits = True
+    llm.generate([prompt], SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True))
+    got = llm.engine.runner.logits_log[0][0]
+    ref_cfg = tiny_ds(False, 0)
+    ref_cfg.moe_intermediate_size = 128
+    W = dict(dummy_weights(ref_cfg, seed=0, std=0.02))
+    for k in list(W):
+        if ".experts." in k:
+            q, s = quantize_w4(W[k][None])
+            W[k] = dequant_w4(q, s)[0]
+    want = DeepseekReferenceDecoder(ref_cfg, W).logits(prompt)[-1]
+    err = (got - want).abs().max() / want.abs().max()
+    assert 0 < err < 0.02, float(err)  # only the per-token e4m3 activation rounding differs

@@ -34,7 +34,7 @@ def test_tiny_deepseek_engine_graph_vs_eager():
     assert outs[True] == outs[False]
 
 
-@pytest.mark.parametrize("quant", [None, "fp8_block"])
+@pytest.mark.parametrize("quant", [None, "fp8_block", "w4afp8"])
 def test_tiny_deepseek_logits_track_reference(quant):
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.models.reference import DeepseekReferenceDecoder

@@ -5,6 +5,10 @@ them with the fused ops of this package.
   becomes one ``allreduce_add_rms_norm`` (the NVSwitch all-reduce + residual + RMSNorm kernel).
 * ``SiluMulQuantFusionPass``      silu_and_mul(x) -> group_quant_fp8(y) becomes one
   ``silu_mul_fp8_quant`` (SwiGLU + 1x128 e4m3 quantisation in one kernel).
+* ``RMSNormQuantFusionPass``      rms_norm(x, w, eps) -> group_quant_fp8(y) becomes one
+  ``rms_norm_quant_fp8``, and fused_add_rms_norm(x, r, w, eps)[0] -> group_quant_fp8 one
+  ``add_rms_norm_quant_fp8`` (residual add + RMSNorm + 1x128 e4m3 quantisation in one pass
+  over the row; the updated residual stays an output).
 
 Ops are matched by qualified name, so graphs traced from this package's ``torch.ops.b200fx.*``
 ops and graphs holding vLLM's equivalents (``vllm.all_reduce``, ``_C.fused_add_rms_norm``,
@@ -14,11 +18,13 @@ custom post-grad pass hook expect).
 
 Reference counterparts: vllm_musa/compilation/passes/pass_manager.py:59-83 (pass manager),
 vllm_musa/_inductor/musa_allreduce_rms_fusion.py:103-844 (AR + RMSNorm fusion),
-compilation/passes/silu_deepgemm_fusion.py:19-85 (SiLU + quant fusion).
+vllm_musa/compilation/passes/silu_deepgemm_fusion.py:19-85 (SiLU + quant fusion),
+vllm_musa/compilation/passes/rms_deepgemm_fusion.py:18-91 (residual RMSNorm + quant fusion).
 """
 from __future__ import annotations
 
 import hashlib
+import operator
 from typing import Callable, Iterable, List, Optional
 
 import torch
@@ -34,6 +40,10 @@ _LIB.define("allreduce_add_rms_norm(Tensor x, Tensor residual, Tensor w, float e
 _LIB.define("silu_and_mul(Tensor x) -> Tensor")
 _LIB.define("group_quant_fp8(Tensor x) -> (Tensor, Tensor)")
 _LIB.define("silu_mul_fp8_quant(Tensor x) -> (Tensor, Tensor)")
+_LIB.define("rms_norm(Tensor x, Tensor w, float eps) -> Tensor")
+_LIB.define("rms_norm_quant_fp8(Tensor x, Tensor w, float eps) -> (Tensor, Tensor)")
+_LIB.define("add_rms_norm_quant_fp8(Tensor x, Tensor residual, Tensor w, float eps) "
+            "-> (Tensor, Tensor, Tensor)")
 
 _COMM: Optional[object] = None  # TP communicator used by the fused all-reduce op
 
@@ -77,7 +87,27 @@ def _silu_mul_quant(x):
     return silu_mul_fp8_quant(x)
 
 
+def _rms_norm(x, w, eps):
+    from .. import ops
+    return ops.rms_norm(x, w, eps)
+
+
+def _rms_norm_quant(x, w, eps):
+    from .. import ops
+    q, sc, _ = ops.rms_norm_quant_fp8(x, w, eps)
+    return q, sc
+
+
+def _add_rms_norm_quant(x, residual, w, eps):
+    from .. import ops
+    r = residual.clone()
+    q, sc, _ = ops.rms_norm_quant_fp8(x, w, eps, residual=r)
+    return q, sc, r
+
+
 for _name, _fn in (("all_reduce", _all_reduce), ("fused_add_rms_norm", _fused_add_rms_norm),
+                   ("rms_norm", _rms_norm), ("rms_norm_quant_fp8", _rms_norm_quant),
+                   ("add_rms_norm_quant_fp8", _add_rms_norm_quant),
                    ("allreduce_add_rms_norm", _allreduce_add_rms_norm),
                    ("silu_and_mul", _silu_and_mul), ("group_quant_fp8", _group_quant),
                    ("silu_mul_fp8_quant", _silu_mul_quant)):
@@ -90,6 +120,7 @@ ALL_REDUCE = ("b200fx.all_reduce", "vllm.all_reduce")
 ADD_RMS = ("b200fx.fused_add_rms_norm", "_C.fused_add_rms_norm")
 SILU_MUL = ("b200fx.silu_and_mul", "_C.silu_and_mul")
 GROUP_QUANT = ("b200fx.group_quant_fp8", "_C.per_token_group_fp8_quant")
+RMS_NORM = ("b200fx.rms_norm",)
 
 
 def _qual(target) -> str:
@@ -160,6 +191,61 @@ class SiluMulQuantFusionPass(_Pass):
         return n
 
 
+class RMSNormQuantFusionPass(_Pass):
+    """group_quant_fp8(rms_norm(x, w, eps)) and group_quant_fp8(fused_add_rms_norm(x, r, w,
+    eps)[0]), with the normalised row used only by the quantiser (an fp8 GEMM's input)."""
+    name = "rms_norm_quant"
+
+    def __call__(self, graph: fx.Graph) -> int:
+        n = 0
+        for node in list(graph.nodes):
+            if not _is(node, GROUP_QUANT):
+                continue
+            src = node.args[0]
+            if not isinstance(src, fx.Node) or len(src.users) != 1:
+                continue
+            if _is(src, RMS_NORM):
+                with graph.inserting_before(node):
+                    fused = graph.call_function(torch.ops.b200fx.rms_norm_quant_fp8.default,
+                                                tuple(src.args[:3]))
+                node.replace_all_uses_with(fused)
+                graph.erase_node(node)
+                graph.erase_node(src)
+                n += 1
+            elif self._add_norm_output(src):
+                self._rewrite_add(graph, node, src)
+                n += 1
+        return n
+
+    @staticmethod
+    def _add_norm_output(g: fx.Node) -> bool:
+        """``g`` is element 0 (the normalised row) of a fused_add_rms_norm whose other users
+        are getitem(1) nodes only (the updated residual)."""
+        if g.target is not operator.getitem or g.args[1] != 0:
+            return False
+        fan = g.args[0]
+        if not isinstance(fan, fx.Node) or not _is(fan, ADD_RMS):
+            return False
+        return all(u.target is operator.getitem and u.args[1] in (0, 1) for u in fan.users)
+
+    @staticmethod
+    def _rewrite_add(graph: fx.Graph, quant: fx.Node, g0: fx.Node) -> None:
+        fan = g0.args[0]
+        with graph.inserting_after(fan):
+            fused = graph.call_function(torch.ops.b200fx.add_rms_norm_quant_fp8.default,
+                                        tuple(fan.args[:4]))
+        with graph.inserting_after(fused):
+            res = graph.call_function(operator.getitem, (fused, 2))
+        # (q, scales) keep their tuple positions 0 and 1; the residual moves to position 2.
+        quant.replace_all_uses_with(fused)
+        graph.erase_node(quant)
+        graph.erase_node(g0)
+        for u in list(fan.users):
+            u.replace_all_uses_with(res)
+            graph.erase_node(u)
+        graph.erase_node(fan)
+
+
 class B200PassManager(_Pass):
     """Runs the fusion passes in order; ``configure`` picks them from a config-like object
     (attributes ``fuse_allreduce_rms`` / ``fuse_act_quant``, default on)."""
@@ -167,7 +253,8 @@ class B200PassManager(_Pass):
 
     def __init__(self, passes: Optional[List[Callable]] = None):
         self.passes = passes if passes is not None else [AllReduceRMSNormFusionPass(),
-                                                         SiluMulQuantFusionPass()]
+                                                         SiluMulQuantFusionPass(),
+                                                         RMSNormQuantFusionPass()]
         self.stats = {}
 
     def configure(self, config=None) -> "B200PassManager":
@@ -176,6 +263,8 @@ class B200PassManager(_Pass):
             ps.append(AllReduceRMSNormFusionPass())
         if getattr(config, "fuse_act_quant", True):
             ps.append(SiluMulQuantFusionPass())
+        if getattr(config, "fuse_norm_quant", True):
+            ps.append(RMSNormQuantFusionPass())
         self.passes = ps
         return self
 

@@ -5,7 +5,7 @@ from __future__ import annotations
 
 from vllm.compilation.passes.pass_manager import PostGradPassManager
 
-from .passes import AllReduceRMSNormFusionPass, SiluMulQuantFusionPass
+from .passes import AllReduceRMSNormFusionPass, RMSNormQuantFusionPass, SiluMulQuantFusionPass
 
 
 class _Wrapped:
@@ -25,7 +25,8 @@ class _Wrapped:
 
 
 def b200_passes() -> list:
-    return [_Wrapped(AllReduceRMSNormFusionPass()), _Wrapped(SiluMulQuantFusionPass())]
+    return [_Wrapped(AllReduceRMSNormFusionPass()), _Wrapped(SiluMulQuantFusionPass()),
+            _Wrapped(RMSNormQuantFusionPass())]
 
 
 class B200PostGradPassManager(PostGradPassManager):

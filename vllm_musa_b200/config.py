@@ -56,7 +56,7 @@ class ModelConfig:
     index_head_dim: int = 0
     index_topk: int = 0
     num_nextn_predict_layers: int = 0
-    quant: Optional[str] = None  # None | "fp8_block"
+    quant: Optional[str] = None  # None | "fp8_block" | "w4afp8" (int4 experts, fp8 linears)
     # hybrid linear attention (Qwen3-Next)
     full_attention_interval: int = 0
     linear_num_key_heads: int = 0
@@ -168,6 +168,14 @@ class ModelConfig:
         qc = hf.get("quantization_config") or {}
         if qc.get("quant_method") == "fp8" and qc.get("weight_block_size"):
             c.quant = "fp8_block"
+        elif qc.get("quant_method") == "w4afp8":
+            # packed int4 routed experts (group 128, bf16 scales) beside block-FP8 linears;
+            # vllm_musa/model_executor/layers/quantization/w4afp8.py:37-44 sets the same limits
+            if int(qc.get("moe_group_size", 128)) != 128:
+                raise ValueError("W4AFP8 requires moe_group_size=128")
+            if qc.get("activation_scheme", "dynamic") != "dynamic":
+                raise ValueError("W4AFP8 requires dynamic FP8 activations")
+            c.quant = "w4afp8"
         return c
 
 

@@ -66,7 +66,7 @@ class Lin:
 class _Layer:
     __slots__ = ("ln1", "ln2", "w_a", "q_a_norm", "kv_a_norm", "w_qb", "w_kb", "w_vb", "o", "idx_ln_w",
                  "idx_ln_b", "gu", "down", "router_w", "router_bias", "experts_gu", "experts_gu_s",
-                 "experts_down", "experts_down_s", "shared_gu", "shared_down",
+                 "experts_down", "experts_down_s", "shared_gu", "shared_down", "w4",
                  # multi-token-prediction layer only
                  "enorm", "hnorm", "eh_proj", "head_norm", "head")
 
@@ -100,7 +100,9 @@ class DeepseekV2ForCausalLM:
         if self.kv_lora != 512 or self.rope != 64 or self.nope != 128:
             raise ValueError("MLA kernels are built for kv_lora 512, rope 64, nope 128")
         # block-FP8 GEMMs run on the GPU in bf16 models; other runs (CPU fp32) dequantise
-        self.fp8 = cfg.quant == "fp8_block" and cfg.dtype == torch.bfloat16
+        self.fp8 = cfg.quant in ("fp8_block", "w4afp8") and cfg.dtype == torch.bfloat16
+        # W4AFP8: routed experts stay packed int4 (group-128 bf16 scales) on every device
+        self.w4 = cfg.quant == "w4afp8"
         self.sparse = cfg.index_topk > 0
         self.idx_heads, self.idx_dim = cfg.index_n_heads, cfg.index_head_dim
         # fused A-projection row layout (every part padded to 128 rows)
@@ -231,8 +233,8 @@ class DeepseekV2ForCausalLM:
         return True
 
     def _needs_scale(self, st, key):
-        return key.endswith(".weight") and st[key].dtype == torch.float8_e4m3fn and \
-            key[:-len("weight")] + "weight_scale_inv" not in st
+        return key.endswith(".weight") and st[key].dtype in (torch.float8_e4m3fn, torch.int8) \
+            and key[:-len("weight")] + "weight_scale_inv" not in st
 
     def _try_finalize(self, i):
         st = self._staging[i]
@@ -289,6 +291,11 @@ class DeepseekV2ForCausalLM:
         L.router_w = self._to(st["mlp.gate.weight"])
         b = st.get("mlp.gate.e_score_correction_bias")
         L.router_bias = b.float().to(self.device).contiguous() if b is not None else None
+        if self.w4:
+            self._finalize_experts_w4(L, st)
+            if self.cfg.shared_expert_intermediate_size:
+                L.shared_gu, L.shared_down = self._swiglu(st, "mlp.shared_experts", r, t)
+            return
         gus, gss, dws, dss = [], [], [], []
         for e in range(self.e0, self.e0 + self.E_local):
             p = f"mlp.experts.{e}."
@@ -320,6 +327,38 @@ class DeepseekV2ForCausalLM:
             L.experts_down = self._to(torch.cat(dws))
         if self.cfg.shared_expert_intermediate_size:
             L.shared_gu, L.shared_down = self._swiglu(st, "mlp.shared_experts", r, t)
+
+    def _finalize_experts_w4(self, L, st):
+        """Routed experts as packed int4: w13 [E, 2I, H/2] ([gate ; up] rows), w2 [E, H, I/2],
+        bf16 scales per (row, 128 columns).  bf16 checkpoint experts (random-init models) are
+        quantised here; TP shards the intermediate, which must stay 128-aligned."""
+        from ..ops.w4afp8 import quantize_w4
+        r, t = self.rank, self.tp
+
+        def w4(st_name):
+            w, s = self._raw(st, st_name)
+            if w.dtype != torch.int8:
+                w, s = quantize_w4(self._deq(w, s))
+            return w, s.to(torch.bfloat16)
+
+        w13, s13, w2, s2 = [], [], [], []
+        for e in range(self.e0, self.e0 + self.E_local):
+            p = f"mlp.experts.{e}."
+            (g, gs), (u, us), (d, ds) = w4(p + "gate_proj"), w4(p + "up_proj"), w4(p + "down_proj")
+            if not self.ep:
+                I = g.shape[0] // t
+                if I % 128:
+                    raise ValueError("W4AFP8 needs a 128-aligned intermediate size per TP rank; "
+                                     "use expert parallelism")
+                g, gs, u, us = (g[r * I:(r + 1) * I], gs[r * I:(r + 1) * I],
+                                u[r * I:(r + 1) * I], us[r * I:(r + 1) * I])
+                d, ds = d[:, r * I // 2:(r + 1) * I // 2], ds[:, r * I // 128:(r + 1) * I // 128]
+            w13.append(torch.cat([g, u]))
+            s13.append(torch.cat([gs, us]))
+            w2.append(d)
+            s2.append(ds)
+        dev = self.device
+        L.w4 = tuple(torch.stack(v).to(dev).contiguous() for v in (w13, s13, w2, s2))
 
     def _swiglu(self, st, prefix, r, t):
         """Dense SwiGLU (TP-sharded intermediate): fp8 -> [gate ; up] rows for the
@@ -597,6 +636,11 @@ class DeepseekV2ForCausalLM:
                                       renorm=cfg.norm_topk_prob, scale=cfg.routed_scaling_factor)
         shared = self._swiglu_fwd(L.shared_gu, L.shared_down, x) if L.shared_gu is not None else None
         out = self.comm.out_buffer(T)
+        if self.w4:
+            from ..ops.w4afp8 import w4afp8_moe
+            w13, s13, w2, s2 = L.w4
+            return w4afp8_moe(x, w13, w2, s13, s2, w, ids, out=out, expert_offset=self.e0,
+                              shared=shared)
         if self.fp8:
             return moe_ops.fused_moe_fp8(x, L.experts_gu, L.experts_gu_s, L.experts_down,
                                          L.experts_down_s, ids, w, self.E_local, shared, out=out,
