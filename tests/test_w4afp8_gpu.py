@@ -3,11 +3,17 @@ whole op (row e4m3 round trips, tcgen05 grouped GEMMs, combine) against the fp32
 import pytest
 import torch
 
+from vllm_musa_b200.ops import _ext
 from vllm_musa_b200.ops import w4afp8 as W
 
 from test_w4afp8_cpu import case
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _loaded():
+    _ext.require()  # registers torch.ops.b200 (fails loudly without the CUDA extension)
 
 
 def test_w4_dequant_kernel_skips_idle_experts():
