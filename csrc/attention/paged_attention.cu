@@ -57,6 +57,7 @@ struct DecodeParams {
   float* ws_o;    // [B, Hq, splits, D]
   float* ws_lse;  // [B, Hq, splits]
   int* err;
+  const float* sinks;  // [Hq] natural-log sink logits or null
 };
 
 struct PrefillParams {
@@ -70,7 +71,14 @@ struct PrefillParams {
   int R, max_tiles, Hq, Hkv, block_size, window;
   float scale_log2;
   int* err;
+  const float* sinks;  // [Hq] natural-log sink logits or null
+  bool causal;
 };
+
+// A sink is a softmax column with no value: it only adds 2^(sink * log2 e - m) to the row sum.
+B200_DEVICE float sink_term(const float* sinks, int head, float m_log2) {
+  return sinks == nullptr ? 0.f : exp2f(sinks[head] * kLog2e - m_log2);
+}
 
 B200_DEVICE void named_barrier_compute() {
   asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
@@ -312,7 +320,8 @@ __global__ void __launch_bounds__(kThreads)
       acc += f * sm_o[(w * 16 + row) * D + d];
     }
     const int head = h * G + row;
-    const float out = L > 0.f ? acc / L : 0.f;
+    const float Ls = (p.num_splits == 1 && L > 0.f) ? L + sink_term(p.sinks, head, Mu) : L;
+    const float out = L > 0.f ? acc / Ls : 0.f;
     if (p.num_splits == 1) {
       p.o[b * p.ld_o + (int64_t)head * D + d] = f2bf(out);
     } else {
@@ -326,7 +335,7 @@ __global__ void __launch_bounds__(kThreads)
 // Merge split-KV partials: O = sum_s 2^(lse_s - M) O_s / sum_s 2^(lse_s - M)
 __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
                                     __nv_bfloat16* __restrict__ o, int64_t ld_o, int Hq, int S,
-                                    int D) {
+                                    int D, const float* __restrict__ sinks) {
   const int b = blockIdx.x, head = blockIdx.y;
   const int64_t base = ((int64_t)b * Hq + head) * S;
   float M = -INFINITY;
@@ -339,7 +348,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float*
       L += f;
       acc += f * ws_o[(base + s) * D + d];
     }
-    o[b * ld_o + (int64_t)head * D + d] = f2bf(L > 0.f ? acc / L : 0.f);
+    o[b * ld_o + (int64_t)head * D + d] =
+        f2bf(L > 0.f ? acc / (L + sink_term(sinks, head, Mu)) : 0.f);
   }
 }
 
@@ -393,7 +403,7 @@ __global__ void __launch_bounds__(kThreads)
   const int ctx = seq_len - (q_end - q_begin);
   const int pos0 = ctx + (q0 - q_begin);          // position of tile row 0
   const int pos_last = pos0 + rows - 1;
-  const int n_chunks = pos_last / CH + 1;
+  const int n_chunks = p.causal ? pos_last / CH + 1 : (seq_len + CH - 1) / CH;
   int first_chunk = 0;
   if (p.window > 0) first_chunk = max(0, pos0 - p.window + 1) / CH;
   const int nc = n_chunks - first_chunk;
@@ -477,7 +487,8 @@ __global__ void __launch_bounds__(kThreads)
     }
     // scale + causal / window mask
     const int kv0 = chunk * CH;
-    const bool need_mask = (kv0 + CH - 1 > pos0 + tw) || (p.window > 0);
+    const bool need_mask = p.causal ? (kv0 + CH - 1 > pos0 + tw) || (p.window > 0)
+                                    : kv0 + CH > seq_len;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -485,7 +496,7 @@ __global__ void __launch_bounds__(kThreads)
         float v = s[nt][j] * p.scale_log2;
         if (need_mask) {
           const int kv = kv0 + nt * 8 + 2 * t + (j & 1);
-          const int qp = my_pos[j >> 1];
+          const int qp = p.causal ? my_pos[j >> 1] : seq_len - 1;
           if (kv > qp || (p.window > 0 && kv <= qp - p.window)) v = -INFINITY;
         }
         s[nt][j] = v;
@@ -548,7 +559,8 @@ __global__ void __launch_bounds__(kThreads)
   for (int rr = 0; rr < 2; ++rr) {
     const int row = tw + g + rr * 8;
     if (row >= rows) continue;
-    const float inv = lrow[rr] > 0.f ? 1.f / lrow[rr] : 0.f;
+    const float mu = mrow[rr] == -INFINITY ? 0.f : mrow[rr];
+    const float inv = lrow[rr] > 0.f ? 1.f / (lrow[rr] + sink_term(p.sinks, head, mu)) : 0.f;
     __nv_bfloat16* dst = p.o + (int64_t)(q0 + row) * p.ld_o + (int64_t)head * D;
 #pragma unroll
     for (int dt = 0; dt < D / 8; ++dt) {
@@ -609,6 +621,7 @@ void run_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.ws_o = a.ws_o;
   p.ws_lse = a.ws_lse;
   p.err = a.err;
+  p.sinks = a.sinks;
   if (p.num_splits > 1)
     B200_REQUIRE(a.ws_o && a.ws_lse, "decode: split-KV needs a workspace");
   dim3 grid(a.B, a.Hkv, p.num_splits);
@@ -633,7 +646,7 @@ void run_decode(const DecodeArgs& a, cudaStream_t stream) {
   count_launch();
   if (p.num_splits > 1) {
     attn_combine_kernel<<<dim3(a.B, a.Hq), 128, 0, stream>>>(a.ws_o, a.ws_lse, p.o, a.ld_o, a.Hq,
-                                                             p.num_splits, a.D);
+                                                             p.num_splits, a.D, a.sinks);
     B200_CUDA_OK(cudaGetLastError());
   count_launch();
   }
@@ -645,7 +658,9 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
   B200_REQUIRE(a.block_size % 16 == 0 && (a.block_size <= 64 || a.block_size % 64 == 0),
                "prefill: block_size must be 16, 32, 64 or a multiple of 64");
   B200_REQUIRE((a.ld_q * 2) % 16 == 0, "prefill: q row stride must be a multiple of 16 bytes");
-  if (prefill_tc_enabled(a.D)) {
+  B200_REQUIRE(a.causal || a.window == 0, "prefill: a sliding window needs causal attention");
+  // the tcgen05 kernels serve the causal, sink-free case; the rest runs on the kernel below
+  if (a.causal && a.sinks == nullptr && prefill_tc_enabled(a.D)) {
     run_prefill_tc(a, stream);
     return;
   }
@@ -674,6 +689,8 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.window = a.window;
   p.scale_log2 = a.scale * kLog2e;
   p.err = a.err;
+  p.sinks = a.sinks;
+  p.causal = a.causal;
   dim3 grid(p.max_tiles, a.Hq);
 #define B200_PRE(DD)                                                                      \
   {                                                                                       \

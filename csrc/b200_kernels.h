@@ -229,6 +229,7 @@ struct DecodeArgs {
   float* ws_o;
   float* ws_lse;
   int* err;
+  const float* sinks = nullptr;  // [Hq] per-head sink logits (softmax-only column), or null
 };
 struct PrefillArgs {
   const void* q;
@@ -246,6 +247,8 @@ struct PrefillArgs {
   int T, R, Hq, Hkv, D, block_size, window;
   float scale;
   int* err;
+  const float* sinks = nullptr;  // [Hq] per-head sink logits, or null
+  bool causal = true;            // false: every query sees its request's whole sequence
 };
 // head_dim 128 prefill on tcgen05 (prefill_tc.cu); B200_ATTN_TC=0 selects the mma.sync kernel.
 bool prefill_tc_enabled(int D);

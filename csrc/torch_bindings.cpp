@@ -533,10 +533,18 @@ void mla_topk(const Tensor& scores, const Tensor& cu_q, const Tensor& seq_lens, 
 }
 
 // ------------------------------------------------------------------------------------- attention
+static const float* sink_ptr(const c10::optional<Tensor>& sinks, int64_t Hq) {
+  if (!sinks.has_value()) return nullptr;
+  TORCH_CHECK(sinks->scalar_type() == at::kFloat && sinks->is_contiguous() && sinks->numel() == Hq,
+              "attention sinks: fp32 [num_q_heads]");
+  return sinks->data_ptr<float>();
+}
+
 void paged_decode(const Tensor& q, Tensor& out, const Tensor& k_cache, const Tensor& v_cache,
                   const Tensor& block_tables, const Tensor& seq_lens, int64_t Hq, int64_t Hkv,
                   int64_t max_seq_len, double scale, int64_t num_splits,
-                  const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse) {
+                  const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse,
+                  const c10::optional<Tensor>& sinks) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   CHECK_ROWMAJOR(q);
@@ -578,13 +586,15 @@ void paged_decode(const Tensor& q, Tensor& out, const Tensor& k_cache, const Ten
     a.ws_o = ws_o->data_ptr<float>();
     a.ws_lse = ws_lse->data_ptr<float>();
   }
+  a.sinks = sink_ptr(sinks, Hq);
   a.err = err_ptr(q);
   guarded([&] { b200::attn::run_decode(a, stream_of(q)); });
 }
 
 void paged_prefill(const Tensor& q, Tensor& out, const Tensor& k_cache, const Tensor& v_cache,
                    const Tensor& cu_q, const Tensor& seq_lens, const Tensor& block_tables,
-                   Tensor& tile_offsets, int64_t Hq, int64_t Hkv, double scale, int64_t window) {
+                   Tensor& tile_offsets, int64_t Hq, int64_t Hkv, double scale, int64_t window,
+                   const c10::optional<Tensor>& sinks, bool causal) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   CHECK_ROWMAJOR(q);
@@ -618,6 +628,8 @@ void paged_prefill(const Tensor& q, Tensor& out, const Tensor& k_cache, const Te
   a.block_size = k_cache.size(2);
   a.window = window;
   a.scale = scale;
+  a.sinks = sink_ptr(sinks, Hq);
+  a.causal = causal;
   a.err = err_ptr(q);
   guarded([&] { b200::attn::run_prefill(a, stream_of(q)); });
 }
@@ -1142,11 +1154,12 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "paged_decode(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor "
       "block_tables, Tensor seq_lens, int num_q_heads, int num_kv_heads, int max_seq_len, float "
-      "scale, int num_splits=1, Tensor(b!)? ws_o=None, Tensor(c!)? ws_lse=None) -> ()");
+      "scale, int num_splits=1, Tensor(b!)? ws_o=None, Tensor(c!)? ws_lse=None, "
+      "Tensor? sinks=None) -> ()");
   m.def(
       "paged_prefill(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor cu_q, "
       "Tensor seq_lens, Tensor block_tables, Tensor(b!) tile_offsets, int num_q_heads, int "
-      "num_kv_heads, float scale, int window=0) -> ()");
+      "num_kv_heads, float scale, int window=0, Tensor? sinks=None, bool causal=True) -> ()");
   m.def(
       "sample(Tensor logits, Tensor? temperature, Tensor? top_k, Tensor? top_p, Tensor? min_p, "
       "Tensor? seeds, Tensor? steps, int vocab_offset, Tensor(a!) out_idx, Tensor(b!)? "

@@ -386,3 +386,58 @@ def test_rope_kv_mrope(section, interleaved, neox):
     torch.testing.assert_close(gq.cpu().float(), ref_qkv.float(), rtol=1e-2, atol=1e-2)
     torch.testing.assert_close(gk.cpu().float(), rk.float(), rtol=1e-2, atol=1e-2)
     torch.testing.assert_close(gv.cpu().float(), rv.float())
+
+
+@pytest.mark.parametrize("splits", [1, 4])
+def test_paged_decode_sinks(splits):
+    D, Hq, Hkv, bs = 64, 8, 2, 64
+    lens = [1, 70, 600, 33]
+    B = len(lens)
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=51)
+    bt = _random_tables(B, lens, bs, nb, seed=9)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    q = _bf(B, (Hq + 2 * Hkv) * D, seed=52)
+    sinks = torch.linspace(-3.0, 4.0, Hq)
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_decode(q.cpu(), kc.cpu(), vc.cpu(), bt, sl, Hq, Hkv, scale, 1024, sinks=sinks)
+    out = ops.paged_decode(q, kc, vc, bt.to(DEV), sl.to(DEV), Hq, Hkv, scale, 1024,
+                           num_splits=splits, sinks=sinks.to(DEV))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("causal,sinks", [(True, True), (False, False), (False, True)])
+def test_paged_prefill_sinks_noncausal(causal, sinks):
+    """Sinks and bidirectional attention run on the mma.sync prefill kernel (the tcgen05 ones
+    serve the causal sink-free case)."""
+    D, Hq, Hkv, bs = 128, 8, 2, 64
+    reqs = [(0, 70), (64, 64), (300, 130), (5, 1)]
+    R = len(reqs)
+    lens = [c + n for c, n in reqs]
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=61)
+    bt = _random_tables(R, lens, bs, nb, seed=4)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([n for _, n in reqs]), 0)), dtype=torch.int32)
+    T = int(cu[-1])
+    q = _bf(T, (Hq + 2 * Hkv) * D, seed=62)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    sk = torch.linspace(-1.0, 2.0, Hq) if sinks else None
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale, 0,
+                            sinks=sk, causal=causal)
+    out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale, 0,
+                            sinks=sk.to(DEV) if sk is not None else None, causal=causal)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_encoder_varlen_attention():
+    from vllm_musa_b200.attention import MMEncoderAttention
+    H, D = 16, 64
+    lens = [1024, 1, 300, 64, 577]
+    T = sum(lens)
+    q, k, v = (_bf(T, H * D, seed=s) for s in (71, 72, 73))
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0)), dtype=torch.int32)
+    attn = MMEncoderAttention(H, D)
+    ref = attn.forward(q.cpu(), k.cpu(), v.cpu(), cu)
+    out = attn.forward(q, k, v, cu.to(DEV))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)

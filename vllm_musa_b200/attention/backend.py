@@ -4,7 +4,8 @@ Dispatches the step's decode rows to the split-KV decode kernel and its prefill 
 chunked-prefill kernel (csrc/attention/paged_attention.cu).  Capabilities mirror what the
 reference's MUSA FlashAttention backend advertises (vllm_musa/v1/attention/backends/
 flash_attn.py:238-400): paged KV with 16/32/64/128-token pages, GQA, causal, sliding
-window; head dims 64/128/256.
+window, attention sinks (per-head softmax-only logits); head dims 64/128/256.  Non-causal
+packed sequences without a cache (encoders) go through ``MMEncoderAttention``.
 """
 from __future__ import annotations
 
@@ -21,12 +22,14 @@ class PagedAttention:
     SUPPORTED_BLOCK_SIZES = (16, 32, 64, 128, 256)
 
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int,
-                 scale: float | None = None, sliding_window: int = 0):
+                 scale: float | None = None, sliding_window: int = 0,
+                 sinks: torch.Tensor | None = None):
         if head_dim not in self.SUPPORTED_HEAD_DIMS:
             raise ValueError(f"head_dim {head_dim} not supported")
         self.hq, self.hkv, self.d = num_heads, num_kv_heads, head_dim
         self.scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
         self.window = sliding_window
+        self.sinks = sinks.float().contiguous() if sinks is not None else None
 
     def forward(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 meta: AttnMetadata, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -38,10 +41,33 @@ class PagedAttention:
         if nd:
             ops.paged_decode(q[:nd], k_cache, v_cache, meta.block_tables[:nd], meta.seq_lens[:nd],
                              self.hq, self.hkv, self.scale, meta.max_seq_len, out=out[:nd],
-                             num_splits=meta.decode_splits)
+                             num_splits=meta.decode_splits, sinks=self.sinks)
         if npf:
             ops.paged_prefill(q, k_cache, v_cache, meta.prefill_cu_q, meta.prefill_seq_lens,
                               meta.prefill_block_tables, self.hq, self.hkv, self.scale,
                               self.window or meta.sliding_window, out=out,
-                              tile_scratch=meta.tile_scratch)
+                              tile_scratch=meta.tile_scratch, sinks=self.sinks)
         return out
+
+
+class MMEncoderAttention:
+    """Bidirectional attention over packed variable-length sequences (vision / audio encoder
+    layers): no KV cache, ``cu_seqlens`` delimits the images or clips.  Reference:
+    vllm_musa/model_executor/layers/attention/mm_encoder_attention.py:14-170."""
+
+    def __init__(self, num_heads: int, head_dim: int, scale: float | None = None,
+                 num_kv_heads: int | None = None):
+        if head_dim not in PagedAttention.SUPPORTED_HEAD_DIMS:
+            raise ValueError(f"head_dim {head_dim} not supported")
+        self.hq, self.d = num_heads, head_dim
+        self.hkv = num_kv_heads or num_heads
+        self.scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                cu_seqlens: torch.Tensor) -> torch.Tensor:
+        """q [T, Hq*D] or [T, Hq, D]; k/v likewise with Hkv heads -> [T, Hq*D]."""
+        T = q.shape[0]
+        q3 = q.reshape(T, self.hq, self.d)
+        k3 = k.reshape(T, self.hkv, self.d)
+        v3 = v.reshape(T, self.hkv, self.d)
+        return ops.varlen_attention(q3, k3, v3, cu_seqlens, self.scale).reshape(T, -1)

@@ -7,7 +7,7 @@ numerics oracle of the kernel tests.
 """
 from . import _ext  # noqa: F401
 from .activation import act_and_mul, silu_and_mul  # noqa: F401
-from .attention import paged_decode, paged_prefill  # noqa: F401
+from .attention import paged_decode, paged_prefill, varlen_attention  # noqa: F401
 from .gemm import linear, linear_silu_mul, interleave_gate_up  # noqa: F401
 from .misc import embedding, gather_rows  # noqa: F401
 from .norm import fused_add_rms_norm, rms_norm, rms_norm_gated, rms_norm_quant_fp8  # noqa: F401

@@ -40,27 +40,35 @@ def _gather_kv(cache: torch.Tensor, table: torch.Tensor, n: int) -> torch.Tensor
     return blocks.permute(0, 2, 1, 3).reshape(nb * bs, cache.shape[1], cache.shape[3])[:n]
 
 
-def _attend_ref(q, k, v, q_pos, scale, window):
-    # q [Tq, Hq, D], k/v [S, Hkv, D]; causal by absolute position
+def _attend_ref(q, k, v, q_pos, scale, window, sinks=None, causal=True):
+    # q [Tq, Hq, D], k/v [S, Hkv, D]; causal by absolute position.  A sink is an extra softmax
+    # column per head (logit sinks[h]) that carries no value.
     Hq, Hkv = q.shape[1], k.shape[1]
     G = Hq // Hkv
     k = k.float().repeat_interleave(G, dim=1)
     v = v.float().repeat_interleave(G, dim=1)
     s = torch.einsum("thd,shd->hts", q.float(), k) * scale
-    kv_pos = torch.arange(k.shape[0])
-    mask = kv_pos[None, :] > q_pos[:, None]
-    if window > 0:
-        mask |= kv_pos[None, :] <= q_pos[:, None] - window
-    s = s.masked_fill(mask[None], float("-inf"))
-    p = torch.softmax(s, dim=-1)
+    if causal:
+        kv_pos = torch.arange(k.shape[0])
+        mask = kv_pos[None, :] > q_pos[:, None]
+        if window > 0:
+            mask |= kv_pos[None, :] <= q_pos[:, None] - window
+        s = s.masked_fill(mask[None], float("-inf"))
+    if sinks is not None:
+        col = sinks.float().cpu().view(Hq, 1, 1).expand(Hq, s.shape[1], 1)
+        p = torch.softmax(torch.cat([s, col], dim=-1), dim=-1)[..., :-1]
+    else:
+        p = torch.softmax(s, dim=-1)
     return torch.einsum("hts,shd->thd", p, v)
 
 
 def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  block_tables: torch.Tensor, seq_lens: torch.Tensor, num_q_heads: int,
                  num_kv_heads: int, scale: float, max_seq_len: int,
-                 out: torch.Tensor | None = None, num_splits: int | None = None) -> torch.Tensor:
-    """One query token per sequence.  q: [B, >= Hq*D] (row stride may exceed Hq*D)."""
+                 out: torch.Tensor | None = None, num_splits: int | None = None,
+                 sinks: torch.Tensor | None = None) -> torch.Tensor:
+    """One query token per sequence.  q: [B, >= Hq*D] (row stride may exceed Hq*D).
+    ``sinks`` fp32 [Hq]: per-head attention-sink logits (a softmax column without a value)."""
     B = q.shape[0]
     D = k_cache.shape[-1]
     Hq = num_q_heads
@@ -75,7 +83,7 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         if num_splits > 1:
             ws_o, ws_l = decode_workspace(q.device, B, Hq, D, num_splits)
         _ext.ops().paged_decode(q, out, k_cache, v_cache, block_tables, seq_lens, Hq,
-                                num_kv_heads, max_seq_len, scale, num_splits, ws_o, ws_l)
+                                num_kv_heads, max_seq_len, scale, num_splits, ws_o, ws_l, sinks)
         return out
     for b in range(B):
         n = int(seq_lens[b])
@@ -85,7 +93,7 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         k = _gather_kv(k_cache, block_tables[b], n)
         v = _gather_kv(v_cache, block_tables[b], n)
         qb = q[b, :Hq * D].view(1, Hq, D)
-        o = _attend_ref(qb, k, v, torch.tensor([n - 1]), scale, 0)
+        o = _attend_ref(qb, k, v, torch.tensor([n - 1]), scale, 0, sinks)
         out[b] = o.reshape(Hq * D).to(out.dtype)
     return out
 
@@ -94,11 +102,13 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   cu_q: torch.Tensor, seq_lens: torch.Tensor, block_tables: torch.Tensor,
                   num_q_heads: int, num_kv_heads: int, scale: float, window: int = 0,
                   out: torch.Tensor | None = None,
-                  tile_scratch: torch.Tensor | None = None) -> torch.Tensor:
-    """Causal attention of each request's new tokens over its whole cached sequence.
+                  tile_scratch: torch.Tensor | None = None,
+                  sinks: torch.Tensor | None = None, causal: bool = True) -> torch.Tensor:
+    """Causal attention of each request's new tokens over its whole cached sequence
+    (``causal=False``: every query sees the whole sequence, as encoders need).
 
     q: [T, >= Hq*D] for the prefill tokens (request r owns rows cu_q[r]:cu_q[r+1]); the K/V
-    of those tokens must already be in the cache.
+    of those tokens must already be in the cache.  ``sinks`` as in ``paged_decode``.
     """
     T = q.shape[0]
     D = k_cache.shape[-1]
@@ -112,7 +122,7 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         if tile_scratch is None:
             tile_scratch = torch.empty(R + 1, dtype=torch.int32, device=q.device)
         _ext.ops().paged_prefill(q, out, k_cache, v_cache, cu_q, seq_lens, block_tables,
-                                 tile_scratch, Hq, num_kv_heads, scale, window)
+                                 tile_scratch, Hq, num_kv_heads, scale, window, sinks, causal)
         return out
     cu = cu_q.tolist()
     for r in range(R):
@@ -124,6 +134,53 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         v = _gather_kv(v_cache, block_tables[r], n)
         qr = q[a:b, :Hq * D].reshape(b - a, Hq, D)
         pos = torch.arange(n - (b - a), n)
-        o = _attend_ref(qr, k, v, pos, scale, window)
+        o = _attend_ref(qr, k, v, pos, scale, window, sinks, causal)
         out[a:b] = o.reshape(b - a, Hq * D).to(out.dtype)
     return out
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
+                     scale: float, causal: bool = False,
+                     sinks: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention over packed variable-length sequences without a KV cache (vision / audio
+    encoders): q [T, Hq, D], k/v [T, Hkv, D], sequence r owns rows cu_seqlens[r]:cu_seqlens[r+1].
+    Returns [T, Hq, D].
+
+    CUDA: K/V are laid into 64-token pages (each sequence starting on a page) and the paged
+    prefill kernel runs with ``causal=False``; the page copy is one gather per tensor.
+    Reference: vllm_musa/model_executor/layers/attention/mm_encoder_attention.py:14-170."""
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    cu = cu_seqlens.to(torch.int32)
+    if T == 0:
+        return torch.empty_like(q)
+    if not q.is_cuda:
+        out = torch.empty(T, Hq, D, dtype=q.dtype)
+        c = cu.tolist()
+        for r in range(len(c) - 1):
+            a, b = c[r], c[r + 1]
+            if b > a:
+                pos = torch.arange(b - a)
+                out[a:b] = _attend_ref(q[a:b], k[a:b], v[a:b], pos, scale, 0, sinks,
+                                       causal).to(q.dtype)
+        return out
+    dev = q.device
+    lens = (cu[1:] - cu[:-1]).long()
+    R = lens.numel()
+    pages = (lens + 63) // 64
+    first = torch.cumsum(pages, 0) - pages                       # first page of each sequence
+    n_pages = int(pages.sum())
+    max_pages = int(pages.max())
+    seq_of = torch.repeat_interleave(torch.arange(R, device=dev), lens, output_size=T)
+    idx = torch.arange(T, device=dev) - cu[:-1].long()[seq_of]   # token index within its sequence
+    page = first[seq_of] + idx // 64
+    off = idx % 64
+    kc = torch.zeros(n_pages, Hkv, 64, D, dtype=k.dtype, device=dev)
+    vc = torch.zeros_like(kc)
+    kc[page, :, off] = k
+    vc[page, :, off] = v
+    table = first[:, None] + torch.arange(max_pages, device=dev)[None, :]
+    table = torch.minimum(table, torch.full_like(table, n_pages - 1)).to(torch.int32)
+    out = paged_prefill(q.reshape(T, Hq * D), kc, vc, cu, lens.to(torch.int32), table, Hq, Hkv,
+                        scale, sinks=sinks, causal=causal)
+    return out.view(T, Hq, D)
