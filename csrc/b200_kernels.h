@@ -102,7 +102,8 @@ void run_fp8(const Fp8GemmArgs& a, cudaStream_t stream);
 namespace gdn {
 void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,
                        const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
-                       int T, int C, void* out, int64_t ldo, cudaStream_t s);
+                       int T, int C, void* out, int64_t ldo, cudaStream_t s,
+                       const void* bias = nullptr);
 void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld_ba,
                        const float* A_log, const float* dt_bias, float* state,
                        const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
@@ -171,6 +172,33 @@ void run_silu_mul_fp8_quant(void* out, float* scales, const void* x, int64_t ld_
 void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, int rows, int K,
                          cudaStream_t s);
 }  // namespace act
+
+// ------------------------------------------------------------------------------- Mamba2
+namespace mamba {
+struct Mamba2Args {
+  const void* xbc;           // bf16 conv output rows: x [H*P] at 0, B [G*N] at b_off, C at c_off
+  int64_t ld_xbc;
+  int b_off, c_off;
+  const void* dt;            // bf16 raw dt [T, >= H] (row stride ld_dt)
+  int64_t ld_dt;
+  const float* dt_bias;      // [H]
+  const float* A_log;        // [H]
+  const float* D;            // [H]
+  float* state;              // [slots, H, P, N] fp32
+  const int32_t* cu_q;
+  const int32_t* seq_lens;
+  const int32_t* slots;
+  void* y;                   // bf16 [T, H*P]
+  int64_t ld_y;
+  int R, H, G, P, N;
+  float dt_min, dt_max;
+};
+void run_mamba2_scan(const Mamba2Args& a, cudaStream_t s);
+// out = RMSNorm over groups of `group` channels of (y * silu(z)), times w
+void run_gated_rmsnorm(void* out, int64_t ld_o, const void* y, int64_t ld_y, const void* z,
+                       int64_t ld_z, const void* w, int T, int C, int group, float eps,
+                       cudaStream_t s);
+}  // namespace mamba
 
 // ------------------------------------------------------------------------------- W4AFP8 MoE
 namespace w4a8 {

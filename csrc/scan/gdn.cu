@@ -51,7 +51,8 @@ __global__ void causal_conv1d_kernel(const __nv_bfloat16* __restrict__ x, int64_
                                      const int32_t* __restrict__ cu_q,
                                      const int32_t* __restrict__ seq_lens,
                                      const int32_t* __restrict__ slots, int R, int C,
-                                     __nv_bfloat16* __restrict__ out, int64_t ldo) {
+                                     __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                     const __nv_bfloat16* __restrict__ bias) {
   pdl_launch_dependents();
   const int t = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -61,7 +62,7 @@ __global__ void causal_conv1d_kernel(const __nv_bfloat16* __restrict__ x, int64_
   const int q_len = cu_q[r + 1] - q0;
   const bool hist = seq_lens[r] - q_len > 0;
   const __nv_bfloat16* st = state + ((size_t)slots[r] * C + c) * 3;
-  float acc = 0.f;
+  float acc = bias != nullptr ? bf2f(bias[c]) : 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int tau = t - 3 + j;  // absolute token index in the batch
@@ -232,13 +233,14 @@ __global__ void sigmoid_gate_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo
 // ------------------------------------------------------------------------------ launchers
 void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,
                        const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
-                       int T, int C, void* out, int64_t ldo, cudaStream_t s) {
+                       int T, int C, void* out, int64_t ldo, cudaStream_t s,
+                       const void* bias) {
   if (T == 0 || R == 0) return;
   const int threads = 128;
   causal_conv1d_kernel<<<dim3((C + threads - 1) / threads, T), threads, 0, s>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<const __nv_bfloat16*>(w),
       reinterpret_cast<const __nv_bfloat16*>(state), cu_q, seq_lens, slots, R, C,
-      reinterpret_cast<__nv_bfloat16*>(out), ldo);
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(bias));
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
   conv_state_update_kernel<<<dim3((C + threads - 1) / threads, R), threads, 0, s>>>(

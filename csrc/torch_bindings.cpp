@@ -710,7 +710,8 @@ Tensor error_word(const Tensor& like) { return error_word_for(like.device()); }
 
 // ------------------------------------------------------------------------------------- GDN
 void causal_conv1d(const Tensor& x, const Tensor& w, Tensor& state, const Tensor& cu_q,
-                   const Tensor& seq_lens, const Tensor& slots, Tensor& out) {
+                   const Tensor& seq_lens, const Tensor& slots, Tensor& out,
+                   const c10::optional<Tensor>& bias) {
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_ROWMAJOR(x);
@@ -726,7 +727,82 @@ void causal_conv1d(const Tensor& x, const Tensor& w, Tensor& state, const Tensor
     b200::gdn::run_causal_conv1d(x.data_ptr(), x.stride(0), w.data_ptr(), state.data_ptr(),
                                  cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
                                  slots.data_ptr<int32_t>(), seq_lens.numel(), x.size(0), C,
-                                 out.data_ptr(), out.stride(0), stream_of(x));
+                                 out.data_ptr(), out.stride(0), stream_of(x),
+                                 bias.has_value() ? bias->data_ptr() : nullptr);
+  });
+}
+
+void mamba2_scan(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& dt,
+                 const Tensor& dt_bias, const Tensor& A_log, const Tensor& D, Tensor& state,
+                 const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots, Tensor& y,
+                 int64_t H, int64_t G, int64_t P, int64_t N, double dt_min, double dt_max) {
+  CHECK_CUDA(xbc);
+  CHECK_BF16(xbc);
+  CHECK_ROWMAJOR(xbc);
+  CHECK_BF16(dt);
+  CHECK_ROWMAJOR(dt);
+  CHECK_BF16(y);
+  CHECK_ROWMAJOR(y);
+  for (const Tensor* t : {&dt_bias, &A_log, &D})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == H,
+                "mamba2: fp32 [H] dt_bias / A_log / D");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4 &&
+                  state.size(1) == H && state.size(2) == P && state.size(3) == N,
+              "mamba2: state [slots, H, P, N] fp32");
+  TORCH_CHECK(xbc.size(1) >= c_off + G * N && b_off >= H * P && dt.size(1) >= H &&
+                  y.size(1) >= H * P && xbc.size(0) == y.size(0) && dt.size(0) == y.size(0),
+              "mamba2: widths");
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  slots.scalar_type() == at::kInt,
+              "mamba2: int32 metadata");
+  const c10::cuda::CUDAGuard g(xbc.device());
+  b200::mamba::Mamba2Args a{};
+  a.xbc = xbc.data_ptr();
+  a.ld_xbc = xbc.stride(0);
+  a.b_off = b_off;
+  a.c_off = c_off;
+  a.dt = dt.data_ptr();
+  a.ld_dt = dt.stride(0);
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.A_log = A_log.data_ptr<float>();
+  a.D = D.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.slots = slots.data_ptr<int32_t>();
+  a.y = y.data_ptr();
+  a.ld_y = y.stride(0);
+  a.R = seq_lens.numel();
+  a.H = H;
+  a.G = G;
+  a.P = P;
+  a.N = N;
+  a.dt_min = dt_min;
+  a.dt_max = dt_max;
+  guarded([&] { b200::mamba::run_mamba2_scan(a, stream_of(xbc)); });
+}
+
+void gated_rmsnorm(Tensor& out, const Tensor& y, const Tensor& z, const Tensor& w, int64_t group,
+                   double eps) {
+  CHECK_CUDA(y);
+  CHECK_BF16(y);
+  CHECK_BF16(z);
+  CHECK_BF16(w);
+  CHECK_ROWMAJOR(y);
+  CHECK_ROWMAJOR(z);
+  CHECK_ROWMAJOR(out);
+  const int C = w.numel();
+  TORCH_CHECK(y.size(1) >= C && z.size(1) >= C && out.size(1) >= C && w.is_contiguous(),
+              "gated rmsnorm: widths");
+  TORCH_CHECK((y.stride(0) * 2) % 16 == 0 && (z.stride(0) * 2) % 16 == 0 &&
+                  (out.stride(0) * 2) % 16 == 0 && (z.storage_offset() * 2) % 16 == 0 &&
+                  (y.storage_offset() * 2) % 16 == 0,
+              "gated rmsnorm: 16-byte aligned rows");
+  const c10::cuda::CUDAGuard g(y.device());
+  guarded([&] {
+    b200::mamba::run_gated_rmsnorm(out.data_ptr(), out.stride(0), y.data_ptr(), y.stride(0),
+                                   z.data_ptr(), z.stride(0), w.data_ptr(), y.size(0), C, group,
+                                   eps, stream_of(y));
   });
 }
 
@@ -1203,7 +1279,12 @@ TORCH_LIBRARY(b200, m) {
       "Tensor? shared_gate=None) -> ()");
   m.def(
       "causal_conv1d(Tensor x, Tensor w, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, "
-      "Tensor slots, Tensor(b!) out) -> ()");
+      "Tensor slots, Tensor(b!) out, Tensor? bias=None) -> ()");
+  m.def(
+      "mamba2_scan(Tensor xbc, int b_off, int c_off, Tensor dt, Tensor dt_bias, Tensor A_log, "
+      "Tensor D, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, Tensor slots, Tensor(b!) y, "
+      "int H, int G, int P, int N, float dt_min, float dt_max) -> ()");
+  m.def("gated_rmsnorm(Tensor(a!) out, Tensor y, Tensor z, Tensor w, int group, float eps) -> ()");
   m.def(
       "gdn_recurrent(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
       "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out) -> ()");
@@ -1245,6 +1326,8 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("row_fp8_qdq", &row_fp8_qdq);
   m.impl("moe_combine", &moe_combine);
   m.impl("causal_conv1d", &causal_conv1d);
+  m.impl("mamba2_scan", &mamba2_scan);
+  m.impl("gated_rmsnorm", &gated_rmsnorm);
   m.impl("gdn_recurrent", &gdn_recurrent);
   m.impl("gdn_chunked", &gdn_chunked);
   m.impl("sigmoid_gate", &sigmoid_gate);

@@ -66,6 +66,16 @@ class ModelConfig:
     linear_conv_kernel_dim: int = 4
     partial_rotary_factor: float = 1.0
     attn_output_gate: bool = False
+    # Mamba2 (state-space) mixers
+    ssm_state_size: int = 0
+    mamba_num_heads: int = 0
+    mamba_head_dim: int = 0
+    mamba_n_groups: int = 1
+    mamba_expand: int = 2
+    mamba_conv_kernel: int = 4
+    mamba_conv_bias: bool = True
+    mamba_dt_min: float = 0.0
+    mamba_dt_max: float = float("inf")
     eos_token_id: Optional[int] = None
     dtype: torch.dtype = torch.bfloat16
     name: str = ""
@@ -94,6 +104,28 @@ class ModelConfig:
         return L * (attn + mlp) + emb
 
     @staticmethod
+    def _from_hf_mamba2(hf: dict, a: str) -> "ModelConfig":
+        """transformers' Mamba2Config keys (state_size, expand, head_dim, n_groups, ...)."""
+        H = hf["hidden_size"]
+        expand = hf.get("expand", 2)
+        P = hf.get("head_dim", 64)
+        nh = hf.get("num_heads") or expand * H // P
+        lim = hf.get("time_step_limit") or (0.0, float("inf"))
+        eos = hf.get("eos_token_id")
+        return ModelConfig(
+            arch="mamba2", vocab_size=hf["vocab_size"], hidden_size=H,
+            num_layers=hf["num_hidden_layers"], num_heads=nh, num_kv_heads=nh, head_dim=P,
+            intermediate_size=expand * H, rms_norm_eps=hf.get("layer_norm_epsilon", 1e-5),
+            max_position=hf.get("max_position_embeddings", 1 << 20),
+            tie_word_embeddings=hf.get("tie_word_embeddings", True),
+            ssm_state_size=hf.get("state_size", 128), mamba_num_heads=nh, mamba_head_dim=P,
+            mamba_n_groups=hf.get("n_groups", 1) or 1, mamba_expand=expand,
+            mamba_conv_kernel=hf.get("conv_kernel", 4), mamba_conv_bias=hf.get("use_conv_bias",
+                                                                               True),
+            mamba_dt_min=float(lim[0]), mamba_dt_max=float(lim[1]),
+            eos_token_id=eos[0] if isinstance(eos, list) else eos, name=a)
+
+    @staticmethod
     def from_hf(config: "str | dict") -> "ModelConfig":
         """Build from a HuggingFace ``config.json`` (path, directory or dict)."""
         if isinstance(config, str):
@@ -105,6 +137,8 @@ class ModelConfig:
         archs = hf.get("architectures") or [""]
         a = archs[0]
         mt = hf.get("model_type", "")
+        if "Mamba2" in a or mt == "mamba2":
+            return ModelConfig._from_hf_mamba2(hf, a)
         if "Qwen3Next" in a or mt == "qwen3_next":
             arch = "qwen3_next"
         elif "Qwen3Moe" in a or mt == "qwen3_moe":

@@ -39,3 +39,5 @@ def _populate():
     from .deepseek_v2 import DeepseekV2ForCausalLM
     for arch in ("deepseek_v2", "deepseek_v3", "deepseek_v32"):
         _REGISTRY[arch] = DeepseekV2ForCausalLM
+    from .mamba2 import Mamba2ForCausalLM
+    _REGISTRY["mamba2"] = Mamba2ForCausalLM

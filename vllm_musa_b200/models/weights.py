@@ -30,9 +30,37 @@ def safetensors_weights(path: str, device: str = "cpu") -> Iterator[Tuple[str, t
                 yield name, fh.get_tensor(name)
 
 
+def _mamba2_shapes(cfg: ModelConfig) -> list:
+    """transformers' Mamba2ForCausalLM parameter names (``backbone.*``)."""
+    H, V = cfg.hidden_size, cfg.vocab_size
+    nh, P, G, N = cfg.mamba_num_heads, cfg.mamba_head_dim, cfg.mamba_n_groups, cfg.ssm_state_size
+    dI = nh * P
+    conv_dim = dI + 2 * G * N
+    out = [("backbone.embeddings.weight", (V, H), "w")]
+    for i in range(cfg.num_layers):
+        p = f"backbone.layers.{i}."
+        m = p + "mixer."
+        out += [(p + "norm.weight", (H,), "norm"),
+                (m + "in_proj.weight", (2 * dI + 2 * G * N + nh, H), "w"),
+                (m + "conv1d.weight", (conv_dim, 1, cfg.mamba_conv_kernel), "conv")]
+        if cfg.mamba_conv_bias:
+            out.append((m + "conv1d.bias", (conv_dim,), "norm0"))
+        out += [(m + "dt_bias", (nh,), "norm"),
+                (m + "A_log", (nh,), "a_log"),
+                (m + "D", (nh,), "norm"),
+                (m + "norm.weight", (dI,), "norm"),
+                (m + "out_proj.weight", (H, dI), "w")]
+    out.append(("backbone.norm_f.weight", (H,), "norm"))
+    if not cfg.tie_word_embeddings:
+        out.append(("lm_head.weight", (V, H), "w"))
+    return out
+
+
 def hf_param_shapes(cfg: ModelConfig) -> list:
     """Ordered (name, shape, kind) list of the dense/MoE decoder parameters (HF names)."""
     H, D, V = cfg.hidden_size, cfg.head_dim, cfg.vocab_size
+    if cfg.arch == "mamba2":
+        return _mamba2_shapes(cfg)
     out = [("model.embed_tokens.weight", (V, H), "w")]
     if cfg.arch.startswith("deepseek"):
         return out + _deepseek_shapes(cfg)

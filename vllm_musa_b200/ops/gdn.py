@@ -15,8 +15,10 @@ from . import _ext
 
 def causal_conv1d(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, cu_q: torch.Tensor,
                   seq_lens: torch.Tensor, slots: torch.Tensor,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [T, >= C] (first C channels used); w [C, 4]; updates ``state`` in place."""
+                  out: torch.Tensor | None = None,
+                  bias: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, >= C] (first C channels used); w [C, 4]; optional bias [C]; updates ``state`` in
+    place.  out = silu(conv(x) + bias)."""
     C = w.shape[0]
     T = x.shape[0]
     if out is None:
@@ -24,7 +26,7 @@ def causal_conv1d(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, cu_q: t
     if T == 0:
         return out
     if x.is_cuda:
-        _ext.ops().causal_conv1d(x, w, state, cu_q, seq_lens, slots, out)
+        _ext.ops().causal_conv1d(x, w, state, cu_q, seq_lens, slots, out, bias)
         return out
     cu = cu_q.tolist()
     for r in range(len(cu) - 1):
@@ -34,6 +36,8 @@ def causal_conv1d(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, cu_q: t
         hist = state[slot].float() if int(seq_lens[r]) - L > 0 else torch.zeros(C, 3)
         xs = torch.cat([hist, x[a:b, :C].float().t()], dim=1)  # [C, 3 + L]
         y = F.conv1d(xs.unsqueeze(0), w.float().unsqueeze(1), groups=C)[0]  # [C, L]
+        if bias is not None:
+            y = y + bias.float().unsqueeze(1)
         out[a:b] = F.silu(y).t().to(out.dtype)
         state[slot] = xs[:, -3:].to(state.dtype)
     return out
