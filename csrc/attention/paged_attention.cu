@@ -73,6 +73,7 @@ struct PrefillParams {
   int* err;
   const float* sinks;  // [Hq] natural-log sink logits or null
   bool causal;
+  const uint64_t* tree_mask;  // per query row: visible draft tokens (bit j), or null
 };
 
 // A sink is a softmax column with no value: it only adds 2^(sink * log2 e - m) to the row sum.
@@ -456,6 +457,12 @@ __global__ void __launch_bounds__(kThreads)
   if (!mbar_wait(qbar, 0, p.err)) return;
   const uint32_t sQa = smem_u32(sQ);
   const int my_pos[2] = {pos0 + tw + g, pos0 + tw + g + 8};
+  uint64_t tmask[2] = {0, 0};
+  if (p.tree_mask != nullptr) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+      if (tw + g + rr * 8 < rows) tmask[rr] = p.tree_mask[q0 + tw + g + rr * 8];
+  }
   int stage = 0;
   uint32_t phase = 0;
   for (int i = 0; i < nc; ++i) {
@@ -487,7 +494,8 @@ __global__ void __launch_bounds__(kThreads)
     }
     // scale + causal / window mask
     const int kv0 = chunk * CH;
-    const bool need_mask = p.causal ? (kv0 + CH - 1 > pos0 + tw) || (p.window > 0)
+    const bool need_mask = p.tree_mask != nullptr ? kv0 + CH > ctx
+                         : p.causal ? (kv0 + CH - 1 > pos0 + tw) || (p.window > 0)
                                     : kv0 + CH > seq_len;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
@@ -497,7 +505,13 @@ __global__ void __launch_bounds__(kThreads)
         if (need_mask) {
           const int kv = kv0 + nt * 8 + 2 * t + (j & 1);
           const int qp = p.causal ? my_pos[j >> 1] : seq_len - 1;
-          if (kv > qp || (p.window > 0 && kv <= qp - p.window)) v = -INFINITY;
+          if (p.tree_mask != nullptr) {
+            const int d = kv - ctx;  // draft index; the context before the drafts is visible
+            if (kv >= seq_len || (d >= 0 && (d >= 64 || !((tmask[j >> 1] >> d) & 1ull))))
+              v = -INFINITY;
+          } else if (kv > qp || (p.window > 0 && kv <= qp - p.window)) {
+            v = -INFINITY;
+          }
         }
         s[nt][j] = v;
       }
@@ -660,7 +674,7 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
   B200_REQUIRE((a.ld_q * 2) % 16 == 0, "prefill: q row stride must be a multiple of 16 bytes");
   B200_REQUIRE(a.causal || a.window == 0, "prefill: a sliding window needs causal attention");
   // the tcgen05 kernels serve the causal, sink-free case; the rest runs on the kernel below
-  if (a.causal && a.sinks == nullptr && prefill_tc_enabled(a.D)) {
+  if (a.causal && a.sinks == nullptr && a.tree_mask == nullptr && prefill_tc_enabled(a.D)) {
     run_prefill_tc(a, stream);
     return;
   }
@@ -691,6 +705,7 @@ void run_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.err = a.err;
   p.sinks = a.sinks;
   p.causal = a.causal;
+  p.tree_mask = a.tree_mask;
   dim3 grid(p.max_tiles, a.Hq);
 #define B200_PRE(DD)                                                                      \
   {                                                                                       \

@@ -277,6 +277,10 @@ struct PrefillArgs {
   int* err;
   const float* sinks = nullptr;  // [Hq] per-head sink logits, or null
   bool causal = true;            // false: every query sees its request's whole sequence
+  // tree attention (speculative token trees): per query row t, bit j of tree_mask[t] lets it
+  // see draft token j of its request (the request's last q_len <= 64 positions); the cached
+  // context before them stays visible.  Null: plain causal.
+  const uint64_t* tree_mask = nullptr;
 };
 // head_dim 128 prefill on tcgen05 (prefill_tc.cu); B200_ATTN_TC=0 selects the mma.sync kernel.
 bool prefill_tc_enabled(int D);

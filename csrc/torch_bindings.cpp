@@ -594,7 +594,8 @@ void paged_decode(const Tensor& q, Tensor& out, const Tensor& k_cache, const Ten
 void paged_prefill(const Tensor& q, Tensor& out, const Tensor& k_cache, const Tensor& v_cache,
                    const Tensor& cu_q, const Tensor& seq_lens, const Tensor& block_tables,
                    Tensor& tile_offsets, int64_t Hq, int64_t Hkv, double scale, int64_t window,
-                   const c10::optional<Tensor>& sinks, bool causal) {
+                   const c10::optional<Tensor>& sinks, bool causal,
+                   const c10::optional<Tensor>& tree_mask) {
   CHECK_CUDA(q);
   CHECK_BF16(q);
   CHECK_ROWMAJOR(q);
@@ -630,6 +631,12 @@ void paged_prefill(const Tensor& q, Tensor& out, const Tensor& k_cache, const Te
   a.scale = scale;
   a.sinks = sink_ptr(sinks, Hq);
   a.causal = causal;
+  if (tree_mask.has_value()) {
+    TORCH_CHECK(tree_mask->scalar_type() == at::kLong && tree_mask->is_contiguous() &&
+                    tree_mask->numel() >= q.size(0) && causal,
+                "tree attention: int64 mask per query row (causal mode)");
+    a.tree_mask = reinterpret_cast<const uint64_t*>(tree_mask->data_ptr<int64_t>());
+  }
   a.err = err_ptr(q);
   guarded([&] { b200::attn::run_prefill(a, stream_of(q)); });
 }
@@ -1235,7 +1242,8 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "paged_prefill(Tensor q, Tensor(a!) out, Tensor k_cache, Tensor v_cache, Tensor cu_q, "
       "Tensor seq_lens, Tensor block_tables, Tensor(b!) tile_offsets, int num_q_heads, int "
-      "num_kv_heads, float scale, int window=0, Tensor? sinks=None, bool causal=True) -> ()");
+      "num_kv_heads, float scale, int window=0, Tensor? sinks=None, bool causal=True, "
+      "Tensor? tree_mask=None) -> ()");
   m.def(
       "sample(Tensor logits, Tensor? temperature, Tensor? top_k, Tensor? top_p, Tensor? min_p, "
       "Tensor? seeds, Tensor? steps, int vocab_offset, Tensor(a!) out_idx, Tensor(b!)? "

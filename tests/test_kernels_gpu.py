@@ -441,3 +441,30 @@ def test_encoder_varlen_attention():
     ref = attn.forward(q.cpu(), k.cpu(), v.cpu(), cu)
     out = attn.forward(q, k, v, cu.to(DEV))
     torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_paged_prefill_tree_mask():
+    """Speculative token trees on the prefill kernel: per-row ancestor masks over the drafts."""
+    from vllm_musa_b200.ops.attention import tree_ancestor_masks
+    D, Hq, Hkv, bs = 128, 8, 2, 64
+    g = torch.Generator().manual_seed(81)
+    trees = [[-1], [-1, 0, 0, 1, 1, 2], [-1] + [int(torch.randint(0, i, (1,), generator=g))
+                                               for i in range(1, 64)], [-1, 0, 1, -1]]
+    ctxs = [0, 70, 300, 5]
+    R = len(trees)
+    lens = [c + len(t) for c, t in zip(ctxs, trees)]
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=82)
+    bt = _random_tables(R, lens, bs, nb, seed=6)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([len(t) for t in trees]), 0)),
+                      dtype=torch.int32)
+    T = int(cu[-1])
+    masks = torch.cat([tree_ancestor_masks(t) for t in trees])
+    q = _bf(T, (Hq + 2 * Hkv) * D, seed=83)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale,
+                            tree_mask=masks)
+    out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale,
+                            tree_mask=masks.to(DEV))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)

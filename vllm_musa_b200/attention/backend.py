@@ -71,3 +71,18 @@ class MMEncoderAttention:
         k3 = k.reshape(T, self.hkv, self.d)
         v3 = v.reshape(T, self.hkv, self.d)
         return ops.varlen_attention(q3, k3, v3, cu_seqlens, self.scale).reshape(T, -1)
+
+
+class TreeAttention(PagedAttention):
+    """Attention of speculative token trees: each request's step tokens are a draft tree (at
+    most 64 nodes) appended after its cached context; a node sees the context and its own
+    ancestors only.  ``tree_mask`` (int64 per step token, from ``ops.attention.
+    tree_ancestor_masks``) carries the visibility bits.  Runs the paged prefill kernel with the
+    tree mask.  Reference: vllm_musa/v1/attention/backends/tree_attn.py:41-451."""
+
+    def forward_tree(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     cu_q: torch.Tensor, seq_lens: torch.Tensor, block_tables: torch.Tensor,
+                     tree_mask: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        return ops.paged_prefill(q, k_cache, v_cache, cu_q, seq_lens, block_tables, self.hq,
+                                 self.hkv, self.scale, out=out, sinks=self.sinks,
+                                 tree_mask=tree_mask)

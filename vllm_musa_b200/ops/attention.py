@@ -40,7 +40,7 @@ def _gather_kv(cache: torch.Tensor, table: torch.Tensor, n: int) -> torch.Tensor
     return blocks.permute(0, 2, 1, 3).reshape(nb * bs, cache.shape[1], cache.shape[3])[:n]
 
 
-def _attend_ref(q, k, v, q_pos, scale, window, sinks=None, causal=True):
+def _attend_ref(q, k, v, q_pos, scale, window, sinks=None, causal=True, allowed=None):
     # q [Tq, Hq, D], k/v [S, Hkv, D]; causal by absolute position.  A sink is an extra softmax
     # column per head (logit sinks[h]) that carries no value.
     Hq, Hkv = q.shape[1], k.shape[1]
@@ -48,7 +48,9 @@ def _attend_ref(q, k, v, q_pos, scale, window, sinks=None, causal=True):
     k = k.float().repeat_interleave(G, dim=1)
     v = v.float().repeat_interleave(G, dim=1)
     s = torch.einsum("thd,shd->hts", q.float(), k) * scale
-    if causal:
+    if allowed is not None:  # [Tq, S] visibility (tree attention)
+        s = s.masked_fill(~allowed[None], float("-inf"))
+    elif causal:
         kv_pos = torch.arange(k.shape[0])
         mask = kv_pos[None, :] > q_pos[:, None]
         if window > 0:
@@ -103,9 +105,13 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   num_q_heads: int, num_kv_heads: int, scale: float, window: int = 0,
                   out: torch.Tensor | None = None,
                   tile_scratch: torch.Tensor | None = None,
-                  sinks: torch.Tensor | None = None, causal: bool = True) -> torch.Tensor:
+                  sinks: torch.Tensor | None = None, causal: bool = True,
+                  tree_mask: torch.Tensor | None = None) -> torch.Tensor:
     """Causal attention of each request's new tokens over its whole cached sequence
     (``causal=False``: every query sees the whole sequence, as encoders need).
+
+    ``tree_mask`` int64 [T] (speculative token trees): bit j of row t lets query t see draft j
+    of its request (its last q_len <= 64 tokens); the cached context stays visible.
 
     q: [T, >= Hq*D] for the prefill tokens (request r owns rows cu_q[r]:cu_q[r+1]); the K/V
     of those tokens must already be in the cache.  ``sinks`` as in ``paged_decode``.
@@ -122,7 +128,8 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         if tile_scratch is None:
             tile_scratch = torch.empty(R + 1, dtype=torch.int32, device=q.device)
         _ext.ops().paged_prefill(q, out, k_cache, v_cache, cu_q, seq_lens, block_tables,
-                                 tile_scratch, Hq, num_kv_heads, scale, window, sinks, causal)
+                                 tile_scratch, Hq, num_kv_heads, scale, window, sinks, causal,
+                                 tree_mask)
         return out
     cu = cu_q.tolist()
     for r in range(R):
@@ -134,7 +141,14 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         v = _gather_kv(v_cache, block_tables[r], n)
         qr = q[a:b, :Hq * D].reshape(b - a, Hq, D)
         pos = torch.arange(n - (b - a), n)
-        o = _attend_ref(qr, k, v, pos, scale, window, sinks, causal)
+        allowed = None
+        if tree_mask is not None:
+            ctx = n - (b - a)
+            bits = tree_mask[a:b].cpu().view(-1, 1)
+            j = torch.arange(n) - ctx
+            allowed = (j[None, :] < 0) | ((j[None, :] < 64) & (j[None, :] >= 0) &
+                                          (((bits >> j.clamp(0, 63)[None, :]) & 1) == 1))
+        o = _attend_ref(qr, k, v, pos, scale, window, sinks, causal, allowed)
         out[a:b] = o.reshape(b - a, Hq * D).to(out.dtype)
     return out
 
@@ -184,3 +198,18 @@ def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqle
     out = paged_prefill(q.reshape(T, Hq * D), kc, vc, cu, lens.to(torch.int32), table, Hq, Hkv,
                         scale, sinks=sinks, causal=causal)
     return out.view(T, Hq, D)
+
+
+def tree_ancestor_masks(parents: list) -> torch.Tensor:
+    """Draft-token tree given as parent indices (-1: child of the last accepted token) -> int64
+    [n] masks: bit j of row i is set when draft j is i or one of its ancestors."""
+    n = len(parents)
+    if n > 64:
+        raise ValueError("tree attention supports at most 64 draft tokens per request")
+    masks = [0] * n
+    for i, par in enumerate(parents):
+        if par >= i:
+            raise ValueError("parents must precede their children")
+        masks[i] = (1 << i) | (masks[par] if par >= 0 else 0)
+    # int64 storage of the unsigned bit pattern
+    return torch.tensor([m - (1 << 64) if m >= 1 << 63 else m for m in masks], dtype=torch.int64)
