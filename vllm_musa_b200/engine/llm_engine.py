@@ -20,7 +20,7 @@ from typing import Dict, List, Optional
 
 import torch
 
-from .. import ops
+from .. import ops, plan
 from ..config import EngineConfig
 from ..models.registry import get_model_class
 from ..models.weights import dummy_weights, safetensors_weights
@@ -60,6 +60,10 @@ class LLMEngine:
     def __init__(self, config: EngineConfig, tokenizer=None):
         self.config = config
         self.tokenizer = tokenizer
+        # which optimised paths this configuration uses (fails closed on unserved combinations)
+        self.contract = plan.resolve(config)
+        plan.validate(self.contract)
+        log.info("optimisation contract %s", self.contract.describe())
         mcfg = config.model
         tp = config.parallel.tensor_parallel_size
         device = torch.device(config.device)
@@ -130,6 +134,7 @@ class LLMEngine:
         sc.chunked_prefill = config.scheduler.enable_chunked_prefill
         # recurrent-state (hybrid) models cannot resume from cached KV blocks alone
         sc.prefix_caching = (config.cache.enable_prefix_caching
+                             and self.contract.prefers(plan.Feature.PREFIX_CACHING)
                              and not hasattr(self.model, "allocate_state"))
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
         self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
