@@ -49,7 +49,7 @@ __global__ void act_and_mul_kernel(__nv_bfloat16* __restrict__ out, int64_t ld_o
 __global__ void silu_mul_fp8_quant_kernel(__nv_fp8_e4m3* __restrict__ out,
                                           float* __restrict__ scales,
                                           const __nv_bfloat16* __restrict__ x, int64_t ld_x,
-                                          int rows, int I) {
+                                          int rows, int I, float limit) {
   const int groups = I / 128;
   const int gid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (gid >= rows * groups) return;
@@ -60,7 +60,12 @@ __global__ void silu_mul_fp8_quant_kernel(__nv_fp8_e4m3* __restrict__ out,
   float amax = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    v[j] = silu(bf2f(gp[j])) * bf2f(up[j]);
+    float gv = bf2f(gp[j]), uv = bf2f(up[j]);
+    if (limit > 0.f) {  // clamped SwiGLU: gate <= limit, |up| <= limit
+      gv = fminf(gv, limit);
+      uv = fmaxf(fminf(uv, limit), -limit);
+    }
+    v[j] = silu(gv) * uv;
     amax = fmaxf(amax, fabsf(v[j]));
   }
   amax = warp_max(amax);
@@ -117,13 +122,13 @@ void run_act_and_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int
 }
 
 void run_silu_mul_fp8_quant(void* out, float* scales, const void* x, int64_t ld_x, int rows, int I,
-                            cudaStream_t s) {
+                            cudaStream_t s, float limit) {
   B200_REQUIRE(I % 128 == 0, "silu_mul_fp8_quant: I must be a multiple of 128");
   const int total = rows * (I / 128);
   if (total == 0) return;
   silu_mul_fp8_quant_kernel<<<(total + 7) / 8, 256, 0, s>>>(
       reinterpret_cast<__nv_fp8_e4m3*>(out), scales, reinterpret_cast<const __nv_bfloat16*>(x),
-      ld_x, rows, I);
+      ld_x, rows, I, limit);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
 }

@@ -168,7 +168,7 @@ namespace act {
 void run_act_and_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int rows, int I,
                      int kind, float limit, cudaStream_t s);
 void run_silu_mul_fp8_quant(void* out, float* scales, const void* x, int64_t ld_x, int rows, int I,
-                            cudaStream_t s);
+                            cudaStream_t s, float limit = 0.f);
 void run_group_quant_fp8(void* out, float* scales, const void* x, int64_t ld_x, int rows, int K,
                          cudaStream_t s);
 }  // namespace act

@@ -288,7 +288,7 @@ void act_and_mul(Tensor& out, const Tensor& x, int64_t kind, double limit) {
   });
 }
 
-void silu_mul_fp8_quant(Tensor& out, Tensor& scales, const Tensor& x) {
+void silu_mul_fp8_quant(Tensor& out, Tensor& scales, const Tensor& x, double limit) {
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_ROWMAJOR(x);
@@ -302,7 +302,7 @@ void silu_mul_fp8_quant(Tensor& out, Tensor& scales, const Tensor& x) {
   const c10::cuda::CUDAGuard g(x.device());
   guarded([&] {
     b200::act::run_silu_mul_fp8_quant(out.data_ptr(), scales.data_ptr<float>(), x.data_ptr(),
-                                      x.stride(0), x.size(0), I, stream_of(x));
+                                      x.stride(0), x.size(0), I, stream_of(x), (float)limit);
   });
 }
 
@@ -1227,7 +1227,7 @@ TORCH_LIBRARY(b200, m) {
   m.def(
       "rms_norm_gated(Tensor(a!) out, Tensor x, Tensor z, Tensor weight, int group, float eps) -> ()");
   m.def("act_and_mul(Tensor(a!) out, Tensor x, int kind=0, float limit=0.0) -> ()");
-  m.def("silu_mul_fp8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
+  m.def("silu_mul_fp8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor x, float limit=0.0) -> ()");
   m.def("group_quant_fp8(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
   m.def(
       "rope_kv(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor? q_norm_w, Tensor? "

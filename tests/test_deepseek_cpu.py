@@ -68,3 +68,21 @@ def test_tiny_deepseek_w4afp8_experts():
     want = DeepseekReferenceDecoder(ref_cfg, W).logits(prompt)[-1]
     err = (got - want).abs().max() / want.abs().max()
     assert 0 < err < 0.02, float(err)  # only the per-token e4m3 activation rounding differs
+
+
+def test_tiny_deepseek_swiglu_clamp():
+    """swiglu_limit clamps the dense MLPs' gate (<= limit) and up (|up| <= limit): a large limit
+    is the plain SwiGLU, a small one changes the logits."""
+    def logits(limit):
+        cfg = tiny_ds(False, 0)
+        cfg.num_experts = 0
+        cfg.swiglu_limit = limit
+        llm = LLM(cfg, device="cpu", block_size=16, seed=0, num_gpu_blocks=64,
+                  max_model_len=128, max_num_seqs=4, max_num_batched_tokens=256)
+        llm.engine.runner.record_logits = True
+        llm.generate([_prompts(1, 12, seed=8)[0]],
+                     SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True))
+        return llm.engine.runner.logits_log[0][0]
+    plain, big, small = logits(0.0), logits(1e4), logits(1e-3)
+    torch.testing.assert_close(big, plain, rtol=1e-4, atol=1e-5)
+    assert (small - plain).abs().max() > 1e-4

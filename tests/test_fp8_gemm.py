@@ -46,9 +46,12 @@ def test_gemm_fp8_gpu(M, N, K, splits):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("T,E,k,H,I,off", [(1, 8, 2, 256, 128, 0), (77, 16, 4, 512, 256, 8),
-                                            (300, 32, 8, 1024, 256, 0)])
-def test_fused_moe_fp8_gpu(T, E, k, H, I, off):
+@pytest.mark.parametrize("T,E,k,H,I,off,limit", [(1, 8, 2, 256, 128, 0, 0.0),
+                                                  (77, 16, 4, 512, 256, 8, 0.0),
+                                                  (300, 32, 8, 1024, 256, 0, 0.0),
+                                                  (77, 16, 4, 512, 256, 0, 0.5)])
+def test_fused_moe_fp8_gpu(T, E, k, H, I, off, limit):
+    """limit > 0: clamped SwiGLU between the expert GEMMs."""
     from vllm_musa_b200.ops import moe as moe_ops
     g = torch.Generator().manual_seed(T + E + off)
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
@@ -63,9 +66,35 @@ def test_fused_moe_fp8_gpu(T, E, k, H, I, off):
     w_gu, s_gu, w_dn, s_dn = torch.cat(gus), torch.cat(gss), torch.cat(dws), torch.cat(dss)
     ids, w = moe_ops.topk_softmax(torch.randn(T, 2 * E, generator=g), k)  # half are other ranks'
     shared = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
-    ref = moe_ops.fused_moe_fp8(x, w_gu, s_gu, w_dn, s_dn, ids, w, E, shared, expert_offset=off)
+    ref = moe_ops.fused_moe_fp8(x, w_gu, s_gu, w_dn, s_dn, ids, w, E, shared, expert_offset=off,
+                                swiglu_limit=limit)
     out = moe_ops.fused_moe_fp8(x.cuda(), w_gu.cuda(), s_gu.cuda(), w_dn.cuda(), s_dn.cuda(),
-                                ids.cuda(), w.cuda(), E, shared.cuda(), expert_offset=off)
+                                ids.cuda(), w.cuda(), E, shared.cuda(), expert_offset=off,
+                                swiglu_limit=limit)
     torch.cuda.synchronize()
     # activations are re-quantised to e4m3 twice on the GPU path: compare at fp8 resolution
     torch.testing.assert_close(out.float().cpu(), ref.float(), rtol=6e-2, atol=6e-2)
+
+
+def test_swiglu_clamp_quant_cpu():
+    from vllm_musa_b200.ops.activation import group_quant_fp8, silu_mul_fp8_quant
+    g = torch.Generator().manual_seed(5)
+    x = (torch.randn(6, 512, generator=g) * 3).to(torch.bfloat16)
+    q, s = silu_mul_fp8_quant(x, 1.5)
+    gt, up = x.float().chunk(2, -1)
+    a = (torch.nn.functional.silu(gt.clamp(max=1.5)) * up.clamp(-1.5, 1.5)).to(torch.bfloat16)
+    rq, rs = group_quant_fp8(a)
+    assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8)) and torch.equal(s, rs)
+    assert float(q.float().mul(s.repeat_interleave(128, 1)).abs().max()) <= 1.5 * 1.5 + 1e-3
+
+
+@pytest.mark.gpu
+def test_swiglu_clamp_quant_gpu():
+    from vllm_musa_b200.ops.activation import silu_mul_fp8_quant
+    g = torch.Generator().manual_seed(6)
+    x = (torch.randn(33, 1024, generator=g) * 3).to(torch.bfloat16)
+    q, s = silu_mul_fp8_quant(x.cuda(), 2.0)
+    rq, rs = silu_mul_fp8_quant(x, 2.0)
+    deq = q.float().cpu() * s.cpu().repeat_interleave(128, 1)
+    ref = rq.float() * rs.repeat_interleave(128, 1)
+    torch.testing.assert_close(deq, ref, rtol=7e-2, atol=1e-2)

@@ -66,6 +66,8 @@ class ModelConfig:
     linear_conv_kernel_dim: int = 4
     partial_rotary_factor: float = 1.0
     attn_output_gate: bool = False
+    # clamped SwiGLU (gate <= limit, |up| <= limit) in MLPs and experts; 0: plain SwiGLU
+    swiglu_limit: float = 0.0
     # Mamba2 (state-space) mixers
     ssm_state_size: int = 0
     mamba_num_heads: int = 0
@@ -195,6 +197,7 @@ class ModelConfig:
             linear_conv_kernel_dim=hf.get("linear_conv_kernel_dim", 4) or 4,
             partial_rotary_factor=hf.get("partial_rotary_factor", 1.0) or 1.0,
             attn_output_gate=arch == "qwen3_next",
+            swiglu_limit=float(hf.get("swiglu_limit") or 0.0),
             eos_token_id=(hf.get("eos_token_id")[0] if isinstance(hf.get("eos_token_id"), list)
                           else hf.get("eos_token_id")),
             name=a,

@@ -375,6 +375,8 @@ class DeepseekV2ForCausalLM:
             gu = self._lin(w, s)
             return gu, self._lin(d, ds)
         g, u, d = self._deq(g, gs), self._deq(u, us), self._deq(d, ds)
+        if self.cfg.swiglu_limit > 0:  # clamped SwiGLU runs after the GEMM: keep [gate ; up]
+            return Lin(self._to(torch.cat([g, u]))), Lin(self._to(d))
         return Lin(self._to(ops.interleave_gate_up(g, u))), Lin(self._to(d))
 
     def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
@@ -640,18 +642,26 @@ class DeepseekV2ForCausalLM:
             from ..ops.w4afp8 import w4afp8_moe
             w13, s13, w2, s2 = L.w4
             return w4afp8_moe(x, w13, w2, s13, s2, w, ids, out=out, expert_offset=self.e0,
-                              shared=shared)
+                              shared=shared, swiglu_limit=cfg.swiglu_limit or None)
         if self.fp8:
             return moe_ops.fused_moe_fp8(x, L.experts_gu, L.experts_gu_s, L.experts_down,
                                          L.experts_down_s, ids, w, self.E_local, shared, out=out,
-                                         expert_offset=self.e0)
+                                         expert_offset=self.e0, swiglu_limit=cfg.swiglu_limit)
+        if cfg.swiglu_limit > 0:
+            raise NotImplementedError("clamped SwiGLU experts need fp8 or W4AFP8 weights")
         return moe_ops.fused_moe(x, L.experts_gu, L.experts_down, ids, w, self.E_local, shared,
                                  out=out, expert_offset=self.e0)
 
     def _swiglu_fwd(self, gu: Lin, down: Lin, x, out=None):
+        """Row-parallel SwiGLU MLP: gate/up GEMM -> (clamped) SwiGLU + 1x128 e4m3 quant ->
+        FP8 down GEMM; the caller's fused all-reduce + residual + RMSNorm completes it
+        (reference: vllm_musa/model_executor/layers/linear.py:31-127, forward_swiglu_clamp)."""
+        limit = self.cfg.swiglu_limit
         if gu.fp8:
-            hq, hs = ops.activation.silu_mul_fp8_quant(gu(x))
+            hq, hs = ops.activation.silu_mul_fp8_quant(gu(x), limit)
             return fp8_ops.gemm_fp8(hq, hs, down.w, down.s, out)
+        if limit > 0:
+            return down(ops.act_and_mul(gu(x), ops.activation.SILU, limit), out=out)
         return down(ops.linear_silu_mul(x, gu.w), out=out)
 
     def compute_logits(self, hidden):

@@ -28,15 +28,17 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     return act_and_mul(x, SILU)
 
 
-def silu_mul_fp8_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """SwiGLU followed by per-token 1x128 FP8 (e4m3) group quantisation -> (q, scales)."""
+def silu_mul_fp8_quant(x: torch.Tensor, limit: float = 0.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """SwiGLU (clamped when ``limit`` > 0: gate <= limit, |up| <= limit) followed by per-token
+    1x128 FP8 (e4m3) group quantisation -> (q, scales).  Reference:
+    csrc/musa/quantization/silu_and_mul_per_token_group_fp8_quant.cu:37 (+clamp variant)."""
     I = x.shape[-1] // 2
     if x.is_cuda:
         q = torch.empty(x.shape[0], I, dtype=torch.float8_e4m3fn, device=x.device)
         s = torch.empty(x.shape[0], I // 128, dtype=torch.float32, device=x.device)
-        _ext.ops().silu_mul_fp8_quant(q, s, x)
+        _ext.ops().silu_mul_fp8_quant(q, s, x, limit)
         return q, s
-    return group_quant_fp8(silu_and_mul(x))
+    return group_quant_fp8(act_and_mul(x, SILU, limit) if limit > 0 else silu_and_mul(x))
 
 
 def group_quant_fp8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

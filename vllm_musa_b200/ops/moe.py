@@ -150,7 +150,8 @@ def _fq(x: torch.Tensor) -> torch.Tensor:
     return q.float() * s.repeat_interleave(128, 1)
 
 
-def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_offset):
+def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_offset,
+                       limit=0.0):
     from .fp8 import dequantize_weight_block
     T, H = x.shape
     I2 = w_gu.shape[0] // E
@@ -164,7 +165,10 @@ def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_
         dn = dequantize_weight_block(w_down[e * H:(e + 1) * H],
                                      s_down[e * (H // 128):(e + 1) * (H // 128)])
         hg = (xf[tok] @ gu.t()).to(torch.bfloat16).float()
-        h = _fq((F.silu(hg[:, :I2 // 2]) * hg[:, I2 // 2:]).to(torch.bfloat16))
+        g, u = hg[:, :I2 // 2], hg[:, I2 // 2:]
+        if limit > 0:
+            g, u = g.clamp(max=limit), u.clamp(-limit, limit)
+        h = _fq((F.silu(g) * u).to(torch.bfloat16))
         y = (h @ dn.t()).to(torch.bfloat16).float()
         out.index_add_(0, tok, y * w[tok, slot].unsqueeze(1).float())
     if shared is not None:
@@ -175,7 +179,7 @@ def _fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, E, shared, expert_
 def fused_moe_fp8(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, w_down: torch.Tensor,
                   s_down: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, num_experts: int,
                   shared: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                  expert_offset: int = 0) -> torch.Tensor:
+                  expert_offset: int = 0, swiglu_limit: float = 0.0) -> torch.Tensor:
     """Block-FP8 routed experts (DeepSeek): w_gu e4m3 [E * 2I, H] with rows [gate (I) ; up (I)]
     per expert and 128x128 scales s_gu [E * 2I/128, H/128]; w_down e4m3 [E * H, I], s_down
     [E * H/128, I/128].
@@ -191,7 +195,7 @@ def fused_moe_fp8(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, w_dow
         return out
     if not x.is_cuda:
         out.copy_(_fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, num_experts, shared,
-                                     expert_offset))
+                                     expert_offset, swiglu_limit))
         return out
     from .activation import group_quant_fp8, silu_mul_fp8_quant
     mod = _ext.require()
@@ -212,7 +216,7 @@ def fused_moe_fp8(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, w_dow
     I2 = w_gu.shape[0] // E
     hg = torch.empty(max_rows, I2, dtype=x.dtype, device=dev)
     ops.gemm_fp8(xq, xsc, w_gu, s_gu, hg, 1, None, None, tile_expert, num_tiles, E)
-    hq, hsc = silu_mul_fp8_quant(hg)
+    hq, hsc = silu_mul_fp8_quant(hg, swiglu_limit)
     y = torch.empty(max_rows, H, dtype=x.dtype, device=dev)
     ops.gemm_fp8(hq, hsc, w_down, s_down, y, 1, None, None, tile_expert, num_tiles, E)
     ops.moe_combine(y, pos, w.contiguous(), shared, out, None)
