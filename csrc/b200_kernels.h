@@ -6,6 +6,7 @@
 // asynchronous on the given stream, allocate nothing, and throw std::runtime_error on bad
 // arguments.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -294,6 +295,52 @@ int decode_num_splits(int B, int Hkv, int max_seq_len);
 void run_decode(const DecodeArgs& a, cudaStream_t s);
 void run_prefill(const PrefillArgs& a, cudaStream_t s);
 }  // namespace attn
+
+// --------------------------------------------------------------- TurboQuant KV cache
+// Quantised KV cache: per (token, KV head) one slot of slot_bytes(D, kb, vb) bytes (key codes,
+// value codes, three fp16 scales); csrc/attention/turboquant.cu describes the format.
+namespace tq {
+struct TQStoreArgs {
+  const __nv_bfloat16* k;  // [T, >= Hkv*D] rows (row stride ld_k elements)
+  const __nv_bfloat16* v;
+  int64_t ld_k, ld_v;
+  const int* slot_mapping;  // [T]; < 0 skips the token
+  uint8_t* cache;           // [num_blocks, Hkv, block_size, slot_bytes]
+  int T, Hkv, block_size, num_blocks, slot_bytes;
+  bool norm_correction;
+  int* err;
+};
+struct TQDecodeArgs {
+  const __nv_bfloat16* q;  // [B, >= Hq*D]
+  int64_t ld_q;
+  __nv_bfloat16* out;      // [B, >= Hq*D]
+  int64_t ld_out;
+  const uint8_t* cache;
+  const int* block_tables;  // [B, ld_bt]
+  int ld_bt;
+  const int* seq_lens;      // [B]
+  int B, Hq, Hkv, block_size, num_blocks, slot_bytes;
+  float scale_log2;         // softmax scale * log2(e)
+  int splits;
+  float* ws_o;              // [B, Hq, splits, D] when splits > 1
+  float* ws_lse;            // [B, Hq, splits]
+  int* err;
+};
+struct TQDequantArgs {
+  const uint8_t* cache;
+  const int* block_tables;  // [R, ld_bt]
+  int ld_bt;
+  const int* seq_lens;      // [R]
+  __nv_bfloat16* k_out;     // [R * W, Hkv, block_size, D]
+  __nv_bfloat16* v_out;
+  int R, W, Hkv, block_size, num_blocks, slot_bytes;
+  int* err;
+};
+int slot_bytes(int D, int kb, int vb);
+void run_store(const TQStoreArgs& a, int D, int kb, int vb, cudaStream_t stream);
+void run_decode(const TQDecodeArgs& a, int D, int kb, int vb, cudaStream_t stream);
+void run_dequant(const TQDequantArgs& a, int D, int kb, int vb, cudaStream_t stream);
+}  // namespace tq
 
 namespace mla {
 // Absorbed multi-head latent attention over a [slots, 576] bf16 latent cache (c_kv | k_pe).

@@ -641,6 +641,129 @@ void paged_prefill(const Tensor& q, Tensor& out, const Tensor& k_cache, const Te
   guarded([&] { b200::attn::run_prefill(a, stream_of(q)); });
 }
 
+
+// ---- TurboQuant KV cache ----
+void tq_store(const Tensor& k, const Tensor& v, Tensor& cache, const Tensor& slot_mapping,
+              int64_t key_bits, int64_t value_bits, bool norm_correction) {
+  CHECK_CUDA(k);
+  CHECK_BF16(k);
+  CHECK_BF16(v);
+  CHECK_ROWMAJOR(k);
+  CHECK_ROWMAJOR(v);
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.is_contiguous() && cache.dim() == 4,
+              "tq_store: cache must be contiguous uint8 [blocks, Hkv, block_size, slot]");
+  TORCH_CHECK(slot_mapping.scalar_type() == at::kInt && slot_mapping.is_contiguous(),
+              "tq_store: slot_mapping");
+  const int T = k.size(0), Hkv = cache.size(1);
+  TORCH_CHECK(v.size(0) == T && slot_mapping.numel() >= T, "tq_store: token count");
+  TORCH_CHECK(k.size(1) % Hkv == 0, "tq_store: k width");
+  const int D = k.size(1) / Hkv;
+  TORCH_CHECK(v.size(1) >= Hkv * D, "tq_store: v width");
+  c10::cuda::CUDAGuard g(k.device());
+  b200::tq::TQStoreArgs a{};
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.ld_k = k.stride(0);
+  a.ld_v = v.stride(0);
+  a.slot_mapping = slot_mapping.data_ptr<int>();
+  a.cache = cache.data_ptr<uint8_t>();
+  a.T = T;
+  a.Hkv = Hkv;
+  a.block_size = cache.size(2);
+  a.num_blocks = cache.size(0);
+  a.slot_bytes = cache.size(3);
+  a.norm_correction = norm_correction;
+  a.err = err_ptr(k);
+  guarded([&] { b200::tq::run_store(a, D, key_bits, value_bits, stream_of(k)); });
+}
+
+void tq_decode(const Tensor& q, Tensor& out, const Tensor& cache, const Tensor& block_tables,
+               const Tensor& seq_lens, int64_t Hq, int64_t head_dim, double scale,
+               int64_t key_bits, int64_t value_bits, int64_t num_splits,
+               const c10::optional<Tensor>& ws_o, const c10::optional<Tensor>& ws_lse) {
+  CHECK_CUDA(q);
+  CHECK_BF16(q);
+  CHECK_BF16(out);
+  CHECK_ROWMAJOR(q);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.is_contiguous() && cache.dim() == 4,
+              "tq_decode: cache");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.stride(1) == 1,
+              "tq_decode: block_tables");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.is_contiguous(), "tq_decode: seq_lens");
+  const int B = q.size(0), D = head_dim;
+  TORCH_CHECK(seq_lens.numel() >= B && block_tables.size(0) >= B, "tq_decode: batch");
+  TORCH_CHECK(q.size(1) >= Hq * D && out.size(1) >= Hq * D, "tq_decode: widths");
+  c10::cuda::CUDAGuard g(q.device());
+  b200::tq::TQDecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.ld_q = q.stride(0);
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ld_out = out.stride(0);
+  a.cache = cache.data_ptr<uint8_t>();
+  a.block_tables = block_tables.data_ptr<int>();
+  a.ld_bt = block_tables.stride(0);
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = cache.size(1);
+  a.block_size = cache.size(2);
+  a.num_blocks = cache.size(0);
+  a.slot_bytes = cache.size(3);
+  a.scale_log2 = float(scale * 1.4426950408889634);
+  a.splits = num_splits;
+  if (num_splits > 1) {
+    TORCH_CHECK(ws_o.has_value() && ws_lse.has_value(), "tq_decode: split workspace");
+    TORCH_CHECK(ws_o->scalar_type() == at::kFloat && ws_o->numel() >= int64_t(B) * Hq * num_splits * D,
+                "tq_decode: ws_o too small");
+    TORCH_CHECK(ws_lse->scalar_type() == at::kFloat && ws_lse->numel() >= int64_t(B) * Hq * num_splits,
+                "tq_decode: ws_lse too small");
+    a.ws_o = ws_o->data_ptr<float>();
+    a.ws_lse = ws_lse->data_ptr<float>();
+  }
+  a.err = err_ptr(q);
+  TORCH_CHECK(a.slot_bytes == b200::tq::slot_bytes(D, key_bits, value_bits), "tq_decode: slot size");
+  guarded([&] { b200::tq::run_decode(a, D, key_bits, value_bits, stream_of(q)); });
+}
+
+void tq_dequant(const Tensor& cache, const Tensor& block_tables, const Tensor& seq_lens,
+                Tensor& k_out, Tensor& v_out, int64_t head_dim, int64_t key_bits,
+                int64_t value_bits) {
+  CHECK_CUDA(cache);
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.is_contiguous() && cache.dim() == 4,
+              "tq_dequant: cache");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.stride(1) == 1,
+              "tq_dequant: block_tables");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.is_contiguous(), "tq_dequant: seq_lens");
+  CHECK_BF16(k_out);
+  CHECK_BF16(v_out);
+  const int R = block_tables.size(0), Hkv = cache.size(1), bs = cache.size(2), D = head_dim;
+  TORCH_CHECK(k_out.is_contiguous() && v_out.is_contiguous() && k_out.dim() == 4 &&
+                  k_out.size(0) % std::max(R, 1) == 0 && k_out.size(1) == Hkv &&
+                  k_out.size(2) == bs && k_out.size(3) == D && v_out.sizes() == k_out.sizes(),
+              "tq_dequant: outputs must be [R * W, Hkv, block_size, D]");
+  c10::cuda::CUDAGuard g(cache.device());
+  b200::tq::TQDequantArgs a{};
+  a.cache = cache.data_ptr<uint8_t>();
+  a.block_tables = block_tables.data_ptr<int>();
+  a.ld_bt = block_tables.stride(0);
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.k_out = reinterpret_cast<__nv_bfloat16*>(k_out.data_ptr());
+  a.v_out = reinterpret_cast<__nv_bfloat16*>(v_out.data_ptr());
+  a.R = R;
+  a.W = R ? k_out.size(0) / R : 0;
+  TORCH_CHECK(a.W <= block_tables.size(1), "tq_dequant: more pages than block-table columns");
+  a.Hkv = Hkv;
+  a.block_size = bs;
+  a.num_blocks = cache.size(0);
+  a.slot_bytes = cache.size(3);
+  a.err = err_ptr(cache);
+  TORCH_CHECK(a.slot_bytes == b200::tq::slot_bytes(D, key_bits, value_bits), "tq_dequant: slot size");
+  guarded([&] { b200::tq::run_dequant(a, D, key_bits, value_bits, stream_of(cache)); });
+}
+
+int64_t tq_slot_bytes(int64_t D, int64_t kb, int64_t vb) { return b200::tq::slot_bytes(D, kb, vb); }
+
 int64_t decode_num_splits(int64_t B, int64_t Hkv, int64_t max_seq_len) {
   return b200::attn::decode_num_splits(B, Hkv, max_seq_len);
 }
@@ -1219,6 +1342,16 @@ TORCH_LIBRARY(b200, m) {
       "Tensor? workspace=None, int mt=0, Tensor(b!)? counters=None) -> ()");
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps, bool gemma=False) -> ()");
   m.def(
+      "tq_store(Tensor k, Tensor v, Tensor(a!) cache, Tensor slot_mapping, int key_bits, "
+      "int value_bits, bool norm_correction) -> ()");
+  m.def(
+      "tq_decode(Tensor q, Tensor(a!) out, Tensor cache, Tensor block_tables, Tensor seq_lens, "
+      "int Hq, int head_dim, float scale, int key_bits, int value_bits, int num_splits, "
+      "Tensor(b!)? ws_o, Tensor(c!)? ws_lse) -> ()");
+  m.def(
+      "tq_dequant(Tensor cache, Tensor block_tables, Tensor seq_lens, Tensor(a!) k_out, "
+      "Tensor(b!) v_out, int head_dim, int key_bits, int value_bits) -> ()");
+  m.def(
       "fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor weight, float eps, "
       "bool gemma=False) -> ()");
   m.def(
@@ -1314,6 +1447,9 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("group_quant_fp8", &group_quant_fp8);
   m.impl("rope_kv", &rope_kv);
   m.impl("paged_decode", &paged_decode);
+  m.impl("tq_store", &tq_store);
+  m.impl("tq_decode", &tq_decode);
+  m.impl("tq_dequant", &tq_dequant);
   m.impl("paged_prefill", &paged_prefill);
   m.impl("sample", &sample);
   m.impl("merge_candidates", &merge_candidates);
@@ -1352,6 +1488,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "select the tcgen05 (true) or mma.sync (false) prefill attention kernel for head_dim 128");
   m.def("gemm_fp8_plan", &gemm_fp8_plan, "automatic (splits, workspace_floats, counters) for fp8");
   m.def("decode_num_splits", &decode_num_splits, "split-KV count for a decode batch");
+  m.def("tq_slot_bytes", &tq_slot_bytes, "TurboQuant slot bytes for (head_dim, key_bits, value_bits)");
   m.def("moe_max_rows", [](int64_t n, int64_t E) { return (int64_t)b200::moe::align_max_rows(n, E); },
         "rows of the expert-sorted buffer for n assignments over E experts");
   m.def("error_word", &error_word, "per-device error word of the bounded waits");

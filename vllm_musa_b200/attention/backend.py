@@ -86,3 +86,51 @@ class TreeAttention(PagedAttention):
         return ops.paged_prefill(q, k_cache, v_cache, cu_q, seq_lens, block_tables, self.hq,
                                  self.hkv, self.scale, out=out, sinks=self.sinks,
                                  tree_mask=tree_mask)
+
+
+class TurboQuantAttention(PagedAttention):
+    """Attention over the TurboQuant quantised KV cache (``kv_cache_dtype`` turboquant_k8v4 /
+    turboquant_4bit_nc / turboquant_k3v4_nc / turboquant_3bit_nc; format in
+    csrc/attention/turboquant.cu).  Decode rows run ``tq_decode_kernel`` straight on the packed
+    slots (q rotated in-kernel for the Hadamard-rotated keys); prefill rows dequantise the pages
+    they read into a bf16 scratch cache and run the paged prefill kernel, so a prompt attends
+    to the same quantised keys and values that its later decode steps see.  Like the
+    reference's backend (vllm_musa/v1/attention/backends/turboquant.py:37-114) it takes no
+    attention sinks, MLA or sparse attention; sliding windows are refused too."""
+
+    def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, kv_cache_dtype: str,
+                 scale: float | None = None, sliding_window: int = 0,
+                 sinks: torch.Tensor | None = None):
+        if sinks is not None:
+            raise ValueError("TurboQuant KV cache does not support attention sinks")
+        if sliding_window:
+            raise ValueError("TurboQuant KV cache does not support sliding-window attention")
+        super().__init__(num_heads, num_kv_heads, head_dim, scale)
+        from ..ops.turboquant import tq_format
+        self.fmt = tq_format(kv_cache_dtype, head_dim)
+
+    def write_kv(self, k: torch.Tensor, v: torch.Tensor, cache: torch.Tensor,
+                 slot_mapping: torch.Tensor) -> None:
+        from ..ops.turboquant import tq_store
+        tq_store(k, v, cache, slot_mapping, self.fmt)
+
+    def forward(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None,
+                meta: AttnMetadata, out: torch.Tensor | None = None) -> torch.Tensor:
+        """q: [T, >= Hq*D]; ``k_cache`` is the packed uint8 cache (``v_cache`` unused)."""
+        from ..ops.turboquant import tq_decode, tq_dequant_pages
+        T = q.shape[0]
+        if out is None:
+            out = torch.empty(T, self.hq * self.d, dtype=q.dtype, device=q.device)
+        nd, npf = meta.num_decodes, meta.num_prefills
+        if nd:
+            tq_decode(q[:nd], k_cache, meta.block_tables[:nd], meta.seq_lens[:nd], self.hq,
+                      self.scale, self.fmt, out=out[:nd], num_splits=meta.decode_splits)
+        if npf:
+            bs = k_cache.shape[2]
+            pages = max(1, -(-int(meta.max_seq_len) // bs))
+            pages = min(pages, meta.prefill_block_tables.shape[1])
+            kd, vd, bt = tq_dequant_pages(k_cache, meta.prefill_block_tables,
+                                          meta.prefill_seq_lens, self.fmt, pages)
+            ops.paged_prefill(q, kd, vd, meta.prefill_cu_q, meta.prefill_seq_lens, bt, self.hq,
+                              self.hkv, self.scale, 0, out=out, tile_scratch=meta.tile_scratch)
+        return out

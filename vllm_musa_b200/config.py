@@ -68,6 +68,9 @@ class ModelConfig:
     attn_output_gate: bool = False
     # clamped SwiGLU (gate <= limit, |up| <= limit) in MLPs and experts; 0: plain SwiGLU
     swiglu_limit: float = 0.0
+    # KV cache storage: "auto" (model dtype) or a TurboQuant preset (turboquant_k8v4,
+    # turboquant_4bit_nc, turboquant_k3v4_nc, turboquant_3bit_nc)
+    kv_cache_dtype: str = "auto"
     # Mamba2 (state-space) mixers
     ssm_state_size: int = 0
     mamba_num_heads: int = 0

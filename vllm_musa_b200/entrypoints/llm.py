@@ -42,7 +42,8 @@ class LLM:
                  enforce_eager: bool = False, seed: int = 0, load_format: Optional[str] = None,
                  device: str = "cuda", dtype=None, tokenizer=None,
                  cuda_graph_sizes: Optional[list] = None, num_layers: Optional[int] = None,
-                 speculative_config: Optional[dict] = None, **unused):
+                 speculative_config: Optional[dict] = None,
+                 kv_cache_dtype: Optional[str] = None, **unused):
         path = None
         if isinstance(model, ModelConfig):
             mcfg = model
@@ -57,6 +58,8 @@ class LLM:
             mcfg.dtype = dtype
         if num_layers is not None:
             mcfg.num_layers = num_layers
+        if kv_cache_dtype is not None:
+            mcfg.kv_cache_dtype = kv_cache_dtype
         if load_format is None:
             load_format = "safetensors" if path else "dummy"
         mlen = max_model_len or min(mcfg.max_position, 8192)

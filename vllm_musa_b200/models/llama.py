@@ -90,7 +90,16 @@ class DenseDecoderForCausalLM:
         self.embed = None
         self.final_norm = None
         self.lm_head = None
-        self.attn = PagedAttention(self.hq, self.hkv, self.D)
+        self.tq = None
+        if cfg.kv_cache_dtype not in ("auto", None, "bf16", "bfloat16"):
+            from ..attention import TurboQuantAttention
+            self.attn = TurboQuantAttention(self.hq, self.hkv, self.D, cfg.kv_cache_dtype)
+            self.tq = self.attn.fmt
+            # model-defined cache: one packed uint8 cache per layer (the runner asks for these)
+            self.allocate_kv_cache = self._tq_allocate_kv_cache
+            self.kv_bytes_per_block = self._tq_kv_bytes_per_block
+        else:
+            self.attn = PagedAttention(self.hq, self.hkv, self.D)
         self.cos_sin = ops.build_cos_sin_cache(cfg.rot_dim, cfg.max_position, cfg.rope_theta,
                                                device=self.device, scaling=cfg.rope_scaling)
         self._staging = defaultdict(dict)
@@ -202,8 +211,18 @@ class DenseDecoderForCausalLM:
         for i, L in enumerate(self.layers):
             kc, vc = kv_caches[i]
             qkv = ops.linear(x, L.qkv_w)
-            ops.rope_kv(qkv, meta.positions, self.cos_sin, kc, vc, meta.slot_mapping, self.hq,
-                        self.hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm, eps)
+            if self.tq is not None:
+                D, hq, hkv = self.D, self.hq, self.hkv
+                ops.rope_kv(qkv, meta.positions, self.cos_sin, None, None, meta.slot_mapping,
+                            hq, hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm, eps,
+                            write_k=True, head_dim=D)
+                self.attn.write_kv(qkv[:, hq * D:(hq + hkv) * D],
+                                   qkv[:, (hq + hkv) * D:(hq + 2 * hkv) * D], kc,
+                                   meta.slot_mapping)
+            else:
+                ops.rope_kv(qkv, meta.positions, self.cos_sin, kc, vc, meta.slot_mapping,
+                            self.hq, self.hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm,
+                            eps)
             a = self.attn.forward(qkv, kc, vc, meta)
             x, residual = self.comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
             nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
@@ -229,6 +248,15 @@ class DenseDecoderForCausalLM:
         return ops.linear(hidden, self.lm_head, out_dtype=torch.float32)
 
     # ------------------------------------------------------------------ KV cache geometry
+    def _tq_kv_bytes_per_block(self, block_size: int) -> int:
+        return self.cfg.num_layers * self.hkv * block_size * self.tq.slot_bytes
+
+    def _tq_allocate_kv_cache(self, num_blocks: int, block_size: int) -> list:
+        """TurboQuant cache per layer: uint8 [num_blocks, Hkv, block_size, slot_bytes]."""
+        buf = torch.zeros(self.cfg.num_layers, num_blocks, self.hkv, block_size,
+                          self.tq.slot_bytes, dtype=torch.uint8, device=self.device)
+        return [(buf[i], None) for i in range(self.cfg.num_layers)]
+
     def kv_cache_spec(self) -> dict:
         return {"num_layers": self.cfg.num_layers, "num_kv_heads": self.hkv,
                 "head_dim": self.D, "dtype": self.dtype}

@@ -47,6 +47,7 @@ class Feature(str, Enum):
     MTP = "spec.mtp"
     GDN_CHUNKED_PREFILL = "gdn.chunked_prefill"
     W4AFP8_EXPERTS = "moe.w4afp8_experts"
+    TURBOQUANT_KV = "attn.turboquant_kv_cache"
 
 
 @dataclass(frozen=True)
@@ -64,6 +65,7 @@ class ModelSignature:
     uses_mla: bool
     sparse_attention: bool
     recurrent_state: bool
+    kv_cache_dtype: str = "auto"
 
 
 @dataclass(frozen=True)
@@ -120,7 +122,8 @@ def model_signature(cfg) -> ModelSignature:
         num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
         num_experts=cfg.num_experts, uses_mla=cfg.kv_lora_rank > 0,
         sparse_attention=cfg.index_topk > 0,
-        recurrent_state=fam in (ModelFamily.HYBRID_GDN, ModelFamily.SSM))
+        recurrent_state=fam in (ModelFamily.HYBRID_GDN, ModelFamily.SSM),
+        kv_cache_dtype=getattr(cfg, "kv_cache_dtype", "auto") or "auto")
 
 
 def execution_signature(config) -> ExecutionSignature:
@@ -178,6 +181,8 @@ def resolve(config) -> OptimizationContract:
         both(Feature.W4AFP8_EXPERTS)
     if m.family == ModelFamily.HYBRID_GDN and cuda:
         both(Feature.GDN_CHUNKED_PREFILL)
+    if m.kv_cache_dtype.startswith("turboquant") and m.family == ModelFamily.DENSE:
+        both(Feature.TURBOQUANT_KV)
     parts = [m.family.value, m.quant or m.dtype, f"tp{tp}"]
     if e.data_parallel_size > 1:
         parts.append(f"dp{e.data_parallel_size}")
@@ -193,5 +198,11 @@ def validate(contract: OptimizationContract) -> None:
     m, e = contract.model, contract.execution
     if e.decode_context_parallel_size > 1 and not m.uses_mla:
         raise ValueError("decode context parallelism is implemented for MLA (DeepSeek) models")
+    if m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
+        if not m.kv_cache_dtype.startswith("turboquant"):
+            raise ValueError(f"kv_cache_dtype {m.kv_cache_dtype!r} is not served")
+        if m.family != ModelFamily.DENSE or m.uses_mla:
+            raise ValueError("the TurboQuant KV cache serves the dense decoders (no MLA, "
+                             "recurrent or MoE families)")
     if e.speculative_method == "mtp" and m.family != ModelFamily.DEEPSEEK:
         raise ValueError("MTP speculative decoding needs a DeepSeek multi-token-prediction layer")
