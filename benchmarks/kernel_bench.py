@@ -132,6 +132,29 @@ def case_attn_decode(it):
            4 * B * ctx * Hq * D)
 
 
+def case_tq_decode(it):
+    """TurboQuant-cache decode (turboquant_4bit_nc, 144-byte slots): bytes = packed slots read."""
+    from vllm_musa_b200.ops import turboquant as tq
+    B, ctx, Hq, Hkv, D, bs = 256, 1152, 32, 8, 128, 64
+    fmt = tq.tq_format("turboquant_4bit_nc", D)
+    nb = B * ctx // bs
+    cache = torch.randint(0, 256, (nb, Hkv, bs, fmt.slot_bytes), dtype=torch.uint8,
+                          device="cuda")
+    m = fmt.meta_offset  # valid fp16 scales in every slot
+    cache[..., m:m + 6] = torch.tensor([0.01, 0.02, -0.1], dtype=torch.float16).view(
+        torch.uint8).cuda()
+    bt = torch.arange(nb, dtype=torch.int32, device="cuda").reshape(B, ctx // bs)
+    q = bf16(B, Hq * D)
+    seq = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq * D, dtype=torch.bfloat16, device="cuda")
+    splits = tq.decode_splits(B, Hkv, ctx)
+    ops.attention.decode_workspace(q.device, B, Hq, D, splits)
+    us = timed(lambda i: tq.tq_decode(q, cache, bt, seq, Hq, D ** -0.5, fmt, out=out,
+                                      num_splits=splits), it)
+    report("tq_decode", [B, ctx, Hq, Hkv, D], us, B * ctx * Hkv * fmt.slot_bytes,
+           4 * B * ctx * Hq * D)
+
+
 def case_attn_prefill(it):
     R, L, Hq, Hkv, D = 8, 1024, 32, 8, 128
     k, v, bt = _paged(R, L, Hkv, D)
