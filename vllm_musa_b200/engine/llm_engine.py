@@ -99,12 +99,7 @@ class LLMEngine:
         cls = get_model_class(mcfg)
         self.model = cls(mcfg, st, self.comm, device)
         t0 = time.time()
-        if config.load_format == "dummy":
-            gdev = "cuda" if device.type == "cuda" else "cpu"
-            self.model.load_weights(dummy_weights(mcfg, config.seed, config.init_std,
-                                                  device=str(device) if gdev == "cuda" else "cpu"))
-        else:
-            self.model.load_weights(safetensors_weights(config.model_path))
+        self._load_weights()
         log.info("weights ready in %.1fs", time.time() - t0)
         self.sampler = Sampler(self.comm, getattr(self.model, "vocab_start", 0), st.tp_size)
         dcp = config.parallel.decode_context_parallel_size
@@ -137,7 +132,11 @@ class LLMEngine:
                              and self.contract.prefers(plan.Feature.PREFIX_CACHING)
                              and not hasattr(self.model, "allocate_state"))
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
+        self._sched_cfg = sc
         self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
+        self.sleep_level = 0
+        self._offloaded: list = []
+        self._profiler = None
         if config.speculative.method == "mtp":
             from .spec_decode import MTPDrafter
             self.drafter = MTPDrafter(self, config.speculative.num_speculative_tokens or 1)
@@ -326,6 +325,128 @@ class LLMEngine:
             self.sync.record(("shutdown",))
             self.sync.exchange()
             self.sync = None
+
+    def _load_weights(self) -> None:
+        cfg, mcfg, device = self.config, self.config.model, self.device
+        if cfg.load_format == "dummy":
+            dev = str(device) if device.type == "cuda" else "cpu"
+            self.model.load_weights(dummy_weights(mcfg, cfg.seed, cfg.init_std, device=dev))
+        else:
+            self.model.load_weights(safetensors_weights(cfg.model_path))
+
+    # ------------------------------------------------------------------ sleep mode
+    def _weight_tensors(self) -> list:
+        """Every tensor the model object graph holds on the engine's device (weights, rotary
+        tables), unique by identity.  Communicator / parallel-state objects are not walked:
+        their peer-mapped buffers must stay where the other ranks mapped them."""
+        out, seen, stack = [], set(), [self.model]
+        while stack:
+            o = stack.pop()
+            if id(o) in seen:
+                continue
+            seen.add(id(o))
+            if isinstance(o, torch.Tensor):
+                if o.device == self.device and o.numel():
+                    out.append(o)
+            elif isinstance(o, (list, tuple)):
+                stack.extend(o)
+            elif isinstance(o, dict):
+                stack.extend(o.values())
+            elif type(o).__module__.startswith(("vllm_musa_b200.models", "vllm_musa_b200.attention")):
+                if hasattr(o, "__dict__"):
+                    stack.extend(vars(o).values())
+                for slot in getattr(type(o), "__slots__", ()):
+                    stack.append(getattr(o, slot, None))
+        return out
+
+    def sleep(self, level: int = 1) -> None:
+        """Give the GPU memory back while the engine idles: level 1 copies the weights to
+        host memory, level 2 discards them (``wake_up`` loads them again); both release the
+        KV cache and the CUDA graphs (their contents are discarded, the prefix cache starts
+        empty after waking).  Reference: the platform declares vLLM's sleep mode available
+        (vllm_musa/platform.py:274-276).  Only between requests; recurrent-state models
+        (Qwen3-Next, Mamba2) keep their state buffers and are refused."""
+        if level not in (1, 2):
+            raise ValueError("sleep level must be 1 or 2")
+        if self.sleep_level:
+            return
+        if self.has_unfinished_requests():
+            raise RuntimeError("sleep() needs an idle engine (requests still running)")
+        if hasattr(self.model, "allocate_state"):
+            raise NotImplementedError("sleep mode does not cover recurrent-state models")
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        self.runner.release_graphs()
+        self._offloaded = []
+        self._discarded = []
+        for t in self._weight_tensors():
+            # level 2 discards the large tensors (the checkpoint weights, which the loader
+            # re-creates); small ones (norms, rotary tables) are kept on the host either way
+            if level == 1 or t.numel() * t.element_size() < (16 << 20):
+                host = torch.empty(t.shape, dtype=t.dtype, pin_memory=t.is_cuda)
+                host.copy_(t)
+                self._offloaded.append((t, host))
+            else:
+                self._discarded.append(t)
+            t.data = torch.empty(0, dtype=t.dtype, device=t.device)
+        self.runner.kv_caches = []
+        self.runner.kv_tensor = None
+        self.sleep_level = level
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+        log.info("engine asleep (level %d)", level)
+
+    def wake_up(self) -> None:
+        """Undo ``sleep``: weights back (host copy or a fresh load), a new KV cache of the same
+        block count, a fresh scheduler (empty prefix cache) and re-captured CUDA graphs."""
+        if not self.sleep_level:
+            return
+        for t, host in self._offloaded:
+            t.data = host.to(self.device, non_blocking=False)
+        self._offloaded = []
+        if self.sleep_level == 2:
+            self._load_weights()
+            live = {id(t) for t in self._weight_tensors()}
+            # a discarded tensor the loader did not replace is still reachable (and empty)
+            lost = [t for t in self._discarded if id(t) in live]
+            self._discarded = []
+            if lost:
+                raise RuntimeError(f"wake_up: {len(lost)} discarded tensors were not re-created "
+                                   "by the weight loader; use sleep(level=1) for this model")
+        self.runner.allocate_kv(self.num_blocks)
+        from .. import _C_runtime
+        self.scheduler = _C_runtime.Scheduler(self._sched_cfg, self.num_blocks,
+                                              self.runner.buf.pointers())
+        self.sleep_level = 0
+        self.runner.capture_graphs()
+        log.info("engine awake")
+
+    # ------------------------------------------------------------------ profiling
+    def start_profile(self) -> None:
+        """torch.profiler over the following steps (CPU ops + CUDA kernels); ``stop_profile``
+        writes a Chrome trace per rank under ``B200_TORCH_PROFILER_DIR``.  Reference: the
+        reference extends vLLM's torch profiler with its device activity."""
+        import torch.profiler as tp
+        acts = [tp.ProfilerActivity.CPU]
+        if self.device.type == "cuda":
+            acts.append(tp.ProfilerActivity.CUDA)
+        self._profiler = tp.profile(activities=acts)
+        self._profiler.__enter__()
+
+    def stop_profile(self) -> Optional[str]:
+        if self._profiler is None:
+            return None
+        from .. import envs
+        prof, self._profiler = self._profiler, None
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        prof.__exit__(None, None, None)
+        d = envs.FLAGS["B200_TORCH_PROFILER_DIR"].get()
+        os.makedirs(d, exist_ok=True)
+        rank = torch.distributed.get_rank() if torch.distributed.is_initialized() else 0
+        path = os.path.join(d, f"trace_rank{rank}_{int(time.time() * 1000)}.json")
+        prof.export_chrome_trace(path)
+        return path
 
     # ------------------------------------------------------------------ lifecycle
     def shutdown(self) -> None:

@@ -167,6 +167,21 @@ class LLM:
                 res[i] = out
         return res
 
+    def sleep(self, level: int = 1) -> None:
+        """Release GPU memory while idle (level 1: weights to host memory; level 2: weights
+        discarded and reloaded by ``wake_up``); the KV cache is released in both."""
+        self.engine.sleep(level)
+
+    def wake_up(self) -> None:
+        self.engine.wake_up()
+
+    def start_profile(self) -> None:
+        self.engine.start_profile()
+
+    def stop_profile(self):
+        """Stop the profiler; returns the path of this rank's Chrome trace."""
+        return self.engine.stop_profile()
+
     def shutdown(self):
         self.engine.shutdown()
         if self.executor is not None:

@@ -55,6 +55,8 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
     EnvFlag("B200_CUSTOM_OP_USE_NATIVE", False, _bool,
             "vLLM plugin: register the custom ops but route them to the PyTorch implementations"),
     EnvFlag("B200_LOG_LEVEL", "INFO", str, "logging level of the vllm_musa_b200 logger"),
+    EnvFlag("B200_TORCH_PROFILER_DIR", "b200_traces", str,
+            "directory of the Chrome traces written by LLM.stop_profile()"),
 ]}
 
 
