@@ -126,8 +126,10 @@ B200_DEVICE float fp8_to_float(uint32_t byte) {
 }
 
 // Dequantise this lane's E key coordinates.  MSE keys come back in the ROTATED space.
+// Per-lane level indices differ, so the table is read from shared memory (`lv`): divergent
+// __constant__ reads would serialise across the warp.
 template <int E, int KB>
-B200_DEVICE void load_key(const uint32_t* sw, int lane, float ksc, float (&k)[E]) {
+B200_DEVICE void load_key(const uint32_t* sw, int lane, float ksc, const float* lv, float (&k)[E]) {
   if constexpr (KB == 8) {
 #pragma unroll
     for (int c = 0; c < E; c += 4) {
@@ -141,7 +143,7 @@ B200_DEVICE void load_key(const uint32_t* sw, int lane, float ksc, float (&k)[E]
   } else {
     const uint32_t bits = get_bits(sw, E * lane * KB, E * KB);
 #pragma unroll
-    for (int e = 0; e < E; ++e) k[e] = level<KB>((bits >> (e * KB)) & ((1u << KB) - 1u)) * ksc;
+    for (int e = 0; e < E; ++e) k[e] = lv[(bits >> (e * KB)) & ((1u << KB) - 1u)] * ksc;
   }
 }
 
@@ -158,6 +160,11 @@ template <int D, int KB, int VB>
 __global__ void __launch_bounds__(256) tq_store_kernel(TQStoreArgs a) {
   constexpr int E = D / 32;
   constexpr int L = (1 << VB) - 1;
+  __shared__ float s_lv[16];
+  if constexpr (KB != 8) {
+    if (threadIdx.x < (1 << KB)) s_lv[threadIdx.x] = level<KB>(threadIdx.x);
+    __syncthreads();
+  }
   extern __shared__ uint32_t tq_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int t = blockIdx.x;
@@ -210,7 +217,7 @@ __global__ void __launch_bounds__(256) tq_store_kernel(TQStoreArgs a) {
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         const int c = nearest_level<KB>(kx[e] * rs * zmul);
-        const float lv = level<KB>(c);
+        const float lv = s_lv[c];
         cs += lv * lv;
         put_bits(w, (E * lane + e) * KB, uint32_t(c), KB);
       }
@@ -254,6 +261,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) tq_decode_kernel(TQDecodeAr
   constexpr int E = D / 32;
   __shared__ float s_m[kDecodeWarps][kMaxGroup], s_l[kDecodeWarps][kMaxGroup];
   __shared__ float s_acc[kDecodeWarps][kMaxGroup][D];
+  __shared__ float s_lv[16];
+  if constexpr (KB != 8) {
+    if (threadIdx.x < (1 << KB)) s_lv[threadIdx.x] = level<KB>(threadIdx.x);
+    __syncthreads();
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
   const int G = a.Hq / a.Hkv;
@@ -298,7 +310,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) tq_decode_kernel(TQDecodeAr
         a.cache + ((int64_t(blk) * a.Hkv + h) * a.block_size + (t % a.block_size)) * a.slot_bytes);
     const float ksc = half_at(sw, meta), vsc = half_at(sw, meta + 2), vz = half_at(sw, meta + 4);
     float k[E], v[E];
-    load_key<E, KB>(sw, lane, ksc, k);
+    load_key<E, KB>(sw, lane, ksc, s_lv, k);
     load_value<E, VB>(sw, key_bytes, lane, vsc, vz, v);
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) {
@@ -382,6 +394,11 @@ __global__ void tq_combine_kernel(TQDecodeArgs a, int D) {
 template <int D, int KB, int VB>
 __global__ void __launch_bounds__(256) tq_dequant_kernel(TQDequantArgs a) {
   constexpr int E = D / 32;
+  __shared__ float s_lv[16];
+  if constexpr (KB != 8) {
+    if (threadIdx.x < (1 << KB)) s_lv[threadIdx.x] = level<KB>(threadIdx.x);
+    __syncthreads();
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int r = blockIdx.x / a.W, wi = blockIdx.x % a.W;
   const int S = a.seq_lens[r];
@@ -401,7 +418,7 @@ __global__ void __launch_bounds__(256) tq_dequant_kernel(TQDequantArgs a) {
         a.cache + ((int64_t(blk) * a.Hkv + h) * a.block_size + off) * a.slot_bytes);
     const float ksc = half_at(sw, meta), vsc = half_at(sw, meta + 2), vz = half_at(sw, meta + 4);
     float k[E], v[E];
-    load_key<E, KB>(sw, lane, ksc, k);
+    load_key<E, KB>(sw, lane, ksc, s_lv, k);
     load_value<E, VB>(sw, key_bytes, lane, vsc, vz, v);
     if constexpr (KB != 8) {
       warp_fwht<E>(k, lane);
