@@ -2,6 +2,7 @@
 // The split partials (fp32 O and log-sum-exp per (sequence, head, split)) are written to a
 // file-scope device array instead of a caller-provided workspace; the attention kernels are
 // the same ones paged_decode launches (paged_attention.cu).
+#include <stdint.h>
 #include <stdio.h>
 
 #include <exception>
@@ -52,6 +53,19 @@ extern "C" int b200_paged_decode_noalloc(const void* q, int64_t ld_q, void* out,
   if (!q || !out || !k_cache || !v_cache || !block_tables || !seq_lens || batch < 0 ||
       num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || num_splits < 1 ||
       max_seq_len < 1 || num_blocks < 1)
+    return B200_NOALLOC_ERR_ARGS;
+  // geometry the decode kernels serve (checked here so that a bad argument is reported as
+  // such, before anything is queued on the stream)
+  if (num_q_heads % num_kv_heads != 0 || num_q_heads / num_kv_heads > 16)
+    return B200_NOALLOC_ERR_ARGS;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return B200_NOALLOC_ERR_ARGS;
+  if (block_size < 16 || block_size % 16 != 0 || (block_size > 64 && block_size % 64 != 0))
+    return B200_NOALLOC_ERR_ARGS;
+  if (ld_q < (int64_t)num_q_heads * head_dim ||
+      ld_out < (int64_t)num_q_heads * head_dim || bt_stride < 1)
+    return B200_NOALLOC_ERR_ARGS;
+  // the caches are read by TMA: 16-byte aligned base addresses
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0)
     return B200_NOALLOC_ERR_ARGS;
   // scratch layout: partial O [batch, Hq, splits, D] fp32, 256-byte aligned LSE after it
   const size_t o_bytes = (size_t)batch * num_q_heads * num_splits * head_dim * sizeof(float);

@@ -1,14 +1,13 @@
 // Allocation-free C entry point for split-KV paged decode attention.
 //
 // This entry point has no counterpart in the reference (MooreThreads/vllm-musa).  It exists
-// for callers that cannot allocate GPU memory while they run attention: code executing
-// inside a host callback or stream callback (where CUDA API allocation calls are not
-// permitted), hosts that hand this library a fixed device-memory budget and forbid it from
-// growing (inference servers with their own allocator, embedded / real-time deployments),
-// and foreign-language runtimes that link the shared library with no PyTorch allocator.
-// Instead of a caller- or torch-allocated workspace, the split-KV partial results live in a
-// file-scope device array of B200_DECODE_NOALLOC_SCRATCH_BYTES (16 MiB), which every GPU that
-// loads the library keeps until the process exits.
+// for callers that cannot allocate GPU memory while they run attention: hosts that hand this
+// library a fixed device-memory budget and forbid it from growing (inference servers with
+// their own allocator, embedded / real-time deployments that reserve all memory up front),
+// and foreign-language runtimes that link the shared library with no PyTorch allocator to
+// draw a workspace from.  Instead of a caller- or torch-allocated workspace, the split-KV
+// partial results live in a file-scope device array of B200_DECODE_NOALLOC_SCRATCH_BYTES
+// (16 MiB), which every GPU that loads the library keeps until the process exits.
 //
 // Usage notes:
 //  * The first call on a device performs set-up for that device (it looks up the scratch
@@ -33,7 +32,10 @@
 #define B200_NOALLOC_OK 0
 #define B200_NOALLOC_ERR_TOO_LARGE 1  // split partials would exceed the scratch array
 #define B200_NOALLOC_ERR_SETUP 2      // no current device / symbol address lookup failed
-#define B200_NOALLOC_ERR_ARGS 3       // null pointer or unsupported geometry
+#define B200_NOALLOC_ERR_ARGS 3       // null / misaligned pointer or unsupported geometry:
+                                      // head_dim not 64, 128 or 256; num_q_heads not a multiple
+                                      // of num_kv_heads or a GQA group above 16; block_size not
+                                      // 16, 32, 64 or a multiple of 64
 #define B200_NOALLOC_ERR_LAUNCH 4     // the kernel launch failed
 
 #ifdef __cplusplus

@@ -36,7 +36,8 @@ import torch.fx as fx
 _LIB = torch.library.Library("b200fx", "DEF")
 _LIB.define("all_reduce(Tensor x) -> Tensor")
 _LIB.define("fused_add_rms_norm(Tensor x, Tensor residual, Tensor w, float eps) -> (Tensor, Tensor)")
-_LIB.define("allreduce_add_rms_norm(Tensor x, Tensor residual, Tensor w, float eps) -> (Tensor, Tensor)")
+_LIB.define("allreduce_add_rms_norm(Tensor x, Tensor residual, Tensor w, float eps, "
+            "str? group_name=None) -> (Tensor, Tensor)")
 _LIB.define("silu_and_mul(Tensor x) -> Tensor")
 _LIB.define("group_quant_fp8(Tensor x) -> (Tensor, Tensor)")
 _LIB.define("silu_mul_fp8_quant(Tensor x) -> (Tensor, Tensor)")
@@ -45,18 +46,36 @@ _LIB.define("rms_norm_quant_fp8(Tensor x, Tensor w, float eps) -> (Tensor, Tenso
 _LIB.define("add_rms_norm_quant_fp8(Tensor x, Tensor residual, Tensor w, float eps) "
             "-> (Tensor, Tensor, Tensor)")
 
-_COMM: Optional[object] = None  # TP communicator used by the fused all-reduce op
+# TP communicators the fused all-reduce op may use, by the name of the process group whose
+# all-reduce the pass replaced (None: this package's own b200fx.all_reduce).  A graph whose
+# group has no communicator bound keeps the group's own all-reduce (vLLM's, by group name):
+# the rewrite never drops a reduction.
+_COMMS: dict = {}
 
 
-def set_communicator(comm) -> None:
-    global _COMM
-    _COMM = comm
+def set_communicator(comm, group_name: Optional[str] = None) -> None:
+    """Bind ``comm`` (a TPCommunicator) to the all-reduces of ``group_name``."""
+    if comm is None:
+        _COMMS.pop(group_name, None)
+    else:
+        _COMMS[group_name] = comm
+
+
+def _bound(group_name: Optional[str] = None):
+    c = _COMMS.get(group_name)
+    return c if c is not None and getattr(c, "world", 1) > 1 else None
+
+
+def _vllm_all_reduce(x, group_name: str):
+    """vLLM's own all-reduce over the named group (the op the fusion replaced)."""
+    return torch.ops.vllm.all_reduce(x, group_name)
 
 
 def _all_reduce(x):
-    if _COMM is None or getattr(_COMM, "world", 1) == 1:
+    c = _bound(None)
+    if c is None:
         return x.clone()
-    return _COMM.all_reduce(x.clone())
+    return c.all_reduce(x.clone())
 
 
 def _fused_add_rms_norm(x, residual, w, eps):
@@ -65,10 +84,12 @@ def _fused_add_rms_norm(x, residual, w, eps):
     return ops.rms_norm(r, w, eps), r
 
 
-def _allreduce_add_rms_norm(x, residual, w, eps):
-    if _COMM is not None and getattr(_COMM, "world", 1) > 1:
-        out, res = _COMM.allreduce_add_rmsnorm(x.clone(), residual.clone(), w, eps)
+def _allreduce_add_rms_norm(x, residual, w, eps, group_name=None):
+    c = _bound(group_name)
+    if c is not None:
+        out, res = c.allreduce_add_rmsnorm(x.clone(), residual.clone(), w, eps)
         return out.clone(), res
+    x = _vllm_all_reduce(x, group_name) if group_name is not None else _all_reduce(x)
     return _fused_add_rms_norm(x, residual, w, eps)
 
 
@@ -117,7 +138,13 @@ for _name, _fn in (("all_reduce", _all_reduce), ("fused_add_rms_norm", _fused_ad
 # Matching helpers
 # --------------------------------------------------------------------------------------------
 ALL_REDUCE = ("b200fx.all_reduce", "vllm.all_reduce")
-ADD_RMS = ("b200fx.fused_add_rms_norm", "_C.fused_add_rms_norm")
+# functional add + RMSNorm returning (normalised, residual): this package's traceable op and
+# vLLM's IR op (vllm.ir.ops.fused_add_rms_norm, default and maybe_inplace overloads)
+ADD_RMS = ("b200fx.fused_add_rms_norm", "vllm_ir.fused_add_rms_norm")
+# in-place add + RMSNorm (vLLM's _C.fused_add_rms_norm mutates input and residual); in
+# post-grad graphs it sits under auto_functionalized, whose output tuple is
+# (None, input', residual')
+ADD_RMS_INPLACE = ("_C.fused_add_rms_norm",)
 SILU_MUL = ("b200fx.silu_and_mul", "_C.silu_and_mul")
 GROUP_QUANT = ("b200fx.group_quant_fp8", "_C.per_token_group_fp8_quant")
 RMS_NORM = ("b200fx.rms_norm",)
@@ -147,25 +174,62 @@ class _Pass:
         raise NotImplementedError
 
 
+def _auto_functionalized_of(node: fx.Node, names: Iterable[str]) -> bool:
+    return (node.op == "call_function" and node.args and
+            node.target is getattr(torch.ops.higher_order, "auto_functionalized", None) and
+            any(_qual(node.args[0]).startswith(n) for n in names))
+
+
 class AllReduceRMSNormFusionPass(_Pass):
-    """all_reduce(x) whose only user is fused_add_rms_norm(ar, residual, w, eps)."""
+    """all_reduce(x) whose only user is an add + RMSNorm of it (functional
+    ``fused_add_rms_norm(ar, residual, w, eps)`` or vLLM's in-place ``_C.fused_add_rms_norm``
+    under ``auto_functionalized``).  The fused node carries the all-reduce's process-group
+    name, so without a bound communicator it still reduces over that group."""
     name = "allreduce_rmsnorm"
+
+    @staticmethod
+    def _source(x) -> Optional[fx.Node]:
+        if isinstance(x, fx.Node) and _is(x, ALL_REDUCE) and len(x.users) == 1:
+            return x
+        return None
+
+    @staticmethod
+    def _fused(graph, ar: fx.Node, residual, w, eps) -> fx.Node:
+        group = ar.args[1] if len(ar.args) > 1 else ar.kwargs.get("group_name")
+        return graph.call_function(torch.ops.b200fx.allreduce_add_rms_norm.default,
+                                   (ar.args[0], residual, w, eps, group))
 
     def __call__(self, graph: fx.Graph) -> int:
         n = 0
         for node in list(graph.nodes):
-            if not _is(node, ADD_RMS):
-                continue
-            src = node.args[0]
-            if not isinstance(src, fx.Node) or not _is(src, ALL_REDUCE) or len(src.users) != 1:
-                continue
-            with graph.inserting_before(node):
-                fused = graph.call_function(torch.ops.b200fx.allreduce_add_rms_norm.default,
-                                            (src.args[0],) + tuple(node.args[1:]))
-            node.replace_all_uses_with(fused)
-            graph.erase_node(node)
-            graph.erase_node(src)
-            n += 1
+            if _is(node, ADD_RMS):
+                if len(node.args) > 4 and node.args[4] is not None:
+                    continue  # variance over a prefix of the row: not this kernel
+                src = self._source(node.args[0])
+                if src is None:
+                    continue
+                with graph.inserting_before(node):
+                    fused = self._fused(graph, src, *node.args[1:4])
+                node.replace_all_uses_with(fused)
+                graph.erase_node(node)
+                graph.erase_node(src)
+                n += 1
+            elif _auto_functionalized_of(node, ADD_RMS_INPLACE):
+                kw = node.kwargs
+                src = self._source(kw.get("input"))
+                if src is None or not all(u.target is operator.getitem and u.args[1] in (1, 2)
+                                          for u in node.users):
+                    continue
+                with graph.inserting_before(node):
+                    fused = self._fused(graph, src, kw["residual"], kw["weight"], kw["epsilon"])
+                for u in list(node.users):
+                    with graph.inserting_before(u):
+                        g = graph.call_function(operator.getitem, (fused, u.args[1] - 1))
+                    u.replace_all_uses_with(g)
+                    graph.erase_node(u)
+                graph.erase_node(node)
+                graph.erase_node(src)
+                n += 1
         return n
 
 

@@ -226,6 +226,10 @@ class LLMEngine:
                         self.abort_request(op[1])
                     elif op[0] == "shutdown":
                         self._stop = True
+                    elif op[0] == "sleep":
+                        self._sleep_local(op[1])
+                    elif op[0] == "wake":
+                        self._wake_local()
             if not self.scheduler.has_unfinished():
                 return []
         spec = self.config.speculative
@@ -365,7 +369,9 @@ class LLMEngine:
         KV cache and the CUDA graphs (their contents are discarded, the prefix cache starts
         empty after waking).  Reference: the platform declares vLLM's sleep mode available
         (vllm_musa/platform.py:274-276).  Only between requests; recurrent-state models
-        (Qwen3-Next, Mamba2) keep their state buffers and are refused."""
+        (Qwen3-Next, Mamba2) keep their state buffers and are refused.  With spawned follower
+        ranks the driver forwards the call, so every rank releases (and later restores) its
+        shards in the same step."""
         if level not in (1, 2):
             raise ValueError("sleep level must be 1 or 2")
         if self.sleep_level:
@@ -374,21 +380,40 @@ class LLMEngine:
             raise RuntimeError("sleep() needs an idle engine (requests still running)")
         if hasattr(self.model, "allocate_state"):
             raise NotImplementedError("sleep mode does not cover recurrent-state models")
+        if self.sync is not None and self.role == "driver":
+            self.sync.record(("sleep", level))
+            self.sync.exchange()
+        self._sleep_local(level)
+
+    def _sleep_local(self, level: int) -> None:
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
         self.runner.release_graphs()
-        self._offloaded = []
-        self._discarded = []
+        # one entry per storage: views that share a storage (a fused weight and slices of it
+        # kept as separate attributes) are offloaded once and re-seated on the same restored
+        # storage, so waking neither grows memory nor splits the aliasing
+        groups: dict = {}
         for t in self._weight_tensors():
-            # level 2 discards the large tensors (the checkpoint weights, which the loader
+            st = t.untyped_storage()
+            g = groups.setdefault(st.data_ptr(), {"storage": st, "views": []})
+            g["views"].append((t, t.storage_offset(), tuple(t.shape), tuple(t.stride())))
+        self._offloaded, self._discarded = [], []
+        for g in groups.values():
+            st = g["storage"]
+            nbytes = st.nbytes()
+            # level 2 discards the large storages (the checkpoint weights, which the loader
             # re-creates); small ones (norms, rotary tables) are kept on the host either way
-            if level == 1 or t.numel() * t.element_size() < (16 << 20):
-                host = torch.empty(t.shape, dtype=t.dtype, pin_memory=t.is_cuda)
-                host.copy_(t)
-                self._offloaded.append((t, host))
+            if level == 1 or nbytes < (16 << 20):
+                whole = torch.empty(0, dtype=torch.uint8, device=self.device).set_(st)
+                host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=self.device.type == "cuda")
+                host.copy_(whole)
+                self._offloaded.append((host, g["views"]))
+                del whole
             else:
-                self._discarded.append(t)
-            t.data = torch.empty(0, dtype=t.dtype, device=t.device)
+                self._discarded.extend(t for t, _, _, _ in g["views"])
+            for t, _, _, _ in g["views"]:
+                t.data = torch.empty(0, dtype=t.dtype, device=t.device)
+        groups.clear()
         self.runner.kv_caches = []
         self.runner.kv_tensor = None
         self.sleep_level = level
@@ -398,11 +423,22 @@ class LLMEngine:
 
     def wake_up(self) -> None:
         """Undo ``sleep``: weights back (host copy or a fresh load), a new KV cache of the same
-        block count, a fresh scheduler (empty prefix cache) and re-captured CUDA graphs."""
+        block count, a fresh scheduler (empty prefix cache) and re-captured CUDA graphs (every
+        rank at once: graph capture runs the tensor-parallel collectives)."""
         if not self.sleep_level:
             return
-        for t, host in self._offloaded:
-            t.data = host.to(self.device, non_blocking=False)
+        if self.sync is not None and self.role == "driver":
+            self.sync.record(("wake",))
+            self.sync.exchange()
+        self._wake_local()
+
+    def _wake_local(self) -> None:
+        for host, views in self._offloaded:
+            dev = host.to(self.device, non_blocking=False)
+            st = dev.untyped_storage()
+            for t, off, shape, stride in views:
+                t.data = torch.empty(0, dtype=t.dtype, device=self.device).set_(
+                    st, off, shape, stride)
         self._offloaded = []
         if self.sleep_level == 2:
             self._load_weights()
