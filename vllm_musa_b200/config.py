@@ -201,6 +201,8 @@ class ModelConfig:
             partial_rotary_factor=hf.get("partial_rotary_factor", 1.0) or 1.0,
             attn_output_gate=arch == "qwen3_next",
             swiglu_limit=float(hf.get("swiglu_limit") or 0.0),
+            # DeepSeek checkpoints rotate interleaved (even, odd) pairs (HF rope_interleave)
+            rope_neox=not (arch == "deepseek_v3" and hf.get("rope_interleave", True)),
             eos_token_id=(hf.get("eos_token_id")[0] if isinstance(hf.get("eos_token_id"), list)
                           else hf.get("eos_token_id")),
             name=a,
