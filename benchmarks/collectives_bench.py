@@ -93,14 +93,18 @@ def main():
             print(json.dumps(d), flush=True)
             out.append(d)
 
-    for T in (1, 8, 64, 256, 1024, 4096):
+    nv = ar.nvls
+    emit(dict(case="setup", nvls=nv is not None))
+    for T in (1, 8, 64, 256, 1024, 4096, 8192):
         x = torch.randn(T, H, device=dev).to(torch.bfloat16)
         res = torch.randn(T, H, device=dev).to(torch.bfloat16)
         two_shot, _ = ar._plan(T)
 
-        def fused():
+        def p2p():  # peer-to-peer kernel (one- or two-shot by size), NVLS switched off
+            ar.nvls = None
             stg = ar.staging_view(T)
             ar.allreduce_add_rmsnorm(stg, res, w, eps)
+            ar.nvls = nv
 
         def nccl():
             y = x.clone()
@@ -108,15 +112,44 @@ def main():
             ops.fused_add_rms_norm(y, res, w, eps)
 
         it = 200 if T <= 256 else 50
-        tf, tn = _time(fused, it, st.tp_group), _time(nccl, it, st.tp_group)
+        tf, tn = _time(p2p, it, st.tp_group), _time(nccl, it, st.tp_group)
         nbytes = T * H * 2
         # one-shot: read the other ranks' full slots; two-shot: read (N-1)/N of each peer's
         # slot for the owned chunk, then write the owned normalised chunk to N-1 peers
         link = (world - 1) * nbytes if not two_shot else (world - 1) * nbytes / world
         roof = link / LINK_BPS * 1e6
-        emit(dict(case="ar_norm", T=T, H=H, two_shot=two_shot, us=round(tf, 2),
-                  nccl_us=round(tn, 2), speedup_vs_nccl=round(tn / tf, 2),
-                  roofline_us=round(roof, 2), frac_of_roofline=round(roof / tf, 3)))
+        rec = dict(case="ar_norm", T=T, H=H, two_shot=two_shot, us=round(tf, 2),
+                   nccl_us=round(tn, 2), speedup_vs_nccl=round(tn / tf, 2),
+                   roofline_us=round(roof, 2), frac_of_roofline=round(roof / tf, 3))
+        if nv is not None and T >= world:
+            k_fn = {}
+            for shot in (True, False):
+                def f(shot=shot):
+                    ar._run_nvls(nv.staging[ar.parity][:T], res, w, eps, two_shot=shot)
+                k_fn[shot] = _time(f, it, st.tp_group)
+            # NVLS two-shot: each rank's link carries ~one message copy per direction
+            # (ld_reduce of the owned rows from every rank + multimem.st of them to every rank)
+            nroof = nbytes / LINK_BPS * 1e6
+            rec.update(nvls2_us=round(k_fn[True], 2), nvls1_us=round(k_fn[False], 2),
+                       nvls_roofline_us=round(nroof, 2),
+                       nvls2_frac_of_roofline=round(nroof / k_fn[True], 3))
+        emit(rec)
+
+    if nv is not None and H % 256 == 0:
+        for T in (8, 256, 2048):
+            x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            res = torch.randn(T, H, device=dev).to(torch.bfloat16)
+
+            def fused_q():
+                ar.allreduce_add_rmsnorm_quant(ar.staging_view(T)[:T], res, w, eps)
+
+            def unfused_q():
+                o, _ = ar.allreduce_add_rmsnorm(ar.staging_view(T), res, w, eps)
+                ops.activation.group_quant_fp8(o)
+
+            tq, tu = _time(fused_q, 100, st.tp_group), _time(unfused_q, 100, st.tp_group)
+            emit(dict(case="ar_norm_fp8", T=T, H=H, us=round(tq, 2), unfused_us=round(tu, 2),
+                      speedup_vs_unfused=round(tu / tq, 2)))
 
     K = 14336
     for T in (256, 1024, 4096):

@@ -34,6 +34,32 @@ struct ArParams {
 
 void run_fused_allreduce(const ArParams& a, cudaStream_t s);
 
+// NVLS variant (nvls_ar.cu): the buffers are bound to an NVLink multicast object; `mc_*` are
+// multicast addresses of this call's slots, the other pointers this rank's own copies.
+struct NvlsParams {
+  int rank, world, T, H, blocks;
+  bool two_shot;
+  const void* mc_staging;  // [T, H] bf16 partial sums of every rank, read with ld_reduce
+  void* mc_out;            // two-shot: normalised rows, stored to every rank
+  void* out_local;         // one-shot: this rank's output copy
+  uint32_t* mc_flags;      // barrier counters [2 phases][kMaxBlocks] (multicast address)
+  uint32_t* flags;         // the same counters, this rank's copy
+  uint32_t* epochs;        // local per-block call counts [2 phases][kMaxBlocks]
+  void* residual;          // [T, H] bf16, updated in place (nullptr: plain all-reduce)
+  const void* weight;      // RMSNorm weight (nullptr: no norm)
+  float eps;
+  // per-token 1x128 e4m3 output instead of the bf16 rows (needs the norm): q [T, H] e4m3 and
+  // scales [T, H / 128] fp32; multicast addresses (two-shot) or local copies (one-shot)
+  void* mc_q = nullptr;
+  void* q_local = nullptr;
+  float* mc_s = nullptr;
+  float* s_local = nullptr;
+  int* err;
+};
+constexpr size_t kNvlsFlagBytes = 2 * kMaxBlocks * sizeof(uint32_t);
+void run_nvls_allreduce(const NvlsParams& a, cudaStream_t s);
+int nvls_blocks(int T, int world, bool two_shot);
+
 // Vocab-parallel sampling exchange: every rank's per-row (score, token) candidate is stored into
 // every peer's candidate region [src rank][row]; after a per-block epoch barrier each rank picks
 // the row maxima (ties -> smaller token id) from local memory.

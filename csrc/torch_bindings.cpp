@@ -1198,6 +1198,46 @@ void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64
   guarded([&] { b200::comm::run_fused_allreduce(a, stream_of(like)); });
 }
 
+// NVLS fused all-reduce.  `ptrs` = [mc_staging, mc_out, out_local, mc_flags, flags, epochs,
+// mc_q, q_local, mc_s, s_local] (0 = absent).
+void nvls_allreduce(const Tensor& like, const std::vector<int64_t>& ptrs, int64_t rank,
+                    int64_t world, int64_t T, int64_t H, bool two_shot,
+                    const c10::optional<Tensor>& residual, const c10::optional<Tensor>& weight,
+                    double eps) {
+  TORCH_CHECK(ptrs.size() == 10, "nvls_allreduce: pointer table size");
+  const c10::cuda::CUDAGuard g(like.device());
+  b200::comm::NvlsParams a{};
+  a.rank = rank;
+  a.world = world;
+  a.T = T;
+  a.H = H;
+  a.two_shot = two_shot;
+  a.blocks = b200::comm::nvls_blocks(T, world, two_shot);
+  a.mc_staging = reinterpret_cast<const void*>(ptrs[0]);
+  a.mc_out = reinterpret_cast<void*>(ptrs[1]);
+  a.out_local = reinterpret_cast<void*>(ptrs[2]);
+  a.mc_flags = reinterpret_cast<uint32_t*>(ptrs[3]);
+  a.flags = reinterpret_cast<uint32_t*>(ptrs[4]);
+  a.epochs = reinterpret_cast<uint32_t*>(ptrs[5]);
+  a.mc_q = reinterpret_cast<void*>(ptrs[6]);
+  a.q_local = reinterpret_cast<void*>(ptrs[7]);
+  a.mc_s = reinterpret_cast<float*>(ptrs[8]);
+  a.s_local = reinterpret_cast<float*>(ptrs[9]);
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->scalar_type() == at::kBFloat16 &&
+                    residual->size(0) >= T && residual->size(1) == H,
+                "nvls_allreduce: residual");
+    a.residual = residual->data_ptr();
+  }
+  if (weight.has_value()) {
+    TORCH_CHECK(weight->numel() == H && weight->scalar_type() == at::kBFloat16, "weight");
+    a.weight = weight->data_ptr();
+  }
+  a.eps = eps;
+  a.err = err_ptr(like);
+  guarded([&] { b200::comm::run_nvls_allreduce(a, stream_of(like)); });
+}
+
 // Expert-parallel all-to-all: `ints` = [rank, world, Tc, row0, H, k, E_local, cap, rs_rows];
 // `ptrs` = [send_cnt, epoch, then per rank (world entries each): recv_x, recv_ids, recv_w,
 // recv_tok, recv_cnt, flags, staging].
@@ -1497,6 +1537,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("world"), py::arg("T"), py::arg("H"), py::arg("blocks"), py::arg("parity"),
         py::arg("two_shot"), py::arg("residual"), py::arg("weight"), py::arg("eps"),
         py::arg("rs_rows") = 0);
+  m.def("nvls_allreduce", &nvls_allreduce,
+        "NVLS (multimem) all-reduce (+ residual + RMSNorm, + optional 1x128 e4m3 output)",
+        py::arg("like"), py::arg("ptrs"), py::arg("rank"), py::arg("world"), py::arg("T"),
+        py::arg("H"), py::arg("two_shot"), py::arg("residual"), py::arg("weight"),
+        py::arg("eps"));
+  m.def("nvls_flag_bytes", []() { return (int64_t)b200::comm::kNvlsFlagBytes; });
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel dispatch over NVLink (+ count exchange)");
   m.def("exchange_candidates", &exchange_candidates,
         "vocab-parallel sampling: per-row candidates exchanged over NVLink and merged");

@@ -49,9 +49,21 @@ def mode_ar(out_path):
         ref_out = ops.norm._rms_ref(ref_res, w, 1e-6, False)
         stg = ar.staging_view(T)
         stg.copy_(x)
+        nvls = ar.use_nvls(T)
         out, res2 = ar.allreduce_add_rmsnorm(stg, res.clone(), w, 1e-6)
         torch.cuda.synchronize()
-        two_shot, _ = ar._plan(T)
+        two_shot = nvls or ar._plan(T)[0]
+        q_err = None
+        if ar.can_quant(x):
+            # the fused fp8 output (1x128 e4m3 groups) against quantising the reference rows
+            stg = ar.staging_view(T)
+            stg.copy_(x)
+            q, s = ar.allreduce_add_rmsnorm_quant(stg, res.clone(), w, 1e-6)
+            torch.cuda.synchronize()
+            rq, rs = ops.activation.group_quant_fp8(ref_out)
+            deq = q.float().view(T, -1, 128) * s.unsqueeze(-1)
+            rdeq = rq.float().view(T, -1, 128) * rs.unsqueeze(-1)
+            q_err = ((deq - rdeq).abs().max() / rdeq.abs().max()).item()
         if two_shot:
             per = (T + world - 1) // world
             r0, r1 = min(T, st.rank * per), min(T, st.rank * per + per)
@@ -59,7 +71,8 @@ def mode_ar(out_path):
         else:
             dres = (res2.float() - ref_res.float()).abs().max().item()
         dout = (out.float() - ref_out.float()).abs().max().item()
-        errs.append({"T": T, "two_shot": two_shot, "dout": dout, "dres": dres})
+        errs.append({"T": T, "two_shot": two_shot, "nvls": nvls, "dout": dout, "dres": dres,
+                     "q_err": q_err})
     ops._ext.check_device_errors()
     ar.close()
     if st.rank == 0:

@@ -94,8 +94,13 @@ class TPCommunicator:
         """Like ``allreduce_add_rmsnorm`` for a normalised output consumed by an fp8 GEMM:
         returns (x, residual, (q, scales)) with x's rows quantised per token (1x128 e4m3).  One
         GPU: residual add, RMSNorm and quantisation in one kernel (x is left unnormalised);
-        TP: the fused all-reduce + norm, then the group quantisation."""
+        TP over NVLS: all-reduce, residual add, RMSNorm and quantisation in one kernel (x is
+        returned as None: the caller consumes only the quantised rows); otherwise the fused
+        all-reduce + norm, then the group quantisation."""
         if self.world > 1:
+            if self.custom is not None and self.custom.can_quant(x):
+                q, sc = self.custom.allreduce_add_rmsnorm_quant(x, residual, weight, eps)
+                return None, residual, (q, sc)
             x, residual = self.allreduce_add_rmsnorm(x, residual, weight, eps)
             return x, residual, ops.activation.group_quant_fp8(x)
         q, sc, _ = ops.rms_norm_quant_fp8(x, weight, eps, residual=residual)

@@ -11,6 +11,12 @@ the residual, normalises and (two-shot) scatters the normalised rows into every 
 slot with NVLink stores.  Slots alternate by call parity; each forward pass has an even
 number of calls and starts at parity 0, so consecutive calls always alternate.
 
+When the GPUs sit on an NVSwitch with multicast support, a second buffer is allocated from
+PyTorch's symmetric memory and bound to one NVLink multicast object (NVLS): the all-reduce of
+larger messages then reduces in the switch with multimem loads and broadcasts the normalised
+rows with multimem stores (csrc/comm/nvls_ar.cu), so each rank's links carry about one copy of
+the message per direction instead of (2 - 2/world) copies.  ``B200_AR_NVLS=0`` disables it.
+
 Set-up is fail-closed like the reference's (vllm_musa/distributed/device_communicators/
 musa_jit_custom_all_reduce.py:1762-1938, MIN consensus over a CPU group): if any rank cannot
 allocate, export or open a buffer, every rank falls back to NCCL.
@@ -38,6 +44,78 @@ ONE_SHOT_READ_BYTES = 2 << 20
 # efficiently than the two-shot kernel's warp-contiguous loads: measured at TP=2 decode
 # (256 tokens, Llama-3-8B) 9.31 ms/step fused vs 8.42 ms unfused, so it is opt-in.
 FUSE_GEMM_RS = os.environ.get("B200_FUSE_GEMM_RS", "0") == "1"
+NVLS = os.environ.get("B200_AR_NVLS", "1") != "0"
+# messages of at most this many bytes stay on the peer-to-peer one-shot kernel (one barrier,
+# plain loads) when NVLS is up; larger ones take the NVLS two-shot kernel
+NVLS_MIN_BYTES = int(os.environ.get("B200_AR_NVLS_MIN_BYTES", str(64 << 10)))
+
+
+def _consensus(ok: bool, group) -> bool:
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return int(t) == 1
+
+
+class NvlsBuffer:
+    """The NVLS half of the communicator: one symmetric-memory buffer per rank, bound to an
+    NVLink multicast object, laid out as
+
+        [staging 0][staging 1][out 0][out 1][q 0][q 1][scales 0][scales 1][counters]
+
+    (staging / out: [max_tokens, hidden] bf16; q: e4m3 rows; scales: fp32 [max_tokens,
+    hidden / 128]; counters: the kernel's barrier counters).  Every offset has a local address
+    (this rank's copy) and a multicast address."""
+
+    def __init__(self, st, device, max_tokens: int, hidden: int, mod):
+        import torch.distributed._symmetric_memory as symm
+        self.mod = mod
+        H, T = hidden, max_tokens
+        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        self.slot = al(T * H * 2)
+        self.qslot = al(T * H)
+        self.sslot = al(T * max(1, H // 128) * 4)
+        self.off_out = 2 * self.slot
+        self.off_q = 4 * self.slot
+        self.off_s = self.off_q + 2 * self.qslot
+        self.off_flags = self.off_s + 2 * self.sslot
+        total = self.off_flags + al(int(mod.nvls_flag_bytes()))
+        group = st.tp_group
+        symm.enable_symm_mem_for_group(group.group_name)
+        self.buf = symm.empty(total, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm.rendezvous(self.buf, group)
+        self.mc = int(self.handle.multicast_ptr) if self.handle.has_multicast_support() else 0
+        self.base = self.buf.data_ptr()
+        self.epochs = torch.zeros(2 * int(mod.comm_max_blocks()), dtype=torch.int32, device=device)
+        dev = device.index
+        self.staging = [mod.tensor_from_ptr(self.base + k * self.slot, [T, H], torch.bfloat16, dev)
+                        for k in range(2)]
+        self.out = [mod.tensor_from_ptr(self.base + self.off_out + k * self.slot, [T, H],
+                                        torch.bfloat16, dev) for k in range(2)]
+        self.q = [mod.tensor_from_ptr(self.base + self.off_q + k * self.qslot, [T, H],
+                                      torch.float8_e4m3fn, dev) for k in range(2)]
+        self.s = [mod.tensor_from_ptr(self.base + self.off_s + k * self.sslot,
+                                      [T, max(1, H // 128)], torch.float32, dev) for k in range(2)]
+
+    def ptrs(self, parity: int, two_shot: bool, quant: bool) -> list:
+        mc, loc = self.mc, self.base
+        st = self.slot * parity
+        out = self.off_out + self.slot * parity
+        q = self.off_q + self.qslot * parity
+        sc = self.off_s + self.sslot * parity
+        return [mc + st,
+                mc + out if two_shot and not quant else 0,
+                loc + out if not two_shot and not quant else 0,
+                mc + self.off_flags, loc + self.off_flags, self.epochs.data_ptr(),
+                mc + q if two_shot and quant else 0,
+                loc + q if not two_shot and quant else 0,
+                mc + sc if two_shot and quant else 0,
+                loc + sc if not two_shot and quant else 0]
+
+    def close(self):
+        self.staging = self.out = self.q = self.s = []
+        self.handle = None
+        self.buf = None
 
 
 def self_world_pad(st) -> int:
@@ -90,6 +168,36 @@ class CustomAllReduce:
             self._bufs.append(staging + out + flags)
         self.parity = 0
         self.cand_parity = 0
+        self.nvls: Optional[NvlsBuffer] = None
+        if NVLS:
+            self._init_nvls(st, device, max_tokens, hidden)
+
+    def _init_nvls(self, st, device, max_tokens, hidden) -> None:
+        """Collective: every rank tries; NVLS is used only if every rank got a multicast
+        mapping (MIN consensus), otherwise every rank releases its buffer."""
+        ok = True
+        try:
+            import torch.distributed._symmetric_memory  # noqa: F401
+            ok = hasattr(self.mod, "nvls_allreduce") and st.tp_group is not None
+        except Exception:  # pragma: no cover - torch built without symmetric memory
+            ok = False
+        if not _consensus(ok, st.tp_cpu_group):
+            return
+        buf = None
+        try:
+            buf = NvlsBuffer(st, device, max_tokens, hidden, self.mod)
+            ok = buf.mc != 0
+        except Exception as e:  # fail closed
+            log.warning("NVLS buffer unavailable on rank %d: %s", st.rank, e)
+            ok = False
+        if _consensus(ok, st.tp_cpu_group):
+            torch.cuda.synchronize(device)
+            dist.barrier(group=st.tp_cpu_group)  # every rank's counters are zero before use
+            self.nvls = buf
+            log.info("NVLS all-reduce enabled (multicast buffer %.0f MiB)",
+                     buf.buf.numel() / 2**20)
+        elif buf is not None:
+            buf.close()
 
     # ------------------------------------------------------------------ interface
     def begin_forward(self) -> None:
@@ -99,17 +207,39 @@ class CustomAllReduce:
         return (x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] == self.hidden and
                 x.shape[0] <= self.max_tokens)
 
+    def use_nvls(self, T: int) -> bool:
+        """NVLS two-shot for messages above the one-shot size (when NVLS is up)."""
+        return self.nvls is not None and T >= self.world and \
+            T * self.hidden * 2 > NVLS_MIN_BYTES
+
     def staging_view(self, T: int) -> torch.Tensor:
+        if self.use_nvls(T):
+            return self.nvls.staging[self.parity][:T]
         return self._staging[self.parity][:T]
 
     def _plan(self, T: int):
+        """Peer-to-peer algorithm for T rows: (two_shot, blocks)."""
         limit = ONE_SHOT_MAX_BYTES or ONE_SHOT_READ_BYTES // max(1, self.world - 1)
         two_shot = T * self.hidden * 2 > limit and T >= self.world
         rows = (T + self.world - 1) // self.world if two_shot else T
         return two_shot, max(1, min(rows, self.max_blocks))
 
+    def _run_nvls(self, x, residual, weight, eps, two_shot=True, quant=False):
+        T = x.shape[0]
+        nv, k = self.nvls, self.parity
+        if x.data_ptr() != nv.staging[k].data_ptr():
+            nv.staging[k][:T].copy_(x)
+        self.mod.nvls_allreduce(x, nv.ptrs(k, two_shot, quant), self.rank, self.world, T,
+                                self.hidden, two_shot, residual, weight, eps)
+        self.parity ^= 1
+        if quant:
+            return nv.q[k][:T], nv.s[k][:T]
+        return nv.out[k][:T]
+
     def _run(self, x, residual, weight, eps):
         T = x.shape[0]
+        if self.use_nvls(T):
+            return self._run_nvls(x, residual, weight, eps)
         if x.data_ptr() != self._staging[self.parity].data_ptr():
             self._staging[self.parity][:T].copy_(x)
         two_shot, blocks = self._plan(T)
@@ -128,6 +258,18 @@ class CustomAllReduce:
 
     def allreduce_add_rmsnorm(self, x, residual, weight, eps):
         return self._run(x, residual, weight, eps), residual
+
+    def can_quant(self, x: torch.Tensor) -> bool:
+        """The fused all-reduce + norm can emit 1x128 e4m3 rows (NVLS kernels)."""
+        return self.nvls is not None and self.can_run(x) and self.hidden % 256 == 0
+
+    def allreduce_add_rmsnorm_quant(self, x, residual, weight, eps):
+        """residual <- AR(x) + residual; returns (q, scales) of RMSNorm(residual) * weight per
+        token in 1x128 e4m3 groups, produced inside the all-reduce kernel (NVLS one-shot for
+        small messages, two-shot beyond)."""
+        T = x.shape[0]
+        two_shot = self.use_nvls(T)
+        return self._run_nvls(x, residual, weight, eps, two_shot=two_shot, quant=True)
 
     def staging_blocks(self, rows: int) -> torch.Tensor:
         """This call's staging slot viewed as world blocks of `rows` rows (epilogue / expert
@@ -201,6 +343,10 @@ class CustomAllReduce:
         return out, residual
 
     def close(self) -> None:
+        if self.nvls is not None:
+            torch.cuda.synchronize(self.device)
+            self.nvls.close()
+            self.nvls = None
         for a in self.opened:
             try:
                 self.mod.ipc_close(a)
