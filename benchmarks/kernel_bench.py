@@ -80,6 +80,17 @@ def case_gemm_decode(it):
     gemm(256, 4096, 14336, it, "gemm_bf16_decode_down")
 
 
+def case_gemm_decode_all(it):
+    """Every Llama-3-8B TP=1 linear at the bench's decode batch (M = 256)."""
+    for name, N, K in (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096),
+                       ("down", 4096, 14336)):
+        gemm(256, N, K, it, f"gemm_bf16_decode_{name}")
+
+
+def case_gemm_decode_qkv(it):
+    gemm(256, 6144, 4096, it, "gemm_bf16_decode_qkv")
+
+
 def case_gemm_prefill(it):
     gemm(8192, 28672, 4096, it, "gemm_bf16_prefill_gate_up")
     gemm(8192, 4096, 4096, it, "gemm_bf16_prefill_o")

@@ -417,6 +417,13 @@ struct SampleArgs {
 void run_sample(const SampleArgs& a, cudaStream_t s);
 void run_merge_candidates(const float* vals, const int64_t* idx, int S, int R, int64_t* out,
                           cudaStream_t s);
+// Repetition / presence / frequency penalties on fp32 logits [R, V_local] (row stride ld) of a
+// vocab shard starting at vocab_offset.  entries [n, 3] int32 = (row, global token id, count of
+// the token in the row's output so far); every listed token occurs in the prompt or the
+// output (rows list each token once).
+void run_apply_penalties(float* logits, int64_t ld, int V_local, int vocab_offset,
+                         const int32_t* entries, int n, const float* rep, const float* pres,
+                         const float* freq, cudaStream_t s);
 }  // namespace sampling
 
 // ------------------------------------------------------------------------------- misc

@@ -296,5 +296,39 @@ void run_merge_candidates(const float* vals, const int64_t* idx, int S, int R, i
   count_launch();
 }
 
+// ------------------------------------------------------------------------------ penalties
+// vLLM's logits-processor semantics (the reference inherits them from upstream vLLM): a token
+// seen in the prompt or the output has its logit divided by the repetition penalty when
+// positive and multiplied by it otherwise; each output occurrence subtracts the frequency
+// penalty, and any output occurrence subtracts the presence penalty once.
+__global__ void apply_penalties_kernel(float* __restrict__ logits, int64_t ld, int V_local,
+                                       int vocab_offset, const int32_t* __restrict__ entries,
+                                       int n, const float* __restrict__ rep,
+                                       const float* __restrict__ pres,
+                                       const float* __restrict__ freq) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int row = entries[3 * i], tok = entries[3 * i + 1] - vocab_offset;
+  const int cnt = entries[3 * i + 2];
+  if (tok < 0 || tok >= V_local) return;  // another rank's vocab shard
+  float* p = logits + (size_t)row * ld + tok;
+  float v = *p;
+  const float r = rep[row];
+  if (r != 1.f) v = v > 0.f ? v / r : v * r;
+  v -= freq[row] * (float)cnt;
+  if (cnt > 0) v -= pres[row];
+  *p = v;
+}
+
+void run_apply_penalties(float* logits, int64_t ld, int V_local, int vocab_offset,
+                         const int32_t* entries, int n, const float* rep, const float* pres,
+                         const float* freq, cudaStream_t s) {
+  if (n == 0) return;
+  apply_penalties_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, ld, V_local, vocab_offset,
+                                                         entries, n, rep, pres, freq);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
 }  // namespace sampling
 }  // namespace b200

@@ -809,6 +809,27 @@ void merge_candidates(const Tensor& vals, const Tensor& idx, Tensor& out) {
   });
 }
 
+void apply_penalties(Tensor& logits, const Tensor& entries, const Tensor& rep, const Tensor& pres,
+                     const Tensor& freq, int64_t vocab_offset) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "apply_penalties: fp32 [R, V] logits");
+  TORCH_CHECK(entries.scalar_type() == at::kInt && entries.is_contiguous() &&
+                  entries.dim() == 2 && entries.size(1) == 3,
+              "apply_penalties: int32 [n, 3] entries");
+  for (const Tensor* t : {&rep, &pres, &freq})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() >= logits.size(0),
+                "apply_penalties: fp32 per-row penalties");
+  const c10::cuda::CUDAGuard g(logits.device());
+  guarded([&] {
+    b200::sampling::run_apply_penalties(logits.data_ptr<float>(), logits.stride(0),
+                                        logits.size(1), vocab_offset, entries.data_ptr<int32_t>(),
+                                        entries.size(0), rep.data_ptr<float>(),
+                                        pres.data_ptr<float>(), freq.data_ptr<float>(),
+                                        stream_of(logits));
+  });
+}
+
 // ------------------------------------------------------------------------------------- misc
 void embedding(Tensor& out, const Tensor& table, const Tensor& ids, int64_t vocab_start) {
   CHECK_CUDA(table);
@@ -1422,6 +1443,8 @@ TORCH_LIBRARY(b200, m) {
       "Tensor? seeds, Tensor? steps, int vocab_offset, Tensor(a!) out_idx, Tensor(b!)? "
       "out_val=None) -> ()");
   m.def("merge_candidates(Tensor vals, Tensor idx, Tensor(a!) out) -> ()");
+  m.def("apply_penalties(Tensor(a!) logits, Tensor entries, Tensor rep, Tensor pres, Tensor freq, "
+        "int vocab_offset) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor table, Tensor ids, int vocab_start=0) -> ()");
   m.def("gather_rows(Tensor(a!) out, Tensor x, Tensor idx) -> ()");
   m.def(
@@ -1493,6 +1516,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("paged_prefill", &paged_prefill);
   m.impl("sample", &sample);
   m.impl("merge_candidates", &merge_candidates);
+  m.impl("apply_penalties", &apply_penalties);
   m.impl("embedding", &embedding);
   m.impl("gather_rows", &gather_rows);
   m.impl("gemm_grouped_bf16", &gemm_grouped_bf16);

@@ -48,6 +48,8 @@ class _Req:
     index: int = 0
     tokens: List[int] = field(default_factory=list)
     first_token_time: Optional[float] = None
+    logprobs: Optional[list] = None       # per generated token {id: Logprob} (if requested)
+    cum_logprob: float = 0.0
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -145,6 +147,7 @@ class LLMEngine:
         self._reqs: Dict[int, _Req] = {}
         self._by_name: Dict[str, int] = {}
         self._parents: Dict[str, dict] = {}
+        self._special: Dict[int, _Req] = {}  # requests with penalties or logprobs
         self.step_end_times: List[float] = []
         self.stream_outputs = False
         self.num_steps = 0
@@ -194,9 +197,18 @@ class LLMEngine:
         sp.top_p = params.top_p
         sp.min_p = params.min_p
         sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
+        special = params.has_penalties or params.logprobs is not None
+        if special and self.config.speculative.method is not None and \
+                self.config.speculative.num_speculative_tokens:
+            raise ValueError("penalties / logprobs are not served with speculative decoding")
         self.scheduler.add_request(iid, list(map(int, prompt_ids)), sp)
-        self._reqs[iid] = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
+        r = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
+        if params.logprobs is not None:
+            r.logprobs = []
+        self._reqs[iid] = r
         self._by_name[name] = iid
+        if special:
+            self._special[iid] = r
 
     def abort_request(self, request_id: str) -> None:
         if self.sync is not None and self.role == "driver":
@@ -208,6 +220,7 @@ class LLMEngine:
                 self.scheduler.abort_request(iid)
                 self._by_name.pop(n, None)
                 self._reqs.pop(iid, None)
+                self._special.pop(iid, None)
                 self.scheduler.forget(iid)
         self._parents.pop(request_id, None)
 
@@ -241,7 +254,10 @@ class LLMEngine:
         plan = self.scheduler.schedule()
         if plan.num_reqs == 0:
             return []
-        sampled = self.runner.execute(plan)
+        extras = self._step_extras(plan) if self._special else None
+        sampled = self.runner.execute(plan, extras)
+        if extras is not None and extras.logprobs is not None:
+            self._record_logprobs(plan, extras, sampled)
         finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
         now = time.time()
         self.step_end_times.append(now)
@@ -261,6 +277,7 @@ class LLMEngine:
                 if iid not in done and iid in self._reqs:
                     outs.append(self._make_output(self._reqs[iid], None, False))
         for iid, reason in finished:
+            self._special.pop(iid, None)
             r = self._reqs.pop(iid, None)
             if r is None:
                 continue
@@ -269,6 +286,51 @@ class LLMEngine:
             if o is not None:
                 outs.append(o)
         return outs
+
+    def _step_extras(self, plan):
+        """Penalty entries and log-probability rows for this step's special requests (every
+        rank builds the same ones: they depend only on the lock-step scheduler state)."""
+        from ..ops.sampling import penalty_entries
+        from .model_runner import StepExtras
+        rows_tok, lp_rows, k = [], [], 0
+        S = plan.num_samples
+        rep = torch.ones(S)
+        pres = torch.zeros(S)
+        freq = torch.zeros(S)
+        for row, iid in enumerate(plan.sample_req_ids):
+            r = self._special.get(iid)
+            if r is None:
+                continue
+            p = r.params
+            if p.has_penalties:
+                n = self.scheduler.num_tokens(iid)
+                toks = self.scheduler.tokens_range(iid, 0, n)
+                np_ = len(r.prompt_token_ids)
+                rows_tok.append((row, toks[:np_], toks[np_:]))
+                rep[row], pres[row], freq[row] = (p.repetition_penalty, p.presence_penalty,
+                                                  p.frequency_penalty)
+            if p.logprobs is not None:
+                lp_rows.append(row)
+                k = max(k, p.logprobs)
+        if not rows_tok and not lp_rows:
+            return None
+        entries = penalty_entries(rows_tok) if rows_tok else None
+        return StepExtras(entries, rep, pres, freq, lp_rows, k)
+
+    def _record_logprobs(self, plan, extras, sampled) -> None:
+        from ..outputs import Logprob
+        ids, vals, tok_lp, rank = (t.tolist() for t in extras.logprobs)
+        for j, row in enumerate(extras.lp_rows):
+            r = self._reqs.get(plan.sample_req_ids[row])
+            if r is None or r.logprobs is None:
+                continue
+            tok = int(sampled[row])
+            d = {tok: Logprob(tok_lp[j], int(rank[j]))}
+            for m in range(r.params.logprobs):
+                if ids[j][m] not in d:
+                    d[ids[j][m]] = Logprob(vals[j][m], m + 1)
+            r.logprobs.append(d)
+            r.cum_logprob += tok_lp[j]
 
     def _step_time(self, step: int) -> Optional[float]:
         # scheduler steps are 1-based and one engine step == one scheduler step
@@ -307,7 +369,9 @@ class LLMEngine:
                 text = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
             except Exception:  # pragma: no cover - tokenizer specific
                 text = ""
-        comp = CompletionOutput(r.index, list(r.tokens), text, reason)
+        comp = CompletionOutput(r.index, list(r.tokens), text, reason,
+                                cumulative_logprob=r.cum_logprob if r.logprobs is not None else None,
+                                logprobs=list(r.logprobs) if r.logprobs is not None else None)
         m = RequestMetrics(r.arrival, first if first is not None else r.first_token_time, last)
         return RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
 

@@ -84,6 +84,18 @@ class StepBuffers:
         return nbytes
 
 
+class StepExtras:
+    """Per-step logits processing beyond sampling, for the rows whose requests ask for it:
+    penalty entries (ops.sampling.penalty_entries) with per-row penalties, and the rows whose
+    raw-logit log-probabilities are returned (top ``lp_k`` per row)."""
+
+    def __init__(self, entries=None, rep=None, pres=None, freq=None, lp_rows=None, lp_k=0):
+        self.entries, self.rep, self.pres, self.freq = entries, rep, pres, freq
+        self.lp_rows = lp_rows or []
+        self.lp_k = lp_k
+        self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
+
+
 class ModelRunner:
     def __init__(self, cfg: EngineConfig, model, sampler, device: torch.device):
         self.cfg = cfg
@@ -119,6 +131,7 @@ class ModelRunner:
             model.allocate_state(sc.max_num_seqs + 1)
         self.record_logits = False  # debugging / tests: keep every step's logits (eager only)
         self.logits_log: list = []
+        self._extras: Optional[StepExtras] = None
 
     # ------------------------------------------------------------------ memory / KV cache
     def kv_bytes_per_block(self) -> int:
@@ -205,11 +218,28 @@ class ModelRunner:
         logits = self.model.compute_logits(rows)
         if self.record_logits:
             self.logits_log.append(logits.detach().float().cpu())
+        ex = self._extras
+        raw = None
+        if ex is not None:
+            if ex.lp_rows:
+                idx = torch.tensor(ex.lp_rows, dtype=torch.int64, device=logits.device)
+                raw = logits.index_select(0, idx)
+            if ex.entries is not None and ex.entries.numel():
+                dev = logits.device
+                ops.apply_penalties(logits, ex.entries.to(dev), ex.rep.to(dev), ex.pres.to(dev),
+                                    ex.freq.to(dev), getattr(self.model, "vocab_start", 0))
         if sampling:
-            return self.sampler(logits, b.d["temperature"][:S], b.d["top_k"][:S],
-                                b.d["top_p"][:S], b.d["min_p"][:S], b.d["seeds"][:S],
-                                b.d["steps"][:S], any_filter=any_filter, generator=self.gen)
-        return self.sampler(logits, None, None, None, None, None, None)
+            ids = self.sampler(logits, b.d["temperature"][:S], b.d["top_k"][:S],
+                               b.d["top_p"][:S], b.d["min_p"][:S], b.d["seeds"][:S],
+                               b.d["steps"][:S], any_filter=any_filter, generator=self.gen)
+        else:
+            ids = self.sampler(logits, None, None, None, None, None, None)
+        if raw is not None:
+            if self.sampler.tp > 1:  # vocab-sharded rows: the full distribution
+                raw = self.sampler.comm.all_gather(raw, dim=1)
+            sel = ids.index_select(0, idx)
+            ex.logprobs = [t.cpu() for t in ops.sampling.token_logprobs(raw, sel, ex.lp_k)]
+        return ids
 
     def _meta(self, T: int, R: int, nd: int, npf: int, max_seq_len: int,
               decode_splits: Optional[int] = None) -> AttnMetadata:
@@ -305,15 +335,17 @@ class ModelRunner:
         self.graph_pool = None
 
     # ------------------------------------------------------------------ step
-    def execute(self, plan) -> torch.Tensor:
-        """Run one scheduled step; returns the sampled ids (host int64 tensor, [num_samples])."""
+    def execute(self, plan, extras: Optional[StepExtras] = None) -> torch.Tensor:
+        """Run one scheduled step; returns the sampled ids (host int64 tensor, [num_samples]).
+        ``extras`` (penalties / log-probabilities for some rows) runs the step eagerly."""
         T, R, S = plan.num_tokens, plan.num_reqs, plan.num_samples
         nd, npf = plan.num_decodes, plan.num_prefills
         b = self.buf
         cuda = self.device.type == "cuda"
         decode_only = npf == 0 and nd == R and S == R
+        self._extras = extras
         B = None
-        if decode_only and self.graphs and not self.record_logits and \
+        if decode_only and self.graphs and not self.record_logits and extras is None and \
                 not (plan.any_filter and self.sampler.tp > 1):
             for s in sorted(self.graphs):
                 if s >= R:
@@ -349,6 +381,7 @@ class ModelRunner:
             meta = self._meta(T, R, nd, npf, plan.max_seq_len)
             ids = self._forward_sample(T, R, S, meta, sampling=sampling,
                                        any_filter=plan.any_filter, decode_only=decode_only)
+        self._extras = None
         out_h = b.sampled_h[:S]
         if cuda:
             out_h.copy_(ids, non_blocking=True)

@@ -21,7 +21,7 @@ from typing import List, Optional
 
 from .protocol import (ChatChoice, ChatCompletionRequest, ChatCompletionResponse, ChatMessage,
                        CompletionChoice, CompletionRequest, CompletionResponse, ErrorResponse,
-                       ModelCard, ModelList, Usage)
+                       ModelCard, ModelList, Usage, chat_logprobs, completion_logprobs)
 
 log = logging.getLogger("vllm_musa_b200")
 
@@ -154,7 +154,8 @@ def build_app(llm, model_name: str, max_model_len: int):
             c = o.outputs[0]
             body = (text or "") + c.text if req.echo else c.text
             choices.append(CompletionChoice(index=idx, text=body, token_ids=c.token_ids,
-                                            finish_reason=c.finish_reason))
+                                            finish_reason=c.finish_reason,
+                                            logprobs=completion_logprobs(c, tok)))
             n_prompt += len(ids)
             n_gen += len(c.token_ids)
         return CompletionResponse(id=rid, model=model_name, choices=choices,
@@ -191,7 +192,9 @@ def build_app(llm, model_name: str, max_model_len: int):
                                            "seed": (p.seed + k) if p.seed is not None else None}),
                     f"{rid}-{k}") for k in range(p.n)])
         choices = [ChatChoice(index=k, message=ChatMessage(role="assistant", content=o.outputs[0].text),
-                              finish_reason=o.outputs[0].finish_reason) for k, o in enumerate(outs)]
+                              finish_reason=o.outputs[0].finish_reason,
+                              logprobs=chat_logprobs(o.outputs[0], tok, req.top_logprobs or 0))
+                   for k, o in enumerate(outs)]
         n_gen = sum(len(o.outputs[0].token_ids) for o in outs)
         return ChatCompletionResponse(id=rid, model=model_name, choices=choices,
                                       usage=Usage(prompt_tokens=len(ids), completion_tokens=n_gen,

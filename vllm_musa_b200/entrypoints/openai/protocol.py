@@ -25,6 +25,12 @@ class _Sampling(BaseModel):
     min_tokens: int = 0
     stream: bool = False
     user: Optional[str] = None
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    repetition_penalty: float = 1.0
+
+    def num_logprobs(self) -> Optional[int]:
+        return None
 
     def sampling_params(self, default_max: int) -> SamplingParams:
         stop = [self.stop] if isinstance(self.stop, str) else list(self.stop or [])
@@ -33,12 +39,20 @@ class _Sampling(BaseModel):
                               max_tokens=self.max_tokens or default_max,
                               min_tokens=self.min_tokens, stop=stop,
                               stop_token_ids=list(self.stop_token_ids or []),
-                              ignore_eos=self.ignore_eos)
+                              ignore_eos=self.ignore_eos,
+                              presence_penalty=self.presence_penalty,
+                              frequency_penalty=self.frequency_penalty,
+                              repetition_penalty=self.repetition_penalty,
+                              logprobs=self.num_logprobs())
 
 
 class CompletionRequest(_Sampling):
     prompt: Union[str, List[int], List[str], List[List[int]]]
     echo: bool = False
+    logprobs: Optional[int] = None  # top log-probabilities per generated token (OpenAI legacy)
+
+    def num_logprobs(self) -> Optional[int]:
+        return self.logprobs
 
 
 class ChatMessage(BaseModel):
@@ -49,6 +63,11 @@ class ChatMessage(BaseModel):
 class ChatCompletionRequest(_Sampling):
     messages: List[ChatMessage]
     max_completion_tokens: Optional[int] = None
+    logprobs: bool = False
+    top_logprobs: Optional[int] = None
+
+    def num_logprobs(self) -> Optional[int]:
+        return (self.top_logprobs or 0) if self.logprobs else None
 
 
 class Usage(BaseModel):
@@ -62,6 +81,7 @@ class CompletionChoice(BaseModel):
     text: str
     token_ids: Optional[List[int]] = None
     finish_reason: Optional[str] = None
+    logprobs: Optional[Dict] = None
 
 
 class CompletionResponse(BaseModel):
@@ -77,6 +97,42 @@ class ChatChoice(BaseModel):
     index: int
     message: ChatMessage
     finish_reason: Optional[str] = None
+    logprobs: Optional[Dict] = None
+
+
+def _tok_str(tokenizer, t: int) -> str:
+    if tokenizer is None:
+        return str(t)
+    try:
+        return tokenizer.decode([t])
+    except Exception:  # pragma: no cover - tokenizer specific
+        return str(t)
+
+
+def completion_logprobs(c, tokenizer) -> Optional[Dict]:
+    """OpenAI completions ``logprobs`` object from a CompletionOutput's per-token logprobs."""
+    if c.logprobs is None:
+        return None
+    toks = [_tok_str(tokenizer, t) for t in c.token_ids]
+    return {"tokens": toks,
+            "token_logprobs": [d[t].logprob for t, d in zip(c.token_ids, c.logprobs)],
+            "top_logprobs": [{_tok_str(tokenizer, k): v.logprob for k, v in d.items()}
+                             for d in c.logprobs],
+            "text_offset": []}
+
+
+def chat_logprobs(c, tokenizer, top: int) -> Optional[Dict]:
+    """OpenAI chat ``logprobs.content`` from a CompletionOutput's per-token logprobs."""
+    if c.logprobs is None:
+        return None
+    content = []
+    for t, d in zip(c.token_ids, c.logprobs):
+        ranked = sorted(((k, v) for k, v in d.items() if v.rank is not None and v.rank <= top),
+                        key=lambda kv: kv[1].rank)
+        content.append({"token": _tok_str(tokenizer, t), "logprob": d[t].logprob,
+                        "top_logprobs": [{"token": _tok_str(tokenizer, k), "logprob": v.logprob}
+                                         for k, v in ranked]})
+    return {"content": content}
 
 
 class ChatCompletionResponse(BaseModel):

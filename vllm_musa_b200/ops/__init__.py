@@ -12,4 +12,4 @@ from .gemm import linear, linear_silu_mul, interleave_gate_up  # noqa: F401
 from .misc import embedding, gather_rows  # noqa: F401
 from .norm import fused_add_rms_norm, rms_norm, rms_norm_gated, rms_norm_quant_fp8  # noqa: F401
 from .rope import build_cos_sin_cache, rope_kv  # noqa: F401
-from .sampling import sample_tokens  # noqa: F401
+from .sampling import apply_penalties, sample_tokens  # noqa: F401

@@ -102,3 +102,64 @@ def sample_tokens(logits: torch.Tensor, temperature: torch.Tensor | None = None,
         i = int(torch.argmax(sc))
         ids[r], vals[r] = i + vocab_offset, sc[i]
     return (ids, vals) if return_values else ids
+
+
+def apply_penalties(logits: torch.Tensor, entries: torch.Tensor, rep: torch.Tensor,
+                    pres: torch.Tensor, freq: torch.Tensor, vocab_offset: int = 0) -> torch.Tensor:
+    """Repetition / presence / frequency penalties, in place, on fp32 logits [R, V] of the vocab
+    shard starting at ``vocab_offset``.  ``entries`` int32 [n, 3] = (row, global token id,
+    occurrences in the row's output); each row lists every token of its prompt and output
+    once.  vLLM semantics: a listed token's logit is divided by the repetition penalty when
+    positive (multiplied when not), minus frequency x count, minus presence if count > 0."""
+    if entries.numel() == 0:
+        return logits
+    if logits.is_cuda:
+        _ext.ops().apply_penalties(logits, entries.contiguous(), rep.contiguous(),
+                                   pres.contiguous(), freq.contiguous(), vocab_offset)
+        return logits
+    V = logits.shape[1]
+    for row, tok, cnt in entries.tolist():
+        t = tok - vocab_offset
+        if not 0 <= t < V:
+            continue
+        v = float(logits[row, t])
+        r = float(rep[row])
+        if r != 1.0:
+            v = v / r if v > 0 else v * r
+        v -= float(freq[row]) * cnt
+        if cnt > 0:
+            v -= float(pres[row])
+        logits[row, t] = v
+    return logits
+
+
+def penalty_entries(rows_tokens) -> torch.Tensor:
+    """[(row, prompt token ids, output token ids)] -> int32 [n, 3] (row, token, output count)
+    with every token of the prompt and output listed once per row."""
+    import numpy as np
+    parts = []
+    for row, prompt, output in rows_tokens:
+        out = np.asarray(output, dtype=np.int64)
+        toks = np.unique(np.concatenate([np.asarray(prompt, dtype=np.int64), out]))
+        cnt = np.zeros(toks.shape[0], dtype=np.int64)
+        if out.size:
+            u, c = np.unique(out, return_counts=True)
+            cnt[np.searchsorted(toks, u)] = c
+        parts.append(np.stack([np.full_like(toks, row), toks, cnt], 1))
+    if not parts:
+        return torch.zeros(0, 3, dtype=torch.int32)
+    return torch.from_numpy(np.concatenate(parts).astype(np.int32))
+
+
+def token_logprobs(raw: torch.Tensor, tokens: torch.Tensor, k: int):
+    """Log-probabilities from raw logits rows [n, V]: (top-k ids [n, k], top-k logprobs [n, k],
+    the given tokens' logprobs [n], their ranks [n] (1 = most likely))."""
+    lp = torch.log_softmax(raw.float(), dim=-1)
+    tok_lp = lp.gather(1, tokens.view(-1, 1).long()).squeeze(1)
+    rank = (lp > tok_lp.unsqueeze(1)).sum(1) + 1
+    if k > 0:
+        vals, ids = lp.topk(k, dim=-1)
+    else:
+        vals = torch.zeros(lp.shape[0], 0, device=lp.device)
+        ids = torch.zeros(lp.shape[0], 0, dtype=torch.int64, device=lp.device)
+    return ids, vals, tok_lp, rank

@@ -2,7 +2,15 @@
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import List, Optional
+from typing import Dict, List, Optional
+
+
+@dataclass
+class Logprob:
+    """Log-probability of one token at one position, with its rank among the vocabulary
+    (1 = most likely), as vLLM reports them."""
+    logprob: float
+    rank: Optional[int] = None
 
 
 @dataclass
@@ -12,6 +20,8 @@ class CompletionOutput:
     text: str = ""
     finish_reason: Optional[str] = None
     cumulative_logprob: Optional[float] = None
+    # per generated token: {token id: Logprob} for the top-k tokens and the generated one
+    logprobs: Optional[List[Dict[int, Logprob]]] = None
 
 
 @dataclass

@@ -19,6 +19,15 @@ class SamplingParams:
     stop: List[str] = field(default_factory=list)
     ignore_eos: bool = False
     detokenize: bool = True
+    # vLLM's logits processors: repetition (> 1 discourages tokens of the prompt and the
+    # output so far), presence and frequency penalties (subtracted per output occurrence)
+    repetition_penalty: float = 1.0
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    # number of most likely tokens whose log-probabilities are returned per generated token
+    # (plus the generated token's own), computed from the raw logits as vLLM's default
+    # logprobs mode; None = no log-probabilities
+    logprobs: Optional[int] = None
 
     def __post_init__(self):
         if self.top_k is None or self.top_k < 0:
@@ -33,9 +42,20 @@ class SamplingParams:
             raise ValueError("max_tokens must be >= 1")
         if self.n < 1:
             raise ValueError("n must be >= 1")
+        if self.repetition_penalty <= 0:
+            raise ValueError("repetition_penalty must be > 0")
+        if not -2.0 <= self.presence_penalty <= 2.0 or not -2.0 <= self.frequency_penalty <= 2.0:
+            raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
+        if self.logprobs is not None and not 0 <= self.logprobs <= 20:
+            raise ValueError("logprobs must be in [0, 20]")
         if self.temperature < 1e-5:
             self.temperature = 0.0  # greedy
 
     @property
     def greedy(self) -> bool:
         return self.temperature == 0.0
+
+    @property
+    def has_penalties(self) -> bool:
+        return (self.repetition_penalty != 1.0 or self.presence_penalty != 0.0 or
+                self.frequency_penalty != 0.0)
