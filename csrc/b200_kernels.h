@@ -417,6 +417,43 @@ struct SampleArgs {
 void run_sample(const SampleArgs& a, cudaStream_t s);
 void run_merge_candidates(const float* vals, const int64_t* idx, int S, int R, int64_t* out,
                           cudaStream_t s);
+// Vocab-parallel top-k / top-p / min-p sampling (topk_exchange.cu): per-shard candidate rows
+// (the <= kCandCap largest scaled logits with their global ids, the shard's max / exp-mass /
+// completeness key and its Gumbel-max winner), exchanged over NVLink and merged per row.
+constexpr int kCandCap = 128;
+struct alignas(16) CandRow {
+  float v[kCandCap];
+  int32_t id[kCandCap];
+  float m, s;        // shard max of l/T and sum exp(l/T - m)
+  int32_t n;         // candidates stored
+  uint32_t thr;      // every shard token with key >= thr is a candidate (0: all of them)
+  float best_v;      // shard Gumbel-max winner (argmax for greedy rows)
+  int32_t best_id;
+  int32_t pad[2];
+};
+struct TopkExchangeArgs {
+  int rank, world, R, parity, V_total;
+  const CandRow* mine;
+  CandRow* region[8];   // this call's candidate region of every rank: [world][R] rows
+  uint32_t* flags[8];   // communicator flag region of every rank
+  uint32_t* epochs;
+  const float* temperature;
+  const int32_t* top_k;
+  const float* top_p;
+  const float* min_p;
+  const int64_t* seeds;
+  const int32_t* steps;
+  int64_t* out;         // sampled global ids, -1 where the candidates cannot decide exactly
+  int* err;
+};
+void run_shard_candidates(const float* logits, int64_t ld, int R, int V, int vocab_offset,
+                          const float* temperature, const int64_t* seeds, const int32_t* steps,
+                          CandRow* out, cudaStream_t s);
+void run_merge_candidates_local(const CandRow* cands, int world, int R, const float* temperature,
+                                const int32_t* top_k, const float* top_p, const float* min_p,
+                                const int64_t* seeds, const int32_t* steps, int V_total,
+                                int64_t* out, cudaStream_t s);
+void run_topk_exchange(const TopkExchangeArgs& a, cudaStream_t s);
 // Repetition / presence / frequency penalties on fp32 logits [R, V_local] (row stride ld) of a
 // vocab shard starting at vocab_offset.  entries [n, 3] int32 = (row, global token id, count of
 // the token in the row's output so far); every listed token occurs in the prompt or the

@@ -1352,6 +1352,92 @@ void exchange_candidates(const Tensor& vals, const Tensor& ids, Tensor& out,
   guarded([&] { b200::comm::run_exchange_candidates(a, stream_of(vals)); });
 }
 
+// ---- vocab-parallel top-k / top-p: per-shard candidate rows, local merge, NVLink exchange
+static const float* opt_f32(const c10::optional<Tensor>& t) {
+  return t.has_value() ? t->data_ptr<float>() : nullptr;
+}
+static const int32_t* opt_i32(const c10::optional<Tensor>& t) {
+  return t.has_value() ? t->data_ptr<int32_t>() : nullptr;
+}
+static const int64_t* opt_i64(const c10::optional<Tensor>& t) {
+  return t.has_value() ? t->data_ptr<int64_t>() : nullptr;
+}
+
+int64_t cand_row_bytes() { return (int64_t)sizeof(b200::sampling::CandRow); }
+
+void shard_candidates(const Tensor& logits, const c10::optional<Tensor>& temperature,
+                      const c10::optional<Tensor>& seeds, const c10::optional<Tensor>& steps,
+                      int64_t vocab_offset, Tensor& out) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "shard_candidates: fp32 [R, V] logits");
+  TORCH_CHECK(out.is_contiguous() &&
+                  out.numel() * out.element_size() >=
+                      logits.size(0) * (int64_t)sizeof(b200::sampling::CandRow) &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "shard_candidates: output rows");
+  const c10::cuda::CUDAGuard g(logits.device());
+  guarded([&] {
+    b200::sampling::run_shard_candidates(
+        logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1), vocab_offset,
+        opt_f32(temperature), opt_i64(seeds), opt_i32(steps),
+        reinterpret_cast<b200::sampling::CandRow*>(out.data_ptr()), stream_of(logits));
+  });
+}
+
+void merge_candidates_local(const Tensor& cands, int64_t world, int64_t R,
+                            const c10::optional<Tensor>& temperature,
+                            const c10::optional<Tensor>& top_k, const c10::optional<Tensor>& top_p,
+                            const c10::optional<Tensor>& min_p, const c10::optional<Tensor>& seeds,
+                            const c10::optional<Tensor>& steps, int64_t V_total, Tensor& out) {
+  CHECK_CUDA(cands);
+  TORCH_CHECK(cands.numel() * cands.element_size() >=
+                  world * R * (int64_t)sizeof(b200::sampling::CandRow) &&
+                  out.scalar_type() == at::kLong && out.numel() >= R,
+              "merge_candidates_local: shapes");
+  const c10::cuda::CUDAGuard g(cands.device());
+  guarded([&] {
+    b200::sampling::run_merge_candidates_local(
+        reinterpret_cast<const b200::sampling::CandRow*>(cands.data_ptr()), world, R,
+        opt_f32(temperature), opt_i32(top_k), opt_f32(top_p), opt_f32(min_p), opt_i64(seeds),
+        opt_i32(steps), V_total, out.data_ptr<int64_t>(), stream_of(cands));
+  });
+}
+
+// ptrs = [candidate region of every rank (world), flag region of every rank (world)]
+void topk_exchange(const Tensor& mine, const std::vector<int64_t>& ptrs, int64_t epochs_ptr,
+                   int64_t rank, int64_t world, int64_t parity, int64_t V_total,
+                   const c10::optional<Tensor>& temperature, const c10::optional<Tensor>& top_k,
+                   const c10::optional<Tensor>& top_p, const c10::optional<Tensor>& min_p,
+                   const c10::optional<Tensor>& seeds, const c10::optional<Tensor>& steps,
+                   Tensor& out) {
+  CHECK_CUDA(mine);
+  TORCH_CHECK((int64_t)ptrs.size() == 2 * world && world <= 8, "topk_exchange: pointer table");
+  TORCH_CHECK(out.scalar_type() == at::kLong, "topk_exchange: int64 out");
+  b200::sampling::TopkExchangeArgs a{};
+  a.rank = rank;
+  a.world = world;
+  a.R = out.size(0);
+  a.parity = parity;
+  a.V_total = V_total;
+  a.mine = reinterpret_cast<const b200::sampling::CandRow*>(mine.data_ptr());
+  for (int p = 0; p < world; ++p) {
+    a.region[p] = reinterpret_cast<b200::sampling::CandRow*>(ptrs[p]);
+    a.flags[p] = reinterpret_cast<uint32_t*>(ptrs[world + p]);
+  }
+  a.epochs = reinterpret_cast<uint32_t*>(epochs_ptr);
+  a.temperature = opt_f32(temperature);
+  a.top_k = opt_i32(top_k);
+  a.top_p = opt_f32(top_p);
+  a.min_p = opt_f32(min_p);
+  a.seeds = opt_i64(seeds);
+  a.steps = opt_i32(steps);
+  a.out = out.data_ptr<int64_t>();
+  a.err = err_ptr(mine);
+  const c10::cuda::CUDAGuard g(mine.device());
+  guarded([&] { b200::sampling::run_topk_exchange(a, stream_of(mine)); });
+}
+
 // Row-parallel GEMM whose epilogue performs the reduce-scatter: C rows go to their owner
 // rank's receive slot (`recv` = every rank's slot address, peers included).
 void gemm_bf16_rs(const Tensor& A, const Tensor& B, const std::vector<int64_t>& recv,
@@ -1561,6 +1647,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("world"), py::arg("T"), py::arg("H"), py::arg("blocks"), py::arg("parity"),
         py::arg("two_shot"), py::arg("residual"), py::arg("weight"), py::arg("eps"),
         py::arg("rs_rows") = 0);
+  m.def("cand_row_bytes", &cand_row_bytes, "bytes of one candidate row");
+  m.def("shard_candidates", &shard_candidates, "per-shard top-k candidates of each logits row",
+        py::arg("logits"), py::arg("temperature"), py::arg("seeds"), py::arg("steps"),
+        py::arg("vocab_offset"), py::arg("out"));
+  m.def("merge_candidates_local", &merge_candidates_local,
+        "merge [world][R] candidate rows held locally and sample (top-k / top-p / min-p)");
+  m.def("topk_exchange", &topk_exchange,
+        "exchange candidate rows over NVLink, then merge and sample each row");
   m.def("nvls_allreduce", &nvls_allreduce,
         "NVLS (multimem) all-reduce (+ residual + RMSNorm, + optional 1x128 e4m3 output)",
         py::arg("like"), py::arg("ptrs"), py::arg("rank"), py::arg("world"), py::arg("T"),

@@ -49,3 +49,39 @@ def test_engine_logprobs_on_gpu():
         for t, d in zip(c.token_ids, c.logprobs):
             assert t in d and len(d) >= 4 and all(v.logprob <= 0 for v in d.values())
     llm.shutdown()
+
+
+def _sampling_batch(R, V, seed):
+    g = torch.Generator().manual_seed(seed)
+    scale = torch.where(torch.arange(R) % 3 == 0, 12.0, 2.0)  # some rows peaked
+    logits = (torch.randn(R, V, generator=g) * scale[:, None]).cuda()
+    temp = torch.tensor([0.0 if r % 7 == 0 else (0.7 if r % 2 else 1.0) for r in range(R)]).cuda()
+    top_k = torch.tensor([[0, 5, 50, 128, 300][r % 5] for r in range(R)], dtype=torch.int32).cuda()
+    top_p = torch.tensor([[1.0, 0.9, 0.5, 1.0][r % 4] for r in range(R)]).cuda()
+    min_p = torch.tensor([[0.0, 0.0, 0.05][r % 3] for r in range(R)]).cuda()
+    seeds = torch.arange(R, dtype=torch.int64).cuda() * 7919 + 3
+    steps = (torch.arange(R, dtype=torch.int32) % 11).cuda()
+    return logits, temp, top_k, top_p, min_p, seeds, steps
+
+
+def test_topk_candidates_merge_matches_full_vocab_sampler():
+    """Vocab shards reduced to candidate rows and merged (the single-GPU form of the NVLink
+    exchange) draw exactly the token the full-vocab sampler draws, on every row they decide;
+    rows with top-k <= 128, greedy rows and unfiltered rows are always decided."""
+    from vllm_musa_b200 import ops
+    from vllm_musa_b200.ops.sampling import merge_candidates_local, shard_candidates
+    R, V, world = 96, 32000, 4
+    Vs = V // world
+    logits, temp, top_k, top_p, min_p, seeds, steps = _sampling_batch(R, V, 5)
+    ref = ops.sample_tokens(logits, temp, top_k, top_p, min_p, seeds, steps)
+    cands = torch.cat([shard_candidates(logits[:, s * Vs:(s + 1) * Vs].contiguous(), temp,
+                                        seeds, steps, s * Vs) for s in range(world)])
+    out = merge_candidates_local(cands, world, R, temp, top_k, top_p, min_p, seeds, steps, V)
+    torch.cuda.synchronize()
+    decided = out >= 0
+    assert torch.equal(out[decided], ref[decided])
+    k, t = top_k.cpu(), temp.cpu()
+    must = (t == 0) | ((k > 0) & (k <= 128)) | \
+        ((k == 0) & (top_p.cpu() == 1.0) & (min_p.cpu() == 0.0))
+    assert bool(decided.cpu()[must].all()), (out.cpu()[must], must.nonzero())
+    assert decided.float().mean() > 0.6

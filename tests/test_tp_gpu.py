@@ -116,3 +116,13 @@ def test_deepseek_dcp2_matches_tp1(tmp_path, eager):
     assert (la - lb).abs().max().item() < 0.05
     same_first = sum(x[0] == y[0] for x, y in zip(a["tokens"], b0["tokens"]))
     assert same_first >= 3
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_vocab_parallel_topk_exchange_2gpu(tmp_path):
+    """Top-k / top-p / min-p rows sampled from candidate rows exchanged over NVLink equal the
+    draws from the gathered logits; greedy and top-k rows are always decided."""
+    out = str(tmp_path / "topk.json")
+    _torchrun(2, ["--mode", "topk", "--out", out], 29671)
+    for r in json.load(open(out)):
+        assert r["mismatch"] == 0 and r["undecided_topk"] == 0 and r["decided"] > 0.5, r

@@ -2,6 +2,8 @@
 
 --mode ar   : fused all-reduce + residual + RMSNorm kernel vs NCCL all-reduce + PyTorch math,
               one-shot and two-shot sizes, several calls in a row (parity / epoch reuse).
+--mode topk : vocab-parallel top-k / top-p / min-p sampling through the NVLink candidate
+              exchange vs sampling the gathered logits.
 --mode llm  : greedy generation of a small Llama-architecture model at TP = WORLD_SIZE;
               writes tokens and first-step logits (gathered to full vocab) as JSON.
 """
@@ -78,6 +80,48 @@ def mode_ar(out_path):
     if st.rank == 0:
         with open(out_path, "w") as f:
             json.dump(errs, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def mode_topk(out_path):
+    """Vocab-parallel top-k / top-p / min-p sampling over NVLink (candidate rows exchanged and
+    merged in one kernel) against sampling the gathered logits on every rank."""
+    from vllm_musa_b200 import ops
+    from vllm_musa_b200.parallel.custom_ar import maybe_create_custom_allreduce
+    from vllm_musa_b200.parallel.state import init_distributed
+    world = int(os.environ["WORLD_SIZE"])
+    st = init_distributed(tp_size=world)
+    dev = torch.device("cuda", st.local_rank)
+    ar = maybe_create_custom_allreduce(st, dev, max_tokens=1024, hidden=1024)
+    assert ar is not None
+    res = []
+    for it, (R, V) in enumerate([(64, 16000), (200, 32000), (7, 8000)]):
+        g = torch.Generator().manual_seed(40 + it)
+        scale = torch.where(torch.arange(R) % 3 == 0, 12.0, 2.0)
+        logits = (torch.randn(R, V, generator=g) * scale[:, None]).to(dev)
+        temp = torch.tensor([0.0 if r % 7 == 0 else 0.8 for r in range(R)], device=dev)
+        top_k = torch.tensor([[0, 5, 50, 128][r % 4] for r in range(R)], dtype=torch.int32,
+                             device=dev)
+        top_p = torch.tensor([[1.0, 0.9, 0.5][r % 3] for r in range(R)], device=dev)
+        min_p = torch.tensor([[0.0, 0.05][r % 2] for r in range(R)], device=dev)
+        seeds = torch.arange(R, dtype=torch.int64, device=dev) * 31 + 1
+        steps = torch.arange(R, dtype=torch.int32, device=dev) % 5
+        Vs = V // world
+        shard = logits[:, st.rank * Vs:(st.rank + 1) * Vs].contiguous()
+        ref = ops.sample_tokens(logits, temp, top_k, top_p, min_p, seeds, steps)
+        out = ar.sample_topk(shard, temp, top_k, top_p, min_p, seeds, steps, st.rank * Vs, V)
+        torch.cuda.synchronize()
+        dec = out >= 0
+        must = (temp == 0) | (top_k > 0)
+        res.append({"R": R, "V": V, "decided": float(dec.float().mean()),
+                    "mismatch": int((out[dec] != ref[dec]).sum()),
+                    "undecided_topk": int((~dec & must).sum())})
+    ops._ext.check_device_errors()
+    ar.close()
+    if st.rank == 0:
+        with open(out_path, "w") as f:
+            json.dump(res, f)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -223,7 +267,7 @@ def mode_llm(out_path, tp, eager, model="dense", ep=False, dcp=1):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["ar", "gemm_rs", "cand", "llm"], required=True)
+    ap.add_argument("--mode", choices=["ar", "gemm_rs", "cand", "topk", "llm"], required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--eager", action="store_true")
@@ -237,5 +281,7 @@ if __name__ == "__main__":
         mode_gemm_rs(a.out)
     elif a.mode == "cand":
         mode_cand(a.out)
+    elif a.mode == "topk":
+        mode_topk(a.out)
     else:
         mode_llm(a.out, a.tp, a.eager, a.model, a.ep, a.dcp)

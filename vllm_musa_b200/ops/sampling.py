@@ -163,3 +163,28 @@ def token_logprobs(raw: torch.Tensor, tokens: torch.Tensor, k: int):
         vals = torch.zeros(lp.shape[0], 0, device=lp.device)
         ids = torch.zeros(lp.shape[0], 0, dtype=torch.int64, device=lp.device)
     return ids, vals, tok_lp, rank
+
+
+def shard_candidates(logits: torch.Tensor, temperature, seeds, steps,
+                     vocab_offset: int = 0) -> torch.Tensor:
+    """Per-row candidate rows of this vocab shard (CUDA): the <= 128 largest scaled logits with
+    their global ids, the shard's max / exp-mass / completeness key and its Gumbel-max winner.
+    Returns uint8 [R, cand_row_bytes] (the layout of the CUDA CandRow)."""
+    mod = _ext.require()
+    R = logits.shape[0]
+    out = torch.empty(R, int(mod.cand_row_bytes()), dtype=torch.uint8, device=logits.device)
+    if R:
+        mod.shard_candidates(logits.contiguous(), temperature, seeds, steps, vocab_offset, out)
+    return out
+
+
+def merge_candidates_local(cands: torch.Tensor, world: int, R: int, temperature, top_k, top_p,
+                           min_p, seeds, steps, V_total: int) -> torch.Tensor:
+    """Merge candidate rows [world][R] held on this GPU and sample each row; -1 marks a row the
+    candidates cannot decide exactly (the caller samples the gathered logits instead)."""
+    mod = _ext.require()
+    out = torch.empty(R, dtype=torch.int64, device=cands.device)
+    if R:
+        mod.merge_candidates_local(cands, world, R, temperature, top_k, top_p, min_p, seeds,
+                                   steps, V_total, out)
+    return out

@@ -84,8 +84,16 @@ class NvlsBuffer:
         self.buf = symm.empty(total, dtype=torch.uint8, device=device)
         self.buf.zero_()
         self.handle = symm.rendezvous(self.buf, group)
-        self.mc = int(self.handle.multicast_ptr) if self.handle.has_multicast_support() else 0
+        from torch._C._autograd import DeviceType
+        from torch._C._distributed_c10d import _SymmetricMemory
         self.base = self.buf.data_ptr()
+        self.mc = 0
+        if _SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index):
+            mc = int(self.handle.multicast_ptr or 0)
+            if mc:
+                # the multicast mapping covers the whole allocation: same offset as the tensor
+                # has from this rank's base of it
+                self.mc = mc + (self.base - int(self.handle.buffer_ptrs[st.tp_rank]))
         self.epochs = torch.zeros(2 * int(mod.comm_max_blocks()), dtype=torch.int32, device=device)
         dev = device.index
         self.staging = [mod.tensor_from_ptr(self.base + k * self.slot, [T, H], torch.bfloat16, dev)
@@ -140,7 +148,12 @@ class CustomAllReduce:
         self.cand_ids_off = (n * 4 + 255) // 256 * 256   # int64 ids after the fp32 scores
         self.cand_parity_bytes = self.cand_ids_off + (n * 8 + 255) // 256 * 256
         cand_bytes = 2 * self.cand_parity_bytes
-        total = self.cand_off + cand_bytes
+        # top-k / top-p candidate rows: [2 parities][world][topk_rows] rows of cand_row_bytes
+        self.topk_rows = min(max_tokens, 1024)
+        self.row_bytes = int(mod.cand_row_bytes())
+        self.topk_off = self.cand_off + cand_bytes
+        self.topk_parity_bytes = (self.world * self.topk_rows * self.row_bytes + 255) // 256 * 256
+        total = self.topk_off + 2 * self.topk_parity_bytes
         self.max_blocks = int(mod.comm_max_blocks())
         self.base = mod.ipc_malloc(total)
         self.opened = []
@@ -307,6 +320,27 @@ class CustomAllReduce:
         self.mod.exchange_candidates(vals.contiguous(), ids.contiguous(), out,
                                      vals_ptrs + ids_ptrs + flags, self.epochs, self.rank,
                                      self.world, k)
+        self.cand_parity ^= 1
+        return out
+
+    def sample_topk(self, logits, temperature, top_k, top_p, min_p, seeds, steps,
+                    vocab_offset: int, V_total: int) -> Optional[torch.Tensor]:
+        """Vocab-parallel sampling with top-k / top-p / min-p: each rank reduces its logits
+        shard to candidate rows (<= 128 per row), one kernel stores them into every peer's
+        region over NVLink, barriers and merges (csrc/sampling/topk_exchange.cu).  Returns the
+        sampled ids, -1 on rows the candidates cannot decide exactly, or None when the batch
+        does not fit the region.  Same parity / ordering argument as ``merge_candidates``."""
+        from ..ops.sampling import shard_candidates
+        R = logits.shape[0]
+        if R > self.topk_rows:
+            return None
+        mine = shard_candidates(logits, temperature, seeds, steps, vocab_offset)
+        k = self.cand_parity
+        regions = [b + self.topk_off + k * self.topk_parity_bytes for b in self.peer_base]
+        flags = [b + self.flag_off for b in self.peer_base]
+        out = torch.empty(R, dtype=torch.int64, device=logits.device)
+        self.mod.topk_exchange(mine, regions + flags, self.epochs, self.rank, self.world, k,
+                               V_total, temperature, top_k, top_p, min_p, seeds, steps, out)
         self.cand_parity ^= 1
         return out
 

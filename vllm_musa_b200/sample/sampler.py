@@ -8,7 +8,9 @@ ranks exchange the [S] candidates (one kernel storing them into every peer's can
 over NVLink, then an epoch barrier and the merge, when the P2P communicator is up; NCCL
 all-gather otherwise), and the max wins: identical on every rank because the
 Gumbel noise is a function of (seed, step, global token id).  Rows that use top-k / top-p /
-min-p need global order statistics, so those batches gather the full logits first.
+min-p need global order statistics: each rank reduces its shard to at most 128 candidates per
+row and the candidate rows (not the logits) cross NVLink, merged into the exact global
+filtered draw; only a batch the candidates cannot decide exactly gathers the full logits.
 """
 from __future__ import annotations
 
@@ -34,6 +36,15 @@ class Sampler:
             return ops.sample_tokens(logits, temperature, top_k, top_p, min_p, seeds, steps,
                                      generator=generator)
         if any_filter:
+            custom = getattr(self.comm, "custom", None)
+            if logits.is_cuda and custom is not None and temperature is not None:
+                # candidate rows exchanged over NVLink instead of the logits; a row the
+                # candidates cannot decide exactly (-1, the same on every rank) sends the
+                # batch through the gathered path below
+                out = custom.sample_topk(logits, temperature, top_k, top_p, min_p, seeds, steps,
+                                         self.vocab_start, logits.shape[1] * self.tp)
+                if out is not None and int(out.min()) >= 0:
+                    return out
             full = self.comm.all_gather(logits, dim=1)
             return ops.sample_tokens(full, temperature, top_k, top_p, min_p, seeds, steps,
                                      generator=generator)
