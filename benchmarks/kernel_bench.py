@@ -215,9 +215,11 @@ def case_gdn_decode(it):
     seq = torch.full((B,), 100, dtype=torch.int32, device="cuda")
     slots = torch.arange(B, dtype=torch.int32, device="cuda")
     out = torch.empty(B, Hv * 128, dtype=torch.bfloat16, device="cuda")
-    us = timed(lambda i: gdn.gdn_recurrent(qkv, ba, A, dt, state, cu, seq, slots, Hk, Hv, out), it)
-    report("gdn_recurrent_decode", [B, Hk, Hv], us, 2 * B * Hv * 128 * 128 * 4,
-           4 * B * Hv * 128 * 128)
+    for single in (True, False):
+        us = timed(lambda i: gdn.gdn_recurrent(qkv, ba, A, dt, state, cu, seq, slots, Hk, Hv, out,
+                                               single_token=single), it)
+        report("gdn_decode" if single else "gdn_recurrent_decode", [B, Hk, Hv], us,
+               2 * B * Hv * 128 * 128 * 4, 4 * B * Hv * 128 * 128)
 
 
 def case_gdn_prefill(it):

@@ -2,9 +2,9 @@
 128-row tiles per CTA, or 4 = a CTA pair on a 256-row tile) for a model's linear shapes
 and write the fastest plan per (N, K, M) to vllm_musa_b200/tuning/gemm_bf16.json.
 
-Timing: CUDA events on the launching stream after warm-up; launches cycle through copies of
-the weight whose total exceeds L2 (every launch reads its weight from HBM), averaged over a
-back-to-back loop; median of --reps.  Also reports cuBLAS (torch.matmul) for the same
+Timing: a loop of launches cycling through copies of the weight whose total exceeds L2 (every
+launch reads its weight from HBM) is captured in a CUDA graph and replayed; CUDA events around
+the replay, averaged over the loop; median of --reps.  Also reports cuBLAS (torch.matmul) for the same
 shape as a yardstick and the achieved TB/s of weight streaming (decode) / TFLOP/s.
 
     python benchmarks/tune_gemm_bf16.py --model llama3-8b --tp 1 [--write]
@@ -45,21 +45,35 @@ def s_ok(M):
 
 
 def timed(fn, ws, reps):
-    """Median per-launch time of ``fn(w)`` cycling through weight copies ``ws`` whose total
-    size exceeds L2, so every launch streams its weights from HBM (as consecutive layers do
-    in a decode step); each sample averages a back-to-back loop of launches."""
+    """Median per-launch device time of ``fn(w)`` cycling through weight copies ``ws`` whose
+    total size exceeds L2, so every launch streams its weights from HBM (as consecutive layers
+    do in a decode step).  The loop of launches is captured once in a CUDA graph and replayed,
+    so the number is the kernels' back-to-back device time (with programmatic dependent launch
+    overlap between neighbours, as in the engine's captured decode steps), not the host's
+    per-call dispatch time."""
     for w in ws:
         fn(w)
-    loop = max(8, len(ws))
+    torch.cuda.synchronize()
+    loop = max(16, len(ws))
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for i in range(loop):
+                fn(ws[i % len(ws)])
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    torch.cuda.synchronize()
     ts = []
     for _ in range(reps):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for i in range(loop):
-            fn(ws[i % len(ws)])
+        g.replay()
         e.record()
         torch.cuda.synchronize()
         ts.append(s.elapsed_time(e) * 1e3 / loop)
+    del g
     return statistics.median(ts)
 
 

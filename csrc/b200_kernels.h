@@ -108,7 +108,8 @@ void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,
 void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld_ba,
                        const float* A_log, const float* dt_bias, float* state,
                        const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
-                       int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s);
+                       int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s,
+                       bool single_token = false);
 void run_sigmoid_gate(void* out, int64_t ldo, const void* gate, int64_t ldg, int T, int W,
                       cudaStream_t s);
 // chunked prefill (gdn_chunked.cu): workspace of chunked_workspace_bytes(max_chunks, Hv) with

@@ -214,6 +214,86 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_recurrent_kernel(RecParams p)
     reinterpret_cast<float4*>(gstate)[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
 }
 
+// Decode form (every request has exactly one new token): one CTA per (request, value head),
+// 8 warps x 16 value rows.  A lane owns key dims [4 lane, 4 lane + 4) of its warp's 16 state
+// rows, so each warp issues 16 independent 16-byte loads per lane before any arithmetic and
+// the whole 64 KB state of the head is in flight at once (the step is a load-update-store of
+// the state: HBM-bound).  Per row: s = e^g S_v; u = beta (v_v - s.k); s += u k; o_v = s.q, with
+// the two dot products as warp reductions.  Same math and state layout as gdn_recurrent_kernel.
+constexpr int kDecThreads = 256;
+constexpr int kDecRowsPerWarp = kDV / (kDecThreads / 32);  // 16
+
+__global__ void __launch_bounds__(kDecThreads, 2) gdn_decode_kernel(RecParams p) {
+  pdl_launch_dependents();
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = p.cu_q[r];
+  const bool hist = p.seq_lens[r] - 1 > 0;
+  const int hk = h / (p.Hv / p.Hk);
+  const int v0 = warp * kDecRowsPerWarp;
+  float* gstate = p.state + (((size_t)p.slots[r] * p.Hv + h) * kDV + v0) * kDK + lane * 4;
+  float4 S[kDecRowsPerWarp];
+  if (hist) {
+#pragma unroll
+    for (int j = 0; j < kDecRowsPerWarp; ++j)
+      S[j] = *reinterpret_cast<const float4*>(gstate + (size_t)j * kDK);
+  } else {
+#pragma unroll
+    for (int j = 0; j < kDecRowsPerWarp; ++j) S[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const __nv_bfloat16* row = p.qkv + (size_t)t * p.ld_qkv;
+  const int qoff = hk * kDK, koff = p.Hk * kDK + hk * kDK, voff = 2 * p.Hk * kDK + h * kDV;
+  const uint2 qr = *reinterpret_cast<const uint2*>(row + qoff + lane * 4);
+  const uint2 kr = *reinterpret_cast<const uint2*>(row + koff + lane * 4);
+  const float vv = lane < kDecRowsPerWarp ? bf2f(row[voff + v0 + lane]) : 0.f;
+  const __nv_bfloat16* ba = p.ba + (size_t)t * p.ld_ba;
+  const float b = bf2f(ba[h]), a = bf2f(ba[p.Hv + h]);
+  float q[4], k[4];
+  {
+    const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qr);
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kr);
+    const float2 q01 = __bfloat1622float2(q2[0]), q23 = __bfloat1622float2(q2[1]);
+    const float2 k01 = __bfloat1622float2(k2[0]), k23 = __bfloat1622float2(k2[1]);
+    q[0] = q01.x; q[1] = q01.y; q[2] = q23.x; q[3] = q23.y;
+    k[0] = k01.x; k[1] = k01.y; k[2] = k23.x; k[3] = k23.y;
+  }
+  const float sqq = warp_sum(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
+  const float skk = warp_sum(k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3]);
+  const float iq = rsqrtf(sqq + 1e-6f) * rsqrtf((float)kDK), ik = rsqrtf(skk + 1e-6f);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    q[e] *= iq;
+    k[e] *= ik;
+  }
+  const float x = a + p.dt_bias[h];
+  const float sp = x > 20.f ? x : log1pf(__expf(x));  // softplus
+  const float decay = __expf(-__expf(p.A_log[h]) * sp);
+  const float beta = 1.f / (1.f + __expf(-b));
+  float mine = 0.f;  // lane j < 16 keeps the output of row v0 + j
+#pragma unroll
+  for (int j = 0; j < kDecRowsPerWarp; ++j) {
+    float4 s4 = S[j];
+    s4.x *= decay;
+    s4.y *= decay;
+    s4.z *= decay;
+    s4.w *= decay;
+    const float dot = warp_sum(s4.x * k[0] + s4.y * k[1] + s4.z * k[2] + s4.w * k[3]);
+    const float u = (__shfl_sync(0xffffffffu, vv, j) - dot) * beta;
+    s4.x += k[0] * u;
+    s4.y += k[1] * u;
+    s4.z += k[2] * u;
+    s4.w += k[3] * u;
+    const float o = warp_sum(s4.x * q[0] + s4.y * q[1] + s4.z * q[2] + s4.w * q[3]);
+    if (lane == j) mine = o;
+    S[j] = s4;
+  }
+#pragma unroll
+  for (int j = 0; j < kDecRowsPerWarp; ++j)
+    *reinterpret_cast<float4*>(gstate + (size_t)j * kDK) = S[j];
+  if (lane < kDecRowsPerWarp)
+    p.out[(size_t)t * p.ld_out + h * kDV + v0 + lane] = f2bf(mine);
+}
+
 // Attention output gate (Qwen3-Next gated attention): out *= sigmoid(gate), both [T, W].
 __global__ void sigmoid_gate_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo,
                                     const __nv_bfloat16* __restrict__ gate, int64_t ldg, int W) {
@@ -253,7 +333,8 @@ void run_causal_conv1d(const void* x, int64_t ldx, const void* w, void* state,
 void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t ld_ba,
                        const float* A_log, const float* dt_bias, float* state,
                        const int32_t* cu_q, const int32_t* seq_lens, const int32_t* slots, int R,
-                       int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s) {
+                       int Hk, int Hv, void* out, int64_t ld_out, cudaStream_t s,
+                       bool single_token) {
   B200_REQUIRE(Hv % Hk == 0, "gdn: value heads must be a multiple of key heads");
   if (R == 0) return;
   RecParams p;
@@ -272,7 +353,10 @@ void run_gdn_recurrent(const void* qkv, int64_t ld_qkv, const void* ba, int64_t 
   p.R = R;
   p.Hk = Hk;
   p.Hv = Hv;
-  gdn_recurrent_kernel<<<dim3(R, Hv, kVSplit), kThreads, 0, s>>>(p);
+  if (single_token)
+    gdn_decode_kernel<<<dim3(R, Hv), kDecThreads, 0, s>>>(p);
+  else
+    gdn_recurrent_kernel<<<dim3(R, Hv, kVSplit), kThreads, 0, s>>>(p);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
 }

@@ -996,7 +996,7 @@ void gdn_chunked(const Tensor& qkv, const Tensor& ba, const Tensor& A_log, const
 
 void gdn_recurrent(const Tensor& qkv, const Tensor& ba, const Tensor& A_log, const Tensor& dt_bias,
                    Tensor& state, const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots,
-                   int64_t Hk, int64_t Hv, Tensor& out) {
+                   int64_t Hk, int64_t Hv, Tensor& out, bool single_token) {
   CHECK_CUDA(qkv);
   CHECK_BF16(qkv);
   CHECK_ROWMAJOR(qkv);
@@ -1014,7 +1014,7 @@ void gdn_recurrent(const Tensor& qkv, const Tensor& ba, const Tensor& A_log, con
                                  state.data_ptr<float>(), cu_q.data_ptr<int32_t>(),
                                  seq_lens.data_ptr<int32_t>(), slots.data_ptr<int32_t>(),
                                  seq_lens.numel(), Hk, Hv, out.data_ptr(), out.stride(0),
-                                 stream_of(qkv));
+                                 stream_of(qkv), single_token);
   });
 }
 
@@ -1577,7 +1577,8 @@ TORCH_LIBRARY(b200, m) {
   m.def("gated_rmsnorm(Tensor(a!) out, Tensor y, Tensor z, Tensor w, int group, float eps) -> ()");
   m.def(
       "gdn_recurrent(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
-      "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out) -> ()");
+      "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out, "
+      "bool single_token=False) -> ()");
   m.def(
       "gdn_chunked(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
       "Tensor cu_q, Tensor seq_lens, Tensor slots, int Hk, int Hv, Tensor(b!) out, "

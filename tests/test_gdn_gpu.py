@@ -62,6 +62,31 @@ def test_gdn_recurrent(Hk, Hv):
     torch.testing.assert_close(st.cpu(), ref_state, rtol=2e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize("Hk,Hv", [(1, 2), (16, 32)])
+def test_gdn_decode_single_token(Hk, Hv):
+    """Decode rows (one new token each, some without history) through the single-token kernel
+    against the fp32 PyTorch recurrence."""
+    g = torch.Generator().manual_seed(5 + Hv)
+    R = 37
+    q_lens, hist = [1] * R, [(r * 7) % 5 for r in range(R)]
+    cu, seq, _ = _batch(q_lens, hist, g)
+    slots = torch.randperm(64, generator=g)[:R].to(torch.int32)
+    T = int(cu[-1])
+    qkv = torch.randn(T, (2 * Hk + Hv) * 128, generator=g).to(torch.bfloat16)
+    ba = torch.randn(T, 2 * Hv, generator=g).to(torch.bfloat16)
+    A_log = torch.log(torch.linspace(1, 16, Hv))
+    dt_bias = torch.randn(Hv, generator=g) * 0.5
+    nslots = 64
+    state = torch.randn(nslots, Hv, 128, 128, generator=g) * 0.05
+    ref_state = state.clone()
+    ref = gdn.gdn_recurrent(qkv, ba, A_log, dt_bias, ref_state, cu, seq, slots, Hk, Hv)
+    st = state.cuda()
+    out = gdn.gdn_recurrent(qkv.cuda(), ba.cuda(), A_log.cuda(), dt_bias.cuda(), st, cu.cuda(),
+                            seq.cuda(), slots.cuda(), Hk, Hv, single_token=True)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(st.cpu(), ref_state, rtol=2e-3, atol=2e-3)
+
+
 def test_sigmoid_gate_and_gated_norm_strided():
     g = torch.Generator().manual_seed(7)
     T, W = 37, 512

@@ -196,12 +196,14 @@ class Qwen3NextForCausalLM(Qwen3MoeForCausalLM):
         T = conv.shape[0]
         if npf == 0 or not conv.is_cuda:
             return gdn_ops.gdn_recurrent(conv, ba, e["A_log"], e["dt_bias"], state, meta.cu_q,
-                                         meta.seq_lens, meta.state_slots, self.Hk_g, self.Hv_g)
+                                         meta.seq_lens, meta.state_slots, self.Hk_g, self.Hv_g,
+                                         single_token=npf == 0)
         out = torch.empty(T, self.Hv_g * 128, dtype=conv.dtype, device=conv.device)
         sl, slots = meta.seq_lens, meta.state_slots
         if nd > 0:
             gdn_ops.gdn_recurrent(conv, ba, e["A_log"], e["dt_bias"], state, meta.cu_q[:nd + 1],
-                                  sl[:nd], slots[:nd], self.Hk_g, self.Hv_g, out=out)
+                                  sl[:nd], slots[:nd], self.Hk_g, self.Hv_g, out=out,
+                                  single_token=True)
         cu_p = meta.cu_q[nd:nd + npf + 1]
         fn = gdn_ops.gdn_chunked if T - nd >= gdn_ops.CHUNK_MIN_TOKENS else \
             gdn_ops.gdn_recurrent

@@ -46,9 +46,11 @@ def causal_conv1d(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, cu_q: t
 def gdn_recurrent(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
                   state: torch.Tensor, cu_q: torch.Tensor, seq_lens: torch.Tensor,
                   slots: torch.Tensor, Hk: int, Hv: int,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, single_token: bool = False) -> torch.Tensor:
     """Gated delta rule over each request's new tokens.  qkv [T, 2*Hk*128 + Hv*128] (conv
-    output: q | k | v), ba [T, 2*Hv] (b | a); state [slots, Hv, 128, 128] updated in place."""
+    output: q | k | v), ba [T, 2*Hv] (b | a); state [slots, Hv, 128, 128] updated in place.
+    ``single_token``: the caller guarantees one new token per request (decode rows), which
+    runs the decode kernel (every value row of a head's state loaded at once)."""
     T = qkv.shape[0]
     D = 128
     if out is None:
@@ -57,7 +59,7 @@ def gdn_recurrent(qkv: torch.Tensor, ba: torch.Tensor, A_log: torch.Tensor, dt_b
         return out
     if qkv.is_cuda:
         _ext.ops().gdn_recurrent(qkv, ba, A_log, dt_bias, state, cu_q, seq_lens, slots, Hk, Hv,
-                                 out)
+                                 out, single_token)
         return out
     rep = Hv // Hk
     cu = cu_q.tolist()
