@@ -120,6 +120,57 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int j = 0; j < E; ++j) dst[j] = f2bf(v[j]);
 }
 
+// Paged KV-cache insert of separate key / value tensors ([T, Hkv, D] with row and head
+// strides, as an attention layer hands them over after its own RoPE): one warp per (token,
+// KV head), 16-byte vectors, slot < 0 skips the token.  Same cache layout as above.
+template <int D>
+__global__ void __launch_bounds__(kWarps * 32)
+    kv_insert_kernel(const __nv_bfloat16* __restrict__ key, int64_t k_ld, int64_t k_hs,
+                     const __nv_bfloat16* __restrict__ value, int64_t v_ld, int64_t v_hs,
+                     __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+                     const int64_t* __restrict__ slot_mapping, int T, int Hkv, int block_size) {
+  constexpr int V = D / 8;  // 16-byte vectors per head row
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int64_t gid = (int64_t)blockIdx.x * kWarps + warp;
+  if (gid >= (int64_t)T * Hkv) return;
+  const int t = gid / Hkv, h = gid % Hkv;
+  const int64_t slot = slot_mapping[t];
+  if (slot < 0) return;
+  const int64_t blk = slot / block_size, off = slot % block_size;
+  const int64_t dst = ((blk * Hkv + h) * block_size + off) * D;
+  const uint4* ks = reinterpret_cast<const uint4*>(key + t * k_ld + h * k_hs);
+  const uint4* vs = reinterpret_cast<const uint4*>(value + t * v_ld + h * v_hs);
+  for (int i = lane; i < V; i += 32) {
+    reinterpret_cast<uint4*>(k_cache + dst)[i] = ks[i];
+    reinterpret_cast<uint4*>(v_cache + dst)[i] = vs[i];
+  }
+}
+
+void run_kv_insert(const void* key, int64_t k_ld, int64_t k_hs, const void* value, int64_t v_ld,
+                   int64_t v_hs, void* k_cache, void* v_cache, const int64_t* slot_mapping, int T,
+                   int Hkv, int D, int block_size, cudaStream_t s) {
+  if (T == 0) return;
+  B200_REQUIRE(k_ld % 8 == 0 && k_hs % 8 == 0 && v_ld % 8 == 0 && v_hs % 8 == 0,
+               "kv_insert: 16-byte aligned rows");
+  const int64_t warps = (int64_t)T * Hkv;
+  const int blocks = (int)((warps + kWarps - 1) / kWarps);
+#define B200_KVI(DD)                                                                           \
+  kv_insert_kernel<DD><<<blocks, kWarps * 32, 0, s>>>(                                         \
+      reinterpret_cast<const __nv_bfloat16*>(key), k_ld, k_hs,                                 \
+      reinterpret_cast<const __nv_bfloat16*>(value), v_ld, v_hs,                               \
+      reinterpret_cast<__nv_bfloat16*>(k_cache), reinterpret_cast<__nv_bfloat16*>(v_cache),   \
+      slot_mapping, T, Hkv, block_size)
+  switch (D) {
+    case 64: B200_KVI(64); break;
+    case 128: B200_KVI(128); break;
+    case 256: B200_KVI(256); break;
+    default: B200_REQUIRE(false, "kv_insert: head_dim must be 64, 128 or 256");
+  }
+#undef B200_KVI
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
 void run_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
   if (a.T == 0) return;
   B200_REQUIRE(a.rot_dim % 2 == 0 && a.rot_dim <= a.D, "rope_kv: rot_dim");

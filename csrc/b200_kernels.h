@@ -239,6 +239,11 @@ struct RopeKvArgs {
   MropeSpec mrope;
 };
 void run_rope_kv(const RopeKvArgs& a, cudaStream_t s);
+// Paged cache insert of separate key / value tensors [T, Hkv, D] (row stride *_ld, head stride
+// *_hs, in elements); caches [num_blocks, Hkv, block_size, D]; int64 slots, < 0 skipped.
+void run_kv_insert(const void* key, int64_t k_ld, int64_t k_hs, const void* value, int64_t v_ld,
+                   int64_t v_hs, void* k_cache, void* v_cache, const int64_t* slot_mapping, int T,
+                   int Hkv, int D, int block_size, cudaStream_t s);
 }  // namespace rope
 
 // ------------------------------------------------------------------------------- attention

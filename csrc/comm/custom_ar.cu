@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(512) fused_ar_kernel(ArParams a) {
       }
     }
   }
-  if (kTwoShot) block_barrier(a, 2 + a.parity, epoch);
+  if (kTwoShot || a.end_barrier) block_barrier(a, 2 + a.parity, epoch);
 }
 
 // Variant for many rows per rank (large T, two-shot or one-shot): one WARP per row and eight rows per
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kWarpRowThreads) fused_ar_warp_kernel(ArParams
       }
     }
   }
-  if (kTwoShot) block_barrier(a, 2 + a.parity, epoch);
+  if (kTwoShot || a.end_barrier) block_barrier(a, 2 + a.parity, epoch);
 }
 
 template <int VPW, bool kNorm, bool kTwoShot>

@@ -30,6 +30,9 @@ struct ArParams {
   // only): this rank's staging slot holds `world` blocks of rs_rows rows, block p = rank p's
   // partial sums of the rows this rank owns, so the reduction reads local memory only.
   int rs_rows = 0;
+  // one-shot calls end with a barrier too (callers whose buffer parity does not strictly
+  // alternate between consecutive calls)
+  bool end_barrier = false;
 };
 
 void run_fused_allreduce(const ArParams& a, cudaStream_t s);

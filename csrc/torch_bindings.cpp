@@ -324,6 +324,28 @@ void group_quant_fp8(Tensor& out, Tensor& scales, const Tensor& x) {
 }
 
 // ------------------------------------------------------------------------------------- rope+kv
+void kv_insert(const Tensor& key, const Tensor& value, Tensor& k_cache, Tensor& v_cache,
+               const Tensor& slot_mapping) {
+  CHECK_CUDA(key);
+  CHECK_BF16(key);
+  CHECK_BF16(value);
+  TORCH_CHECK(key.dim() == 3 && value.dim() == 3 && key.stride(2) == 1 && value.stride(2) == 1,
+              "kv_insert: key / value [T, Hkv, D] with unit inner stride");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous() &&
+                  k_cache.size(1) == key.size(1) && k_cache.size(3) == key.size(2),
+              "kv_insert: caches [num_blocks, Hkv, block_size, D]");
+  TORCH_CHECK(slot_mapping.scalar_type() == at::kLong && slot_mapping.is_contiguous(),
+              "kv_insert: int64 slot_mapping");
+  const int T = std::min<int64_t>(slot_mapping.numel(), key.size(0));
+  const c10::cuda::CUDAGuard g(key.device());
+  guarded([&] {
+    b200::rope::run_kv_insert(key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(),
+                              value.stride(0), value.stride(1), k_cache.data_ptr(),
+                              v_cache.data_ptr(), slot_mapping.data_ptr<int64_t>(), T,
+                              key.size(1), key.size(2), k_cache.size(2), stream_of(key));
+  });
+}
+
 void rope_kv(Tensor& qkv, const Tensor& positions, const Tensor& cos_sin,
              const c10::optional<Tensor>& q_norm_w, const c10::optional<Tensor>& k_norm_w,
              const c10::optional<Tensor>& k_cache_opt, const c10::optional<Tensor>& v_cache_opt,
@@ -1186,7 +1208,8 @@ void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w,
 void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64_t epochs_ptr,
                      int64_t rank, int64_t world, int64_t T, int64_t H, int64_t blocks,
                      int64_t parity, bool two_shot, const c10::optional<Tensor>& residual,
-                     const c10::optional<Tensor>& weight, double eps, int64_t rs_rows) {
+                     const c10::optional<Tensor>& weight, double eps, int64_t rs_rows,
+                     bool end_barrier) {
   TORCH_CHECK((int64_t)bufs.size() == 3 * world, "fused_allreduce: buffer table size");
   const c10::cuda::CUDAGuard g(like.device());
   b200::comm::ArParams a{};
@@ -1215,6 +1238,7 @@ void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64
   }
   a.eps = eps;
   a.rs_rows = rs_rows;
+  a.end_barrier = end_barrier;
   a.err = err_ptr(like);
   guarded([&] { b200::comm::run_fused_allreduce(a, stream_of(like)); });
 }
@@ -1510,6 +1534,9 @@ TORCH_LIBRARY(b200, m) {
   m.def("silu_mul_fp8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor x, float limit=0.0) -> ()");
   m.def("group_quant_fp8(Tensor(a!) out, Tensor(b!) scales, Tensor x) -> ()");
   m.def(
+      "kv_insert(Tensor key, Tensor value, Tensor(a!) k_cache, Tensor(b!) v_cache, "
+      "Tensor slot_mapping) -> ()");
+  m.def(
       "rope_kv(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor? q_norm_w, Tensor? "
       "k_norm_w, Tensor(b!)? k_cache, Tensor(c!)? v_cache, Tensor slot_mapping, int num_q_heads, "
       "int num_kv_heads, int rot_dim, bool neox=True, float eps=1e-6, int head_dim=0, "
@@ -1603,6 +1630,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("paged_prefill", &paged_prefill);
   m.impl("sample", &sample);
   m.impl("merge_candidates", &merge_candidates);
+  m.impl("kv_insert", &kv_insert);
   m.impl("apply_penalties", &apply_penalties);
   m.impl("embedding", &embedding);
   m.impl("gather_rows", &gather_rows);
@@ -1647,7 +1675,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("like"), py::arg("bufs"), py::arg("epochs_ptr"), py::arg("rank"),
         py::arg("world"), py::arg("T"), py::arg("H"), py::arg("blocks"), py::arg("parity"),
         py::arg("two_shot"), py::arg("residual"), py::arg("weight"), py::arg("eps"),
-        py::arg("rs_rows") = 0);
+        py::arg("rs_rows") = 0, py::arg("end_barrier") = false);
   m.def("cand_row_bytes", &cand_row_bytes, "bytes of one candidate row");
   m.def("shard_candidates", &shard_candidates, "per-shard top-k candidates of each logits row",
         py::arg("logits"), py::arg("temperature"), py::arg("seeds"), py::arg("steps"),

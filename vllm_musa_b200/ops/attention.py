@@ -213,3 +213,23 @@ def tree_ancestor_masks(parents: list) -> torch.Tensor:
         masks[i] = (1 << i) | (masks[par] if par >= 0 else 0)
     # int64 storage of the unsigned bit pattern
     return torch.tensor([m - (1 << 64) if m >= 1 << 63 else m for m in masks], dtype=torch.int64)
+
+
+def kv_insert(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+              v_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """Write key / value rows [T, Hkv, D] into the paged caches [num_blocks, Hkv, block_size,
+    D] at ``slot_mapping`` (int64, slot = block * block_size + offset; < 0 skipped; only the
+    first len(slot_mapping) rows are written)."""
+    n = min(int(slot_mapping.numel()), key.shape[0])
+    if n == 0:
+        return
+    if key.is_cuda:
+        _ext.ops().kv_insert(key, value, k_cache, v_cache, slot_mapping.to(torch.int64))
+        return
+    bs = k_cache.shape[2]
+    s = slot_mapping[:n].long()
+    keep = s >= 0
+    s = s[keep]
+    blk, off = s // bs, s % bs
+    k_cache[blk, :, off, :] = key[:n][keep].to(k_cache.dtype)
+    v_cache[blk, :, off, :] = value[:n][keep].to(v_cache.dtype)

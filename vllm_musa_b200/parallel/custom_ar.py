@@ -181,6 +181,9 @@ class CustomAllReduce:
             self._bufs.append(staging + out + flags)
         self.parity = 0
         self.cand_parity = 0
+        # every kernel ends with a barrier (needed when calls are not strictly alternating
+        # buffers, e.g. vLLM mixing eager calls and graph replays)
+        self.end_barrier = False
         self.nvls: Optional[NvlsBuffer] = None
         if NVLS:
             self._init_nvls(st, device, max_tokens, hidden)
@@ -258,10 +261,14 @@ class CustomAllReduce:
         two_shot, blocks = self._plan(T)
         self.mod.fused_allreduce(x, self._bufs[self.parity], self.epochs, self.rank, self.world,
                                  T, self.hidden, blocks, self.parity, two_shot, residual, weight,
-                                 eps)
+                                 eps, 0, self.end_barrier)
         out = self._out[self.parity][:T]
         self.parity ^= 1
         return out
+
+    def all_reduce_out_of_place(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum over the ranks into a new tensor (x unchanged)."""
+        return self._run(x, None, None, 0.0).clone()
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         out = self._run(x, None, None, 0.0)

@@ -2,8 +2,9 @@
 
 Subclasses vLLM's NVML CUDA platform and changes what the reference's MUSAPlatform changes for
 its device (vllm_musa/platform.py:245-955): default KV block size 64 (one TMA box per page),
-the b200 IR-op providers first in priority, custom ops enabled, the custom all-reduce on, a
-device-architecture check at worker start.
+the b200 IR-op providers first in priority, custom ops enabled, this package's attention
+backend (vllm_backend.py) and device communicator (vllm_comm.py: NVSwitch all-reduce), the
+post-grad fusion passes, a device-architecture check at worker start.
 """
 from __future__ import annotations
 
@@ -50,6 +51,26 @@ class B200Platform(_Base):
     @classmethod
     def get_pass_manager_cls(cls) -> str:
         return "vllm_musa_b200.compile.vllm_pass_manager.B200PostGradPassManager"
+
+    @classmethod
+    def get_attn_backend_cls(cls, selected_backend, attn_selector_config, num_heads=None) -> str:
+        """This package's paged-attention backend for the decoder attention it serves (bf16,
+        head size 64 / 128 / 256, bf16 KV cache, no MLA / sparse / encoder attention) when no
+        backend was requested explicitly; vLLM's CUDA selection otherwise.  Reference:
+        vllm_musa/platform.py:730-836 (get_valid_backends / get_attn_backend_cls)."""
+        from . import vllm_backend
+        if selected_backend is None and vllm_backend.serves(attn_selector_config):
+            path = vllm_backend.register()
+            log.info("attention backend: %s", path)
+            return path
+        return super().get_attn_backend_cls(selected_backend, attn_selector_config,  # type: ignore[misc]
+                                            num_heads)
+
+    @classmethod
+    def get_device_communicator_cls(cls) -> str:
+        """vLLM's CUDA communicator with the tensor-parallel all-reduce on this package's
+        NVSwitch kernels (reference: vllm_musa/platform.py:890-892)."""
+        return "vllm_musa_b200.vllm_comm.B200Communicator"
 
     @classmethod
     def use_custom_allreduce(cls) -> bool:
