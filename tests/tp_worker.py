@@ -33,6 +33,10 @@ def mode_ar(out_path):
     st = init_distributed(tp_size=world)
     dev = torch.device("cuda", st.local_rank)
     H = 4096
+    import vllm_musa_b200.parallel.custom_ar as car
+    # numerics of every kernel: NVLS two-shot above 64 KiB, peer-to-peer below
+    car.NVLS_MIN_BYTES = {w: 64 << 10 for w in (2, 4, 8)}
+    car.NVLS_QUANT_MIN_ROWS = 1
     ar = maybe_create_custom_allreduce(st, dev, max_tokens=2048, hidden=H)
     assert ar is not None, "custom all-reduce did not initialise"
     errs = []

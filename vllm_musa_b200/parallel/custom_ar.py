@@ -45,9 +45,20 @@ ONE_SHOT_READ_BYTES = 2 << 20
 # (256 tokens, Llama-3-8B) 9.31 ms/step fused vs 8.42 ms unfused, so it is opt-in.
 FUSE_GEMM_RS = os.environ.get("B200_FUSE_GEMM_RS", "0") == "1"
 NVLS = os.environ.get("B200_AR_NVLS", "1") != "0"
-# messages of at most this many bytes stay on the peer-to-peer one-shot kernel (one barrier,
-# plain loads) when NVLS is up; larger ones take the NVLS two-shot kernel
-NVLS_MIN_BYTES = int(os.environ.get("B200_AR_NVLS_MIN_BYTES", str(64 << 10)))
+# Per-size choice between the peer-to-peer kernels and the NVLS kernel, by world size: messages
+# of more than NVLS_MIN_BYTES[world] bytes take NVLS two-shot (None: never).  Measured at TP=2
+# (CUDA-graph replays, H=4096): peer-to-peer wins at every size (one-shot 22.0 us vs NVLS
+# 30.3 / 25.1 us at 256 rows; two-shot 127.5 us vs NVLS 204.6 us at 8192 rows): with two ranks
+# NVLS moves twice the bytes per link (the switch reads every copy, the local one included).
+# Its byte advantage starts at four ranks (1.25 vs 1.5 message copies per direction; 1.125 vs
+# 1.75 at eight); until those sizes are measured the default stays peer-to-peer and
+# B200_AR_NVLS_MIN_BYTES sets the threshold for every world size.
+NVLS_MIN_BYTES = {2: None, 4: None, 8: None}
+if os.environ.get("B200_AR_NVLS_MIN_BYTES"):
+    NVLS_MIN_BYTES = {w: int(os.environ["B200_AR_NVLS_MIN_BYTES"]) for w in (2, 4, 8)}
+# the NVLS kernel's fused 1x128 e4m3 output replaces AR + norm + a separate quantisation from
+# this many rows up (TP=2: 61.5 vs 81.6 us at 2048 rows, 33.3 vs 32.2 us at 256)
+NVLS_QUANT_MIN_ROWS = int(os.environ.get("B200_AR_NVLS_QUANT_MIN_ROWS", "1024"))
 
 
 def _consensus(ok: bool, group) -> bool:
@@ -224,9 +235,10 @@ class CustomAllReduce:
                 x.shape[0] <= self.max_tokens)
 
     def use_nvls(self, T: int) -> bool:
-        """NVLS two-shot for messages above the one-shot size (when NVLS is up)."""
-        return self.nvls is not None and T >= self.world and \
-            T * self.hidden * 2 > NVLS_MIN_BYTES
+        """NVLS two-shot for messages above the measured threshold of this world size."""
+        lim = NVLS_MIN_BYTES.get(self.world)
+        return self.nvls is not None and lim is not None and T >= self.world and \
+            T * self.hidden * 2 > lim
 
     def staging_view(self, T: int) -> torch.Tensor:
         if self.use_nvls(T):
@@ -280,16 +292,17 @@ class CustomAllReduce:
         return self._run(x, residual, weight, eps), residual
 
     def can_quant(self, x: torch.Tensor) -> bool:
-        """The fused all-reduce + norm can emit 1x128 e4m3 rows (NVLS kernels)."""
-        return self.nvls is not None and self.can_run(x) and self.hidden % 256 == 0
+        """The fused all-reduce + norm emits the 1x128 e4m3 rows itself (NVLS kernels), for
+        batches where that beats all-reduce + norm followed by the group quantisation."""
+        return (self.nvls is not None and self.can_run(x) and self.hidden % 256 == 0 and
+                x.shape[0] >= max(NVLS_QUANT_MIN_ROWS, self.world))
 
     def allreduce_add_rmsnorm_quant(self, x, residual, weight, eps):
         """residual <- AR(x) + residual; returns (q, scales) of RMSNorm(residual) * weight per
         token in 1x128 e4m3 groups, produced inside the all-reduce kernel (NVLS one-shot for
         small messages, two-shot beyond)."""
         T = x.shape[0]
-        two_shot = self.use_nvls(T)
-        return self._run_nvls(x, residual, weight, eps, two_shot=two_shot, quant=True)
+        return self._run_nvls(x, residual, weight, eps, two_shot=T >= self.world, quant=True)
 
     def staging_blocks(self, rows: int) -> torch.Tensor:
         """This call's staging slot viewed as world blocks of `rows` rows (epilogue / expert
