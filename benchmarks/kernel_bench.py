@@ -261,6 +261,92 @@ def case_moe(it):
            2 * T * k * 3 * H * I)
 
 
+def case_rope_kv(it):
+    """Fused RoPE + paged KV insert over one 8192-token prefill chunk (Llama-3-8B heads)."""
+    T, Hq, Hkv, D, bs = 8192, 32, 8, 128, 64
+    qkv = bf16(T, (Hq + 2 * Hkv) * D)
+    cs = ops.build_cos_sin_cache(D, 16384, 5e5, device="cuda")
+    pos = (torch.arange(T, device="cuda") % 8192).to(torch.int32)
+    nb = T // bs + 8
+    kc = bf16(nb, Hkv, bs, D)
+    vc = bf16(nb, Hkv, bs, D)
+    slots = torch.randperm(nb * bs, device="cuda")[:T].to(torch.int32)
+    us = timed(lambda i: ops.rope_kv(qkv, pos, cs, kc, vc, slots, Hq, Hkv, D, True), it)
+    # read q, k, v; write q back, k and v into the cache
+    report("rope_kv_prefill", [T, Hq, Hkv, D], us, T * (Hq + 2 * Hkv) * D * 2 * 2, 0)
+
+
+def case_silu_fp8(it):
+    """SwiGLU + 1x128 e4m3 quantisation of a gate/up output (DeepSeek dense MLP, 4096 tokens)."""
+    T, I = 4096, 18432 // 8
+    x = bf16(T, 2 * I)
+    us = timed(lambda i: ops.activation.silu_mul_fp8_quant(x), it)
+    report("silu_mul_fp8_quant", [T, I], us, T * 2 * I * 2 + T * I + T * I // 128 * 4, 0)
+
+
+def case_routers(it):
+    from vllm_musa_b200.ops import moe
+    T = 8192
+    lg = torch.randn(T, 128, device="cuda")
+    us = timed(lambda i: moe.topk_softmax(lg, 8), it)
+    report("topk_softmax_router", [T, 128, 8], us, T * 128 * 4 + T * 8 * 8, 0)
+    lg2 = torch.randn(T, 256, device="cuda")
+    bias = torch.randn(256, device="cuda") * 0.1
+    us = timed(lambda i: moe.grouped_topk(lg2, 8, 8, 4, bias=bias, sigmoid=True), it)
+    report("grouped_topk_router", [T, 256, 8], us, T * 256 * 4 + T * 8 * 8, 0)
+
+
+def case_indexer(it):
+    """Lightning-indexer scores + top-2048 for 64 decode rows over 8192-token contexts."""
+    from vllm_musa_b200.ops import mla
+    B, L, bs, k = 64, 8192, 64, 2048
+    per = L // bs
+    cache = bf16(B * per, bs, 128)
+    bt = torch.arange(B * per, dtype=torch.int32, device="cuda").view(B, per)
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    seq = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    q = bf16(B, 64 * 128)
+    w = torch.randn(B, 64, device="cuda") * 0.1
+    scores = torch.empty(B, L, device="cuda")
+    us = timed(lambda i: mla.indexer_scores(q, w, cache, bt, cu, seq, scores), it)
+    report("indexer_scores_decode", [B, L, 64, 128], us, B * L * 128 * 2 + B * L * 4,
+           2 * B * L * 64 * 128)
+    us = timed(lambda i: mla.topk_indices(scores, cu, seq, k), it)
+    report("indexer_topk_2048", [B, L, k], us, B * L * 4, 0)
+
+
+def case_conv1d(it):
+    """Causal conv1d (kernel 4) + SiLU over a prefill chunk of Qwen3-Next GDN channels."""
+    from vllm_musa_b200.ops import gdn
+    T, C = 8192, 2 * 16 * 128 + 32 * 128
+    x = bf16(T, C)
+    wt = bf16(C, 4)
+    state = bf16(4, C, 3)
+    cu = torch.tensor([0, T // 2, T], dtype=torch.int32, device="cuda")
+    seq = torch.tensor([T // 2 + 10, T // 2], dtype=torch.int32, device="cuda")
+    slots = torch.tensor([0, 1], dtype=torch.int32, device="cuda")
+    out = torch.empty(T, C, dtype=torch.bfloat16, device="cuda")
+    us = timed(lambda i: gdn.causal_conv1d(x, wt, state, cu, seq, slots, out), it)
+    report("causal_conv1d", [T, C], us, 2 * T * C * 2, 8 * T * C)
+
+
+def case_mamba2(it):
+    """Mamba2 SSD recurrence, one decode step for 256 sequences (Mamba2-2.7B heads)."""
+    from vllm_musa_b200.ops import mamba as M
+    B, H, G, P, N = 256, 80, 1, 64, 128
+    xbc = bf16(B, H * P + 2 * G * N)
+    dt = bf16(B, H)
+    dtb, Alog, D = (torch.rand(H, device="cuda") for _ in range(3))
+    st = torch.randn(B, H, P, N, device="cuda") * 0.1
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    sl = torch.full((B,), 100, dtype=torch.int32, device="cuda")
+    slots = torch.arange(B, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, H * P, dtype=torch.bfloat16, device="cuda")
+    us = timed(lambda i: M.mamba2_scan(xbc, H * P, H * P + G * N, dt, dtb, Alog, D, st, cu, sl,
+                                       slots, H, G, P, N, out=out), it)
+    report("mamba2_decode", [B, H, P, N], us, 2 * B * H * P * N * 4, 6 * B * H * P * N)
+
+
 def case_rmsnorm(it):
     T, H = 32768, 4096
     x, r = bf16(T, H), bf16(T, H)

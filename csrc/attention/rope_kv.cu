@@ -120,6 +120,118 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int j = 0; j < E; ++j) dst[j] = f2bf(v[j]);
 }
 
+// Vectorised form for the common layouts (no M-RoPE): lane l owns the E = D / 32 consecutive
+// elements [E l, E l + E) of the head, loaded and stored as one 4 / 8 / 16-byte vector; NeoX
+// pairs (i, i + rot_dim / 2) sit in lanes l and l ^ (rot_dim / 2E) and are exchanged with one
+// warp shuffle per element (rot_dim / 2E is a power of two for every supported rot_dim), GPT-J
+// pairs (i, i ^ 1) sit in the same lane; cos / sin come in as vectors of E (NeoX) or E / 2
+// (GPT-J) floats.  Same results as rope_kv_kernel.
+template <int E>
+struct BfVec;
+template <>
+struct BfVec<2> { using T = uint32_t; };
+template <>
+struct BfVec<4> { using T = uint2; };
+template <>
+struct BfVec<8> { using T = uint4; };
+
+template <int E>
+B200_DEVICE void load_bf(const __nv_bfloat16* p, float (&v)[E]) {
+  const typename BfVec<E>::T raw = *reinterpret_cast<const typename BfVec<E>::T*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < E / 2; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+template <int E>
+B200_DEVICE void store_bf(__nv_bfloat16* p, const float (&v)[E]) {
+  typename BfVec<E>::T raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < E / 2; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<typename BfVec<E>::T*>(p) = raw;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWarps * 32)
+    rope_kv_vec_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld_qkv,
+                       const int32_t* __restrict__ positions, const float* __restrict__ cos_sin,
+                       const __nv_bfloat16* __restrict__ q_norm_w,
+                       const __nv_bfloat16* __restrict__ k_norm_w,
+                       __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+                       const int32_t* __restrict__ slot_mapping, int T, int Hq, int Hkv,
+                       int block_size, int rot_dim, int neox, float eps) {
+  constexpr int E = D / 32;
+  pdl_launch_dependents();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  const int64_t gid = (int64_t)blockIdx.x * kWarps + warp;
+  if (gid >= (int64_t)T * heads) return;
+  const int t = gid / heads, h = gid % heads;
+  __nv_bfloat16* src = qkv + t * ld_qkv + (int64_t)h * D + lane * E;
+  float v[E];
+  load_bf<E>(src, v);
+  const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv, is_v = h >= Hq + Hkv;
+  if (!is_v) {
+    const __nv_bfloat16* nw = is_q ? q_norm_w : k_norm_w;
+    if (nw) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) ss += v[j] * v[j];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / D + eps);
+      float w[E];
+      load_bf<E>(nw + lane * E, w);
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = v[j] * inv * w[j];
+    }
+    if (rot_dim > 0) {
+      const int half = rot_dim / 2;
+      const float* cs = cos_sin + (int64_t)positions[t] * rot_dim;
+      if (neox) {
+        const int P = half / E;  // partner lane distance (power of two)
+        float o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) o[j] = __shfl_xor_sync(0xffffffffu, v[j], P);
+        if (lane < 2 * P) {
+          const int f0 = E * (lane & (P - 1));
+          const bool lo = lane < P;
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            const float c = cs[f0 + j], sn = cs[half + f0 + j];
+            v[j] = lo ? v[j] * c - o[j] * sn : v[j] * c + o[j] * sn;
+          }
+        }
+      } else if (lane * E < rot_dim) {
+#pragma unroll
+        for (int j = 0; j < E; j += 2) {
+          const int f = (lane * E + j) / 2;
+          const float c = cs[f], sn = cs[half + f];
+          const float a = v[j], b = v[j + 1];
+          v[j] = a * c - b * sn;
+          v[j + 1] = b * c + a * sn;
+        }
+      }
+    }
+  }
+  if (is_q || (is_k && k_cache == nullptr)) {
+    store_bf<E>(src, v);
+    return;
+  }
+  if (k_cache == nullptr) return;
+  const int32_t slot = slot_mapping ? slot_mapping[t] : -1;
+  if (slot < 0) return;
+  const int kvh = is_k ? h - Hq : h - Hq - Hkv;
+  const int64_t blk = slot / block_size, off = slot % block_size;
+  __nv_bfloat16* dst = (is_k ? k_cache : v_cache) + ((blk * Hkv + kvh) * block_size + off) * D +
+                       lane * E;
+  store_bf<E>(dst, v);
+}
+
 // Paged KV-cache insert of separate key / value tensors ([T, Hkv, D] with row and head
 // strides, as an attention layer hands them over after its own RoPE): one warp per (token,
 // KV head), 16-byte vectors, slot < 0 skips the token.  Same cache layout as above.
@@ -181,6 +293,41 @@ void run_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
   B200_REQUIRE(a.mrope.mode == 0 || a.mrope.pos_stride >= a.T, "rope_kv: M-RoPE position rows");
   const int64_t warps = (int64_t)a.T * (a.Hq + 2 * a.Hkv);
   const int blocks = (int)((warps + kWarps - 1) / kWarps);
+  // vectorised kernel: no M-RoPE, 4-byte aligned rows, and for NeoX a partner-lane distance
+  // rot_dim / (2E) that is a power of two
+  const int E = a.D / 32;
+  const int P = a.rot_dim / 2 / (E > 0 ? E : 1);
+  const bool vec = a.mrope.mode == 0 && (a.ld_qkv % E) == 0 && a.D % 64 == 0 &&
+                   (a.rot_dim == 0 || (a.neox ? (a.rot_dim % (2 * E) == 0 && P > 0 &&
+                                                 (P & (P - 1)) == 0)
+                                               : a.rot_dim % E == 0)) &&
+                   (reinterpret_cast<uintptr_t>(a.qkv) % (2 * E)) == 0;
+  if (vec) {
+#define B200_ROPE_VEC(DD)                                                                        \
+  rope_kv_vec_kernel<DD><<<blocks, kWarps * 32, 0, s>>>(                                         \
+      reinterpret_cast<__nv_bfloat16*>(a.qkv), a.ld_qkv, a.positions, a.cos_sin,                 \
+      reinterpret_cast<const __nv_bfloat16*>(a.q_norm_w),                                        \
+      reinterpret_cast<const __nv_bfloat16*>(a.k_norm_w),                                        \
+      reinterpret_cast<__nv_bfloat16*>(a.k_cache), reinterpret_cast<__nv_bfloat16*>(a.v_cache), \
+      a.slot_mapping, a.T, a.Hq, a.Hkv, a.block_size, a.rot_dim, a.neox ? 1 : 0, a.eps)
+    switch (a.D) {
+      case 64:
+        B200_ROPE_VEC(64);
+        break;
+      case 128:
+        B200_ROPE_VEC(128);
+        break;
+      case 256:
+        B200_ROPE_VEC(256);
+        break;
+      default:
+        B200_REQUIRE(false, "rope_kv: head_dim must be 64, 128 or 256");
+    }
+#undef B200_ROPE_VEC
+    B200_CUDA_OK(cudaGetLastError());
+    count_launch();
+    return;
+  }
 #define B200_ROPE_LAUNCH(DD)                                                                     \
   rope_kv_kernel<DD><<<blocks, kWarps * 32, 0, s>>>(                                             \
       reinterpret_cast<__nv_bfloat16*>(a.qkv), a.ld_qkv, a.positions, a.cos_sin,                 \
