@@ -256,9 +256,12 @@ class ParallelConfig:
 class SpeculativeConfig:
     """Speculative decoding.  ``ngram``: prompt lookup (drafts copied from the continuation of
     the latest earlier occurrence of the context's suffix n-gram, n in [prompt_lookup_min,
-    prompt_lookup_max]); ``mtp``: the checkpoint's multi-token-prediction layer (DeepSeek)."""
-    method: Optional[str] = None  # None | "ngram" | "mtp"
+    prompt_lookup_max]); ``mtp``: the checkpoint's multi-token-prediction layer (DeepSeek);
+    ``eagle``: an EAGLE-1 head over a dense decoder, loaded from ``model`` (a safetensors
+    directory) or, without one, seeded random weights."""
+    method: Optional[str] = None  # None | "ngram" | "mtp" | "eagle"
     num_speculative_tokens: int = 0
+    model: Optional[str] = None
     prompt_lookup_min: int = 1
     prompt_lookup_max: int = 4
 

@@ -102,6 +102,8 @@ class LLMEngine:
         self.model = cls(mcfg, st, self.comm, device)
         t0 = time.time()
         self._load_weights()
+        if config.speculative.method == "eagle":
+            self._load_eagle()
         log.info("weights ready in %.1fs", time.time() - t0)
         self.sampler = Sampler(self.comm, getattr(self.model, "vocab_start", 0), st.tp_size)
         dcp = config.parallel.decode_context_parallel_size
@@ -110,7 +112,7 @@ class LLMEngine:
                 raise ValueError("decode context parallelism needs an MLA model (DeepSeek-V2/V3)")
             self.model.enable_dcp(dcp, config.cache.block_size)
         self.runner = ModelRunner(config, self.model, self.sampler, device)
-        self.drafter = None  # model-based speculative proposer (MTP)
+        self.drafter = None  # model-based speculative proposer (MTP / EAGLE)
         num_blocks = self.runner.profile_and_allocate_kv()
         if st.tp_size > 1:
             # every rank must run with the same block count (lock-step schedulers)
@@ -142,6 +144,9 @@ class LLMEngine:
         if config.speculative.method == "mtp":
             from .spec_decode import MTPDrafter
             self.drafter = MTPDrafter(self, config.speculative.num_speculative_tokens or 1)
+        elif config.speculative.method == "eagle":
+            from .spec_decode import EagleDrafter
+            self.drafter = EagleDrafter(self, config.speculative.num_speculative_tokens or 1)
         self.runner.capture_graphs()
         self._ids = itertools.count()
         self._reqs: Dict[int, _Req] = {}
@@ -249,7 +254,7 @@ class LLMEngine:
         if spec.method == "ngram" and spec.num_speculative_tokens > 0:
             self.scheduler.propose_ngram(spec.num_speculative_tokens, spec.prompt_lookup_min,
                                          spec.prompt_lookup_max)
-        elif spec.method == "mtp" and self.drafter is not None:
+        elif spec.method in ("mtp", "eagle") and self.drafter is not None:
             self.drafter.propose(self.scheduler)
         plan = self.scheduler.schedule()
         if plan.num_reqs == 0:
@@ -401,6 +406,20 @@ class LLMEngine:
             self.model.load_weights(dummy_weights(mcfg, cfg.seed, cfg.init_std, device=dev))
         else:
             self.model.load_weights(safetensors_weights(cfg.model_path))
+
+    def _load_eagle(self) -> None:
+        """Attach an EAGLE head to the dense decoder (its KV is one extra cache layer)."""
+        from ..models.eagle import EagleHead, eagle_param_shapes
+        cfg, mcfg, device = self.config, self.config.model, self.device
+        head = EagleHead(self.model)
+        path = cfg.speculative.model
+        if path:
+            head.load_weights(safetensors_weights(path))
+        else:
+            dev = str(device) if device.type == "cuda" else "cpu"
+            head.load_weights(dummy_weights(mcfg, cfg.seed + 1, cfg.init_std, device=dev,
+                                            shapes=eagle_param_shapes(mcfg)))
+        self.model.draft_head = head
 
     # ------------------------------------------------------------------ sleep mode
     def _weight_tensors(self) -> list:

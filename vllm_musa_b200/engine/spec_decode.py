@@ -1,12 +1,14 @@
 """Model-based speculative proposers.
 
+Both drafters are one extra decoder layer fed by the target's own features:
 ``MTPDrafter`` drives DeepSeek's multi-token-prediction layer (the checkpoint's layer
-``num_layers``).  After every engine step it runs the MTP layer over each request's positions
-whose next token is now known: position p combines the embedding of token p+1 with the main
-model's final hidden state at p, writes the MTP layer's latent KV for p (same block table and
-slots as the main model), and its logits predict token p+2.  The prediction made at the
-position just before the request's pending token becomes the draft the scheduler verifies in
-the next step (exact acceptance, see csrc/runtime/scheduler.cpp).  Positions of rejected
+``num_layers``), ``EagleDrafter`` an EAGLE head over a dense decoder (``models/eagle.py``).
+After every engine step the drafter runs its layer over each request's positions whose next
+token is now known: position p combines the embedding of token p+1 with the main model's final
+hidden state at p, writes the draft layer's KV for p (extra cache layer ``num_layers``, same
+block table and slots as the main model), and its logits predict token p+2.  The prediction
+made at the position just before the request's pending token becomes the draft the scheduler
+verifies in the next step (exact acceptance, see csrc/runtime/scheduler.cpp).  Positions of rejected
 drafts are skipped: their main-model KV and hidden states are stale and get overwritten.
 
 Reference counterparts: vllm_musa/v1/spec_decode/utils.py:4-124 (eagle / MTP input
@@ -19,17 +21,18 @@ import torch
 from ..attention.metadata import AttnMetadata
 
 
-class MTPDrafter:
-    def __init__(self, engine, num_tokens: int = 1):
-        model = engine.model
-        if getattr(model, "mtp", None) is None:
-            raise ValueError("speculative method 'mtp' needs a checkpoint with an MTP layer "
-                             "(num_nextn_predict_layers > 0)")
+class ModelDrafter:
+    """One-token drafts from a draft layer: ``forward(ids, prev_hidden, meta, kv_caches)`` ->
+    hidden rows, ``logits(hidden)`` -> this rank's vocab shard of the draft logits."""
+
+    def __init__(self, engine, forward, logits, num_tokens: int = 1):
         if num_tokens != 1:
-            raise ValueError("the MTP drafter proposes one token per step")
+            raise ValueError("model-based drafters propose one token per step")
         self.engine = engine
-        self.model = model
+        self.model = engine.model
         self.runner = engine.runner
+        self.forward = forward
+        self.logits = logits
         self.proposed = 0
 
     def propose(self, scheduler) -> None:
@@ -79,12 +82,31 @@ class MTPDrafter:
                             tile_scratch=self.runner.tile_scratch,
                             state_slots=b.d["state_slots"][:R])
         prev = hidden[rows_t]
-        cache = self.runner.kv_caches[self.model.cfg.num_layers]
-        x = self.model.forward_mtp(ids, prev, meta, cache)
+        x = self.forward(ids, prev, meta, self.runner.kv_caches)
         last_rows = torch.tensor([c - 1 for c in cus[1:]], dtype=torch.long, device=dev)
-        logits = self.model.compute_logits_mtp(x[last_rows])
+        logits = self.logits(x[last_rows])
         draft = self.runner.sampler(logits, None, None, None, None, None, None).cpu().tolist()
         for k, (rid, ready) in enumerate(who):
             if ready:
                 sch.set_draft(rid, [int(draft[k])])
                 self.proposed += 1
+
+
+class MTPDrafter(ModelDrafter):
+    def __init__(self, engine, num_tokens: int = 1):
+        model = engine.model
+        if getattr(model, "mtp", None) is None:
+            raise ValueError("speculative method 'mtp' needs a checkpoint with an MTP layer "
+                             "(num_nextn_predict_layers > 0)")
+        n = model.cfg.num_layers
+        super().__init__(engine, lambda ids, prev, meta, kv: model.forward_mtp(ids, prev, meta,
+                                                                              kv[n]),
+                         model.compute_logits_mtp, num_tokens)
+
+
+class EagleDrafter(ModelDrafter):
+    def __init__(self, engine, num_tokens: int = 1):
+        head = getattr(engine.model, "draft_head", None)
+        if head is None:
+            raise ValueError("speculative method 'eagle' needs an EAGLE head on the model")
+        super().__init__(engine, head.forward_draft, head.compute_logits, num_tokens)

@@ -91,6 +91,7 @@ class DenseDecoderForCausalLM:
         self.final_norm = None
         self.lm_head = None
         self.tq = None
+        self.draft_head = None  # EAGLE head (speculative decoding): one extra cache layer
         if cfg.kv_cache_dtype not in ("auto", None, "bf16", "bfloat16"):
             from ..attention import TurboQuantAttention
             self.attn = TurboQuantAttention(self.hq, self.hkv, self.D, cfg.kv_cache_dtype)
@@ -258,5 +259,6 @@ class DenseDecoderForCausalLM:
         return [(buf[i], None) for i in range(self.cfg.num_layers)]
 
     def kv_cache_spec(self) -> dict:
-        return {"num_layers": self.cfg.num_layers, "num_kv_heads": self.hkv,
+        n = self.cfg.num_layers + (1 if self.draft_head is not None else 0)
+        return {"num_layers": n, "num_kv_heads": self.hkv,
                 "head_dim": self.D, "dtype": self.dtype}

@@ -39,6 +39,13 @@ class ReferenceDecoder:
     @torch.no_grad()
     def logits(self, tokens: List[int]) -> torch.Tensor:
         """Logits [S, V] for every position of ``tokens``."""
+        w = self.w
+        head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
+        return self.hidden(tokens) @ head.t()
+
+    @torch.no_grad()
+    def hidden(self, tokens: List[int]) -> torch.Tensor:
+        """Final normalised hidden states [S, H] for every position of ``tokens``."""
         cfg, w, D = self.cfg, self.w, self.D
         S = len(tokens)
         ids = torch.tensor(tokens)
@@ -66,9 +73,7 @@ class ReferenceDecoder:
             g = x @ w[p + "mlp.gate_proj.weight"].t()
             u = x @ w[p + "mlp.up_proj.weight"].t()
             h = h + (F.silu(g) * u) @ w[p + "mlp.down_proj.weight"].t()
-        h = self._rms(h, w["model.norm.weight"])
-        head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
-        return h @ head.t()
+        return self._rms(h, w["model.norm.weight"])
 
     def greedy(self, prompt: List[int], n: int):
         """Greedy continuation of ``n`` tokens; returns (tokens, per-step logits list)."""

@@ -45,6 +45,7 @@ class Feature(str, Enum):
     MLA_DCP = "deepseek.mla_decode_context_parallel"
     SPARSE_INDEXER = "deepseek.sparse_indexer"
     MTP = "spec.mtp"
+    EAGLE = "spec.eagle"
     GDN_CHUNKED_PREFILL = "gdn.chunked_prefill"
     W4AFP8_EXPERTS = "moe.w4afp8_experts"
     TURBOQUANT_KV = "attn.turboquant_kv_cache"
@@ -177,6 +178,8 @@ def resolve(config) -> OptimizationContract:
             both(Feature.MLA_DCP)
         if e.speculative_method == "mtp":
             both(Feature.MTP)
+    if m.family == ModelFamily.DENSE and e.speculative_method == "eagle":
+        both(Feature.EAGLE)
     if m.quant == "w4afp8" and m.num_experts:
         both(Feature.W4AFP8_EXPERTS)
     if m.family == ModelFamily.HYBRID_GDN and cuda:
@@ -206,3 +209,10 @@ def validate(contract: OptimizationContract) -> None:
                              "recurrent or MoE families)")
     if e.speculative_method == "mtp" and m.family != ModelFamily.DEEPSEEK:
         raise ValueError("MTP speculative decoding needs a DeepSeek multi-token-prediction layer")
+    if e.speculative_method == "eagle":
+        if m.family != ModelFamily.DENSE:
+            raise ValueError("EAGLE heads are served over the dense decoders (Llama / Qwen)")
+        if m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
+            raise ValueError("EAGLE drafts need a bf16 KV cache")
+    if e.speculative_method not in (None, "ngram", "mtp", "eagle"):
+        raise ValueError(f"speculative method {e.speculative_method!r} is not served")
