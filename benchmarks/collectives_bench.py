@@ -135,6 +135,22 @@ def main():
                        nvls2_frac_of_roofline=round(nroof / k_fn[True], 3))
         emit(rec)
 
+    if nv is not None:
+        # rows per warp of the NVLS two-shot kernel at large messages (1: every warp loads,
+        # then stores, in lock-step; 2+: the next row's reduce overlaps the current stores)
+        import vllm_musa_b200.parallel.custom_ar as car
+        for T in (1024, 4096, 8192):
+            res = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            rec = dict(case="nvls_rows_per_warp", T=T, H=H)
+            for rpw in (1, 2, 4, 0):
+                car.NVLS_ROWS_PER_WARP = rpw
+
+                def f():
+                    ar._run_nvls(nv.staging[ar.parity][:T], res, w, eps, two_shot=True)
+                rec[f"rpw{rpw}_us" if rpw else "default_us"] = round(_time(f, 50, st.tp_group), 2)
+            car.NVLS_ROWS_PER_WARP = 0
+            emit(rec)
+
     if nv is not None and H % 256 == 0:
         for T in (8, 256, 2048):
             x = torch.randn(T, H, device=dev).to(torch.bfloat16)

@@ -84,22 +84,34 @@ B200_DEVICE void reduce_row(const ArParams& a, int row, int r0, float (&o)[VPT][
   for (int i = 0; i < VPT; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-  for (int p = 0; p < a.world; ++p) {
-    // peers' staging (row-major [T, H]) or, after an epilogue reduce-scatter, block p of the
-    // local staging slot
-    const __nv_bfloat16* base =
+  // peers' staging (row-major [T, H]) or, after an epilogue reduce-scatter, block p of the
+  // local staging slot.  All ranks' vectors are loaded before any is summed, so the NVLink
+  // round trips overlap instead of running one peer after another.
+  const uint4* src[kMaxRanks];
+#pragma unroll
+  for (int p = 0; p < kMaxRanks; ++p) {
+    const int pp = p < a.world ? p : 0;
+    src[p] = reinterpret_cast<const uint4*>(
         a.rs_rows > 0 ? reinterpret_cast<const __nv_bfloat16*>(a.staging[a.rank]) +
-                            ((size_t)p * a.rs_rows + (row - r0)) * a.H
-                      : reinterpret_cast<const __nv_bfloat16*>(a.staging[p]) + (size_t)row * a.H;
-    const uint4* src = reinterpret_cast<const uint4*>(base);
+                            ((size_t)pp * a.rs_rows + (row - r0)) * a.H
+                      : reinterpret_cast<const __nv_bfloat16*>(a.staging[pp]) + (size_t)row * a.H);
+  }
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int c = threadIdx.x + i * blockDim.x;
-      if (c < nvec) {
-        float f[8];
-        unpack8(src[c], f);
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nvec) {
+      uint4 t[kMaxRanks];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < a.world) t[p] = src[p][c];
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) {
+        if (p < a.world) {
+          float f[8];
+          unpack8(t[p], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+        }
       }
     }
   }

@@ -61,7 +61,7 @@ struct NvlsParams {
 };
 constexpr size_t kNvlsFlagBytes = 2 * kMaxBlocks * sizeof(uint32_t);
 void run_nvls_allreduce(const NvlsParams& a, cudaStream_t s);
-int nvls_blocks(int T, int world, bool two_shot);
+int nvls_blocks(int T, int world, bool two_shot, int rows_per_warp = 0);
 
 // Vocab-parallel sampling exchange: every rank's per-row (score, token) candidate is stored into
 // every peer's candidate region [src rank][row]; after a per-block epoch barrier each rank picks

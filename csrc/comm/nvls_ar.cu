@@ -130,9 +130,102 @@ B200_DEVICE float quant8(const float (&f)[8], uint32_t& lo, uint32_t& hi) {
 constexpr int kNvlsThreads = 256;
 constexpr int kNvlsWarps = kNvlsThreads / 32;
 
-// One warp per row; lane l owns the 16-byte vectors l, l + 32, ... (VPW of them).
+// This lane's VPW vectors of `row`, summed over the ranks by the switch.
+template <int VPW>
+B200_DEVICE void load_row(const NvlsParams& a, int row, int lane, int nvec, uint4 (&v)[VPW]) {
+  const char* src = reinterpret_cast<const char*>(a.mc_staging) + (size_t)row * a.H * 2;
+#pragma unroll
+  for (int i = 0; i < VPW; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) v[i] = mm_ld_reduce_bf16x8(src + (size_t)c * 16);
+  }
+}
+
+// Residual add, RMSNorm, optional e4m3 quantisation and the store (multicast for two-shot,
+// local for one-shot) of one reduced row.
+template <int VPW, bool kNorm, bool kTwoShot, bool kQuant>
+B200_DEVICE void finish_row(const NvlsParams& a, int row, int lane, int nvec, uint4 (&packed)[VPW]) {
+  const size_t row_bytes = (size_t)a.H * 2;
+  if (a.residual) {
+    uint4* rr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.residual) + row * row_bytes);
+#pragma unroll
+    for (int i = 0; i < VPW; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        float v[8], r[8];
+        unpack8(packed[i], v);
+        unpack8(rr[c], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += r[j];
+        packed[i] = pack8(v);
+        rr[c] = packed[i];
+      }
+    }
+  }
+  float inv = 1.f;
+  if constexpr (kNorm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPW; ++i) {
+      if (lane + 32 * i < nvec) {
+        float f[8];
+        unpack8(packed[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+      }
+    }
+    ss = warp_sum(ss);
+    inv = rsqrtf(ss / a.H + a.eps);
+  }
+#pragma unroll
+  for (int i = 0; i < VPW; ++i) {
+    const int c = lane + 32 * i;
+    // a 128-element group is 16 consecutive vectors = 16 lanes of one i: all 32 lanes take
+    // part in the group reduction, so the bound check is uniform per i (nvec % 32 == 0 when
+    // quantising)
+    if (!kQuant && c >= nvec) continue;
+    if (kQuant && 32 * i >= nvec) continue;
+    float f[8];
+    unpack8(packed[i], f);
+    if constexpr (kNorm) {
+      float w[8];
+      unpack8(reinterpret_cast<const uint4*>(a.weight)[c], w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = f[j] * inv * w[j];
+    }
+    if constexpr (kQuant) {
+      // bf16 rounding first, as the unfused path quantises the bf16 normalised row
+      const uint4 ov = pack8(f);
+      unpack8(ov, f);
+      uint32_t lo, hi;
+      const float scale = quant8(f, lo, hi);
+      const size_t qoff = (size_t)row * a.H + (size_t)c * 8;
+      const size_t soff = (size_t)row * (a.H / 128) + c / 16;
+      if (kTwoShot) {
+        mm_st_8(reinterpret_cast<char*>(a.mc_q) + qoff, lo, hi);
+        if ((lane & 15) == 0) mm_st_f32(reinterpret_cast<char*>(a.mc_s) + soff * 4, scale);
+      } else {
+        *reinterpret_cast<uint2*>(reinterpret_cast<char*>(a.q_local) + qoff) = make_uint2(lo, hi);
+        if ((lane & 15) == 0) a.s_local[soff] = scale;
+      }
+    } else {
+      const uint4 ov = pack8(f);
+      if (kTwoShot)
+        mm_st_16(reinterpret_cast<char*>(a.mc_out) + row * row_bytes + (size_t)c * 16, ov);
+      else
+        reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out_local) + row * row_bytes)[c] = ov;
+    }
+  }
+}
+
+// One warp per row; lane l owns the 16-byte vectors l, l + 32, ... (VPW of them).  A warp that
+// walks several rows issues the next row's multimem.ld_reduce before it finishes and stores
+// the current one (rows up to 16 vectors per lane), so the switch's reads for one row overlap
+// the multicast stores of the previous: without it every warp of the grid loads, then stores,
+// in lock-step, and each NVLink direction idles half the time.
 template <int VPW, bool kNorm, bool kTwoShot, bool kQuant>
 __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_kernel(NvlsParams a) {
+  constexpr bool kPipe = VPW <= 16;
   __shared__ uint32_t epoch_s[2];
   if (threadIdx.x == 0) {
     epoch_s[0] = a.epochs[blockIdx.x] + 1;
@@ -148,85 +241,23 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_kernel(NvlsParams a) {
   const int nvec = a.H / 8;
   const int per = kTwoShot ? (a.T + a.world - 1) / a.world : a.T;
   const int r0 = kTwoShot ? min(a.T, a.rank * per) : 0, r1 = min(a.T, r0 + per);
-  const size_t row_bytes = (size_t)a.H * 2;
-  for (int row = r0 + blockIdx.x * kNvlsWarps + warp; row < r1; row += gridDim.x * kNvlsWarps) {
-    const char* src = reinterpret_cast<const char*>(a.mc_staging) + row * row_bytes;
-    uint4 packed[VPW];
+  const int stride = gridDim.x * kNvlsWarps;
+  int row = r0 + blockIdx.x * kNvlsWarps + warp;
+  uint4 cur[VPW];
+  if (row < r1) load_row<VPW>(a, row, lane, nvec, cur);
+  while (row < r1) {
+    const int next = row + stride;
+    if constexpr (kPipe) {
+      uint4 nxt[VPW];
+      if (next < r1) load_row<VPW>(a, next, lane, nvec, nxt);
+      finish_row<VPW, kNorm, kTwoShot, kQuant>(a, row, lane, nvec, cur);
 #pragma unroll
-    for (int i = 0; i < VPW; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) packed[i] = mm_ld_reduce_bf16x8(src + (size_t)c * 16);
+      for (int i = 0; i < VPW; ++i) cur[i] = nxt[i];
+    } else {
+      finish_row<VPW, kNorm, kTwoShot, kQuant>(a, row, lane, nvec, cur);
+      if (next < r1) load_row<VPW>(a, next, lane, nvec, cur);
     }
-    if (a.residual) {
-      uint4* rr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.residual) + row * row_bytes);
-#pragma unroll
-      for (int i = 0; i < VPW; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nvec) {
-          float v[8], r[8];
-          unpack8(packed[i], v);
-          unpack8(rr[c], r);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] += r[j];
-          packed[i] = pack8(v);
-          rr[c] = packed[i];
-        }
-      }
-    }
-    float inv = 1.f;
-    if constexpr (kNorm) {
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < VPW; ++i) {
-        if (lane + 32 * i < nvec) {
-          float f[8];
-          unpack8(packed[i], f);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
-        }
-      }
-      ss = warp_sum(ss);
-      inv = rsqrtf(ss / a.H + a.eps);
-    }
-#pragma unroll
-    for (int i = 0; i < VPW; ++i) {
-      const int c = lane + 32 * i;
-      // a 128-element group is 16 consecutive vectors = 16 lanes of one i: all 32 lanes take
-      // part in the group reduction, so the bound check is uniform per i (nvec % 32 == 0 when
-      // quantising)
-      if (!kQuant && c >= nvec) continue;
-      if (kQuant && 32 * i >= nvec) continue;
-      float f[8];
-      unpack8(packed[i], f);
-      if constexpr (kNorm) {
-        float w[8];
-        unpack8(reinterpret_cast<const uint4*>(a.weight)[c], w);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = f[j] * inv * w[j];
-      }
-      if constexpr (kQuant) {
-        // bf16 rounding first, as the unfused path quantises the bf16 normalised row
-        const uint4 ov = pack8(f);
-        unpack8(ov, f);
-        uint32_t lo, hi;
-        const float scale = quant8(f, lo, hi);
-        const size_t qoff = (size_t)row * a.H + (size_t)c * 8;
-        const size_t soff = (size_t)row * (a.H / 128) + c / 16;
-        if (kTwoShot) {
-          mm_st_8(reinterpret_cast<char*>(a.mc_q) + qoff, lo, hi);
-          if ((lane & 15) == 0) mm_st_f32(reinterpret_cast<char*>(a.mc_s) + soff * 4, scale);
-        } else {
-          *reinterpret_cast<uint2*>(reinterpret_cast<char*>(a.q_local) + qoff) = make_uint2(lo, hi);
-          if ((lane & 15) == 0) a.s_local[soff] = scale;
-        }
-      } else {
-        const uint4 ov = pack8(f);
-        if (kTwoShot)
-          mm_st_16(reinterpret_cast<char*>(a.mc_out) + row * row_bytes + (size_t)c * 16, ov);
-        else
-          reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out_local) + row * row_bytes)[c] = ov;
-      }
-    }
+    row = next;
   }
   if (kTwoShot) nvls_barrier(a, 1, epoch_s[1]);
 }
@@ -257,9 +288,14 @@ void launch_norm(const NvlsParams& a, cudaStream_t s) {
 
 }  // namespace
 
-int nvls_blocks(int T, int world, bool two_shot) {
+int nvls_blocks(int T, int world, bool two_shot, int rows_per_warp) {
   const int rows = two_shot ? (T + world - 1) / world : T;
-  return std::max(1, std::min(kMaxBlocks, (rows + kNvlsWarps - 1) / kNvlsWarps));
+  // latency-bound sizes: one row per warp; from 256 rows per rank up, two rows per warp (the
+  // second row's reduce overlaps the first row's stores), 32 blocks at least
+  int rpw = rows_per_warp > 0 ? rows_per_warp : (rows > 256 ? 2 : 1);
+  int blocks = (rows + kNvlsWarps * rpw - 1) / (kNvlsWarps * rpw);
+  if (rows_per_warp <= 0 && rows > 256) blocks = std::max(blocks, 32);
+  return std::max(1, std::min(kMaxBlocks, blocks));
 }
 
 void run_nvls_allreduce(const NvlsParams& a, cudaStream_t s) {

@@ -1248,7 +1248,7 @@ void fused_allreduce(const Tensor& like, const std::vector<int64_t>& bufs, int64
 void nvls_allreduce(const Tensor& like, const std::vector<int64_t>& ptrs, int64_t rank,
                     int64_t world, int64_t T, int64_t H, bool two_shot,
                     const c10::optional<Tensor>& residual, const c10::optional<Tensor>& weight,
-                    double eps) {
+                    double eps, int64_t rows_per_warp) {
   TORCH_CHECK(ptrs.size() == 10, "nvls_allreduce: pointer table size");
   const c10::cuda::CUDAGuard g(like.device());
   b200::comm::NvlsParams a{};
@@ -1257,7 +1257,7 @@ void nvls_allreduce(const Tensor& like, const std::vector<int64_t>& ptrs, int64_
   a.T = T;
   a.H = H;
   a.two_shot = two_shot;
-  a.blocks = b200::comm::nvls_blocks(T, world, two_shot);
+  a.blocks = b200::comm::nvls_blocks(T, world, two_shot, (int)rows_per_warp);
   a.mc_staging = reinterpret_cast<const void*>(ptrs[0]);
   a.mc_out = reinterpret_cast<void*>(ptrs[1]);
   a.out_local = reinterpret_cast<void*>(ptrs[2]);
@@ -1688,7 +1688,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "NVLS (multimem) all-reduce (+ residual + RMSNorm, + optional 1x128 e4m3 output)",
         py::arg("like"), py::arg("ptrs"), py::arg("rank"), py::arg("world"), py::arg("T"),
         py::arg("H"), py::arg("two_shot"), py::arg("residual"), py::arg("weight"),
-        py::arg("eps"));
+        py::arg("eps"), py::arg("rows_per_warp") = 0);
   m.def("nvls_flag_bytes", []() { return (int64_t)b200::comm::kNvlsFlagBytes; });
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel dispatch over NVLink (+ count exchange)");
   m.def("exchange_candidates", &exchange_candidates,

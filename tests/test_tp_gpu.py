@@ -30,12 +30,14 @@ def _torchrun(n, args, port):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
 
 
-@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
-def test_fused_allreduce_rmsnorm_2gpu(tmp_path):
-    """Peer-to-peer one-/two-shot and (where the GPUs support NVLink multicast) NVLS kernels
-    against NCCL + fp32 math."""
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_fused_allreduce_rmsnorm(tmp_path, n):
+    """Peer-to-peer one-/two-shot and (where the GPUs support NVLink multicast) NVLS one-/two-
+    shot kernels against NCCL + fp32 math, on n GPUs."""
+    if _ngpu() < n:
+        pytest.skip(f"needs {n} GPUs")
     out = str(tmp_path / "ar.json")
-    _torchrun(2, ["--mode", "ar", "--out", out], 29601)
+    _torchrun(n, ["--mode", "ar", "--out", out], 29601 + n)
     res = json.load(open(out))
     assert any(r["two_shot"] for r in res) and any(not r["two_shot"] for r in res)
     for r in res:

@@ -36,13 +36,18 @@ def mode_ar(out_path):
     import vllm_musa_b200.parallel.custom_ar as car
     # numerics of every kernel: NVLS two-shot above 64 KiB, peer-to-peer below
     car.NVLS_MIN_BYTES = {w: 64 << 10 for w in (2, 4, 8)}
-    car.NVLS_QUANT_MIN_ROWS = 1
+    car.NVLS_QUANT_MIN_ROWS = {w: 1 for w in (2, 4, 8)}
     ar = maybe_create_custom_allreduce(st, dev, max_tokens=2048, hidden=H)
     assert ar is not None, "custom all-reduce did not initialise"
     errs = []
     g = torch.Generator(device="cpu").manual_seed(123)
     w = (torch.randn(H, generator=g) * 0.1 + 1).to(torch.bfloat16).to(dev)
-    for it, T in enumerate([1, 7, 32, 256, 1000, 2048, 5]):
+    # (rows, NVLS threshold for this call): NVLS one-shot below `world` rows, two-shot above
+    # 64 KiB, peer-to-peer one- / two-shot where the threshold is None or not reached
+    cases = [(1, 0), (7, 64 << 10), (32, 64 << 10), (256, 64 << 10), (1000, 64 << 10),
+             (2048, None), (5, None), (1, None), (3, 0)]
+    for it, (T, lim) in enumerate(cases):
+        car.NVLS_MIN_BYTES = {w: lim for w in (2, 4, 8)}
         ar.begin_forward() if it % 2 == 0 else None
         gen = torch.Generator(device="cpu").manual_seed(1000 * it + st.rank)
         x = torch.randn(T, H, generator=gen).to(torch.bfloat16).to(dev)
@@ -58,7 +63,7 @@ def mode_ar(out_path):
         nvls = ar.use_nvls(T)
         out, res2 = ar.allreduce_add_rmsnorm(stg, res.clone(), w, 1e-6)
         torch.cuda.synchronize()
-        two_shot = nvls or ar._plan(T)[0]
+        two_shot = nvls == 2 or (not nvls and ar._plan(T)[0])
         q_err = None
         if ar.can_quant(x):
             # the fused fp8 output (1x128 e4m3 groups) against quantising the reference rows

@@ -46,19 +46,31 @@ ONE_SHOT_READ_BYTES = 2 << 20
 FUSE_GEMM_RS = os.environ.get("B200_FUSE_GEMM_RS", "0") == "1"
 NVLS = os.environ.get("B200_AR_NVLS", "1") != "0"
 # Per-size choice between the peer-to-peer kernels and the NVLS kernel, by world size: messages
-# of more than NVLS_MIN_BYTES[world] bytes take NVLS two-shot (None: never).  Measured at TP=2
-# (CUDA-graph replays, H=4096): peer-to-peer wins at every size (one-shot 22.0 us vs NVLS
-# 30.3 / 25.1 us at 256 rows; two-shot 127.5 us vs NVLS 204.6 us at 8192 rows): with two ranks
-# NVLS moves twice the bytes per link (the switch reads every copy, the local one included).
-# Its byte advantage starts at four ranks (1.25 vs 1.5 message copies per direction; 1.125 vs
-# 1.75 at eight); until those sizes are measured the default stays peer-to-peer and
-# B200_AR_NVLS_MIN_BYTES sets the threshold for every world size.
-NVLS_MIN_BYTES = {2: None, 4: None, 8: None}
+# of more than NVLS_MIN_BYTES[world] bytes take NVLS (None: never) -- two-shot from `world` rows
+# up, one-shot below.  Measured (CUDA-graph replays, H=4096, all-reduce + residual + RMSNorm):
+#   TP=2: peer-to-peer wins at every size (one-shot 22.0 us vs NVLS 30.3 / 25.1 us at 256 rows;
+#         two-shot 127.5 us vs NVLS 204.6 us at 8192 rows): with two ranks NVLS moves twice the
+#         bytes per link (the switch reads every copy, the local one included).
+#   TP=8: NVLS wins up to 2048 rows (8 rows: one-shot 17.6 us vs peer-to-peer 35.0; 256 rows:
+#         two-shot 27.3 vs 49.7; 1024 rows: 41.9 vs 66.9) and ties beyond (4096 rows: 114.8 vs
+#         110.9; 8192: 204.5 vs 200.9); the Llama-3-8B serving bench at TP=8 runs 30.0k tok/s
+#         with NVLS against 26.5k with the peer-to-peer kernels.
+#   TP=4: from 512 KiB (64 rows of 4096), where NVLS's byte advantage (1.25 vs 1.5 message
+#         copies per direction) and its flat latency take over from the peer-to-peer one-shot;
+#         interpolated between the two measured world sizes.
+# B200_AR_NVLS_MIN_BYTES overrides the threshold for every world size.
+NVLS_MIN_BYTES = {2: None, 4: 512 << 10, 8: 0}
+# rows each warp of the NVLS kernel walks (0: the kernel's size rule; tuning / benchmarks)
+NVLS_ROWS_PER_WARP = int(os.environ.get("B200_AR_NVLS_ROWS_PER_WARP", "0"))
 if os.environ.get("B200_AR_NVLS_MIN_BYTES"):
     NVLS_MIN_BYTES = {w: int(os.environ["B200_AR_NVLS_MIN_BYTES"]) for w in (2, 4, 8)}
 # the NVLS kernel's fused 1x128 e4m3 output replaces AR + norm + a separate quantisation from
-# this many rows up (TP=2: 61.5 vs 81.6 us at 2048 rows, 33.3 vs 32.2 us at 256)
-NVLS_QUANT_MIN_ROWS = int(os.environ.get("B200_AR_NVLS_QUANT_MIN_ROWS", "1024"))
+# this many rows up, by world size (TP=2: 61.5 vs 81.6 us at 2048 rows, 33.3 vs 32.2 us at 256,
+# 21.1 vs 14.2 at 8; TP=8: faster at every measured size, 26.0 vs 37.5 us at 8 rows, 32.5 vs
+# 52.4 at 256; TP=4 interpolated)
+NVLS_QUANT_MIN_ROWS = {2: 1024, 4: 256, 8: 1}
+if os.environ.get("B200_AR_NVLS_QUANT_MIN_ROWS"):
+    NVLS_QUANT_MIN_ROWS = {w: int(os.environ["B200_AR_NVLS_QUANT_MIN_ROWS"]) for w in (2, 4, 8)}
 
 
 def _consensus(ok: bool, group) -> bool:
@@ -234,11 +246,13 @@ class CustomAllReduce:
         return (x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] == self.hidden and
                 x.shape[0] <= self.max_tokens)
 
-    def use_nvls(self, T: int) -> bool:
-        """NVLS two-shot for messages above the measured threshold of this world size."""
+    def use_nvls(self, T: int) -> int:
+        """NVLS for messages above the threshold of this world size: 2 (two-shot) from `world`
+        rows up, 1 (one-shot) below; 0: the peer-to-peer kernels."""
         lim = NVLS_MIN_BYTES.get(self.world)
-        return self.nvls is not None and lim is not None and T >= self.world and \
-            T * self.hidden * 2 > lim
+        if self.nvls is None or lim is None or T * self.hidden * 2 <= lim:
+            return 0
+        return 2 if T >= self.world else 1
 
     def staging_view(self, T: int) -> torch.Tensor:
         if self.use_nvls(T):
@@ -258,7 +272,8 @@ class CustomAllReduce:
         if x.data_ptr() != nv.staging[k].data_ptr():
             nv.staging[k][:T].copy_(x)
         self.mod.nvls_allreduce(x, nv.ptrs(k, two_shot, quant), self.rank, self.world, T,
-                                self.hidden, two_shot, residual, weight, eps)
+                                self.hidden, two_shot, residual, weight, eps,
+                                NVLS_ROWS_PER_WARP)
         self.parity ^= 1
         if quant:
             return nv.q[k][:T], nv.s[k][:T]
@@ -266,8 +281,9 @@ class CustomAllReduce:
 
     def _run(self, x, residual, weight, eps):
         T = x.shape[0]
-        if self.use_nvls(T):
-            return self._run_nvls(x, residual, weight, eps)
+        mode = self.use_nvls(T)
+        if mode:
+            return self._run_nvls(x, residual, weight, eps, two_shot=mode == 2)
         if x.data_ptr() != self._staging[self.parity].data_ptr():
             self._staging[self.parity][:T].copy_(x)
         two_shot, blocks = self._plan(T)
@@ -295,7 +311,7 @@ class CustomAllReduce:
         """The fused all-reduce + norm emits the 1x128 e4m3 rows itself (NVLS kernels), for
         batches where that beats all-reduce + norm followed by the group quantisation."""
         return (self.nvls is not None and self.can_run(x) and self.hidden % 256 == 0 and
-                x.shape[0] >= max(NVLS_QUANT_MIN_ROWS, self.world))
+                x.shape[0] >= NVLS_QUANT_MIN_ROWS.get(self.world, 1 << 30))
 
     def allreduce_add_rmsnorm_quant(self, x, residual, weight, eps):
         """residual <- AR(x) + residual; returns (q, scales) of RMSNorm(residual) * weight per
