@@ -128,3 +128,19 @@ def test_vocab_parallel_topk_exchange_2gpu(tmp_path):
     _torchrun(2, ["--mode", "topk", "--out", out], 29671)
     for r in json.load(open(out)):
         assert r["mismatch"] == 0 and r["undecided_topk"] == 0 and r["decided"] > 0.5, r
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_pipeline_parallel_2gpu_matches_tp1(tmp_path):
+    """PP=2 over NCCL send / recv (micro-batched stages, tokens broadcast from the last stage)
+    against one GPU: last-stage logits of the first step and greedy tokens."""
+    p1, p2 = str(tmp_path / "one"), str(tmp_path / "pp")
+    _torchrun(1, ["--mode", "llm", "--out", p1, "--tp", "1", "--eager"], 29671)
+    _torchrun(2, ["--mode", "llm", "--out", p2, "--tp", "1", "--pp", "2"], 29681)
+    a = json.load(open(p1 + ".0"))
+    b0, b1 = json.load(open(p2 + ".0")), json.load(open(p2 + ".1"))
+    assert b0["tokens"] == b1["tokens"], "pipeline ranks diverged"
+    la, lb = torch.tensor(a["logits0"]), torch.tensor(b1["logits0"])
+    assert (la - lb).abs().max().item() < 0.05
+    same = sum(x == y for x, y in zip(a["tokens"], b1["tokens"]))
+    assert same >= 3

@@ -244,11 +244,12 @@ def ds_cfg():
                        index_topk=0, rope_neox=False, name="tp-ds-test")
 
 
-def mode_llm(out_path, tp, eager, model="dense", ep=False, dcp=1):
+def mode_llm(out_path, tp, eager, model="dense", ep=False, dcp=1, pp=1):
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.parallel.state import destroy_distributed, get_parallel_state
     cfg = moe_cfg() if model == "moe" else ds_cfg() if model == "ds" else small_cfg()
-    llm = LLM(cfg, tensor_parallel_size=tp, block_size=64, seed=0, num_gpu_blocks=256,
+    llm = LLM(cfg, tensor_parallel_size=tp, pipeline_parallel_size=pp, block_size=64, seed=0,
+              num_gpu_blocks=256,
               max_model_len=1024, max_num_seqs=16, max_num_batched_tokens=1024,
               enforce_eager=eager, cuda_graph_sizes=[1, 2, 4, 8, 16],
               enable_expert_parallel=ep, decode_context_parallel_size=dcp)
@@ -258,8 +259,9 @@ def mode_llm(out_path, tp, eager, model="dense", ep=False, dcp=1):
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (7, 100, 300, 64)]
     outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True))
-    first = llm.engine.runner.logits_log[0].cuda()
     st = get_parallel_state()
+    log = llm.engine.runner.logits_log
+    first = log[0].cuda() if log else torch.zeros(1, 1, device="cuda")  # last stage only (PP)
     if st.tp_size > 1:
         parts = [torch.empty_like(first) for _ in range(st.tp_size)]
         dist.all_gather(parts, first, group=st.tp_group)
@@ -283,6 +285,7 @@ if __name__ == "__main__":
     ap.add_argument("--model", default="dense")
     ap.add_argument("--ep", action="store_true")
     ap.add_argument("--dcp", type=int, default=1)
+    ap.add_argument("--pp", type=int, default=1)
     a = ap.parse_args()
     if a.mode == "ar":
         mode_ar(a.out)
@@ -293,4 +296,4 @@ if __name__ == "__main__":
     elif a.mode == "topk":
         mode_topk(a.out)
     else:
-        mode_llm(a.out, a.tp, a.eager, a.model, a.ep, a.dcp)
+        mode_llm(a.out, a.tp, a.eager, a.model, a.ep, a.dcp, a.pp)

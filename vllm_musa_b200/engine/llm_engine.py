@@ -68,13 +68,15 @@ class LLMEngine:
         log.info("optimisation contract %s", self.contract.describe())
         mcfg = config.model
         tp = config.parallel.tensor_parallel_size
+        pp = config.parallel.pipeline_parallel_size
         device = torch.device(config.device)
         if device.type == "cuda":
             ops._ext.require()
         st = get_parallel_state()
-        if tp > 1 and st.tp_size != tp:
+        if (tp > 1 or pp > 1) and (st.tp_size != tp or st.pp_size != pp):
             st = init_distributed(tp_size=tp, ep=config.parallel.enable_expert_parallel,
-                                  backend="nccl" if device.type == "cuda" else "gloo")
+                                  backend="nccl" if device.type == "cuda" else "gloo",
+                                  pp_size=pp)
         if device.type == "cuda":
             device = torch.device("cuda", st.local_rank if st.world_size > 1 else
                                   (device.index or 0))
@@ -114,10 +116,11 @@ class LLMEngine:
         self.runner = ModelRunner(config, self.model, self.sampler, device)
         self.drafter = None  # model-based speculative proposer (MTP / EAGLE)
         num_blocks = self.runner.profile_and_allocate_kv()
-        if st.tp_size > 1:
-            # every rank must run with the same block count (lock-step schedulers)
+        if st.mp_size > 1:
+            # every rank of the replica must run with the same block count (lock-step
+            # schedulers; pipeline stages hold different layer counts)
             t = torch.tensor([num_blocks], dtype=torch.int64)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=st.tp_cpu_group)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=st.mp_cpu_group)
             if int(t) != num_blocks:
                 num_blocks = int(t)
                 self.runner.allocate_kv(num_blocks)
@@ -157,11 +160,11 @@ class LLMEngine:
         self.stream_outputs = False
         self.num_steps = 0
         # multi-process TP without torchrun: the driver broadcasts request ops every step
-        self.role = os.environ.get("B200_SPMD_ROLE", "replicated") if st.tp_size > 1 else "single"
+        self.role = os.environ.get("B200_SPMD_ROLE", "replicated") if st.mp_size > 1 else "single"
         self.sync = None
         if self.role in ("driver", "follower"):
             from .executor import StepSync
-            self.sync = StepSync(st.tp_cpu_group, st.tp_rank)
+            self.sync = StepSync(st.mp_cpu_group, st.mp_rank)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_token_ids: List[int],

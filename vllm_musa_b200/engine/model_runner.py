@@ -6,16 +6,23 @@ Per engine step:
   3. decode-only steps replay a captured CUDA graph of the padded batch size (forward +
      LM head + sampler in one replay); prefill / mixed steps run eagerly;
   4. the sampled token ids come back device->host into a pinned buffer.
+Under pipeline parallelism the step runs as micro-batches of whole requests: each stage
+receives a micro-batch's residual stream from the previous stage (NCCL send / recv on the
+stage pair), runs its layers and sends it on while the next micro-batch arrives, so the stages
+overlap; the last stage samples the whole step and broadcasts the token ids to the other
+stages of its pipeline (every rank's scheduler stays in lock-step).  Pipeline steps run eagerly.
 The reference uses vLLM's GPUModelRunner with its static graph wrapper and graph-capture
 hooks (vllm_musa/platform.py:908-910, v1/worker/*); this runner is written for this engine.
 """
 from __future__ import annotations
 
 import logging
+import os
 import time
 from typing import Optional
 
 import torch
+import torch.distributed as dist
 
 from .. import ops
 from ..attention import AttnMetadata
@@ -132,6 +139,12 @@ class ModelRunner:
         self.record_logits = False  # debugging / tests: keep every step's logits (eager only)
         self.logits_log: list = []
         self._extras: Optional[StepExtras] = None
+        st = getattr(model, "pstate", None)
+        self.pp = st if st is not None and st.pp_size > 1 else None
+        if self.pp is not None:
+            self.use_graphs = False
+            self.pp_micro_batches = int(os.environ.get("B200_PP_MICRO_BATCHES",
+                                                       str(self.pp.pp_size)))
 
     # ------------------------------------------------------------------ memory / KV cache
     def kv_bytes_per_block(self) -> int:
@@ -212,8 +225,15 @@ class ModelRunner:
     def _forward_sample(self, T: int, R: int, S: int, meta: AttnMetadata, sampling: bool,
                         any_filter: bool, decode_only: bool = False) -> torch.Tensor:
         b = self.buf
+        if self.pp is not None:
+            return self._forward_sample_pp(T, R, S, meta, sampling, any_filter, decode_only)
         hidden = self.model.forward(b.d["input_ids"][:T], meta, self.kv_caches)
         self.last_hidden = hidden  # final hidden states of the step (the MTP drafter reads them)
+        return self._sample_hidden(hidden, S, sampling, any_filter, decode_only)
+
+    def _sample_hidden(self, hidden: torch.Tensor, S: int, sampling: bool, any_filter: bool,
+                       decode_only: bool) -> torch.Tensor:
+        b = self.buf
         rows = hidden if decode_only else ops.gather_rows(hidden, b.d["logits_idx"][:S])
         logits = self.model.compute_logits(rows)
         if self.record_logits:
@@ -239,6 +259,79 @@ class ModelRunner:
                 raw = self.sampler.comm.all_gather(raw, dim=1)
             sel = ids.index_select(0, idx)
             ex.logprobs = [t.cpu() for t in ops.sampling.token_logprobs(raw, sel, ex.lp_k)]
+        return ids
+
+    # ------------------------------------------------------------------ pipeline parallelism
+    def _pp_chunks(self, meta: AttnMetadata, T: int, R: int) -> list:
+        """Micro-batches of whole requests with about equal token counts: (r0, r1, t0, t1)."""
+        cu = meta.cu_q[:R + 1].tolist()
+        m = max(1, min(self.pp_micro_batches, R))
+        out, r0 = [], 0
+        for k in range(m):
+            if r0 >= R:
+                break
+            goal = T * (k + 1) / m
+            r1 = r0 + 1
+            while r1 < R and cu[r1] < goal and R - r1 > m - k - 1:
+                r1 += 1
+            if k == m - 1:
+                r1 = R
+            out.append((r0, r1, cu[r0], cu[r1]))
+            r0 = r1
+        return out
+
+    @staticmethod
+    def _meta_slice(meta: AttnMetadata, r0: int, r1: int, t0: int, t1: int) -> AttnMetadata:
+        nd = max(0, min(r1, meta.num_decodes) - r0)
+        return AttnMetadata(t1 - t0, nd, (r1 - r0) - nd, meta.positions[t0:t1],
+                            meta.slot_mapping[t0:t1], meta.seq_lens[r0:r1],
+                            meta.block_tables[r0:r1], meta.cu_q[r0:r1 + 1] - t0,
+                            max_seq_len=meta.max_seq_len, tile_scratch=meta.tile_scratch,
+                            sliding_window=meta.sliding_window,
+                            state_slots=None if meta.state_slots is None
+                            else meta.state_slots[r0:r1])
+
+    def _forward_sample_pp(self, T: int, R: int, S: int, meta: AttnMetadata, sampling: bool,
+                           any_filter: bool, decode_only: bool) -> torch.Tensor:
+        st, b, dev = self.pp, self.buf, self.device
+        first, last = st.is_first_stage, st.is_last_stage
+        H, dt = self.model.cfg.hidden_size, self.model.dtype
+        chunks = self._pp_chunks(meta, T, R)
+        recvs = []
+        if not first:  # post every micro-batch's receive up front
+            src = st.pp_ranks[st.pp_rank - 1]
+            for (_, _, t0, t1) in chunks:
+                buf = torch.empty(t1 - t0, H, dtype=dt, device=dev)
+                recvs.append((buf, dist.irecv(buf, src=src, group=st.pp_group)))
+        hidden = torch.empty(T, H, dtype=dt, device=dev) if last else None
+        sends = []
+        ids_all = b.d["input_ids"][:T]
+        for k, (r0, r1, t0, t1) in enumerate(chunks):
+            m = self._meta_slice(meta, r0, r1, t0, t1)
+            hin = None
+            if recvs:
+                hin, work = recvs[k]
+                work.wait()
+            out = self.model.forward(ids_all[t0:t1], m, self.kv_caches, hidden_in=hin)
+            if last:
+                hidden[t0:t1].copy_(out)
+            else:
+                out = out.contiguous()
+                sends.append((out, dist.isend(out, dst=st.pp_ranks[st.pp_rank + 1],
+                                              group=st.pp_group)))
+        for _, work in sends:
+            work.wait()
+        if last:
+            self.last_hidden = hidden
+            ids = self._sample_hidden(hidden, S, sampling, any_filter, decode_only).to(torch.int64)
+        else:
+            ids = torch.empty(S, dtype=torch.int64, device=dev)
+        dist.broadcast(ids, src=st.pp_ranks[-1], group=st.pp_group)
+        ex = self._extras
+        if ex is not None and ex.lp_rows:
+            obj = [ex.logprobs]
+            dist.broadcast_object_list(obj, src=st.pp_ranks[-1], group=st.pp_cpu_group)
+            ex.logprobs = obj[0]
         return ids
 
     def _meta(self, T: int, R: int, nd: int, npf: int, max_seq_len: int,

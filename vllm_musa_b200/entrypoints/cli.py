@@ -21,6 +21,7 @@ def main(argv=None) -> int:
     gp.add_argument("--max-tokens", type=int, default=16)
     gp.add_argument("--temperature", type=float, default=0.0)
     gp.add_argument("--tensor-parallel-size", "-tp", type=int, default=1)
+    gp.add_argument("--pipeline-parallel-size", "-pp", type=int, default=1)
     gp.add_argument("--device", default="cuda")
     sub.add_parser("collect-env", help="print the environment report")
     sub.add_parser("version")
@@ -32,7 +33,8 @@ def main(argv=None) -> int:
         run_server(a)
     elif a.cmd == "generate":
         from .. import LLM, SamplingParams
-        llm = LLM(a.model, tensor_parallel_size=a.tensor_parallel_size, device=a.device)
+        llm = LLM(a.model, tensor_parallel_size=a.tensor_parallel_size,
+                  pipeline_parallel_size=a.pipeline_parallel_size, device=a.device)
         prompt = ([int(x) for x in a.prompt_token_ids.split(",")] if a.prompt_token_ids
                   else a.prompt)
         out = llm.generate([prompt], SamplingParams(temperature=a.temperature,

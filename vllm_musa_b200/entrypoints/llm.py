@@ -33,7 +33,8 @@ def _load_tokenizer(path: Optional[str]):
 
 class LLM:
     def __init__(self, model: Union[str, ModelConfig, None] = None, *,
-                 tensor_parallel_size: int = 1, enable_expert_parallel: bool = False,
+                 tensor_parallel_size: int = 1, pipeline_parallel_size: int = 1,
+                 enable_expert_parallel: bool = False,
                  decode_context_parallel_size: int = 1, data_parallel_size: int = 1,
                  max_model_len: Optional[int] = None, max_num_seqs: int = 256,
                  max_num_batched_tokens: int = 8192, block_size: int = 64,
@@ -73,6 +74,7 @@ class LLM:
                                       max_model_len=mlen,
                                       enable_chunked_prefill=enable_chunked_prefill),
             parallel=ParallelConfig(tensor_parallel_size=tensor_parallel_size,
+                                    pipeline_parallel_size=pipeline_parallel_size,
                                     enable_expert_parallel=enable_expert_parallel,
                                     decode_context_parallel_size=decode_context_parallel_size,
                                     data_parallel_size=data_parallel_size),
@@ -87,18 +89,21 @@ class LLM:
             # [k*tp, (k+1)*tp) run engine replica k (its own TP group, KV cache and scheduler)
             # and generate() splits the prompts over the replicas
             world = int(os.environ.get("WORLD_SIZE", "1"))
-            if world != data_parallel_size * tensor_parallel_size:
-                raise ValueError("data_parallel_size > 1 needs WORLD_SIZE == "
-                                 "data_parallel_size * tensor_parallel_size (torchrun)")
+            mp = tensor_parallel_size * pipeline_parallel_size
+            if world != data_parallel_size * mp:
+                raise ValueError("data_parallel_size > 1 needs WORLD_SIZE == data_parallel_size"
+                                 " * tensor_parallel_size * pipeline_parallel_size (torchrun)")
             from ..parallel.state import init_distributed
             st = init_distributed(tp_size=tensor_parallel_size,
                                   ep=enable_expert_parallel,
-                                  backend="nccl" if device == "cuda" else "gloo")
+                                  backend="nccl" if device == "cuda" else "gloo",
+                                  pp_size=pipeline_parallel_size)
             self.dp_size, self.dp_rank = st.dp_size, st.dp_rank
-        if tensor_parallel_size > 1 and "WORLD_SIZE" not in os.environ:
+        mp = tensor_parallel_size * pipeline_parallel_size
+        if mp > 1 and "WORLD_SIZE" not in os.environ:
             # no launcher: spawn follower ranks and drive them from this process
             from ..engine.executor import MultiprocExecutor
-            self.executor = MultiprocExecutor(cfg, tensor_parallel_size)
+            self.executor = MultiprocExecutor(cfg, mp)
         self.engine = LLMEngine(cfg, tok)
         self._counter = 0
 

@@ -210,7 +210,11 @@ def make_arg_parser(p: Optional[argparse.ArgumentParser] = None) -> argparse.Arg
     p.add_argument("--host", default="0.0.0.0")
     p.add_argument("--port", type=int, default=8000)
     p.add_argument("--tensor-parallel-size", "-tp", type=int, default=1)
+    p.add_argument("--pipeline-parallel-size", "-pp", type=int, default=1)
     p.add_argument("--enable-expert-parallel", action="store_true")
+    p.add_argument("--speculative-config", type=json.loads, default=None,
+                   help='JSON, e.g. {"method": "eagle", "num_speculative_tokens": 1, '
+                        '"model": "/path/to/eagle"}')
     p.add_argument("--max-model-len", type=int, default=None)
     p.add_argument("--max-num-seqs", type=int, default=256)
     p.add_argument("--max-num-batched-tokens", type=int, default=8192)
@@ -227,6 +231,8 @@ def make_arg_parser(p: Optional[argparse.ArgumentParser] = None) -> argparse.Arg
 def build_llm(args):
     from ..llm import LLM
     return LLM(args.model, tensor_parallel_size=args.tensor_parallel_size,
+               pipeline_parallel_size=getattr(args, "pipeline_parallel_size", 1),
+               speculative_config=getattr(args, "speculative_config", None),
                enable_expert_parallel=args.enable_expert_parallel,
                max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs,
                max_num_batched_tokens=args.max_num_batched_tokens, block_size=args.block_size,

@@ -61,7 +61,7 @@ class EagleHead:
         self.fc = None
         self.fc_bias = None
         self.norm = None
-        self.cache_index = target.cfg.num_layers  # the extra cache layer after the target's
+        self.cache_index = target.l1 - target.l0  # the extra cache layer after the target's
 
     def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
         t, L = self.t, self.layer

@@ -44,6 +44,16 @@ def shard_cols(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     return w[:, rank * s:(rank + 1) * s]
 
 
+def pp_layer_range(num_layers: int, pp_size: int, pp_rank: int) -> Tuple[int, int]:
+    """Layers [l0, l1) of pipeline stage ``pp_rank``: an even split, the remainder going to the
+    first stages (the last one also runs the final norm and the LM head)."""
+    if pp_size > num_layers:
+        raise ValueError("pipeline_parallel_size exceeds the number of layers")
+    base, extra = divmod(num_layers, pp_size)
+    l0 = pp_rank * base + min(pp_rank, extra)
+    return l0, l0 + base + (1 if pp_rank < extra else 0)
+
+
 def kv_head_range(num_kv_heads: int, rank: int, world: int) -> Tuple[int, int]:
     """KV heads owned by ``rank``; heads are replicated when there are fewer than ranks."""
     if num_kv_heads >= world:
@@ -87,6 +97,13 @@ class DenseDecoderForCausalLM:
             raise ValueError("vocab_size must be divisible by tensor_parallel_size")
         self.vocab_start = self.rank * self.vocab_local
         self.layers = [_Layer() for _ in range(cfg.num_layers)]
+        # pipeline stage: layers [l0, l1); the first stage embeds, the last normalises and
+        # projects to the vocabulary; between stages the residual stream is handed on
+        self.l0, self.l1 = pp_layer_range(cfg.num_layers, self.pstate.pp_size,
+                                          self.pstate.pp_rank)
+        self.first_stage = self.pstate.pp_rank == 0
+        self.last_stage = self.pstate.pp_rank == self.pstate.pp_size - 1
+        self._stage_norm = None  # unit norm weight closing a non-last stage's last layer
         self.embed = None
         self.final_norm = None
         self.lm_head = None
@@ -116,29 +133,36 @@ class DenseDecoderForCausalLM:
     def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
         """Consume HF-named tensors; shard, fuse (qkv, interleaved gate/up) and keep them."""
         cfg = self.cfg
+        first, last = self.first_stage, self.last_stage
         for name, w in weights:
             if name == "model.embed_tokens.weight":
-                self.embed = self._to(w)
-                if cfg.tie_word_embeddings:
+                if first:
+                    self.embed = self._to(w)
+                if cfg.tie_word_embeddings and last:
                     self.lm_head = self._to(shard_rows(w, self.rank, self.tp))
             elif name == "lm_head.weight":
-                self.lm_head = self._to(shard_rows(w, self.rank, self.tp))
+                if last:
+                    self.lm_head = self._to(shard_rows(w, self.rank, self.tp))
             elif name == "model.norm.weight":
-                self.final_norm = self._to(w)
+                if last:
+                    self.final_norm = self._to(w)
             else:
                 m = _LAYER_RE.match(name)
                 if not m:
                     continue
                 i, key = int(m.group(1)), m.group(2)
-                if i >= cfg.num_layers or not self._wanted(i, key):
+                if not self.l0 <= i < self.l1 or not self._wanted(i, key):
                     continue
                 self._staging[i][key] = w
                 self._try_finalize(i)
-        missing = [i for i in range(cfg.num_layers) if self.layers[i].qkv_w is None]
-        if missing or self.embed is None or self.final_norm is None or self.lm_head is None:
+        missing = [i for i in range(self.l0, self.l1) if self.layers[i].qkv_w is None]
+        if missing or (first and self.embed is None) or \
+                (last and (self.final_norm is None or self.lm_head is None)):
             raise RuntimeError(f"incomplete checkpoint: layers {missing[:8]} ... embed/norm/lm_head "
                                f"present={self.embed is not None},{self.final_norm is not None},"
                                f"{self.lm_head is not None}")
+        if not last:
+            self._stage_norm = torch.ones(cfg.hidden_size, dtype=self.dtype, device=self.device)
         self._staging.clear()
 
     def _wanted(self, i: int, key: str) -> bool:
@@ -191,7 +215,7 @@ class DenseDecoderForCausalLM:
 
     def linear_shapes(self) -> list:
         """(N, K) of every dense GEMM weight, for workspace planning."""
-        out = {tuple(self.lm_head.shape)}
+        out = {tuple(self.lm_head.shape)} if self.lm_head is not None else set()
         for L in self.layers:
             for w in (L.qkv_w, L.o_w, L.gu_w, L.down_w):
                 if w is not None:
@@ -199,18 +223,21 @@ class DenseDecoderForCausalLM:
         return sorted(out)
 
     # ------------------------------------------------------------------ forward
-    def forward(self, input_ids: torch.Tensor, meta: AttnMetadata,
-                kv_caches: list) -> torch.Tensor:
-        """input_ids int32 [T] -> final normalised hidden states [T, H]."""
+    def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_caches: list,
+                hidden_in: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """input_ids int32 [T] -> final normalised hidden states [T, H].  Under pipeline
+        parallelism a stage after the first starts from ``hidden_in`` (the residual stream the
+        previous stage returned), and a stage before the last returns its residual stream."""
         cfg, eps = self.cfg, self.cfg.rms_norm_eps
-        T = input_ids.shape[0]
+        T = meta.num_tokens
         self.comm.begin_forward()
-        h = ops.embedding(input_ids, self.embed)
+        h = ops.embedding(input_ids, self.embed) if self.first_stage else hidden_in
         residual = h
-        x = ops.rms_norm(h, self.layers[0].ln1, eps)
-        n = len(self.layers)
-        for i, L in enumerate(self.layers):
-            kc, vc = kv_caches[i]
+        x = ops.rms_norm(h, self.layers[self.l0].ln1, eps)
+        n = self.l1
+        for i in range(self.l0, self.l1):
+            L = self.layers[i]
+            kc, vc = kv_caches[i - self.l0]
             qkv = ops.linear(x, L.qkv_w)
             if self.tq is not None:
                 D, hq, hkv = self.D, self.hq, self.hkv
@@ -226,9 +253,10 @@ class DenseDecoderForCausalLM:
                             eps)
             a = self.attn.forward(qkv, kc, vc, meta)
             x, residual = self.comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
-            nxt = self.layers[i + 1].ln1 if i + 1 < n else self.final_norm
+            nxt = self.layers[i + 1].ln1 if i + 1 < n else \
+                (self.final_norm if self.last_stage else self._stage_norm)
             x, residual = self._mlp_allreduce(i, L, x, T, residual, nxt, eps)
-        return x
+        return x if self.last_stage else residual
 
     def _mlp_allreduce(self, i, L, x, T, residual, nxt, eps):
         """MLP + all-reduce + residual + next norm; the dense down projection fuses its
@@ -250,15 +278,17 @@ class DenseDecoderForCausalLM:
 
     # ------------------------------------------------------------------ KV cache geometry
     def _tq_kv_bytes_per_block(self, block_size: int) -> int:
-        return self.cfg.num_layers * self.hkv * block_size * self.tq.slot_bytes
+        return (self.l1 - self.l0) * self.hkv * block_size * self.tq.slot_bytes
 
     def _tq_allocate_kv_cache(self, num_blocks: int, block_size: int) -> list:
         """TurboQuant cache per layer: uint8 [num_blocks, Hkv, block_size, slot_bytes]."""
-        buf = torch.zeros(self.cfg.num_layers, num_blocks, self.hkv, block_size,
+        n = self.l1 - self.l0
+        buf = torch.zeros(n, num_blocks, self.hkv, block_size,
                           self.tq.slot_bytes, dtype=torch.uint8, device=self.device)
-        return [(buf[i], None) for i in range(self.cfg.num_layers)]
+        return [(buf[i], None) for i in range(n)]
 
     def kv_cache_spec(self) -> dict:
-        n = self.cfg.num_layers + (1 if self.draft_head is not None else 0)
+        """Cache layers of this stage (its decoder layers, plus the EAGLE head's layer)."""
+        n = self.l1 - self.l0 + (1 if self.draft_head is not None else 0)
         return {"num_layers": n, "num_kv_heads": self.hkv,
                 "head_dim": self.D, "dtype": self.dtype}

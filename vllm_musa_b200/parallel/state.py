@@ -31,7 +31,29 @@ class ParallelState:
     ep_size: int = 1
     ep_rank: int = 0
     ep_group: Optional[object] = None
+    pp_size: int = 1
+    pp_rank: int = 0
+    pp_group: Optional[object] = None      # device group of this rank's pipeline (one rank per stage)
+    pp_cpu_group: Optional[object] = None
+    pp_ranks: tuple = ()                    # global ranks of the pipeline, stage order
+    mp_cpu_group: Optional[object] = None  # Gloo group of the model replica (tp x pp ranks)
     comm: Optional[object] = None          # TP communicator (parallel.communicator)
+
+    @property
+    def mp_size(self) -> int:
+        return self.tp_size * self.pp_size
+
+    @property
+    def mp_rank(self) -> int:
+        return self.pp_rank * self.tp_size + self.tp_rank
+
+    @property
+    def is_first_stage(self) -> bool:
+        return self.pp_rank == 0
+
+    @property
+    def is_last_stage(self) -> bool:
+        return self.pp_rank == self.pp_size - 1
 
     @property
     def is_driver(self) -> bool:
@@ -51,21 +73,27 @@ def set_parallel_state(st: ParallelState) -> None:
 
 
 def init_distributed(tp_size: int = 1, ep: bool = False, backend: Optional[str] = None,
-                     timeout_s: float = 300.0) -> ParallelState:
-    """Initialise torch.distributed from the environment and build the TP/EP/DP groups.
+                     timeout_s: float = 300.0, pp_size: int = 1) -> ParallelState:
+    """Initialise torch.distributed from the environment and build the TP/PP/EP/DP groups.
 
-    World = tp_size * dp_size; ranks [k*tp, (k+1)*tp) form TP group k.  EP reuses the TP ranks
-    (experts sharded over the same GPUs that shard attention).  Single process: no groups.
+    World = dp_size * pp_size * tp_size, rank = (dp * pp_size + stage) * tp_size + tp_rank:
+    ranks [k*tp, (k+1)*tp) form TP group k (one pipeline stage of one replica), the ranks
+    with the same replica and TP rank form a pipeline group (stage order), and the tp * pp
+    ranks of a replica form its model-parallel group (host-side lock-step).  EP reuses the TP
+    ranks (experts sharded over the same GPUs that shard attention).  Single process: no
+    groups.
     """
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
     st = ParallelState(world_size=world, rank=rank, local_rank=local_rank)
-    if world == 1 and tp_size == 1:
+    if world == 1 and tp_size == 1 and pp_size == 1:
         set_parallel_state(st)
         return st
-    if world % tp_size != 0:
-        raise ValueError(f"world size {world} not divisible by tensor_parallel_size {tp_size}")
+    mp = tp_size * pp_size
+    if world % mp != 0:
+        raise ValueError(f"world size {world} not divisible by tensor_parallel_size x "
+                         f"pipeline_parallel_size = {mp}")
     if backend is None:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
     if not dist.is_initialized():
@@ -77,16 +105,34 @@ def init_distributed(tp_size: int = 1, ep: bool = False, backend: Optional[str] 
             kw["device_id"] = torch.device("cuda", local_rank)
         dist.init_process_group(backend=backend, rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=timeout_s), **kw)
-    st.tp_size = tp_size
-    st.dp_size = world // tp_size
-    st.dp_rank = rank // tp_size
+    st.tp_size, st.pp_size = tp_size, pp_size
+    st.dp_size = world // mp
+    st.dp_rank = rank // mp
+    st.pp_rank = (rank % mp) // tp_size
     st.tp_rank = rank % tp_size
-    for k in range(st.dp_size):
+    # every rank creates every group, in the same order
+    for k in range(st.dp_size * pp_size):
         ranks = list(range(k * tp_size, (k + 1) * tp_size))
         g = dist.new_group(ranks, backend=backend) if tp_size < world else dist.group.WORLD
         cg = dist.new_group(ranks, backend="gloo")
         if rank in ranks:
             st.tp_group, st.tp_cpu_group = g, cg
+    if pp_size > 1:
+        for d in range(st.dp_size):
+            for t in range(tp_size):
+                ranks = [d * mp + p * tp_size + t for p in range(pp_size)]
+                g = dist.new_group(ranks, backend=backend)
+                cg = dist.new_group(ranks, backend="gloo")
+                if rank in ranks:
+                    st.pp_group, st.pp_cpu_group, st.pp_ranks = g, cg, tuple(ranks)
+        for d in range(st.dp_size):
+            ranks = list(range(d * mp, (d + 1) * mp))
+            cg = dist.new_group(ranks, backend="gloo")
+            if rank in ranks:
+                st.mp_cpu_group = cg
+    else:
+        st.pp_ranks = (rank,)
+        st.mp_cpu_group = st.tp_cpu_group
     if ep:
         st.ep_size, st.ep_rank, st.ep_group = st.tp_size, st.tp_rank, st.tp_group
     set_parallel_state(st)

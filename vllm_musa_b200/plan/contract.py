@@ -46,6 +46,7 @@ class Feature(str, Enum):
     SPARSE_INDEXER = "deepseek.sparse_indexer"
     MTP = "spec.mtp"
     EAGLE = "spec.eagle"
+    PIPELINE_MICROBATCH = "pp.microbatched_stages"
     GDN_CHUNKED_PREFILL = "gdn.chunked_prefill"
     W4AFP8_EXPERTS = "moe.w4afp8_experts"
     TURBOQUANT_KV = "attn.turboquant_kv_cache"
@@ -74,6 +75,7 @@ class ExecutionSignature:
     device: str
     tensor_parallel_size: int
     data_parallel_size: int
+    pipeline_parallel_size: int
     decode_context_parallel_size: int
     enable_expert_parallel: bool
     use_custom_allreduce: bool
@@ -132,6 +134,7 @@ def execution_signature(config) -> ExecutionSignature:
     return ExecutionSignature(
         device=str(config.device).split(":")[0], tensor_parallel_size=p.tensor_parallel_size,
         data_parallel_size=p.data_parallel_size,
+        pipeline_parallel_size=p.pipeline_parallel_size,
         decode_context_parallel_size=p.decode_context_parallel_size,
         enable_expert_parallel=p.enable_expert_parallel,
         use_custom_allreduce=p.use_custom_allreduce,
@@ -186,7 +189,11 @@ def resolve(config) -> OptimizationContract:
         both(Feature.GDN_CHUNKED_PREFILL)
     if m.kv_cache_dtype.startswith("turboquant") and m.family == ModelFamily.DENSE:
         both(Feature.TURBOQUANT_KV)
+    if e.pipeline_parallel_size > 1:
+        both(Feature.PIPELINE_MICROBATCH)
     parts = [m.family.value, m.quant or m.dtype, f"tp{tp}"]
+    if e.pipeline_parallel_size > 1:
+        parts.append(f"pp{e.pipeline_parallel_size}")
     if e.data_parallel_size > 1:
         parts.append(f"dp{e.data_parallel_size}")
     if e.enable_expert_parallel:
@@ -214,5 +221,13 @@ def validate(contract: OptimizationContract) -> None:
             raise ValueError("EAGLE heads are served over the dense decoders (Llama / Qwen)")
         if m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
             raise ValueError("EAGLE drafts need a bf16 KV cache")
+    if e.pipeline_parallel_size > 1:
+        if m.family not in (ModelFamily.DENSE, ModelFamily.MOE):
+            raise ValueError("pipeline parallelism is served for the dense and MoE decoders")
+        if e.speculative_method in ("mtp", "eagle") or e.decode_context_parallel_size > 1:
+            raise ValueError("pipeline parallelism does not combine with model-based drafters "
+                             "or decode context parallelism")
+        if m.num_layers < e.pipeline_parallel_size:
+            raise ValueError("pipeline_parallel_size exceeds the number of layers")
     if e.speculative_method not in (None, "ngram", "mtp", "eagle"):
         raise ValueError(f"speculative method {e.speculative_method!r} is not served")
