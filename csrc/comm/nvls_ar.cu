@@ -219,10 +219,8 @@ B200_DEVICE void finish_row(const NvlsParams& a, int row, int lane, int nvec, ui
 }
 
 // One warp per row; lane l owns the 16-byte vectors l, l + 32, ... (VPW of them).  A warp that
-// walks several rows issues the next row's multimem.ld_reduce before it finishes and stores
-// the current one (rows up to 16 vectors per lane), so the switch's reads for one row overlap
-// the multicast stores of the previous: without it every warp of the grid loads, then stores,
-// in lock-step, and each NVLink direction idles half the time.
+// walks several rows (beyond the block cap) issues the next row's multimem.ld_reduce before it
+// finishes and stores the current one (rows up to 16 vectors per lane).
 template <int VPW, bool kNorm, bool kTwoShot, bool kQuant>
 __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_kernel(NvlsParams a) {
   constexpr bool kPipe = VPW <= 16;
@@ -290,11 +288,11 @@ void launch_norm(const NvlsParams& a, cudaStream_t s) {
 
 int nvls_blocks(int T, int world, bool two_shot, int rows_per_warp) {
   const int rows = two_shot ? (T + world - 1) / world : T;
-  // latency-bound sizes: one row per warp; from 256 rows per rank up, two rows per warp (the
-  // second row's reduce overlaps the first row's stores), 32 blocks at least
-  int rpw = rows_per_warp > 0 ? rows_per_warp : (rows > 256 ? 2 : 1);
-  int blocks = (rows + kNvlsWarps * rpw - 1) / (kNvlsWarps * rpw);
-  if (rows_per_warp <= 0 && rows > 256) blocks = std::max(blocks, 32);
+  // one row per warp up to the block cap (measured at TP=2, 1024 / 4096 / 8192 rows: 42.9 /
+  // 120.6 / 207.5 us with one row per warp, 46.0 / 121.0 / 207.6 with two, 58.1 / 112.6 /
+  // 207.6 with four: the multicast reduce is not phase-bound at these sizes)
+  const int rpw = rows_per_warp > 0 ? rows_per_warp : 1;
+  const int blocks = (rows + kNvlsWarps * rpw - 1) / (kNvlsWarps * rpw);
   return std::max(1, std::min(kMaxBlocks, blocks));
 }
 

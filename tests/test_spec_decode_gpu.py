@@ -38,22 +38,34 @@ def test_oracle_drafts_cut_steps_and_keep_tokens():
 
 
 def test_eagle_head_on_gpu_keeps_tokens():
-    """EAGLE head over the bf16 tiny Llama with CUDA-graph decode: the draft layer runs the
-    GEMM / RoPE-KV / paged-attention kernels on its extra cache layer; verified outputs equal
-    plain decoding up to bf16 near-ties."""
+    """EAGLE head over the bf16 tiny Llama: the draft layer runs the GEMM / RoPE-KV /
+    paged-attention kernels on its extra cache layer after every step, and the verified outputs
+    stay a greedy continuation of the target: teacher-forced against the fp32 reference, every
+    emitted token is the argmax up to bf16 resolution (exact position-by-position agreement
+    with plain decoding is not required: a bf16 near-tie may flip between the one-token decode
+    kernel and the two-token verification step, after which the sequences part)."""
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.models.presets import tiny_llama
+    from vllm_musa_b200.models.reference import ReferenceDecoder
+    from vllm_musa_b200.models.weights import dummy_weights
     cfg = tiny_llama()
     cfg.dtype = torch.bfloat16
     g = torch.Generator().manual_seed(2)
     prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (20, 64, 130)]
-    sp = SamplingParams(temperature=0.0, max_tokens=24, ignore_eos=True)
+    sp = SamplingParams(temperature=0.0, max_tokens=16, ignore_eos=True)
     kw = dict(block_size=64, seed=0, num_gpu_blocks=64, max_model_len=512, max_num_seqs=8,
               max_num_batched_tokens=256)
-    plain = [o.outputs[0].token_ids for o in LLM(cfg, **kw).generate(prompts, sp)]
     llm = LLM(cfg, speculative_config={"method": "eagle", "num_speculative_tokens": 1}, **kw)
     got = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
-    agree = sum(a == b for x, y in zip(got, plain) for a, b in zip(x, y)) / sum(map(len, plain))
-    assert agree > 0.9, agree
     assert llm.engine.drafter.proposed > 0
     assert llm.engine.scheduler.spec_proposed() > 0
+    llm.shutdown()
+    ref_cfg = tiny_llama()
+    W = {k: v.cpu() for k, v in dummy_weights(ref_cfg, seed=0, std=0.02, device="cuda")}
+    ref = ReferenceDecoder(ref_cfg, W)
+    for p, toks in zip(prompts, got):
+        assert len(toks) == 16
+        for k, t in enumerate(toks):
+            want = ref.logits(p + toks[:k])[-1]
+            gap = float(want.max() - want[t]) / float(want.abs().max())
+            assert gap < 0.03, (k, gap)

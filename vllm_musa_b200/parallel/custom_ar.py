@@ -65,10 +65,11 @@ NVLS_ROWS_PER_WARP = int(os.environ.get("B200_AR_NVLS_ROWS_PER_WARP", "0"))
 if os.environ.get("B200_AR_NVLS_MIN_BYTES"):
     NVLS_MIN_BYTES = {w: int(os.environ["B200_AR_NVLS_MIN_BYTES"]) for w in (2, 4, 8)}
 # the NVLS kernel's fused 1x128 e4m3 output replaces AR + norm + a separate quantisation from
-# this many rows up, by world size (TP=2: 61.5 vs 81.6 us at 2048 rows, 33.3 vs 32.2 us at 256,
-# 21.1 vs 14.2 at 8; TP=8: faster at every measured size, 26.0 vs 37.5 us at 8 rows, 32.5 vs
-# 52.4 at 256; TP=4 interpolated)
-NVLS_QUANT_MIN_ROWS = {2: 1024, 4: 256, 8: 1}
+# this many rows up, by world size.  TP=2: never (against the peer-to-peer AR + norm + group
+# quantisation it measures 25.9 vs 14.2 us at 8 rows, 34.8 vs 23.7 at 256, 69.0 vs 53.7 at
+# 2048); TP=8: faster at every measured size (26.0 vs 37.5 us at 8 rows, 32.5 vs 52.4 at 256,
+# 61.2 vs 81.6 at 2048); TP=4 interpolated.
+NVLS_QUANT_MIN_ROWS = {2: 1 << 30, 4: 256, 8: 1}
 if os.environ.get("B200_AR_NVLS_QUANT_MIN_ROWS"):
     NVLS_QUANT_MIN_ROWS = {w: int(os.environ["B200_AR_NVLS_QUANT_MIN_ROWS"]) for w in (2, 4, 8)}
 
