@@ -49,6 +49,7 @@ struct GemmPlan {
   int mt;
 };
 GemmPlan plan_bf16(int M, int N, int K);
+void set_katoms(int katoms);  // K atoms per pipeline stage: 0 automatic, else forced (tuning)
 void run_bf16(const GemmArgs& a, cudaStream_t s);
 struct GroupedGemmArgs {
   const void* A;  // [max_rows, K] expert-sorted rows

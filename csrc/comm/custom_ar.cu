@@ -58,7 +58,8 @@ B200_DEVICE bool block_barrier(const ArParams& a, int phase, uint32_t epoch) {
     st_release_sys(peer_slot, epoch);
     const uint32_t* my_slot = a.flags[a.rank] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + p;
     const long long t0 = clock64();
-    while ((int32_t)(ld_acquire_sys(my_slot) - epoch) < 0) {
+    for (uint32_t spin = 1; (int32_t)(ld_acquire_sys(my_slot) - epoch) < 0; ++spin) {
+      if ((spin & 31) != 0) continue;  // error word / clock every 32nd poll
       if (clock64() - t0 > kWaitBudgetCycles) {
         record_error(a.err, kErrPeerTimeout);
         ok_all = 0;
@@ -96,7 +97,9 @@ B200_DEVICE void reduce_row(const ArParams& a, int row, int r0, float (&o)[VPT][
                             ((size_t)pp * a.rs_rows + (row - r0)) * a.H
                       : reinterpret_cast<const __nv_bfloat16*>(a.staging[pp]) + (size_t)row * a.H);
   }
-#pragma unroll
+  // (rows of up to 2 vectors per thread keep every rank's loads in registers at once; wider
+  // rows take one vector index at a time to stay within the register budget)
+#pragma unroll(VPT <= 2 ? VPT : 1)
   for (int i = 0; i < VPT; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nvec) {
@@ -412,7 +415,8 @@ __global__ void __launch_bounds__(256) cand_exchange_kernel(CandParams a) {
     st_release_sys(peer_slot, epoch);
     const uint32_t* my_slot = a.flags[a.rank] + (phase * kMaxBlocks + blockIdx.x) * kMaxRanks + p;
     const long long t0 = clock64();
-    while ((int32_t)(ld_acquire_sys(my_slot) - epoch) < 0) {
+    for (uint32_t spin = 1; (int32_t)(ld_acquire_sys(my_slot) - epoch) < 0; ++spin) {
+      if ((spin & 31) != 0) continue;  // error word / clock every 32nd poll
       if (clock64() - t0 > kWaitBudgetCycles) {
         record_error(a.err, kErrPeerTimeout);
         ok_all = 0;

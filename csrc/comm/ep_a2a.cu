@@ -98,7 +98,8 @@ __global__ void ep_exchange_kernel(A2AParams p) {
     st_release_sys(p.flags[q] + p.rank, epoch);
     const uint32_t* mine = p.flags[p.rank] + q;
     const long long t0 = clock64();
-    while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
+    for (uint32_t spin = 1; (int32_t)(ld_acquire_sys(mine) - epoch) < 0; ++spin) {
+      if ((spin & 31) != 0) continue;  // error word / clock every 32nd poll
       if (clock64() - t0 > kWaitBudgetCycles) {
         record_error(p.err, kErrPeerTimeout);
         break;

@@ -90,7 +90,8 @@ B200_DEVICE bool nvls_barrier(const NvlsParams& a, int phase, uint32_t epoch) {
     mm_red_add_release(a.mc_flags + idx, 1u);
     const uint32_t target = epoch * (uint32_t)a.world;
     const long long t0 = clock64();
-    while ((int32_t)(ld_acquire_sys_u32(a.flags + idx) - target) < 0) {
+    for (uint32_t spin = 1; (int32_t)(ld_acquire_sys_u32(a.flags + idx) - target) < 0; ++spin) {
+      if ((spin & 31) != 0) continue;  // error word / clock every 32nd poll
       if (clock64() - t0 > kWaitBudgetCycles) {
         record_error(a.err, kErrPeerTimeout);
         ok_all = 0;

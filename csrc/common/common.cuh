@@ -171,18 +171,22 @@ B200_DEVICE bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase.  Returns false (and records kErrMbarTimeout) when the
-// budget runs out or another warp already raised an error.
+// budget runs out or another warp already raised an error.  The error word lives in global
+// memory: it is polled only every 32nd failed try (a volatile load is an L2 round trip, and a
+// pipeline hand-off waiting behind one notices its phase that much later).
 B200_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(a, parity)) return true;
-    if (clock64() - t0 > kWaitBudgetCycles) {
-      record_error(err, kErrMbarTimeout);
-      return false;
+    if ((n & 31) == 0) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        record_error(err, kErrMbarTimeout);
+        return false;
+      }
+      if (error_raised(err)) return false;
     }
-    if (error_raised(err)) return false;
   }
 }
 

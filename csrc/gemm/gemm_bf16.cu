@@ -65,6 +65,7 @@ struct Params {
   int M, N, K;
   int bn, stages, acc_bufs, tmem_cols;
   int num_m, num_n, num_kb, splits, kb_per_split;
+  int katoms;  // 64-element K atoms per pipeline stage (one TMA box per operand and atom)
   int total_units;
   void* C;  // output (bf16 or fp32) or fp32 workspace for split-K
   int ldc;  // elements
@@ -206,8 +207,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int STAGES = p.stages;
-  const int A_BYTES = a_tile_bytes(MT);
-  const int B_BYTES = b_tile_bytes(p.bn);
+  const int KA = p.katoms;
+  const int A_ATOM = a_tile_bytes(MT);
+  const int B_ATOM = b_tile_bytes(p.bn);
+  const int A_BYTES = A_ATOM * KA;
+  const int B_BYTES = B_ATOM * KA;
   const int STAGE_BYTES = A_BYTES + B_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* full = bars;
@@ -256,7 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         unit_coords(blockIdx.x, p, m, n, ks);
         const int kb0 = ks * p.kb_per_split;
         const int kb1 = min(p.num_kb, kb0 + 2 * STAGES);
-        for (int kb = kb0; kb < kb1; ++kb) tma_prefetch_l2_2d(&tmB, kb * BK, n * BN);
+        for (int kb = kb0; kb < kb1; ++kb)
+          for (int a = 0; a < KA; ++a) tma_prefetch_l2_2d(&tmB, (kb * KA + a) * BK, n * BN);
       }
       pdl_wait();
       for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
@@ -271,9 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* st = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(st, &tmA, &full[stage], kb * BK, m * BM * MT);
           const int brow = GROUPED ? p.tile_expert[m] * p.N + n * BN : n * BN;
-          tma_load_2d(st + A_BYTES, &tmB, &full[stage], kb * BK, brow);
+          for (int a = 0; a < KA; ++a) {
+            const int x = (kb * KA + a) * BK;
+            tma_load_2d(st + a * A_ATOM, &tmA, &full[stage], x, m * BM * MT);
+            tma_load_2d(st + A_BYTES + a * B_ATOM, &tmB, &full[stage], x, brow);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -316,15 +324,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc::fence_after_sync();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-          const uint64_t bdesc = tc::smem_desc_kmajor_sw128(sa + A_BYTES);
+          for (int a = 0; a < KA; ++a) {
+            const uint64_t bdesc = tc::smem_desc_kmajor_sw128(sa + A_BYTES + a * B_ATOM);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
+            for (int k = 0; k < BK / 16; ++k) {
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const uint64_t adesc = tc::smem_desc_kmajor_sw128(sa + mt * BM * 128);
-              // +32 bytes along K inside the 128-byte swizzle atom -> +2 in the >>4 field
-              tc::mma_f16_ss(d_tmem + mt * BN, adesc + 2 * k, bdesc + 2 * k, idesc,
-                             (kb > kb0 || k > 0) ? 1u : 0u);
+              for (int mt = 0; mt < MT; ++mt) {
+                const uint64_t adesc =
+                    tc::smem_desc_kmajor_sw128(sa + a * A_ATOM + mt * BM * 128);
+                // +32 bytes along K inside the 128-byte swizzle atom -> +2 in the >>4 field
+                tc::mma_f16_ss(d_tmem + mt * BN, adesc + 2 * k, bdesc + 2 * k, idesc,
+                               (kb > kb0 || a > 0 || k > 0) ? 1u : 0u);
+              }
             }
           }
           tc::mma_commit(&empty[stage]);
@@ -570,8 +581,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   const int STAGES = p.stages;
   const int BN = p.bn, HALF = BN / 2;
-  const int A_BYTES = BM * BK * 2;
-  const int B_BYTES = HALF * BK * 2;
+  const int KA = p.katoms;
+  const int A_ATOM = BM * BK * 2;
+  const int B_ATOM = HALF * BK * 2;
+  const int A_BYTES = A_ATOM * KA;
+  const int B_BYTES = B_ATOM * KA;
   const int STAGE_BYTES = A_BYTES + B_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* full = bars;
@@ -626,8 +640,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = smem + stage * STAGE_BYTES;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
           const uint32_t fullc = mapa_shared(smem_u32(&full[stage]), 0);
-          tma_load_2d_pair(st, &tmA, fullc, kb * BK, m * 2 * BM + (int)crank * BM);
-          tma_load_2d_pair(st + A_BYTES, &tmB, fullc, kb * BK, n * BN + (int)crank * HALF);
+          for (int a = 0; a < KA; ++a) {
+            const int x = (kb * KA + a) * BK;
+            tma_load_2d_pair(st + a * A_ATOM, &tmA, fullc, x, m * 2 * BM + (int)crank * BM);
+            tma_load_2d_pair(st + A_BYTES + a * B_ATOM, &tmB, fullc, x,
+                             n * BN + (int)crank * HALF);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -666,12 +684,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc::fence_after_sync();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-          const uint64_t adesc = tc::smem_desc_kmajor_sw128(sa);
-          const uint64_t bdesc = tc::smem_desc_kmajor_sw128(sa + A_BYTES);
+          for (int a = 0; a < KA; ++a) {
+            const uint64_t adesc = tc::smem_desc_kmajor_sw128(sa + a * A_ATOM);
+            const uint64_t bdesc = tc::smem_desc_kmajor_sw128(sa + A_BYTES + a * B_ATOM);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            tc::mma_f16_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc,
-                                (kb > kb0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k)
+              tc::mma_f16_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc,
+                                  (kb > kb0 || a > 0 || k > 0) ? 1u : 0u);
+          }
           tc::mma_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
@@ -853,10 +873,26 @@ static int pair_bn(int M, int N) {
   return best;
 }
 
-static int stages_for(int mt, int bn) {
-  const int stage = a_tile_bytes(mt) + b_tile_bytes(bn);
-  return std::min(kMaxStages, (kSmemBudget - kSmemOverhead) / stage);
+// K atoms per pipeline stage.  Measured on B200 with a TMA-only probe (one CTA per SM, tiled
+// 128-byte-swizzled boxes, L2-resident source): a stage's mbarrier round trip costs ~250-340
+// ns almost regardless of its size, so one CTA pulls 33 / 66 / 132 GB/s with 8 / 16 / 32 KiB
+// stages but 190-230 GB/s with 64 KiB stages (the 148 SMs together saturate L2 at ~19 TB/s).
+// A decode-sized GEMM streams its whole K range through few stages per CTA, so stages are
+// made at least 48 KiB (two or four 64-element K atoms, one TMA box per operand and atom)
+// while at least three still fit.  0: automatic; set_katoms() forces a count (tuning).
+static int g_katoms = 0;
+void set_katoms(int k) { g_katoms = k; }
+
+static int choose_katoms(int stage1, int K, int splits, int budget) {
+  auto ok = [&](int ka, int min_stages) {
+    return K % (BK * ka) == 0 && budget / (stage1 * ka) >= min_stages && K / (BK * ka) >= splits;
+  };
+  if (g_katoms > 0) return ok(g_katoms, 2) || g_katoms == 1 ? g_katoms : 1;
+  int ka = 1;
+  while (ka < 4 && stage1 * ka < 48 * 1024 && ok(2 * ka, 3)) ka *= 2;
+  return ka;
 }
+
 
 // Cost model.  A unit's time is the largest of (a) its MMA time, (b) filling shared memory
 // with its A and B tiles through L2 at its share of L2 bandwidth (capped per SM), and (c)
@@ -944,8 +980,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
                    cudaStream_t stream) {
   auto kern = gemm_bf16_kernel<MT, EPI>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
-  const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) + kSmemOverhead +
-                   (EPI == kScatter || kTransposed<EPI> ? kScatterBytes : 0);
+  const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) * p.katoms +
+                   kSmemOverhead + (EPI == kScatter || kTransposed<EPI> ? kScatterBytes : 0);
   const int grid = std::min(p.total_units, num_sms());
   launch_pdl(kern, grid, smem, stream, ta, tb, p);
   count_launch();
@@ -956,7 +992,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Para
                         cudaStream_t stream) {
   auto kern = gemm_bf16_pair_kernel<EPI>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
-  const int smem = p.stages * (BM * BK * 2 + (p.bn / 2) * BK * 2) + kSmemOverhead;
+  const int smem = p.stages * (BM * BK * 2 + (p.bn / 2) * BK * 2) * p.katoms + kSmemOverhead;
   const int pairs = std::max(1, std::min(p.total_units, num_sms() / 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
@@ -1040,14 +1076,19 @@ void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
   p.N = N;
   p.K = K;
   p.bn = bn;
-  p.stages = stages_for(1, bn);
+  {
+    const int stage1 = a_tile_bytes(1) + b_tile_bytes(bn);
+    const int budget = kSmemBudget - kSmemOverhead;
+    p.katoms = choose_katoms(stage1, K, 1, budget);
+    p.stages = std::min(kMaxStages, budget / (stage1 * p.katoms));
+  }
   p.acc_bufs = 2 * bn <= 512 ? 2 : 1;
   int cols = 32;
   while (cols < p.acc_bufs * bn) cols <<= 1;
   p.tmem_cols = cols;
   p.num_m = a.max_rows / BM;  // upper bound; the kernel reads the live count
   p.num_n = (N + bn - 1) / bn;
-  p.num_kb = (K + BK - 1) / BK;
+  p.num_kb = (K + BK * p.katoms - 1) / (BK * p.katoms);
   p.splits = 1;
   p.kb_per_split = p.num_kb;
   p.total_units = p.num_m * p.num_n;
@@ -1067,7 +1108,7 @@ void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
                   (uint64_t)a.num_experts * N, a.ldb, BK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   auto go = [&](auto kern) {
     ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
-    const int smem = p.stages * (a_tile_bytes(1) + b_tile_bytes(bn)) + kSmemOverhead;
+    const int smem = p.stages * (a_tile_bytes(1) + b_tile_bytes(bn)) * p.katoms + kSmemOverhead;
     const int grid = std::min(p.total_units, num_sms());
     launch_pdl(kern, grid, smem, stream, ta, tb, p);
   };
@@ -1132,12 +1173,15 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.N = N;
   p.K = K;
   p.bn = plan.bn;
-  p.stages = pair ? std::min(kMaxStages, (kSmemBudget - kSmemOverhead) /
-                                             (BM * BK * 2 + (plan.bn / 2) * BK * 2))
-                  : stages_for(plan.mt, plan.bn);
-  if (a.mode == kModeScatter || transposed)  // room for the epilogue's shared-memory staging
-    p.stages = std::min(p.stages, (kSmemBudget - kSmemOverhead - kScatterBytes) /
-                                      (a_tile_bytes(plan.mt) + b_tile_bytes(plan.bn)));
+  {
+    const int stage1 = pair ? BM * BK * 2 + (plan.bn / 2) * BK * 2
+                            : a_tile_bytes(plan.mt) + b_tile_bytes(plan.bn);
+    // room for the epilogue's shared-memory staging (scatter / transposed stores)
+    const int budget = kSmemBudget - kSmemOverhead -
+                       (a.mode == kModeScatter || transposed ? kScatterBytes : 0);
+    p.katoms = choose_katoms(stage1, K, std::max(1, plan.splits), budget);
+    p.stages = std::min(kMaxStages, budget / (stage1 * p.katoms));
+  }
   const int acc_cols = plan.mt * plan.bn;
   p.acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
   int cols = 32;
@@ -1145,7 +1189,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.tmem_cols = cols;
   p.num_m = pair ? (M + 2 * BM - 1) / (2 * BM) : (M + BM * plan.mt - 1) / (BM * plan.mt);
   p.num_n = (N + plan.bn - 1) / plan.bn;
-  p.num_kb = (K + BK - 1) / BK;
+  p.num_kb = (K + BK * p.katoms - 1) / (BK * p.katoms);
   p.splits = std::max(1, std::min<int>(plan.splits, p.num_kb));
   p.kb_per_split = (p.num_kb + p.splits - 1) / p.splits;
   p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;

@@ -347,7 +347,8 @@ __global__ void __launch_bounds__(kMergeThreads) topk_exchange_kernel(ExchangePa
     const uint32_t* my_slot =
         a.flags[a.rank] + (phase * comm::kMaxBlocks + blockIdx.x) * comm::kMaxRanks + p;
     const long long t0 = clock64();
-    while ((int32_t)(ld_acquire_sys_u32(my_slot) - epoch_s) < 0) {
+    for (uint32_t spin = 1; (int32_t)(ld_acquire_sys_u32(my_slot) - epoch_s) < 0; ++spin) {
+      if ((spin & 31) != 0) continue;  // error word / clock every 32nd poll
       if (clock64() - t0 > kWaitBudgetCycles) {
         record_error(a.err, kErrPeerTimeout);
         ok_all = 0;

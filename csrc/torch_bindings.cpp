@@ -1661,6 +1661,8 @@ void register_runtime(pybind11::module_& m);  // csrc/runtime/bindings.cpp
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vllm_musa_b200 native extension (sm_100a kernels + host runtime)";
   m.def("gemm_plan", &gemm_plan, "automatic (bn, splits, workspace_floats) for a bf16 GEMM");
+  m.def("gemm_set_katoms", [](int64_t k) { b200::gemm::set_katoms((int)k); },
+        "64-element K atoms per bf16 GEMM pipeline stage: 0 automatic, 1 / 2 / 4 forced");
   m.def("set_prefill_tc2", [](bool on) { b200::attn::set_prefill_tc2(on); },
         "allow (true) the two-heads-per-CTA tcgen05 prefill kernel for even GQA groups");
   m.def("set_prefill_tc", [](bool on) { b200::attn::set_prefill_tc(on); },

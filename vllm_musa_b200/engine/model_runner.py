@@ -143,8 +143,8 @@ class ModelRunner:
         self.pp = st if st is not None and st.pp_size > 1 else None
         if self.pp is not None:
             self.use_graphs = False
-            self.pp_micro_batches = int(os.environ.get("B200_PP_MICRO_BATCHES",
-                                                       str(self.pp.pp_size)))
+            self.pp_micro_batches = int(os.environ.get("B200_PP_MICRO_BATCHES", "0")) or \
+                self.pp.pp_size
 
     # ------------------------------------------------------------------ memory / KV cache
     def kv_bytes_per_block(self) -> int:

@@ -54,6 +54,30 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
             "vLLM plugin: activate the B200 platform even if no sm_100 device is detected"),
     EnvFlag("B200_CUSTOM_OP_USE_NATIVE", False, _bool,
             "vLLM plugin: register the custom ops but route them to the PyTorch implementations"),
+    EnvFlag("B200_AR_NVLS", True, _bool,
+            "allow the NVLS (multimem) all-reduce where every rank got a multicast mapping"),
+    EnvFlag("B200_AR_NVLS_MIN_BYTES", None, int,
+            "NVLS for messages above this many bytes at every world size (default: the "
+            "measured per-world table in parallel/custom_ar.py)"),
+    EnvFlag("B200_AR_NVLS_QUANT_MIN_ROWS", None, int,
+            "rows from which the NVLS kernel emits the 1x128 e4m3 output itself (default: "
+            "per-world table)"),
+    EnvFlag("B200_AR_NVLS_ROWS_PER_WARP", 0, int,
+            "rows each warp of the NVLS kernel walks (0: one row per warp up to the block cap)"),
+    EnvFlag("B200_FUSE_GEMM_RS", False, _bool,
+            "row-parallel GEMM with the reduce-scatter in its epilogue (peer stores) + local "
+            "reduce / norm / all-gather, instead of GEMM + fused all-reduce"),
+    EnvFlag("B200_EP_A2A", True, _bool,
+            "MoE expert parallelism over the NVLink dispatch / return all-to-all kernels"),
+    EnvFlag("B200_PP_MICRO_BATCHES", 0, int,
+            "micro-batches per pipeline-parallel step (0: pipeline_parallel_size)"),
+    EnvFlag("B200_ATTN_TC", True, _bool, "tcgen05 prefill attention (head_dim 128)"),
+    EnvFlag("B200_ATTN_TC2", True, _bool,
+            "two-heads-per-CTA tcgen05 prefill attention where the GQA group allows"),
+    EnvFlag("B200_GEMM_PAIR_MIN_ROWS", 2048, int,
+            "rows from which untuned GEMM shapes use CTA-pair (cta_group::2) tiles (<= 0: never)"),
+    EnvFlag("B200_GEMM_SPLITK_REDUCE", True, _bool,
+            "split-K partial sums reduced by a separate grid (PDL) instead of the last CTA"),
     EnvFlag("B200_LOG_LEVEL", "INFO", str, "logging level of the vllm_musa_b200 logger"),
     EnvFlag("B200_TORCH_PROFILER_DIR", "b200_traces", str,
             "directory of the Chrome traces written by LLM.stop_profile()"),
