@@ -1,5 +1,6 @@
 """Sweep the tcgen05 BF16 GEMM's plans (tile width BN x split-K x row tiles: MT = 1 or 2
-128-row tiles per CTA, or 4 = a CTA pair on a 256-row tile) for a model's linear shapes
+128-row tiles per CTA, 3 = one 128-row tile per CTA with the K splits reduced inside a
+cluster, or 4 = a CTA pair on a 256-row tile) for a model's linear shapes
 and write the fastest plan per (N, K, M) to vllm_musa_b200/tuning/gemm_bf16.json.
 
 Timing: a loop of launches cycling through copies of the weight whose total exceeds L2 (every
@@ -101,7 +102,7 @@ def main():
                            ws, a.reps)
             best = (t_auto, auto[0], auto[1], auto[3])
             kb = (K + 63) // 64
-            for mt in ((1, 2, 4) if M > 128 else (1,)):
+            for mt in ((1, 2, 4, 3) if M > 128 else (1, 3) if M <= 512 else (1,)):
                 for bn in (256, 224, 208, 192, 176, 160, 144, 128, 112, 96, 64, 48, 32):
                     if mt == 4 and (bn % 32 or bn < 128):  # CTA pairs: 256-row tiles
                         continue
@@ -109,8 +110,9 @@ def main():
                         continue
                     if M >= 1024 and mt != 4 and (bn % 64 or mt * bn * 2 > 512):
                         continue
+                    # mt 3: one-CTA tiles whose 2-4 K splits reduce inside a cluster
                     for s in ((1,) if M >= 1024 else (1, 2, 3, 4) if mt == 4 else
-                              (1, 2, 3, 4, 6, 8)):
+                              (2, 3, 4) if mt == 3 else (1, 2, 3, 4, 6, 8)):
                         if s > 1 and kb // s < 4:
                             continue
                         if s * M * N > (64 << 20):
@@ -145,13 +147,15 @@ def main():
                 entries.append({"n": N, "k": K, "m": M, "bn": swap_best[1],
                                 "splits": swap_best[2], "mt": swap_best[3], "swap": 1,
                                 "us": round(swap_best[0], 2)})
-    table = {"device": torch.cuda.get_device_name(), "model": a.model, "tp": a.tp,
+    table = {"device": torch.cuda.get_device_name(), "model": a.model, "tp": str(a.tp),
              "entries": entries}
     if a.write:
         path = a.out or path_of("gemm_bf16")
         old = {"entries": []}
         if os.path.exists(path):
             old = json.load(open(path))
+            tps = set(str(old.get("tp", "")).split(",")) | {str(a.tp)}
+            table["tp"] = ",".join(sorted((t for t in tps if t), key=int))
         fresh = {(x["n"], x["k"], x["m"]) for x in entries}
         keep = [e for e in old["entries"] if (e["n"], e["k"], e["m"]) not in fresh]
         table["entries"] = keep + entries

@@ -33,6 +33,7 @@
 // Every mbarrier wait is bounded (common.cuh); a timeout leaves an error code and the kernel
 // drains, frees TMEM and returns.
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "../b200_kernels.h"
@@ -55,6 +56,12 @@ constexpr int kScatterBytes = 4 * kScatterWarpBytes;
 
 enum Epilogue : int { kStore = 0, kSiluMul = 1, kF32 = 2, kScatter = 3, kStoreT = 4, kSiluT = 5 };
 
+B200_DEVICE void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+
 // Transposed ("swap-AB") epilogues compute C^T = W . X^T so a decode-sized token count sits in
 // the MMA's N dimension (one 128 x M tile per 128 weight rows, the efficient tcgen05 shape) and
 // write C[token][feature] through a per-warp shared-memory transpose.
@@ -66,6 +73,7 @@ struct Params {
   int bn, stages, acc_bufs, tmem_cols;
   int num_m, num_n, num_kb, splits, kb_per_split;
   int katoms;  // 64-element K atoms per pipeline stage (one TMA box per operand and atom)
+  int csplit;  // > 1: split-K over a cluster of csplit CTAs reduced through distributed smem
   int total_units;
   void* C;  // output (bf16 or fp32) or fp32 workspace for split-K
   int ldc;  // elements
@@ -98,8 +106,14 @@ B200_HOST_DEVICE int b_tile_bytes(int bn) { return bn * BK * 2; }
 
 B200_DEVICE void unit_coords(int u, const Params& p, int& m, int& n, int& ks) {
   const int tiles = p.num_m * p.num_n;
-  ks = u / tiles;
-  const int t = u - ks * tiles;
+  int t;
+  if (p.csplit > 1) {  // the K splits of a tile are the consecutive CTAs of one cluster
+    ks = u % p.csplit;
+    t = u / p.csplit;
+  } else {
+    ks = u / tiles;
+    t = u - ks * tiles;
+  }
   const int group = kGroupN * p.num_m;
   const int g = t / group;
   const int r = t - g * group;
@@ -188,6 +202,76 @@ B200_DEVICE void store_chunk16(const Params& p, int row, int col, const float (&
       if (col + 4 * v < p.N)
         *reinterpret_cast<float4*>(C + 4 * v) =
             make_float4(f[4 * v], f[4 * v + 1], f[4 * v + 2], f[4 * v + 3]);
+  }
+}
+
+// Cluster split-K reduction (one-CTA kernel, MT = 1).  The csplit CTAs of a cluster computed
+// the same 128 x BN tile over different K ranges; each holds its partial sum in TMEM.  Row
+// quarter q (TMEM lanes 32q..32q+31, epilogue warp q) is owned by cluster rank q % csplit: the
+// other ranks' epilogue warps store their quarter-q rows into the owner's shared memory
+// (distributed shared memory, over the idle pipeline ring), and the owner adds them to its own
+// rows and runs the epilogue.  Two cluster barriers bracket the exchange; every thread of every
+// CTA reaches both, error or not.  Row layout in a receive slot: 32 rows x BN fp32 with the
+// 16-byte chunks XOR-swizzled by row (conflict-free 16-byte stores and loads per 8 lanes).
+template <int EPI>
+B200_DEVICE void csplit_reduce(const Params& p, uint8_t* smem, uint32_t tmem_base, int warp,
+                               int lane) {
+  const int S = p.csplit;
+  const int BN = p.bn;
+  const uint32_t rank = cluster_ctarank();
+  int m, n, ks;
+  unit_coords(blockIdx.x, p, m, n, ks);
+  const bool epi = warp >= 2;
+  const int q = warp & 3;
+  const int owner = q % S;
+  const int nch = BN / 4;
+  const uint32_t slot_bytes = 32u * BN * 4u;
+  const uint32_t region = smem_u32(smem) + (uint32_t)(q / S) * (S - 1) * slot_bytes;
+  const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16);
+  auto chunk = [&](int c) { return (uint32_t)(((c | 7) < nch ? (c ^ (lane & 7)) : c) * 16); };
+  tc::fence_before_sync();
+  __syncwarp();
+  cluster_sync();  // every accumulator final, every pipeline ring idle
+  tc::fence_after_sync();
+  if (epi && (int)rank != owner) {
+    const int slot = (int)rank < owner ? (int)rank : (int)rank - 1;
+    const uint32_t dst = mapa_shared(region + slot * slot_bytes + lane * BN * 4u, owner);
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tc::tmem_ld_32x32b_x16(t_row + c, r);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        st_cluster_v4(dst + chunk(c / 4 + v), r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+    }
+  }
+  __syncwarp();
+  cluster_sync();  // every partial delivered
+  if (epi && (int)rank == owner) {
+    const int row = m * BM + q * 32 + lane;
+    const float* mine = reinterpret_cast<const float*>(smem + (region - smem_u32(smem)) +
+                                                       lane * BN * 4);
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tc::tmem_ld_32x32b_x16(t_row + c, r);
+      tc::tmem_ld_wait();
+      float f[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(r[j]);
+      for (int sl = 0; sl < S - 1; ++sl) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(mine) + sl * slot_bytes;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 x = *reinterpret_cast<const float4*>(src + chunk(c / 4 + v));
+          f[4 * v] += x.x;
+          f[4 * v + 1] += x.y;
+          f[4 * v + 2] += x.z;
+          f[4 * v + 3] += x.w;
+        }
+      }
+      const int col = n * BN + c;
+      if (row < p.M && col < p.N) store_chunk16<EPI>(p, row, col, f);
+    }
   }
 }
 
@@ -352,6 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if (p.csplit > 1) {
+    // ------------------------------------------------------------------ cluster split-K
+    // one unit per CTA: wait for the accumulator; the exchange follows (csplit_reduce)
+    if (mbar_wait(&acc_full[0], 0, p.err)) tc::fence_after_sync();
   } else {
     // ------------------------------------------------------------------ epilogue
     __shared__ int s_last;
@@ -553,6 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if constexpr (!GROUPED && MT == 1 && (EPI == kStore || EPI == kSiluMul || EPI == kF32)) {
+    if (p.csplit > 1) csplit_reduce<EPI>(p, smem, tmem_base, warp, lane);
+  }
   // peer stores of the scatter epilogue are made visible system-wide before the kernel ends
   if constexpr (EPI == kScatter) __threadfence_system();
   tc::fence_before_sync();
@@ -1048,6 +1139,91 @@ static bool splitk_reduce_kernel_on() {
   return v == 1;
 }
 
+// Plans with mt = 3 run one-CTA 128-row tiles whose K splits form a cluster and are reduced
+// through distributed shared memory (csplit_reduce) instead of fp32 partials in global memory
+// plus a reduction pass.  Measured on decode shapes: a win with two splits (e.g. M = 256,
+// N = K = 4096: 16.7 vs 18.6 us; N = 3584, K = 4096: 16.4 vs 19.7 us), a loss once the clusters
+// no longer fit one wave (three or four splits with 100+ tiles), so the tuner chooses it per
+// shape and the launcher falls back to the global path when the clusters would not all be
+// resident at once.  B200_GEMM_CLUSTER_SPLITK=0 disables it.
+static bool cluster_splitk_on() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("B200_GEMM_CLUSTER_SPLITK");
+    v = (e == nullptr || atoi(e) != 0) ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// How many clusters of `csplit` one-CTA GEMM blocks with `smem` bytes can be resident at once.
+template <int EPI>
+static int max_active_clusters(int csplit, int smem) {
+  static std::mutex mu;
+  static std::vector<std::pair<long, int>> cache;
+  const long key = (long)csplit << 32 | (unsigned)smem;
+  std::lock_guard<std::mutex> g(mu);
+  for (auto& kv : cache)
+    if (kv.first == key) return kv.second;
+  auto kern = gemm_bf16_kernel<1, EPI>;
+  ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(csplit * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache.push_back({key, n});
+  return n;
+}
+
+// Largest receive region one cluster rank needs: its owned row quarters x (csplit - 1) slots of
+// 32 rows x bn fp32.
+static int csplit_region_bytes(int csplit, int bn) {
+  const int owned = (4 + csplit - 1) / csplit;
+  return owned * (csplit - 1) * 32 * bn * 4;
+}
+
+template <int EPI>
+static void launch_csplit(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                          cudaStream_t stream) {
+  auto kern = gemm_bf16_kernel<1, EPI>;
+  ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
+  const int smem = p.stages * (a_tile_bytes(1) + b_tile_bytes(p.bn)) * p.katoms + kSmemOverhead;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.total_units);  // one unit per CTA; each tile's splits form a cluster
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.csplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string("b200: cluster split-K gemm launch failed: ") +
+                             cudaGetErrorString(e) + " grid=" + std::to_string(p.total_units) +
+                             " cluster=" + std::to_string(p.csplit) +
+                             " smem=" + std::to_string(smem));
+  }
+  count_launch();
+}
+
 template <int EPI>
 static void dispatch_mt(int mt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                         cudaStream_t s) {
@@ -1076,6 +1252,7 @@ void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
   p.N = N;
   p.K = K;
   p.bn = bn;
+  p.csplit = 1;
   {
     const int stage1 = a_tile_bytes(1) + b_tile_bytes(bn);
     const int budget = kSmemBudget - kSmemOverhead;
@@ -1147,6 +1324,9 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.bn > 0) plan.bn = a.bn;
   if (a.splits > 0) plan.splits = a.splits;
   if (a.mt > 0) plan.mt = a.mt;
+  // mt = 3: one-CTA tiles (mt 1) with the K splits reduced inside a cluster
+  const bool want_cluster = plan.mt == 3;
+  if (want_cluster) plan.mt = 1;
   // CTA pairs (mt = 4): 256-row tiles; chosen automatically for large M (no split-K)
   const bool transposed = a.mode == kModeStoreT || a.mode == kModeSiluT;
   B200_REQUIRE(a.mode != kModeSiluT || M % 16 == 0,
@@ -1166,7 +1346,8 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   }
   B200_REQUIRE(plan.bn >= 16 && plan.bn <= 256 && plan.bn % 16 == 0,
                "gemm_bf16: bn must be a multiple of 16 in [16, 256]");
-  B200_REQUIRE(plan.mt == 1 || plan.mt == 2, "gemm_bf16: mt must be 1, 2 or 4 (CTA pair)");
+  B200_REQUIRE(plan.mt == 1 || plan.mt == 2,
+               "gemm_bf16: mt must be 1, 2, 3 (1 + cluster split-K) or 4 (CTA pair)");
   B200_REQUIRE(!pair || plan.bn % 32 == 0, "gemm_bf16: CTA-pair tiles need bn % 32 == 0");
   Params p;
   p.M = M;
@@ -1196,6 +1377,17 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.total_units = p.num_m * p.num_n * p.splits;
   p.err = a.err;
   p.ldc = (int)a.ldc;
+  p.csplit = 1;
+  if (want_cluster && p.splits >= 2 && p.splits <= 4 && cluster_splitk_on() &&
+      (a.mode == kModeStore || a.mode == kModeSiluMul || a.mode == kModeF32)) {
+    const int ring = p.stages * (a_tile_bytes(1) + b_tile_bytes(plan.bn)) * p.katoms;
+    const int smem = ring + kSmemOverhead;
+    const int active = a.mode == kModeStore     ? max_active_clusters<kStore>(p.splits, smem)
+                       : a.mode == kModeSiluMul ? max_active_clusters<kSiluMul>(p.splits, smem)
+                                                : max_active_clusters<kF32>(p.splits, smem);
+    if (csplit_region_bytes(p.splits, plan.bn) <= ring && p.num_m * p.num_n <= active)
+      p.csplit = p.splits;
+  }
 
   const CUtensorMap ta =
       make_tma_2d(const_cast<void*>(a.A), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, a.lda, BK,
@@ -1220,7 +1412,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
       B200_REQUIRE(a.peers[i] != nullptr && reinterpret_cast<uintptr_t>(a.peers[i]) % 16 == 0,
                    "gemm_bf16 scatter: receive slots must be 16-byte aligned");
   }
-  if (p.splits > 1) {
+  if (p.splits > 1 && p.csplit == 1) {
     const int64_t need = (int64_t)p.splits * M * N;
     B200_REQUIRE(a.workspace != nullptr && a.workspace_numel >= need,
                  "gemm_bf16: split-K workspace too small");
@@ -1231,9 +1423,17 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
     p.counters = a.counters;
   }
   // deferred split-K reduction (separate grid): the GEMM only writes partials
-  const bool deferred = p.splits > 1 && (pair || (splitk_reduce_kernel_on() && !transposed));
+  const bool deferred =
+      p.splits > 1 && p.csplit == 1 && (pair || (splitk_reduce_kernel_on() && !transposed));
   if (deferred) p.counters = nullptr;
-  if (pair) {
+  if (p.csplit > 1) {
+    if (a.mode == kModeStore)
+      launch_csplit<kStore>(ta, tb, p, stream);
+    else if (a.mode == kModeSiluMul)
+      launch_csplit<kSiluMul>(ta, tb, p, stream);
+    else
+      launch_csplit<kF32>(ta, tb, p, stream);
+  } else if (pair) {
     if (a.mode == kModeStore)
       launch_pair<kStore>(ta, tb, p, stream);
     else if (a.mode == kModeSiluMul)

@@ -6,8 +6,9 @@ sweep scripts under benchmarks/ and consulted at run time by the kernel wrappers
 
 Table ``gemm_bf16``: {"device": str, "entries": [{"n": N, "k": K, "m": M, "bn": BN,
 "splits": S, "mt": MT, "us": t}, ...]}: the fastest plan measured for each (N, K) at each M
-bucket (BN a multiple of 16 up to 256; MT = 128-row tiles per CTA, or 4 = a 2-CTA cluster on a
-256-row tile with cta_group::2 MMAs).
+bucket (BN a multiple of 16 up to 256; MT = 128-row tiles per CTA (1 or 2), 3 = one 128-row tile
+per CTA with the K splits reduced inside a thread-block cluster through distributed shared
+memory, or 4 = a 2-CTA cluster on a 256-row tile with cta_group::2 MMAs).
 """
 from __future__ import annotations
 
