@@ -37,7 +37,8 @@ def mode_ar(out_path):
     # numerics of every kernel: NVLS two-shot above 64 KiB, peer-to-peer below
     car.NVLS_MIN_BYTES = {w: 64 << 10 for w in (2, 4, 8)}
     car.NVLS_QUANT_MIN_ROWS = {w: 1 for w in (2, 4, 8)}
-    ar = maybe_create_custom_allreduce(st, dev, max_tokens=2048, hidden=H)
+    # up to 4096 rows: at TP=2 the NVLS kernel's warps then walk two rows each (pipelined)
+    ar = maybe_create_custom_allreduce(st, dev, max_tokens=4096, hidden=H)
     assert ar is not None, "custom all-reduce did not initialise"
     errs = []
     g = torch.Generator(device="cpu").manual_seed(123)
@@ -45,7 +46,7 @@ def mode_ar(out_path):
     # (rows, NVLS threshold for this call): NVLS one-shot below `world` rows, two-shot above
     # 64 KiB, peer-to-peer one- / two-shot where the threshold is None or not reached
     cases = [(1, 0), (7, 64 << 10), (32, 64 << 10), (256, 64 << 10), (1000, 64 << 10),
-             (2048, None), (5, None), (1, None), (3, 0)]
+             (2048, None), (5, None), (1, None), (3, 0), (4096, 0)]
     for it, (T, lim) in enumerate(cases):
         car.NVLS_MIN_BYTES = {w: lim for w in (2, 4, 8)}
         ar.begin_forward() if it % 2 == 0 else None
