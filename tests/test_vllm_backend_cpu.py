@@ -114,3 +114,40 @@ def test_platform_selects_backend_and_communicator():
                       importlib.import_module(
                           "vllm.distributed.device_communicators.cuda_communicator"
                       ).CudaCommunicator)
+
+
+def test_quant_fp8_override_matches_vllm_native():
+    """The QuantFP8 OOT class quantises 1x128 groups like vLLM's native path and defers every
+    other configuration to vLLM."""
+    from vllm.config import DeviceConfig, VllmConfig, set_current_vllm_config
+    from vllm.model_executor.layers.quantization.utils.quant_utils import GroupShape
+    from vllm_musa_b200.plugin import make_quant_fp8_class
+    cls = make_quant_fp8_class()
+    with set_current_vllm_config(VllmConfig(device_config=DeviceConfig(device="cpu"))):
+        op = cls(static=False, group_shape=GroupShape(1, 128))
+        per_token = cls(static=False, group_shape=GroupShape.PER_TOKEN)
+    op.use_ue8m0 = False
+    torch.manual_seed(0)
+    x = (torch.randn(5, 512) * 3).to(torch.bfloat16)
+    assert op._b200_serves(x, None)
+    q, s = op.forward_oot(x)
+    qn, sn = op.forward_native(x)
+    torch.testing.assert_close(s.float(), sn.float().reshape(s.shape), rtol=1e-3, atol=1e-6)
+    deq = q.float().view(5, 4, 128) * s.unsqueeze(-1)
+    deqn = qn.float().view(5, 4, 128) * sn.float().reshape(5, 4, 1)
+    assert (deq - deqn).abs().max() <= 0.0625 * x.float().abs().max()
+    assert not per_token._b200_serves(x, None)
+
+
+def test_platform_selects_worker_class():
+    from vllm_musa_b200.platform import B200Platform
+    par = SimpleNamespace(worker_cls="auto")
+    cfg = SimpleNamespace(parallel_config=par, cache_config=None, compilation_config=None)
+    try:
+        B200Platform.check_and_update_config(cfg)
+    except Exception:
+        pass  # vLLM's own checks need a full config; the worker choice happens first
+    assert par.worker_cls == "vllm_musa_b200.vllm_worker.B200Worker"
+    from vllm.v1.worker.gpu_worker import Worker
+    from vllm_musa_b200.vllm_worker import B200Worker
+    assert issubclass(B200Worker, Worker)

@@ -4,7 +4,8 @@ Subclasses vLLM's NVML CUDA platform and changes what the reference's MUSAPlatfo
 its device (vllm_musa/platform.py:245-955): default KV block size 64 (one TMA box per page),
 the b200 IR-op providers first in priority, custom ops enabled, this package's attention
 backend (vllm_backend.py) and device communicator (vllm_comm.py: NVSwitch all-reduce), the
-post-grad fusion passes, a device-architecture check at worker start.
+post-grad fusion passes, and its worker (vllm_worker.py: device-architecture check and op
+preloading at worker start).
 """
 from __future__ import annotations
 
@@ -29,8 +30,13 @@ class B200Platform(_Base):
         except Exception:
             return "NVIDIA B200"
 
+    worker_cls: str = "vllm_musa_b200.vllm_worker.B200Worker"
+
     @classmethod
     def check_and_update_config(cls, vllm_config) -> None:
+        par = getattr(vllm_config, "parallel_config", None)
+        if par is not None and getattr(par, "worker_cls", None) == "auto":
+            par.worker_cls = cls.worker_cls
         if hasattr(super(), "check_and_update_config"):
             super().check_and_update_config(vllm_config)  # type: ignore[misc]
         cache = getattr(vllm_config, "cache_config", None)

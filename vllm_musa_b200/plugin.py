@@ -4,7 +4,7 @@
 an sm_100 device is present; ``register_custom_ops`` (group ``vllm.general_plugins``) registers
 this package's kernels with vLLM:
   * IR-op providers ``b200`` for ``rms_norm`` / ``fused_add_rms_norm`` (vllm.ir),
-  * CustomOp out-of-tree overrides for ``SiluAndMul`` and ``RotaryEmbedding``.
+  * CustomOp out-of-tree overrides for ``SiluAndMul``, ``RotaryEmbedding`` and ``QuantFP8``.
 Reference counterparts: vllm_musa/__init__.py:52-193 (musa_platform_plugin,
 register_custom_ops), vllm_musa/kernels/musa_ops.py:66-241 (IR providers),
 vllm_musa/model_executor/layers/activation.py:11-53, rotary_embedding/base.py:8-35.
@@ -104,6 +104,37 @@ def make_custom_op_classes():
     return B200SiluAndMul, B200RotaryEmbedding
 
 
+def make_quant_fp8_class():
+    """OOT subclass of vLLM's QuantFP8: dynamic per-token 1x128 e4m3 group quantisation of bf16
+    activations (row-major fp32 scales, amax / 448) on the b200 group-quant kernel; every other
+    configuration (static scales, per-tensor / per-token, column-major or TMA-aligned or UE8M0
+    scales) stays on vLLM's path.  Reference counterpart: vllm_musa/model_executor/layers/
+    quantization/input_quant_fp8.py (the QuantFP8 OOT override over the MUSA group-quant op)."""
+    import torch
+    from vllm.model_executor.layers.quantization.input_quant_fp8 import QuantFP8
+
+    from . import ops
+
+    use_native = envs.get("B200_CUSTOM_OP_USE_NATIVE")
+
+    class B200QuantFP8(QuantFP8):
+        def _b200_serves(self, x, scale) -> bool:
+            return (not use_native and self.is_group_quant and not self.static and
+                    scale is None and getattr(self, "group_size", 0) == 128 and
+                    not self.column_major_scales and not self.tma_aligned_scales and
+                    not self.use_ue8m0 and x.dtype == torch.bfloat16 and x.dim() == 2 and
+                    x.shape[-1] % 128 == 0 and x.is_contiguous())
+
+        def forward_oot(self, x, scale=None, scale_ub=None, use_triton=False):
+            if self._b200_serves(x, scale):
+                return ops.activation.group_quant_fp8(x)
+            if x.is_cuda:
+                return self.forward_cuda(x, scale, scale_ub, use_triton)
+            return self.forward_native(x, scale, scale_ub, use_triton)
+
+    return B200QuantFP8
+
+
 # Modules that register torch.ops.b200.* and the IR providers; they must be imported before
 # vLLM traces or compiles a model so the ops exist in every process (workers included).
 # Reference counterpart: vllm_musa/custom_op_modules.py:5-27.
@@ -135,4 +166,8 @@ def register_custom_ops() -> None:
     silu, rope = make_custom_op_classes()
     CustomOp.register_oot(silu, name="SiluAndMul")
     CustomOp.register_oot(rope, name="RotaryEmbedding")
+    try:
+        CustomOp.register_oot(make_quant_fp8_class(), name="QuantFP8")
+    except Exception as e:  # an older vLLM without QuantFP8
+        log.info("QuantFP8 override not registered: %s", e)
     _REGISTERED = True
