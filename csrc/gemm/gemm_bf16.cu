@@ -74,7 +74,6 @@ struct Params {
   int num_m, num_n, num_kb, splits, kb_per_split;
   int katoms;  // 64-element K atoms per pipeline stage (one TMA box per operand and atom)
   int csplit;  // > 1: split-K over a cluster of csplit CTAs reduced through distributed smem
-  int ctas_per_sm;  // 2: half-size rings so two CTAs (two producer / MMA pipelines) share an SM
   int total_units;
   void* C;  // output (bf16 or fp32) or fp32 workspace for split-K
   int ldc;  // elements
@@ -277,7 +276,7 @@ B200_DEVICE void csplit_reduce(const Params& p, uint8_t* smem, uint32_t tmem_bas
 }
 
 template <int MT, int EPI, bool GROUPED = false>
-__global__ void __launch_bounds__(kThreads, MT == 1 ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, Params p) {
   // Programmatic dependent launch: let the next kernel in the stream start its prologue as
@@ -1074,7 +1073,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   ensure_dynamic_smem(reinterpret_cast<const void*>(kern), kSmemBudget);
   const int smem = p.stages * (a_tile_bytes(MT) + b_tile_bytes(p.bn)) * p.katoms +
                    kSmemOverhead + (EPI == kScatter || kTransposed<EPI> ? kScatterBytes : 0);
-  const int grid = std::min(p.total_units, num_sms() * p.ctas_per_sm);
+  const int grid = std::min(p.total_units, num_sms());
   launch_pdl(kern, grid, smem, stream, ta, tb, p);
   count_launch();
 }
@@ -1254,7 +1253,6 @@ void run_grouped_bf16(const GroupedGemmArgs& a, cudaStream_t stream) {
   p.K = K;
   p.bn = bn;
   p.csplit = 1;
-  p.ctas_per_sm = 1;
   {
     const int stage1 = a_tile_bytes(1) + b_tile_bytes(bn);
     const int budget = kSmemBudget - kSmemOverhead;
@@ -1326,10 +1324,7 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.bn > 0) plan.bn = a.bn;
   if (a.splits > 0) plan.splits = a.splits;
   if (a.mt > 0) plan.mt = a.mt;
-  // mt bit 3 (8): two CTAs per SM on half-size rings (one-CTA tiles); mt & 7 = 3: one-CTA
-  // tiles (mt 1) with the K splits reduced inside a cluster
-  const bool two_per_sm = (plan.mt & 8) != 0;
-  plan.mt &= 7;
+  // mt = 3: one-CTA tiles (mt 1) with the K splits reduced inside a cluster
   const bool want_cluster = plan.mt == 3;
   if (want_cluster) plan.mt = 1;
   // CTA pairs (mt = 4): 256-row tiles; chosen automatically for large M (no split-K)
@@ -1359,23 +1354,18 @@ void run_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.N = N;
   p.K = K;
   p.bn = plan.bn;
-  p.ctas_per_sm = two_per_sm && !pair && plan.mt == 1 ? 2 : 1;
   {
     const int stage1 = pair ? BM * BK * 2 + (plan.bn / 2) * BK * 2
                             : a_tile_bytes(plan.mt) + b_tile_bytes(plan.bn);
-    // room for the epilogue's shared-memory staging (scatter / transposed stores); two CTAs
-    // per SM split the SM's shared memory
-    const int budget = (p.ctas_per_sm == 2 ? kSmemBudget / 2 - 1024 : kSmemBudget) -
-                       kSmemOverhead -
+    // room for the epilogue's shared-memory staging (scatter / transposed stores)
+    const int budget = kSmemBudget - kSmemOverhead -
                        (a.mode == kModeScatter || transposed ? kScatterBytes : 0);
     p.katoms = choose_katoms(stage1, K, std::max(1, plan.splits), budget);
     p.stages = std::min(kMaxStages, budget / (stage1 * p.katoms));
   }
   const int acc_cols = plan.mt * plan.bn;
-  // TMEM: 512 columns per SM, shared by the CTAs on it
-  p.acc_bufs = 2 * acc_cols <= 512 / p.ctas_per_sm ? 2 : 1;
-  B200_REQUIRE(p.stages >= 1 && acc_cols <= 512 / p.ctas_per_sm,
-               "gemm_bf16: the tile does not fit the shared memory / TMEM of its CTA");
+  p.acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
+  B200_REQUIRE(p.stages >= 1, "gemm_bf16: the tile does not fit the shared memory of its CTA");
   int cols = 32;
   while (cols < p.acc_bufs * acc_cols) cols <<= 1;
   p.tmem_cols = cols;
