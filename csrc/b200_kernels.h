@@ -465,6 +465,8 @@ void run_topk_exchange(const TopkExchangeArgs& a, cudaStream_t s);
 // vocab shard starting at vocab_offset.  entries [n, 3] int32 = (row, global token id, count of
 // the token in the row's output so far); every listed token occurs in the prompt or the
 // output (rows list each token once).
+void run_token_bitmask(float* logits, int64_t ld, const int32_t* bitmask, int words,
+                       const int32_t* rows, int R, int V_local, int vocab_offset, cudaStream_t s);
 void run_apply_penalties(float* logits, int64_t ld, int V_local, int vocab_offset,
                          const int32_t* entries, int n, const float* rep, const float* pres,
                          const float* freq, cudaStream_t s);

@@ -17,6 +17,7 @@
 // Reference counterparts: csrc/musa/sampler.mu:124 (top-k/top-p sampling from probs),
 // csrc/musa/top_k_mask_logits.mu:91 and top_p_mask_logits.mu:149 (radix select on logits),
 // csrc/musa/min_p_sampler.mu:98-207 (min-p), vllm_musa/v1/sample/topk_topp_sampler.py:351.
+#include <algorithm>
 #include "../b200_kernels.h"
 #include "../common/common.cuh"
 #include "sampling_common.cuh"
@@ -188,6 +189,34 @@ void run_apply_penalties(float* logits, int64_t ld, int V_local, int vocab_offse
   if (n == 0) return;
   apply_penalties_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, ld, V_local, vocab_offset,
                                                          entries, n, rep, pres, freq);
+  B200_CUDA_OK(cudaGetLastError());
+  count_launch();
+}
+
+// Constrained decoding: logits[rows[r]][j] = -inf where bit (vocab_offset + j) of bitmask row r
+// is clear (bit t of 32-bit word t / 32 allows token t; tokens past the bitmask are masked).
+__global__ void token_bitmask_kernel(float* __restrict__ logits, int64_t ld,
+                                     const int32_t* __restrict__ bitmask, int words,
+                                     const int32_t* __restrict__ rows, int V_local,
+                                     int vocab_offset) {
+  const int r = blockIdx.y;
+  const int row = rows[r];
+  const int32_t* bm = bitmask + (int64_t)r * words;
+  float* out = logits + (int64_t)row * ld;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < V_local; j += gridDim.x * blockDim.x) {
+    const int t = vocab_offset + j;
+    const int w = t >> 5;
+    if (w >= words || ((bm[w] >> (t & 31)) & 1) == 0) out[j] = -INFINITY;
+  }
+}
+
+void run_token_bitmask(float* logits, int64_t ld, const int32_t* bitmask, int words,
+                       const int32_t* rows, int R, int V_local, int vocab_offset,
+                       cudaStream_t s) {
+  if (R == 0 || V_local == 0) return;
+  const dim3 grid(std::min(64, (V_local + 1023) / 1024), R);
+  token_bitmask_kernel<<<grid, 256, 0, s>>>(logits, ld, bitmask, words, rows, V_local,
+                                            vocab_offset);
   B200_CUDA_OK(cudaGetLastError());
   count_launch();
 }

@@ -852,6 +852,27 @@ void apply_penalties(Tensor& logits, const Tensor& entries, const Tensor& rep, c
   });
 }
 
+void apply_token_bitmask(Tensor& logits, const Tensor& bitmask, const Tensor& rows,
+                         int64_t vocab_offset) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "apply_token_bitmask: fp32 [S, V] logits");
+  TORCH_CHECK(bitmask.scalar_type() == at::kInt && bitmask.dim() == 2 && bitmask.is_contiguous(),
+              "apply_token_bitmask: int32 [R, words] bitmask");
+  TORCH_CHECK(rows.scalar_type() == at::kInt && rows.is_contiguous() &&
+                  rows.numel() == bitmask.size(0),
+              "apply_token_bitmask: int32 [R] logits rows");
+  TORCH_CHECK(bitmask.device() == logits.device() && rows.device() == logits.device(),
+              "apply_token_bitmask: tensors on the logits' device");
+  const c10::cuda::CUDAGuard g(logits.device());
+  guarded([&] {
+    b200::sampling::run_token_bitmask(logits.data_ptr<float>(), logits.stride(0),
+                                      bitmask.data_ptr<int32_t>(), bitmask.size(1),
+                                      rows.data_ptr<int32_t>(), rows.numel(), logits.size(1),
+                                      vocab_offset, stream_of(logits));
+  });
+}
+
 // ------------------------------------------------------------------------------------- misc
 void embedding(Tensor& out, const Tensor& table, const Tensor& ids, int64_t vocab_start) {
   CHECK_CUDA(table);
@@ -1558,6 +1579,8 @@ TORCH_LIBRARY(b200, m) {
   m.def("merge_candidates(Tensor vals, Tensor idx, Tensor(a!) out) -> ()");
   m.def("apply_penalties(Tensor(a!) logits, Tensor entries, Tensor rep, Tensor pres, Tensor freq, "
         "int vocab_offset) -> ()");
+  m.def("apply_token_bitmask(Tensor(a!) logits, Tensor bitmask, Tensor rows, int vocab_offset) "
+        "-> ()");
   m.def("embedding(Tensor(a!) out, Tensor table, Tensor ids, int vocab_start=0) -> ()");
   m.def("gather_rows(Tensor(a!) out, Tensor x, Tensor idx) -> ()");
   m.def(
@@ -1632,6 +1655,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("merge_candidates", &merge_candidates);
   m.impl("kv_insert", &kv_insert);
   m.impl("apply_penalties", &apply_penalties);
+  m.impl("apply_token_bitmask", &apply_token_bitmask);
   m.impl("embedding", &embedding);
   m.impl("gather_rows", &gather_rows);
   m.impl("gemm_grouped_bf16", &gemm_grouped_bf16);

@@ -85,3 +85,40 @@ def test_topk_candidates_merge_matches_full_vocab_sampler():
         ((k == 0) & (top_p.cpu() == 1.0) & (min_p.cpu() == 0.0))
     assert bool(decided.cpu()[must].all()), (out.cpu()[must], must.nonzero())
     assert decided.float().mean() > 0.6
+
+
+def test_token_bitmask_kernel_matches_reference():
+    """The constrained-decoding mask kernel against the PyTorch bit test, including a vocab
+    shard at an offset and tokens past the bitmask."""
+    import torch
+    from vllm_musa_b200.ops.sampling import apply_token_bitmask
+    g = torch.Generator().manual_seed(3)
+    logits = torch.randn(6, 5000, generator=g)
+    bm = torch.randint(-2**31, 2**31 - 1, (3, 150), generator=g, dtype=torch.int64).to(torch.int32)
+    rows = torch.tensor([5, 0, 2], dtype=torch.int32)
+    for off in (0, 96):
+        want = apply_token_bitmask(logits[:, off:].clone(), bm, rows, vocab_offset=off)
+        got = apply_token_bitmask(logits[:, off:].clone().cuda(), bm.cuda(), rows.cuda(),
+                                  vocab_offset=off)
+        assert torch.equal(got.cpu(), want)
+
+
+def test_structured_outputs_on_gpu():
+    import json
+    import os
+    import sys
+    import torch
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_structured_outputs_cpu import SCHEMA, CharTokenizer, _cfg
+    from vllm_musa_b200 import LLM, SamplingParams
+    cfg = _cfg()
+    cfg.dtype = torch.bfloat16
+    llm = LLM(cfg, tokenizer=CharTokenizer(), block_size=64, seed=0, num_gpu_blocks=64,
+              max_model_len=512, max_num_seqs=8, max_num_batched_tokens=256)
+    sps = [SamplingParams(temperature=0.9, seed=3 + i, max_tokens=120, structured_outputs=so)
+           for i, so in enumerate([{"json": SCHEMA, "disable_any_whitespace": True},
+                                   {"choice": ["yes", "no"]}])]
+    outs = llm.generate([[5, 6, 7], [8, 9, 10]], sps)
+    obj = json.loads(outs[0].outputs[0].text)
+    assert obj["color"] in ("red", "green") and isinstance(obj["ok"], bool)
+    assert outs[1].outputs[0].text in ("yes", "no")

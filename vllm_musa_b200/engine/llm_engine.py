@@ -50,6 +50,7 @@ class _Req:
     first_token_time: Optional[float] = None
     logprobs: Optional[list] = None       # per generated token {id: Logprob} (if requested)
     cum_logprob: float = 0.0
+    matcher: Optional[object] = None      # structured outputs: the request's grammar matcher
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -205,18 +206,35 @@ class LLMEngine:
         sp.top_p = params.top_p
         sp.min_p = params.min_p
         sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
-        special = params.has_penalties or params.logprobs is not None
+        so = params.structured_outputs
+        special = params.has_penalties or params.logprobs is not None or so is not None
         if special and self.config.speculative.method is not None and \
                 self.config.speculative.num_speculative_tokens:
-            raise ValueError("penalties / logprobs are not served with speculative decoding")
+            raise ValueError("penalties / logprobs / structured outputs are not served with "
+                             "speculative decoding")
+        matcher = self._grammar_backend().matcher(so) if so is not None else None
         self.scheduler.add_request(iid, list(map(int, prompt_ids)), sp)
         r = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
         if params.logprobs is not None:
             r.logprobs = []
+        r.matcher = matcher
         self._reqs[iid] = r
         self._by_name[name] = iid
         if special:
             self._special[iid] = r
+
+    def _grammar_backend(self):
+        """Structured-output grammar compiler over the model's vocabulary (created on the first
+        constrained request; needs the tokenizer)."""
+        if getattr(self, "_grammar", None) is None:
+            from ..sample.structured import GrammarBackend
+            tok = self.tokenizer
+            if tok is None and self.config.model_path:
+                from ..entrypoints.llm import _load_tokenizer
+                tok = self.tokenizer = _load_tokenizer(self.config.model_path)
+            self._grammar = GrammarBackend(tok, self.config.model.vocab_size,
+                                           self.config.model.eos_token_id)
+        return self._grammar
 
     def abort_request(self, request_id: str) -> None:
         if self.sync is not None and self.role == "driver":
@@ -266,6 +284,8 @@ class LLMEngine:
         sampled = self.runner.execute(plan, extras)
         if extras is not None and extras.logprobs is not None:
             self._record_logprobs(plan, extras, sampled)
+        if extras is not None and extras.mask_rows:
+            self._advance_grammars(plan, extras, sampled)
         finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
         now = time.time()
         self.step_end_times.append(now)
@@ -301,6 +321,7 @@ class LLMEngine:
         from ..ops.sampling import penalty_entries
         from .model_runner import StepExtras
         rows_tok, lp_rows, k = [], [], 0
+        mask_rows, matchers = [], []
         S = plan.num_samples
         rep = torch.ones(S)
         pres = torch.zeros(S)
@@ -310,6 +331,9 @@ class LLMEngine:
             if r is None:
                 continue
             p = r.params
+            if r.matcher is not None:
+                mask_rows.append(row)
+                matchers.append(r.matcher)
             if p.has_penalties:
                 n = self.scheduler.num_tokens(iid)
                 toks = self.scheduler.tokens_range(iid, 0, n)
@@ -320,10 +344,21 @@ class LLMEngine:
             if p.logprobs is not None:
                 lp_rows.append(row)
                 k = max(k, p.logprobs)
-        if not rows_tok and not lp_rows:
+        if not rows_tok and not lp_rows and not mask_rows:
             return None
         entries = penalty_entries(rows_tok) if rows_tok else None
-        return StepExtras(entries, rep, pres, freq, lp_rows, k)
+        bitmask = self._grammar_backend().bitmask(matchers) if matchers else None
+        return StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
+
+    def _advance_grammars(self, plan, extras, sampled) -> None:
+        """Feed each constrained request's sampled token to its matcher."""
+        for row in extras.mask_rows:
+            r = self._reqs.get(plan.sample_req_ids[row])
+            if r is None or r.matcher is None:
+                continue
+            tok = int(sampled[row])
+            if not r.matcher.is_terminated() and not r.matcher.accept_token(tok):
+                log.warning("request %s: token %d rejected by its grammar", r.request_id, tok)
 
     def _record_logprobs(self, plan, extras, sampled) -> None:
         from ..outputs import Logprob

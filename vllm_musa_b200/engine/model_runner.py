@@ -93,13 +93,17 @@ class StepBuffers:
 
 class StepExtras:
     """Per-step logits processing beyond sampling, for the rows whose requests ask for it:
-    penalty entries (ops.sampling.penalty_entries) with per-row penalties, and the rows whose
-    raw-logit log-probabilities are returned (top ``lp_k`` per row)."""
+    penalty entries (ops.sampling.penalty_entries) with per-row penalties, the rows whose
+    raw-logit log-probabilities are returned (top ``lp_k`` per row), and the constrained rows
+    with their next-token bitmasks (int32 [len(mask_rows), words], structured outputs)."""
 
-    def __init__(self, entries=None, rep=None, pres=None, freq=None, lp_rows=None, lp_k=0):
+    def __init__(self, entries=None, rep=None, pres=None, freq=None, lp_rows=None, lp_k=0,
+                 bitmask=None, mask_rows=None):
         self.entries, self.rep, self.pres, self.freq = entries, rep, pres, freq
         self.lp_rows = lp_rows or []
         self.lp_k = lp_k
+        self.bitmask = bitmask
+        self.mask_rows = mask_rows or []
         self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
 
 
@@ -248,6 +252,12 @@ class ModelRunner:
                 dev = logits.device
                 ops.apply_penalties(logits, ex.entries.to(dev), ex.rep.to(dev), ex.pres.to(dev),
                                     ex.freq.to(dev), getattr(self.model, "vocab_start", 0))
+            if ex.mask_rows:
+                dev = logits.device
+                ops.sampling.apply_token_bitmask(
+                    logits, ex.bitmask.to(dev),
+                    torch.tensor(ex.mask_rows, dtype=_I32, device=dev),
+                    getattr(self.model, "vocab_start", 0))
         if sampling:
             ids = self.sampler(logits, b.d["temperature"][:S], b.d["top_k"][:S],
                                b.d["top_p"][:S], b.d["min_p"][:S], b.d["seeds"][:S],

@@ -28,8 +28,31 @@ class _Sampling(BaseModel):
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
     repetition_penalty: float = 1.0
+    # structured outputs: vLLM's extra parameters and the OpenAI response_format
+    structured_outputs: Optional[Dict] = None
+    guided_json: Optional[Union[Dict, str]] = None
+    guided_regex: Optional[str] = None
+    guided_choice: Optional[List[str]] = None
+    guided_grammar: Optional[str] = None
+    response_format: Optional[Dict] = None
 
     def num_logprobs(self) -> Optional[int]:
+        return None
+
+    def structured(self) -> Optional[Dict]:
+        """The request's constraint as StructuredOutputsParams fields (None: unconstrained)."""
+        if self.structured_outputs:
+            return dict(self.structured_outputs)
+        for key, val in (("json", self.guided_json), ("regex", self.guided_regex),
+                         ("choice", self.guided_choice), ("grammar", self.guided_grammar)):
+            if val is not None:
+                return {key: val}
+        rf = self.response_format or {}
+        if rf.get("type") == "json_object":
+            return {"json_object": True}
+        if rf.get("type") == "json_schema":
+            js = rf.get("json_schema") or {}
+            return {"json": js.get("schema", js)}
         return None
 
     def sampling_params(self, default_max: int) -> SamplingParams:
@@ -43,7 +66,8 @@ class _Sampling(BaseModel):
                               presence_penalty=self.presence_penalty,
                               frequency_penalty=self.frequency_penalty,
                               repetition_penalty=self.repetition_penalty,
-                              logprobs=self.num_logprobs())
+                              logprobs=self.num_logprobs(),
+                              structured_outputs=self.structured())
 
 
 class CompletionRequest(_Sampling):

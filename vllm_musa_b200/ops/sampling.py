@@ -133,6 +133,28 @@ def apply_penalties(logits: torch.Tensor, entries: torch.Tensor, rep: torch.Tens
     return logits
 
 
+def apply_token_bitmask(logits: torch.Tensor, bitmask: torch.Tensor, rows: torch.Tensor,
+                        vocab_offset: int = 0) -> torch.Tensor:
+    """Constrained decoding, in place: logits row ``rows[r]`` (fp32 [S, V] of the vocab shard at
+    ``vocab_offset``) keeps token t only where bit t % 32 of ``bitmask[r, t // 32]`` (int32) is
+    set; the rest become -inf."""
+    if rows.numel() == 0:
+        return logits
+    if logits.is_cuda:
+        _ext.ops().apply_token_bitmask(logits, bitmask.contiguous(), rows.contiguous(),
+                                       vocab_offset)
+        return logits
+    V = logits.shape[1]
+    t = torch.arange(vocab_offset, vocab_offset + V)
+    words = bitmask.shape[1]
+    w = (t >> 5).clamp(max=words - 1)
+    bits = (bitmask[:, w] >> (t & 31)) & 1
+    allowed = (bits == 1) & (t < words * 32)
+    for r, row in enumerate(rows.tolist()):
+        logits[row].masked_fill_(~allowed[r], float("-inf"))
+    return logits
+
+
 def penalty_entries(rows_tokens) -> torch.Tensor:
     """[(row, prompt token ids, output token ids)] -> int32 [n, 3] (row, token, output count)
     with every token of the prompt and output listed once per row."""

@@ -2,7 +2,39 @@
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import List, Optional
+from typing import Any, List, Optional, Union
+
+
+@dataclass
+class StructuredOutputsParams:
+    """Constrained decoding (vLLM's ``StructuredOutputsParams``): exactly one of a JSON schema
+    (dict or JSON text), ``json_object`` (any JSON object), a regular expression, a list of
+    choices or an EBNF grammar.  Generated tokens always keep the output a prefix of a valid
+    string; the request stops at the end of the structure."""
+    json: Optional[Union[dict, str]] = None
+    json_object: bool = False
+    regex: Optional[str] = None
+    choice: Optional[List[str]] = None
+    grammar: Optional[str] = None
+    # JSON without free whitespace between tokens (compact separators)
+    disable_any_whitespace: bool = False
+
+    def __post_init__(self):
+        given = [self.json is not None, bool(self.json_object), self.regex is not None,
+                 self.choice is not None, self.grammar is not None]
+        if sum(given) != 1:
+            raise ValueError("structured outputs: give exactly one of json, json_object, regex, "
+                             "choice, grammar")
+        if self.choice is not None and not self.choice:
+            raise ValueError("structured outputs: choice needs at least one string")
+
+    def key(self) -> tuple:
+        import json as _json
+        j = self.json if self.json is None or isinstance(self.json, str) else \
+            _json.dumps(self.json, sort_keys=True)
+        return (j, self.json_object, self.regex,
+                None if self.choice is None else tuple(self.choice), self.grammar,
+                self.disable_any_whitespace)
 
 
 @dataclass
@@ -28,8 +60,12 @@ class SamplingParams:
     # (plus the generated token's own), computed from the raw logits as vLLM's default
     # logprobs mode; None = no log-probabilities
     logprobs: Optional[int] = None
+    # constrained decoding (JSON schema / regex / choice / grammar); a dict is accepted too
+    structured_outputs: Optional[Any] = None
 
     def __post_init__(self):
+        if isinstance(self.structured_outputs, dict):
+            self.structured_outputs = StructuredOutputsParams(**self.structured_outputs)
         if self.top_k is None or self.top_k < 0:
             self.top_k = 0
         if self.temperature < 0:
