@@ -132,3 +132,21 @@ def test_structured_outputs_tp2():
         assert p.exitcode == 0
     assert res[0] == res[1], "ranks diverged"
     _check(*res[0])
+
+
+def test_stop_strings():
+    """A stop string ends the request as soon as the output text contains it; the text is cut
+    before it (or keeps it with include_stop_str_in_output), finish_reason "stop"."""
+    llm = _llm()
+    prompt = [[7, 30, 44, 2]]
+    free = llm.generate(prompt, SamplingParams(temperature=0.0, max_tokens=30, ignore_eos=True))
+    text = free[0].outputs[0].text
+    stop = text[5:7]
+    at = text.find(stop)
+    out = llm.generate(prompt, SamplingParams(temperature=0.0, max_tokens=30, ignore_eos=True,
+                                              stop=[stop, "\x00never"]))[0].outputs[0]
+    assert out.text == text[:at] and out.finish_reason == "stop" and out.stop_reason == stop
+    assert len(out.token_ids) < 30
+    kept = llm.generate(prompt, SamplingParams(temperature=0.0, max_tokens=30, ignore_eos=True,
+                                               stop=stop, include_stop_str_in_output=True))
+    assert kept[0].outputs[0].text == text[:at + len(stop)]

@@ -51,6 +51,7 @@ class _Req:
     logprobs: Optional[list] = None       # per generated token {id: Logprob} (if requested)
     cum_logprob: float = 0.0
     matcher: Optional[object] = None      # structured outputs: the request's grammar matcher
+    stop_hit: Optional[tuple] = None      # (stop string, text up to it) once one matched
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -207,7 +208,10 @@ class LLMEngine:
         sp.min_p = params.min_p
         sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
         so = params.structured_outputs
-        special = params.has_penalties or params.logprobs is not None or so is not None
+        if params.stop and self.tokenizer is None:
+            raise ValueError("stop strings need the model's tokenizer")
+        special = params.has_penalties or params.logprobs is not None or so is not None or \
+            bool(params.stop)
         if special and self.config.speculative.method is not None and \
                 self.config.speculative.num_speculative_tokens:
             raise ValueError("penalties / logprobs / structured outputs are not served with "
@@ -287,6 +291,8 @@ class LLMEngine:
         if extras is not None and extras.mask_rows:
             self._advance_grammars(plan, extras, sampled)
         finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
+        if self._special:
+            finished = self._match_stop_strings(plan, finished)
         now = time.time()
         self.step_end_times.append(now)
         self.num_steps += 1
@@ -350,6 +356,29 @@ class LLMEngine:
         bitmask = self._grammar_backend().bitmask(matchers) if matchers else None
         return StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
 
+    def _match_stop_strings(self, plan, finished):
+        """Finish (reason "stop") every request whose output text now contains one of its stop
+        strings; its text is cut before the string (kept with include_stop_str_in_output).
+        Every rank decides the same: the tokens are lock-step."""
+        done = {iid for iid, _ in finished}
+        extra = []
+        for iid in plan.sample_req_ids:
+            r = self._special.get(iid)
+            if r is None or not r.params.stop or iid in done:
+                continue
+            text = self.tokenizer.decode(list(self.scheduler.output_tokens(iid)),
+                                         skip_special_tokens=True)
+            # the newest token can complete a stop string that starts up to len - 1 chars back
+            hits = [(text.find(s), s) for s in r.params.stop if s in text]
+            if not hits:
+                continue
+            at, s = min(hits)
+            keep = at + len(s) if r.params.include_stop_str_in_output else at
+            r.stop_hit = (s, text[:keep])
+            self.scheduler.abort_request(iid)
+            extra.append((iid, 2))  # reason code 2 = "stop"
+        return list(finished) + extra
+
     def _advance_grammars(self, plan, extras, sampled) -> None:
         """Feed each constrained request's sampled token to its matcher."""
         for row in extras.mask_rows:
@@ -412,9 +441,13 @@ class LLMEngine:
                 text = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
             except Exception:  # pragma: no cover - tokenizer specific
                 text = ""
+        stop_reason = None
+        if r.stop_hit is not None:
+            stop_reason, text = r.stop_hit
         comp = CompletionOutput(r.index, list(r.tokens), text, reason,
                                 cumulative_logprob=r.cum_logprob if r.logprobs is not None else None,
-                                logprobs=list(r.logprobs) if r.logprobs is not None else None)
+                                logprobs=list(r.logprobs) if r.logprobs is not None else None,
+                                stop_reason=stop_reason)
         m = RequestMetrics(r.arrival, first if first is not None else r.first_token_time, last)
         return RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
 

@@ -22,6 +22,8 @@ class CompletionOutput:
     cumulative_logprob: Optional[float] = None
     # per generated token: {token id: Logprob} for the top-k tokens and the generated one
     logprobs: Optional[List[Dict[int, Logprob]]] = None
+    # the stop string that ended the request (finish_reason "stop"), if one did
+    stop_reason: Optional[str] = None
 
 
 @dataclass

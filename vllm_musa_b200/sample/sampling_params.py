@@ -49,6 +49,8 @@ class SamplingParams:
     min_tokens: int = 0
     stop_token_ids: List[int] = field(default_factory=list)
     stop: List[str] = field(default_factory=list)
+    # keep the matched stop string at the end of the returned text (vLLM: excluded)
+    include_stop_str_in_output: bool = False
     ignore_eos: bool = False
     detokenize: bool = True
     # vLLM's logits processors: repetition (> 1 discourages tokens of the prompt and the
@@ -84,6 +86,9 @@ class SamplingParams:
             raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
         if self.logprobs is not None and not 0 <= self.logprobs <= 20:
             raise ValueError("logprobs must be in [0, 20]")
+        if isinstance(self.stop, str):
+            self.stop = [self.stop]
+        self.stop = [x for x in self.stop if x]
         if self.temperature < 1e-5:
             self.temperature = 0.0  # greedy
 
