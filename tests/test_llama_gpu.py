@@ -66,3 +66,46 @@ def test_llama_graph_decode_matches_eager():
         res[eager] = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
         llm.shutdown()
     assert res[True] == res[False]
+
+
+def test_lora_on_gpu_tracks_merged_reference(tmp_path):
+    """Two adapters and the base model in one batch on B200 (adapter deltas through this
+    package's GEMMs): teacher-forced against the fp32 reference on merged weights, every
+    greedy token is the argmax up to bf16 resolution."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_lora_cpu import make_adapter, merged_reference
+    from vllm_musa_b200 import LLM, SamplingParams
+    from vllm_musa_b200.lora import LoRARequest
+    from vllm_musa_b200.models.reference import ReferenceDecoder
+    from vllm_musa_b200.models.weights import dummy_weights
+    cfg = _tiny()
+    ref_cfg = _tiny()
+    ref_cfg.dtype = torch.float32
+    ta = make_adapter(str(tmp_path / "a"), ref_cfg, 8, 16, 1)
+    tb = make_adapter(str(tmp_path / "b"), ref_cfg, 4, 4, 2)
+    W = {k: v.cpu() for k, v in dummy_weights(ref_cfg, seed=0, std=0.02, device="cuda")}
+
+    def merged(t, r, alpha):
+        w = dict(W)
+        for name, a in t.items():
+            if name.endswith("lora_A.weight"):
+                b = t[name.replace("lora_A", "lora_B")]
+                key = name.replace("base_model.model.", "").replace(".lora_A.weight", ".weight")
+                w[key] = w[key] + (alpha / r) * b @ a
+        return ReferenceDecoder(ref_cfg, w)
+    refs = [merged(ta, 8, 16), merged(tb, 4, 4), ReferenceDecoder(ref_cfg, W)]
+    loras = [LoRARequest("a", 1, str(tmp_path / "a")), LoRARequest("b", 2, str(tmp_path / "b")),
+             None]
+    g = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (30, 70, 12)]
+    llm = LLM(cfg, block_size=64, seed=0, num_gpu_blocks=64, max_model_len=512, max_num_seqs=8,
+              max_num_batched_tokens=256, enable_lora=True, max_loras=2, max_lora_rank=16)
+    outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True),
+                        lora_request=loras)
+    for ref, p, o in zip(refs, prompts, outs):
+        toks = o.outputs[0].token_ids
+        for k, t in enumerate(toks):
+            want = ref.logits(p + toks[:k])[-1]
+            assert float(want.max() - want[t]) / float(want.abs().max()) < 0.03, k

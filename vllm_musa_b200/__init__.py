@@ -12,8 +12,9 @@ from __future__ import annotations
 
 __version__ = "0.1.0"
 
-__all__ = ["LLM", "LLMEngine", "SamplingParams", "EngineConfig", "ModelConfig",
-           "b200_platform_plugin", "register_custom_ops", "__version__"]
+__all__ = ["LLM", "LLMEngine", "SamplingParams", "StructuredOutputsParams", "LoRARequest",
+           "EngineConfig", "ModelConfig", "b200_platform_plugin", "register_custom_ops",
+           "__version__"]
 
 
 def __getattr__(name):
@@ -23,9 +24,12 @@ def __getattr__(name):
     if name == "LLMEngine":
         from .engine.llm_engine import LLMEngine
         return LLMEngine
-    if name == "SamplingParams":
-        from .sample.sampling_params import SamplingParams
-        return SamplingParams
+    if name in ("SamplingParams", "StructuredOutputsParams"):
+        from .sample import sampling_params
+        return getattr(sampling_params, name)
+    if name == "LoRARequest":
+        from .lora import LoRARequest
+        return LoRARequest
     if name in ("EngineConfig", "ModelConfig"):
         from . import config
         return getattr(config, name)

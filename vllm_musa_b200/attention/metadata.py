@@ -29,6 +29,7 @@ class AttnMetadata:
     tile_scratch: Optional[torch.Tensor] = None
     sliding_window: int = 0
     state_slots: Optional[torch.Tensor] = None  # int32 [R] recurrent-state slot per request
+    lora: Optional[object] = None  # LoRABatch: token groups per adapter slot (lora.py)
 
     @property
     def prefill_cu_q(self) -> torch.Tensor:

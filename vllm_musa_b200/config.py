@@ -274,6 +274,14 @@ class SpeculativeConfig:
 
 
 @dataclass
+class LoRAConfig:
+    """Multi-LoRA serving: adapters of rank <= max_lora_rank in max_loras device slots."""
+    enable_lora: bool = False
+    max_loras: int = 4
+    max_lora_rank: int = 64
+
+
+@dataclass
 class EngineConfig:
     model: ModelConfig = field(default_factory=ModelConfig)
     cache: CacheConfig = field(default_factory=CacheConfig)
@@ -287,6 +295,7 @@ class EngineConfig:
     enforce_eager: bool = False
     cuda_graph_sizes: Optional[list] = None
     speculative: SpeculativeConfig = field(default_factory=SpeculativeConfig)
+    lora: LoRAConfig = field(default_factory=lambda: LoRAConfig())
 
     def replace(self, **kw: Any) -> "EngineConfig":
         return dataclasses.replace(self, **kw)

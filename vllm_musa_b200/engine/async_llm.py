@@ -55,14 +55,14 @@ class AsyncLLM:
 
     # ------------------------------------------------------------------ API side
     async def generate(self, prompt_ids: List[int], params: SamplingParams,
-                       request_id: Optional[str] = None,
-                       prompt: Optional[str] = None) -> AsyncIterator[RequestOutput]:
+                       request_id: Optional[str] = None, prompt: Optional[str] = None,
+                       lora_request=None) -> AsyncIterator[RequestOutput]:
         rid = request_id or uuid.uuid4().hex
         loop = asyncio.get_running_loop()
         st = _Stream(loop, asyncio.Queue(), params, len(prompt_ids))
         with self._lock:
             self._streams[rid] = st
-        self._in.put(("add", rid, list(prompt_ids), params, prompt))
+        self._in.put(("add", rid, list(prompt_ids), params, prompt, lora_request))
         self._wake.set()
         try:
             while True:
@@ -95,8 +95,8 @@ class AsyncLLM:
                 return
             try:
                 if op[0] == "add":
-                    _, rid, ids, params, prompt = op
-                    self.engine.add_request(rid, ids, params, prompt=prompt)
+                    _, rid, ids, params, prompt, lora = op
+                    self.engine.add_request(rid, ids, params, prompt=prompt, lora_request=lora)
                     self.stats["prompt_tokens"] += len(ids)
                 else:
                     self._finish(op[1], None, "abort", abort_engine=True)

@@ -52,6 +52,8 @@ class _Req:
     cum_logprob: float = 0.0
     matcher: Optional[object] = None      # structured outputs: the request's grammar matcher
     stop_hit: Optional[tuple] = None      # (stop string, text up to it) once one matched
+    lora: Optional[object] = None         # LoRARequest of the request (None: base model)
+    lora_slot: int = -1
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -108,6 +110,12 @@ class LLMEngine:
         self._load_weights()
         if config.speculative.method == "eagle":
             self._load_eagle()
+        if config.lora.enable_lora:
+            from ..lora import LoRAManager
+            if not hasattr(self.model, "lora") or not hasattr(self.model, "I_pad"):
+                raise ValueError("LoRA adapters are served for the Llama / Qwen decoders")
+            self.model.lora = LoRAManager(self.model, config.lora.max_loras,
+                                          config.lora.max_lora_rank)
         log.info("weights ready in %.1fs", time.time() - t0)
         self.sampler = Sampler(self.comm, getattr(self.model, "vocab_start", 0), st.tp_size)
         dcp = config.parallel.decode_context_parallel_size
@@ -137,9 +145,11 @@ class LLMEngine:
         sc.max_blocks_per_seq = self.runner.max_blocks
         sc.chunked_prefill = config.scheduler.enable_chunked_prefill
         # recurrent-state (hybrid) models cannot resume from cached KV blocks alone
+        # (adapters change the KV of a prompt: no cross-request cache reuse with LoRA on)
         sc.prefix_caching = (config.cache.enable_prefix_caching
                              and self.contract.prefers(plan.Feature.PREFIX_CACHING)
-                             and not hasattr(self.model, "allocate_state"))
+                             and not hasattr(self.model, "allocate_state")
+                             and not config.lora.enable_lora)
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
         self._sched_cfg = sc
         self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
@@ -171,13 +181,16 @@ class LLMEngine:
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_token_ids: List[int],
                     params: Optional[SamplingParams] = None, arrival_time: Optional[float] = None,
-                    prompt: Optional[str] = None) -> None:
+                    prompt: Optional[str] = None, lora_request=None) -> None:
         params = params or SamplingParams()
         arrival = time.time() if arrival_time is None else arrival_time
+        if lora_request is not None and getattr(self.model, "lora", None) is None:
+            raise ValueError("lora_request needs LLM(..., enable_lora=True)")
         if self.sync is not None:
             if self.role == "follower":
                 raise RuntimeError("requests are added on the driver rank only")
-            self.sync.record(("add", request_id, list(prompt_token_ids), params, arrival, prompt))
+            self.sync.record(("add", request_id, list(prompt_token_ids), params, arrival, prompt,
+                              lora_request))
         if params.n > 1:
             self._parents[request_id] = {"n": params.n, "done": {}, "prompt_ids": prompt_token_ids,
                                          "prompt": prompt, "arrival": arrival}
@@ -186,11 +199,12 @@ class LLMEngine:
                 if params.seed is not None:
                     child.seed = params.seed + k
                 self._add_one(f"{request_id}#{k}", prompt_token_ids, child, arrival, prompt,
-                              parent=request_id, index=k)
+                              parent=request_id, index=k, lora=lora_request)
             return
-        self._add_one(request_id, prompt_token_ids, params, arrival, prompt)
+        self._add_one(request_id, prompt_token_ids, params, arrival, prompt, lora=lora_request)
 
-    def _add_one(self, name, prompt_ids, params, arrival, prompt, parent=None, index=0):
+    def _add_one(self, name, prompt_ids, params, arrival, prompt, parent=None, index=0,
+                 lora=None):
         if name in self._by_name:
             raise ValueError(f"duplicate request id {name!r}")
         iid = next(self._ids)
@@ -211,7 +225,11 @@ class LLMEngine:
         if params.stop and self.tokenizer is None:
             raise ValueError("stop strings need the model's tokenizer")
         special = params.has_penalties or params.logprobs is not None or so is not None or \
-            bool(params.stop)
+            bool(params.stop) or lora is not None
+        if lora is not None and self.config.speculative.method is not None and \
+                self.config.speculative.num_speculative_tokens:
+            raise ValueError("LoRA is not served with speculative decoding")
+        lora_slot = self.model.lora.acquire(lora) if lora is not None else -1
         if special and self.config.speculative.method is not None and \
                 self.config.speculative.num_speculative_tokens:
             raise ValueError("penalties / logprobs / structured outputs are not served with "
@@ -222,6 +240,7 @@ class LLMEngine:
         if params.logprobs is not None:
             r.logprobs = []
         r.matcher = matcher
+        r.lora, r.lora_slot = lora, lora_slot
         self._reqs[iid] = r
         self._by_name[name] = iid
         if special:
@@ -249,7 +268,9 @@ class LLMEngine:
             if iid is not None:
                 self.scheduler.abort_request(iid)
                 self._by_name.pop(n, None)
-                self._reqs.pop(iid, None)
+                r = self._reqs.pop(iid, None)
+                if r is not None and r.lora is not None:
+                    self.model.lora.release(r.lora.lora_int_id)
                 self._special.pop(iid, None)
                 self.scheduler.forget(iid)
         self._parents.pop(request_id, None)
@@ -315,6 +336,8 @@ class LLMEngine:
             r = self._reqs.pop(iid, None)
             if r is None:
                 continue
+            if r.lora is not None:
+                self.model.lora.release(r.lora.lora_int_id)
             self._by_name.pop(r.request_id, None)
             o = self._finish(r, _REASONS.get(reason, "stop"))
             if o is not None:
@@ -350,11 +373,31 @@ class LLMEngine:
             if p.logprobs is not None:
                 lp_rows.append(row)
                 k = max(k, p.logprobs)
-        if not rows_tok and not lp_rows and not mask_rows:
+        lora = self._lora_batch(plan)
+        if not rows_tok and not lp_rows and not mask_rows and lora is None:
             return None
         entries = penalty_entries(rows_tok) if rows_tok else None
         bitmask = self._grammar_backend().bitmask(matchers) if matchers else None
-        return StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
+        ex = StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
+        ex.lora = lora
+        return ex
+
+    def _lora_batch(self, plan):
+        """Token indices of this step grouped by adapter slot (None: no adapter in the step)."""
+        if getattr(self.model, "lora", None) is None:
+            return None
+        from ..lora import LoRABatch
+        cu = self.runner.buf.h["cu_q"][:plan.num_reqs + 1].tolist()
+        by_slot = {}
+        for i, iid in enumerate(plan.req_ids):
+            r = self._reqs.get(iid)
+            if r is not None and r.lora_slot >= 0:
+                by_slot.setdefault(r.lora_slot, []).extend(range(cu[i], cu[i + 1]))
+        if not by_slot:
+            return None
+        dev = self.runner.device
+        return LoRABatch([(s, torch.tensor(t, dtype=torch.long, device=dev))
+                          for s, t in sorted(by_slot.items())])
 
     def _match_stop_strings(self, plan, finished):
         """Finish (reason "stop") every request whose output text now contains one of its stop
@@ -451,10 +494,10 @@ class LLMEngine:
         m = RequestMetrics(r.arrival, first if first is not None else r.first_token_time, last)
         return RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
 
-    def _follower_add(self, request_id, prompt_ids, params, arrival, prompt):
+    def _follower_add(self, request_id, prompt_ids, params, arrival, prompt, lora_request=None):
         sync, self.sync = self.sync, None  # apply locally without re-recording
         try:
-            self.add_request(request_id, prompt_ids, params, arrival, prompt)
+            self.add_request(request_id, prompt_ids, params, arrival, prompt, lora_request)
         finally:
             self.sync = sync
 

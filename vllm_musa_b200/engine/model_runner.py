@@ -104,6 +104,7 @@ class StepExtras:
         self.lp_k = lp_k
         self.bitmask = bitmask
         self.mask_rows = mask_rows or []
+        self.lora = None  # LoRABatch of the step (adapters in use)
         self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
 
 
@@ -293,13 +294,22 @@ class ModelRunner:
     @staticmethod
     def _meta_slice(meta: AttnMetadata, r0: int, r1: int, t0: int, t1: int) -> AttnMetadata:
         nd = max(0, min(r1, meta.num_decodes) - r0)
-        return AttnMetadata(t1 - t0, nd, (r1 - r0) - nd, meta.positions[t0:t1],
-                            meta.slot_mapping[t0:t1], meta.seq_lens[r0:r1],
-                            meta.block_tables[r0:r1], meta.cu_q[r0:r1 + 1] - t0,
-                            max_seq_len=meta.max_seq_len, tile_scratch=meta.tile_scratch,
-                            sliding_window=meta.sliding_window,
-                            state_slots=None if meta.state_slots is None
-                            else meta.state_slots[r0:r1])
+        m = AttnMetadata(t1 - t0, nd, (r1 - r0) - nd, meta.positions[t0:t1],
+                         meta.slot_mapping[t0:t1], meta.seq_lens[r0:r1],
+                         meta.block_tables[r0:r1], meta.cu_q[r0:r1 + 1] - t0,
+                         max_seq_len=meta.max_seq_len, tile_scratch=meta.tile_scratch,
+                         sliding_window=meta.sliding_window,
+                         state_slots=None if meta.state_slots is None
+                         else meta.state_slots[r0:r1])
+        if meta.lora is not None:  # adapter token groups re-based to the micro-batch
+            from ..lora import LoRABatch
+            groups = []
+            for slot, idx in meta.lora.groups:
+                sel = idx[(idx >= t0) & (idx < t1)] - t0
+                if sel.numel():
+                    groups.append((slot, sel))
+            m.lora = LoRABatch(groups) if groups else None
+        return m
 
     def _forward_sample_pp(self, T: int, R: int, S: int, meta: AttnMetadata, sampling: bool,
                            any_filter: bool, decode_only: bool) -> torch.Tensor:
@@ -482,6 +492,7 @@ class ModelRunner:
             sampling = not plan.all_greedy
             self.h2d_bytes += b.upload(T, R, S, sampling)
             meta = self._meta(T, R, nd, npf, plan.max_seq_len)
+            meta.lora = extras.lora if extras is not None else None
             ids = self._forward_sample(T, R, S, meta, sampling=sampling,
                                        any_filter=plan.any_filter, decode_only=decode_only)
         self._extras = None

@@ -11,8 +11,8 @@ from __future__ import annotations
 import os
 from typing import List, Optional, Sequence, Union
 
-from ..config import (CacheConfig, EngineConfig, ModelConfig, ParallelConfig, SchedulerConfig,
-                      SpeculativeConfig)
+from ..config import (CacheConfig, EngineConfig, LoRAConfig, ModelConfig, ParallelConfig,
+                      SchedulerConfig, SpeculativeConfig)
 from ..engine.llm_engine import LLMEngine
 from ..models.presets import PRESETS, get_preset
 from ..outputs import RequestOutput
@@ -44,6 +44,7 @@ class LLM:
                  device: str = "cuda", dtype=None, tokenizer=None,
                  cuda_graph_sizes: Optional[list] = None, num_layers: Optional[int] = None,
                  speculative_config: Optional[dict] = None,
+                 enable_lora: bool = False, max_loras: int = 4, max_lora_rank: int = 64,
                  kv_cache_dtype: Optional[str] = None, **unused):
         path = None
         if isinstance(model, ModelConfig):
@@ -80,7 +81,9 @@ class LLM:
                                     data_parallel_size=data_parallel_size),
             device=device, seed=seed, load_format=load_format, model_path=path,
             enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes,
-            speculative=SpeculativeConfig.from_dict(speculative_config))
+            speculative=SpeculativeConfig.from_dict(speculative_config),
+            lora=LoRAConfig(enable_lora=enable_lora, max_loras=max_loras,
+                            max_lora_rank=max_lora_rank))
         tok = tokenizer if tokenizer is not None else _load_tokenizer(path)
         self.executor = None
         self.dp_size, self.dp_rank = 1, 0
@@ -125,7 +128,9 @@ class LLM:
 
     def generate(self, prompts: Union[PromptType, Sequence[PromptType]],
                  sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
-                 use_tqdm: bool = False) -> List[RequestOutput]:
+                 use_tqdm: bool = False, lora_request=None) -> List[RequestOutput]:
+        """``lora_request``: one LoRARequest for every prompt, or a list with one (or None)
+        per prompt."""
         if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and
                                                 isinstance(prompts[0], int)):
             prompts = [prompts]
@@ -133,14 +138,18 @@ class LLM:
             sampling_params = SamplingParams()
         if isinstance(sampling_params, SamplingParams):
             sampling_params = [sampling_params] * len(prompts)
+        loras = lora_request if isinstance(lora_request, (list, tuple)) else \
+            [lora_request] * len(prompts)
         if self.dp_size > 1:
+            if any(x is not None for x in loras):
+                raise ValueError("LoRA with data parallelism is not served")
             return self._generate_dp(prompts, sampling_params)
         order = []
-        for p, sp in zip(prompts, sampling_params):
+        for p, sp, lr in zip(prompts, sampling_params, loras):
             ids, text = self._prompt_ids(p)
             rid = str(self._counter)
             self._counter += 1
-            self.engine.add_request(rid, ids, sp, prompt=text)
+            self.engine.add_request(rid, ids, sp, prompt=text, lora_request=lr)
             order.append(rid)
         done = {}
         while self.engine.has_unfinished_requests():

@@ -37,8 +37,9 @@ def _chat_prompt(tokenizer, messages: List[ChatMessage]) -> List[int]:
     return tokenizer.encode(text)
 
 
-def build_app(llm, model_name: str, max_model_len: int):
-    """FastAPI app over an ``AsyncLLM``."""
+def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[dict] = None):
+    """FastAPI app over an ``AsyncLLM``.  ``lora_modules``: served adapter name -> LoRARequest
+    (a request whose ``model`` names an adapter runs with it)."""
     from fastapi import FastAPI, Request
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -78,9 +79,20 @@ def build_app(llm, model_name: str, max_model_len: int):
         from ... import __version__
         return {"version": __version__}
 
+    loras = dict(lora_modules or {})
+
+    def lora_of(req):
+        if req.model is None or req.model == model_name:
+            return None
+        if req.model in loras:
+            return loras[req.model]
+        raise ValueError(f"model {req.model!r} is not served")
+
     @app.get("/v1/models")
     async def models():
-        return ModelList(data=[ModelCard(id=model_name, max_model_len=max_model_len)]).model_dump()
+        cards = [ModelCard(id=model_name, max_model_len=max_model_len)]
+        cards += [ModelCard(id=n, max_model_len=max_model_len) for n in loras]
+        return ModelList(data=cards).model_dump()
 
     @app.get("/metrics")
     async def metrics():
@@ -107,15 +119,16 @@ def build_app(llm, model_name: str, max_model_len: int):
             lines.append(f"b200_{name}_sum {sum(vals):.6f}")
         return PlainTextResponse("\n".join(lines) + "\n")
 
-    async def run_one(ids, params, rid):
+    async def run_one(ids, params, rid, lora=None):
         final = None
-        async for o in llm.generate(ids, params, rid):
+        async for o in llm.generate(ids, params, rid, lora_request=lora):
             final = o
         return final
 
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
         try:
+            lora = lora_of(req)
             prompts = encode_prompts(req.prompt)
             base = req.sampling_params(default_max)
             jobs = []
@@ -133,7 +146,7 @@ def build_app(llm, model_name: str, max_model_len: int):
             async def gen():
                 qs = []
                 for idx, ids, text, p in jobs:
-                    qs.append((idx, llm.generate(ids, p, f"{rid}-{idx}")))
+                    qs.append((idx, llm.generate(ids, p, f"{rid}-{idx}", lora_request=lora)))
                 for idx, it in qs:
                     sent = ""
                     async for o in it:
@@ -148,7 +161,8 @@ def build_app(llm, model_name: str, max_model_len: int):
                         yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}") for idx, ids, _, p in jobs])
+        outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}", lora)
+                                      for idx, ids, _, p in jobs])
         choices, n_prompt, n_gen = [], 0, 0
         for (idx, ids, text, _), o in zip(jobs, outs):
             c = o.outputs[0]
@@ -165,6 +179,7 @@ def build_app(llm, model_name: str, max_model_len: int):
     @app.post("/v1/chat/completions")
     async def chat(req: ChatCompletionRequest):
         try:
+            lora = lora_of(req)
             ids = _chat_prompt(tok, req.messages)
             p = req.sampling_params(req.max_completion_tokens or default_max)
             if req.max_completion_tokens:
@@ -176,7 +191,8 @@ def build_app(llm, model_name: str, max_model_len: int):
         if req.stream:
             async def gen():
                 sent = ""
-                async for o in llm.generate(ids, SamplingParams(**{**p.__dict__, "n": 1}), rid):
+                async for o in llm.generate(ids, SamplingParams(**{**p.__dict__, "n": 1}), rid,
+                                            lora_request=lora):
                     c = o.outputs[0]
                     delta = c.text[len(sent):]
                     sent = c.text
@@ -190,7 +206,7 @@ def build_app(llm, model_name: str, max_model_len: int):
         outs = await asyncio.gather(*[
             run_one(ids, SamplingParams(**{**p.__dict__, "n": 1,
                                            "seed": (p.seed + k) if p.seed is not None else None}),
-                    f"{rid}-{k}") for k in range(p.n)])
+                    f"{rid}-{k}", lora) for k in range(p.n)])
         choices = [ChatChoice(index=k, message=ChatMessage(role="assistant", content=o.outputs[0].text),
                               finish_reason=o.outputs[0].finish_reason,
                               logprobs=chat_logprobs(o.outputs[0], tok, req.top_logprobs or 0))
@@ -212,6 +228,11 @@ def make_arg_parser(p: Optional[argparse.ArgumentParser] = None) -> argparse.Arg
     p.add_argument("--tensor-parallel-size", "-tp", type=int, default=1)
     p.add_argument("--pipeline-parallel-size", "-pp", type=int, default=1)
     p.add_argument("--enable-expert-parallel", action="store_true")
+    p.add_argument("--enable-lora", action="store_true")
+    p.add_argument("--max-loras", type=int, default=4)
+    p.add_argument("--max-lora-rank", type=int, default=64)
+    p.add_argument("--lora-modules", nargs="*", default=[],
+                   help="name=path adapters served under their own model names")
     p.add_argument("--speculative-config", type=json.loads, default=None,
                    help='JSON, e.g. {"method": "eagle", "num_speculative_tokens": 1, '
                         '"model": "/path/to/eagle"}')
@@ -233,6 +254,10 @@ def build_llm(args):
     return LLM(args.model, tensor_parallel_size=args.tensor_parallel_size,
                pipeline_parallel_size=getattr(args, "pipeline_parallel_size", 1),
                speculative_config=getattr(args, "speculative_config", None),
+               enable_lora=(getattr(args, "enable_lora", False) or
+                            bool(getattr(args, "lora_modules", []))),
+               max_loras=getattr(args, "max_loras", 4),
+               max_lora_rank=getattr(args, "max_lora_rank", 64),
                enable_expert_parallel=args.enable_expert_parallel,
                max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs,
                max_num_batched_tokens=args.max_num_batched_tokens, block_size=args.block_size,
@@ -240,6 +265,18 @@ def build_llm(args):
                enforce_eager=args.enforce_eager,
                enable_prefix_caching=not args.no_enable_prefix_caching, seed=args.seed,
                device=args.device, num_gpu_blocks=args.num_gpu_blocks)
+
+
+def parse_lora_modules(specs) -> dict:
+    """["name=path", ...] -> {name: LoRARequest} (ids 1, 2, ... in order)."""
+    from ...lora import LoRARequest
+    out = {}
+    for k, spec in enumerate(specs or []):
+        name, _, path = spec.partition("=")
+        if not name or not path:
+            raise ValueError(f"--lora-modules entries are name=path, got {spec!r}")
+        out[name] = LoRARequest(name, k + 1, path)
+    return out
 
 
 def run_server(args) -> None:
@@ -257,7 +294,8 @@ def run_server(args) -> None:
         return
     alm = AsyncLLM(llm.engine)
     name = args.served_model_name or args.model
-    app = build_app(alm, name, llm.engine.config.scheduler.max_model_len)
+    app = build_app(alm, name, llm.engine.config.scheduler.max_model_len,
+                    parse_lora_modules(getattr(args, "lora_modules", [])))
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:

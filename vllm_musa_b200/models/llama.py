@@ -109,6 +109,7 @@ class DenseDecoderForCausalLM:
         self.lm_head = None
         self.tq = None
         self.draft_head = None  # EAGLE head (speculative decoding): one extra cache layer
+        self.lora = None        # LoRAManager when adapters are enabled
         if cfg.kv_cache_dtype not in ("auto", None, "bf16", "bfloat16"):
             from ..attention import TurboQuantAttention
             self.attn = TurboQuantAttention(self.hq, self.hkv, self.D, cfg.kv_cache_dtype)
@@ -239,6 +240,9 @@ class DenseDecoderForCausalLM:
             L = self.layers[i]
             kc, vc = kv_caches[i - self.l0]
             qkv = ops.linear(x, L.qkv_w)
+            lora = getattr(meta, "lora", None)
+            if lora is not None:
+                self._lora_qkv(i, x, qkv, lora)
             if self.tq is not None:
                 D, hq, hkv = self.D, self.hq, self.hkv
                 ops.rope_kv(qkv, meta.positions, self.cos_sin, None, None, meta.slot_mapping,
@@ -252,11 +256,45 @@ class DenseDecoderForCausalLM:
                             self.hq, self.hkv, cfg.rot_dim, cfg.rope_neox, L.q_norm, L.k_norm,
                             eps)
             a = self.attn.forward(qkv, kc, vc, meta)
-            x, residual = self.comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
+            delta = None
+            if lora is not None and self.lora.has(i, "o"):
+                delta = lambda inp, out, i=i: self.lora.add_delta(i, "o", inp, out, lora)  # noqa: E731
+            x, residual = self.comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps,
+                                                                 delta=delta)
             nxt = self.layers[i + 1].ln1 if i + 1 < n else \
                 (self.final_norm if self.last_stage else self._stage_norm)
-            x, residual = self._mlp_allreduce(i, L, x, T, residual, nxt, eps)
+            if lora is not None and self.lora.has(i, "down"):
+                x, residual = self._lora_mlp(i, L, x, residual, nxt, eps, lora)
+            else:
+                x, residual = self._mlp_allreduce(i, L, x, T, residual, nxt, eps)
         return x if self.last_stage else residual
+
+    # ------------------------------------------------------------------ LoRA
+    def _lora_qkv(self, i, x, qkv, batch) -> None:
+        D, hq, hkv = self.D, self.hq, self.hkv
+        cuts = {"q": (0, hq * D), "k": (hq * D, (hq + hkv) * D),
+                "v": ((hq + hkv) * D, (hq + 2 * hkv) * D)}
+        for mod, (c0, c1) in cuts.items():
+            if self.lora.has(i, mod):
+                self.lora.add_delta(i, mod, x, qkv[:, c0:c1], batch)
+
+    def _lora_mlp(self, i, L, x, residual, nxt, eps, batch):
+        """Dense MLP with adapters: plain gate/up GEMM, gate and up deltas added before the
+        SwiGLU, down projection's delta added to its partial sum before the all-reduce."""
+        from ..lora import add_interleaved, silu_mul_interleaved
+        T = x.shape[0]
+        gu = ops.linear(x, L.gu_w)
+        dg = torch.zeros(T, self.I_pad, dtype=gu.dtype, device=gu.device)
+        du = torch.zeros_like(dg)
+        if self.lora.has(i, "gate"):
+            self.lora.add_delta(i, "gate", x, dg[:, :self.I], batch)
+        if self.lora.has(i, "up"):
+            self.lora.add_delta(i, "up", x, du[:, :self.I], batch)
+        add_interleaved(gu, dg, du)
+        act = silu_mul_interleaved(gu)
+        return self.comm.linear_allreduce_add_rmsnorm(
+            act, L.down_w, residual, nxt, eps,
+            delta=lambda inp, out: self.lora.add_delta(i, "down", inp, out, batch))
 
     def _mlp_allreduce(self, i, L, x, T, residual, nxt, eps):
         """MLP + all-reduce + residual + next norm; the dense down projection fuses its

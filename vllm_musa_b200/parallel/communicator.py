@@ -107,16 +107,19 @@ class TPCommunicator:
         return x, residual, (q, sc)
 
     def linear_allreduce_add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor,
-                                     residual: torch.Tensor, weight: torch.Tensor, eps: float
-                                     ) -> tuple[torch.Tensor, torch.Tensor]:
+                                     residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                                     delta=None) -> tuple[torch.Tensor, torch.Tensor]:
         """Row-parallel projection followed by all-reduce + residual + RMSNorm.  On the
         NVSwitch communicator the reduce-scatter is fused into the GEMM epilogue; otherwise
-        GEMM into the staging buffer, then ``allreduce_add_rmsnorm``."""
+        GEMM into the staging buffer, then ``allreduce_add_rmsnorm``.  ``delta(x, o)`` adds to
+        the projection's partial sum ``o`` in place before the reduction (LoRA)."""
         T = x.shape[0]
-        if self.world > 1 and self.custom is not None and x.is_cuda and \
+        if delta is None and self.world > 1 and self.custom is not None and x.is_cuda and \
                 self.custom.can_fuse_gemm(T):
             return self.custom.linear_allreduce_add_rmsnorm(x, w, residual, weight, eps)
         o = ops.linear(x, w, out=self.out_buffer(T))
+        if delta is not None:
+            delta(x, o)
         return self.allreduce_add_rmsnorm(o, residual, weight, eps)
 
     def close(self) -> None:
