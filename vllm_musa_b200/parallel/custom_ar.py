@@ -55,11 +55,10 @@ NVLS = os.environ.get("B200_AR_NVLS", "1") != "0"
 #         two-shot 27.3 vs 49.7; 1024 rows: 41.9 vs 66.9) and ties beyond (4096 rows: 114.8 vs
 #         110.9; 8192: 204.5 vs 200.9); the Llama-3-8B serving bench at TP=8 runs 30.0k tok/s
 #         with NVLS against 26.5k with the peer-to-peer kernels.
-#   TP=4: from 512 KiB (64 rows of 4096), where NVLS's byte advantage (1.25 vs 1.5 message
-#         copies per direction) and its flat latency take over from the peer-to-peer one-shot;
-#         interpolated between the two measured world sizes.
+#   TP=4: peer-to-peer wins or ties at every size (8 rows: one-shot 12.0 us vs NVLS 16.4;
+#         256 rows: two-shot 26.6 vs 25.6; 1024: 42.2 vs 41.7; 8192: 171.2 vs 210.1).
 # B200_AR_NVLS_MIN_BYTES overrides the threshold for every world size.
-NVLS_MIN_BYTES = {2: None, 4: 512 << 10, 8: 0}
+NVLS_MIN_BYTES = {2: None, 4: None, 8: 0}
 # rows each warp of the NVLS kernel walks (0: the kernel's size rule; tuning / benchmarks)
 NVLS_ROWS_PER_WARP = int(os.environ.get("B200_AR_NVLS_ROWS_PER_WARP", "0"))
 if os.environ.get("B200_AR_NVLS_MIN_BYTES"):
@@ -67,9 +66,10 @@ if os.environ.get("B200_AR_NVLS_MIN_BYTES"):
 # the NVLS kernel's fused 1x128 e4m3 output replaces AR + norm + a separate quantisation from
 # this many rows up, by world size.  TP=2: never (against the peer-to-peer AR + norm + group
 # quantisation it measures 25.9 vs 14.2 us at 8 rows, 34.8 vs 23.7 at 256, 69.0 vs 53.7 at
+# 2048); TP=4: from ~1k rows (24.1 vs 14.1 us at 8 rows, 28.4 vs 28.7 at 256, 58.3 vs 76.0 at
 # 2048); TP=8: faster at every measured size (26.0 vs 37.5 us at 8 rows, 32.5 vs 52.4 at 256,
-# 61.2 vs 81.6 at 2048); TP=4 interpolated.
-NVLS_QUANT_MIN_ROWS = {2: 1 << 30, 4: 256, 8: 1}
+# 61.2 vs 81.6 at 2048).
+NVLS_QUANT_MIN_ROWS = {2: 1 << 30, 4: 1024, 8: 1}
 if os.environ.get("B200_AR_NVLS_QUANT_MIN_ROWS"):
     NVLS_QUANT_MIN_ROWS = {w: int(os.environ["B200_AR_NVLS_QUANT_MIN_ROWS"]) for w in (2, 4, 8)}
 
