@@ -90,3 +90,39 @@ def test_peer_barrier_timeout_returns_error_status():
     torch.cuda.synchronize()
     assert torch.isfinite(y)
     _ext.check_device_errors()
+
+
+class _FakeNvml:
+    """NVML stand-in: GPUs by bus id; `nvlink` lists the bus-id pairs joined by NVLink."""
+    NVML_P2P_CAPS_INDEX_NVLINK = 5
+    NVML_P2P_STATUS_OK = 0
+
+    def __init__(self, nvlink):
+        self.nvlink = {frozenset(p) for p in nvlink}
+        self.inits = 0
+
+    def nvmlInit(self):
+        self.inits += 1
+
+    def nvmlShutdown(self):
+        self.inits -= 1
+
+    def nvmlDeviceGetHandleByPciBusId(self, b):
+        return b
+
+    def nvmlDeviceGetP2PStatus(self, a, b, cap):
+        assert cap == self.NVML_P2P_CAPS_INDEX_NVLINK
+        return self.NVML_P2P_STATUS_OK if frozenset((a, b)) in self.nvlink else 4
+
+
+def test_nvlink_topology_check_with_fake_nvml():
+    """The communicator's NVLink full-mesh check: OK only if this GPU reaches every peer over
+    NVLink (a PCIe-only pair, or an NVML error, keeps the group on NCCL)."""
+    from vllm_musa_b200.parallel.topology import nvlink_to_all
+    ids = ["0000:1b:00.0", "0000:43:00.0", "0000:52:00.0"]
+    full = _FakeNvml([(ids[0], ids[1]), (ids[0], ids[2]), (ids[1], ids[2])])
+    assert nvlink_to_all(ids[0], ids, full) and full.inits == 0
+    partial = _FakeNvml([(ids[0], ids[1])])
+    assert nvlink_to_all(ids[0], ids[:2], partial)
+    assert not nvlink_to_all(ids[0], ids, partial)
+    assert not nvlink_to_all(ids[2], ids, partial) and partial.inits == 0

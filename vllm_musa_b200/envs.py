@@ -54,6 +54,8 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
             "vLLM plugin: activate the B200 platform even if no sm_100 device is detected"),
     EnvFlag("B200_CUSTOM_OP_USE_NATIVE", False, _bool,
             "vLLM plugin: register the custom ops but route them to the PyTorch implementations"),
+    EnvFlag("B200_SKIP_NVLINK_CHECK", False, _bool,
+            "build the peer-memory communicator without the NVML NVLink full-mesh check"),
     EnvFlag("B200_AR_NVLS", True, _bool,
             "allow the NVLS (multimem) all-reduce where every rank got a multicast mapping"),
     EnvFlag("B200_AR_NVLS_MIN_BYTES", None, int,

@@ -441,8 +441,14 @@ def maybe_create_custom_allreduce(st, device, max_tokens: int = 8192, hidden: in
     if os.environ.get("B200_DISABLE_CUSTOM_AR", "0") == "1":
         return None
     comm, ok = None, 1
+    from .topology import group_nvlink_ok
+    if os.environ.get("B200_SKIP_NVLINK_CHECK", "0") != "1" and \
+            not group_nvlink_ok(device, st.tp_cpu_group):
+        log.warning("rank %d: not every peer GPU is reachable over NVLink; NCCL all-reduce",
+                    st.rank)
+        ok = 0
     try:
-        comm = CustomAllReduce(st, device, max_tokens, hidden)
+        comm = CustomAllReduce(st, device, max_tokens, hidden) if ok else None
     except Exception as e:  # fail closed
         log.warning("custom all-reduce unavailable on rank %d: %s", st.rank, e)
         ok = 0
