@@ -54,6 +54,9 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
             "vLLM plugin: activate the B200 platform even if no sm_100 device is detected"),
     EnvFlag("B200_CUSTOM_OP_USE_NATIVE", False, _bool,
             "vLLM plugin: register the custom ops but route them to the PyTorch implementations"),
+    EnvFlag("B200_DEBUG_BOUNDS", False, _bool,
+            "check index tensors (KV slots, block tables, row indices) against the kernels' "
+            "bounds at every op call and raise IndexError (synchronises: debugging only)"),
     EnvFlag("B200_SKIP_NVLINK_CHECK", False, _bool,
             "build the peer-memory communicator without the NVML NVLink full-mesh check"),
     EnvFlag("B200_AR_NVLS", True, _bool,

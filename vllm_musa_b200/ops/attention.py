@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from . import _ext
+from . import _bounds, _ext
 
 _WS: dict = {}
 
@@ -64,6 +64,18 @@ def _attend_ref(q, k, v, q_pos, scale, window, sinks=None, causal=True, allowed=
     return torch.einsum("hts,shd->thd", p, v)
 
 
+def _check_tables(op, k_cache, block_tables, seq_lens) -> None:
+    """Debug bounds: the pages a request's length reaches are cache blocks; the length fits the
+    table's width."""
+    bs = k_cache.shape[2]
+    W = block_tables.shape[1]
+    _bounds.check(op, "seq_lens", seq_lens, W * bs + 1)
+    if seq_lens.numel():
+        used = (torch.arange(W, device=block_tables.device)[None, :] * bs <
+                seq_lens.to(block_tables.device).long()[:, None])
+        _bounds.check(op, "block_tables", block_tables[used], k_cache.shape[0])
+
+
 def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  block_tables: torch.Tensor, seq_lens: torch.Tensor, num_q_heads: int,
                  num_kv_heads: int, scale: float, max_seq_len: int,
@@ -78,6 +90,8 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         out = torch.empty(B, Hq * D, dtype=q.dtype, device=q.device)
     if B == 0:
         return out
+    if _bounds.enabled():
+        _check_tables("paged_decode", k_cache, block_tables[:B], seq_lens[:B])
     if q.is_cuda:
         if num_splits is None:
             num_splits = num_decode_splits(B, num_kv_heads, max_seq_len)
@@ -124,6 +138,9 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
     if T == 0 or R == 0:
         return out
+    if _bounds.enabled():
+        _check_tables("paged_prefill", k_cache, block_tables[:R], seq_lens[:R])
+        _bounds.check("paged_prefill", "cu_q", cu_q[:R + 1], T + 1)
     if q.is_cuda:
         if tile_scratch is None:
             tile_scratch = torch.empty(R + 1, dtype=torch.int32, device=q.device)
@@ -223,6 +240,8 @@ def kv_insert(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
     n = min(int(slot_mapping.numel()), key.shape[0])
     if n == 0:
         return
+    _bounds.check("kv_insert", "slot_mapping", slot_mapping[:n],
+                  k_cache.shape[0] * k_cache.shape[2], skip_negative=True)
     if key.is_cuda:
         _ext.ops().kv_insert(key, value, k_cache, v_cache, slot_mapping.to(torch.int64))
         return

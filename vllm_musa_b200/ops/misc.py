@@ -3,7 +3,7 @@ from __future__ import annotations
 
 import torch
 
-from . import _ext
+from . import _bounds, _ext
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
@@ -12,6 +12,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
     T, H = ids.shape[0], table.shape[1]
     if out is None:
         out = torch.empty(T, H, dtype=table.dtype, device=table.device)
+    _bounds.check("embedding", "ids", ids, 1 << 31)  # token ids are never negative
     if table.is_cuda:
         if T:
             _ext.ops().embedding(out, table, ids, vocab_start)
@@ -26,6 +27,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
 def gather_rows(x: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(idx.shape[0], x.shape[1], dtype=x.dtype, device=x.device)
+    _bounds.check("gather_rows", "idx", idx, x.shape[0])
     if x.is_cuda:
         if idx.shape[0]:
             _ext.ops().gather_rows(out, x, idx)

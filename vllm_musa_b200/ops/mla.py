@@ -15,7 +15,7 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
-from . import _ext
+from . import _bounds, _ext
 
 LAT, PE = 512, 64
 
@@ -114,6 +114,15 @@ def mla_attention(q_lat: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor,
     T = q_lat.shape[0]
     if T == 0:
         return out
+    if _bounds.enabled():
+        bs = cache.shape[1] if cache.dim() == 3 else cache.shape[-2]
+        R = seq_lens.shape[0]
+        W = block_tables.shape[1]
+        _bounds.check("mla_attention", "seq_lens", seq_lens, W * bs * max(1, dcp[0]) + 1)
+        _bounds.check("mla_attention", "block_tables", block_tables[:R], cache.shape[0])
+        if indices is not None:
+            _bounds.check("mla_attention", "indices", indices, int(seq_lens.max()) + 1,
+                          skip_negative=True)
     if q_lat.is_cuda:
         wo, wl = ws if ws is not None else (None, None)
         _ext.ops().mla_attention(q_lat, q_pe, cache, block_tables, cu_q, seq_lens, indices, out,

@@ -7,7 +7,7 @@ import math
 
 import torch
 
-from . import _ext
+from . import _bounds, _ext
 
 
 def build_cos_sin_cache(rot_dim: int, max_pos: int, theta: float, device=None,
@@ -93,6 +93,11 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
     if head_dim is None:
         head_dim = k_cache.shape[-1] if k_cache is not None else qkv.shape[1] // (
             num_q_heads + 2 * num_kv_heads)
+    if _bounds.enabled():
+        if k_cache is not None:
+            _bounds.check("rope_kv", "slot_mapping", slot_mapping,
+                          k_cache.shape[0] * k_cache.shape[2], skip_negative=True)
+        _bounds.check("rope_kv", "positions", positions, cos_sin.shape[0])
     if qkv.is_cuda:
         _ext.ops().rope_kv(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache,
                            slot_mapping, num_q_heads, num_kv_heads, rot_dim, neox, eps, head_dim,
