@@ -15,6 +15,8 @@
 //     kernel rotates q once per warp, so keys are never rotated back on the decode path.
 //   key, fp8 mode (8 bits): e4m3 with one fp16 scale (amax / 448) per vector, not rotated.
 //   value (3 or 4 bits): uniform levels between the vector's min and max (fp16 scale, zero).
+//   value, fp8 mode (8 bits): e4m3 with one fp16 scale (amax / 448) per vector (zero unused);
+//     with fp8 keys this is the "fp8" KV cache (e4m3 with per-vector scales).
 //
 // Slot of one (token, KV head), bytes: [key codes D*kb/8 | value codes D*vb/8 | key scale f16 |
 // value scale f16 | value zero f16 | pad to 16].  Codes are a little-endian bit stream: the
@@ -150,9 +152,15 @@ B200_DEVICE void load_key(const uint32_t* sw, int lane, float ksc, const float* 
 template <int E, int VB>
 B200_DEVICE void load_value(const uint32_t* sw, int key_bytes, int lane, float vsc, float vz,
                             float (&v)[E]) {
-  const uint32_t bits = get_bits(sw, key_bytes * 8 + E * lane * VB, E * VB);
+  if constexpr (VB == 8) {  // e4m3 codes, byte-aligned after the key codes
+    const uint8_t* bytes = reinterpret_cast<const uint8_t*>(sw) + key_bytes + E * lane;
 #pragma unroll
-  for (int e = 0; e < E; ++e) v[e] = float((bits >> (e * VB)) & ((1u << VB) - 1u)) * vsc + vz;
+    for (int e = 0; e < E; ++e) v[e] = fp8_to_float(bytes[e]) * vsc;
+  } else {
+    const uint32_t bits = get_bits(sw, key_bytes * 8 + E * lane * VB, E * VB);
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = float((bits >> (e * VB)) & ((1u << VB) - 1u)) * vsc + vz;
+  }
 }
 
 // ------------------------------------------------------------------------------------ store
@@ -225,22 +233,39 @@ __global__ void __launch_bounds__(256) tq_store_kernel(TQStoreArgs a) {
       ksc = a.norm_correction ? (cs > 0.f ? norm / sqrtf(cs) : 0.f) : norm * rs;
       ksc = __half2float(__float2half_rn(ksc));
     }
-    float vmin = vx[0], vmax = vx[0];
+    __half hsc, hz;
+    if constexpr (VB == 8) {
+      float am = 0.f;
 #pragma unroll
-    for (int e = 1; e < E; ++e) {
-      vmin = fminf(vmin, vx[e]);
-      vmax = fmaxf(vmax, vx[e]);
-    }
-    vmin = -warp_max(-vmin);
-    vmax = warp_max(vmax);
-    const __half hsc = __float2half_rn((vmax - vmin) / float(L));
-    const __half hz = __float2half_rn(vmin);
-    const float vsc = __half2float(hsc), vz = __half2float(hz);
+      for (int e = 0; e < E; ++e) am = fmaxf(am, fabsf(vx[e]));
+      am = warp_max(am);
+      hsc = __float2half_rn(am / 448.f);
+      hz = __float2half_rn(0.f);
+      const float vsc = __half2float(hsc);
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      int c = 0;
-      if (vsc > 0.f) c = min(L, max(0, __float2int_rn((vx[e] - vz) / vsc)));
-      put_bits(w, key_bytes * 8 + (E * lane + e) * VB, uint32_t(c), VB);
+      for (int e = 0; e < E; ++e) {
+        const float x = vsc > 0.f ? vx[e] / vsc : 0.f;
+        const uint32_t b = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+        put_bits(w, key_bytes * 8 + (E * lane + e) * 8, b, 8);
+      }
+    } else {
+      float vmin = vx[0], vmax = vx[0];
+#pragma unroll
+      for (int e = 1; e < E; ++e) {
+        vmin = fminf(vmin, vx[e]);
+        vmax = fmaxf(vmax, vx[e]);
+      }
+      vmin = -warp_max(-vmin);
+      vmax = warp_max(vmax);
+      hsc = __float2half_rn((vmax - vmin) / float(L));
+      hz = __float2half_rn(vmin);
+      const float vsc = __half2float(hsc), vz = __half2float(hz);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        int c = 0;
+        if (vsc > 0.f) c = min(L, max(0, __float2int_rn((vx[e] - vz) / vsc)));
+        put_bits(w, key_bytes * 8 + (E * lane + e) * VB, uint32_t(c), VB);
+      }
     }
     if (lane == 0) {
       const uint32_t kb16 = __half_as_ushort(__float2half_rn(ksc));
@@ -441,6 +466,7 @@ template <template <int, int, int> class F, typename... Args>
 void dispatch(int D, int kb, int vb, Args&&... args) {
   auto by_bits = [&](auto dtag) {
     constexpr int DD = decltype(dtag)::value;
+    if (kb == 8 && vb == 8) return F<DD, 8, 8>::run(args...);
     if (kb == 8 && vb == 4) return F<DD, 8, 4>::run(args...);
     if (kb == 4 && vb == 4) return F<DD, 4, 4>::run(args...);
     if (kb == 3 && vb == 4) return F<DD, 3, 4>::run(args...);

@@ -38,11 +38,14 @@ def test_slot_sizes():
     assert tq.tq_format("turboquant_k8v4", 128).slot_bytes == 208
     assert tq.tq_format("turboquant_k3v4_nc", 128).slot_bytes == 128
     assert tq.tq_format("turboquant_3bit_nc", 64).slot_bytes == 64
+    # fp8: 128 + 128 code bytes + 6 scale bytes, padded to 16 (vs 512 bytes of bf16 K + V)
+    assert tq.tq_format("fp8", 128).slot_bytes == 272
+    assert tq.tq_format("fp8_e4m3", 64).slot_bytes == 144
     with pytest.raises(ValueError):
-        tq.tq_format("fp8", 128)
+        tq.tq_format("fp4", 128)
 
 
-@pytest.mark.parametrize("name,kerr,verr", [("turboquant_k8v4", 0.05, 0.2),
+@pytest.mark.parametrize("name,kerr,verr", [("fp8", 0.05, 0.05), ("turboquant_k8v4", 0.05, 0.2),
                                             ("turboquant_4bit_nc", 0.15, 0.2),
                                             ("turboquant_k3v4_nc", 0.25, 0.2),
                                             ("turboquant_3bit_nc", 0.25, 0.4)])
@@ -112,7 +115,7 @@ def test_tiny_llama_with_turboquant_cache(name):
     # first sampled step (prefill logits) stays close to the bf16-cache model
     a, b = logits[0].flatten(), base_logits[0].flatten()
     cos = torch.nn.functional.cosine_similarity(a, b, dim=0).item()
-    assert cos > (0.99 if name == "turboquant_k8v4" else 0.95), cos
+    assert cos > (0.99 if name in ("turboquant_k8v4", "fp8", "fp8_e4m3") else 0.95), cos
     assert not math.isnan(cos)
 
 

@@ -104,7 +104,7 @@ def test_tq_dequant_pages_matches_oracle(name):
     assert bt2.cpu().tolist() == [[0, 1, 2, 3, 4], [5, 6, 7, 8, 9]]
 
 
-@pytest.mark.parametrize("name", ["turboquant_k8v4", "turboquant_4bit_nc"])
+@pytest.mark.parametrize("name", ["turboquant_k8v4", "turboquant_4bit_nc", "fp8"])
 def test_tiny_llama_generates_on_turboquant_cache(name):
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.models.presets import tiny_llama

@@ -1,6 +1,8 @@
 """TurboQuant-style quantised KV cache: formats, store / decode / dequant ops.
 
-Cache dtypes (the names the reference's backend accepts, vllm_musa/v1/attention/backends/
+Cache dtypes: ``fp8`` / ``fp8_e4m3`` (e4m3 keys and values, one fp16 scale per vector: vLLM's
+fp8 KV cache surface, reference flash_attn.py:349-370) and the names the reference's TurboQuant
+backend accepts (vllm_musa/v1/attention/backends/
 turboquant.py:69-75): ``turboquant_k8v4`` (e4m3 keys, 4-bit values), ``turboquant_4bit_nc``,
 ``turboquant_k3v4_nc``, ``turboquant_3bit_nc`` (Lloyd-Max keys after a randomised Hadamard
 rotation, uniform values, norm correction).  The slot format, the rotation and the level
@@ -18,6 +20,9 @@ from . import _ext
 
 # name -> (key bits, value bits, norm correction)
 PRESETS = {
+    # e4m3 keys and values with one fp16 scale per vector: the "fp8" KV cache
+    "fp8": (8, 8, False),
+    "fp8_e4m3": (8, 8, False),
     "turboquant_k8v4": (8, 4, False),
     "turboquant_4bit_nc": (4, 4, True),
     "turboquant_k3v4_nc": (3, 4, True),
@@ -173,16 +178,24 @@ def quantize_vectors(k: torch.Tensor, v: torch.Tensor, fmt: TQFormat) -> torch.T
             ksc = norm / math.sqrt(D)
         ksc = ksc.to(torch.float16).float()
         kcodes = _pack(idx, fmt.key_bits)
-    L = (1 << fmt.value_bits) - 1
-    vmin, vmax = v.amin(-1), v.amax(-1)
-    vsc = ((vmax - vmin) / L).to(torch.float16).float()
-    vz = vmin.to(torch.float16).float()
-    safe = torch.where(vsc > 0, vsc, torch.ones_like(vsc))
-    vc = torch.round((v - vz[:, None]) / safe[:, None]).clamp(0, L)
-    vc = torch.where(vsc[:, None] > 0, vc, torch.zeros_like(vc)).long()
+    if fmt.value_bits == 8:  # e4m3 values, per-vector scale amax / 448
+        vsc = (v.abs().amax(-1) / 448.0).to(torch.float16).float()
+        vz = torch.zeros_like(vsc)
+        safe = torch.where(vsc > 0, vsc, torch.ones_like(vsc))
+        x = torch.where(vsc[:, None] > 0, v / safe[:, None], torch.zeros_like(v))
+        vcodes = x.clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+    else:
+        L = (1 << fmt.value_bits) - 1
+        vmin, vmax = v.amin(-1), v.amax(-1)
+        vsc = ((vmax - vmin) / L).to(torch.float16).float()
+        vz = vmin.to(torch.float16).float()
+        safe = torch.where(vsc > 0, vsc, torch.ones_like(vsc))
+        vc = torch.round((v - vz[:, None]) / safe[:, None]).clamp(0, L)
+        vc = torch.where(vsc[:, None] > 0, vc, torch.zeros_like(vc)).long()
+        vcodes = _pack(vc, fmt.value_bits)
     out = torch.zeros(N, fmt.slot_bytes, dtype=torch.uint8, device=k.device)
     out[:, :fmt.key_bytes] = kcodes
-    out[:, fmt.key_bytes:fmt.meta_offset] = _pack(vc, fmt.value_bits)
+    out[:, fmt.key_bytes:fmt.meta_offset] = vcodes
     m = fmt.meta_offset
     out[:, m:m + 2] = _f16_bytes(ksc)
     out[:, m + 2:m + 4] = _f16_bytes(vsc)
@@ -204,6 +217,9 @@ def dequantize_slots(slots: torch.Tensor, fmt: TQFormat, rotated_keys: bool = Fa
         k = lv[_unpack(slots[:, :fmt.key_bytes], fmt.key_bits, D)] * ksc[:, None]
         if not rotated_keys:
             k = unrotate(k)
+    if fmt.value_bits == 8:
+        v = slots[:, fmt.key_bytes:m].contiguous().view(torch.float8_e4m3fn).float() * vsc[:, None]
+        return k, v
     vc = _unpack(slots[:, fmt.key_bytes:m], fmt.value_bits, D).float()
     return k, vc * vsc[:, None] + vz[:, None]
 

@@ -187,7 +187,7 @@ def resolve(config) -> OptimizationContract:
         both(Feature.W4AFP8_EXPERTS)
     if m.family == ModelFamily.HYBRID_GDN and cuda:
         both(Feature.GDN_CHUNKED_PREFILL)
-    if m.kv_cache_dtype.startswith("turboquant") and m.family == ModelFamily.DENSE:
+    if _quantized_kv(m.kv_cache_dtype) and m.family == ModelFamily.DENSE:
         both(Feature.TURBOQUANT_KV)
     if e.pipeline_parallel_size > 1:
         both(Feature.PIPELINE_MICROBATCH)
@@ -203,17 +203,22 @@ def resolve(config) -> OptimizationContract:
     return OptimizationContract(m, e, "-".join(parts), frozenset(sup), frozenset(pref))
 
 
+def _quantized_kv(kv_cache_dtype: str) -> bool:
+    """fp8 (e4m3 keys and values, per-vector scales) or a TurboQuant format."""
+    return kv_cache_dtype.startswith("turboquant") or kv_cache_dtype in ("fp8", "fp8_e4m3")
+
+
 def validate(contract: OptimizationContract) -> None:
     """Fail closed on combinations no path serves."""
     m, e = contract.model, contract.execution
     if e.decode_context_parallel_size > 1 and not m.uses_mla:
         raise ValueError("decode context parallelism is implemented for MLA (DeepSeek) models")
     if m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
-        if not m.kv_cache_dtype.startswith("turboquant"):
+        if not _quantized_kv(m.kv_cache_dtype):
             raise ValueError(f"kv_cache_dtype {m.kv_cache_dtype!r} is not served")
         if m.family != ModelFamily.DENSE or m.uses_mla:
-            raise ValueError("the TurboQuant KV cache serves the dense decoders (no MLA, "
-                             "recurrent or MoE families)")
+            raise ValueError("quantised KV caches (fp8, TurboQuant) serve the dense decoders "
+                             "(no MLA, recurrent or MoE families)")
     if e.speculative_method == "mtp" and m.family != ModelFamily.DEEPSEEK:
         raise ValueError("MTP speculative decoding needs a DeepSeek multi-token-prediction layer")
     if e.speculative_method == "eagle":
