@@ -494,8 +494,11 @@ __global__ void __launch_bounds__(kThreads)
     }
     // scale + causal / window mask
     const int kv0 = chunk * CH;
-    const bool need_mask = p.tree_mask != nullptr ? kv0 + CH > ctx
-                         : p.causal ? (kv0 + CH - 1 > pos0 + tw) || (p.window > 0)
+    // tree rows mask the step's own tokens; zero tree rows (and causal launches) mask by
+    // position
+    const bool causal_cut = (kv0 + CH - 1 > pos0 + tw) || (p.window > 0);
+    const bool need_mask = p.tree_mask != nullptr ? (kv0 + CH > ctx) || causal_cut
+                         : p.causal ? causal_cut
                                     : kv0 + CH > seq_len;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
@@ -505,7 +508,7 @@ __global__ void __launch_bounds__(kThreads)
         if (need_mask) {
           const int kv = kv0 + nt * 8 + 2 * t + (j & 1);
           const int qp = p.causal ? my_pos[j >> 1] : seq_len - 1;
-          if (p.tree_mask != nullptr) {
+          if (p.tree_mask != nullptr && tmask[j >> 1] != 0) {
             const int d = kv - ctx;  // draft index; the context before the drafts is visible
             if (kv >= seq_len || (d >= 0 && (d >= 64 || !((tmask[j >> 1] >> d) & 1ull))))
               v = -INFINITY;

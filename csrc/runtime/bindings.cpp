@@ -24,6 +24,9 @@ static StepBuffers buffers_from(py::dict d) {
   b.seeds = reinterpret_cast<int64_t*>(d["seeds"].cast<uintptr_t>());
   b.steps = p32("steps");
   b.state_slots = d.contains("state_slots") ? p32("state_slots") : nullptr;
+  b.tree_mask = d.contains("tree_mask")
+                    ? reinterpret_cast<int64_t*>(d["tree_mask"].cast<uintptr_t>())
+                    : nullptr;
   b.max_tokens = d["max_tokens"].cast<int>();
   b.max_reqs = d["max_reqs"].cast<int>();
   return b;
@@ -68,6 +71,7 @@ void register_runtime(py::module_& m) {
       .def_readonly("sample_req_ids", &StepPlan::sample_req_ids)
       .def_readonly("sample_counts", &StepPlan::sample_counts)
       .def_readonly("num_spec_tokens", &StepPlan::num_spec_tokens)
+      .def_readonly("tree", &StepPlan::tree)
       .def_readonly("req_ids", &StepPlan::req_ids);
 
   py::class_<Scheduler>(m, "Scheduler")
@@ -92,6 +96,12 @@ void register_runtime(py::module_& m) {
       .def("propose_ngram", &Scheduler::propose_ngram, py::arg("k"), py::arg("n_min") = 1,
            py::arg("n_max") = 4)
       .def("set_draft", &Scheduler::set_draft)
+      .def("set_draft_tree", &Scheduler::set_draft_tree, py::arg("id"), py::arg("tokens"),
+           py::arg("parents"))
+      .def("propose_ngram_tree", &Scheduler::propose_ngram_tree, py::arg("k"),
+           py::arg("n_min") = 1, py::arg("n_max") = 4, py::arg("width") = 2)
+      .def("take_kv_moves", &Scheduler::take_kv_moves)
+      .def("last_path", &Scheduler::last_path)
       .def("decode_request_ids", &Scheduler::decode_request_ids)
       .def("tokens_range", &Scheduler::tokens_range)
       .def("num_tokens", &Scheduler::num_tokens)
@@ -114,6 +124,8 @@ void register_runtime(py::module_& m) {
         d["num_preemptions"] = r->num_preemptions;
         d["num_blocks"] = (int)r->blocks.size();
         d["state_slot"] = r->state_slot;
+        d["draft"] = r->draft;
+        d["draft_parent"] = r->draft_parent;
         return d;
       });
 }

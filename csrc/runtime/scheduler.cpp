@@ -199,6 +199,29 @@ void Scheduler::register_full_blocks(Request& r) {
   }
 }
 
+// Keep the first ``cap`` drafts of a tree and, of those, the ones shallower than ``max_depth``
+// (depth 0 = child of the pending token) whose parent is kept; parents are re-indexed.
+// Returns the depth of every kept draft.
+static std::vector<int> prune_tree(std::vector<int32_t>& tok, std::vector<int32_t>& par,
+                                   int cap, int max_depth) {
+  const int n = std::max(0, std::min((int)tok.size(), cap));
+  std::vector<int> depth(n), remap(n, -1), kept;
+  int m = 0;
+  for (int j = 0; j < n; ++j) {
+    const int p = par[j];
+    depth[j] = p < 0 ? 0 : depth[p] + 1;
+    if (depth[j] >= max_depth || (p >= 0 && remap[p] < 0)) continue;
+    remap[j] = m;
+    tok[m] = tok[j];
+    par[m] = p < 0 ? -1 : remap[p];
+    kept.push_back(depth[j]);
+    ++m;
+  }
+  tok.resize(m);
+  par.resize(m);
+  return kept;
+}
+
 StepPlan Scheduler::schedule() {
   StepPlan plan;
   if (waiting_.empty() && running_.empty()) return plan;
@@ -208,6 +231,8 @@ StepPlan Scheduler::schedule() {
     int start, q;
     bool samples;
     int spec;  // draft tokens appended to a decode
+    bool tree;
+    std::vector<int> depth;  // tree drafts: depth of every node
   };
   std::vector<Item> items;
   items.reserve(running_.size() + 16);
@@ -222,11 +247,21 @@ StepPlan Scheduler::schedule() {
     if (cfg_.long_prefill_threshold > 0 && q > 1) q = std::min(q, cfg_.long_prefill_threshold);
     if (!cfg_.chunked_prefill && q < remaining) continue;
     int spec = 0;
+    bool tree = false;
+    std::vector<int> depth;
     if (remaining == 1 && !r.draft.empty()) {
       // verify drafts: never past the model length or the request's token budget
-      const int room = std::min(cfg_.max_model_len - (int)r.tokens.size(),
-                                r.sp.max_tokens - r.num_output() - 1);
-      spec = std::max(0, std::min({(int)r.draft.size(), budget - 1, room}));
+      const int len_room = cfg_.max_model_len - (int)r.tokens.size();
+      const int tok_room = r.sp.max_tokens - r.num_output() - 1;
+      if (r.draft_parent.empty()) {
+        spec = std::max(0, std::min({(int)r.draft.size(), budget - 1, len_room, tok_room}));
+      } else {
+        // every node takes a KV slot; only paths up to tok_room tokens can be accepted
+        depth = prune_tree(r.draft, r.draft_parent,
+                           std::min({budget - 1, len_room, kMaxTreeDrafts}), tok_room);
+        spec = (int)r.draft.size();
+        tree = spec > 0;
+      }
       q += spec;
     }
     bool self_preempted = false;
@@ -243,7 +278,7 @@ StepPlan Scheduler::schedule() {
     }
     if (self_preempted) break;
     items.push_back({&r, r.num_computed, q, r.num_computed + q - spec == (int)r.tokens.size(),
-                     spec});
+                     spec, tree, std::move(depth)});
     budget -= q;
   }
 
@@ -263,7 +298,8 @@ StepPlan Scheduler::schedule() {
       free_slots_.pop_back();
     }
     running_.push_back(r.id);
-    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size(), 0});
+    items.push_back({&r, r.num_computed, q, r.num_computed + q == (int)r.tokens.size(), 0,
+                     false, {}});
     budget -= q;
   }
 
@@ -275,14 +311,34 @@ StepPlan Scheduler::schedule() {
   buf_.cu_q[0] = 0;
   last_sample_ids_.clear();
   last_sample_counts_.clear();
+  for (const Item& it : items) plan.tree = plan.tree || it.tree;
+  if (plan.tree && buf_.tree_mask == nullptr)
+    throw std::runtime_error("scheduler: draft trees need the tree_mask step buffer");
   for (size_t i = 0; i < items.size(); ++i) {
     Item& it = items[i];
     Request& r = *it.r;
+    r.last_path.clear();
+    const int base = it.q - it.spec;  // step tokens before the drafts
+    uint64_t anc[kMaxTreeDrafts];     // tree drafts: the node and its ancestors (bit = node)
     for (int j = 0; j < it.q; ++j) {
-      const int pos = it.start + j;
-      buf_.input_ids[t] = j < it.q - it.spec ? r.tokens[pos] : r.draft[j - (it.q - it.spec)];
-      buf_.positions[t] = pos;
+      const int pos = it.start + j;  // sequence index = KV slot
+      const int d = j - base;
+      buf_.input_ids[t] = d < 0 ? r.tokens[pos] : r.draft[d];
+      buf_.positions[t] = d >= 0 && it.tree ? it.start + base + it.depth[d] : pos;
       buf_.slot_mapping[t] = r.blocks[pos / bs] * bs + pos % bs;
+      if (plan.tree) {
+        uint64_t m = 0;  // non-tree rows: causal
+        if (it.tree) {
+          if (d >= 0) {
+            const int p = r.draft_parent[d];
+            anc[d] = (1ull << d) | (p >= 0 ? anc[p] : 0ull);
+            m = (anc[d] << 1) | 1ull;  // step token 0 is the pending token
+          } else {
+            m = 1ull;
+          }
+        }
+        buf_.tree_mask[t] = (int64_t)m;
+      }
       ++t;
     }
     buf_.cu_q[i + 1] = t;
@@ -308,7 +364,8 @@ StepPlan Scheduler::schedule() {
         buf_.top_p[s] = r.sp.top_p;
         buf_.min_p[s] = r.sp.min_p;
         buf_.seeds[s] = r.sp.seed;
-        buf_.steps[s] = r.num_output() + j;  // same noise as without speculation
+        // same noise as without speculation: the output index the row's token would take
+        buf_.steps[s] = r.num_output() + (j > 0 && it.tree ? it.depth[j - 1] + 1 : j);
         ++s;
       }
       if (r.sp.temperature > 0.f) plan.all_greedy = false;
@@ -326,6 +383,7 @@ StepPlan Scheduler::schedule() {
       spec_proposed_ += it.spec;
     } else {
       r.draft.clear();
+      r.draft_parent.clear();
     }
     r.num_computed = seq_len;
     register_full_blocks(r);
@@ -344,6 +402,7 @@ std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, i
     throw std::runtime_error("scheduler.update: expected " + std::to_string(rows) +
                              " sampled rows, got " + std::to_string(n));
   std::vector<std::pair<int64_t, int>> finished;
+  kv_moves_.clear();
   int row = 0;
   for (size_t k = 0; k < last_sample_ids_.size(); ++k) {
     const int cnt = last_sample_counts_[k];
@@ -354,20 +413,46 @@ std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, i
     Request& r = itr->second;
     if (r.status != kRunning) continue;  // aborted or preempted while in flight
     // tokens this step contributes: accepted drafts, then the token drawn at the first
-    // position whose draft was rejected (or after the last draft)
+    // position whose draft was rejected (or after the last draft).  rows[j] = sampling row of
+    // the j-th contributed token.
     int accept = 0;
     const int d = cnt - 1;
-    while (accept < d && (int32_t)y[accept] == r.draft[accept]) ++accept;
+    const bool tree = d > 0 && !r.draft_parent.empty();
+    std::vector<int> rows(1, 0);
+    r.last_path.clear();
+    if (tree) {
+      // walk down the tree: the child whose token equals the token drawn at its parent
+      int cur = -1;
+      for (;;) {
+        const int32_t want = (int32_t)y[cur + 1];
+        int next = -1;
+        for (int c = cur + 1; c < d; ++c)
+          if (r.draft_parent[c] == cur && r.draft[c] == want) {
+            next = c;
+            break;
+          }
+        if (next < 0) break;
+        r.last_path.push_back(next);
+        rows.push_back(next + 1);
+        cur = next;
+      }
+      accept = (int)r.last_path.size();
+    } else {
+      while (accept < d && (int32_t)y[accept] == r.draft[accept]) ++accept;
+      for (int j = 1; j <= accept; ++j) rows.push_back(j);
+    }
+    const int spec_start = r.spec_start;
     if (d > 0) {
       spec_accepted_ += accept;
       // KV is valid for the pending token and the accepted drafts only
       r.num_computed = r.spec_start + 1 + accept;
       r.draft.clear();
+      r.draft_parent.clear();
       r.spec_start = -1;
     }
     FinishReason why = kNotFinished;
     for (int j = 0; j <= accept && why == kNotFinished; ++j) {
-      const int32_t tok = (int32_t)y[j];
+      const int32_t tok = (int32_t)y[rows[j]];
       r.tokens.push_back(tok);
       if (r.first_token_step < 0) r.first_token_step = step_;
       const int out = r.num_output();
@@ -382,6 +467,17 @@ std::vector<std::pair<int64_t, int>> Scheduler::update(const int64_t* sampled, i
     }
     if (d > 0) {
       r.num_computed = std::min(r.num_computed, (int)r.tokens.size() - 1);
+      if (tree && why == kNotFinished) {
+        // accepted node k sits at slot spec_start + 1 + node; its token now has index
+        // spec_start + 1 + k (sources never precede destinations, so the copies are ordered)
+        const int bs = cfg_.block_size;
+        for (int k = 0; k < accept; ++k) {
+          const int dst = spec_start + 1 + k, src = spec_start + 1 + r.last_path[k];
+          if (src == dst || dst >= r.num_computed) continue;
+          kv_moves_.emplace_back((int64_t)r.blocks[src / bs] * bs + src % bs,
+                                 (int64_t)r.blocks[dst / bs] * bs + dst % bs);
+        }
+      }
       register_full_blocks(r);
     }
     if (why != kNotFinished) {
@@ -430,6 +526,97 @@ void Scheduler::set_draft(int64_t id, const std::vector<int32_t>& draft) {
   auto it = reqs_.find(id);
   if (it == reqs_.end() || it->second.status != kRunning) return;
   it->second.draft = draft;
+  it->second.draft_parent.clear();
+}
+
+void Scheduler::set_draft_tree(int64_t id, const std::vector<int32_t>& tokens,
+                               const std::vector<int32_t>& parents) {
+  if (tokens.size() != parents.size())
+    throw std::invalid_argument("set_draft_tree: tokens and parents differ in length");
+  if ((int)tokens.size() > kMaxTreeDrafts)
+    throw std::invalid_argument("set_draft_tree: at most 63 draft nodes");
+  for (size_t j = 0; j < parents.size(); ++j)
+    if (parents[j] < -1 || parents[j] >= (int)j)
+      throw std::invalid_argument("set_draft_tree: every parent must precede its child");
+  auto it = reqs_.find(id);
+  if (it == reqs_.end() || it->second.status != kRunning) return;
+  it->second.draft = tokens;
+  it->second.draft_parent = parents;
+  // a one-node-per-level tree in order is a chain: verify it without a mask
+  bool chain = true;
+  for (size_t j = 0; j < parents.size() && chain; ++j) chain = parents[j] == (int)j - 1;
+  if (chain) it->second.draft_parent.clear();
+}
+
+std::vector<std::pair<int64_t, int64_t>> Scheduler::take_kv_moves() {
+  std::vector<std::pair<int64_t, int64_t>> out;
+  out.swap(kv_moves_);
+  return out;
+}
+
+std::vector<int32_t> Scheduler::last_path(int64_t id) const {
+  auto it = reqs_.find(id);
+  return it == reqs_.end() ? std::vector<int32_t>{} : it->second.last_path;
+}
+
+int Scheduler::propose_ngram_tree(int k, int n_min, int n_max, int width) {
+  k = std::min(k, kMaxTreeDrafts);
+  int total = 0;
+  for (int64_t id : running_) {
+    Request& r = reqs_.at(id);
+    r.draft.clear();
+    r.draft_parent.clear();
+    const int L = (int)r.tokens.size();
+    if (L - r.num_computed != 1 || k <= 0 || width <= 0) continue;
+    const int32_t* tk = r.tokens.data();
+    // continuation starts of the chosen occurrences, distinct as k-token strings
+    std::vector<int> from;
+    for (int n = std::min(n_max, L - 1); n >= n_min && (int)from.size() < width; --n) {
+      for (int st = L - n - 1; st >= 0 && (int)from.size() < width; --st) {
+        if (!std::equal(tk + st, tk + st + n, tk + L - n)) continue;
+        const int f = st + n, len = std::min(k, L - f);
+        bool dup = false;
+        for (int g : from) {
+          const int lg = std::min(k, L - g);
+          if (lg >= len && std::equal(tk + f, tk + f + len, tk + g)) dup = true;
+        }
+        if (!dup) from.push_back(f);
+      }
+    }
+    if (from.empty()) continue;
+    // merge level by level: node of every continuation at the current depth
+    std::vector<int> at(from.size(), -1);
+    for (int depth = 0; (int)r.draft.size() < k; ++depth) {
+      bool grew = false;
+      for (size_t c = 0; c < from.size() && (int)r.draft.size() < k; ++c) {
+        if (at[c] == -2 || from[c] + depth >= L) continue;
+        const int32_t tok = tk[from[c] + depth];
+        int node = -1;
+        for (int j = 0; j < (int)r.draft.size(); ++j)
+          if (r.draft_parent[j] == at[c] && r.draft[j] == tok) {
+            node = j;
+            break;
+          }
+        if (node < 0) {
+          node = (int)r.draft.size();
+          r.draft.push_back(tok);
+          r.draft_parent.push_back(at[c]);
+        }
+        at[c] = node;
+        grew = true;
+      }
+      // continuations that ran out stop; the rest continue at the next depth
+      for (size_t c = 0; c < from.size(); ++c)
+        if (at[c] != -2 && from[c] + depth + 1 >= L) at[c] = -2;
+      if (!grew) break;
+    }
+    bool chain = true;
+    for (size_t j = 0; j < r.draft_parent.size() && chain; ++j)
+      chain = r.draft_parent[j] == (int)j - 1;
+    if (chain) r.draft_parent.clear();
+    total += (int)r.draft.size();
+  }
+  return total;
 }
 
 int Scheduler::propose_ngram(int k, int n_min, int n_max) {

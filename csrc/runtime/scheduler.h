@@ -49,6 +49,10 @@ struct Request {
   SamplingCfg sp;
   int32_t state_slot = -1;      // per-request recurrent-state slot (hybrid models)
   std::vector<int32_t> draft;   // speculative tokens proposed for the next step
+  // Token tree of the drafts: parent index of every draft (-1 = child of the pending token,
+  // otherwise an earlier draft).  Empty = the drafts form one chain.
+  std::vector<int32_t> draft_parent;
+  std::vector<int32_t> last_path;  // drafts accepted by the last verification (tree order)
   int spec_start = -1;          // first position of the in-flight verification step
   int64_t first_token_step = -1;
   int64_t finish_step = -1;
@@ -110,6 +114,10 @@ struct StepBuffers {
   int64_t* seeds;         // [max_reqs]
   int32_t* steps;         // [max_reqs]  output index of the token being drawn
   int32_t* state_slots;   // [max_reqs]  recurrent-state slot of every scheduled request
+  // [max_tokens] per-token attention masks of steps that verify a draft tree (null: no tree
+  // verification): bit j of a tree request's row lets it see the request's step token j; a
+  // zero row is plain causal
+  int64_t* tree_mask;
   int max_tokens, max_reqs;
 };
 
@@ -125,6 +133,7 @@ struct StepPlan {
   bool all_greedy = true;
   bool any_filter = false;  // some row uses top-k / top-p / min-p
   int num_spec_tokens = 0;  // draft tokens under verification this step
+  bool tree = false;        // some request verifies a draft tree: tree_mask is filled
   std::vector<int64_t> sample_req_ids;
   std::vector<int32_t> sample_counts;  // sampling rows per request (1 + drafts)
   std::vector<int64_t> req_ids;        // every scheduled request, in step-buffer order
@@ -149,6 +158,22 @@ class Scheduler {
   // followed by its continuation.  Returns the number of drafts set.
   int propose_ngram(int k, int n_min, int n_max);
   void set_draft(int64_t id, const std::vector<int32_t>& draft);
+  // Draft tree: tokens in an order where every parent precedes its children (parents[j] in
+  // [-1, j); -1 = child of the pending token), at most kMaxTreeDrafts nodes.  A verification
+  // step runs the pending token and every node (position = pending + 1 + depth, KV slot =
+  // pending + 1 + node index, attention over the context and the node's ancestors); update()
+  // follows the drawn tokens down the tree and moves the KV of the accepted path into place.
+  void set_draft_tree(int64_t id, const std::vector<int32_t>& tokens,
+                      const std::vector<int32_t>& parents);
+  // Prompt lookup with several continuations: the continuations of up to ``width`` earlier
+  // occurrences of the context's suffix n-gram (longest n first, most recent first, duplicates
+  // skipped) merged into a token trie, level by level, of at most k nodes.
+  int propose_ngram_tree(int k, int n_min, int n_max, int width);
+  // KV copies (source slot, destination slot) that the last update() needs: the accepted path
+  // of a draft tree moved to consecutive slots.  Must run before the next step's forward.
+  std::vector<std::pair<int64_t, int64_t>> take_kv_moves();
+  std::vector<int32_t> last_path(int64_t id) const;
+  static constexpr int kMaxTreeDrafts = 63;  // + the pending token = 64 mask bits
   std::vector<int64_t> decode_request_ids() const;  // running requests with one token pending
   // tokens[start, start + n) of a request (clipped to what exists), and its token count
   std::vector<int32_t> tokens_range(int64_t id, int start, int n) const;
@@ -183,6 +208,7 @@ class Scheduler {
   std::vector<int64_t> running_;
   std::vector<int64_t> last_sample_ids_;
   std::vector<int32_t> last_sample_counts_;
+  std::vector<std::pair<int64_t, int64_t>> kv_moves_;
   int64_t spec_accepted_ = 0, spec_proposed_ = 0;
   std::vector<int32_t> free_slots_;
   void release_slot(Request& r);

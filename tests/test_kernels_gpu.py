@@ -443,6 +443,41 @@ def test_encoder_varlen_attention():
     torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
 
 
+def test_paged_prefill_tree_mask_with_causal_rows():
+    """A tree-verification step batching prefill chunks: zero mask rows are causal (a chunk of
+    150 queries, longer than the 64 mask bits, and a short one) beside two draft trees."""
+    from vllm_musa_b200.ops.attention import tree_ancestor_masks
+    D, Hq, Hkv, bs = 128, 8, 2, 64
+    trees = [[-1, -1, 0, 1, 1, 2], None, [-1, 0, 0], None]
+    qlens = [7, 150, 4, 9]
+    ctxs = [90, 40, 200, 0]
+    R = len(qlens)
+    lens = [c + q for c, q in zip(ctxs, qlens)]
+    nb = sum((l + bs - 1) // bs for l in lens) + 4
+    kc, vc = _make_cache(nb, Hkv, bs, D, seed=85)
+    bt = _random_tables(R, lens, bs, nb, seed=7)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(qlens), 0)), dtype=torch.int32)
+    T = int(cu[-1])
+    parts = []
+    for t, ql in zip(trees, qlens):
+        if t is None:
+            parts.append(torch.zeros(ql, dtype=torch.int64))
+        else:  # step token 0 = the pending token, then the drafts
+            parts.append(torch.cat([torch.ones(1, dtype=torch.int64),
+                                    (tree_ancestor_masks(t) << 1) | 1]))
+    masks = torch.cat(parts)
+    q = _bf(T, (Hq + 2 * Hkv) * D, seed=86)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1.0 / math.sqrt(D)
+    ref = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale,
+                            tree_mask=masks)
+    plain = ops.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), cu, sl, bt, Hq, Hkv, scale)
+    torch.testing.assert_close(ref[7:157], plain[7:157])  # zero rows = causal (oracle check)
+    out = ops.paged_prefill(q, kc, vc, cu.to(DEV), sl.to(DEV), bt.to(DEV), Hq, Hkv, scale,
+                            tree_mask=masks.to(DEV))
+    torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
 def test_paged_prefill_tree_mask():
     """Speculative token trees on the prefill kernel: per-row ancestor masks over the drafts."""
     from vllm_musa_b200.ops.attention import tree_ancestor_masks

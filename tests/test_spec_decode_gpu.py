@@ -69,3 +69,41 @@ def test_eagle_head_on_gpu_keeps_tokens():
             want = ref.logits(p + toks[:k])[-1]
             gap = float(want.max() - want[t]) / float(want.abs().max())
             assert gap < 0.03, (k, gap)
+
+
+def test_oracle_tree_drafts_compact_kv_on_gpu():
+    """Draft trees whose right continuation is on a non-first branch (nodes 1 -> 3 -> 4): the
+    tree-masked verification, the accepted-path KV copies and the next steps keep the plain
+    greedy tokens (up to bf16 near-ties) while cutting the step count."""
+    from vllm_musa_b200 import LLM, SamplingParams
+    from vllm_musa_b200.models.presets import tiny_llama
+    cfg = tiny_llama()
+    cfg.dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (20, 64, 100)]
+    sp = SamplingParams(temperature=0.0, max_tokens=30, ignore_eos=True)
+    kw = dict(block_size=64, seed=0, num_gpu_blocks=64, max_model_len=512, max_num_seqs=8,
+              max_num_batched_tokens=256, enforce_eager=True)
+    plain = [o.outputs[0].token_ids for o in LLM(cfg, **kw).generate(prompts, sp)]
+    llm = LLM(cfg, **kw)
+    eng = llm.engine
+    for i, p in enumerate(prompts):
+        eng.add_request(f"r{i}", p, sp)
+    iids = {eng._by_name[f"r{i}"]: i for i in range(3)}
+    outs = {}
+    while eng.has_unfinished_requests():
+        for iid in eng.scheduler.decode_request_ids():
+            done = len(eng.scheduler.output_tokens(iid))
+            right = plain[iids[iid]][done:done + 3]
+            if len(right) < 3:
+                continue
+            wrong = [(t + 1) % 1024 for t in right]
+            eng.scheduler.set_draft_tree(iid, [wrong[0], right[0], wrong[1], right[1], right[2],
+                                               wrong[2]], [-1, -1, 1, 1, 3, 0])
+        for o in eng.step():
+            outs[o.request_id] = o.outputs[0].token_ids
+    got = [outs[f"r{i}"] for i in range(3)]
+    agree = sum(a == b for x, y in zip(got, plain) for a, b in zip(x, y)) / sum(map(len, plain))
+    assert agree > 0.9, agree
+    assert eng.num_steps < 20
+    assert eng.scheduler.spec_accepted() > 0

@@ -46,7 +46,8 @@ class PagedAttention:
             ops.paged_prefill(q, k_cache, v_cache, meta.prefill_cu_q, meta.prefill_seq_lens,
                               meta.prefill_block_tables, self.hq, self.hkv, self.scale,
                               self.window or meta.sliding_window, out=out,
-                              tile_scratch=meta.tile_scratch, sinks=self.sinks)
+                              tile_scratch=meta.tile_scratch, sinks=self.sinks,
+                              tree_mask=meta.tree_mask)
         return out
 
 

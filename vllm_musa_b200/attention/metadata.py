@@ -30,6 +30,8 @@ class AttnMetadata:
     sliding_window: int = 0
     state_slots: Optional[torch.Tensor] = None  # int32 [R] recurrent-state slot per request
     lora: Optional[object] = None  # LoRABatch: token groups per adapter slot (lora.py)
+    # int64 [T] draft-tree attention masks (steps verifying a token tree; 0 = causal row)
+    tree_mask: Optional[torch.Tensor] = None
 
     @property
     def prefill_cu_q(self) -> torch.Tensor:

@@ -258,12 +258,39 @@ class SpeculativeConfig:
     the latest earlier occurrence of the context's suffix n-gram, n in [prompt_lookup_min,
     prompt_lookup_max]); ``mtp``: the checkpoint's multi-token-prediction layer (DeepSeek);
     ``eagle``: an EAGLE-1 head over a dense decoder, loaded from ``model`` (a safetensors
-    directory) or, without one, seeded random weights."""
+    directory) or, without one, seeded random weights.
+
+    Token trees (``tree_width`` > 1): ``ngram`` merges the continuations of up to
+    ``tree_width`` earlier occurrences of the suffix into a trie of at most
+    ``num_speculative_tokens`` nodes; ``eagle`` proposes the head's top ``tree_width`` tokens as
+    siblings.  vLLM's ``speculative_token_tree`` (a list of child-index paths such as
+    ``"[(0,), (1,), (2,)]"``) is accepted for one-level trees and sets ``tree_width``.  The
+    whole tree is verified in one step under per-node ancestor masks."""
     method: Optional[str] = None  # None | "ngram" | "mtp" | "eagle"
     num_speculative_tokens: int = 0
     model: Optional[str] = None
     prompt_lookup_min: int = 1
     prompt_lookup_max: int = 4
+    tree_width: int = 1
+    speculative_token_tree: Optional[str] = None
+
+    def __post_init__(self):
+        if self.speculative_token_tree:
+            import ast
+            paths = ast.literal_eval(self.speculative_token_tree) \
+                if isinstance(self.speculative_token_tree, str) else self.speculative_token_tree
+            paths = [tuple(p) for p in paths]
+            if not paths or any(len(p) != 1 for p in paths) or \
+                    sorted(p[0] for p in paths) != list(range(len(paths))):
+                raise ValueError("speculative_token_tree: one-level trees [(0,), (1,), ...] "
+                                 "are served")
+            self.tree_width = len(paths)
+        if self.tree_width < 1:
+            raise ValueError("tree_width must be >= 1")
+
+    @property
+    def tree(self) -> bool:
+        return self.tree_width > 1
 
     @staticmethod
     def from_dict(d: Optional[dict]) -> "SpeculativeConfig":

@@ -158,10 +158,12 @@ class LLMEngine:
         self._profiler = None
         if config.speculative.method == "mtp":
             from .spec_decode import MTPDrafter
-            self.drafter = MTPDrafter(self, config.speculative.num_speculative_tokens or 1)
+            self.drafter = MTPDrafter(self, config.speculative.num_speculative_tokens or 1,
+                                      config.speculative.tree_width)
         elif config.speculative.method == "eagle":
             from .spec_decode import EagleDrafter
-            self.drafter = EagleDrafter(self, config.speculative.num_speculative_tokens or 1)
+            self.drafter = EagleDrafter(self, config.speculative.num_speculative_tokens or 1,
+                                        config.speculative.tree_width)
         self.runner.capture_graphs()
         self._ids = itertools.count()
         self._reqs: Dict[int, _Req] = {}
@@ -298,10 +300,20 @@ class LLMEngine:
                 return []
         spec = self.config.speculative
         if spec.method == "ngram" and spec.num_speculative_tokens > 0:
-            self.scheduler.propose_ngram(spec.num_speculative_tokens, spec.prompt_lookup_min,
-                                         spec.prompt_lookup_max)
+            if spec.tree:
+                self.scheduler.propose_ngram_tree(spec.num_speculative_tokens,
+                                                  spec.prompt_lookup_min, spec.prompt_lookup_max,
+                                                  spec.tree_width)
+            else:
+                self.scheduler.propose_ngram(spec.num_speculative_tokens,
+                                             spec.prompt_lookup_min, spec.prompt_lookup_max)
         elif spec.method in ("mtp", "eagle") and self.drafter is not None:
             self.drafter.propose(self.scheduler)
+        if self._special and spec.method is not None:
+            # penalties, log-probabilities and grammars are applied per drawn token: requests
+            # that use them decode without drafts
+            for iid in self._special:
+                self.scheduler.set_draft(iid, [])
         plan = self.scheduler.schedule()
         if plan.num_reqs == 0:
             return []
@@ -312,6 +324,8 @@ class LLMEngine:
         if extras is not None and extras.mask_rows:
             self._advance_grammars(plan, extras, sampled)
         finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
+        if plan.tree:  # accepted tree paths: KV rows to consecutive slots before the next step
+            self.runner.apply_kv_moves(self.scheduler.take_kv_moves())
         if self._special:
             finished = self._match_stop_strings(plan, finished)
         now = time.time()
@@ -355,10 +369,13 @@ class LLMEngine:
         rep = torch.ones(S)
         pres = torch.zeros(S)
         freq = torch.zeros(S)
-        for row, iid in enumerate(plan.sample_req_ids):
+        row_req, nxt = {}, 0
+        for iid, cnt in zip(plan.sample_req_ids, plan.sample_counts):
+            row, nxt = nxt, nxt + cnt  # the request's first sampling row
             r = self._special.get(iid)
             if r is None:
                 continue
+            row_req[row] = iid
             p = r.params
             if r.matcher is not None:
                 mask_rows.append(row)
@@ -380,6 +397,7 @@ class LLMEngine:
         bitmask = self._grammar_backend().bitmask(matchers) if matchers else None
         ex = StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
         ex.lora = lora
+        ex.row_req = row_req
         return ex
 
     def _lora_batch(self, plan):
@@ -425,7 +443,7 @@ class LLMEngine:
     def _advance_grammars(self, plan, extras, sampled) -> None:
         """Feed each constrained request's sampled token to its matcher."""
         for row in extras.mask_rows:
-            r = self._reqs.get(plan.sample_req_ids[row])
+            r = self._reqs.get(extras.row_req[row])
             if r is None or r.matcher is None:
                 continue
             tok = int(sampled[row])
@@ -436,7 +454,7 @@ class LLMEngine:
         from ..outputs import Logprob
         ids, vals, tok_lp, rank = (t.tolist() for t in extras.logprobs)
         for j, row in enumerate(extras.lp_rows):
-            r = self._reqs.get(plan.sample_req_ids[row])
+            r = self._reqs.get(extras.row_req[row])
             if r is None or r.logprobs is None:
                 continue
             tok = int(sampled[row])

@@ -41,7 +41,7 @@ class StepBuffers:
               ("block_tables", "bt", _I32), ("logits_idx", "smp", _I32),
               ("temperature", "smp", _F32), ("top_k", "smp", _I32), ("top_p", "smp", _F32),
               ("min_p", "smp", _F32), ("seeds", "smp", _I64), ("steps", "smp", _I32),
-              ("state_slots", "req", _I32)]
+              ("state_slots", "req", _I32), ("tree_mask", "tok", _I64)]
     # sampling rows: one per request, or 1 + drafts under speculative verification; never
     # more than the step's tokens
 
@@ -66,7 +66,8 @@ class StepBuffers:
     def bt2d(self, which: str = "d") -> torch.Tensor:
         return getattr(self, which)["block_tables"].view(self.max_reqs, self.max_blocks)
 
-    def upload(self, n_tok: int, n_req: int, n_sample: int, sampling: bool) -> int:
+    def upload(self, n_tok: int, n_req: int, n_sample: int, sampling: bool,
+               tree: bool = False) -> int:
         """Copy the used prefixes host->device.  Returns the number of bytes copied."""
         if self.device.type != "cuda":
             return 0
@@ -85,6 +86,8 @@ class StepBuffers:
         cp("state_slots", n_req)
         cp("block_tables", n_req * self.max_blocks)
         cp("logits_idx", n_sample)
+        if tree:
+            cp("tree_mask", n_tok)
         if sampling:
             for name in ("temperature", "top_k", "top_p", "min_p", "seeds", "steps"):
                 cp(name, n_sample)
@@ -105,6 +108,7 @@ class StepExtras:
         self.bitmask = bitmask
         self.mask_rows = mask_rows or []
         self.lora = None  # LoRABatch of the step (adapters in use)
+        self.row_req = {}  # sampling row -> request id of the rows above
         self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
 
 
@@ -226,6 +230,26 @@ class ModelRunner:
         self.kv_caches = [(self.kv_tensor[i, 0], self.kv_tensor[i, 1])
                           for i in range(spec["num_layers"])]
 
+    def apply_kv_moves(self, moves) -> None:
+        """Copy KV rows between cache slots (slot = block * block_size + offset) in every layer:
+        the accepted path of a verified draft tree moved to consecutive positions.  All rows
+        are gathered before any is written (a destination may be another move's source)."""
+        if not moves:
+            return
+        bs = self.block_size
+        src = torch.tensor([m[0] for m in moves], dtype=torch.long)
+        dst = torch.tensor([m[1] for m in moves], dtype=torch.long)
+        sb, so = (src // bs).to(self.device), (src % bs).to(self.device)
+        db, do = (dst // bs).to(self.device), (dst % bs).to(self.device)
+        if self.kv_tensor is not None:  # [L, 2, blocks, Hkv, bs, D]: one gather + one scatter
+            rows = self.kv_tensor[:, :, sb, :, so]
+            self.kv_tensor[:, :, db, :, do] = rows
+            return
+        for kc, vc in self.kv_caches:  # per-layer [blocks, Hkv, bs, D] pairs
+            for c in (kc, vc):
+                rows = c[sb, :, so]
+                c[db, :, do] = rows
+
     # ------------------------------------------------------------------ forward
     def _forward_sample(self, T: int, R: int, S: int, meta: AttnMetadata, sampling: bool,
                         any_filter: bool, decode_only: bool = False) -> torch.Tensor:
@@ -301,6 +325,8 @@ class ModelRunner:
                          sliding_window=meta.sliding_window,
                          state_slots=None if meta.state_slots is None
                          else meta.state_slots[r0:r1])
+        if meta.tree_mask is not None:
+            m.tree_mask = meta.tree_mask[t0:t1]
         if meta.lora is not None:  # adapter token groups re-based to the micro-batch
             from ..lora import LoRABatch
             groups = []
@@ -490,9 +516,11 @@ class ModelRunner:
             ids = out[:S]
         else:
             sampling = not plan.all_greedy
-            self.h2d_bytes += b.upload(T, R, S, sampling)
+            self.h2d_bytes += b.upload(T, R, S, sampling, plan.tree)
             meta = self._meta(T, R, nd, npf, plan.max_seq_len)
             meta.lora = extras.lora if extras is not None else None
+            if plan.tree:
+                meta.tree_mask = b.d["tree_mask"][:T]
             ids = self._forward_sample(T, R, S, meta, sampling=sampling,
                                        any_filter=plan.any_filter, decode_only=decode_only)
         self._extras = None

@@ -8,7 +8,9 @@ token is now known: position p combines the embedding of token p+1 with the main
 hidden state at p, writes the draft layer's KV for p (extra cache layer ``num_layers``, same
 block table and slots as the main model), and its logits predict token p+2.  The prediction
 made at the position just before the request's pending token becomes the draft the scheduler
-verifies in the next step (exact acceptance, see csrc/runtime/scheduler.cpp).  Positions of rejected
+verifies in the next step (exact acceptance, see csrc/runtime/scheduler.cpp); with a tree
+width w > 1 the top w predictions are verified together as sibling nodes of a token tree, and
+the hidden state of the accepted node feeds the next draft.  Positions of rejected
 drafts are skipped: their main-model KV and hidden states are stale and get overwritten.
 
 Reference counterparts: vllm_musa/v1/spec_decode/utils.py:4-124 (eagle / MTP input
@@ -25,7 +27,7 @@ class ModelDrafter:
     """One-token drafts from a draft layer: ``forward(ids, prev_hidden, meta, kv_caches)`` ->
     hidden rows, ``logits(hidden)`` -> this rank's vocab shard of the draft logits."""
 
-    def __init__(self, engine, forward, logits, num_tokens: int = 1):
+    def __init__(self, engine, forward, logits, num_tokens: int = 1, tree_width: int = 1):
         if num_tokens != 1:
             raise ValueError("model-based drafters propose one token per step")
         self.engine = engine
@@ -33,6 +35,7 @@ class ModelDrafter:
         self.runner = engine.runner
         self.forward = forward
         self.logits = logits
+        self.tree_width = tree_width  # > 1: the top tree_width tokens, verified as siblings
         self.proposed = 0
 
     def propose(self, scheduler) -> None:
@@ -48,7 +51,9 @@ class ModelDrafter:
             return
         cu = h["cu_q"][:plan.num_reqs + 1].tolist()
         pos_all = h["positions"][:plan.num_tokens]
-        rows, next_ids, cus, lens, req_rows, who = [], [], [0], [], [], []
+        # rows: step rows whose KV slot now holds positions start.. (consecutive after the
+        # accepted path of a draft tree was compacted); hid_rows: the rows that computed them
+        rows, hid_rows, pos, next_ids, cus, lens, req_rows, who = [], [], [], [], [0], [], [], []
         for i, rid in enumerate(plan.req_ids):
             n_tok = sch.num_tokens(rid)
             if n_tok == 0:
@@ -58,8 +63,15 @@ class ModelDrafter:
             last = min(start + q - 1, n_tok - 2)  # positions whose next token is known
             if last < start:
                 continue
-            nxt = sch.tokens_range(rid, start + 1, last - start + 1)
-            rows.extend(range(cu[i], cu[i] + (last - start + 1)))
+            n = last - start + 1
+            nxt = sch.tokens_range(rid, start + 1, n)
+            rows.extend(range(cu[i], cu[i] + n))
+            path = sch.last_path(rid) if plan.tree else []
+            if path:
+                hid_rows.extend([cu[i]] + [cu[i] + 1 + j for j in path[:n - 1]])
+            else:
+                hid_rows.extend(range(cu[i], cu[i] + n))
+            pos.extend(range(start, start + n))
             next_ids.extend(nxt)
             cus.append(cus[-1] + len(nxt))
             lens.append(last + 1)
@@ -71,7 +83,7 @@ class ModelDrafter:
         rows_t = torch.tensor(rows, dtype=torch.long, device=dev)
         T = len(rows)
         ids = torch.tensor(next_ids, dtype=torch.int32, device=dev)
-        positions = b.d["positions"][:plan.num_tokens][rows_t].contiguous()
+        positions = torch.tensor(pos, dtype=torch.int32, device=dev)
         slots = b.d["slot_mapping"][:plan.num_tokens][rows_t].contiguous()
         rr = torch.tensor(req_rows, dtype=torch.long, device=dev)
         bt = b.bt2d()[:plan.num_reqs][rr].contiguous()
@@ -81,10 +93,21 @@ class ModelDrafter:
         meta = AttnMetadata(T, 0, R, positions, slots, sl, bt, cu_t, max_seq_len=max(lens),
                             tile_scratch=self.runner.tile_scratch,
                             state_slots=b.d["state_slots"][:R])
-        prev = hidden[rows_t]
+        prev = hidden[torch.tensor(hid_rows, dtype=torch.long, device=dev)]
         x = self.forward(ids, prev, meta, self.runner.kv_caches)
         last_rows = torch.tensor([c - 1 for c in cus[1:]], dtype=torch.long, device=dev)
         logits = self.logits(x[last_rows])
+        if self.tree_width > 1:
+            smp = self.runner.sampler
+            if smp.tp > 1:  # vocab-sharded rows: the full distribution
+                logits = smp.comm.all_gather(logits, dim=1)
+            logits = logits[:, :self.model.cfg.vocab_size]
+            top = torch.topk(logits.float(), self.tree_width, dim=-1).indices.cpu().tolist()
+            for k, (rid, ready) in enumerate(who):
+                if ready:
+                    sch.set_draft_tree(rid, [int(t) for t in top[k]], [-1] * self.tree_width)
+                    self.proposed += self.tree_width
+            return
         draft = self.runner.sampler(logits, None, None, None, None, None, None).cpu().tolist()
         for k, (rid, ready) in enumerate(who):
             if ready:
@@ -93,7 +116,7 @@ class ModelDrafter:
 
 
 class MTPDrafter(ModelDrafter):
-    def __init__(self, engine, num_tokens: int = 1):
+    def __init__(self, engine, num_tokens: int = 1, tree_width: int = 1):
         model = engine.model
         if getattr(model, "mtp", None) is None:
             raise ValueError("speculative method 'mtp' needs a checkpoint with an MTP layer "
@@ -101,12 +124,13 @@ class MTPDrafter(ModelDrafter):
         n = model.cfg.num_layers
         super().__init__(engine, lambda ids, prev, meta, kv: model.forward_mtp(ids, prev, meta,
                                                                               kv[n]),
-                         model.compute_logits_mtp, num_tokens)
+                         model.compute_logits_mtp, num_tokens, tree_width)
 
 
 class EagleDrafter(ModelDrafter):
-    def __init__(self, engine, num_tokens: int = 1):
+    def __init__(self, engine, num_tokens: int = 1, tree_width: int = 1):
         head = getattr(engine.model, "draft_head", None)
         if head is None:
             raise ValueError("speculative method 'eagle' needs an EAGLE head on the model")
-        super().__init__(engine, head.forward_draft, head.compute_logits, num_tokens)
+        super().__init__(engine, head.forward_draft, head.compute_logits, num_tokens,
+                         tree_width)

@@ -125,7 +125,8 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     (``causal=False``: every query sees the whole sequence, as encoders need).
 
     ``tree_mask`` int64 [T] (speculative token trees): bit j of row t lets query t see draft j
-    of its request (its last q_len <= 64 tokens); the cached context stays visible.
+    of its request (its last q_len <= 64 tokens); the cached context stays visible.  A zero row
+    is an ordinary causal row (prefill chunks and chains batched with a tree).
 
     q: [T, >= Hq*D] for the prefill tokens (request r owns rows cu_q[r]:cu_q[r+1]); the K/V
     of those tokens must already be in the cache.  ``sinks`` as in ``paged_decode``.
@@ -165,6 +166,10 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
             j = torch.arange(n) - ctx
             allowed = (j[None, :] < 0) | ((j[None, :] < 64) & (j[None, :] >= 0) &
                                           (((bits >> j.clamp(0, 63)[None, :]) & 1) == 1))
+            causal_rows = torch.arange(n)[None, :] <= pos[:, None]
+            if window > 0:
+                causal_rows &= torch.arange(n)[None, :] > pos[:, None] - window
+            allowed = torch.where(bits == 0, causal_rows, allowed)
         o = _attend_ref(qr, k, v, pos, scale, window, sinks, causal, allowed)
         out[a:b] = o.reshape(b - a, Hq * D).to(out.dtype)
     return out

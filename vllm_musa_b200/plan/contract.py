@@ -46,6 +46,7 @@ class Feature(str, Enum):
     SPARSE_INDEXER = "deepseek.sparse_indexer"
     MTP = "spec.mtp"
     EAGLE = "spec.eagle"
+    SPEC_TREE = "spec.token_tree"
     PIPELINE_MICROBATCH = "pp.microbatched_stages"
     GDN_CHUNKED_PREFILL = "gdn.chunked_prefill"
     W4AFP8_EXPERTS = "moe.w4afp8_experts"
@@ -83,6 +84,7 @@ class ExecutionSignature:
     enforce_eager: bool
     block_size: int
     max_num_seqs: int
+    speculative_tree: bool = False
 
 
 @dataclass(frozen=True)
@@ -139,7 +141,8 @@ def execution_signature(config) -> ExecutionSignature:
         enable_expert_parallel=p.enable_expert_parallel,
         use_custom_allreduce=p.use_custom_allreduce,
         speculative_method=config.speculative.method, enforce_eager=config.enforce_eager,
-        block_size=config.cache.block_size, max_num_seqs=config.scheduler.max_num_seqs)
+        block_size=config.cache.block_size, max_num_seqs=config.scheduler.max_num_seqs,
+        speculative_tree=config.speculative.tree)
 
 
 def resolve(config) -> OptimizationContract:
@@ -183,6 +186,8 @@ def resolve(config) -> OptimizationContract:
             both(Feature.MTP)
     if m.family == ModelFamily.DENSE and e.speculative_method == "eagle":
         both(Feature.EAGLE)
+    if e.speculative_tree:
+        both(Feature.SPEC_TREE)
     if m.quant == "w4afp8" and m.num_experts:
         both(Feature.W4AFP8_EXPERTS)
     if m.family == ModelFamily.HYBRID_GDN and cuda:
@@ -234,5 +239,11 @@ def validate(contract: OptimizationContract) -> None:
                              "or decode context parallelism")
         if m.num_layers < e.pipeline_parallel_size:
             raise ValueError("pipeline_parallel_size exceeds the number of layers")
+    if e.speculative_tree:
+        if e.speculative_method not in ("ngram", "eagle"):
+            raise ValueError("token trees are proposed by the ngram and eagle drafters")
+        if m.family != ModelFamily.DENSE or m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
+            raise ValueError("token-tree verification runs the paged bf16 attention of the "
+                             "dense decoders (Llama / Qwen)")
     if e.speculative_method not in (None, "ngram", "mtp", "eagle"):
         raise ValueError(f"speculative method {e.speculative_method!r} is not served")
