@@ -347,6 +347,34 @@ def case_mamba2(it):
     report("mamba2_decode", [B, H, P, N], us, 2 * B * H * P * N * 4, 6 * B * H * P * N)
 
 
+def case_mamba2_prefill(it):
+    """Mamba2 SSD over 2 x 4096 new tokens (Mamba2-2.7B: 80 heads of 64, state 128, 1 group):
+    chunked kernels (chunk states, state pass, chunk scan) and, for comparison, the token
+    recurrence."""
+    from vllm_musa_b200.ops import mamba as M
+    R, L, H, G, P, N = 2, 4096, 80, 1, 64, 128
+    T = R * L
+    xbc = bf16(T, H * P + 2 * G * N, scale=0.5)
+    dt = bf16(T, H)
+    dtb, Alog, D = (torch.rand(H, device="cuda") for _ in range(3))
+    st = torch.zeros(R, H, P, N, device="cuda")
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")
+    sl = torch.full((R,), L, dtype=torch.int32, device="cuda")
+    slots = torch.arange(R, dtype=torch.int32, device="cuda")
+    out = torch.empty(T, H * P, dtype=torch.bfloat16, device="cuda")
+    # matrix-form FLOPs per chunk and head: Sc = x^T B (C P N), C S0^T (C N P), C B^T (C^2 N),
+    # G x (C^2 P)
+    C = 64
+    flops = 2 * (T // C) * H * (2 * C * P * N + C * C * N + C * C * P)
+    nbytes = T * (H * P + 2 * G * N + H) * 2 + T * H * P * 2
+    us = timed(lambda i: M.mamba2_chunked(xbc, H * P, H * P + G * N, dt, dtb, Alog, D, st, cu,
+                                          sl, slots, H, G, P, N, out=out), it)
+    report("mamba2_chunked_prefill", [R, L, H, P, N], us, nbytes, flops)
+    us = timed(lambda i: M.mamba2_scan(xbc, H * P, H * P + G * N, dt, dtb, Alog, D, st, cu, sl,
+                                       slots, H, G, P, N, out=out), max(2, it // 4))
+    report("mamba2_recurrent_prefill", [R, L, H, P, N], us, nbytes, flops)
+
+
 def case_rmsnorm(it):
     T, H = 32768, 4096
     x, r = bf16(T, H), bf16(T, H)

@@ -197,6 +197,12 @@ struct Mamba2Args {
   float dt_min, dt_max;
 };
 void run_mamba2_scan(const Mamba2Args& a, cudaStream_t s);
+// Chunked SSD prefill (64-token chunks, three launches; same contract as run_mamba2_scan).
+// T = tokens of the batch; workspaces sized by mamba2_chunked_max_chunks(T, R).
+bool mamba2_chunked_supported(int P, int N, int64_t ld_xbc, int b_off, int c_off, int64_t ld_y);
+size_t mamba2_chunked_max_chunks(int T, int R);
+void run_mamba2_chunked(const Mamba2Args& a, int T, int32_t* chunk_offsets, float* states,
+                        float* decay, cudaStream_t s);
 // out = RMSNorm over groups of `group` channels of (y * silu(z)), times w
 void run_gated_rmsnorm(void* out, int64_t ld_o, const void* y, int64_t ld_y, const void* z,
                        int64_t ld_z, const void* w, int T, int C, int group, float eps,

@@ -926,10 +926,12 @@ void causal_conv1d(const Tensor& x, const Tensor& w, Tensor& state, const Tensor
   });
 }
 
-void mamba2_scan(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& dt,
-                 const Tensor& dt_bias, const Tensor& A_log, const Tensor& D, Tensor& state,
-                 const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots, Tensor& y,
-                 int64_t H, int64_t G, int64_t P, int64_t N, double dt_min, double dt_max) {
+static b200::mamba::Mamba2Args mamba2_args(const Tensor& xbc, int64_t b_off, int64_t c_off,
+                                           const Tensor& dt, const Tensor& dt_bias,
+                                           const Tensor& A_log, const Tensor& D, Tensor& state,
+                                           const Tensor& cu_q, const Tensor& seq_lens,
+                                           const Tensor& slots, Tensor& y, int64_t H, int64_t G,
+                                           int64_t P, int64_t N, double dt_min, double dt_max) {
   CHECK_CUDA(xbc);
   CHECK_BF16(xbc);
   CHECK_ROWMAJOR(xbc);
@@ -949,7 +951,6 @@ void mamba2_scan(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& 
   TORCH_CHECK(cu_q.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
                   slots.scalar_type() == at::kInt,
               "mamba2: int32 metadata");
-  const c10::cuda::CUDAGuard g(xbc.device());
   b200::mamba::Mamba2Args a{};
   a.xbc = xbc.data_ptr();
   a.ld_xbc = xbc.stride(0);
@@ -973,7 +974,49 @@ void mamba2_scan(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& 
   a.N = N;
   a.dt_min = dt_min;
   a.dt_max = dt_max;
+  return a;
+}
+
+void mamba2_scan(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& dt,
+                 const Tensor& dt_bias, const Tensor& A_log, const Tensor& D, Tensor& state,
+                 const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots, Tensor& y,
+                 int64_t H, int64_t G, int64_t P, int64_t N, double dt_min, double dt_max) {
+  const c10::cuda::CUDAGuard g(xbc.device());
+  const auto a = mamba2_args(xbc, b_off, c_off, dt, dt_bias, A_log, D, state, cu_q, seq_lens,
+                             slots, y, H, G, P, N, dt_min, dt_max);
   guarded([&] { b200::mamba::run_mamba2_scan(a, stream_of(xbc)); });
+}
+
+// Chunked SSD prefill (csrc/scan/mamba2_chunked.cu): ``num_tokens`` = cu_q[R] - cu_q[0];
+// workspaces chunk_offsets int32 [R+1], states fp32 [max_chunks * H * P * N], decay fp32
+// [max_chunks * H] with max_chunks = ceil(num_tokens / 64) + R.
+void mamba2_chunked(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& dt,
+                    const Tensor& dt_bias, const Tensor& A_log, const Tensor& D, Tensor& state,
+                    const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots, Tensor& y,
+                    int64_t H, int64_t G, int64_t P, int64_t N, double dt_min, double dt_max,
+                    Tensor& chunk_offsets, Tensor& states, Tensor& decay, int64_t num_tokens) {
+  const c10::cuda::CUDAGuard g(xbc.device());
+  const auto a = mamba2_args(xbc, b_off, c_off, dt, dt_bias, A_log, D, state, cu_q, seq_lens,
+                             slots, y, H, G, P, N, dt_min, dt_max);
+  const size_t mc = b200::mamba::mamba2_chunked_max_chunks((int)num_tokens, a.R);
+  TORCH_CHECK(chunk_offsets.scalar_type() == at::kInt && chunk_offsets.numel() >= a.R + 1,
+              "mamba2_chunked: chunk_offsets [R+1] int32");
+  TORCH_CHECK(states.scalar_type() == at::kFloat && states.is_contiguous() &&
+                  (size_t)states.numel() >= mc * H * P * N,
+              "mamba2_chunked: states workspace too small");
+  TORCH_CHECK(decay.scalar_type() == at::kFloat && (size_t)decay.numel() >= mc * H,
+              "mamba2_chunked: decay workspace too small");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(xbc.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(states.data_ptr()) % 16 == 0,
+              "mamba2_chunked: 16-byte aligned xbc / states");
+  TORCH_CHECK(b200::mamba::mamba2_chunked_supported((int)P, (int)N, a.ld_xbc, a.b_off, a.c_off,
+                                                    a.ld_y),
+              "mamba2_chunked: head_dim 32/64, state 64/128, rows of multiples of 8 elements");
+  guarded([&] {
+    b200::mamba::run_mamba2_chunked(a, (int)num_tokens, chunk_offsets.data_ptr<int32_t>(),
+                                    states.data_ptr<float>(), decay.data_ptr<float>(),
+                                    stream_of(xbc));
+  });
 }
 
 void gated_rmsnorm(Tensor& out, const Tensor& y, const Tensor& z, const Tensor& w, int64_t group,
@@ -1624,6 +1667,11 @@ TORCH_LIBRARY(b200, m) {
       "mamba2_scan(Tensor xbc, int b_off, int c_off, Tensor dt, Tensor dt_bias, Tensor A_log, "
       "Tensor D, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, Tensor slots, Tensor(b!) y, "
       "int H, int G, int P, int N, float dt_min, float dt_max) -> ()");
+  m.def(
+      "mamba2_chunked(Tensor xbc, int b_off, int c_off, Tensor dt, Tensor dt_bias, "
+      "Tensor A_log, Tensor D, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, Tensor slots, "
+      "Tensor(b!) y, int H, int G, int P, int N, float dt_min, float dt_max, "
+      "Tensor(c!) chunk_offsets, Tensor(d!) states, Tensor(e!) decay, int num_tokens) -> ()");
   m.def("gated_rmsnorm(Tensor(a!) out, Tensor y, Tensor z, Tensor w, int group, float eps) -> ()");
   m.def(
       "gdn_recurrent(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
@@ -1674,6 +1722,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("moe_combine", &moe_combine);
   m.impl("causal_conv1d", &causal_conv1d);
   m.impl("mamba2_scan", &mamba2_scan);
+  m.impl("mamba2_chunked", &mamba2_chunked);
   m.impl("gated_rmsnorm", &gated_rmsnorm);
   m.impl("gdn_recurrent", &gdn_recurrent);
   m.impl("gdn_chunked", &gdn_chunked);

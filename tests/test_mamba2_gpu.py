@@ -46,6 +46,40 @@ def test_scan_kernel(H, G, P, N):
     torch.testing.assert_close(st_gpu.cpu(), st_ref, rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("H,G,P,N", [(8, 1, 64, 128), (16, 4, 64, 64), (4, 2, 32, 128),
+                                     (6, 3, 32, 64)])
+def test_chunked_scan_kernels(H, G, P, N):
+    """Chunked SSD kernels (chunk states, state pass, chunk scan) against the fp32 token
+    recurrence on CPU: one-token, multi-chunk, exactly-one-chunk and one-past-a-chunk
+    requests, with and without cached states."""
+    g = torch.Generator().manual_seed(H * N + P)
+    lens = [(0, 1), (0, 300), (20, 64), (7, 65), (0, 129)]
+    T = sum(n for _, n in lens)
+    xbc = (torch.randn(T, H * P + 2 * G * N, generator=g) * 0.5).to(torch.bfloat16)
+    dt = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    dtb = torch.randn(H, generator=g) * 0.5
+    Alog = torch.rand(H, generator=g) * 2
+    D = torch.randn(H, generator=g)
+    st = torch.randn(6, H, P, N, generator=g) * 0.1
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor([n for _, n in lens]), 0)),
+                      dtype=torch.int32)
+    sl = torch.tensor([c + n for c, n in lens], dtype=torch.int32)
+    slots = torch.tensor([3, 0, 5, 1, 2], dtype=torch.int32)
+    st_ref = st.clone()
+    ref = M.mamba2_scan(xbc, H * P, H * P + G * N, dt, dtb, Alog, D, st_ref, cu, sl, slots,
+                        H, G, P, N, 0.0, 10.0)
+    st_gpu = st.to(DEV)
+    out = M.mamba2_chunked(xbc.to(DEV), H * P, H * P + G * N, dt.to(DEV), dtb.to(DEV),
+                           Alog.to(DEV), D.to(DEV), st_gpu, cu.to(DEV), sl.to(DEV),
+                           slots.to(DEV), H, G, P, N, 0.0, 10.0)
+    torch.cuda.synchronize()
+    _ext.check_device_errors()
+    err = (out.cpu().float() - ref.float()).abs()
+    scale = ref.float().abs().max()
+    assert float(err.max()) < 0.03 * float(scale) + 0.03, (float(err.max()), float(scale))
+    torch.testing.assert_close(st_gpu.cpu(), st_ref, rtol=2e-2, atol=2e-2)
+
+
 def test_gated_rmsnorm_and_conv_bias():
     g = torch.Generator().manual_seed(9)
     T, C, group = 19, 512, 128

@@ -57,6 +57,9 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
     EnvFlag("B200_DEBUG_BOUNDS", False, _bool,
             "check index tensors (KV slots, block tables, row indices) against the kernels' "
             "bounds at every op call and raise IndexError (synchronises: debugging only)"),
+    EnvFlag("B200_MAMBA_CHUNKED", True, _bool,
+            "Mamba2 prefill parts of >= 64 tokens through the chunked SSD kernels (off: the "
+            "token recurrence for every request)"),
     EnvFlag("B200_SKIP_NVLINK_CHECK", False, _bool,
             "build the peer-memory communicator without the NVML NVLink full-mesh check"),
     EnvFlag("B200_AR_NVLS", True, _bool,

@@ -62,6 +62,9 @@ class Mamba2ForCausalLM:
         self.group = self.dI // G  # norm group (channels per group, same on every rank)
         self.conv_dim = self.dI_l + 2 * self.G_l * self.N
         self.dt_off = self.dI_l + self.conv_dim
+        from .. import envs
+        self.chunked = mamba_ops.mamba2_chunked_supported(self.P, self.N) and \
+            envs.get("B200_MAMBA_CHUNKED")
         self.in_width = (self.dt_off + self.H_l + 63) // 64 * 64  # 128-byte aligned rows
         if cfg.vocab_size % self.tp:
             raise ValueError("vocab_size must be divisible by tensor_parallel_size")
@@ -169,16 +172,29 @@ class Mamba2ForCausalLM:
             xbc = gdn_ops.causal_conv1d(zx[:, self.dI_l:], L.conv_w, self.conv_state[i],
                                         meta.cu_q, meta.seq_lens, meta.state_slots,
                                         bias=L.conv_b)
-            y = mamba_ops.mamba2_scan(xbc, self.dI_l, self.dI_l + self.G_l * self.N,
-                                      zx[:, self.dt_off:], L.dt_bias, L.A_log, L.D,
-                                      self.ssm_state[i], meta.cu_q, meta.seq_lens,
-                                      meta.state_slots, self.H_l, self.G_l, self.P, self.N,
-                                      cfg.mamba_dt_min, cfg.mamba_dt_max)
+            y = self._scan(i, L, xbc, zx, meta, T)
             g = mamba_ops.gated_rmsnorm(y, zx, L.norm_w, self.group, eps)
             o = ops.linear(g, L.out_w, out=self.comm.out_buffer(T))
             nxt = self.layers[i + 1].norm if i + 1 < n else self.final_norm
             x, residual = self.comm.allreduce_add_rmsnorm(o, residual, nxt, eps)
         return x
+
+    def _scan(self, i, L, xbc, zx, meta, T):
+        """SSD scan of one layer: decode rows through the token recurrence, a prefill part of
+        at least CHUNK_MIN_TOKENS tokens through the chunked kernels."""
+        cfg = self.cfg
+        nd, npf = meta.num_decodes, meta.num_prefills
+        args = (xbc, self.dI_l, self.dI_l + self.G_l * self.N, zx[:, self.dt_off:], L.dt_bias,
+                L.A_log, L.D, self.ssm_state[i])
+        geo = (self.H_l, self.G_l, self.P, self.N, cfg.mamba_dt_min, cfg.mamba_dt_max)
+        sl, slots = meta.seq_lens, meta.state_slots
+        if T - nd < mamba_ops.CHUNK_MIN_TOKENS or not self.chunked:
+            return mamba_ops.mamba2_scan(*args, meta.cu_q, sl, slots, *geo)
+        y = torch.empty(T, self.H_l * self.P, dtype=xbc.dtype, device=xbc.device)
+        if nd > 0:
+            mamba_ops.mamba2_scan(*args, meta.cu_q[:nd + 1], sl[:nd], slots[:nd], *geo, out=y)
+        return mamba_ops.mamba2_chunked(*args, meta.cu_q[nd:nd + npf + 1], sl[nd:nd + npf],
+                                        slots[nd:nd + npf], *geo, out=y, num_tokens=T - nd)
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         return ops.linear(hidden, self.lm_head, out_dtype=torch.float32)
