@@ -261,6 +261,31 @@ def case_moe(it):
            2 * T * k * 3 * H * I)
 
 
+def case_moe_small(it):
+    """Routed bf16 experts at decode batch sizes (Qwen3-30B-A3B at TP1: 128 experts, top-8,
+    hidden 2048, expert intermediate 768): per-pair GEMVs against align + gather + grouped
+    GEMMs, for the dispatch threshold."""
+    import os
+    from vllm_musa_b200.ops import moe
+    E, k, H, I = 128, 8, 2048, 768
+    w_gu = bf16(E * 2 * I, H, scale=0.02)
+    w_dn = bf16(E * H, I, scale=0.02)
+    for T in (1, 2, 4, 8, 16, 32, 64):
+        x = bf16(T, H)
+        # 16 routings in turn: the experts they touch (1.2 GB in all) do not stay in L2
+        routes = [moe.topk_softmax(torch.randn(T, E, device="cuda"), k) for _ in range(16)]
+        live = sum(int(torch.unique(r[0]).numel()) for r in routes) / len(routes)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        nbytes = live * 3 * H * I * 2
+        for name, limit in (("gemv", 1 << 20), ("grouped", 0)):
+            os.environ["B200_MOE_GEMV_MAX_PAIRS"] = str(limit)
+            us = timed(lambda i: moe.fused_moe(x, w_gu, w_dn, routes[i % 16][0], routes[i % 16][1],
+                                               E, None, out=out), it)
+            report(f"fused_moe_{name}", [T, E, k, H, I, round(live, 1)], us, nbytes,
+                   2 * T * k * 3 * H * I)
+    os.environ.pop("B200_MOE_GEMV_MAX_PAIRS", None)
+
+
 def case_rope_kv(it):
     """Fused RoPE + paged KV insert over one 8192-token prefill chunk (Llama-3-8B heads)."""
     T, Hq, Hkv, D, bs = 8192, 32, 8, 128, 64

@@ -139,6 +139,13 @@ void run_moe_gather(const void* x, int64_t ldx, const int32_t* sorted_ids, const
 void run_moe_combine(const void* y, const int32_t* pos, const float* w, int T, int k, int H,
                      const void* shared, const float* shared_gate, int64_t ld_gate, void* out,
                      int64_t ldo, cudaStream_t s);
+// Routed bf16 experts for a few tokens as per-(token, slot) GEMVs: h = SwiGLU(x W_gu_e^T)
+// [T*k, I], y = h W_down_e^T [T*k, H], pos [T, k] = pair index or -1 (expert not local);
+// combine with run_moe_combine.  w_gu / w_down in the grouped-GEMM layouts.
+bool moe_gemv_supported(int H, int I);
+void run_moe_gemv(const void* x, int64_t ldx, const int32_t* ids, int T, int k, int E, int e0,
+                  const void* w_gu, const void* w_down, int H, int I, void* h, void* y,
+                  int32_t* pos, cudaStream_t s);
 }  // namespace moe
 
 // ------------------------------------------------------------------------------- norms
@@ -202,7 +209,7 @@ void run_mamba2_scan(const Mamba2Args& a, cudaStream_t s);
 bool mamba2_chunked_supported(int P, int N, int64_t ld_xbc, int b_off, int c_off, int64_t ld_y);
 size_t mamba2_chunked_max_chunks(int T, int R);
 void run_mamba2_chunked(const Mamba2Args& a, int T, int32_t* chunk_offsets, float* states,
-                        float* decay, cudaStream_t s);
+                        void* start_bf16, float* decay, cudaStream_t s);
 // out = RMSNorm over groups of `group` channels of (y * silu(z)), times w
 void run_gated_rmsnorm(void* out, int64_t ld_o, const void* y, int64_t ld_y, const void* z,
                        int64_t ld_z, const void* w, int T, int C, int group, float eps,

@@ -11,10 +11,10 @@
 //   ssd_chunk_state_kernel  one CTA per (chunk, head), all chunks in parallel: Sc as an mma.sync
 //                           product (x^T scaled by the decay weights) x B, [P, N] fp32 to the
 //                           workspace, and the chunk's total decay e^{a_Q}.
-//   ssd_state_pass_kernel   one CTA per (request, head): walks the request's chunks in order,
-//                           replaces each chunk's Sc by the state at its start (elementwise
-//                           S = e^{a_Q} S + Sc, [P, N] spread over 256 threads), writes the final
-//                           state to the request's slot.
+//   ssd_state_pass_kernel   one CTA per (request, head, 1024 state elements): walks the
+//                           request's chunks in order (elementwise S = e^{a_Q} S + Sc in fp32),
+//                           writes each chunk's start state in bf16 (the scan's operand) and
+//                           the final state to the request's slot.
 //   ssd_chunk_scan_kernel   one CTA per (chunk, head), all chunks in parallel: three tensor-core
 //                           products per warp (16 rows of the chunk): C S0^T (scaled by e^{a_i}),
 //                           G = C B^T masked to j <= i and weighted by e^{a_i - a_j} dt_j in
@@ -37,12 +37,12 @@ namespace {
 
 constexpr int kQ = 64;          // chunk length (tokens)
 constexpr int kThreads = 128;   // chunk kernels: 4 warps of 16 rows
-constexpr int kPassThreads = 256;
 
 struct SsdParams {
   Mamba2Args a;
   int32_t* chunk_offsets;  // [R+1] first chunk of every request
-  float* states;           // [max_chunks, H, P, N]: chunk contributions, then chunk-start states
+  float* states;           // [max_chunks, H, P, N] fp32 chunk contributions Sc
+  __nv_bfloat16* start_bf16;  // [max_chunks, H, P, N] chunk-start states (the scan's operand)
   float* decay;            // [max_chunks, H]: e^{a_Q} of every chunk
   int max_chunks;
 };
@@ -73,16 +73,14 @@ B200_DEVICE uint32_t sw_elem(uint32_t base, int row, int col) {
   return mma::sw128(base, row, col >> 3) + ((col & 7) << 1);
 }
 
-B200_DEVICE void st_bf16(uint32_t addr, float v) {
-  const __nv_bfloat16 b = f2bf(v);
-  asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(*reinterpret_cast<const uint16_t*>(&b)));
-}
-
 B200_DEVICE float ld_bf16(uint32_t addr) {
   uint16_t u;
   asm volatile("ld.shared.b16 %0, [%1];" : "=h"(u) : "r"(addr));
   return __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(&u));
 }
+
+// cp_async16 takes a generic pointer to the shared destination
+B200_DEVICE void* smem_ptr(uint32_t addr) { return __cvta_shared_to_generic(addr); }
 
 B200_DEVICE void st_16(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
@@ -118,10 +116,14 @@ B200_DEVICE void chunk_gates(const Mamba2Args& a, int t0, int n, int h, float A,
 }
 
 // ------------------------------------------------------------------------------ chunk states
+// Staging: every global row goes to shared memory with cp.async (16-byte pieces, the token-major
+// rows as they are: x [j][p], B [j][n]; rows past the chunk zero-filled), all issued before the
+// gates are computed so the loads overlap them.  The MMA reads both operands K-major (k = token)
+// through transposing ldmatrix.
 template <int P, int N>
 __global__ void __launch_bounds__(kThreads) ssd_chunk_state_kernel(SsdParams p) {
-  __shared__ __align__(1024) __nv_bfloat16 sXw[P * 64];  // [p][j] x_j[p] e^{a_Q - a_j} dt_j
-  __shared__ __align__(1024) __nv_bfloat16 sBT[N * 64];  // [n][j] B_j[n]
+  __shared__ __align__(1024) __nv_bfloat16 sX[kQ * 64];       // [j][p] (128-byte rows)
+  __shared__ __align__(1024) __nv_bfloat16 sB[kQ * N];        // [j][n], N / 64 halves
   __shared__ float sdt[kQ], sac[kQ], wtot;
   const Mamba2Args& a = p.a;
   const int chunk = blockIdx.x, h = blockIdx.y;
@@ -130,35 +132,44 @@ __global__ void __launch_bounds__(kThreads) ssd_chunk_state_kernel(SsdParams p) 
   const int t0 = a.cu_q[r] + (chunk - p.chunk_offsets[r]) * kQ;
   const int n = min(kQ, a.cu_q[r + 1] - t0);
   const int g = h / (a.H / a.G);
+  const __nv_bfloat16* xbc = reinterpret_cast<const __nv_bfloat16*>(a.xbc);
+  const uint32_t bX = smem_u32(sX), bB = smem_u32(sB);
+  constexpr int kHalf = kQ * 128;
+  const int tid = threadIdx.x;
+  for (int e = tid; e < kQ * (P / 8); e += kThreads) {
+    const int j = e / (P / 8), c = e % (P / 8);
+    const __nv_bfloat16* src = xbc + (size_t)(t0 + (j < n ? j : 0)) * a.ld_xbc + h * P + c * 8;
+    cp_async16(smem_ptr(mma::sw128(bX, j, c)), src, j < n);
+  }
+  for (int e = tid; e < kQ * (N / 8); e += kThreads) {
+    const int j = e / (N / 8), c = e % (N / 8);
+    const __nv_bfloat16* src =
+        xbc + (size_t)(t0 + (j < n ? j : 0)) * a.ld_xbc + a.b_off + g * N + c * 8;
+    cp_async16(smem_ptr(mma::sw128(bB + (c >> 3) * kHalf, j, c & 7)), src, j < n);
+  }
+  cp_async_commit();
   const float A = -expf(a.A_log[h]);
   chunk_gates(a, t0, n, h, A, a.dt_bias[h], sdt, sac, &wtot);
   const float last = sac[kQ - 1];
-  const __nv_bfloat16* xbc = reinterpret_cast<const __nv_bfloat16*>(a.xbc);
-  const uint32_t bX = smem_u32(sXw), bB = smem_u32(sBT);
-  const int tid = threadIdx.x;
+  cp_async_wait<0>();
+  __syncthreads();
+  // x_j *= e^{a_Q - a_j} dt_j (zero past the chunk), in place
   for (int e = tid; e < kQ * (P / 8); e += kThreads) {
-    const int j = e / (P / 8), pc = e % (P / 8);
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (j < n) {
-      unpack8(*reinterpret_cast<const uint4*>(xbc + (size_t)(t0 + j) * a.ld_xbc + h * P + pc * 8), v);
-      const float w = expf(last - sac[j]) * sdt[j];
+    const int j = e / (P / 8), c = e % (P / 8);
+    const uint32_t ad = mma::sw128(bX, j, c);
+    const float w = expf(last - sac[j]) * sdt[j];
+    uint4 u;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "r"(ad));
+    float v[8];
+    unpack8(u, v);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] *= w;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) st_bf16(sw_elem(bX, pc * 8 + k, j), v[k]);
-  }
-  for (int e = tid; e < kQ * (N / 8); e += kThreads) {
-    const int j = e / (N / 8), nc = e % (N / 8);
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (j < n)
-      unpack8(*reinterpret_cast<const uint4*>(xbc + (size_t)(t0 + j) * a.ld_xbc + a.b_off +
-                                              g * N + nc * 8), v);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) st_bf16(sw_elem(bB, nc * 8 + k, j), v[k]);
+    for (int k = 0; k < 8; ++k) v[k] *= w;
+    st_16(ad, pack8(v));
   }
   __syncthreads();
-  // Sc [P][N] = sXw [P][64] * sBT^T: warp -> 16 rows (p) x NT n-tiles
+  // Sc [P][N] = Xw^T B: warp -> 16 rows (p) x NT n-tiles; A = Xw^T and B both K-major (k = j)
   constexpr int MT = P / 16, WPM = 4 / MT, NT = (N / 8) / WPM;
   const int warp = tid >> 5, lane = tid & 31, gq = lane >> 2, t = lane & 3;
   const int mt = warp % MT, nt0 = (warp / MT) * NT;
@@ -171,13 +182,15 @@ __global__ void __launch_bounds__(kThreads) ssd_chunk_state_kernel(SsdParams p) 
 #pragma unroll
   for (int ks = 0; ks < kQ / 16; ++ks) {
     uint32_t af[4];
-    mma::ldsm_x4(mma::sw128(bX, mt * 16 + (m & 1) * 8 + rr8, ks * 2 + (m >> 1)), af[0], af[1],
-                 af[2], af[3]);
+    mma::ldsm_x4_t(mma::sw128(bX, ks * 16 + (m >> 1) * 8 + rr8, mt * 2 + (m & 1)), af[0],
+                   af[1], af[2], af[3]);
+    const int tok = ks * 16 + (m & 1) * 8 + rr8;
 #pragma unroll
     for (int np = 0; np < NT / 2; ++np) {
+      const int ng = nt0 / 2 + np;  // 16-column group of n
       uint32_t b0, b1, b2, b3;
-      mma::ldsm_x4(mma::sw128(bB, (nt0 / 2 + np) * 16 + (m >> 1) * 8 + rr8, ks * 2 + (m & 1)),
-                   b0, b1, b2, b3);
+      mma::ldsm_x4_t(mma::sw128(bB + (ng >> 2) * kHalf, tok, (ng & 3) * 2 + (m >> 1)), b0, b1,
+                     b2, b3);
       mma::mma_bf16(acc[2 * np], af, b0, b1);
       mma::mma_bf16(acc[2 * np + 1], af, b2, b3);
     }
@@ -195,32 +208,52 @@ __global__ void __launch_bounds__(kThreads) ssd_chunk_state_kernel(SsdParams p) 
 }
 
 // ------------------------------------------------------------------------------- state pass
+// CTA = (request, head, slice of 1024 state elements); thread = 8 consecutive elements.  The
+// next chunk's contribution and decay are loaded before the current chunk's start state is
+// stored, so one load latency per chunk is in flight instead of one per element.
+constexpr int kPassThreads = 128;
+constexpr int kPassSlice = kPassThreads * 8;
+
 template <int P, int N>
 __global__ void __launch_bounds__(kPassThreads) ssd_state_pass_kernel(SsdParams p) {
-  constexpr int E = P * N / kPassThreads;
   const Mamba2Args& a = p.a;
   const int r = blockIdx.x, h = blockIdx.y;
   const int c0 = p.chunk_offsets[r], c1 = p.chunk_offsets[r + 1];
   if (c1 <= c0) return;
+  const int e0 = (blockIdx.z * kPassThreads + threadIdx.x) * 8;
   const int L = a.cu_q[r + 1] - a.cu_q[r];
   const bool hist = a.seq_lens[r] - L > 0;
-  float* st = a.state + ((size_t)a.slots[r] * a.H + h) * P * N;
-  float s[E];
+  float* st = a.state + ((size_t)a.slots[r] * a.H + h) * P * N + e0;
+  float s[8];
+  if (hist) {
+    const float4 lo = *reinterpret_cast<const float4*>(st), hi = *reinterpret_cast<const float4*>(st + 4);
+    s[0] = lo.x; s[1] = lo.y; s[2] = lo.z; s[3] = lo.w;
+    s[4] = hi.x; s[5] = hi.y; s[6] = hi.z; s[7] = hi.w;
+  } else {
 #pragma unroll
-  for (int k = 0; k < E; ++k) s[k] = hist ? st[threadIdx.x + k * kPassThreads] : 0.f;
-  for (int c = c0; c < c1; ++c) {
-    float* blk = p.states + ((size_t)c * a.H + h) * P * N;
-    const float d = p.decay[(size_t)c * a.H + h];
-#pragma unroll
-    for (int k = 0; k < E; ++k) {
-      const int e = threadIdx.x + k * kPassThreads;
-      const float contrib = blk[e];
-      blk[e] = s[k];
-      s[k] = fmaf(s[k], d, contrib);
-    }
+    for (int k = 0; k < 8; ++k) s[k] = 0.f;
   }
+  const size_t stride = (size_t)a.H * P * N;
+  const float* src = p.states + ((size_t)c0 * a.H + h) * P * N + e0;
+  __nv_bfloat16* dst = p.start_bf16 + ((size_t)c0 * a.H + h) * P * N + e0;
+  float4 lo = *reinterpret_cast<const float4*>(src), hi = *reinterpret_cast<const float4*>(src + 4);
+  float d = p.decay[(size_t)c0 * a.H + h];
+  for (int c = c0; c < c1; ++c) {
+    const float f[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    const float dc = d;
+    if (c + 1 < c1) {
+      src += stride;
+      lo = *reinterpret_cast<const float4*>(src);
+      hi = *reinterpret_cast<const float4*>(src + 4);
+      d = p.decay[(size_t)(c + 1) * a.H + h];
+    }
+    *reinterpret_cast<uint4*>(dst) = pack8(s);
+    dst += stride;
 #pragma unroll
-  for (int k = 0; k < E; ++k) st[threadIdx.x + k * kPassThreads] = s[k];
+    for (int k = 0; k < 8; ++k) s[k] = fmaf(s[k], dc, f[k]);
+  }
+  *reinterpret_cast<float4*>(st) = make_float4(s[0], s[1], s[2], s[3]);
+  *reinterpret_cast<float4*>(st + 4) = make_float4(s[4], s[5], s[6], s[7]);
 }
 
 // ------------------------------------------------------------------------------- chunk scan
@@ -231,8 +264,8 @@ struct ScanSmem {
   static constexpr int kC = 0;                   // C  [i][n], N/64 halves
   static constexpr int kB = kC + (N / 64) * kHalfC;   // B  [j][n]
   static constexpr int kS = kB + (N / 64) * kHalfC;   // S0 [p][n] (bf16)
-  static constexpr int kX = kS + (N / 64) * kHalfS;   // x^T [p][j]
-  static constexpr int kF = kX + kHalfS;              // fp32 dt, a, scratch
+  static constexpr int kX = kS + (N / 64) * kHalfS;   // x [j][p] (128-byte rows)
+  static constexpr int kF = kX + kHalfC;              // fp32 dt, a, scratch
   static constexpr int kBytes = kF + (2 * kQ + 4) * 4;
 };
 
@@ -247,41 +280,36 @@ __global__ void __launch_bounds__(kThreads) ssd_chunk_scan_kernel(SsdParams p) {
   const int t0 = a.cu_q[r] + (chunk - p.chunk_offsets[r]) * kQ;
   const int n = min(kQ, a.cu_q[r + 1] - t0);
   const int g = h / (a.H / a.G);
-  const float A = -expf(a.A_log[h]);
   float* sdt = reinterpret_cast<float*>(smem + L::kF);
   float* sac = sdt + kQ;
-  chunk_gates(a, t0, n, h, A, a.dt_bias[h], sdt, sac, sac + kQ);
   const uint32_t base = smem_u32(smem);
   const uint32_t bC = base + L::kC, bB = base + L::kB, bS = base + L::kS, bX = base + L::kX;
   const __nv_bfloat16* xbc = reinterpret_cast<const __nv_bfloat16*>(a.xbc);
   const int tid = threadIdx.x;
+  // cp.async staging of C, B [i][n], the bf16 chunk-start state [p][n] and x [j][p], issued
+  // before the gates so the loads overlap them; rows past the chunk are zero-filled
   for (int e = tid; e < kQ * (N / 8); e += kThreads) {
-    const int i = e / (N / 8), nc = e % (N / 8);
-    uint4 vc = make_uint4(0, 0, 0, 0), vb = vc;
-    if (i < n) {
-      const __nv_bfloat16* row = xbc + (size_t)(t0 + i) * a.ld_xbc + g * N + nc * 8;
-      vb = *reinterpret_cast<const uint4*>(row + a.b_off);
-      vc = *reinterpret_cast<const uint4*>(row + a.c_off);
-    }
-    st_16(mma::sw128(bC + (nc >> 3) * L::kHalfC, i, nc & 7), vc);
-    st_16(mma::sw128(bB + (nc >> 3) * L::kHalfC, i, nc & 7), vb);
+    const int i = e / (N / 8), c = e % (N / 8);
+    const __nv_bfloat16* row = xbc + (size_t)(t0 + (i < n ? i : 0)) * a.ld_xbc + g * N + c * 8;
+    const uint32_t off = (c >> 3) * L::kHalfC;
+    cp_async16(smem_ptr(mma::sw128(bC + off, i, c & 7)), row + a.c_off, i < n);
+    cp_async16(smem_ptr(mma::sw128(bB + off, i, c & 7)), row + a.b_off, i < n);
   }
-  const float* s0 = p.states + ((size_t)chunk * a.H + h) * P * N;
+  const __nv_bfloat16* s0 = p.start_bf16 + ((size_t)chunk * a.H + h) * P * N;
   for (int e = tid; e < P * (N / 8); e += kThreads) {
-    const int pr = e / (N / 8), nc = e % (N / 8);
-    const float4 lo = *reinterpret_cast<const float4*>(s0 + (size_t)pr * N + nc * 8);
-    const float4 hi = *reinterpret_cast<const float4*>(s0 + (size_t)pr * N + nc * 8 + 4);
-    const float f[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    st_16(mma::sw128(bS + (nc >> 3) * L::kHalfS, pr, nc & 7), pack8(f));
+    const int pr = e / (N / 8), c = e % (N / 8);
+    cp_async16(smem_ptr(mma::sw128(bS + (c >> 3) * L::kHalfS, pr, c & 7)),
+               s0 + (size_t)pr * N + c * 8);
   }
   for (int e = tid; e < kQ * (P / 8); e += kThreads) {
-    const int j = e / (P / 8), pc = e % (P / 8);
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (j < n)
-      unpack8(*reinterpret_cast<const uint4*>(xbc + (size_t)(t0 + j) * a.ld_xbc + h * P + pc * 8), v);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) st_bf16(sw_elem(bX, pc * 8 + k, j), v[k]);
+    const int j = e / (P / 8), c = e % (P / 8);
+    const __nv_bfloat16* src = xbc + (size_t)(t0 + (j < n ? j : 0)) * a.ld_xbc + h * P + c * 8;
+    cp_async16(smem_ptr(mma::sw128(bX, j, c)), src, j < n);
   }
+  cp_async_commit();
+  const float A = -expf(a.A_log[h]);
+  chunk_gates(a, t0, n, h, A, a.dt_bias[h], sdt, sac, sac + kQ);
+  cp_async_wait<0>();
   __syncthreads();
 
   const int warp = tid >> 5, lane = tid & 31, gq = lane >> 2, t = lane & 3;
@@ -348,11 +376,11 @@ __global__ void __launch_bounds__(kThreads) ssd_chunk_scan_kernel(SsdParams p) {
     pa[1] = pack_bf16x2(gacc[2 * kk][2], gacc[2 * kk][3]);
     pa[2] = pack_bf16x2(gacc[2 * kk + 1][0], gacc[2 * kk + 1][1]);
     pa[3] = pack_bf16x2(gacc[2 * kk + 1][2], gacc[2 * kk + 1][3]);
+    const int tok = kk * 16 + (m & 1) * 8 + rr8;
 #pragma unroll
     for (int np = 0; np < P / 16; ++np) {
       uint32_t b0, b1, b2, b3;
-      mma::ldsm_x4(mma::sw128(bX, np * 16 + (m >> 1) * 8 + rr8, kk * 2 + (m & 1)), b0, b1, b2,
-                   b3);
+      mma::ldsm_x4_t(mma::sw128(bX, tok, np * 2 + (m >> 1)), b0, b1, b2, b3);
       mma::mma_bf16(acc[2 * np], pa, b0, b1);
       mma::mma_bf16(acc[2 * np + 1], pa, b2, b3);
     }
@@ -367,7 +395,7 @@ __global__ void __launch_bounds__(kThreads) ssd_chunk_scan_kernel(SsdParams p) {
 #pragma unroll
     for (int nt = 0; nt < P / 8; ++nt) {
       const int pc = nt * 8 + 2 * t;
-      const float x0 = ld_bf16(sw_elem(bX, pc, i)), x1 = ld_bf16(sw_elem(bX, pc + 1, i));
+      const float x0 = ld_bf16(sw_elem(bX, i, pc)), x1 = ld_bf16(sw_elem(bX, i, pc + 1));
       *reinterpret_cast<uint32_t*>(dst + pc) =
           pack_bf16x2(fmaf(Dh, x0, acc[nt][2 * rr]), fmaf(Dh, x1, acc[nt][2 * rr + 1]));
     }
@@ -378,7 +406,8 @@ template <int P, int N>
 void launch(const SsdParams& p, cudaStream_t s) {
   const dim3 grid(p.max_chunks, p.a.H);
   ssd_chunk_state_kernel<P, N><<<grid, kThreads, 0, s>>>(p);
-  ssd_state_pass_kernel<P, N><<<dim3(p.a.R, p.a.H), kPassThreads, 0, s>>>(p);
+  static_assert((P * N) % kPassSlice == 0, "state pass slices");
+  ssd_state_pass_kernel<P, N><<<dim3(p.a.R, p.a.H, P * N / kPassSlice), kPassThreads, 0, s>>>(p);
   const int smem = ScanSmem<P, N>::kBytes;
   ensure_dynamic_smem(reinterpret_cast<const void*>(ssd_chunk_scan_kernel<P, N>), smem);
   ssd_chunk_scan_kernel<P, N><<<grid, kThreads, smem, s>>>(p);
@@ -394,7 +423,7 @@ bool mamba2_chunked_supported(int P, int N, int64_t ld_xbc, int b_off, int c_off
 size_t mamba2_chunked_max_chunks(int T, int R) { return (size_t)(T + kQ - 1) / kQ + R; }
 
 void run_mamba2_chunked(const Mamba2Args& a, int T, int32_t* chunk_offsets, float* states,
-                        float* decay, cudaStream_t s) {
+                        void* start_bf16, float* decay, cudaStream_t s) {
   if (a.R == 0 || T == 0) return;
   B200_REQUIRE(mamba2_chunked_supported(a.P, a.N, a.ld_xbc, a.b_off, a.c_off, a.ld_y),
                "mamba2 chunked: head_dim 32/64, state 64/128, 16-byte aligned rows");
@@ -403,6 +432,7 @@ void run_mamba2_chunked(const Mamba2Args& a, int T, int32_t* chunk_offsets, floa
   p.a = a;
   p.chunk_offsets = chunk_offsets;
   p.states = states;
+  p.start_bf16 = reinterpret_cast<__nv_bfloat16*>(start_bf16);
   p.decay = decay;
   p.max_chunks = (int)mamba2_chunked_max_chunks(T, a.R);
   ssd_chunk_offsets_kernel<<<1, 32, 0, s>>>(a.cu_q, a.R, chunk_offsets);

@@ -988,13 +988,14 @@ void mamba2_scan(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& 
 }
 
 // Chunked SSD prefill (csrc/scan/mamba2_chunked.cu): ``num_tokens`` = cu_q[R] - cu_q[0];
-// workspaces chunk_offsets int32 [R+1], states fp32 [max_chunks * H * P * N], decay fp32
-// [max_chunks * H] with max_chunks = ceil(num_tokens / 64) + R.
+// workspaces chunk_offsets int32 [R+1], states fp32 and start_bf16 bf16 [max_chunks * H * P * N],
+// decay fp32 [max_chunks * H] with max_chunks = ceil(num_tokens / 64) + R.
 void mamba2_chunked(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tensor& dt,
                     const Tensor& dt_bias, const Tensor& A_log, const Tensor& D, Tensor& state,
                     const Tensor& cu_q, const Tensor& seq_lens, const Tensor& slots, Tensor& y,
                     int64_t H, int64_t G, int64_t P, int64_t N, double dt_min, double dt_max,
-                    Tensor& chunk_offsets, Tensor& states, Tensor& decay, int64_t num_tokens) {
+                    Tensor& chunk_offsets, Tensor& states, Tensor& start_bf16, Tensor& decay,
+                    int64_t num_tokens) {
   const c10::cuda::CUDAGuard g(xbc.device());
   const auto a = mamba2_args(xbc, b_off, c_off, dt, dt_bias, A_log, D, state, cu_q, seq_lens,
                              slots, y, H, G, P, N, dt_min, dt_max);
@@ -1004,6 +1005,10 @@ void mamba2_chunked(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tenso
   TORCH_CHECK(states.scalar_type() == at::kFloat && states.is_contiguous() &&
                   (size_t)states.numel() >= mc * H * P * N,
               "mamba2_chunked: states workspace too small");
+  TORCH_CHECK(start_bf16.scalar_type() == at::kBFloat16 && start_bf16.is_contiguous() &&
+                  (size_t)start_bf16.numel() >= mc * H * P * N &&
+                  reinterpret_cast<uintptr_t>(start_bf16.data_ptr()) % 16 == 0,
+              "mamba2_chunked: bf16 chunk-start state workspace");
   TORCH_CHECK(decay.scalar_type() == at::kFloat && (size_t)decay.numel() >= mc * H,
               "mamba2_chunked: decay workspace too small");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(xbc.data_ptr()) % 16 == 0 &&
@@ -1014,7 +1019,8 @@ void mamba2_chunked(const Tensor& xbc, int64_t b_off, int64_t c_off, const Tenso
               "mamba2_chunked: head_dim 32/64, state 64/128, rows of multiples of 8 elements");
   guarded([&] {
     b200::mamba::run_mamba2_chunked(a, (int)num_tokens, chunk_offsets.data_ptr<int32_t>(),
-                                    states.data_ptr<float>(), decay.data_ptr<float>(),
+                                    states.data_ptr<float>(), start_bf16.data_ptr(),
+                                    decay.data_ptr<float>(),
                                     stream_of(xbc));
   });
 }
@@ -1263,6 +1269,39 @@ void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w,
                                shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
                                shared_gate.has_value() ? shared_gate->stride(0) : 0,
                                out.data_ptr(), out.stride(0), stream_of(y));
+  });
+}
+
+void moe_gemv(const Tensor& x, const Tensor& ids, int64_t E, int64_t expert_offset,
+              const Tensor& w_gu, const Tensor& w_down, Tensor& h, Tensor& y, Tensor& pos) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.dim() == 2,
+              "moe_gemv: int32 ids [T, k]");
+  const int64_t T = ids.size(0), k = ids.size(1), H = x.size(1);
+  TORCH_CHECK(x.size(0) == T, "moe_gemv: x rows");
+  TORCH_CHECK(w_gu.is_contiguous() && w_down.is_contiguous() && w_gu.size(1) == H &&
+                  w_gu.size(0) % (2 * E) == 0,
+              "moe_gemv: w_gu [E * 2I, H], w_down [E * H, I]");
+  const int64_t I = w_gu.size(0) / E / 2;
+  TORCH_CHECK(w_down.size(0) == E * H && w_down.size(1) == I, "moe_gemv: w_down [E * H, I]");
+  TORCH_CHECK(h.is_contiguous() && h.numel() >= T * k * I && y.is_contiguous() &&
+                  y.numel() >= T * k * H && pos.scalar_type() == at::kInt &&
+                  pos.is_contiguous() && pos.numel() >= T * k,
+              "moe_gemv: h [T*k, I], y [T*k, H], pos [T, k] int32");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(w_gu.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(w_down.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(h.data_ptr()) % 16 == 0,
+              "moe_gemv: 16-byte aligned operands");
+  TORCH_CHECK(b200::moe::moe_gemv_supported((int)H, (int)I), "moe_gemv: H, I % 32");
+  const c10::cuda::CUDAGuard g(x.device());
+  guarded([&] {
+    b200::moe::run_moe_gemv(x.data_ptr(), x.stride(0), ids.data_ptr<int32_t>(), (int)T, (int)k,
+                            (int)E, (int)expert_offset, w_gu.data_ptr(), w_down.data_ptr(),
+                            (int)H, (int)I, h.data_ptr(), y.data_ptr(), pos.data_ptr<int32_t>(),
+                            stream_of(x));
   });
 }
 
@@ -1658,6 +1697,8 @@ TORCH_LIBRARY(b200, m) {
   m.def("moe_gather(Tensor x, Tensor sorted_ids, Tensor num_tiles, int k, Tensor(a!) out) -> ()");
   m.def("w4_dequant(Tensor(a!) out, Tensor packed, Tensor scales, Tensor? offsets) -> ()");
   m.def("row_fp8_qdq(Tensor(a!) out, Tensor x, bool swiglu, float limit, Tensor? num_tiles) -> ()");
+  m.def("moe_gemv(Tensor x, Tensor ids, int E, int expert_offset, Tensor w_gu, Tensor w_down, "
+        "Tensor(a!) h, Tensor(b!) y, Tensor(c!) pos) -> ()");
   m.def("moe_combine(Tensor y, Tensor pos, Tensor w, Tensor? shared, Tensor(a!) out, "
       "Tensor? shared_gate=None) -> ()");
   m.def(
@@ -1671,7 +1712,8 @@ TORCH_LIBRARY(b200, m) {
       "mamba2_chunked(Tensor xbc, int b_off, int c_off, Tensor dt, Tensor dt_bias, "
       "Tensor A_log, Tensor D, Tensor(a!) state, Tensor cu_q, Tensor seq_lens, Tensor slots, "
       "Tensor(b!) y, int H, int G, int P, int N, float dt_min, float dt_max, "
-      "Tensor(c!) chunk_offsets, Tensor(d!) states, Tensor(e!) decay, int num_tokens) -> ()");
+      "Tensor(c!) chunk_offsets, Tensor(d!) states, Tensor(e!) start_bf16, Tensor(f!) decay, "
+      "int num_tokens) -> ()");
   m.def("gated_rmsnorm(Tensor(a!) out, Tensor y, Tensor z, Tensor w, int group, float eps) -> ()");
   m.def(
       "gdn_recurrent(Tensor qkv, Tensor ba, Tensor A_log, Tensor dt_bias, Tensor(a!) state, "
@@ -1720,6 +1762,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("w4_dequant", &w4_dequant);
   m.impl("row_fp8_qdq", &row_fp8_qdq);
   m.impl("moe_combine", &moe_combine);
+  m.impl("moe_gemv", &moe_gemv);
   m.impl("causal_conv1d", &causal_conv1d);
   m.impl("mamba2_scan", &mamba2_scan);
   m.impl("mamba2_chunked", &mamba2_chunked);

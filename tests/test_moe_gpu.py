@@ -82,6 +82,31 @@ def test_fused_moe(T, E, k, H, I):
     torch.testing.assert_close(out.cpu().float(), ref.float(), rtol=3e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("T,E,k,H,I,e0", [(1, 128, 8, 2048, 768, 0), (5, 64, 8, 1024, 256, 16),
+                                           (16, 32, 4, 512, 512, 0)])
+def test_moe_gemv_matches_grouped_and_reference(T, E, k, H, I, e0, monkeypatch):
+    """Small-batch dispatch: the per-pair GEMV path and the grouped-GEMM path give the same
+    combined output as the fp32 reference, also with expert parallelism (this rank holds
+    experts [e0, e0 + E) of 2E; the rest contribute nothing here)."""
+    g = torch.Generator().manual_seed(T * 7 + E)
+    E_all = 2 * E if e0 else E
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w_gu = (torch.randn(E * 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)
+    w_dn = (torch.randn(E * H, I, generator=g) * 0.05).to(torch.bfloat16)
+    ids, w = moe_ops.topk_softmax(torch.randn(T, E_all, generator=g), k)
+    shared = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
+    ref = moe_ops.fused_moe(x, w_gu, w_dn, ids, w, E, shared, expert_offset=e0)
+    outs = {}
+    for name, limit in (("gemv", 1 << 20), ("grouped", 0)):
+        monkeypatch.setenv("B200_MOE_GEMV_MAX_PAIRS", str(limit))
+        assert moe_ops.use_gemv(T, k, H, I) == (name == "gemv")
+        outs[name] = moe_ops.fused_moe(x.cuda(), w_gu.cuda(), w_dn.cuda(), ids.cuda(), w.cuda(),
+                                       E, shared.cuda(), expert_offset=e0).cpu().float()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(outs["gemv"], ref.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(outs["gemv"], outs["grouped"], rtol=3e-2, atol=3e-2)
+
+
 def test_tiny_moe_engine_graph_vs_eager():
     from vllm_musa_b200 import LLM, SamplingParams
     from vllm_musa_b200.config import ModelConfig

@@ -57,6 +57,9 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
     EnvFlag("B200_DEBUG_BOUNDS", False, _bool,
             "check index tensors (KV slots, block tables, row indices) against the kernels' "
             "bounds at every op call and raise IndexError (synchronises: debugging only)"),
+    EnvFlag("B200_MOE_GEMV_MAX_PAIRS", 256, int,
+            "bf16 MoE layers with at most this many routed (token, slot) pairs run per-pair "
+            "GEMVs instead of align + gather + grouped GEMMs (0: always grouped)"),
     EnvFlag("B200_MAMBA_CHUNKED", True, _bool,
             "Mamba2 prefill parts of >= 64 tokens through the chunked SSD kernels (off: the "
             "token recurrence for every request)"),

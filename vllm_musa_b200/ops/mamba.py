@@ -138,9 +138,10 @@ def mamba2_chunked(xbc: torch.Tensor, b_off: int, c_off: int, dt: torch.Tensor,
     dev = xbc.device
     offs = torch.empty(R + 1, dtype=torch.int32, device=dev)
     ws = torch.empty(mc * H * P * N, dtype=torch.float32, device=dev)
+    start = torch.empty(mc * H * P * N, dtype=torch.bfloat16, device=dev)
     decay = torch.empty(mc * H, dtype=torch.float32, device=dev)
     _ext.ops().mamba2_chunked(xbc, b_off, c_off, dt, dt_bias, A_log, D, state, cu_q, seq_lens,
-                              slots, out, H, G, P, N, dt_min, dt_max, offs, ws, decay, nt)
+                              slots, out, H, G, P, N, dt_min, dt_max, offs, ws, start, decay, nt)
     return out
 
 

@@ -109,9 +109,37 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
         out.copy_(_fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared, expert_offset,
                                  shared_gate))
         return out
-    y, pos = moe_experts(x, w_gu, w_down, ids, num_experts, expert_offset)
+    if use_gemv(T, k, H, w_gu.shape[0] // num_experts // 2):
+        y, pos = moe_experts_gemv(x, w_gu, w_down, ids, num_experts, expert_offset)
+    else:
+        y, pos = moe_experts(x, w_gu, w_down, ids, num_experts, expert_offset)
     torch.ops.b200.moe_combine(y, pos, w.contiguous(), shared, out, shared_gate)
     return out
+
+
+def use_gemv(T: int, k: int, H: int, I: int) -> bool:
+    """Dispatch policy: per-pair GEMVs for at most ``B200_MOE_GEMV_MAX_PAIRS`` routed (token,
+    slot) pairs, the grouped GEMMs above (decided on host shapes only: graph-capture safe)."""
+    from .. import envs
+    return T * k <= envs.get("B200_MOE_GEMV_MAX_PAIRS") and H % 32 == 0 and I % 32 == 0
+
+
+def moe_experts_gemv(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor,
+                     ids: torch.Tensor, num_experts: int,
+                     expert_offset: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Routed experts of a few tokens as per-(token, slot) GEMVs (CUDA): same outputs as
+    ``moe_experts`` (y rows addressed through pos)."""
+    T, H = x.shape
+    k = ids.shape[1]
+    E = num_experts
+    I = w_gu.shape[0] // E // 2
+    dev = x.device
+    h = torch.empty(T * k, I, dtype=x.dtype, device=dev)
+    y = torch.empty(T * k, H, dtype=x.dtype, device=dev)
+    pos = torch.empty(T, k, dtype=torch.int32, device=dev)
+    _ext.require()
+    torch.ops.b200.moe_gemv(x, ids.contiguous(), E, expert_offset, w_gu, w_down, h, y, pos)
+    return y, pos
 
 
 def moe_experts(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: torch.Tensor,
