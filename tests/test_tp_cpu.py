@@ -34,7 +34,7 @@ def _model(name):
 
 
 def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp=1, dp=1,
-            pp=1):
+            pp=1, spec=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     torch.set_num_threads(1)
@@ -47,7 +47,8 @@ def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp
               pipeline_parallel_size=pp, data_parallel_size=dp,
               block_size=16, seed=0,
               num_gpu_blocks=64, max_model_len=128, max_num_seqs=4, max_num_batched_tokens=64,
-              enable_expert_parallel=ep, decode_context_parallel_size=dcp)
+              enable_expert_parallel=ep, decode_context_parallel_size=dcp,
+              speculative_config=spec)
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, min(1024, cfg.vocab_size), (3, 20), generator=g).tolist()
     outs = llm.generate(prompts, SamplingParams(temperature=temperature, max_tokens=8,
@@ -57,16 +58,23 @@ def _worker(rank, world, port, q, temperature, model="tiny-llama", ep=False, dcp
         assert m.l1 - m.l0 < cfg.num_layers
         assert len(llm.engine.runner.kv_caches) == m.l1 - m.l0
         assert (m.embed is not None) == (m.l0 == 0)
+    if spec is not None and spec.get("method") == "eagle":
+        head = llm.engine.model.draft_head
+        assert llm.engine.drafter.proposed > 0
+        assert head.replicated == (spec.get("draft_tensor_parallel_size") == 1 and world > 1)
+        if head.replicated:  # whole head, own cache with every KV head
+            assert head.own_kv[0].shape[1] == cfg.num_kv_heads
+            assert len(llm.engine.runner.kv_caches) == cfg.num_layers
     q.put((rank, [o.outputs[0].token_ids for o in outs]))
     destroy_distributed()
 
 
-def _run(world, temperature=0.0, model="tiny-llama", ep=False, dcp=1, dp=1, pp=1):
+def _run(world, temperature=0.0, model="tiny-llama", ep=False, dcp=1, dp=1, pp=1, spec=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker,
-                         args=(r, world, port, q, temperature, model, ep, dcp, dp, pp))
+                         args=(r, world, port, q, temperature, model, ep, dcp, dp, pp, spec))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -161,3 +169,17 @@ def test_pipeline_parallel_matches_single(world, pp, model):
         got = _run(world, temperature, model, pp=pp)
         assert all(got[r] == got[0] for r in got), "ranks diverged"
         assert got[0] == one
+
+
+@pytest.mark.parametrize("draft_tp", [None, 1])
+def test_tp2_eagle_drafts_match_tp1(draft_tp):
+    """EAGLE under TP=2 with the head sharded like the target, or whole on every rank
+    (draft_tensor_parallel_size=1: no collectives in the draft layer, its own all-head cache):
+    the verified tokens equal plain TP=1 decoding and both ranks stay in lock-step."""
+    plain = _run(1)[0]
+    spec = {"method": "eagle", "num_speculative_tokens": 1}
+    if draft_tp is not None:
+        spec["draft_tensor_parallel_size"] = draft_tp
+    two = _run(2, spec=spec)
+    assert two[0] == two[1], "ranks diverged"
+    assert two[0] == plain

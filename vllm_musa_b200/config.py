@@ -265,7 +265,10 @@ class SpeculativeConfig:
     ``num_speculative_tokens`` nodes; ``eagle`` proposes the head's top ``tree_width`` tokens as
     siblings.  vLLM's ``speculative_token_tree`` (a list of child-index paths such as
     ``"[(0,), (1,), (2,)]"``) is accepted for one-level trees and sets ``tree_width``.  The
-    whole tree is verified in one step under per-node ancestor masks."""
+    whole tree is verified in one step under per-node ancestor masks.
+
+    ``draft_tensor_parallel_size=1`` keeps a whole EAGLE head on every rank of a
+    tensor-parallel target (its layer then needs no all-reduce)."""
     method: Optional[str] = None  # None | "ngram" | "mtp" | "eagle"
     num_speculative_tokens: int = 0
     model: Optional[str] = None
@@ -273,6 +276,9 @@ class SpeculativeConfig:
     prompt_lookup_max: int = 4
     tree_width: int = 1
     speculative_token_tree: Optional[str] = None
+    # 1: the draft head runs whole on every rank (no collectives in the draft layer) under a
+    # tensor-parallel target; None: sharded like the target
+    draft_tensor_parallel_size: Optional[int] = None
 
     def __post_init__(self):
         if self.speculative_token_tree:
@@ -287,6 +293,9 @@ class SpeculativeConfig:
             self.tree_width = len(paths)
         if self.tree_width < 1:
             raise ValueError("tree_width must be >= 1")
+        if self.draft_tensor_parallel_size == 1 and self.method == "mtp":
+            raise ValueError("draft_tensor_parallel_size=1 serves EAGLE heads (the MTP layer "
+                             "is sharded like the target)")
 
     @property
     def tree(self) -> bool:

@@ -543,7 +543,11 @@ class LLMEngine:
         """Attach an EAGLE head to the dense decoder (its KV is one extra cache layer)."""
         from ..models.eagle import EagleHead, eagle_param_shapes
         cfg, mcfg, device = self.config, self.config.model, self.device
-        head = EagleHead(self.model)
+        dtp = cfg.speculative.draft_tensor_parallel_size
+        tp = cfg.parallel.tensor_parallel_size
+        if dtp not in (None, 1, tp):
+            raise ValueError(f"draft_tensor_parallel_size must be 1 or {tp} (the target's)")
+        head = EagleHead(self.model, replicated=dtp == 1)
         path = cfg.speculative.model
         if path:
             head.load_weights(safetensors_weights(path))

@@ -161,7 +161,8 @@ class ModelRunner:
             return self.model.kv_bytes_per_block(self.block_size)
         spec = self.model.kv_cache_spec()
         elt = torch.tensor([], dtype=spec["dtype"]).element_size()
-        return spec["num_layers"] * 2 * spec["num_kv_heads"] * self.block_size * spec["head_dim"] * elt
+        heads = spec["num_layers"] * spec["num_kv_heads"] + spec.get("draft_kv_heads", 0)
+        return heads * 2 * self.block_size * spec["head_dim"] * elt
 
     def profile_and_allocate_kv(self) -> int:
         """Measure the activation peak of a full-budget prefill, then size the KV cache."""
@@ -229,6 +230,10 @@ class ModelRunner:
                                      device=self.device)
         self.kv_caches = [(self.kv_tensor[i, 0], self.kv_tensor[i, 1])
                           for i in range(spec["num_layers"])]
+        if spec.get("draft_kv_heads"):  # replicated draft layer: all KV heads, same pages
+            shape = (num_blocks, spec["draft_kv_heads"], self.block_size, spec["head_dim"])
+            self.model.draft_head.own_kv = tuple(
+                torch.zeros(shape, dtype=spec["dtype"], device=self.device) for _ in range(2))
 
     def apply_kv_moves(self, moves) -> None:
         """Copy KV rows between cache slots (slot = block * block_size + offset) in every layer:

@@ -52,7 +52,15 @@ def eagle_param_shapes(cfg) -> list:
 
 
 class EagleHead:
-    def __init__(self, target):
+    """``replicated=True`` (draft tensor-parallel size 1 under a TP>1 target): every rank holds
+    the whole head (all heads, the whole MLP) and its own K/V cache with all KV heads (same
+    block ids and slots as the target's, allocated by the runner as ``own_kv``), so the draft
+    layer runs without collectives; every rank computes the same drafts from the same
+    (replicated) target hidden states.  The logits still go through the target's vocab-parallel
+    LM head and sampler.  Reference: the per-rank TP=1 draft group of
+    patches/vllm__distributed__parallel_state.patch.py:77-209."""
+
+    def __init__(self, target, replicated: bool = False):
         if getattr(target, "tq", None) is not None:
             raise ValueError("EAGLE drafts need a bf16 KV cache (not TurboQuant)")
         self.t = target
@@ -61,7 +69,19 @@ class EagleHead:
         self.fc = None
         self.fc_bias = None
         self.norm = None
+        self.replicated = replicated and target.tp > 1
         self.cache_index = target.l1 - target.l0  # the extra cache layer after the target's
+        self.own_kv = None
+        if self.replicated:
+            from ..attention import PagedAttention
+            from ..parallel.communicator import LocalCommunicator
+            cfg = self.cfg
+            self.hq, self.hkv = cfg.num_heads, cfg.num_kv_heads
+            self.attn = PagedAttention(self.hq, self.hkv, target.D)
+            self.comm = LocalCommunicator(target.device)
+        else:
+            self.hq, self.hkv = target.hq, target.hkv
+            self.attn, self.comm = target.attn, target.comm
 
     def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
         t, L = self.t, self.layer
@@ -71,14 +91,26 @@ class EagleHead:
             raise RuntimeError(f"EAGLE checkpoint is missing {miss}")
         D, r, tp = t.D, t.rank, t.tp
         a, m = "layers.0.self_attn.", "layers.0.mlp."
-        q = shard_rows(st[a + "q_proj.weight"], r, tp)
-        k = st[a + "k_proj.weight"][t.kv0 * D:(t.kv0 + t.hkv) * D]
-        v = st[a + "v_proj.weight"][t.kv0 * D:(t.kv0 + t.hkv) * D]
-        L.qkv_w = t._to(torch.cat([q, k, v], 0))
-        L.o_w = t._to(shard_cols(st[a + "o_proj.weight"], r, tp))
-        L.gu_w, L.down_w = t._dense_mlp_weights(st[m + "gate_proj.weight"],
-                                                st[m + "up_proj.weight"],
-                                                st[m + "down_proj.weight"])
+        if self.replicated:
+            L.qkv_w = t._to(torch.cat([st[a + "q_proj.weight"], st[a + "k_proj.weight"],
+                                       st[a + "v_proj.weight"]], 0))
+            L.o_w = t._to(st[a + "o_proj.weight"])
+            gate, up, down = (st[m + n + "_proj.weight"] for n in ("gate", "up", "down"))
+            pad = (-gate.shape[0]) % 8
+            L.gu_w = t._to(ops.interleave_gate_up(gate, up))
+            if pad:
+                down = torch.cat([down, torch.zeros(down.shape[0], pad, dtype=down.dtype,
+                                                    device=down.device)], 1)
+            L.down_w = t._to(down)
+        else:
+            q = shard_rows(st[a + "q_proj.weight"], r, tp)
+            k = st[a + "k_proj.weight"][t.kv0 * D:(t.kv0 + t.hkv) * D]
+            v = st[a + "v_proj.weight"][t.kv0 * D:(t.kv0 + t.hkv) * D]
+            L.qkv_w = t._to(torch.cat([q, k, v], 0))
+            L.o_w = t._to(shard_cols(st[a + "o_proj.weight"], r, tp))
+            L.gu_w, L.down_w = t._dense_mlp_weights(st[m + "gate_proj.weight"],
+                                                    st[m + "up_proj.weight"],
+                                                    st[m + "down_proj.weight"])
         H = self.cfg.hidden_size
         L.ln2 = t._to(st.get("layers.0.post_attention_layernorm.weight", torch.ones(H)))
         self.norm = t._to(st["norm.weight"]) if "norm.weight" in st else None
@@ -90,24 +122,25 @@ class EagleHead:
                       kv_caches: list) -> torch.Tensor:
         """Hidden states whose logits draft token p+2 for each row (position p)."""
         t, L, cfg, eps = self.t, self.layer, self.cfg, self.cfg.rms_norm_eps
-        T = next_ids.shape[0]
-        t.comm.begin_forward()
+        comm = self.comm
+        comm.begin_forward()
         e = ops.embedding(next_ids, t.embed)
         x = ops.linear(torch.cat([e, prev_hidden.to(e.dtype)], -1).contiguous(), self.fc)
         if self.fc_bias is not None:
             x = x + self.fc_bias
         residual = x
-        kc, vc = kv_caches[self.cache_index]
+        kc, vc = self.own_kv if self.replicated else kv_caches[self.cache_index]
         qkv = ops.linear(x, L.qkv_w)
-        ops.rope_kv(qkv, meta.positions, t.cos_sin, kc, vc, meta.slot_mapping, t.hq, t.hkv,
-                    cfg.rot_dim, cfg.rope_neox, None, None, eps)
-        a = t.attn.forward(qkv, kc, vc, meta)
-        x, residual = t.comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
+        ops.rope_kv(qkv, meta.positions, t.cos_sin, kc, vc, meta.slot_mapping, self.hq,
+                    self.hkv, cfg.rot_dim, cfg.rope_neox, None, None, eps)
+        a = self.attn.forward(qkv, kc, vc, meta)
+        x, residual = comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
+        act = ops.linear_silu_mul(x, L.gu_w)
         if self.norm is not None:
-            x, residual = t._mlp_allreduce(cfg.num_layers, L, x, T, residual, self.norm, eps)
+            x, residual = comm.linear_allreduce_add_rmsnorm(act, L.down_w, residual, self.norm,
+                                                            eps)
             return x
-        d = ops.linear(ops.linear_silu_mul(x, L.gu_w), L.down_w)
-        return t.comm.all_reduce(d) + residual
+        return comm.all_reduce(ops.linear(act, L.down_w)) + residual
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         return self.t.compute_logits(hidden)

@@ -327,6 +327,10 @@ class DenseDecoderForCausalLM:
 
     def kv_cache_spec(self) -> dict:
         """Cache layers of this stage (its decoder layers, plus the EAGLE head's layer)."""
-        n = self.l1 - self.l0 + (1 if self.draft_head is not None else 0)
-        return {"num_layers": n, "num_kv_heads": self.hkv,
-                "head_dim": self.D, "dtype": self.dtype}
+        d = self.draft_head
+        n = self.l1 - self.l0 + (1 if d is not None and not d.replicated else 0)
+        spec = {"num_layers": n, "num_kv_heads": self.hkv, "head_dim": self.D,
+                "dtype": self.dtype}
+        if d is not None and d.replicated:  # a whole-head draft layer keeps its own cache
+            spec["draft_kv_heads"] = d.hkv
+        return spec
