@@ -79,11 +79,13 @@ __global__ void causal_conv1d_kernel(const __nv_bfloat16* __restrict__ x, int64_
 }
 
 // Vectorised form: a thread owns 8 consecutive channels (one 16-byte vector) of kConvTok
-// consecutive tokens, keeping the 3 + kConvTok input rows it needs in registers, so each input
-// element is loaded ~1.2 times instead of 4 and every access is a 16-byte vector.  Tokens keep
+// consecutive tokens and walks them with a rolling window of the 4 input rows a token needs
+// (packed bf16, 4 registers a row), the next two rows already in flight, so each input element
+// is loaded (kConvTok + 3) / kConvTok times and every access is a 16-byte vector.  (Holding all
+// kConvTok + 3 rows unpacked took 212 registers a thread and 2 CTAs per SM.)  Tokens keep
 // their own request's history rule (inputs before the request's first new token come from its
 // conv state slot, or zeros).  Same results as causal_conv1d_kernel.
-constexpr int kConvTok = 16;
+constexpr int kConvTok = 32;
 
 __global__ void __launch_bounds__(128)
     causal_conv1d_vec_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
@@ -100,41 +102,33 @@ __global__ void __launch_bounds__(128)
   const int t1 = min(T, t0 + kConvTok);
   float wt[8][4], b[8];
   {
-    float wv[32];
     const uint4* wp = reinterpret_cast<const uint4*>(w + (size_t)c0 * 4);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float f[8];
       unpack8(wp[q], f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) wv[q * 8 + j] = f[j];
+      for (int j = 0; j < 8; ++j) wt[q * 2 + j / 4][j % 4] = f[j];
     }
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) wt[ch][j] = wv[ch * 4 + j];
     if (bias != nullptr)
       unpack8(*reinterpret_cast<const uint4*>(bias + c0), b);
     else
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) b[ch] = 0.f;
   }
-  // input rows t0-3 .. t1-1 of these channels (rows before 0 are never used)
-  float xin[kConvTok + 3][8];
-#pragma unroll
-  for (int i = 0; i < kConvTok + 3; ++i) {
-    const int tau = t0 - 3 + i;
-    if (tau >= 0 && tau < t1)
-      unpack8(*reinterpret_cast<const uint4*>(x + (size_t)tau * ldx + c0), xin[i]);
-    else
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) xin[i][ch] = 0.f;
-  }
+  auto row = [&](int tau) -> uint4 {  // input row tau of these channels (zeros outside [0, t1))
+    return tau >= 0 && tau < t1 ? *reinterpret_cast<const uint4*>(x + (size_t)tau * ldx + c0)
+                                : make_uint4(0, 0, 0, 0);
+  };
+  // window w0..w2 = rows t-3..t-1; n1, n2 = rows t, t+1 (in flight)
+  uint4 w0 = row(t0 - 3), w1 = row(t0 - 2), w2 = row(t0 - 1);
+  uint4 n1 = row(t0), n2 = row(t0 + 1);
   int r = find_req(cu_q, R, t0);
-#pragma unroll
-  for (int i = 0; i < kConvTok; ++i) {
-    const int t = t0 + i;
-    if (t >= t1) break;
+#pragma unroll 1
+  for (int t = t0; t < t1; ++t) {
+    const uint4 w3 = n1;
+    n1 = n2;
+    n2 = row(t + 2);
     while (r + 1 < R && t >= cu_q[r + 1]) ++r;
     const int q0 = cu_q[r];
     const bool hist = seq_lens[r] - (cu_q[r + 1] - q0) > 0;
@@ -145,8 +139,10 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < 4; ++j) {
       const int tau = t - 3 + j;
       if (tau >= q0) {
+        float xv[8];
+        unpack8(j == 0 ? w0 : j == 1 ? w1 : j == 2 ? w2 : w3, xv);
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) acc[ch] += xin[i + j][ch] * wt[ch][j];
+        for (int ch = 0; ch < 8; ++ch) acc[ch] += xv[ch] * wt[ch][j];
       } else if (hist) {
         const int back = q0 - tau;  // 1..3 tokens before the chunk
         const __nv_bfloat16* st = state + ((size_t)slots[r] * C + c0) * 3 + (3 - back);
@@ -158,6 +154,9 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) o[ch] = acc[ch] / (1.f + __expf(-acc[ch]));
     *reinterpret_cast<uint4*>(out + (size_t)t * ldo + c0) = pack8(o);
+    w0 = w1;
+    w1 = w2;
+    w2 = w3;
   }
 }
 
