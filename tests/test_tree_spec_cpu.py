@@ -240,3 +240,64 @@ def test_mixed_causal_and_tree_rows_cpu():
                               lens[1:], bt[1:], Hq, Hkv, D ** -0.5, tree_mask=masks)
     torch.testing.assert_close(both[:10], causal)
     torch.testing.assert_close(both[10:], alone)
+
+
+def test_tree_pruned_by_token_budget_and_max_tokens():
+    """Trees cut by the step's token budget (node count) and by the request's remaining tokens
+    (depth) still verify exactly: outputs equal plain decoding, max_tokens is never exceeded."""
+    for budget, max_tokens in ((8, 7), (12, 5), (40, 3)):
+        sp = SamplingParams(temperature=0.0, max_tokens=max_tokens, ignore_eos=True)
+        plain = [o.outputs[0].token_ids for o in _llm().generate(_prompts(), sp)]
+        llm = _llm(max_num_batched_tokens=max(budget, 48))
+        eng = llm.engine
+        for i, p in enumerate(_prompts()):
+            eng.add_request(f"r{i}", p, sp)
+        iids = {eng._by_name[f"r{i}"]: i for i in range(3)}
+        outs = {}
+        while eng.has_unfinished_requests():
+            for iid in eng.scheduler.decode_request_ids():
+                done = len(eng.scheduler.output_tokens(iid))
+                right = plain[iids[iid]][done:done + 6] + [0] * 6
+                # a deep chain along the right path with a wrong sibling at every level
+                toks, par = [], []
+                prev = -1
+                for d in range(6):
+                    toks += [(right[d] + 1) % V, right[d]]
+                    par += [prev, prev]
+                    prev = len(toks) - 1
+                eng.scheduler.set_draft_tree(iid, toks, par)
+            for o in eng.step():
+                outs[o.request_id] = o.outputs[0].token_ids
+        got = [outs[f"r{i}"] for i in range(3)]
+        assert got == plain, (budget, max_tokens)
+        assert all(len(g) == max_tokens for g in got)
+
+
+def test_tree_verification_under_preemption():
+    """A pool too small for all requests preempts (recomputes) requests while they verify
+    trees; the outputs still equal plain decoding."""
+    sp = SamplingParams(temperature=0.0, max_tokens=24, ignore_eos=True)
+    kw = dict(num_gpu_blocks=9, max_model_len=96)
+    plain = [o.outputs[0].token_ids for o in _llm(**kw).generate(_prompts(), sp)]
+    llm = _llm(**kw)
+    eng = llm.engine
+    for i, p in enumerate(_prompts()):
+        eng.add_request(f"r{i}", p, sp)
+    iids = {eng._by_name[f"r{i}"]: i for i in range(3)}
+    outs, preempted = {}, []
+    run = eng.runner.execute
+
+    def spy(plan, extras=None):
+        preempted.append(plan.num_preempted)
+        return run(plan, extras)
+
+    eng.runner.execute = spy
+    while eng.has_unfinished_requests():
+        for iid in eng.scheduler.decode_request_ids():
+            done = len(eng.scheduler.output_tokens(iid))
+            toks, par = _oracle_tree(plain[iids[iid]][done:done + 3])
+            eng.scheduler.set_draft_tree(iid, toks, par)
+        for o in eng.step():
+            outs[o.request_id] = o.outputs[0].token_ids
+    assert sum(preempted) > 0
+    assert [outs[f"r{i}"] for i in range(3)] == plain
