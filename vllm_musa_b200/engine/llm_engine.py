@@ -7,7 +7,7 @@
 Tensor parallelism is SPMD: every rank (one process per GPU, launched by torchrun) runs
 its own engine on the same requests; the schedulers stay in lock-step because every rank
 draws the same tokens (vocab-parallel sampler, parallel/sampler).  The reference gets this
-layer from upstream vLLM's V1 EngineCore (SURVEY section 3.2).
+layer from upstream vLLM's V1 EngineCore.
 """
 from __future__ import annotations
 

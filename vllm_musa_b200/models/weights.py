@@ -5,7 +5,7 @@ loading path (``load_weights``) that shards and fuses.  Random weights are drawn
 by parameter from one seeded generator in a fixed order, full logical shape first and then
 sharded by the model, so a tensor-parallel run sees the same logical weights as a
 single-GPU run.  Reference: upstream vLLM's loader (HF safetensors, ``load_format=dummy``),
-used by the reference unchanged (checkpoint row).
+used by the reference unchanged.
 """
 from __future__ import annotations
 
