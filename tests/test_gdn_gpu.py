@@ -135,8 +135,9 @@ def test_tiny_qwen3_next_engine_graph_vs_eager():
 @pytest.mark.parametrize("lens,ctx", [([64], [0]), ([200, 1, 77], [0, 9, 130]),
                                       ([1000, 65], [64, 0])])
 def test_gdn_chunked_matches_recurrent(lens, ctx):
-    """Chunked prefill kernels (parallel chunk prep + tensor-core chunk scan) against the
-    token-recurrent kernel: outputs and the carried state."""
+    """Chunked prefill kernels (parallel chunk prep + tensor-core chunk scan) against the fp32
+    PyTorch token recurrence on CPU (the oracle) and against the token-recurrent kernel:
+    outputs and the carried state."""
     from vllm_musa_b200.ops import gdn
     Hk, Hv = 2, 4
     T = sum(lens)
@@ -158,3 +159,8 @@ def test_gdn_chunked_matches_recurrent(lens, ctx):
     _ext.check_device_errors()
     torch.testing.assert_close(got.float(), ref.float(), rtol=3e-2, atol=3e-2)
     torch.testing.assert_close(s_got, s_ref, rtol=3e-2, atol=3e-2)
+    s_cpu = st0.cpu()
+    oracle = gdn.gdn_recurrent(qkv.cpu(), ba.cpu(), A_log.cpu(), dt_bias.cpu(), s_cpu, cu.cpu(),
+                               sl.cpu(), slots.cpu(), Hk, Hv)
+    torch.testing.assert_close(got.cpu().float(), oracle.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(s_got.cpu(), s_cpu, rtol=3e-2, atol=3e-2)
