@@ -94,3 +94,34 @@ def test_logprobs_of_raw_logits():
     # without the request, no log-probabilities are computed or returned
     plain = _llm().generate(prompts[:1], SamplingParams(temperature=0.0, max_tokens=2))
     assert plain[0].outputs[0].logprobs is None
+
+
+def test_special_requests_beside_speculative_decoding():
+    """With n-gram speculation configured, requests with penalties or log-probabilities run
+    without drafts in the same batches as drafted requests: every output equals its run
+    without speculation, and the plain repetitive request still gets drafts accepted."""
+    g = torch.Generator().manual_seed(5)
+    base = torch.randint(0, 1024, (12,), generator=g).tolist()
+    rep = (base * 4)[:40]
+    prompts = [rep, _prompts(1, 20, seed=3)[0], rep[:30]]
+    params = [SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True),
+              SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True,
+                             repetition_penalty=1.3, presence_penalty=0.2),
+              SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True, logprobs=2)]
+
+    def run(spec):
+        llm = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=64,
+                  max_model_len=128, max_num_seqs=4, max_num_batched_tokens=256,
+                  speculative_config=spec)
+        outs = llm.generate(prompts, params)
+        return outs, llm.engine.scheduler
+
+    plain, _ = run(None)
+    spec, sch = run({"method": "ngram", "num_speculative_tokens": 3})
+    for a, b in zip(plain, spec):
+        assert a.outputs[0].token_ids == b.outputs[0].token_ids
+    for x, y in zip(plain[2].outputs[0].logprobs, spec[2].outputs[0].logprobs):
+        assert x.keys() == y.keys()
+        for t in x:
+            assert abs(x[t].logprob - y[t].logprob) < 1e-4
+    assert sch.spec_accepted() > 0

@@ -228,14 +228,10 @@ class LLMEngine:
             raise ValueError("stop strings need the model's tokenizer")
         special = params.has_penalties or params.logprobs is not None or so is not None or \
             bool(params.stop) or lora is not None
-        if lora is not None and self.config.speculative.method is not None and \
-                self.config.speculative.num_speculative_tokens:
-            raise ValueError("LoRA is not served with speculative decoding")
+        # with speculative decoding configured, these requests simply decode without drafts
+        # (their penalties, log-probabilities, grammars, stop strings and adapters apply per
+        # drawn token); the other requests of the batch keep theirs
         lora_slot = self.model.lora.acquire(lora) if lora is not None else -1
-        if special and self.config.speculative.method is not None and \
-                self.config.speculative.num_speculative_tokens:
-            raise ValueError("penalties / logprobs / structured outputs are not served with "
-                             "speculative decoding")
         matcher = self._grammar_backend().matcher(so) if so is not None else None
         self.scheduler.add_request(iid, list(map(int, prompt_ids)), sp)
         r = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
