@@ -54,6 +54,7 @@ class _Req:
     stop_hit: Optional[tuple] = None      # (stop string, text up to it) once one matched
     lora: Optional[object] = None         # LoRARequest of the request (None: base model)
     lora_slot: int = -1
+    bad_words_ids: Optional[list] = None  # token-id sequences of the request's bad words
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -224,10 +225,14 @@ class LLMEngine:
         sp.min_p = params.min_p
         sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
         so = params.structured_outputs
-        if params.stop and self.tokenizer is None:
-            raise ValueError("stop strings need the model's tokenizer")
+        if (params.stop or params.bad_words) and self.tokenizer is None:
+            raise ValueError("stop strings and bad words need the model's tokenizer")
+        V = self.config.model.vocab_size
+        for t in list(params.logit_bias or {}) + list(params.allowed_token_ids or []):
+            if not 0 <= t < V:
+                raise ValueError(f"token id {t} is outside the vocabulary (size {V})")
         special = params.has_penalties or params.logprobs is not None or so is not None or \
-            bool(params.stop) or lora is not None
+            bool(params.stop) or lora is not None or params.has_logits_processors
         # with speculative decoding configured, these requests simply decode without drafts
         # (their penalties, log-probabilities, grammars, stop strings and adapters apply per
         # drawn token); the other requests of the batch keep theirs
@@ -239,10 +244,32 @@ class LLMEngine:
             r.logprobs = []
         r.matcher = matcher
         r.lora, r.lora_slot = lora, lora_slot
+        if params.bad_words:
+            r.bad_words_ids = self._bad_words_ids(params.bad_words)
         self._reqs[iid] = r
         self._by_name[name] = iid
         if special:
             self._special[iid] = r
+
+    def _bad_words_ids(self, words) -> list:
+        """Token sequences of each bad word: the word as written (leading spaces dropped) and,
+        when it tokenizes to as many tokens with a different first token, with one leading
+        space (the form it takes inside a sentence)."""
+        def enc(text):
+            try:
+                return self.tokenizer.encode(text, add_special_tokens=False)
+            except TypeError:  # tokenizers without the keyword add no special tokens
+                return self.tokenizer.encode(text)
+
+        out = []
+        for w in words:
+            base = enc(w.lstrip())
+            if base:
+                out.append(list(base))
+            spaced = enc(" " + w.lstrip())
+            if spaced and base and len(spaced) == len(base) and spaced[0] != base[0]:
+                out.append(list(spaced))
+        return out
 
     def _grammar_backend(self):
         """Structured-output grammar compiler over the model's vocabulary (created on the first
@@ -366,6 +393,8 @@ class LLMEngine:
         pres = torch.zeros(S)
         freq = torch.zeros(S)
         row_req, nxt = {}, 0
+        bias = []       # (row, token, value) added to the raw logits
+        allowed = {}    # row -> allowed token ids
         for iid, cnt in zip(plan.sample_req_ids, plan.sample_counts):
             row, nxt = nxt, nxt + cnt  # the request's first sampling row
             r = self._special.get(iid)
@@ -373,9 +402,19 @@ class LLMEngine:
                 continue
             row_req[row] = iid
             p = r.params
-            if r.matcher is not None:
+            if r.matcher is not None or p.allowed_token_ids:
                 mask_rows.append(row)
                 matchers.append(r.matcher)
+                if p.allowed_token_ids:
+                    allowed[len(mask_rows) - 1] = p.allowed_token_ids
+            if p.logit_bias:
+                bias.extend((row, t, v) for t, v in p.logit_bias.items())
+            if r.bad_words_ids:
+                out = self.scheduler.output_tokens(iid)
+                for seq in r.bad_words_ids:
+                    pre = seq[:-1]
+                    if not pre or (len(out) >= len(pre) and list(out[len(out) - len(pre):]) == pre):
+                        bias.append((row, seq[-1], float("-inf")))
             if p.has_penalties:
                 n = self.scheduler.num_tokens(iid)
                 toks = self.scheduler.tokens_range(iid, 0, n)
@@ -387,14 +426,40 @@ class LLMEngine:
                 lp_rows.append(row)
                 k = max(k, p.logprobs)
         lora = self._lora_batch(plan)
-        if not rows_tok and not lp_rows and not mask_rows and lora is None:
+        if not rows_tok and not lp_rows and not mask_rows and lora is None and not bias:
             return None
         entries = penalty_entries(rows_tok) if rows_tok else None
-        bitmask = self._grammar_backend().bitmask(matchers) if matchers else None
+        bitmask = self._token_masks(matchers, allowed) if matchers else None
         ex = StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
         ex.lora = lora
         ex.row_req = row_req
+        if bias:
+            ex.bias = (torch.tensor([b[0] for b in bias], dtype=torch.int64),
+                       torch.tensor([b[1] for b in bias], dtype=torch.int64),
+                       torch.tensor([b[2] for b in bias], dtype=torch.float32))
         return ex
+
+    def _token_masks(self, matchers, allowed) -> torch.Tensor:
+        """int32 [len(matchers), words] next-token bitmasks: a grammar's mask where the row has
+        a matcher (all tokens otherwise), ANDed with the row's allowed_token_ids."""
+        words = (self.config.model.vocab_size + 31) // 32
+        if any(m is not None for m in matchers):
+            gb = self._grammar_backend()
+            words = gb.words
+            bm = torch.full((len(matchers), words), -1, dtype=torch.int32)
+            for i, m in enumerate(matchers):
+                if m is not None:
+                    m.fill_next_token_bitmask(bm, i)
+        else:
+            bm = torch.full((len(matchers), words), -1, dtype=torch.int32)
+        for i, ids in allowed.items():
+            row = torch.zeros(words * 32, dtype=torch.bool)
+            row[torch.tensor(ids, dtype=torch.long)] = True
+            bits = row.view(words, 32).to(torch.int64) << torch.arange(32, dtype=torch.int64)
+            packed = bits.sum(1)
+            packed = torch.where(packed >= 2 ** 31, packed - 2 ** 32, packed).to(torch.int32)
+            bm[i] &= packed
+        return bm
 
     def _lora_batch(self, plan):
         """Token indices of this step grouped by adapter slot (None: no adapter in the step)."""

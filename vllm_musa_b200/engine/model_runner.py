@@ -109,6 +109,8 @@ class StepExtras:
         self.mask_rows = mask_rows or []
         self.lora = None  # LoRABatch of the step (adapters in use)
         self.row_req = {}  # sampling row -> request id of the rows above
+        self.bias = None   # (rows, token ids, values) added to the raw logits (logit_bias,
+        #                    bad words as -inf)
         self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
 
 
@@ -282,6 +284,14 @@ class ModelRunner:
                 dev = logits.device
                 ops.apply_penalties(logits, ex.entries.to(dev), ex.rep.to(dev), ex.pres.to(dev),
                                     ex.freq.to(dev), getattr(self.model, "vocab_start", 0))
+            if ex.bias is not None:
+                r, c, v = ex.bias
+                vs, Vl = getattr(self.model, "vocab_start", 0), logits.shape[1]
+                keep = (c >= vs) & (c < vs + Vl)  # this rank's vocab shard
+                if bool(keep.any()):
+                    dev = logits.device
+                    logits.index_put_((r[keep].to(dev), (c[keep] - vs).to(dev)),
+                                      v[keep].to(dev), accumulate=True)
             if ex.mask_rows:
                 dev = logits.device
                 ops.sampling.apply_token_bitmask(

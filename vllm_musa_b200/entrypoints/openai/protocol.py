@@ -28,6 +28,11 @@ class _Sampling(BaseModel):
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
     repetition_penalty: float = 1.0
+    # OpenAI logit_bias (token id as a string -> bias in [-100, 100]); vLLM's allowed_token_ids
+    # and bad_words
+    logit_bias: Optional[Dict[str, float]] = None
+    allowed_token_ids: Optional[List[int]] = None
+    bad_words: Optional[List[str]] = None
     # structured outputs: vLLM's extra parameters and the OpenAI response_format
     structured_outputs: Optional[Dict] = None
     guided_json: Optional[Union[Dict, str]] = None
@@ -67,7 +72,11 @@ class _Sampling(BaseModel):
                               frequency_penalty=self.frequency_penalty,
                               repetition_penalty=self.repetition_penalty,
                               logprobs=self.num_logprobs(),
-                              structured_outputs=self.structured())
+                              structured_outputs=self.structured(),
+                              logit_bias=({int(k): v for k, v in self.logit_bias.items()}
+                                          if self.logit_bias else None),
+                              allowed_token_ids=self.allowed_token_ids,
+                              bad_words=self.bad_words)
 
 
 class CompletionRequest(_Sampling):

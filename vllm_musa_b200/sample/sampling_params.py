@@ -2,7 +2,7 @@
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any, List, Optional, Union
+from typing import Any, Dict, List, Optional, Union
 
 
 @dataclass
@@ -64,6 +64,12 @@ class SamplingParams:
     logprobs: Optional[int] = None
     # constrained decoding (JSON schema / regex / choice / grammar); a dict is accepted too
     structured_outputs: Optional[Any] = None
+    # vLLM / OpenAI logits processors: token id -> bias added to the raw logits (clamped to
+    # [-100, 100]); the only tokens that may be drawn; words (strings) that are never completed
+    # (the last token of a word is banned when the output ends with the rest of it)
+    logit_bias: Optional[Dict[int, float]] = None
+    allowed_token_ids: Optional[List[int]] = None
+    bad_words: Optional[List[str]] = None
 
     def __post_init__(self):
         if isinstance(self.structured_outputs, dict):
@@ -91,10 +97,26 @@ class SamplingParams:
         self.stop = [x for x in self.stop if x]
         if self.temperature < 1e-5:
             self.temperature = 0.0  # greedy
+        if self.logit_bias:
+            self.logit_bias = {int(k): max(-100.0, min(100.0, float(v)))
+                               for k, v in self.logit_bias.items()}
+        else:
+            self.logit_bias = None
+        if self.allowed_token_ids is not None:
+            self.allowed_token_ids = sorted({int(t) for t in self.allowed_token_ids})
+            if not self.allowed_token_ids:
+                raise ValueError("allowed_token_ids must not be empty")
+        if isinstance(self.bad_words, str):
+            self.bad_words = [self.bad_words]
+        self.bad_words = [w for w in (self.bad_words or []) if w] or None
 
     @property
     def greedy(self) -> bool:
         return self.temperature == 0.0
+
+    @property
+    def has_logits_processors(self) -> bool:
+        return bool(self.logit_bias or self.allowed_token_ids or self.bad_words)
 
     @property
     def has_penalties(self) -> bool:
