@@ -125,3 +125,42 @@ def test_special_requests_beside_speculative_decoding():
         for t in x:
             assert abs(x[t].logprob - y[t].logprob) < 1e-4
     assert sch.spec_accepted() > 0
+
+
+def test_logprobs_modes():
+    """logprobs_mode: raw_logits reports the model's logits; processed_logprobs the
+    log_softmax of the logits after the penalties; processed_logits those logits divided by
+    the temperature."""
+    cfg = tiny_llama()
+    ref = ReferenceDecoder(cfg, dict(dummy_weights(cfg, seed=0, std=0.02)))
+    p = _prompts(1, 16, seed=12)[0]
+
+    def run(mode, sp):
+        llm = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=64,
+                  max_model_len=128, max_num_seqs=4, max_num_batched_tokens=256,
+                  logprobs_mode=mode)
+        return llm.generate([p], sp)[0].outputs[0]
+
+    c = run("raw_logits", SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True,
+                                         logprobs=2))
+    for k, (t, d) in enumerate(zip(c.token_ids, c.logprobs)):
+        l = ref.logits(p + c.token_ids[:k])[-1]
+        assert abs(d[t].logprob - float(l[t])) < 1e-4 and d[t].rank == 1
+    rep = 1.5
+    c = run("processed_logprobs", SamplingParams(temperature=0.0, max_tokens=4,
+                                                 ignore_eos=True, logprobs=2,
+                                                 repetition_penalty=rep))
+    for k, (t, d) in enumerate(zip(c.token_ids, c.logprobs)):
+        l = _penalised(ref.logits(p + c.token_ids[:k])[-1], p, c.token_ids[:k], rep, 0.0, 0.0)
+        lp = torch.log_softmax(l, -1)
+        assert abs(d[t].logprob - float(lp[t])) < 1e-4
+    temp = 0.7
+    c = run("processed_logits", SamplingParams(temperature=temp, max_tokens=4, seed=4,
+                                               ignore_eos=True, logprobs=1,
+                                               repetition_penalty=rep))
+    for k, (t, d) in enumerate(zip(c.token_ids, c.logprobs)):
+        l = _penalised(ref.logits(p + c.token_ids[:k])[-1], p, c.token_ids[:k], rep, 0.0, 0.0)
+        assert abs(d[t].logprob - float(l[t]) / temp) < 1e-4
+    import pytest
+    with pytest.raises(ValueError):
+        run("softmax", SamplingParams(max_tokens=1))

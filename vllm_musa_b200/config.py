@@ -317,6 +317,9 @@ class LoRAConfig:
     max_lora_rank: int = 64
 
 
+LOGPROBS_MODES = ("raw_logprobs", "raw_logits", "processed_logprobs", "processed_logits")
+
+
 @dataclass
 class EngineConfig:
     model: ModelConfig = field(default_factory=ModelConfig)
@@ -332,6 +335,14 @@ class EngineConfig:
     cuda_graph_sizes: Optional[list] = None
     speculative: SpeculativeConfig = field(default_factory=SpeculativeConfig)
     lora: LoRAConfig = field(default_factory=lambda: LoRAConfig())
+    # what ``logprobs`` report (vLLM's logprobs_mode): raw_logprobs (log_softmax of the model's
+    # logits, the default), raw_logits, processed_logprobs / processed_logits (after penalties,
+    # logit bias, bad words, token masks and the temperature division)
+    logprobs_mode: str = "raw_logprobs"
+
+    def __post_init__(self):
+        if self.logprobs_mode not in LOGPROBS_MODES:
+            raise ValueError(f"logprobs_mode must be one of {LOGPROBS_MODES}")
 
     def replace(self, **kw: Any) -> "EngineConfig":
         return dataclasses.replace(self, **kw)

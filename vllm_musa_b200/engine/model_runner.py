@@ -276,10 +276,12 @@ class ModelRunner:
             self.logits_log.append(logits.detach().float().cpu())
         ex = self._extras
         raw = None
+        mode = self.cfg.logprobs_mode
         if ex is not None:
             if ex.lp_rows:
                 idx = torch.tensor(ex.lp_rows, dtype=torch.int64, device=logits.device)
-                raw = logits.index_select(0, idx)
+                if mode.startswith("raw"):
+                    raw = logits.index_select(0, idx)
             if ex.entries is not None and ex.entries.numel():
                 dev = logits.device
                 ops.apply_penalties(logits, ex.entries.to(dev), ex.rep.to(dev), ex.pres.to(dev),
@@ -298,6 +300,11 @@ class ModelRunner:
                     logits, ex.bitmask.to(dev),
                     torch.tensor(ex.mask_rows, dtype=_I32, device=dev),
                     getattr(self.model, "vocab_start", 0))
+        if ex is not None and ex.lp_rows and not mode.startswith("raw"):
+            raw = logits.index_select(0, idx)  # processed: after penalties / bias / masks
+            if sampling:
+                t = b.d["temperature"][:S].index_select(0, idx).float()
+                raw = raw / torch.where(t > 0, t, torch.ones_like(t)).unsqueeze(1)
         if sampling:
             ids = self.sampler(logits, b.d["temperature"][:S], b.d["top_k"][:S],
                                b.d["top_p"][:S], b.d["min_p"][:S], b.d["seeds"][:S],
@@ -308,7 +315,8 @@ class ModelRunner:
             if self.sampler.tp > 1:  # vocab-sharded rows: the full distribution
                 raw = self.sampler.comm.all_gather(raw, dim=1)
             sel = ids.index_select(0, idx)
-            ex.logprobs = [t.cpu() for t in ops.sampling.token_logprobs(raw, sel, ex.lp_k)]
+            ex.logprobs = [t.cpu() for t in ops.sampling.token_logprobs(
+                raw, sel, ex.lp_k, as_logits=mode.endswith("logits"))]
         return ids
 
     # ------------------------------------------------------------------ pipeline parallelism

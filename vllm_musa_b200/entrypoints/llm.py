@@ -45,7 +45,8 @@ class LLM:
                  cuda_graph_sizes: Optional[list] = None, num_layers: Optional[int] = None,
                  speculative_config: Optional[dict] = None,
                  enable_lora: bool = False, max_loras: int = 4, max_lora_rank: int = 64,
-                 kv_cache_dtype: Optional[str] = None, **unused):
+                 kv_cache_dtype: Optional[str] = None, logprobs_mode: str = "raw_logprobs",
+                 **unused):
         path = None
         if isinstance(model, ModelConfig):
             mcfg = model
@@ -83,7 +84,8 @@ class LLM:
             enforce_eager=enforce_eager, cuda_graph_sizes=cuda_graph_sizes,
             speculative=SpeculativeConfig.from_dict(speculative_config),
             lora=LoRAConfig(enable_lora=enable_lora, max_loras=max_loras,
-                            max_lora_rank=max_lora_rank))
+                            max_lora_rank=max_lora_rank),
+            logprobs_mode=logprobs_mode)
         tok = tokenizer if tokenizer is not None else _load_tokenizer(path)
         self.executor = None
         self.dp_size, self.dp_rank = 1, 0

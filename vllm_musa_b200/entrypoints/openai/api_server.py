@@ -246,6 +246,11 @@ def make_arg_parser(p: Optional[argparse.ArgumentParser] = None) -> argparse.Arg
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--device", default="cuda")
     p.add_argument("--num-gpu-blocks", type=int, default=None)
+    p.add_argument("--kv-cache-dtype", default=None,
+                   help="auto | fp8 | turboquant_k8v4 | turboquant_4bit_nc | ...")
+    p.add_argument("--logprobs-mode", default="raw_logprobs",
+                   choices=["raw_logprobs", "raw_logits", "processed_logprobs",
+                            "processed_logits"])
     return p
 
 
@@ -264,7 +269,9 @@ def build_llm(args):
                gpu_memory_utilization=args.gpu_memory_utilization,
                enforce_eager=args.enforce_eager,
                enable_prefix_caching=not args.no_enable_prefix_caching, seed=args.seed,
-               device=args.device, num_gpu_blocks=args.num_gpu_blocks)
+               device=args.device, num_gpu_blocks=args.num_gpu_blocks,
+               kv_cache_dtype=getattr(args, "kv_cache_dtype", None),
+               logprobs_mode=getattr(args, "logprobs_mode", "raw_logprobs"))
 
 
 def parse_lora_modules(specs) -> dict:

@@ -173,10 +173,11 @@ def penalty_entries(rows_tokens) -> torch.Tensor:
     return torch.from_numpy(np.concatenate(parts).astype(np.int32))
 
 
-def token_logprobs(raw: torch.Tensor, tokens: torch.Tensor, k: int):
-    """Log-probabilities from raw logits rows [n, V]: (top-k ids [n, k], top-k logprobs [n, k],
-    the given tokens' logprobs [n], their ranks [n] (1 = most likely))."""
-    lp = torch.log_softmax(raw.float(), dim=-1)
+def token_logprobs(raw: torch.Tensor, tokens: torch.Tensor, k: int, as_logits: bool = False):
+    """Log-probabilities from logits rows [n, V]: (top-k ids [n, k], top-k logprobs [n, k],
+    the given tokens' logprobs [n], their ranks [n] (1 = most likely)); ``as_logits`` reports
+    the logits themselves instead of their log_softmax (same ids and ranks)."""
+    lp = raw.float() if as_logits else torch.log_softmax(raw.float(), dim=-1)
     tok_lp = lp.gather(1, tokens.view(-1, 1).long()).squeeze(1)
     rank = (lp > tok_lp.unsqueeze(1)).sum(1) + 1
     if k > 0:
