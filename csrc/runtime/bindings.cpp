@@ -44,7 +44,8 @@ void register_runtime(py::module_& m) {
       .def_readwrite("top_k", &SamplingCfg::top_k)
       .def_readwrite("top_p", &SamplingCfg::top_p)
       .def_readwrite("min_p", &SamplingCfg::min_p)
-      .def_readwrite("seed", &SamplingCfg::seed);
+      .def_readwrite("seed", &SamplingCfg::seed)
+      .def_readwrite("no_prefix_cache", &SamplingCfg::no_prefix_cache);
 
   py::class_<SchedulerConfig>(m, "SchedulerConfig")
       .def(py::init<>())

@@ -166,7 +166,7 @@ bool Scheduler::ensure_blocks(Request& r, int num_tokens) {
 }
 
 void Scheduler::admit_prefix(Request& r) {
-  if (!cfg_.prefix_caching) return;
+  if (!cfg_.prefix_caching || r.sp.no_prefix_cache) return;
   const int bs = cfg_.block_size;
   const int n_full = ((int)r.tokens.size() - 1) / bs;  // keep >= 1 token to compute
   uint64_t parent = 0;

@@ -34,6 +34,7 @@ struct SamplingCfg {
   float top_p = 1.f;
   float min_p = 0.f;
   int64_t seed = 0;
+  bool no_prefix_cache = false;  // compute every prompt token (e.g. prompt log-probabilities)
 };
 
 struct Request {

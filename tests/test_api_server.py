@@ -89,3 +89,25 @@ def test_bad_request(client):
     c, _ = client
     r = c.post("/v1/completions", json={"prompt": list(range(300)), "max_tokens": 4})
     assert r.status_code == 400
+
+
+def test_completion_logits_processors_and_prompt_logprobs(client):
+    """logit_bias (string keys, OpenAI), allowed_token_ids and prompt_logprobs through the
+    server: a +100 bias wins every step, allowed ids bound the output, prompt_logprobs lists
+    None then one entry per later prompt token."""
+    c, _ = client
+    prompt = list(range(50, 70))
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 4, "temperature": 0,
+                                        "ignore_eos": True, "logit_bias": {"321": 100}}).json()
+    assert r["choices"][0]["token_ids"] == [321] * 4
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 5, "temperature": 0.9,
+                                        "ignore_eos": True, "allowed_token_ids": [7, 8, 9],
+                                        "prompt_logprobs": 1}).json()
+    ch = r["choices"][0]
+    assert set(ch["token_ids"]) <= {7, 8, 9}
+    plp = ch["prompt_logprobs"]
+    assert len(plp) == len(prompt) and plp[0] is None
+    assert all(str(t) in d for t, d in zip(prompt[1:], plp[1:]))
+    bad = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 2,
+                                          "logit_bias": {"5000": 1}})
+    assert bad.status_code == 400

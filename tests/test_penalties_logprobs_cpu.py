@@ -164,3 +164,30 @@ def test_logprobs_modes():
     import pytest
     with pytest.raises(ValueError):
         run("softmax", SamplingParams(max_tokens=1))
+
+
+def test_prompt_logprobs_match_reference():
+    """prompt_logprobs: every prompt position after the first carries the log_softmax of the
+    reference logits at the previous position (the prompt token's own entry plus the top k),
+    also when the prompt is prefilled in chunks and when a prefix of it is cached by another
+    request (the request recomputes its whole prompt)."""
+    cfg = tiny_llama()
+    ref = ReferenceDecoder(cfg, dict(dummy_weights(cfg, seed=0, std=0.02)))
+    p = _prompts(1, 40, seed=13)[0]
+    for budget in (256, 16):
+        llm = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=64,
+                  max_model_len=128, max_num_seqs=4, max_num_batched_tokens=budget)
+        llm.generate([p], SamplingParams(temperature=0.0, max_tokens=2))  # caches the prefix
+        o = llm.generate([p], SamplingParams(temperature=0.0, max_tokens=3, prompt_logprobs=2))[0]
+        plp = o.prompt_logprobs
+        assert len(plp) == len(p) and plp[0] is None
+        lp = torch.log_softmax(ref.logits(p), -1)  # row j predicts token j + 1
+        for j in range(1, len(p)):
+            d = plp[j]
+            assert abs(d[p[j]].logprob - float(lp[j - 1, p[j]])) < 1e-4
+            assert d[p[j]].rank == int((lp[j - 1] > lp[j - 1, p[j]]).sum()) + 1
+            top = torch.topk(lp[j - 1], 2).indices.tolist()
+            assert set(top) <= set(d)
+        plain = llm.generate([p], SamplingParams(temperature=0.0, max_tokens=3))[0]
+        assert plain.prompt_logprobs is None
+        assert o.outputs[0].token_ids == plain.outputs[0].token_ids

@@ -55,6 +55,7 @@ class _Req:
     lora: Optional[object] = None         # LoRARequest of the request (None: base model)
     lora_slot: int = -1
     bad_words_ids: Optional[list] = None  # token-id sequences of the request's bad words
+    prompt_logprobs: Optional[list] = None  # per prompt position (None first), if requested
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -232,7 +233,9 @@ class LLMEngine:
             if not 0 <= t < V:
                 raise ValueError(f"token id {t} is outside the vocabulary (size {V})")
         special = params.has_penalties or params.logprobs is not None or so is not None or \
-            bool(params.stop) or lora is not None or params.has_logits_processors
+            bool(params.stop) or lora is not None or params.has_logits_processors or \
+            params.prompt_logprobs is not None
+        sp.no_prefix_cache = params.prompt_logprobs is not None
         # with speculative decoding configured, these requests simply decode without drafts
         # (their penalties, log-probabilities, grammars, stop strings and adapters apply per
         # drawn token); the other requests of the batch keep theirs
@@ -242,6 +245,8 @@ class LLMEngine:
         r = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
         if params.logprobs is not None:
             r.logprobs = []
+        if params.prompt_logprobs is not None:
+            r.prompt_logprobs = [None]
         r.matcher = matcher
         r.lora, r.lora_slot = lora, lora_slot
         if params.bad_words:
@@ -344,6 +349,8 @@ class LLMEngine:
         sampled = self.runner.execute(plan, extras)
         if extras is not None and extras.logprobs is not None:
             self._record_logprobs(plan, extras, sampled)
+        if extras is not None and extras.prompt_logprobs is not None:
+            self._record_prompt_logprobs(extras)
         if extras is not None and extras.mask_rows:
             self._advance_grammars(plan, extras, sampled)
         finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
@@ -425,19 +432,73 @@ class LLMEngine:
             if p.logprobs is not None:
                 lp_rows.append(row)
                 k = max(k, p.logprobs)
+        plp = self._prompt_logprob_rows(plan)
         lora = self._lora_batch(plan)
-        if not rows_tok and not lp_rows and not mask_rows and lora is None and not bias:
+        if not rows_tok and not lp_rows and not mask_rows and lora is None and not bias and \
+                plp is None:
             return None
         entries = penalty_entries(rows_tok) if rows_tok else None
         bitmask = self._token_masks(matchers, allowed) if matchers else None
         ex = StepExtras(entries, rep, pres, freq, lp_rows, k, bitmask, mask_rows)
         ex.lora = lora
         ex.row_req = row_req
+        ex.plp = plp
         if bias:
             ex.bias = (torch.tensor([b[0] for b in bias], dtype=torch.int64),
                        torch.tensor([b[1] for b in bias], dtype=torch.int64),
                        torch.tensor([b[2] for b in bias], dtype=torch.float32))
         return ex
+
+    def _prompt_logprob_rows(self, plan):
+        """Step rows whose next token is a prompt token of a request asking for prompt
+        log-probabilities: (rows, target tokens, top-k, [(request id, row count)]) or None."""
+        if not any(r.prompt_logprobs is not None for r in self._special.values()):
+            return None
+        h = self.runner.buf.h
+        cu = h["cu_q"][:plan.num_reqs + 1].tolist()
+        pos = h["positions"]
+        rows, targets, owners, k = [], [], [], 0
+        for i, iid in enumerate(plan.req_ids):
+            r = self._special.get(iid)
+            if r is None or r.prompt_logprobs is None:
+                continue
+            P = len(r.prompt_token_ids)
+            have = len(r.prompt_logprobs)  # positions already recorded (a recompute repeats)
+            start = int(pos[cu[i]])
+            n = 0
+            for j in range(cu[i + 1] - cu[i]):
+                p = start + j  # this row predicts token p + 1
+                if p + 1 >= P:
+                    break
+                if p + 1 < have:
+                    continue
+                rows.append(cu[i] + j)
+                targets.append(r.prompt_token_ids[p + 1])
+                n += 1
+            if n:
+                owners.append((iid, n))
+                k = max(k, r.params.prompt_logprobs)
+        if not rows:
+            return None
+        return (torch.tensor(rows, dtype=torch.int64), torch.tensor(targets, dtype=torch.int64),
+                k, owners)
+
+    def _record_prompt_logprobs(self, extras) -> None:
+        from ..outputs import Logprob
+        ids, vals, tok_lp, rank = (t.tolist() for t in extras.prompt_logprobs)
+        at = 0
+        for iid, n in extras.plp[3]:
+            r = self._reqs.get(iid)
+            for j in range(at, at + n):
+                if r is None:
+                    continue
+                tok = extras.plp[1][j].item()
+                d = {tok: Logprob(tok_lp[j], int(rank[j]))}
+                for m in range(r.params.prompt_logprobs):
+                    if ids[j][m] not in d:
+                        d[ids[j][m]] = Logprob(vals[j][m], m + 1)
+                r.prompt_logprobs.append(d)
+            at += n
 
     def _token_masks(self, matchers, allowed) -> torch.Tensor:
         """int32 [len(matchers), words] next-token bitmasks: a grammar's mask where the row has
@@ -554,13 +615,24 @@ class LLMEngine:
         ltimes = [par["done"][k].metrics.finished_time for k in range(par["n"])]
         m = RequestMetrics(par["arrival"], min([t for t in ftimes if t] or [None]) if any(ftimes) else None,
                            max([t for t in ltimes if t] or [None]) if any(ltimes) else None)
-        return RequestOutput(r.parent, par["prompt_ids"], comps, True, par["prompt"], m)
+        out = RequestOutput(r.parent, par["prompt_ids"], comps, True, par["prompt"], m)
+        out.prompt_logprobs = par["done"][0].prompt_logprobs
+        return out
+
+    def _decode(self, ids, params) -> str:
+        kw = {"skip_special_tokens": params.skip_special_tokens}
+        if not params.spaces_between_special_tokens:
+            kw["spaces_between_special_tokens"] = False
+        try:
+            return self.tokenizer.decode(ids, **kw)
+        except TypeError:  # tokenizers without the spacing option
+            return self.tokenizer.decode(ids, skip_special_tokens=params.skip_special_tokens)
 
     def _make_output(self, r: _Req, reason, finished, first=None, last=None) -> RequestOutput:
         text = ""
         if self.tokenizer is not None and r.params.detokenize:
             try:
-                text = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
+                text = self._decode(r.tokens, r.params)
             except Exception:  # pragma: no cover - tokenizer specific
                 text = ""
         stop_reason = None
@@ -571,7 +643,10 @@ class LLMEngine:
                                 logprobs=list(r.logprobs) if r.logprobs is not None else None,
                                 stop_reason=stop_reason)
         m = RequestMetrics(r.arrival, first if first is not None else r.first_token_time, last)
-        return RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
+        out = RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
+        if r.prompt_logprobs is not None:
+            out.prompt_logprobs = list(r.prompt_logprobs)
+        return out
 
     def _follower_add(self, request_id, prompt_ids, params, arrival, prompt, lora_request=None):
         sync, self.sync = self.sync, None  # apply locally without re-recording

@@ -111,6 +111,8 @@ class StepExtras:
         self.row_req = {}  # sampling row -> request id of the rows above
         self.bias = None   # (rows, token ids, values) added to the raw logits (logit_bias,
         #                    bad words as -inf)
+        self.plp = None    # prompt log-probabilities: (rows, target tokens, top-k, owners)
+        self.prompt_logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
         self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
 
 
@@ -277,6 +279,8 @@ class ModelRunner:
         ex = self._extras
         raw = None
         mode = self.cfg.logprobs_mode
+        if ex is not None and ex.plp is not None:
+            ex.prompt_logprobs = self._prompt_logprobs(hidden, ex.plp, mode)
         if ex is not None:
             if ex.lp_rows:
                 idx = torch.tensor(ex.lp_rows, dtype=torch.int64, device=logits.device)
@@ -318,6 +322,23 @@ class ModelRunner:
             ex.logprobs = [t.cpu() for t in ops.sampling.token_logprobs(
                 raw, sel, ex.lp_k, as_logits=mode.endswith("logits"))]
         return ids
+
+    def _prompt_logprobs(self, hidden: torch.Tensor, plp, mode: str) -> list:
+        """Log-probabilities of prompt tokens from the step's hidden rows, 256 rows at a time
+        (each block's logits are [256, V] fp32): (top ids, top values, token value, rank), on
+        the host.  Prompt positions see raw logits (no sampling parameters apply to them)."""
+        rows, targets, k, _ = plp
+        dev = hidden.device
+        parts = []
+        for a in range(0, rows.numel(), 256):
+            r = rows[a:a + 256].to(dev)
+            lg = self.model.compute_logits(hidden.index_select(0, r).contiguous())
+            if self.sampler.tp > 1:
+                lg = self.sampler.comm.all_gather(lg, dim=1)
+            lg = lg[:, :self.model.cfg.vocab_size]
+            parts.append([t.cpu() for t in ops.sampling.token_logprobs(
+                lg, targets[a:a + 256].to(dev), k, as_logits=mode.endswith("logits"))])
+        return [torch.cat([p[i] for p in parts]) for i in range(4)]
 
     # ------------------------------------------------------------------ pipeline parallelism
     def _pp_chunks(self, meta: AttnMetadata, T: int, R: int) -> list:
@@ -397,10 +418,10 @@ class ModelRunner:
             ids = torch.empty(S, dtype=torch.int64, device=dev)
         dist.broadcast(ids, src=st.pp_ranks[-1], group=st.pp_group)
         ex = self._extras
-        if ex is not None and ex.lp_rows:
-            obj = [ex.logprobs]
+        if ex is not None and (ex.lp_rows or ex.plp is not None):
+            obj = [ex.logprobs, ex.prompt_logprobs]
             dist.broadcast_object_list(obj, src=st.pp_ranks[-1], group=st.pp_cpu_group)
-            ex.logprobs = obj[0]
+            ex.logprobs, ex.prompt_logprobs = obj
         return ids
 
     def _meta(self, T: int, R: int, nd: int, npf: int, max_seq_len: int,

@@ -21,7 +21,8 @@ from typing import List, Optional
 
 from .protocol import (ChatChoice, ChatCompletionRequest, ChatCompletionResponse, ChatMessage,
                        CompletionChoice, CompletionRequest, CompletionResponse, ErrorResponse,
-                       ModelCard, ModelList, Usage, chat_logprobs, completion_logprobs)
+                       ModelCard, ModelList, Usage, chat_logprobs, completion_logprobs,
+                       prompt_logprobs_json)
 
 log = logging.getLogger("vllm_musa_b200")
 
@@ -161,15 +162,19 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
                         yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}", lora)
-                                      for idx, ids, _, p in jobs])
+        try:
+            outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}", lora)
+                                          for idx, ids, _, p in jobs])
+        except ValueError as e:  # rejected by the engine (e.g. a token id off the vocabulary)
+            return err(str(e))
         choices, n_prompt, n_gen = [], 0, 0
         for (idx, ids, text, _), o in zip(jobs, outs):
             c = o.outputs[0]
             body = (text or "") + c.text if req.echo else c.text
             choices.append(CompletionChoice(index=idx, text=body, token_ids=c.token_ids,
                                             finish_reason=c.finish_reason,
-                                            logprobs=completion_logprobs(c, tok)))
+                                            logprobs=completion_logprobs(c, tok),
+                                            prompt_logprobs=prompt_logprobs_json(o, tok)))
             n_prompt += len(ids)
             n_gen += len(c.token_ids)
         return CompletionResponse(id=rid, model=model_name, choices=choices,
@@ -203,10 +208,13 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        outs = await asyncio.gather(*[
-            run_one(ids, SamplingParams(**{**p.__dict__, "n": 1,
-                                           "seed": (p.seed + k) if p.seed is not None else None}),
-                    f"{rid}-{k}", lora) for k in range(p.n)])
+        try:
+            outs = await asyncio.gather(*[
+                run_one(ids, SamplingParams(**{**p.__dict__, "n": 1,
+                                               "seed": (p.seed + k) if p.seed is not None else None}),
+                        f"{rid}-{k}", lora) for k in range(p.n)])
+        except ValueError as e:
+            return err(str(e))
         choices = [ChatChoice(index=k, message=ChatMessage(role="assistant", content=o.outputs[0].text),
                               finish_reason=o.outputs[0].finish_reason,
                               logprobs=chat_logprobs(o.outputs[0], tok, req.top_logprobs or 0))

@@ -33,6 +33,10 @@ class _Sampling(BaseModel):
     logit_bias: Optional[Dict[str, float]] = None
     allowed_token_ids: Optional[List[int]] = None
     bad_words: Optional[List[str]] = None
+    # vLLM extensions: prompt log-probabilities, detokenization options
+    prompt_logprobs: Optional[int] = None
+    skip_special_tokens: bool = True
+    spaces_between_special_tokens: bool = True
     # structured outputs: vLLM's extra parameters and the OpenAI response_format
     structured_outputs: Optional[Dict] = None
     guided_json: Optional[Union[Dict, str]] = None
@@ -76,7 +80,10 @@ class _Sampling(BaseModel):
                               logit_bias=({int(k): v for k, v in self.logit_bias.items()}
                                           if self.logit_bias else None),
                               allowed_token_ids=self.allowed_token_ids,
-                              bad_words=self.bad_words)
+                              bad_words=self.bad_words,
+                              prompt_logprobs=self.prompt_logprobs,
+                              skip_special_tokens=self.skip_special_tokens,
+                              spaces_between_special_tokens=self.spaces_between_special_tokens)
 
 
 class CompletionRequest(_Sampling):
@@ -115,6 +122,7 @@ class CompletionChoice(BaseModel):
     token_ids: Optional[List[int]] = None
     finish_reason: Optional[str] = None
     logprobs: Optional[Dict] = None
+    prompt_logprobs: Optional[List[Optional[Dict]]] = None
 
 
 class CompletionResponse(BaseModel):
@@ -140,6 +148,17 @@ def _tok_str(tokenizer, t: int) -> str:
         return tokenizer.decode([t])
     except Exception:  # pragma: no cover - tokenizer specific
         return str(t)
+
+
+def prompt_logprobs_json(o, tokenizer) -> Optional[List[Optional[Dict]]]:
+    """vLLM's ``prompt_logprobs`` field: per prompt position None or {token id: {logprob,
+    rank, decoded_token}}."""
+    if o.prompt_logprobs is None:
+        return None
+    return [None if d is None else
+            {str(t): {"logprob": v.logprob, "rank": v.rank,
+                      "decoded_token": _tok_str(tokenizer, t)} for t, v in d.items()}
+            for d in o.prompt_logprobs]
 
 
 def completion_logprobs(c, tokenizer) -> Optional[Dict]:

@@ -47,6 +47,8 @@ class RequestOutput:
     finished: bool
     prompt: Optional[str] = None
     metrics: RequestMetrics = field(default_factory=RequestMetrics)
+    # per prompt position: {token id: Logprob} (None at position 0), when requested
+    prompt_logprobs: Optional[List[Optional[Dict[int, Logprob]]]] = None
 
     def tpot(self) -> Optional[float]:
         m = self.metrics

@@ -70,6 +70,13 @@ class SamplingParams:
     logit_bias: Optional[Dict[int, float]] = None
     allowed_token_ids: Optional[List[int]] = None
     bad_words: Optional[List[str]] = None
+    # log-probabilities of every prompt token given the tokens before it (top ``k`` per
+    # position plus the prompt token's own; the first position has none); the request's
+    # prompt is computed in full (no prefix-cache reuse)
+    prompt_logprobs: Optional[int] = None
+    # detokenization of the returned text
+    skip_special_tokens: bool = True
+    spaces_between_special_tokens: bool = True
 
     def __post_init__(self):
         if isinstance(self.structured_outputs, dict):
@@ -92,6 +99,8 @@ class SamplingParams:
             raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
         if self.logprobs is not None and not 0 <= self.logprobs <= 20:
             raise ValueError("logprobs must be in [0, 20]")
+        if self.prompt_logprobs is not None and not 0 <= self.prompt_logprobs <= 20:
+            raise ValueError("prompt_logprobs must be in [0, 20]")
         if isinstance(self.stop, str):
             self.stop = [self.stop]
         self.stop = [x for x in self.stop if x]
