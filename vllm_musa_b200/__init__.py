@@ -13,6 +13,7 @@ from __future__ import annotations
 __version__ = "0.1.0"
 
 __all__ = ["LLM", "LLMEngine", "SamplingParams", "StructuredOutputsParams", "LoRARequest",
+           "BeamSearchParams", "PoolingParams",
            "EngineConfig", "ModelConfig", "b200_platform_plugin", "register_custom_ops",
            "__version__"]
 
@@ -24,7 +25,8 @@ def __getattr__(name):
     if name == "LLMEngine":
         from .engine.llm_engine import LLMEngine
         return LLMEngine
-    if name in ("SamplingParams", "StructuredOutputsParams"):
+    if name in ("SamplingParams", "StructuredOutputsParams", "BeamSearchParams",
+                "PoolingParams"):
         from .sample import sampling_params
         return getattr(sampling_params, name)
     if name == "LoRARequest":

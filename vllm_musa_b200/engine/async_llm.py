@@ -139,7 +139,8 @@ class AsyncLLM:
             return
         comp = out.outputs[0]
         st.token_ids = list(comp.token_ids)
-        if st.params.detokenize and self.tokenizer is not None:
+        # embedding requests (PoolingParams) carry no text options
+        if getattr(st.params, "detokenize", False) and self.tokenizer is not None:
             st.text = self._decode(st.token_ids)
             comp.text = st.text
             for s in st.params.stop:

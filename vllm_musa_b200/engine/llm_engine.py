@@ -56,6 +56,9 @@ class _Req:
     lora_slot: int = -1
     bad_words_ids: Optional[list] = None  # token-id sequences of the request's bad words
     prompt_logprobs: Optional[list] = None  # per prompt position (None first), if requested
+    pooling: Optional[object] = None        # PoolingParams of an embedding request
+    pool_sum: Optional[object] = None       # running sum of the pooled hidden rows
+    pool_n: int = 0
 
 
 def _mix_seed(a: int, b: int) -> int:
@@ -187,6 +190,19 @@ class LLMEngine:
                     params: Optional[SamplingParams] = None, arrival_time: Optional[float] = None,
                     prompt: Optional[str] = None, lora_request=None) -> None:
         params = params or SamplingParams()
+        from ..sample.sampling_params import PoolingParams
+        if isinstance(params, PoolingParams):
+            if self.sync is not None and self.role == "follower":
+                raise RuntimeError("requests are added on the driver rank only")
+            if self.sync is not None:
+                self.sync.record(("add", request_id, list(prompt_token_ids), params,
+                                  time.time() if arrival_time is None else arrival_time,
+                                  prompt, lora_request))
+            self._add_one(request_id, prompt_token_ids,
+                          SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True),
+                          time.time() if arrival_time is None else arrival_time, prompt,
+                          lora=lora_request, pooling=params)
+            return
         arrival = time.time() if arrival_time is None else arrival_time
         if lora_request is not None and getattr(self.model, "lora", None) is None:
             raise ValueError("lora_request needs LLM(..., enable_lora=True)")
@@ -208,7 +224,7 @@ class LLMEngine:
         self._add_one(request_id, prompt_token_ids, params, arrival, prompt, lora=lora_request)
 
     def _add_one(self, name, prompt_ids, params, arrival, prompt, parent=None, index=0,
-                 lora=None):
+                 lora=None, pooling=None):
         if name in self._by_name:
             raise ValueError(f"duplicate request id {name!r}")
         iid = next(self._ids)
@@ -234,8 +250,10 @@ class LLMEngine:
                 raise ValueError(f"token id {t} is outside the vocabulary (size {V})")
         special = params.has_penalties or params.logprobs is not None or so is not None or \
             bool(params.stop) or lora is not None or params.has_logits_processors or \
-            params.prompt_logprobs is not None
-        sp.no_prefix_cache = params.prompt_logprobs is not None
+            params.prompt_logprobs is not None or pooling is not None
+        # prompt log-probabilities and mean / cls pooling read every prompt row
+        sp.no_prefix_cache = params.prompt_logprobs is not None or \
+            (pooling is not None and pooling.pooling_type != "last")
         # with speculative decoding configured, these requests simply decode without drafts
         # (their penalties, log-probabilities, grammars, stop strings and adapters apply per
         # drawn token); the other requests of the batch keep theirs
@@ -247,6 +265,7 @@ class LLMEngine:
             r.logprobs = []
         if params.prompt_logprobs is not None:
             r.prompt_logprobs = [None]
+        r.pooling = pooling
         r.matcher = matcher
         r.lora, r.lora_slot = lora, lora_slot
         if params.bad_words:
@@ -351,6 +370,8 @@ class LLMEngine:
             self._record_logprobs(plan, extras, sampled)
         if extras is not None and extras.prompt_logprobs is not None:
             self._record_prompt_logprobs(extras)
+        if extras is not None and extras.pooled is not None:
+            self._record_pooled(extras)
         if extras is not None and extras.mask_rows:
             self._advance_grammars(plan, extras, sampled)
         finished = self.scheduler.update(sampled.data_ptr(), plan.num_samples)
@@ -433,9 +454,10 @@ class LLMEngine:
                 lp_rows.append(row)
                 k = max(k, p.logprobs)
         plp = self._prompt_logprob_rows(plan)
+        pool = self._pool_rows(plan)
         lora = self._lora_batch(plan)
         if not rows_tok and not lp_rows and not mask_rows and lora is None and not bias and \
-                plp is None:
+                plp is None and not pool:
             return None
         entries = penalty_entries(rows_tok) if rows_tok else None
         bitmask = self._token_masks(matchers, allowed) if matchers else None
@@ -443,6 +465,7 @@ class LLMEngine:
         ex.lora = lora
         ex.row_req = row_req
         ex.plp = plp
+        ex.pool = pool
         if bias:
             ex.bias = (torch.tensor([b[0] for b in bias], dtype=torch.int64),
                        torch.tensor([b[1] for b in bias], dtype=torch.int64),
@@ -482,6 +505,49 @@ class LLMEngine:
             return None
         return (torch.tensor(rows, dtype=torch.int64), torch.tensor(targets, dtype=torch.int64),
                 k, owners)
+
+    def _pool_rows(self, plan) -> list:
+        """Step rows each embedding request pools: [(request id, first row, end row)] --
+        the last prompt row (last), the prompt rows of the step (mean), the first (cls)."""
+        if not any(r.pooling is not None for r in self._special.values()):
+            return []
+        h = self.runner.buf.h
+        cu = h["cu_q"][:plan.num_reqs + 1].tolist()
+        pos = h["positions"]
+        out = []
+        for i, iid in enumerate(plan.req_ids):
+            r = self._special.get(iid)
+            if r is None or r.pooling is None:
+                continue
+            P = len(r.prompt_token_ids)
+            start = int(pos[cu[i]])
+            q = cu[i + 1] - cu[i]
+            kind = r.pooling.pooling_type
+            if kind == "last" and start <= P - 1 < start + q:
+                a = cu[i] + (P - 1 - start)
+                out.append((iid, a, a + 1))
+            elif kind == "mean" and start < P:
+                out.append((iid, cu[i], cu[i] + min(q, P - start)))
+            elif kind == "cls" and start == 0:
+                out.append((iid, cu[i], cu[i] + 1))
+        return out
+
+    def _record_pooled(self, extras) -> None:
+        for (iid, a, b), v in zip(extras.pool, extras.pooled):
+            r = self._reqs.get(iid)
+            if r is None:
+                continue
+            r.pool_sum = v if r.pool_sum is None else r.pool_sum + v
+            r.pool_n += b - a
+
+    def _embedding(self, r) -> list:
+        pp = r.pooling
+        v = r.pool_sum / max(1, r.pool_n) if pp.pooling_type == "mean" else r.pool_sum
+        if pp.dimensions is not None:
+            v = v[:pp.dimensions]
+        if pp.normalize:
+            v = v / v.norm().clamp_min(1e-12)
+        return v.tolist()
 
     def _record_prompt_logprobs(self, extras) -> None:
         from ..outputs import Logprob
@@ -646,6 +712,8 @@ class LLMEngine:
         out = RequestOutput(r.request_id, r.prompt_token_ids, [comp], finished, r.prompt, m)
         if r.prompt_logprobs is not None:
             out.prompt_logprobs = list(r.prompt_logprobs)
+        if r.pooling is not None and finished and r.pool_sum is not None:
+            out.embedding = self._embedding(r)
         return out
 
     def _follower_add(self, request_id, prompt_ids, params, arrival, prompt, lora_request=None):

@@ -113,6 +113,8 @@ class StepExtras:
         #                    bad words as -inf)
         self.plp = None    # prompt log-probabilities: (rows, target tokens, top-k, owners)
         self.prompt_logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
+        self.pool = []       # embedding requests: (request id, first row, end row) to sum
+        self.pooled = None   # filled by the runner: fp32 host vectors, one per pool entry
         self.logprobs = None  # filled by the runner: (top ids, top logprobs, logprob, rank)
 
 
@@ -281,6 +283,9 @@ class ModelRunner:
         mode = self.cfg.logprobs_mode
         if ex is not None and ex.plp is not None:
             ex.prompt_logprobs = self._prompt_logprobs(hidden, ex.plp, mode)
+        if ex is not None and ex.pool:
+            ex.pooled = list(torch.stack([hidden[a:b].float().sum(0) for _, a, b in ex.pool])
+                             .cpu().unbind(0))
         if ex is not None:
             if ex.lp_rows:
                 idx = torch.tensor(ex.lp_rows, dtype=torch.int64, device=logits.device)
@@ -418,10 +423,10 @@ class ModelRunner:
             ids = torch.empty(S, dtype=torch.int64, device=dev)
         dist.broadcast(ids, src=st.pp_ranks[-1], group=st.pp_group)
         ex = self._extras
-        if ex is not None and (ex.lp_rows or ex.plp is not None):
-            obj = [ex.logprobs, ex.prompt_logprobs]
+        if ex is not None and (ex.lp_rows or ex.plp is not None or ex.pool):
+            obj = [ex.logprobs, ex.prompt_logprobs, ex.pooled]
             dist.broadcast_object_list(obj, src=st.pp_ranks[-1], group=st.pp_cpu_group)
-            ex.logprobs, ex.prompt_logprobs = obj
+            ex.logprobs, ex.prompt_logprobs, ex.pooled = obj
         return ids
 
     def _meta(self, T: int, R: int, nd: int, npf: int, max_seq_len: int,

@@ -160,6 +160,103 @@ class LLM:
                     done[o.request_id] = o
         return [done[r] for r in order]
 
+    def chat(self, messages, sampling_params: Union[SamplingParams, Sequence[SamplingParams],
+                                                    None] = None,
+             lora_request=None, add_generation_prompt: bool = True) -> List[RequestOutput]:
+        """Chat completion offline: ``messages`` is one conversation ([{"role", "content"}, ...])
+        or a list of conversations; each is rendered with the tokenizer's chat template (a
+        ``role: content`` transcript without one) and generated like ``generate``."""
+        from .chat_utils import chat_prompt_ids
+        convs = [messages] if messages and isinstance(messages[0], dict) else list(messages)
+        tok = self.engine.tokenizer
+        prompts = [{"prompt_token_ids": chat_prompt_ids(tok, c, add_generation_prompt)}
+                   for c in convs]
+        return self.generate(prompts, sampling_params, lora_request=lora_request)
+
+    def embed(self, prompts, pooling_params=None, use_tqdm: bool = False) -> list:
+        """Embeddings of the prompts (vLLM's ``LLM.embed``): each prompt runs once and its final
+        hidden states are pooled per ``pooling_params`` (PoolingParams: last token by default,
+        L2-normalised).  Returns EmbeddingRequestOutput objects (``.outputs.embedding``)."""
+        from ..outputs import EmbeddingOutput, EmbeddingRequestOutput
+        from ..sample.sampling_params import PoolingParams
+        if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and
+                                                isinstance(prompts[0], int)):
+            prompts = [prompts]
+        pp = pooling_params or PoolingParams()
+        pps = pp if isinstance(pp, (list, tuple)) else [pp] * len(prompts)
+        order = []
+        for p, q in zip(prompts, pps):
+            ids, text = self._prompt_ids(p)
+            rid = str(self._counter)
+            self._counter += 1
+            self.engine.add_request(rid, ids, q, prompt=text)
+            order.append((rid, ids))
+        done = {}
+        while self.engine.has_unfinished_requests():
+            for o in self.engine.step():
+                if o.finished:
+                    done[o.request_id] = o
+        return [EmbeddingRequestOutput(rid, ids, EmbeddingOutput(done[rid].embedding))
+                for rid, ids in order]
+
+    encode = embed
+
+    def beam_search(self, prompts, params) -> list:
+        """Beam search over the engine (vLLM's ``LLM.beam_search``): each step runs every live
+        beam of every prompt as a one-token request with the top 2 x beam_width
+        log-probabilities (prefix caching serves the shared prefixes), keeps the best
+        beam_width continuations per prompt and sets aside the finished ones.  Returns one
+        BeamSearchOutput per prompt with its best beam_width sequences, best first."""
+        from ..outputs import BeamSearchOutput, BeamSearchSequence
+        if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and
+                                                isinstance(prompts[0], int)):
+            prompts = [prompts]
+        w = params.beam_width
+        eos = self.engine.config.model.eos_token_id
+        base = [self._prompt_ids(p)[0] for p in prompts]
+        live = [[([], [], 0.0)] for _ in base]      # per prompt: (generated, logprobs, cum)
+        done = [[] for _ in base]
+        step_sp = SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True, logprobs=2 * w)
+
+        def score(prompt_len, gen, cum):
+            n = prompt_len + len(gen) - (1 if gen and eos is not None and gen[-1] == eos else 0)
+            return cum / (max(n, 1) ** params.length_penalty)
+
+        for _ in range(params.max_tokens):
+            jobs = [(i, b) for i, beams in enumerate(live) for b in beams]
+            if not jobs:
+                break
+            outs = self.generate([{"prompt_token_ids": base[i] + b[0]} for i, b in jobs],
+                                 step_sp)
+            cands = [[] for _ in base]
+            for (i, (gen, lps, cum)), o in zip(jobs, outs):
+                for tok, lp in o.outputs[0].logprobs[0].items():
+                    cands[i].append((gen + [tok], lps + [lp.logprob], cum + lp.logprob))
+            for i, cs in enumerate(cands):
+                cs.sort(key=lambda c: c[2], reverse=True)
+                keep = []
+                for c in cs:
+                    if not params.ignore_eos and eos is not None and c[0][-1] == eos:
+                        done[i].append(c)
+                    else:
+                        keep.append(c)
+                    if len(keep) == w:
+                        break
+                live[i] = keep
+        tok = self.engine.tokenizer
+        res = []
+        for i, p in enumerate(base):
+            allb = done[i] + live[i]
+            allb.sort(key=lambda c: score(len(p), c[0], c[2]), reverse=True)
+            seqs = []
+            for gen, lps, cum in allb[:w]:
+                text = tok.decode(gen, skip_special_tokens=True) if tok is not None else None
+                fin = "stop" if (eos is not None and gen and gen[-1] == eos and
+                                 not params.ignore_eos) else "length"
+                seqs.append(BeamSearchSequence(list(p) + gen, lps, cum, text, fin))
+            res.append(BeamSearchOutput(seqs))
+        return res
+
     def _generate_dp(self, prompts, sampling_params) -> List[RequestOutput]:
         """Replica k serves prompts k, k + dp, ...; the outputs are exchanged over the world
         group so every rank returns the full list in prompt order."""

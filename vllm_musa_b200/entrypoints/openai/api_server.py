@@ -21,21 +21,16 @@ from typing import List, Optional
 
 from .protocol import (ChatChoice, ChatCompletionRequest, ChatCompletionResponse, ChatMessage,
                        CompletionChoice, CompletionRequest, CompletionResponse, ErrorResponse,
-                       ModelCard, ModelList, Usage, chat_logprobs, completion_logprobs,
+                       DetokenizeRequest, EmbeddingRequest, ModelCard, ModelList,
+                       TokenizeRequest, Usage, chat_logprobs, completion_logprobs,
                        prompt_logprobs_json)
 
 log = logging.getLogger("vllm_musa_b200")
 
 
 def _chat_prompt(tokenizer, messages: List[ChatMessage]) -> List[int]:
-    msgs = [m.model_dump() for m in messages]
-    if tokenizer is None:
-        raise ValueError("chat completions need a tokenizer (serve a checkpoint directory)")
-    if getattr(tokenizer, "chat_template", None):
-        ids = tokenizer.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True)
-        return list(ids["input_ids"] if isinstance(ids, dict) else ids)
-    text = "".join(f"{m['role']}: {m['content']}\n" for m in msgs) + "assistant:"
-    return tokenizer.encode(text)
+    from ..chat_utils import chat_prompt_ids
+    return chat_prompt_ids(tokenizer, [m.model_dump() for m in messages])
 
 
 def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[dict] = None):
@@ -125,6 +120,42 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
         async for o in llm.generate(ids, params, rid, lora_request=lora):
             final = o
         return final
+
+    @app.post("/v1/embeddings")
+    async def embeddings(req: EmbeddingRequest):
+        from ...sample.sampling_params import PoolingParams
+        try:
+            lora_of(req)
+            prompts = encode_prompts(req.input)
+            pp = PoolingParams(pooling_type=req.pooling_type, normalize=req.normalize,
+                               dimensions=req.dimensions)
+            for ids, _ in prompts:
+                if len(ids) + 1 > max_model_len:
+                    raise ValueError(f"input has {len(ids)} tokens; max_model_len is "
+                                     f"{max_model_len}")
+            rid = f"embd-{uuid.uuid4().hex}"
+            outs = await asyncio.gather(*[run_one(ids, pp, f"{rid}-{i}")
+                                          for i, (ids, _) in enumerate(prompts)])
+        except ValueError as e:
+            return err(str(e))
+        n = sum(len(ids) for ids, _ in prompts)
+        data = [{"object": "embedding", "index": i, "embedding": o.embedding}
+                for i, o in enumerate(outs)]
+        return {"object": "list", "data": data, "model": model_name,
+                "usage": {"prompt_tokens": n, "total_tokens": n}}
+
+    @app.post("/tokenize")
+    async def tokenize(req: TokenizeRequest):
+        if tok is None:
+            return err("tokenize needs a tokenizer")
+        ids = list(tok.encode(req.prompt))
+        return {"tokens": ids, "count": len(ids), "max_model_len": max_model_len}
+
+    @app.post("/detokenize")
+    async def detokenize(req: DetokenizeRequest):
+        if tok is None:
+            return err("detokenize needs a tokenizer")
+        return {"prompt": tok.decode(list(req.tokens))}
 
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):

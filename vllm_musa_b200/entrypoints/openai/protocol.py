@@ -215,3 +215,24 @@ class ErrorResponse(BaseModel):
     type: str = "invalid_request_error"
     code: int = 400
     extra: Optional[Dict] = None
+
+
+class EmbeddingRequest(BaseModel):
+    """OpenAI /v1/embeddings: ``input`` is a string, a list of strings, a list of token ids or
+    a list of token-id lists; vLLM's extras choose the pooling."""
+    model: Optional[str] = None
+    input: Union[str, List[str], List[int], List[List[int]]]
+    encoding_format: str = "float"
+    dimensions: Optional[int] = None
+    pooling_type: str = "last"
+    normalize: bool = True
+
+
+class TokenizeRequest(BaseModel):
+    model: Optional[str] = None
+    prompt: str = ""
+
+
+class DetokenizeRequest(BaseModel):
+    model: Optional[str] = None
+    tokens: List[int] = Field(default_factory=list)

@@ -49,6 +49,7 @@ class RequestOutput:
     metrics: RequestMetrics = field(default_factory=RequestMetrics)
     # per prompt position: {token id: Logprob} (None at position 0), when requested
     prompt_logprobs: Optional[List[Optional[Dict[int, Logprob]]]] = None
+    embedding: Optional[List[float]] = None  # pooled hidden state of an embedding request
 
     def tpot(self) -> Optional[float]:
         m = self.metrics
@@ -56,3 +57,32 @@ class RequestOutput:
         if m.first_token_time is None or m.finished_time is None or n < 2:
             return None
         return (m.finished_time - m.first_token_time) / (n - 1)
+
+
+@dataclass
+class BeamSearchSequence:
+    """One beam: prompt + generated token ids, the generated tokens' log-probabilities and
+    their sum, the decoded text of the generated part (with a tokenizer)."""
+    tokens: List[int]
+    logprobs: List[float]
+    cum_logprob: float
+    text: Optional[str] = None
+    finish_reason: Optional[str] = None
+
+
+@dataclass
+class BeamSearchOutput:
+    sequences: List[BeamSearchSequence]
+
+
+@dataclass
+class EmbeddingOutput:
+    embedding: List[float]
+
+
+@dataclass
+class EmbeddingRequestOutput:
+    request_id: str
+    prompt_token_ids: List[int]
+    outputs: EmbeddingOutput
+    finished: bool = True

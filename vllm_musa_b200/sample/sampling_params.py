@@ -131,3 +131,37 @@ class SamplingParams:
     def has_penalties(self) -> bool:
         return (self.repetition_penalty != 1.0 or self.presence_penalty != 0.0 or
                 self.frequency_penalty != 0.0)
+
+
+@dataclass
+class BeamSearchParams:
+    """Offline beam search (``LLM.beam_search``): ``beam_width`` live sequences per prompt, each
+    step expanded by its 2 x beam_width most likely next tokens; finished sequences (EOS unless
+    ``ignore_eos``) are ranked with the live ones by cumulative log-probability divided by
+    (sequence length ** ``length_penalty``)."""
+    beam_width: int
+    max_tokens: int
+    ignore_eos: bool = False
+    length_penalty: float = 1.0
+
+    def __post_init__(self):
+        if self.beam_width < 1 or self.max_tokens < 1:
+            raise ValueError("beam_width and max_tokens must be >= 1")
+
+
+@dataclass
+class PoolingParams:
+    """Embedding requests (``LLM.embed`` / ``/v1/embeddings``): the prompt is run once and its
+    final hidden states are pooled -- ``last`` token (the decoder-embedding default), ``mean``
+    over the prompt, or ``cls`` (the first token) -- then L2-normalised when ``normalize``, and
+    truncated to ``dimensions`` (Matryoshka) when given."""
+    pooling_type: str = "last"
+    normalize: bool = True
+    dimensions: Optional[int] = None
+
+    def __post_init__(self):
+        self.pooling_type = self.pooling_type.lower()
+        if self.pooling_type not in ("last", "mean", "cls"):
+            raise ValueError("pooling_type must be last, mean or cls")
+        if self.dimensions is not None and self.dimensions < 1:
+            raise ValueError("dimensions must be >= 1")
