@@ -45,7 +45,8 @@ void register_runtime(py::module_& m) {
       .def_readwrite("top_p", &SamplingCfg::top_p)
       .def_readwrite("min_p", &SamplingCfg::min_p)
       .def_readwrite("seed", &SamplingCfg::seed)
-      .def_readwrite("no_prefix_cache", &SamplingCfg::no_prefix_cache);
+      .def_readwrite("no_prefix_cache", &SamplingCfg::no_prefix_cache)
+      .def_readwrite("priority", &SamplingCfg::priority);
 
   py::class_<SchedulerConfig>(m, "SchedulerConfig")
       .def(py::init<>())
@@ -56,7 +57,8 @@ void register_runtime(py::module_& m) {
       .def_readwrite("max_blocks_per_seq", &SchedulerConfig::max_blocks_per_seq)
       .def_readwrite("chunked_prefill", &SchedulerConfig::chunked_prefill)
       .def_readwrite("prefix_caching", &SchedulerConfig::prefix_caching)
-      .def_readwrite("long_prefill_threshold", &SchedulerConfig::long_prefill_threshold);
+      .def_readwrite("long_prefill_threshold", &SchedulerConfig::long_prefill_threshold)
+      .def_readwrite("priority_policy", &SchedulerConfig::priority_policy);
 
   py::class_<StepPlan>(m, "StepPlan")
       .def_readonly("num_tokens", &StepPlan::num_tokens)

@@ -111,8 +111,46 @@ void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt,
   r.tokens = prompt;
   r.num_prompt = (int)prompt.size();
   r.sp = sp;
+  r.arrival_seq = arrival_seq_++;
   reqs_.emplace(id, std::move(r));
-  waiting_.push_back(id);
+  enqueue_waiting(id, false);
+}
+
+// FCFS: new requests at the back, preempted ones back at the front.  Priority: both by
+// (priority, arrival), so a preempted request returns to the place its priority gives it.
+void Scheduler::enqueue_waiting(int64_t id, bool front) {
+  if (!cfg_.priority_policy) {
+    if (front)
+      waiting_.push_front(id);
+    else
+      waiting_.push_back(id);
+    return;
+  }
+  const Request& r = reqs_.at(id);
+  auto later = [&](int64_t other) {
+    const Request& o = reqs_.at(other);
+    return o.sp.priority > r.sp.priority ||
+           (o.sp.priority == r.sp.priority && o.arrival_seq > r.arrival_seq);
+  };
+  auto it = std::find_if(waiting_.begin(), waiting_.end(), later);
+  waiting_.insert(it, id);
+}
+
+// The running request to preempt when blocks run out: the most recently admitted (FCFS), or
+// the one that sorts last by (priority, arrival) among those not yet scheduled this step.
+int64_t Scheduler::pick_victim(size_t from) const {
+  // only requests not yet placed in this step's batch (index >= from) can give up blocks
+  if (!cfg_.priority_policy) return running_.back();
+  int64_t best = running_.back();
+  for (size_t k = from; k < running_.size(); ++k) {
+    const int64_t id = running_[k];
+    const Request& a = reqs_.at(id);
+    const Request& b = reqs_.at(best);
+    if (a.sp.priority > b.sp.priority ||
+        (a.sp.priority == b.sp.priority && a.arrival_seq > b.arrival_seq))
+      best = id;
+  }
+  return best;
 }
 
 void Scheduler::release_slot(Request& r) {
@@ -153,7 +191,7 @@ void Scheduler::preempt(Request& r) {
   r.num_cached_prefix = 0;
   r.status = kWaiting;
   r.num_preemptions++;
-  waiting_.push_front(r.id);
+  enqueue_waiting(r.id, true);
 }
 
 bool Scheduler::ensure_blocks(Request& r, int num_tokens) {
@@ -266,8 +304,8 @@ StepPlan Scheduler::schedule() {
     }
     bool self_preempted = false;
     while (!ensure_blocks(r, r.num_computed + q)) {
-      const int64_t victim = running_.back();
-      running_.pop_back();
+      const int64_t victim = pick_victim(i);
+      running_.erase(std::find(running_.begin(), running_.end(), victim));
       preempted = true;
       plan.num_preempted++;
       preempt(reqs_.at(victim));
@@ -289,8 +327,14 @@ StepPlan Scheduler::schedule() {
     const int remaining = (int)r.tokens.size() - r.num_computed;
     int q = std::min(remaining, budget);
     if (cfg_.long_prefill_threshold > 0 && q > 1) q = std::min(q, cfg_.long_prefill_threshold);
-    if (!cfg_.chunked_prefill && q < remaining) break;
-    if (!ensure_blocks(r, r.num_computed + q)) break;
+    if ((!cfg_.chunked_prefill && q < remaining) || !ensure_blocks(r, r.num_computed + q)) {
+      // not admitted this step: give back the prefix-cache blocks admit_prefix pinned, or
+      // waiting requests could hold the whole pool while nothing runs
+      free_request_blocks(r);
+      r.num_computed = 0;
+      r.num_cached_prefix = 0;
+      break;
+    }
     waiting_.pop_front();
     r.status = kRunning;
     if (r.state_slot < 0 && !free_slots_.empty()) {

@@ -35,6 +35,7 @@ struct SamplingCfg {
   float min_p = 0.f;
   int64_t seed = 0;
   bool no_prefix_cache = false;  // compute every prompt token (e.g. prompt log-probabilities)
+  int priority = 0;              // priority policy: lower values are served first
 };
 
 struct Request {
@@ -58,6 +59,7 @@ struct Request {
   int64_t first_token_step = -1;
   int64_t finish_step = -1;
   int num_preemptions = 0;
+  int64_t arrival_seq = 0;  // admission order of add_request (ties of equal priority)
   int num_output() const { return (int)tokens.size() - num_prompt; }
 };
 
@@ -97,6 +99,9 @@ struct SchedulerConfig {
   bool chunked_prefill = true;
   bool prefix_caching = true;
   int long_prefill_threshold = 0;  // 0 = no per-request cap on one prefill chunk
+  // false: first come first served; true: waiting requests are admitted by (priority,
+  // arrival) and the preemption victim is the running request that sorts last
+  bool priority_policy = false;
 };
 
 // Pinned host buffers the scheduler writes each step (capacities fixed at construction).
@@ -197,6 +202,8 @@ class Scheduler {
   bool ensure_blocks(Request& r, int num_tokens);
   void free_request_blocks(Request& r);
   void preempt(Request& r);
+  void enqueue_waiting(int64_t id, bool front);
+  int64_t pick_victim(size_t from) const;
   void admit_prefix(Request& r);
   void register_full_blocks(Request& r);
   uint64_t block_hash(uint64_t parent, const int32_t* toks, int n) const;
@@ -214,6 +221,7 @@ class Scheduler {
   std::vector<int32_t> free_slots_;
   void release_slot(Request& r);
   int64_t step_ = 0;
+  int64_t arrival_seq_ = 0;
 };
 
 }  // namespace rt

@@ -237,6 +237,12 @@ class SchedulerConfig:
     max_model_len: int = 4096
     enable_chunked_prefill: bool = True
     long_prefill_token_threshold: int = 0
+    # "fcfs" or "priority" (requests carry an int priority, lower first; vLLM's policy names)
+    scheduling_policy: str = "fcfs"
+
+    def __post_init__(self):
+        if self.scheduling_policy not in ("fcfs", "priority"):
+            raise ValueError("scheduling_policy must be 'fcfs' or 'priority'")
 
 
 @dataclass

@@ -56,13 +56,13 @@ class AsyncLLM:
     # ------------------------------------------------------------------ API side
     async def generate(self, prompt_ids: List[int], params: SamplingParams,
                        request_id: Optional[str] = None, prompt: Optional[str] = None,
-                       lora_request=None) -> AsyncIterator[RequestOutput]:
+                       lora_request=None, priority: int = 0) -> AsyncIterator[RequestOutput]:
         rid = request_id or uuid.uuid4().hex
         loop = asyncio.get_running_loop()
         st = _Stream(loop, asyncio.Queue(), params, len(prompt_ids))
         with self._lock:
             self._streams[rid] = st
-        self._in.put(("add", rid, list(prompt_ids), params, prompt, lora_request))
+        self._in.put(("add", rid, list(prompt_ids), params, prompt, lora_request, priority))
         self._wake.set()
         try:
             while True:
@@ -95,8 +95,9 @@ class AsyncLLM:
                 return
             try:
                 if op[0] == "add":
-                    _, rid, ids, params, prompt, lora = op
-                    self.engine.add_request(rid, ids, params, prompt=prompt, lora_request=lora)
+                    _, rid, ids, params, prompt, lora, prio = op
+                    self.engine.add_request(rid, ids, params, prompt=prompt, lora_request=lora,
+                                            priority=prio)
                     self.stats["prompt_tokens"] += len(ids)
                 else:
                     self._finish(op[1], None, "abort", abort_engine=True)

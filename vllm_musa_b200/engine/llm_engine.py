@@ -156,6 +156,7 @@ class LLMEngine:
                              and not hasattr(self.model, "allocate_state")
                              and not config.lora.enable_lora)
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
+        sc.priority_policy = config.scheduler.scheduling_policy == "priority"
         self._sched_cfg = sc
         self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
         self.sleep_level = 0
@@ -188,7 +189,7 @@ class LLMEngine:
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_token_ids: List[int],
                     params: Optional[SamplingParams] = None, arrival_time: Optional[float] = None,
-                    prompt: Optional[str] = None, lora_request=None) -> None:
+                    prompt: Optional[str] = None, lora_request=None, priority: int = 0) -> None:
         params = params or SamplingParams()
         from ..sample.sampling_params import PoolingParams
         if isinstance(params, PoolingParams):
@@ -197,11 +198,11 @@ class LLMEngine:
             if self.sync is not None:
                 self.sync.record(("add", request_id, list(prompt_token_ids), params,
                                   time.time() if arrival_time is None else arrival_time,
-                                  prompt, lora_request))
+                                  prompt, lora_request, priority))
             self._add_one(request_id, prompt_token_ids,
                           SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True),
                           time.time() if arrival_time is None else arrival_time, prompt,
-                          lora=lora_request, pooling=params)
+                          lora=lora_request, pooling=params, priority=priority)
             return
         arrival = time.time() if arrival_time is None else arrival_time
         if lora_request is not None and getattr(self.model, "lora", None) is None:
@@ -210,7 +211,7 @@ class LLMEngine:
             if self.role == "follower":
                 raise RuntimeError("requests are added on the driver rank only")
             self.sync.record(("add", request_id, list(prompt_token_ids), params, arrival, prompt,
-                              lora_request))
+                              lora_request, priority))
         if params.n > 1:
             self._parents[request_id] = {"n": params.n, "done": {}, "prompt_ids": prompt_token_ids,
                                          "prompt": prompt, "arrival": arrival}
@@ -219,12 +220,13 @@ class LLMEngine:
                 if params.seed is not None:
                     child.seed = params.seed + k
                 self._add_one(f"{request_id}#{k}", prompt_token_ids, child, arrival, prompt,
-                              parent=request_id, index=k, lora=lora_request)
+                              parent=request_id, index=k, lora=lora_request, priority=priority)
             return
-        self._add_one(request_id, prompt_token_ids, params, arrival, prompt, lora=lora_request)
+        self._add_one(request_id, prompt_token_ids, params, arrival, prompt, lora=lora_request,
+                      priority=priority)
 
     def _add_one(self, name, prompt_ids, params, arrival, prompt, parent=None, index=0,
-                 lora=None, pooling=None):
+                 lora=None, pooling=None, priority=0):
         if name in self._by_name:
             raise ValueError(f"duplicate request id {name!r}")
         iid = next(self._ids)
@@ -241,6 +243,7 @@ class LLMEngine:
         sp.top_p = params.top_p
         sp.min_p = params.min_p
         sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
+        sp.priority = int(priority)
         so = params.structured_outputs
         if (params.stop or params.bad_words) and self.tokenizer is None:
             raise ValueError("stop strings and bad words need the model's tokenizer")
@@ -716,10 +719,12 @@ class LLMEngine:
             out.embedding = self._embedding(r)
         return out
 
-    def _follower_add(self, request_id, prompt_ids, params, arrival, prompt, lora_request=None):
+    def _follower_add(self, request_id, prompt_ids, params, arrival, prompt, lora_request=None,
+                      priority=0):
         sync, self.sync = self.sync, None  # apply locally without re-recording
         try:
-            self.add_request(request_id, prompt_ids, params, arrival, prompt, lora_request)
+            self.add_request(request_id, prompt_ids, params, arrival, prompt, lora_request,
+                             priority)
         finally:
             self.sync = sync
 

@@ -46,7 +46,7 @@ class LLM:
                  speculative_config: Optional[dict] = None,
                  enable_lora: bool = False, max_loras: int = 4, max_lora_rank: int = 64,
                  kv_cache_dtype: Optional[str] = None, logprobs_mode: str = "raw_logprobs",
-                 **unused):
+                 scheduling_policy: str = "fcfs", **unused):
         path = None
         if isinstance(model, ModelConfig):
             mcfg = model
@@ -74,7 +74,8 @@ class LLM:
             scheduler=SchedulerConfig(max_num_seqs=max_num_seqs,
                                       max_num_batched_tokens=max(max_num_batched_tokens, max_num_seqs),
                                       max_model_len=mlen,
-                                      enable_chunked_prefill=enable_chunked_prefill),
+                                      enable_chunked_prefill=enable_chunked_prefill,
+                                      scheduling_policy=scheduling_policy),
             parallel=ParallelConfig(tensor_parallel_size=tensor_parallel_size,
                                     pipeline_parallel_size=pipeline_parallel_size,
                                     enable_expert_parallel=enable_expert_parallel,
@@ -130,9 +131,11 @@ class LLM:
 
     def generate(self, prompts: Union[PromptType, Sequence[PromptType]],
                  sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
-                 use_tqdm: bool = False, lora_request=None) -> List[RequestOutput]:
+                 use_tqdm: bool = False, lora_request=None,
+                 priority: Optional[List[int]] = None) -> List[RequestOutput]:
         """``lora_request``: one LoRARequest for every prompt, or a list with one (or None)
-        per prompt."""
+        per prompt.  ``priority``: one int per prompt (lower first) under
+        ``scheduling_policy="priority"``."""
         if isinstance(prompts, (str, dict)) or (isinstance(prompts, list) and prompts and
                                                 isinstance(prompts[0], int)):
             prompts = [prompts]
@@ -146,12 +149,15 @@ class LLM:
             if any(x is not None for x in loras):
                 raise ValueError("LoRA with data parallelism is not served")
             return self._generate_dp(prompts, sampling_params)
+        prios = list(priority) if priority is not None else [0] * len(prompts)
+        if len(prios) != len(prompts):
+            raise ValueError("priority needs one value per prompt")
         order = []
-        for p, sp, lr in zip(prompts, sampling_params, loras):
+        for p, sp, lr, pr in zip(prompts, sampling_params, loras, prios):
             ids, text = self._prompt_ids(p)
             rid = str(self._counter)
             self._counter += 1
-            self.engine.add_request(rid, ids, sp, prompt=text, lora_request=lr)
+            self.engine.add_request(rid, ids, sp, prompt=text, lora_request=lr, priority=pr)
             order.append(rid)
         done = {}
         while self.engine.has_unfinished_requests():

@@ -115,9 +115,9 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
             lines.append(f"b200_{name}_sum {sum(vals):.6f}")
         return PlainTextResponse("\n".join(lines) + "\n")
 
-    async def run_one(ids, params, rid, lora=None):
+    async def run_one(ids, params, rid, lora=None, priority=0):
         final = None
-        async for o in llm.generate(ids, params, rid, lora_request=lora):
+        async for o in llm.generate(ids, params, rid, lora_request=lora, priority=priority):
             final = o
         return final
 
@@ -178,7 +178,8 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
             async def gen():
                 qs = []
                 for idx, ids, text, p in jobs:
-                    qs.append((idx, llm.generate(ids, p, f"{rid}-{idx}", lora_request=lora)))
+                    qs.append((idx, llm.generate(ids, p, f"{rid}-{idx}", lora_request=lora,
+                                                 priority=req.priority)))
                 for idx, it in qs:
                     sent = ""
                     async for o in it:
@@ -194,7 +195,7 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
         try:
-            outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}", lora)
+            outs = await asyncio.gather(*[run_one(ids, p, f"{rid}-{idx}", lora, req.priority)
                                           for idx, ids, _, p in jobs])
         except ValueError as e:  # rejected by the engine (e.g. a token id off the vocabulary)
             return err(str(e))
@@ -287,6 +288,7 @@ def make_arg_parser(p: Optional[argparse.ArgumentParser] = None) -> argparse.Arg
     p.add_argument("--num-gpu-blocks", type=int, default=None)
     p.add_argument("--kv-cache-dtype", default=None,
                    help="auto | fp8 | turboquant_k8v4 | turboquant_4bit_nc | ...")
+    p.add_argument("--scheduling-policy", default="fcfs", choices=["fcfs", "priority"])
     p.add_argument("--logprobs-mode", default="raw_logprobs",
                    choices=["raw_logprobs", "raw_logits", "processed_logprobs",
                             "processed_logits"])
@@ -310,7 +312,8 @@ def build_llm(args):
                enable_prefix_caching=not args.no_enable_prefix_caching, seed=args.seed,
                device=args.device, num_gpu_blocks=args.num_gpu_blocks,
                kv_cache_dtype=getattr(args, "kv_cache_dtype", None),
-               logprobs_mode=getattr(args, "logprobs_mode", "raw_logprobs"))
+               logprobs_mode=getattr(args, "logprobs_mode", "raw_logprobs"),
+               scheduling_policy=getattr(args, "scheduling_policy", "fcfs"))
 
 
 def parse_lora_modules(specs) -> dict:

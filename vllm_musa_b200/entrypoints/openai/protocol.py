@@ -35,6 +35,7 @@ class _Sampling(BaseModel):
     bad_words: Optional[List[str]] = None
     # vLLM extensions: prompt log-probabilities, detokenization options
     prompt_logprobs: Optional[int] = None
+    priority: int = 0  # under --scheduling-policy priority: lower values are served first
     skip_special_tokens: bool = True
     spaces_between_special_tokens: bool = True
     # structured outputs: vLLM's extra parameters and the OpenAI response_format
