@@ -140,6 +140,13 @@ class LLMEngine:
                 num_blocks = int(t)
                 self.runner.allocate_kv(num_blocks)
         self.num_blocks = num_blocks
+        cap = num_blocks * config.cache.block_size * dcp
+        if cap < config.scheduler.max_model_len:
+            # a request of max_model_len tokens could never hold its blocks: it would be
+            # preempted and re-admitted forever
+            raise ValueError(f"the KV cache holds {cap} tokens ({num_blocks} blocks), fewer than "
+                             f"max_model_len={config.scheduler.max_model_len}: lower "
+                             f"max_model_len or give the cache more memory / blocks")
         from .. import _C_runtime
         sc = _C_runtime.SchedulerConfig()
         # with decode context parallelism a scheduler block spans dcp ranks' cache blocks
