@@ -191,3 +191,13 @@ def test_prompt_logprobs_match_reference():
         plain = llm.generate([p], SamplingParams(temperature=0.0, max_tokens=3))[0]
         assert plain.prompt_logprobs is None
         assert o.outputs[0].token_ids == plain.outputs[0].token_ids
+
+
+def test_truncate_prompt_tokens():
+    p = _prompts(1, 40, seed=14)[0]
+    sp = SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True, truncate_prompt_tokens=12)
+    got = _llm().generate([p], sp)[0]
+    want = _llm().generate([p[-12:]], SamplingParams(temperature=0.0, max_tokens=4,
+                                                      ignore_eos=True))[0]
+    assert got.prompt_token_ids == p[-12:]
+    assert got.outputs[0].token_ids == want.outputs[0].token_ids

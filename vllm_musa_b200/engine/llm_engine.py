@@ -198,6 +198,10 @@ class LLMEngine:
                     params: Optional[SamplingParams] = None, arrival_time: Optional[float] = None,
                     prompt: Optional[str] = None, lora_request=None, priority: int = 0) -> None:
         params = params or SamplingParams()
+        k = getattr(params, "truncate_prompt_tokens", None)
+        if k is not None and len(prompt_token_ids) > k:
+            prompt_token_ids = list(prompt_token_ids)[-k:]
+            prompt = None  # the text no longer matches the ids
         from ..sample.sampling_params import PoolingParams
         if isinstance(params, PoolingParams):
             if self.sync is not None and self.role == "follower":

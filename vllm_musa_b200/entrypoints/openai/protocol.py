@@ -36,6 +36,7 @@ class _Sampling(BaseModel):
     # vLLM extensions: prompt log-probabilities, detokenization options
     prompt_logprobs: Optional[int] = None
     priority: int = 0  # under --scheduling-policy priority: lower values are served first
+    truncate_prompt_tokens: Optional[int] = None
     skip_special_tokens: bool = True
     spaces_between_special_tokens: bool = True
     # structured outputs: vLLM's extra parameters and the OpenAI response_format
@@ -83,6 +84,7 @@ class _Sampling(BaseModel):
                               allowed_token_ids=self.allowed_token_ids,
                               bad_words=self.bad_words,
                               prompt_logprobs=self.prompt_logprobs,
+                              truncate_prompt_tokens=self.truncate_prompt_tokens,
                               skip_special_tokens=self.skip_special_tokens,
                               spaces_between_special_tokens=self.spaces_between_special_tokens)
 

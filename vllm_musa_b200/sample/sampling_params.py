@@ -74,6 +74,8 @@ class SamplingParams:
     # position plus the prompt token's own; the first position has none); the request's
     # prompt is computed in full (no prefix-cache reuse)
     prompt_logprobs: Optional[int] = None
+    # keep only the last k prompt tokens (vLLM's truncate_prompt_tokens; None: the whole prompt)
+    truncate_prompt_tokens: Optional[int] = None
     # detokenization of the returned text
     skip_special_tokens: bool = True
     spaces_between_special_tokens: bool = True
@@ -101,6 +103,8 @@ class SamplingParams:
             raise ValueError("logprobs must be in [0, 20]")
         if self.prompt_logprobs is not None and not 0 <= self.prompt_logprobs <= 20:
             raise ValueError("prompt_logprobs must be in [0, 20]")
+        if self.truncate_prompt_tokens is not None and self.truncate_prompt_tokens < 1:
+            raise ValueError("truncate_prompt_tokens must be >= 1")
         if isinstance(self.stop, str):
             self.stop = [self.stop]
         self.stop = [x for x in self.stop if x]
