@@ -62,9 +62,12 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
         return out
 
     def check_len(ids, params: SamplingParams):
-        if len(ids) + 1 > max_model_len:
-            raise ValueError(f"prompt has {len(ids)} tokens; max_model_len is {max_model_len}")
-        params.max_tokens = min(params.max_tokens, max_model_len - len(ids))
+        n = len(ids)
+        if params.truncate_prompt_tokens is not None:
+            n = min(n, params.truncate_prompt_tokens)  # the engine keeps the last tokens
+        if n + 1 > max_model_len:
+            raise ValueError(f"prompt has {n} tokens; max_model_len is {max_model_len}")
+        params.max_tokens = min(params.max_tokens, max_model_len - n)
 
     @app.get("/health")
     async def health():
