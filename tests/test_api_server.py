@@ -39,7 +39,11 @@ def test_models_health_metrics(client):
     c, _ = client
     assert c.get("/health").status_code == 200
     assert c.get("/v1/models").json()["data"][0]["id"] == "tiny"
-    assert "b200_request_success_total" in c.get("/metrics").text
+    m = c.get("/metrics").text
+    for name in ("b200_request_success_total", "b200_kv_cache_usage_perc",
+                 "b200_prefix_cache_hits_total", "b200_spec_decode_num_accepted_tokens_total",
+                 "b200_engine_steps_total"):
+        assert name in m
 
 
 def test_completion_token_ids_matches_offline(client):

@@ -111,6 +111,23 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
             "# TYPE b200_kv_cache_free_blocks gauge",
             f"b200_kv_cache_free_blocks {eng.scheduler.num_free_blocks()}",
         ]
+        total = max(1, getattr(eng, "num_blocks", 0))
+        sch = eng.scheduler
+        q, h = sch.prefix_cache_queries(), sch.prefix_cache_hits()
+        lines += [
+            "# TYPE b200_kv_cache_usage_perc gauge",
+            f"b200_kv_cache_usage_perc {1.0 - sch.num_free_blocks() / total:.6f}",
+            "# TYPE b200_prefix_cache_queries_total counter",
+            f"b200_prefix_cache_queries_total {q}",
+            "# TYPE b200_prefix_cache_hits_total counter",
+            f"b200_prefix_cache_hits_total {h}",
+            "# TYPE b200_spec_decode_num_draft_tokens_total counter",
+            f"b200_spec_decode_num_draft_tokens_total {sch.spec_proposed()}",
+            "# TYPE b200_spec_decode_num_accepted_tokens_total counter",
+            f"b200_spec_decode_num_accepted_tokens_total {sch.spec_accepted()}",
+            "# TYPE b200_engine_steps_total counter",
+            f"b200_engine_steps_total {eng.num_steps}",
+        ]
         for name, vals in (("time_to_first_token_seconds", s["ttft"]),
                            ("time_per_output_token_seconds", s["tpot"])):
             lines.append(f"# TYPE b200_{name} summary")
