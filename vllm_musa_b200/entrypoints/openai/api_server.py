@@ -1,5 +1,6 @@
 """OpenAI-compatible HTTP server (``/v1/completions``, ``/v1/chat/completions``,
-``/v1/models``, ``/health``, ``/metrics``), the role ``vllm serve`` plays for the reference
+``/v1/embeddings``, ``/v1/models``, ``/tokenize``, ``/detokenize``, ``/health``, ``/metrics``),
+the role ``vllm serve`` plays for the reference
 (usage: docs/usage.md of the reference).
 
     python -m vllm_musa_b200.entrypoints.openai.api_server --model /path/or/preset --port 8000
