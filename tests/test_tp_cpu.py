@@ -121,6 +121,13 @@ outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=8, ignor
 print("TOKENS", [o.outputs[0].token_ids for o in outs])
 outs2 = llm.generate(prompts[:1], SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True))
 print("TOKENS2", [o.outputs[0].token_ids for o in outs2])
+# a request the driver rejects never reaches the follower (ids stay in lock-step)
+try:
+    llm.generate(prompts[:1], SamplingParams(max_tokens=2, logit_bias={5000: 1.0}))
+except ValueError:
+    print("REJECTED")
+outs3 = llm.generate(prompts[:1], SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True))
+print("TOKENS3", [o.outputs[0].token_ids for o in outs3])
 llm.shutdown()
 '''
     env = dict(os.environ)
@@ -134,6 +141,9 @@ llm.shutdown()
     assert toks == one
     line2 = [l for l in r.stdout.splitlines() if l.startswith("TOKENS2 ")][0]
     assert eval(line2[len("TOKENS2 "):])[0] == one[0][:4]
+    assert "REJECTED" in r.stdout
+    line3 = [l for l in r.stdout.splitlines() if l.startswith("TOKENS3 ")][0]
+    assert eval(line3[len("TOKENS3 "):])[0] == one[0][:4]
 
 
 @pytest.mark.parametrize("dcp", [1, 2])

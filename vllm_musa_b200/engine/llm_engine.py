@@ -202,27 +202,25 @@ class LLMEngine:
         if k is not None and len(prompt_token_ids) > k:
             prompt_token_ids = list(prompt_token_ids)[-k:]
             prompt = None  # the text no longer matches the ids
-        from ..sample.sampling_params import PoolingParams
-        if isinstance(params, PoolingParams):
-            if self.sync is not None and self.role == "follower":
-                raise RuntimeError("requests are added on the driver rank only")
-            if self.sync is not None:
-                self.sync.record(("add", request_id, list(prompt_token_ids), params,
-                                  time.time() if arrival_time is None else arrival_time,
-                                  prompt, lora_request, priority))
-            self._add_one(request_id, prompt_token_ids,
-                          SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True),
-                          time.time() if arrival_time is None else arrival_time, prompt,
-                          lora=lora_request, pooling=params, priority=priority)
-            return
         arrival = time.time() if arrival_time is None else arrival_time
+        if self.sync is not None and self.role == "follower":
+            raise RuntimeError("requests are added on the driver rank only")
         if lora_request is not None and getattr(self.model, "lora", None) is None:
             raise ValueError("lora_request needs LLM(..., enable_lora=True)")
-        if self.sync is not None:
-            if self.role == "follower":
-                raise RuntimeError("requests are added on the driver rank only")
+        self._add_local(request_id, prompt_token_ids, params, arrival, prompt, lora_request,
+                        priority)
+        if self.sync is not None:  # followers replay only requests the driver accepted
             self.sync.record(("add", request_id, list(prompt_token_ids), params, arrival, prompt,
                               lora_request, priority))
+
+    def _add_local(self, request_id, prompt_token_ids, params, arrival, prompt, lora_request,
+                   priority) -> None:
+        from ..sample.sampling_params import PoolingParams
+        if isinstance(params, PoolingParams):
+            self._add_one(request_id, prompt_token_ids,
+                          SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True),
+                          arrival, prompt, lora=lora_request, pooling=params, priority=priority)
+            return
         if params.n > 1:
             self._parents[request_id] = {"n": params.n, "done": {}, "prompt_ids": prompt_token_ids,
                                          "prompt": prompt, "arrival": arrival}
@@ -240,6 +238,23 @@ class LLMEngine:
                  lora=None, pooling=None, priority=0):
         if name in self._by_name:
             raise ValueError(f"duplicate request id {name!r}")
+        # every check that can reject the request comes before its internal id is taken: the
+        # ranks of a tensor-parallel group draw ids in lock-step and only see accepted requests
+        so = params.structured_outputs
+        if (params.stop or params.bad_words) and self.tokenizer is None:
+            raise ValueError("stop strings and bad words need the model's tokenizer")
+        V = self.config.model.vocab_size
+        for t in list(params.logit_bias or {}) + list(params.allowed_token_ids or []):
+            if not 0 <= t < V:
+                raise ValueError(f"token id {t} is outside the vocabulary (size {V})")
+        if not prompt_ids:
+            raise ValueError("empty prompt")
+        if len(prompt_ids) >= self.config.scheduler.max_model_len:
+            raise ValueError(f"prompt has {len(prompt_ids)} tokens; max_model_len is "
+                             f"{self.config.scheduler.max_model_len}")
+        matcher = self._grammar_backend().matcher(so) if so is not None else None
+        bad_words_ids = self._bad_words_ids(params.bad_words) if params.bad_words else None
+        lora_slot = self.model.lora.acquire(lora) if lora is not None else -1
         iid = next(self._ids)
         from .. import _C_runtime
         sp = _C_runtime.SamplingCfg()
@@ -255,13 +270,6 @@ class LLMEngine:
         sp.min_p = params.min_p
         sp.seed = _mix_seed(self.config.seed, iid) if params.seed is None else int(params.seed)
         sp.priority = int(priority)
-        so = params.structured_outputs
-        if (params.stop or params.bad_words) and self.tokenizer is None:
-            raise ValueError("stop strings and bad words need the model's tokenizer")
-        V = self.config.model.vocab_size
-        for t in list(params.logit_bias or {}) + list(params.allowed_token_ids or []):
-            if not 0 <= t < V:
-                raise ValueError(f"token id {t} is outside the vocabulary (size {V})")
         special = params.has_penalties or params.logprobs is not None or so is not None or \
             bool(params.stop) or lora is not None or params.has_logits_processors or \
             params.prompt_logprobs is not None or pooling is not None
@@ -271,8 +279,6 @@ class LLMEngine:
         # with speculative decoding configured, these requests simply decode without drafts
         # (their penalties, log-probabilities, grammars, stop strings and adapters apply per
         # drawn token); the other requests of the batch keep theirs
-        lora_slot = self.model.lora.acquire(lora) if lora is not None else -1
-        matcher = self._grammar_backend().matcher(so) if so is not None else None
         self.scheduler.add_request(iid, list(map(int, prompt_ids)), sp)
         r = _Req(name, iid, list(prompt_ids), params, arrival, prompt, parent, index)
         if params.logprobs is not None:
@@ -282,8 +288,7 @@ class LLMEngine:
         r.pooling = pooling
         r.matcher = matcher
         r.lora, r.lora_slot = lora, lora_slot
-        if params.bad_words:
-            r.bad_words_ids = self._bad_words_ids(params.bad_words)
+        r.bad_words_ids = bad_words_ids
         self._reqs[iid] = r
         self._by_name[name] = iid
         if special:
