@@ -115,3 +115,25 @@ def test_completion_logits_processors_and_prompt_logprobs(client):
     bad = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 2,
                                           "logit_bias": {"5000": 1}})
     assert bad.status_code == 400
+
+
+def test_engine_failure_reports_dead():
+    """A step that raises stops the engine loop: open and later requests fail (HTTP 500 / 503
+    style errors instead of hanging) and /health answers 503."""
+    from fastapi.testclient import TestClient
+    llm = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=64,
+              max_model_len=256, max_num_seqs=4, max_num_batched_tokens=256)
+    alm = AsyncLLM(llm.engine)
+
+    def boom():
+        raise RuntimeError("injected step failure")
+
+    llm.engine.step = boom
+    app = build_app(alm, "tiny", 256)
+    with TestClient(app, raise_server_exceptions=False) as c:
+        r = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 2})
+        assert r.status_code >= 500
+        assert c.get("/health").status_code == 503
+        r2 = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 2})
+        assert r2.status_code >= 500
+    alm._stop = True

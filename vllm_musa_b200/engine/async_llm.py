@@ -37,6 +37,10 @@ class _Stream:
     token_ids: List[int] = field(default_factory=list)
 
 
+class EngineDeadError(RuntimeError):
+    """The engine loop stopped after a step raised (vLLM's EngineDeadError)."""
+
+
 class AsyncLLM:
     def __init__(self, engine: LLMEngine):
         self.engine = engine
@@ -47,6 +51,7 @@ class AsyncLLM:
         self._lock = threading.Lock()
         self._wake = threading.Event()
         self._stop = False
+        self.dead: Optional[BaseException] = None  # the error that stopped the engine loop
         self.idle_sync_s = float(os.environ.get("B200_IDLE_SYNC_S", "1.0"))
         self.stats = {"finished": 0, "ttft": [], "tpot": [], "prompt_tokens": 0,
                       "generation_tokens": 0}
@@ -57,6 +62,8 @@ class AsyncLLM:
     async def generate(self, prompt_ids: List[int], params: SamplingParams,
                        request_id: Optional[str] = None, prompt: Optional[str] = None,
                        lora_request=None, priority: int = 0) -> AsyncIterator[RequestOutput]:
+        if self.dead is not None:
+            raise EngineDeadError(f"the engine stopped after an error: {self.dead!r}")
         rid = request_id or uuid.uuid4().hex
         loop = asyncio.get_running_loop()
         st = _Stream(loop, asyncio.Queue(), params, len(prompt_ids))
@@ -179,6 +186,7 @@ class AsyncLLM:
                     outs = self.engine.step()
                 except Exception as e:  # engine failure: fail every open request
                     log.exception("engine step failed")
+                    self.dead = e  # later requests fail at once; /health reports 503
                     with self._lock:
                         rids = list(self._streams)
                     for rid in rids:

@@ -72,6 +72,8 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
 
     @app.get("/health")
     async def health():
+        if getattr(llm, "dead", None) is not None:
+            return PlainTextResponse(f"engine dead: {llm.dead!r}", status_code=503)
         return PlainTextResponse("ok")
 
     @app.get("/version")
