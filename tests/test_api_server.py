@@ -137,3 +137,34 @@ def test_engine_failure_reports_dead():
         r2 = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 2})
         assert r2.status_code >= 500
     alm._stop = True
+
+
+def test_streaming_with_speculation_and_usage():
+    """Streaming under n-gram speculation: a step can add several tokens and every one of
+    them reaches a chunk; stream_options.include_usage adds the final usage chunk."""
+    from fastapi.testclient import TestClient
+    llm = LLM(tiny_llama(), device="cpu", block_size=16, seed=0, num_gpu_blocks=128,
+              max_model_len=256, max_num_seqs=8, max_num_batched_tokens=256,
+              tokenizer=ToyTokenizer(),
+              speculative_config={"method": "ngram", "num_speculative_tokens": 4})
+    alm = AsyncLLM(llm.engine)
+    app = build_app(alm, "tiny", 256)
+    g = torch.Generator().manual_seed(5)
+    base = torch.randint(0, 1024, (12,), generator=g).tolist()
+    prompt = (base * 4)[:40]
+    try:
+        with TestClient(app) as c:
+            full = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 16,
+                                                   "temperature": 0, "ignore_eos": True}).json()
+            with c.stream("POST", "/v1/completions",
+                          json={"prompt": prompt, "max_tokens": 16, "temperature": 0,
+                                "ignore_eos": True, "stream": True,
+                                "stream_options": {"include_usage": True}}) as r:
+                events = [json.loads(l[6:]) for l in r.iter_lines()
+                          if l.startswith("data: ") and l != "data: [DONE]"]
+        ids = [t for e in events if e["choices"] for t in e["choices"][0]["token_ids"]]
+        assert ids == full["choices"][0]["token_ids"]
+        assert events[-1]["choices"] == [] and events[-1]["usage"]["completion_tokens"] == 16
+        assert llm.engine.scheduler.spec_accepted() > 0
+    finally:
+        alm.shutdown()

@@ -203,18 +203,27 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
                 for idx, ids, text, p in jobs:
                     qs.append((idx, llm.generate(ids, p, f"{rid}-{idx}", lora_request=lora,
                                                  priority=req.priority)))
-                for idx, it in qs:
-                    sent = ""
+                n_prompt = n_gen = 0
+                for (idx, ids, _, _), (_, it) in zip(jobs, qs):
+                    sent, n_ids = "", 0
                     async for o in it:
                         c = o.outputs[0]
                         delta = c.text[len(sent):]
                         sent = c.text
+                        # every token since the last chunk (a speculative step adds several)
+                        new_ids = list(c.token_ids[n_ids:])
+                        n_ids = len(c.token_ids)
                         chunk = {"id": rid, "object": "text_completion", "created": int(time.time()),
                                  "model": model_name,
-                                 "choices": [{"index": idx, "text": delta,
-                                              "token_ids": c.token_ids[-1:] if c.token_ids else [],
+                                 "choices": [{"index": idx, "text": delta, "token_ids": new_ids,
                                               "finish_reason": c.finish_reason if o.finished else None}]}
                         yield f"data: {json.dumps(chunk)}\n\n"
+                    n_prompt += len(ids)
+                    n_gen += n_ids
+                if (req.stream_options or {}).get("include_usage"):
+                    usage = {"prompt_tokens": n_prompt, "completion_tokens": n_gen,
+                             "total_tokens": n_prompt + n_gen}
+                    yield f"data: {json.dumps({'id': rid, 'object': 'text_completion', 'created': int(time.time()), 'model': model_name, 'choices': [], 'usage': usage})}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
         try:
@@ -251,16 +260,22 @@ def build_app(llm, model_name: str, max_model_len: int, lora_modules: Optional[d
         if req.stream:
             async def gen():
                 sent = ""
+                n_gen = 0
                 async for o in llm.generate(ids, SamplingParams(**{**p.__dict__, "n": 1}), rid,
-                                            lora_request=lora):
+                                            lora_request=lora, priority=req.priority):
                     c = o.outputs[0]
                     delta = c.text[len(sent):]
                     sent = c.text
+                    n_gen = len(c.token_ids)
                     chunk = {"id": rid, "object": "chat.completion.chunk", "created": int(time.time()),
                              "model": model_name,
                              "choices": [{"index": 0, "delta": {"role": "assistant", "content": delta},
                                           "finish_reason": c.finish_reason if o.finished else None}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
+                if (req.stream_options or {}).get("include_usage"):
+                    usage = {"prompt_tokens": len(ids), "completion_tokens": n_gen,
+                             "total_tokens": len(ids) + n_gen}
+                    yield f"data: {json.dumps({'id': rid, 'object': 'chat.completion.chunk', 'created': int(time.time()), 'model': model_name, 'choices': [], 'usage': usage})}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
         try:

@@ -24,6 +24,8 @@ class _Sampling(BaseModel):
     ignore_eos: bool = False
     min_tokens: int = 0
     stream: bool = False
+    # OpenAI: {"include_usage": true} adds a final chunk with the token counts
+    stream_options: Optional[Dict] = None
     user: Optional[str] = None
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
