@@ -76,3 +76,27 @@ def test_embeddings_on_gpu_track_reference():
             cos = float(torch.nn.functional.cosine_similarity(got, want / want.norm(), dim=0))
             assert cos > 0.99, (kind, cos)
     llm.shutdown()
+
+
+def test_eagle3_head_on_gpu_keeps_tokens():
+    """EAGLE-3 over the bf16 tiny Llama with CUDA graphs: the model records three residual
+    streams per step into a static buffer (graph replays included) and the head drafts from
+    them; every emitted token is the fp32 reference argmax up to bf16 resolution."""
+    from vllm_musa_b200 import LLM, SamplingParams
+    cfg = _cfg()
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (20, 90)]
+    sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
+    llm = LLM(cfg, block_size=64, seed=0, num_gpu_blocks=32, max_model_len=512,
+              max_num_seqs=8, max_num_batched_tokens=512,
+              speculative_config={"method": "eagle3", "num_speculative_tokens": 1})
+    got = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    assert llm.engine.drafter.proposed > 0
+    llm.shutdown()
+    ref = _ref()
+    for p, toks in zip(prompts, got):
+        assert len(toks) == 12
+        for k, t in enumerate(toks):
+            want = ref.logits(p + toks[:k])[-1]
+            gap = float(want.max() - want[t]) / float(want.abs().max())
+            assert gap < 0.03, (k, gap)

@@ -115,6 +115,8 @@ class LLMEngine:
         self._load_weights()
         if config.speculative.method == "eagle":
             self._load_eagle()
+        elif config.speculative.method == "eagle3":
+            self._load_eagle3()
         if config.lora.enable_lora:
             from ..lora import LoRAManager
             if not hasattr(self.model, "lora") or not hasattr(self.model, "I_pad"):
@@ -177,6 +179,10 @@ class LLMEngine:
             from .spec_decode import EagleDrafter
             self.drafter = EagleDrafter(self, config.speculative.num_speculative_tokens or 1,
                                         config.speculative.tree_width)
+        elif config.speculative.method == "eagle3":
+            from .spec_decode import Eagle3Drafter
+            self.drafter = Eagle3Drafter(self, config.speculative.num_speculative_tokens or 1,
+                                         config.speculative.tree_width)
         self.runner.capture_graphs()
         self._ids = itertools.count()
         self._reqs: Dict[int, _Req] = {}
@@ -373,7 +379,7 @@ class LLMEngine:
             else:
                 self.scheduler.propose_ngram(spec.num_speculative_tokens,
                                              spec.prompt_lookup_min, spec.prompt_lookup_max)
-        elif spec.method in ("mtp", "eagle") and self.drafter is not None:
+        elif spec.method in ("mtp", "eagle", "eagle3") and self.drafter is not None:
             self.drafter.propose(self.scheduler)
         if self._special and spec.method is not None:
             # penalties, log-probabilities and grammars are applied per drawn token: requests
@@ -763,6 +769,24 @@ class LLMEngine:
             self.model.load_weights(dummy_weights(mcfg, cfg.seed, cfg.init_std, device=dev))
         else:
             self.model.load_weights(safetensors_weights(cfg.model_path))
+
+    def _load_eagle3(self) -> None:
+        """Attach an EAGLE-3 head (whole on this rank, its own KV cache) and make the model
+        record the residual streams the head reads."""
+        from ..models.eagle import Eagle3Head, eagle3_param_shapes
+        cfg, mcfg, device = self.config, self.config.model, self.device
+        if not hasattr(self.model, "enable_aux"):
+            raise ValueError("EAGLE-3 heads are served over the dense decoders (Llama / Qwen)")
+        head = Eagle3Head(self.model)
+        path = cfg.speculative.model
+        if path:
+            head.load_weights(safetensors_weights(path))
+        else:
+            dev = str(device) if device.type == "cuda" else "cpu"
+            head.load_weights(dummy_weights(mcfg, cfg.seed + 1, cfg.init_std, device=dev,
+                                            shapes=eagle3_param_shapes(mcfg)))
+        self.model.enable_aux(head.aux_layers, cfg.scheduler.max_num_batched_tokens)
+        self.model.draft_head = head
 
     def _load_eagle(self) -> None:
         """Attach an EAGLE head to the dense decoder (its KV is one extra cache layer)."""

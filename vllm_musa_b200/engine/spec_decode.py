@@ -27,7 +27,8 @@ class ModelDrafter:
     """One-token drafts from a draft layer: ``forward(ids, prev_hidden, meta, kv_caches)`` ->
     hidden rows, ``logits(hidden)`` -> this rank's vocab shard of the draft logits."""
 
-    def __init__(self, engine, forward, logits, num_tokens: int = 1, tree_width: int = 1):
+    def __init__(self, engine, forward, logits, num_tokens: int = 1, tree_width: int = 1,
+                 features=None, pick=None):
         if num_tokens != 1:
             raise ValueError("model-based drafters propose one token per step")
         self.engine = engine
@@ -37,6 +38,10 @@ class ModelDrafter:
         self.logits = logits
         self.tree_width = tree_width  # > 1: the top tree_width tokens, verified as siblings
         self.proposed = 0
+        # per-step-row features the head reads (default: the target's final hidden states)
+        self.features = features or (lambda: self.runner.last_hidden)
+        # logits -> [S, k] target token ids (default: the target's vocab-parallel sampler)
+        self.pick = pick
 
     def propose(self, scheduler) -> None:
         """Drafts were set right after the previous step; nothing to do before scheduling."""
@@ -46,7 +51,7 @@ class ModelDrafter:
         sch = self.engine.scheduler
         b = self.runner.buf
         h = b.h
-        hidden = self.runner.last_hidden
+        hidden = self.features()
         if hidden is None or plan.num_reqs == 0:
             return
         cu = h["cu_q"][:plan.num_reqs + 1].tolist()
@@ -97,6 +102,17 @@ class ModelDrafter:
         x = self.forward(ids, prev, meta, self.runner.kv_caches)
         last_rows = torch.tensor([c - 1 for c in cus[1:]], dtype=torch.long, device=dev)
         logits = self.logits(x[last_rows])
+        if self.pick is not None:  # the head's own vocabulary, whole on this rank
+            top = self.pick(logits, self.tree_width).cpu().tolist()
+            for k, (rid, ready) in enumerate(who):
+                if not ready:
+                    continue
+                if self.tree_width > 1:
+                    sch.set_draft_tree(rid, [int(t) for t in top[k]], [-1] * self.tree_width)
+                else:
+                    sch.set_draft(rid, [int(top[k][0])])
+                self.proposed += self.tree_width
+            return
         if self.tree_width > 1:
             smp = self.runner.sampler
             if smp.tp > 1:  # vocab-sharded rows: the full distribution
@@ -134,3 +150,16 @@ class EagleDrafter(ModelDrafter):
             raise ValueError("speculative method 'eagle' needs an EAGLE head on the model")
         super().__init__(engine, head.forward_draft, head.compute_logits, num_tokens,
                          tree_width)
+
+
+class Eagle3Drafter(ModelDrafter):
+    """EAGLE-3: the head reads three of the target's residual streams per position (recorded
+    by the model into ``aux_buf`` during its forward, graph replays included) and drafts from
+    its own vocabulary, mapped to target ids."""
+
+    def __init__(self, engine, num_tokens: int = 1, tree_width: int = 1):
+        head = getattr(engine.model, "draft_head", None)
+        if head is None or getattr(engine.model, "aux_buf", None) is None:
+            raise ValueError("speculative method 'eagle3' needs an EAGLE-3 head on the model")
+        super().__init__(engine, head.forward_draft, head.compute_logits, num_tokens,
+                         tree_width, features=lambda: engine.model.aux_buf, pick=head.pick)

@@ -109,6 +109,8 @@ class DenseDecoderForCausalLM:
         self.lm_head = None
         self.tq = None
         self.draft_head = None  # EAGLE head (speculative decoding): one extra cache layer
+        self.aux_buf = None     # EAGLE-3: residual streams entering the aux layers, [T, k*H]
+        self._aux_pos = {}      # layer index -> column block of aux_buf
         self.lora = None        # LoRAManager when adapters are enabled
         if cfg.kv_cache_dtype not in ("auto", None, "bf16", "bfloat16"):
             from ..attention import TurboQuantAttention
@@ -238,6 +240,9 @@ class DenseDecoderForCausalLM:
         n = self.l1
         for i in range(self.l0, self.l1):
             L = self.layers[i]
+            for k in self._aux_pos.get(i, ()):  # EAGLE-3: the stream entering layer i
+                H = cfg.hidden_size
+                self.aux_buf[:T, k * H:(k + 1) * H].copy_(residual[:T])
             kc, vc = kv_caches[i - self.l0]
             qkv = ops.linear(x, L.qkv_w)
             lora = getattr(meta, "lora", None)
@@ -268,6 +273,16 @@ class DenseDecoderForCausalLM:
             else:
                 x, residual = self._mlp_allreduce(i, L, x, T, residual, nxt, eps)
         return x if self.last_stage else residual
+
+    def enable_aux(self, layers, max_tokens: int) -> None:
+        """Record the residual stream entering each of ``layers`` into ``aux_buf`` (one H-wide
+        column block per layer, rows = step tokens) on every forward."""
+        H = self.cfg.hidden_size
+        self._aux_pos = {}
+        for k, l in enumerate(layers):
+            self._aux_pos.setdefault(int(l), []).append(k)
+        self.aux_buf = torch.zeros(max_tokens, len(layers) * H, dtype=self.dtype,
+                                   device=self.device)
 
     # ------------------------------------------------------------------ LoRA
     def _lora_qkv(self, i, x, qkv, batch) -> None:

@@ -6,7 +6,7 @@ SwiGLU MLP -> residual] x L -> RMSNorm -> LM head.  Computation in fp32.
 """
 from __future__ import annotations
 
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import torch
 import torch.nn.functional as F
@@ -44,8 +44,9 @@ class ReferenceDecoder:
         return self.hidden(tokens) @ head.t()
 
     @torch.no_grad()
-    def hidden(self, tokens: List[int]) -> torch.Tensor:
-        """Final normalised hidden states [S, H] for every position of ``tokens``."""
+    def hidden(self, tokens: List[int], streams: Optional[dict] = None) -> torch.Tensor:
+        """Final normalised hidden states [S, H] for every position of ``tokens``; ``streams``
+        (a dict) receives the residual stream entering each layer, by layer index."""
         cfg, w, D = self.cfg, self.w, self.D
         S = len(tokens)
         ids = torch.tensor(tokens)
@@ -54,6 +55,8 @@ class ReferenceDecoder:
         G = cfg.num_heads // cfg.num_kv_heads
         mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
         for i in range(cfg.num_layers):
+            if streams is not None:
+                streams[i] = h.clone()
             p = f"model.layers.{i}."
             x = self._rms(h, w[p + "input_layernorm.weight"])
             q = (x @ w[p + "self_attn.q_proj.weight"].t()).view(S, cfg.num_heads, D)

@@ -46,6 +46,7 @@ class Feature(str, Enum):
     SPARSE_INDEXER = "deepseek.sparse_indexer"
     MTP = "spec.mtp"
     EAGLE = "spec.eagle"
+    EAGLE3 = "spec.eagle3"
     SPEC_TREE = "spec.token_tree"
     PIPELINE_MICROBATCH = "pp.microbatched_stages"
     GDN_CHUNKED_PREFILL = "gdn.chunked_prefill"
@@ -186,6 +187,8 @@ def resolve(config) -> OptimizationContract:
             both(Feature.MTP)
     if m.family == ModelFamily.DENSE and e.speculative_method == "eagle":
         both(Feature.EAGLE)
+    if m.family == ModelFamily.DENSE and e.speculative_method == "eagle3":
+        both(Feature.EAGLE3)
     if e.speculative_tree:
         both(Feature.SPEC_TREE)
     if m.quant == "w4afp8" and m.num_experts:
@@ -226,6 +229,13 @@ def validate(contract: OptimizationContract) -> None:
                              "(no MLA, recurrent or MoE families)")
     if e.speculative_method == "mtp" and m.family != ModelFamily.DEEPSEEK:
         raise ValueError("MTP speculative decoding needs a DeepSeek multi-token-prediction layer")
+    if e.speculative_method == "eagle3":
+        if m.family != ModelFamily.DENSE or m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
+            raise ValueError("EAGLE-3 heads are served over the dense decoders with a bf16 KV "
+                             "cache")
+        if e.tensor_parallel_size > 1 or e.pipeline_parallel_size > 1:
+            raise ValueError("EAGLE-3 is served at tensor / pipeline parallel size 1 (its "
+                             "features are the target's full residual streams)")
     if e.speculative_method == "eagle":
         if m.family != ModelFamily.DENSE:
             raise ValueError("EAGLE heads are served over the dense decoders (Llama / Qwen)")
@@ -234,16 +244,17 @@ def validate(contract: OptimizationContract) -> None:
     if e.pipeline_parallel_size > 1:
         if m.family not in (ModelFamily.DENSE, ModelFamily.MOE):
             raise ValueError("pipeline parallelism is served for the dense and MoE decoders")
-        if e.speculative_method in ("mtp", "eagle") or e.decode_context_parallel_size > 1:
+        if e.speculative_method in ("mtp", "eagle", "eagle3") or \
+                e.decode_context_parallel_size > 1:
             raise ValueError("pipeline parallelism does not combine with model-based drafters "
                              "or decode context parallelism")
         if m.num_layers < e.pipeline_parallel_size:
             raise ValueError("pipeline_parallel_size exceeds the number of layers")
     if e.speculative_tree:
-        if e.speculative_method not in ("ngram", "eagle"):
-            raise ValueError("token trees are proposed by the ngram and eagle drafters")
+        if e.speculative_method not in ("ngram", "eagle", "eagle3"):
+            raise ValueError("token trees are proposed by the ngram and EAGLE drafters")
         if m.family != ModelFamily.DENSE or m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
             raise ValueError("token-tree verification runs the paged bf16 attention of the "
                              "dense decoders (Llama / Qwen)")
-    if e.speculative_method not in (None, "ngram", "mtp", "eagle"):
+    if e.speculative_method not in (None, "ngram", "mtp", "eagle", "eagle3"):
         raise ValueError(f"speculative method {e.speculative_method!r} is not served")
