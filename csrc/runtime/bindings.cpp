@@ -105,6 +105,8 @@ void register_runtime(py::module_& m) {
            py::arg("n_min") = 1, py::arg("n_max") = 4, py::arg("width") = 2)
       .def("take_kv_moves", &Scheduler::take_kv_moves)
       .def("last_path", &Scheduler::last_path)
+      .def("reserve_slots", &Scheduler::reserve_slots)
+      .def("block_ids", &Scheduler::block_ids)
       .def("decode_request_ids", &Scheduler::decode_request_ids)
       .def("tokens_range", &Scheduler::tokens_range)
       .def("num_tokens", &Scheduler::num_tokens)

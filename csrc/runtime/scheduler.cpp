@@ -598,6 +598,25 @@ std::vector<std::pair<int64_t, int64_t>> Scheduler::take_kv_moves() {
   return out;
 }
 
+std::vector<int64_t> Scheduler::reserve_slots(int64_t id, int start, int n) {
+  std::vector<int64_t> out(std::max(0, n), -1);
+  auto it = reqs_.find(id);
+  if (it == reqs_.end() || it->second.status != kRunning) return out;
+  Request& r = it->second;
+  const int bs = cfg_.block_size;
+  for (int k = 0; k < n; ++k) {
+    const int pos = start + k;
+    if (pos < 0 || pos >= cfg_.max_model_len || !ensure_blocks(r, pos + 1)) break;
+    out[k] = (int64_t)r.blocks[pos / bs] * bs + pos % bs;
+  }
+  return out;
+}
+
+std::vector<int32_t> Scheduler::block_ids(int64_t id) const {
+  auto it = reqs_.find(id);
+  return it == reqs_.end() ? std::vector<int32_t>{} : it->second.blocks;
+}
+
 std::vector<int32_t> Scheduler::last_path(int64_t id) const {
   auto it = reqs_.find(id);
   return it == reqs_.end() ? std::vector<int32_t>{} : it->second.last_path;

@@ -179,6 +179,11 @@ class Scheduler {
   // of a draft tree moved to consecutive slots.  Must run before the next step's forward.
   std::vector<std::pair<int64_t, int64_t>> take_kv_moves();
   std::vector<int32_t> last_path(int64_t id) const;
+  // KV slots of positions [start, start + n) of a running request, allocating blocks as needed
+  // (a model drafter writes its own layer's K/V there while chaining drafts); -1 where the pool
+  // has no block left.  block_ids: the request's block table.
+  std::vector<int64_t> reserve_slots(int64_t id, int start, int n);
+  std::vector<int32_t> block_ids(int64_t id) const;
   static constexpr int kMaxTreeDrafts = 63;  // + the pending token = 64 mask bits
   std::vector<int64_t> decode_request_ids() const;  // running requests with one token pending
   // tokens[start, start + n) of a request (clipped to what exists), and its token count

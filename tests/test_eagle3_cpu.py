@@ -131,3 +131,17 @@ def test_eagle3_sibling_tree_matches_plain():
                                        "speculative_token_tree": "[(0,), (1,), (2,)]"}, **KW)
     assert [o.outputs[0].token_ids for o in llm.generate(prompts, sp)] == plain
     assert llm.engine.drafter.proposed > 0
+
+
+def test_eagle3_chained_drafts_keep_outputs():
+    """num_speculative_tokens = 3: the chained steps feed the head's own pre-norm output back
+    (3H features only at the first draft); verified outputs equal plain decoding."""
+    cfg = _cfg()
+    prompts = _prompts()
+    sp = SamplingParams(temperature=0.0, max_tokens=10, ignore_eos=True)
+    plain = [o.outputs[0].token_ids for o in LLM(cfg, **KW).generate(prompts, sp)]
+    llm = LLM(cfg, speculative_config={"method": "eagle3", "num_speculative_tokens": 3}, **KW)
+    rec = _Recorder(llm.engine.scheduler)
+    llm.engine.scheduler = rec
+    assert [o.outputs[0].token_ids for o in llm.generate(prompts, sp)] == plain
+    assert any(len(d) == 3 for _, d in rec.drafts)

@@ -128,7 +128,74 @@ def test_eagle_contract():
     k = C.resolve(e)
     C.validate(k)
     assert C.Feature.EAGLE in k.preferred
-    with pytest.raises(ValueError):
-        LLM(cfg, speculative_config={"method": "eagle", "num_speculative_tokens": 2}, **KW)
+    with pytest.raises(ValueError):  # chained drafts are verified as chains, not trees
+        LLM(cfg, speculative_config={"method": "eagle", "num_speculative_tokens": 2,
+                                     "tree_width": 2}, **KW)
     with pytest.raises(ValueError):
         LLM(cfg, speculative_config={"method": "medusa", "num_speculative_tokens": 1}, **KW)
+
+
+def _head_layer(ref, ew, X):
+    """The EAGLE-1 decoder layer over post-fc inputs X [P, H]: (pre-norm output, logits)."""
+    cfg, w, D = ref.cfg, ref.w, ref.D
+    P = X.shape[0]
+    a = "layers.0.self_attn."
+    q = (X @ ew[a + "q_proj.weight"].t()).view(P, cfg.num_heads, D)
+    k = (X @ ew[a + "k_proj.weight"].t()).view(P, cfg.num_kv_heads, D)
+    v = (X @ ew[a + "v_proj.weight"].t()).view(P, cfg.num_kv_heads, D)
+    pos = torch.arange(P)
+    q, k = ref._rope(q, pos), ref._rope(k, pos)
+    G = cfg.num_heads // cfg.num_kv_heads
+    k, v = k.repeat_interleave(G, 1), v.repeat_interleave(G, 1)
+    s = torch.einsum("qhd,khd->hqk", q, k) / D ** 0.5
+    s = s.masked_fill(torch.triu(torch.ones(P, P, dtype=torch.bool), 1)[None], float("-inf"))
+    h = X + torch.einsum("hqk,khd->qhd", s.softmax(-1), v).reshape(P, -1) @ \
+        ew[a + "o_proj.weight"].t()
+    y = ref._rms(h, ew["layers.0.post_attention_layernorm.weight"])
+    m = "layers.0.mlp."
+    h = h + (F.silu(y @ ew[m + "gate_proj.weight"].t()) * (y @ ew[m + "up_proj.weight"].t())) \
+        @ ew[m + "down_proj.weight"].t()
+    out = ref._rms(h, ew["norm.weight"]) if "norm.weight" in ew else h
+    return h, out @ w.get("lm_head.weight", w["model.embed_tokens.weight"]).t()
+
+
+def eagle_chain(ref, ew, tokens, k):
+    """k chained EAGLE-1 drafts after ``tokens``: positions 0..n-2 read the target's hidden
+    states, later ones the head's own previous pre-norm output and the previous draft."""
+    ew = {n: v.float() for n, v in ew.items()}
+    w = ref.w
+    n = len(tokens)
+    hid = ref.hidden(tokens)[:n - 1]
+    emb = w["model.embed_tokens.weight"]
+
+    def fc(e, h):
+        x = torch.cat([e, h], -1) @ ew["fc.weight"].t()
+        return x + ew["fc.bias"] if "fc.bias" in ew else x
+
+    X = fc(emb[torch.tensor(tokens[1:])], hid)
+    drafts = []
+    for _ in range(k):
+        h, lg = _head_layer(ref, ew, X)
+        d = int(torch.argmax(lg[-1]))
+        drafts.append(d)
+        X = torch.cat([X, fc(emb[d].unsqueeze(0), h[-1:])], 0)
+    return drafts
+
+
+def test_eagle_chained_drafts_match_reference():
+    """num_speculative_tokens = 3: each step's three chained drafts equal the pure-PyTorch
+    chain, and outputs equal plain greedy decoding."""
+    cfg = tiny_llama()
+    prompts = _prompts()
+    sp = SamplingParams(temperature=0.0, max_tokens=10, ignore_eos=True)
+    plain = [o.outputs[0].token_ids for o in LLM(cfg, **KW).generate(prompts, sp)]
+    llm = LLM(cfg, speculative_config={"method": "eagle", "num_speculative_tokens": 3}, **KW)
+    rec = _Recorder(llm.engine.scheduler)
+    llm.engine.scheduler = rec
+    outs = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    assert outs == plain
+    ref = ReferenceDecoder(cfg, dict(dummy_weights(cfg, seed=0, std=0.02)))
+    ew = dict(dummy_weights(cfg, seed=1, std=0.02, shapes=eagle_param_shapes(cfg)))
+    assert rec.drafts and any(len(d) == 3 for _, d in rec.drafts)
+    for toks, draft in rec.drafts:
+        assert draft == eagle_chain(ref, ew, toks, len(draft))

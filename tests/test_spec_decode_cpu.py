@@ -101,8 +101,9 @@ def test_mtp_spec_decode_matches_plain_deepseek():
     kw = dict(device="cpu", block_size=16, seed=0, num_gpu_blocks=64, max_model_len=128,
               max_num_seqs=4, max_num_batched_tokens=64)
     plain = [o.outputs[0].token_ids for o in LLM(cfg, **kw).generate(prompts, sp)]
-    llm = LLM(cfg, speculative_config={"method": "mtp", "num_speculative_tokens": 1}, **kw)
-    outs = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
-    assert outs == plain
-    assert llm.engine.drafter.proposed > 0
-    assert llm.engine.scheduler.spec_proposed() > 0
+    for k in (1, 2):  # 2: the MTP layer chained on its own output
+        llm = LLM(cfg, speculative_config={"method": "mtp", "num_speculative_tokens": k}, **kw)
+        outs = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+        assert outs == plain
+        assert llm.engine.drafter.proposed > 0
+        assert llm.engine.scheduler.spec_proposed() > 0

@@ -29,8 +29,12 @@ class ModelDrafter:
 
     def __init__(self, engine, forward, logits, num_tokens: int = 1, tree_width: int = 1,
                  features=None, pick=None):
-        if num_tokens != 1:
-            raise ValueError("model-based drafters propose one token per step")
+        if num_tokens < 1:
+            raise ValueError("num_speculative_tokens must be >= 1")
+        if num_tokens > 1 and tree_width > 1:
+            raise ValueError("chained drafts (num_speculative_tokens > 1) are verified as a "
+                             "chain: token trees take one draft level")
+        self.k = num_tokens
         self.engine = engine
         self.model = engine.model
         self.runner = engine.runner
@@ -99,9 +103,17 @@ class ModelDrafter:
                             tile_scratch=self.runner.tile_scratch,
                             state_slots=b.d["state_slots"][:R])
         prev = hidden[torch.tensor(hid_rows, dtype=torch.long, device=dev)]
-        x = self.forward(ids, prev, meta, self.runner.kv_caches)
+        x, xc = self._run(ids, prev, meta)
         last_rows = torch.tensor([c - 1 for c in cus[1:]], dtype=torch.long, device=dev)
         logits = self.logits(x[last_rows])
+        if self.k > 1:
+            ready = [j for j, (_, r) in enumerate(who) if r]
+            if ready:
+                sel = torch.tensor(ready, dtype=torch.long, device=dev)
+                first = self._greedy(logits.index_select(0, sel))
+                self._chain([who[j][0] for j in ready], [lens[j] + 1 for j in ready], first,
+                            xc[last_rows].index_select(0, sel))
+            return
         if self.pick is not None:  # the head's own vocabulary, whole on this rank
             top = self.pick(logits, self.tree_width).cpu().tolist()
             for k, (rid, ready) in enumerate(who):
@@ -129,6 +141,62 @@ class ModelDrafter:
             if ready:
                 sch.set_draft(rid, [int(draft[k])])
                 self.proposed += 1
+
+
+    def _run(self, ids, prev, meta):
+        """The head's forward -> (hidden for its logits, hidden that feeds a chained step)."""
+        out = self.forward(ids, prev, meta, self.runner.kv_caches)
+        return out if isinstance(out, tuple) else (out, out)
+
+    def _greedy(self, logits) -> list:
+        """Most likely target token id of each row."""
+        if self.pick is not None:
+            return [int(t) for t in self.pick(logits, 1)[:, 0].cpu().tolist()]
+        return [int(t) for t in
+                self.runner.sampler(logits, None, None, None, None, None, None).cpu().tolist()]
+
+    def _chain(self, rids, n_toks, first, h) -> None:
+        """Drafts 2..k: step j runs the head once per request at position n_tok - 2 + j on the
+        previous draft token, fed with its own previous output instead of the target's (not yet
+        computed) hidden state, writing its layer's K/V at that position's slot (reserved here);
+        a request whose slot cannot be reserved keeps the drafts it has."""
+        sch = self.engine.scheduler
+        dev = h.device
+        drafts = {rid: [t] for rid, t in zip(rids, first)}
+        live = list(range(len(rids)))
+        width = self.runner.max_blocks
+        for j in range(1, self.k):
+            keep, pos, slots, tables = [], [], [], []
+            for i in live:
+                p = n_toks[i] - 2 + j
+                slot = sch.reserve_slots(rids[i], p, 1)[0]
+                if slot < 0:
+                    continue
+                blocks = list(sch.block_ids(rids[i]))[:width]
+                keep.append(i)
+                pos.append(p)
+                slots.append(slot)
+                tables.append(blocks + [0] * (width - len(blocks)))
+            if not keep:
+                break
+            R = len(keep)
+            idx = torch.tensor([live.index(i) for i in keep], dtype=torch.long, device=dev)
+            h = h.index_select(0, idx)
+            ids = torch.tensor([drafts[rids[i]][-1] for i in keep], dtype=torch.int32, device=dev)
+            meta = AttnMetadata(R, 0, R, torch.tensor(pos, dtype=torch.int32, device=dev),
+                                torch.tensor(slots, dtype=torch.int32, device=dev),
+                                torch.tensor([p + 1 for p in pos], dtype=torch.int32, device=dev),
+                                torch.tensor(tables, dtype=torch.int32, device=dev),
+                                torch.arange(R + 1, dtype=torch.int32, device=dev),
+                                max_seq_len=max(pos) + 1, tile_scratch=self.runner.tile_scratch,
+                                state_slots=self.runner.buf.d["state_slots"][:R])
+            x, h = self._run(ids, h, meta)
+            for i, t in zip(keep, self._greedy(self.logits(x))):
+                drafts[rids[i]].append(t)
+            live = keep
+        for rid in rids:
+            sch.set_draft(rid, drafts[rid])
+            self.proposed += len(drafts[rid])
 
 
 class MTPDrafter(ModelDrafter):

@@ -136,10 +136,8 @@ class EagleHead:
         a = self.attn.forward(qkv, kc, vc, meta)
         x, residual = comm.linear_allreduce_add_rmsnorm(a, L.o_w, residual, L.ln2, eps)
         act = ops.linear_silu_mul(x, L.gu_w)
-        if self.norm is not None:
-            x, residual = comm.linear_allreduce_add_rmsnorm(act, L.down_w, residual, self.norm,
-                                                            eps)
-            return x
+        if self.norm is not None:  # (normalised for the logits, pre-norm for a chained step)
+            return comm.linear_allreduce_add_rmsnorm(act, L.down_w, residual, self.norm, eps)
         return comm.all_reduce(ops.linear(act, L.down_w)) + residual
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
@@ -244,7 +242,10 @@ class Eagle3Head:
         comm = self.comm
         comm.begin_forward()
         e = ops.embedding(next_ids, t.embed)
-        g = ops.linear(aux.to(e.dtype).contiguous(), self.fc)
+        H = cfg.hidden_size
+        # the target's three streams (first draft) or the head's own pre-norm output (chained)
+        g = aux.to(e.dtype) if aux.shape[1] == H else \
+            ops.linear(aux.to(e.dtype).contiguous(), self.fc)
         x = torch.cat([ops.rms_norm(e, self.in_ln, eps), ops.rms_norm(g, self.hidden_norm, eps)],
                       -1).contiguous()
         kc, vc = self.own_kv
@@ -254,8 +255,8 @@ class Eagle3Head:
         a = self.attn.forward(qkv, kc, vc, meta)
         x, residual = comm.linear_allreduce_add_rmsnorm(a, L.o_w, g, L.ln2, eps)
         act = ops.linear_silu_mul(x, L.gu_w)
-        x, _ = comm.linear_allreduce_add_rmsnorm(act, L.down_w, residual, self.norm, eps)
-        return x
+        # (normalised for the logits, pre-norm for a chained step)
+        return comm.linear_allreduce_add_rmsnorm(act, L.down_w, residual, self.norm, eps)
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """[S, H] -> fp32 logits over the draft vocabulary [S, Vd]."""
