@@ -123,3 +123,26 @@ def test_eagle_chained_drafts_on_gpu_keep_tokens():
             want = ref.logits(p + toks[:k])[-1]
             gap = float(want.max() - want[t]) / float(want.abs().max())
             assert gap < 0.03, (k, gap)
+
+
+def test_medusa_on_gpu_keeps_tokens():
+    """Medusa heads (chained and tree drafts) over the bf16 tiny Llama with CUDA graphs: every
+    emitted token is the fp32 reference argmax up to bf16 resolution."""
+    from vllm_musa_b200 import LLM, SamplingParams
+    g = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (20, 90)]
+    sp = SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True)
+    ref = _ref()
+    for spec in ({"method": "medusa", "num_speculative_tokens": 3},
+                 {"method": "medusa", "num_speculative_tokens": 6, "tree_width": 2}):
+        llm = LLM(_cfg(), block_size=64, seed=0, num_gpu_blocks=32, max_model_len=512,
+                  max_num_seqs=8, max_num_batched_tokens=512, speculative_config=spec)
+        got = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+        assert llm.engine.drafter.proposed > 0
+        llm.shutdown()
+        for p, toks in zip(prompts, got):
+            assert len(toks) == 12
+            for k, t in enumerate(toks):
+                want = ref.logits(p + toks[:k])[-1]
+                gap = float(want.max() - want[t]) / float(want.abs().max())
+                assert gap < 0.03, (spec, k, gap)

@@ -275,7 +275,7 @@ class SpeculativeConfig:
 
     ``draft_tensor_parallel_size=1`` keeps a whole EAGLE head on every rank of a
     tensor-parallel target (its layer then needs no all-reduce)."""
-    method: Optional[str] = None  # None | "ngram" | "mtp" | "eagle" | "eagle3"
+    method: Optional[str] = None  # None | "ngram" | "mtp" | "eagle" | "eagle3" | "medusa"
     num_speculative_tokens: int = 0
     model: Optional[str] = None
     prompt_lookup_min: int = 1

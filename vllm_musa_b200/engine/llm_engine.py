@@ -117,6 +117,8 @@ class LLMEngine:
             self._load_eagle()
         elif config.speculative.method == "eagle3":
             self._load_eagle3()
+        elif config.speculative.method == "medusa":
+            self._load_medusa()
         if config.lora.enable_lora:
             from ..lora import LoRAManager
             if not hasattr(self.model, "lora") or not hasattr(self.model, "I_pad"):
@@ -179,6 +181,10 @@ class LLMEngine:
             from .spec_decode import EagleDrafter
             self.drafter = EagleDrafter(self, config.speculative.num_speculative_tokens or 1,
                                         config.speculative.tree_width)
+        elif config.speculative.method == "medusa":
+            from .spec_decode import MedusaDrafter
+            self.drafter = MedusaDrafter(self, config.speculative.num_speculative_tokens or 1,
+                                         config.speculative.tree_width)
         elif config.speculative.method == "eagle3":
             from .spec_decode import Eagle3Drafter
             self.drafter = Eagle3Drafter(self, config.speculative.num_speculative_tokens or 1,
@@ -379,7 +385,7 @@ class LLMEngine:
             else:
                 self.scheduler.propose_ngram(spec.num_speculative_tokens,
                                              spec.prompt_lookup_min, spec.prompt_lookup_max)
-        elif spec.method in ("mtp", "eagle", "eagle3") and self.drafter is not None:
+        elif spec.method in ("mtp", "eagle", "eagle3", "medusa") and self.drafter is not None:
             self.drafter.propose(self.scheduler)
         if self._special and spec.method is not None:
             # penalties, log-probabilities and grammars are applied per drawn token: requests
@@ -769,6 +775,28 @@ class LLMEngine:
             self.model.load_weights(dummy_weights(mcfg, cfg.seed, cfg.init_std, device=dev))
         else:
             self.model.load_weights(safetensors_weights(cfg.model_path))
+
+    def _load_medusa(self) -> None:
+        """Attach Medusa heads: as many as the checkpoint has, or (random init) one per chained
+        draft / four for a tree."""
+        import re as _re
+        from ..models.medusa import MedusaHeads, medusa_param_shapes
+        cfg, mcfg, device = self.config, self.config.model, self.device
+        spec = cfg.speculative
+        path = spec.model
+        if path:
+            st = list(safetensors_weights(path))
+            n = 1 + max(int(m.group(1)) for m in
+                        (_re.match(r"blocks\.(\d+)\.", name) for name, _ in st) if m)
+        else:
+            n = spec.num_speculative_tokens if spec.tree_width == 1 else \
+                min(4, spec.num_speculative_tokens)
+            dev = str(device) if device.type == "cuda" else "cpu"
+            st = dummy_weights(mcfg, cfg.seed + 1, cfg.init_std, device=dev,
+                               shapes=medusa_param_shapes(mcfg, n))
+        heads = MedusaHeads(self.model, n)
+        heads.load_weights(st)
+        self.model.medusa = heads
 
     def _load_eagle3(self) -> None:
         """Attach an EAGLE-3 head (whole on this rank, its own KV cache) and make the model

@@ -231,3 +231,70 @@ class Eagle3Drafter(ModelDrafter):
             raise ValueError("speculative method 'eagle3' needs an EAGLE-3 head on the model")
         super().__init__(engine, head.forward_draft, head.compute_logits, num_tokens,
                          tree_width, features=lambda: engine.model.aux_buf, pick=head.pick)
+
+
+class MedusaDrafter:
+    """Medusa drafts right after every step, from the target's final hidden state at the
+    position whose next token is the pending one (``models/medusa.py``): a chain of each head's
+    argmax, or with ``tree_width`` w > 1 a token tree filled level by level."""
+
+    def __init__(self, engine, num_tokens: int, tree_width: int = 1):
+        self.engine = engine
+        self.runner = engine.runner
+        self.heads = engine.model.medusa
+        self.budget = min(num_tokens, 63)
+        self.w = tree_width
+        self.proposed = 0
+
+    def propose(self, scheduler) -> None:
+        """Drafts were set right after the previous step."""
+
+    @torch.no_grad()
+    def after_step(self, plan, sampled) -> None:
+        sch = self.engine.scheduler
+        hidden = self.runner.last_hidden
+        if hidden is None or plan.num_reqs == 0:
+            return
+        h = self.runner.buf.h
+        cu = h["cu_q"][:plan.num_reqs + 1].tolist()
+        pos_all = h["positions"][:plan.num_tokens]
+        rows, rids = [], []
+        for i, rid in enumerate(plan.req_ids):
+            n_tok = sch.num_tokens(rid)
+            if n_tok == 0:
+                continue
+            start, q = int(pos_all[cu[i]]), cu[i + 1] - cu[i]
+            p = n_tok - 2  # its next token is the pending one
+            if not start <= p < start + q:
+                continue  # a prompt chunk that does not reach the end of the prompt
+            m = p - start
+            path = sch.last_path(rid) if plan.tree else []
+            rows.append(cu[i] if m == 0 else (cu[i] + 1 + path[m - 1] if path else cu[i] + m))
+            rids.append(rid)
+        if not rows:
+            return
+        r = torch.tensor(rows, dtype=torch.long, device=hidden.device)
+        logits = self.heads.logits(hidden.index_select(0, r))
+        if self.w == 1:
+            d = torch.stack([lg.argmax(-1) for lg in logits], 1)[:, :self.budget].cpu().tolist()
+            for rid, toks in zip(rids, d):
+                sch.set_draft(rid, [int(t) for t in toks])
+                self.proposed += len(toks)
+            return
+        tops = [torch.topk(lg, self.w, dim=-1).indices.cpu().tolist() for lg in logits]
+        for n, rid in enumerate(rids):
+            toks, par, level = [], [], [-1]
+            for depth, top in enumerate(tops):
+                nxt = []
+                for parent in level:
+                    for t in top[n]:
+                        if len(toks) == self.budget:
+                            break
+                        toks.append(int(t))
+                        par.append(parent)
+                        nxt.append(len(toks) - 1)
+                level = nxt
+                if len(toks) == self.budget or not level:
+                    break
+            sch.set_draft_tree(rid, toks, par)
+            self.proposed += len(toks)

@@ -251,10 +251,14 @@ def validate(contract: OptimizationContract) -> None:
         if m.num_layers < e.pipeline_parallel_size:
             raise ValueError("pipeline_parallel_size exceeds the number of layers")
     if e.speculative_tree:
-        if e.speculative_method not in ("ngram", "eagle", "eagle3"):
-            raise ValueError("token trees are proposed by the ngram and EAGLE drafters")
+        if e.speculative_method not in ("ngram", "eagle", "eagle3", "medusa"):
+            raise ValueError("token trees are proposed by the ngram, EAGLE and Medusa drafters")
         if m.family != ModelFamily.DENSE or m.kv_cache_dtype not in ("auto", "bf16", "bfloat16"):
             raise ValueError("token-tree verification runs the paged bf16 attention of the "
                              "dense decoders (Llama / Qwen)")
-    if e.speculative_method not in (None, "ngram", "mtp", "eagle", "eagle3"):
+    if e.speculative_method == "medusa":
+        if m.family not in (ModelFamily.DENSE, ModelFamily.MOE) or e.pipeline_parallel_size > 1:
+            raise ValueError("Medusa heads are served over the dense and MoE decoders without "
+                             "pipeline stages")
+    if e.speculative_method not in (None, "ngram", "mtp", "eagle", "eagle3", "medusa"):
         raise ValueError(f"speculative method {e.speculative_method!r} is not served")
