@@ -132,7 +132,7 @@ def test_eagle_contract():
         LLM(cfg, speculative_config={"method": "eagle", "num_speculative_tokens": 2,
                                      "tree_width": 2}, **KW)
     with pytest.raises(ValueError):
-        LLM(cfg, speculative_config={"method": "medusa", "num_speculative_tokens": 1}, **KW)
+        LLM(cfg, speculative_config={"method": "lookahead", "num_speculative_tokens": 1}, **KW)
 
 
 def _head_layer(ref, ew, X):
