@@ -263,6 +263,9 @@ class SpeculativeConfig:
     """Speculative decoding.  ``ngram``: prompt lookup (drafts copied from the continuation of
     the latest earlier occurrence of the context's suffix n-gram, n in [prompt_lookup_min,
     prompt_lookup_max]); ``mtp``: the checkpoint's multi-token-prediction layer (DeepSeek);
+    ``eagle3``: an EAGLE-3 head (three target residual streams, own draft vocabulary);
+    ``medusa``: Medusa heads on the final hidden state (chains or token trees); model drafters
+    chain ``num_speculative_tokens`` > 1 drafts through their layer;
     ``eagle``: an EAGLE-1 head over a dense decoder, loaded from ``model`` (a safetensors
     directory) or, without one, seeded random weights.
 

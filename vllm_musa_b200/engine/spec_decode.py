@@ -24,7 +24,8 @@ from ..attention.metadata import AttnMetadata
 
 
 class ModelDrafter:
-    """One-token drafts from a draft layer: ``forward(ids, prev_hidden, meta, kv_caches)`` ->
+    """Drafts from a draft layer (one, or a chain of ``num_tokens`` fed back through the layer):
+    ``forward(ids, prev_hidden, meta, kv_caches)`` ->
     hidden rows, ``logits(hidden)`` -> this rank's vocab shard of the draft logits."""
 
     def __init__(self, engine, forward, logits, num_tokens: int = 1, tree_width: int = 1,
