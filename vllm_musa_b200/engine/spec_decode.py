@@ -1,8 +1,10 @@
 """Model-based speculative proposers.
 
-Both drafters are one extra decoder layer fed by the target's own features:
+The layer drafters are one extra decoder layer fed by the target's own features:
 ``MTPDrafter`` drives DeepSeek's multi-token-prediction layer (the checkpoint's layer
-``num_layers``), ``EagleDrafter`` an EAGLE head over a dense decoder (``models/eagle.py``).
+``num_layers``), ``EagleDrafter`` an EAGLE head over a dense decoder (``models/eagle.py``),
+``Eagle3Drafter`` an EAGLE-3 head reading three of the target's residual streams.
+``MedusaDrafter`` needs no layer: its heads read the final hidden state only.
 After every engine step the drafter runs its layer over each request's positions whose next
 token is now known: position p combines the embedding of token p+1 with the main model's final
 hidden state at p, writes the draft layer's KV for p (extra cache layer ``num_layers``, same
@@ -10,8 +12,10 @@ block table and slots as the main model), and its logits predict token p+2.  The
 made at the position just before the request's pending token becomes the draft the scheduler
 verifies in the next step (exact acceptance, see csrc/runtime/scheduler.cpp); with a tree
 width w > 1 the top w predictions are verified together as sibling nodes of a token tree, and
-the hidden state of the accepted node feeds the next draft.  Positions of rejected
-drafts are skipped: their main-model KV and hidden states are stale and get overwritten.
+the hidden state of the accepted node feeds the next draft.  With ``num_speculative_tokens``
+k > 1 the layer then runs k - 1 more single-token steps on its own output (chained drafts,
+KV slots reserved ahead of verification).  Positions of rejected drafts are skipped: their
+main-model KV and hidden states are stale and get overwritten.
 
 Reference counterparts: vllm_musa/v1/spec_decode/utils.py:4-124 (eagle / MTP input
 preparation kernels) and patches/vllm__v1__spec_decode__eagle.patch.py (drafter wiring).
