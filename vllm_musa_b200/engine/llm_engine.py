@@ -30,6 +30,7 @@ from ..parallel.state import get_parallel_state, init_distributed
 from ..sample.sampler import Sampler
 from ..sample.sampling_params import SamplingParams
 from .model_runner import ModelRunner
+from ..ops._ext import require as _native  # C++ scheduler + KV block pool (csrc/runtime)
 
 log = logging.getLogger("vllm_musa_b200")
 
@@ -151,8 +152,7 @@ class LLMEngine:
             raise ValueError(f"the KV cache holds {cap} tokens ({num_blocks} blocks), fewer than "
                              f"max_model_len={config.scheduler.max_model_len}: lower "
                              f"max_model_len or give the cache more memory / blocks")
-        from .. import _C_runtime
-        sc = _C_runtime.SchedulerConfig()
+        sc = _native().SchedulerConfig()
         # with decode context parallelism a scheduler block spans dcp ranks' cache blocks
         sc.block_size = config.cache.block_size * dcp
         sc.max_num_seqs = config.scheduler.max_num_seqs
@@ -169,7 +169,7 @@ class LLMEngine:
         sc.long_prefill_threshold = config.scheduler.long_prefill_token_threshold
         sc.priority_policy = config.scheduler.scheduling_policy == "priority"
         self._sched_cfg = sc
-        self.scheduler = _C_runtime.Scheduler(sc, num_blocks, self.runner.buf.pointers())
+        self.scheduler = _native().Scheduler(sc, num_blocks, self.runner.buf.pointers())
         self.sleep_level = 0
         self._offloaded: list = []
         self._profiler = None
@@ -268,8 +268,7 @@ class LLMEngine:
         bad_words_ids = self._bad_words_ids(params.bad_words) if params.bad_words else None
         lora_slot = self.model.lora.acquire(lora) if lora is not None else -1
         iid = next(self._ids)
-        from .. import _C_runtime
-        sp = _C_runtime.SamplingCfg()
+        sp = _native().SamplingCfg()
         sp.max_tokens = params.max_tokens
         sp.min_tokens = params.min_tokens
         sp.ignore_eos = params.ignore_eos
@@ -946,8 +945,7 @@ class LLMEngine:
                 raise RuntimeError(f"wake_up: {len(lost)} discarded tensors were not re-created "
                                    "by the weight loader; use sleep(level=1) for this model")
         self.runner.allocate_kv(self.num_blocks)
-        from .. import _C_runtime
-        self.scheduler = _C_runtime.Scheduler(self._sched_cfg, self.num_blocks,
+        self.scheduler = _native().Scheduler(self._sched_cfg, self.num_blocks,
                                               self.runner.buf.pointers())
         self.sleep_level = 0
         self.runner.capture_graphs()
