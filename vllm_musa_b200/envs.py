@@ -60,6 +60,13 @@ FLAGS: Dict[str, EnvFlag] = {f.name: f for f in [
     EnvFlag("B200_MOE_GEMV_MAX_PAIRS", 256, int,
             "bf16 MoE layers with at most this many routed (token, slot) pairs run per-pair "
             "GEMVs instead of align + gather + grouped GEMMs (0: always grouped)"),
+    EnvFlag("B200_MOE_SHAPE_INVENTORY", "", str,
+            "append one JSON line per eager MoE layer call (shape, dispatch path, routed-token "
+            "histogram) to this file; empty: off (synchronises: shape collection only)"),
+    EnvFlag("B200_MOE_SHAPE_INVENTORY_MIN_TOKENS", 0, int,
+            "smallest token count an MoE call needs to be recorded in the shape inventory"),
+    EnvFlag("B200_MOE_SHAPE_INVENTORY_MAX_RECORDS", 64, int,
+            "shape inventory records per process (< 0: unlimited)"),
     EnvFlag("B200_MAMBA_CHUNKED", True, _bool,
             "Mamba2 prefill parts of >= 64 tokens through the chunked SSD kernels (off: the "
             "token recurrence for every request)"),

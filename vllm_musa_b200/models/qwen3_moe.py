@@ -15,6 +15,7 @@ import torch
 
 from .. import ops
 from ..ops import moe as moe_ops
+from ..utils import moe_inventory
 from .llama import DenseDecoderForCausalLM, shard_cols, shard_rows
 
 
@@ -102,6 +103,8 @@ class Qwen3MoeForCausalLM(DenseDecoderForCausalLM):
         ids, w = moe_ops.topk_softmax(logits[:, :self.E], self.topk, self.cfg.norm_topk_prob)
 
         def experts(rx, rids):
+            moe_inventory.note("ep_grouped", rx, rids, self.E_local,
+                               L.experts_gu.shape[0] // self.E_local // 2, L.experts_gu.dtype)
             return moe_ops.moe_experts(rx, L.experts_gu, L.experts_down, rids, self.E_local)
 
         return a2a.moe_allreduce_add_rmsnorm(x, ids, w, experts, None, residual, nxt, eps)

@@ -19,6 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _ext
+from ..utils import moe_inventory
 from .gemm import deinterleave_gate_up
 
 
@@ -105,11 +106,15 @@ def fused_moe(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, ids: to
         out = torch.empty(T, H, dtype=x.dtype, device=x.device)
     if T == 0:
         return out
+    I = w_gu.shape[0] // num_experts // 2
+    gemv = x.is_cuda and use_gemv(T, k, H, I)
+    moe_inventory.note("cpu" if not x.is_cuda else "gemv" if gemv else "grouped", x, ids,
+                       num_experts, I, w_gu.dtype, expert_offset)
     if not x.is_cuda:
         out.copy_(_fused_moe_ref(x, w_gu, w_down, ids, w, num_experts, shared, expert_offset,
                                  shared_gate))
         return out
-    if use_gemv(T, k, H, w_gu.shape[0] // num_experts // 2):
+    if gemv:
         y, pos = moe_experts_gemv(x, w_gu, w_down, ids, num_experts, expert_offset)
     else:
         y, pos = moe_experts(x, w_gu, w_down, ids, num_experts, expert_offset)
@@ -221,6 +226,8 @@ def fused_moe_fp8(x: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor, w_dow
         out = torch.empty(T, H, dtype=x.dtype, device=x.device)
     if T == 0:
         return out
+    moe_inventory.note("fp8_grouped" if x.is_cuda else "cpu", x, ids, num_experts,
+                       w_gu.shape[0] // num_experts // 2, w_gu.dtype, expert_offset)
     if not x.is_cuda:
         out.copy_(_fused_moe_fp8_ref(x, w_gu, s_gu, w_down, s_down, ids, w, num_experts, shared,
                                      expert_offset, swiglu_limit))
